@@ -1,0 +1,372 @@
+"""CPU oracle of the flat HTRC operator's production (INT8) path, in NumPy.
+
+TEST INFRASTRUCTURE ONLY.  This module is the checker the parity tests, ``__graft_entry__.smoke()``
+and ``bench.py``'s CPU-baseline leg compare the CUDA library against.  Nothing in the shipped
+operator (``htrc_b200``) imports it; the CUDA path never falls back to it.
+
+It restates, step by step, the arithmetic of the reference operator
+``flat_attention(**PROD, leaf=L)`` of ASarych/HTRC, i.e. ``backend="triton", store="int8",
+dot="bf16", select="max", curvature="lin"``:
+
+  K INT8 pack ............ h3/htrc_flat.py:213-219       (round-half-even, IEEE divide by the scale)
+  tile centres ........... h3/htrc_flat.py:142-156       (mean over the tile's real rows)
+  leaf statistics ........ h3/htrc_flat_triton.py:41-85  (lz, g -> g8/sg half-away, vbar -> bf16)
+  row-max selection ...... h3/htrc_flat_triton.py:214-254 (dq8 . g8 * sdq * sg, max over rows, + lz)
+  top-E routing .......... h3/htrc_flat.py:232-265       (sink leaves forced, topk, exclusion mask)
+  far + near + tail ...... h3/htrc_flat_triton.py:88-211 (online softmax, bf16 P for PV)
+  split merge ............ h3/htrc_flat_triton.py:257-273 (normalised output) + log-Z (addition)
+
+Precision of the restatement: the leaf statistics are computed in float64 and rounded once to
+float32 (the reference computes them with tf32 tensor-core dots on the GPU); every quantisation
+formula is evaluated in float32 exactly as written in the reference; the softmax sums are float64.
+Division is IEEE float32 (the reference's torch code uses IEEE division; its Triton kernels use
+``/`` whose GPU lowering may be approximate).
+
+Parity status: pinned against outputs of the reference itself run in the build container
+(``tests/golden/make_golden.py`` runs h3/htrc_flat.py on CPU; the fixtures it wrote live in
+``tests/golden/*.npz``; ``tests/test_oracle.py`` checks this module against them).
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+F32 = np.float32
+INV127 = F32(1.0 / 127.0)      # the constant (1.0 / 127.0) the reference multiplies by, as float32
+EPS_ROW = F32(1e-20)           # row-scale floor (h3/htrc_flat.py:217, h3/htrc_flat_triton.py:112)
+EPS_SLOPE = F32(1e-30)         # slope abs-max floor (h3/htrc_flat_triton.py:75)
+
+
+# ----------------------------------------------------------------------------- bf16 helpers
+def bf16_bits(x):
+    """float32 -> bfloat16 bit pattern (uint16), round to nearest even (finite inputs)."""
+    b = np.ascontiguousarray(x, dtype=F32).view(np.uint32).astype(np.uint64)
+    b = (b + 0x7FFF + ((b >> 16) & 1)) >> 16
+    return b.astype(np.uint16)
+
+
+def bf16_to_f32(bits):
+    """bfloat16 bit pattern (uint16) -> float32 (exact)."""
+    return (np.asarray(bits, dtype=np.uint16).astype(np.uint32) << 16).view(F32)
+
+
+def bf16_round(x):
+    """Round float32 values to the nearest bfloat16 value (ties to even), returned as float32."""
+    return bf16_to_f32(bf16_bits(x))
+
+
+# ----------------------------------------------------------------------------- INT8 packing
+def pack_rows_half_even(x):
+    """Per-row INT8 pack of the near-field keys (h3/htrc_flat.py:216-218).
+
+    ks = max(amax_row|x| * (1/127), 1e-20);  x8 = clamp(round_half_even(x / ks), -127, 127).
+    Returns (x8 int8 [R, D], ks float32 [R])."""
+    x = np.asarray(x, dtype=F32)
+    s = np.maximum(np.abs(x).max(-1) * INV127, EPS_ROW).astype(F32)
+    y = (x / s[:, None]).astype(F32)
+    return np.clip(np.rint(y), -127, 127).astype(np.int8), s
+
+
+def _round_half_away_i8(y):
+    y = np.asarray(y, dtype=F32)
+    z = np.where(y >= 0, y + F32(0.5), y - F32(0.5)).astype(F32)
+    return np.trunc(z).astype(np.int8)
+
+
+def pack_rows_half_away(x):
+    """Per-row INT8 pack of query rows q and offsets dq = q - mu (h3/htrc_flat_triton.py:110-117,
+    :230-233): s = max(amax_row|x| * (1/127), 1e-20);  x8 = trunc(x / s +- 0.5) (half away).
+    Returns (x8 int8 [R, D], s float32 [R])."""
+    x = np.asarray(x, dtype=F32)
+    s = np.maximum(np.abs(x).max(-1) * INV127, EPS_ROW).astype(F32)
+    return _round_half_away_i8(x / s[..., None]), s
+
+
+def pack_slope(g):
+    """INT8 far-field slope per (tile, leaf) row (h3/htrc_flat_triton.py:73-79):
+    am = max(amax|g|, 1e-30); sg = am * (1/127); g8 = trunc(g * (127 / am) +- 0.5).
+    Returns (g8 int8 [..., D], sg float32 [...])."""
+    g = np.asarray(g, dtype=F32)
+    am = np.maximum(np.abs(g).max(-1), EPS_SLOPE).astype(F32)
+    sg = (am * INV127).astype(F32)
+    r = (F32(127.0) / am).astype(F32)
+    return _round_half_away_i8(g * r[..., None]), sg
+
+
+# ----------------------------------------------------------------------------- stages
+def tile_centres(q, tile):
+    """(qt float32 [nt, T, D], mu float32 [nt, D], n) with the last tile padded by repeats of the
+    last row and its centre taken over its real rows (h3/htrc_flat.py:142-156).  The mean is
+    evaluated in float64 and rounded once."""
+    q = np.asarray(q, dtype=F32)
+    n, d = q.shape
+    nt = -(-n // tile)
+    npad = nt * tile
+    qs = q if npad == n else np.concatenate([q, np.repeat(q[-1:], npad - n, 0)], 0)
+    qt = qs.reshape(nt, tile, d)
+    mu = qt.astype(np.float64).mean(1)
+    if npad > n:
+        mu[-1] = qt[-1, : n - (nt - 1) * tile].astype(np.float64).mean(0)
+    return qt, mu.astype(F32), n
+
+
+def leaf_stats(mu, k, v, leaf, scale):
+    """Exact leaf cumulants at the tile centres (h3/htrc_flat_triton.py:41-85):
+    a = scale mu.k_s, lz = logsumexp_s a, w = softmax a, g = scale sum w k, vbar = sum w v.
+    Returns float32 (g [nt, nb, D], lz [nt, nb], vbar [nt, nb, D])."""
+    mu = np.asarray(mu, dtype=np.float64)
+    k = np.asarray(k, dtype=np.float64)
+    v = np.asarray(v, dtype=np.float64)
+    nb = k.shape[0] // leaf
+    d = k.shape[1]
+    k3 = k[: nb * leaf].reshape(nb, leaf, d)
+    v3 = v[: nb * leaf].reshape(nb, leaf, d)
+    a = np.einsum("td,lsd->tls", mu, k3) * float(scale)
+    m = a.max(-1, keepdims=True)
+    w = np.exp(a - m)
+    z = w.sum(-1, keepdims=True)
+    w /= z
+    lz = (m + np.log(z))[..., 0]
+    g = np.einsum("tls,lsd->tld", w, k3) * float(scale)
+    vb = np.einsum("tls,lsd->tld", w, v3)
+    return g.astype(F32), lz.astype(F32), vb.astype(F32)
+
+
+def state_int8(g, vb):
+    """The stored far-field state: (g8, sg, vbar as bf16-rounded float32)
+    (h3/htrc_flat_triton.py:73-81)."""
+    g8, sg = pack_slope(g)
+    return g8, sg, bf16_round(vb)
+
+
+def query_codes(qt, mu):
+    """Per-row INT8 codes of the tile rows and of their offsets from the tile centre, as the tile
+    and row-max kernels form them in-register (h3/htrc_flat_triton.py:103-117)."""
+    qt = np.asarray(qt, dtype=F32)
+    dq = (qt - np.asarray(mu, dtype=F32)[:, None, :]).astype(F32)
+    q8, sq = pack_rows_half_away(qt)
+    dq8, sdq = pack_rows_half_away(dq)
+    return q8, sq, dq8, sdq
+
+
+def rowmax_select(dq8, sdq, g8, sg, lz):
+    """SEL[t, l] = max_r (dq8_r . g8_l) * (sdq_r * sg_l) + lz_l (h3/htrc_flat_triton.py:240-254)."""
+    dot = np.einsum("trd,tld->trl", dq8.astype(np.int32), g8.astype(np.int32))
+    sc = dot.astype(F32) * (sdq[:, :, None] * sg[:, None, :]).astype(F32)
+    return (sc.max(1) + lz).astype(F32)
+
+
+def route(sel, exact_leaves, sink_leaves=0):
+    """Top-E near-leaf routing per tile (h3/htrc_flat.py:232-233, :250-265).
+
+    Returns (idx int32 [nt, kx] sorted ascending, excl uint8 [nt, nb]).  The reference's
+    torch.topk returns the same set in an unspecified order; ties at the boundary are broken
+    here towards the lower leaf index."""
+    sel = np.array(sel, dtype=F32, copy=True)
+    nt, nb = sel.shape
+    sink = max(0, min(int(sink_leaves), nb))
+    kx = min(int(exact_leaves) + sink, nb)
+    excl = np.zeros((nt, nb), np.uint8)
+    if kx <= 0:
+        return np.zeros((nt, 0), np.int32), excl
+    if sink:
+        sel[:, :sink] = np.inf
+    order = np.argsort(-sel, axis=1, kind="stable")[:, :kx]
+    idx = np.sort(order, axis=1).astype(np.int32)
+    np.put_along_axis(excl, idx.astype(np.int64), 1, axis=1)
+    return idx, excl
+
+
+def tile_attention(qt, q8, sq, dq8, sdq, g8, sg, lz, vb, excl, idx, k8, ks, v, leaf, scale,
+                   tail=None):
+    """Far field + near field + tail of every tile, merged; returns (out float32 [nt*T, D],
+    lse float32 [nt*T]) (h3/htrc_flat_triton.py:88-211, merge :257-273).
+
+    far  : logit = (dq8 . g8_l) * (sdq * sg_l) + lz_l over the non-excluded leaves, value vbar_l
+    near : logit = (q8 . k8_j) * (sq * ks_j * scale) over the tokens of the routed leaves, value v_j
+    tail : logit = bf16(q) . bf16(tk_j) * scale (<= 16 keys) or the float32 product (> 16 keys),
+           value tv_j (h3/htrc_flat_triton.py:187-207, :381-388)
+    P is rounded to bfloat16 for the value product; the normaliser sums float32 P."""
+    nt, T, d = qt.shape
+    nb = lz.shape[1]
+    v = np.asarray(v, dtype=F32)
+    out = np.zeros((nt, T, d), F32)
+    lse = np.zeros((nt, T), F32)
+    ar = np.arange(leaf)
+    if tail is not None and tail[0].shape[0] > 0:
+        tk = np.asarray(tail[0], dtype=F32)
+        tv = np.asarray(tail[1], dtype=F32)
+        small = tk.shape[0] <= 16
+        if small:
+            tk, tv = bf16_round(tk), bf16_round(tv)
+    else:
+        tk = tv = None
+    for t in range(nt):
+        parts_s, parts_v = [], []
+        keep = excl[t] == 0
+        if keep.any():
+            dot = dq8[t].astype(np.int32) @ g8[t][keep].astype(np.int32).T
+            sc = dot.astype(F32) * (sdq[t][:, None] * sg[t][keep][None, :]).astype(F32) + lz[t][keep][None, :]
+            parts_s.append(sc.astype(F32))
+            parts_v.append(vb[t][keep])
+        if idx.shape[1]:
+            tok = (idx[t][:, None].astype(np.int64) * leaf + ar[None, :]).reshape(-1)
+            dot = q8[t].astype(np.int32) @ k8[tok].astype(np.int32).T
+            sc = dot.astype(F32) * ((sq[t][:, None] * ks[tok][None, :]).astype(F32) * F32(scale)).astype(F32)
+            parts_s.append(sc.astype(F32))
+            parts_v.append(v[tok])
+        if tk is not None:
+            if small:
+                sc = (bf16_round(qt[t]).astype(np.float64) @ tk.astype(np.float64).T).astype(F32) * F32(scale)
+            else:
+                sc = (qt[t].astype(np.float64) @ tk.astype(np.float64).T).astype(F32) * F32(scale)
+            parts_s.append(sc.astype(F32))
+            parts_v.append(tv)
+        s = np.concatenate(parts_s, 1).astype(np.float64)
+        vv = np.concatenate(parts_v, 0).astype(np.float64)
+        m = s.max(1, keepdims=True)
+        p = np.exp(s - m)
+        den = p.sum(1)
+        num = bf16_round(p.astype(F32)).astype(np.float64) @ vv
+        out[t] = (num / np.maximum(den, 1e-30)[:, None]).astype(F32)
+        lse[t] = (m[:, 0] + np.log(den)).astype(F32)
+    return out.reshape(nt * T, d), lse.reshape(nt * T)
+
+
+def _split(n, ns, bn):
+    """Per-split extent rounded up to the block width (h3/htrc_flat_triton.py:297-299)."""
+    per = -(-n // ns)
+    return max(bn, -(-per // bn) * bn)
+
+
+def tile_attention_ordered(qt, q8, sq, dq8, sdq, g8, sg, lz, vb, excl, idx, k8, ks, v, leaf, scale,
+                           tail=None, splits=4, bn=64):
+    """Same operator evaluated in the reference kernel's exact order: ``splits`` split programs per
+    tile, blocks of ``bn`` leaves / tokens, float32 online softmax with P rounded to bfloat16
+    against the running maximum, then the split merge (h3/htrc_flat_triton.py:118-211, :257-273).
+    ``idx`` must be in the reference's (unsorted) order.  Pins the restatement bit-for-bit
+    (up to float32 summation order) against fixtures recorded from the reference; returns
+    (out [nt*T, D], lse [nt*T])."""
+    nt, T, d = qt.shape
+    nb = lz.shape[1]
+    kx = idx.shape[1]
+    lps = _split(nb, splits, bn)
+    e_n = kx * leaf
+    eps = _split(e_n, splits, bn)
+    v = np.asarray(v, dtype=F32)
+    small_tail = tail is not None and 0 < tail[0].shape[0] <= 16
+    if small_tail:
+        tk, tv = bf16_round(tail[0]), bf16_round(tail[1])
+    out = np.zeros((nt, T, d), F32)
+    lse = np.zeros((nt, T), F32)
+    scale = F32(scale)
+
+    def step(m, l, acc, sc, vals):
+        mn = np.maximum(m, sc.max(1))
+        ms = np.where(mn == -np.inf, F32(0), mn).astype(F32)
+        p = np.exp(sc - ms[:, None]).astype(F32)
+        al = np.exp(m - ms).astype(F32)
+        l = (l * al + p.sum(1)).astype(F32)
+        acc = (acc * al[:, None] + (bf16_round(p).astype(np.float64) @ vals.astype(np.float64))).astype(F32)
+        return mn, l, acc
+
+    for t in range(nt):
+        pms, pls, paccs = [], [], []
+        for sp in range(splits):
+            m = np.full(T, -np.inf, F32)
+            l = np.zeros(T, F32)
+            acc = np.zeros((T, d), F32)
+            lo, hi = sp * lps, min(nb, sp * lps + lps)
+            for n0 in range(lo, hi, bn):
+                c = np.arange(n0, min(n0 + bn, hi))
+                dot = dq8[t].astype(np.int32) @ g8[t][c].astype(np.int32).T
+                sc = (dot.astype(F32) * (sdq[t][:, None] * sg[t][c][None, :]).astype(F32) + lz[t][c][None, :]).astype(F32)
+                sc = np.where((excl[t][c] == 0)[None, :], sc, F32(-np.inf))
+                m, l, acc = step(m, l, acc, sc, vb[t][c])
+            e_lo, e_hi = sp * eps, min(e_n, sp * eps + eps)
+            for e0 in range(e_lo, e_hi, bn):
+                j = np.arange(e0, min(e0 + bn, e_hi))
+                tok = idx[t][j // leaf].astype(np.int64) * leaf + j % leaf
+                dot = q8[t].astype(np.int32) @ k8[tok].astype(np.int32).T
+                sc = (dot.astype(F32) * ((sq[t][:, None] * ks[tok][None, :]).astype(F32) * scale)).astype(F32)
+                m, l, acc = step(m, l, acc, sc, v[tok])
+            if small_tail and sp == splits - 1:
+                sc = ((bf16_round(qt[t]).astype(np.float64) @ tk.astype(np.float64).T).astype(F32) * scale).astype(F32)
+                m, l, acc = step(m, l, acc, sc, tv)
+            pms.append(m)
+            pls.append(l)
+            paccs.append(acc)
+        if tail is not None and tail[0].shape[0] > 16:
+            tk32 = np.asarray(tail[0], F32)
+            lg = (qt[t].astype(np.float64) @ tk32.astype(np.float64).T).astype(F32) * scale
+            tm = lg.max(1)
+            te = np.exp(lg - tm[:, None]).astype(F32)
+            pms.append(tm.astype(F32))
+            pls.append(te.sum(1).astype(F32))
+            paccs.append((te.astype(np.float64) @ np.asarray(tail[1], np.float64)).astype(F32))
+        pm, pl, pa = np.array(pms), np.array(pls), np.array(paccs)
+        mm = pm.max(0)
+        mm = np.where(mm == -np.inf, F32(0), mm)
+        w = np.exp(pm - mm).astype(F32)
+        den = (pl * w).sum(0)
+        out[t] = ((pa * w[:, :, None]).sum(0) / np.maximum(den, F32(1e-30))[:, None]).astype(F32)
+        lse[t] = (mm + np.log(np.maximum(den, F32(1e-30)))).astype(F32)
+    return out.reshape(nt * T, d), lse.reshape(nt * T)
+
+
+def pack_k(k):
+    """Near-field key pack of bf16 keys: (k8, ks) (h3/htrc_flat.py:211-219)."""
+    return pack_rows_half_even(bf16_round(np.asarray(k, dtype=F32)))
+
+
+def flat_attention(q, k, v, *, tile=64, exact_leaves=256, leaf=64, scale=None, sink_leaves=0,
+                   tail=None, return_stages=False):
+    """The whole production path for one head: q [N, D], k/v [M, D] (float32 arrays holding the
+    caller's values; k and v are rounded to bfloat16 as the reference's bf16 path stores them).
+    Returns (out float32 [N, D], lse float32 [N]) and, with return_stages, a dict of every stage."""
+    q = np.asarray(q, dtype=F32)
+    k = bf16_round(np.asarray(k, dtype=F32))
+    v = bf16_round(np.asarray(v, dtype=F32))
+    n, d = q.shape
+    m = k.shape[0]
+    if m % leaf:
+        raise ValueError("key count must be a multiple of the leaf size")
+    scale = 1.0 / math.sqrt(d) if scale is None else float(scale)
+    k8, ks = pack_rows_half_even(k)
+    qt, mu, _ = tile_centres(q, tile)
+    g, lz, vbf = leaf_stats(mu, k, v, leaf, scale)
+    g8, sg, vb = state_int8(g, vbf)
+    q8, sq, dq8, sdq = query_codes(qt, mu)
+    nb = m // leaf
+    sink = max(0, min(int(sink_leaves), nb))
+    kx = min(int(exact_leaves) + sink, nb)
+    if kx > 0:
+        sel = rowmax_select(dq8, sdq, g8, sg, lz)
+    else:
+        sel = np.zeros((qt.shape[0], nb), F32)
+    idx, excl = route(sel, exact_leaves, sink)
+    out, lse = tile_attention(qt, q8, sq, dq8, sdq, g8, sg, lz, vb, excl, idx, k8, ks, v, leaf,
+                              scale, tail=tail)
+    out, lse = out[:n], lse[:n]
+    if not return_stages:
+        return out, lse
+    return out, lse, dict(k8=k8, ks=ks, qt=qt, mu=mu, g=g, g8=g8, sg=sg, lz=lz, vb=vb, q8=q8,
+                          sq=sq, dq8=dq8, sdq=sdq, sel=sel, idx=idx, excl=excl)
+
+
+def exact_attention(q, k, v, scale=None, tail=None):
+    """Dense softmax attention in float64 (for reporting the operator's approximation error):
+    returns (out float32 [N, D], lse float32 [N])."""
+    q = np.asarray(q, np.float64)
+    k = np.asarray(k, np.float64)
+    v = np.asarray(v, np.float64)
+    if tail is not None and tail[0].shape[0]:
+        k = np.concatenate([k, np.asarray(tail[0], np.float64)], 0)
+        v = np.concatenate([v, np.asarray(tail[1], np.float64)], 0)
+    scale = 1.0 / math.sqrt(q.shape[1]) if scale is None else float(scale)
+    s = (q @ k.T) * scale
+    m = s.max(1, keepdims=True)
+    p = np.exp(s - m)
+    den = p.sum(1, keepdims=True)
+    return (p @ v / den).astype(F32), (m[:, 0] + np.log(den[:, 0])).astype(F32)

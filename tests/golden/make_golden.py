@@ -1,0 +1,188 @@
+"""Generate the golden fixtures of the flat HTRC production path by running the REFERENCE itself.
+
+Run once, in a container that has the reference checkout (default ``/root/reference``; override
+with ``HTRC_REFERENCE``):
+
+    TRITON_INTERPRET=1 python tests/golden/make_golden.py
+
+It imports the reference's ``h3/htrc_flat.py`` unmodified and calls
+``flat_attention(q, k, v, **PROD, leaf=L, exact_leaves=E, ...)`` on CPU tensors with Triton's
+interpreter, recording every stage the reference passes between its kernels (the INT8 keys, the
+leaf state g8/sg/lz/vbar, the row-max selection, the exclusion mask, the split partials and the
+output).  The fixtures are written as ``tests/golden/<case>.npz`` and are the only thing the tests
+read; the reference is never needed at test time.
+
+Triton 3.6's interpreter has two defects on this path, fixed here by a harness-side shim (the
+reference is not modified):
+  1. ``create_dot`` multiplies bfloat16 operands as their raw uint16 bit patterns -> the shim widens
+     bfloat16 operands to float32 before the product;
+  2. float32 -> bfloat16 casts truncate -> the shim rounds to nearest even, as the GPU does.
+The interpreter also evaluates ``tl.dot(..., input_precision="tf32")`` in float32 and ``/`` as
+IEEE division; the fixtures therefore pin the reference's arithmetic at float32 precision.
+"""
+from __future__ import annotations
+
+import importlib.util
+import os
+import sys
+from pathlib import Path
+
+os.environ.setdefault("TRITON_INTERPRET", "1")
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parents[1]
+REF = Path(os.environ.get("HTRC_REFERENCE", "/root/reference"))
+sys.path.insert(0, str(REPO))
+
+from htrc_b200 import synth  # noqa: E402
+
+
+def _shim():
+    from triton.runtime import interpreter as itp
+    import triton.language as tl
+
+    B = itp.InterpreterBuilder
+    orig_dot = B.create_dot
+    orig_cast = B.cast_impl
+    orig_fp2fp = B.create_fp_to_fp
+
+    def widen(h):
+        if h.dtype.scalar == tl.bfloat16:
+            data = (h.data.astype(np.uint32) << 16).view(np.float32)
+            return itp.TensorHandle(data, tl.float32)
+        return h
+
+    def create_dot(self, a, b, d, input_precision, max_num_imprecise_acc):
+        return orig_dot(self, widen(a), widen(b), d, input_precision, max_num_imprecise_acc)
+
+    def to_bf16(src, dst_type):
+        x = np.ascontiguousarray(src.data, dtype=np.float32).view(np.uint32).astype(np.uint64)
+        bits = ((x + 0x7FFF + ((x >> 16) & 1)) >> 16).astype(np.uint16)
+        return itp.TensorHandle(bits, dst_type.scalar)
+
+    def cast_impl(self, src, dst_type):
+        if src.dtype.scalar == tl.float32 and dst_type.scalar == tl.bfloat16:
+            return to_bf16(src, dst_type)
+        return orig_cast(self, src, dst_type)
+
+    def create_fp_to_fp(self, src, dst_type, rounding_mode):
+        if src.dtype.scalar == tl.float32 and dst_type.scalar == tl.bfloat16:
+            return to_bf16(src, dst_type)
+        return orig_fp2fp(self, src, dst_type, rounding_mode)
+
+    B.create_dot = create_dot
+    B.cast_impl = cast_impl
+    B.create_fp_to_fp = create_fp_to_fp
+
+
+def _load_reference():
+    spec = importlib.util.spec_from_file_location("_ref_htrc_flat", REF / "h3" / "htrc_flat.py")
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["_ref_htrc_flat"] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def _recorder(flat):
+    """Wrap the reference's kernel wrappers to record what flows between them."""
+    tri = flat._load_triton()
+    rec = {"stats": [], "sel": [], "tile": []}
+    o_stats, o_sel, o_tile = tri.leaf_stats, tri.rowmax_select, tri.tile_attention
+
+    def leaf_stats(mu, kf, vf, nb, scale, **kw):
+        g, lz, vb, sg, sv = o_stats(mu, kf, vf, nb, scale, **kw)
+        rec["stats"].append(dict(mu=mu.clone(), g8=g.clone(), lz=lz.clone(), vb=vb.clone(), sg=sg.clone()))
+        return g, lz, vb, sg, sv
+
+    def rowmax_select(*a, **kw):
+        sel = o_sel(*a, **kw)
+        rec["sel"].append(sel.clone())
+        return sel
+
+    def tile_attention(q_c, mu_c, g, lz, vb, excl, idx, k_ex, v_ex, scale, **kw):
+        ws = kw.get("ws")
+        res = o_tile(q_c, mu_c, g, lz, vb, excl, idx, k_ex, v_ex, scale, **kw)
+        ent = dict(q_c=q_c.clone(), excl=excl.clone(), k8=k_ex.clone(), ks=kw["ks"].clone(),
+                   out=res.clone())
+        if idx is not None:
+            ent["idx"] = idx.clone()
+        if ws is not None:
+            ent["pm"], ent["pl"] = ws["pm"][: q_c.shape[0]].clone(), ws["pl"][: q_c.shape[0]].clone()
+        rec["tile"].append(ent)
+        return res
+
+    tri.leaf_stats, tri.rowmax_select, tri.tile_attention = leaf_stats, rowmax_select, tile_attention
+    return rec
+
+
+def _cat(lst, key):
+    return torch.cat([e[key] for e in lst], 0)
+
+
+CASES = [
+    # name, grid (t,h,w) or (n, m) low-rank, leaf, exact_leaves, sink, tail rows, n_query_trim
+    dict(name="base", grid=(2, 16, 16), leaf=64, E=2, sink=0, tail=0, trim=0, seed=11),
+    dict(name="ragged", grid=(2, 16, 16), leaf=64, E=3, sink=0, tail=0, trim=37, seed=12),
+    dict(name="sink_tail", grid=(2, 16, 16), leaf=64, E=2, sink=1, tail=5, trim=0, seed=13),
+    dict(name="all_exact", grid=(2, 16, 16), leaf=64, E=8, sink=0, tail=0, trim=0, seed=14),
+    dict(name="no_exact", grid=(2, 16, 16), leaf=64, E=0, sink=0, tail=0, trim=0, seed=15),
+    dict(name="big_tail", grid=(2, 16, 16), leaf=64, E=2, sink=0, tail=20, trim=0, seed=16),
+    dict(name="leaf32", grid=(2, 16, 16), leaf=32, E=4, sink=0, tail=0, trim=0, seed=17),
+    dict(name="wide", grid=(4, 16, 32), leaf=64, E=4, sink=0, tail=0, trim=0, seed=18),
+]
+
+
+def run_case(flat, c):
+    q, k, v = synth.head_inputs(c["grid"], 128, base_seed=c["seed"])
+    tk = tv = None
+    if c["tail"]:
+        tk = k[-c["tail"]:].float().clone()
+        tv = v[-c["tail"]:].float().clone()
+        k, v = k[: -c["tail"]], v[: -c["tail"]]
+        keep = (k.shape[0] // c["leaf"]) * c["leaf"]
+        k, v = k[:keep].contiguous(), v[:keep].contiguous()
+    if c["trim"]:
+        q = q[: -c["trim"]].contiguous()
+    rec = _recorder(flat)
+    ws = {}
+    cfg = dict(flat.PROD)
+    cfg.update(leaf=c["leaf"], exact_leaves=c["E"], sink_leaves=c["sink"], tile_chunk=4096)
+    out = flat.flat_attention(q, k, v, tail=(tk, tv) if tk is not None else None, ws=ws, **cfg)
+    st = rec["stats"]
+    ti = rec["tile"]
+    res = dict(q=q.float().numpy(), k=k.float().numpy(), v=v.float().numpy(),
+               leaf=np.int64(c["leaf"]), exact_leaves=np.int64(c["E"]), sink_leaves=np.int64(c["sink"]),
+               mu=_cat(st, "mu").numpy(), g8=_cat(st, "g8").numpy(), sg=_cat(st, "sg").numpy(),
+               lz=_cat(st, "lz").numpy(), vb=_cat(st, "vb").float().numpy(),
+               excl=_cat(ti, "excl").numpy().astype(np.uint8), k8=ti[0]["k8"].numpy(),
+               ks=ti[0]["ks"].numpy(), out=out.float().numpy())
+    if rec["sel"]:
+        res["sel"] = torch.cat(rec["sel"], 0).numpy()
+    if "idx" in ti[0]:
+        res["idx"] = _cat(ti, "idx").numpy().astype(np.int32)
+    if "pm" in ti[0] and c["tail"] <= 16:          # a >16-key tail is a host partial outside ws
+        pm, pl = _cat(ti, "pm").double(), _cat(ti, "pl").double()
+        mm = pm.amax(1, keepdim=True)
+        lse = (mm[:, 0] + torch.log((pl * torch.exp(pm - mm)).sum(1))).float()
+        res["lse"] = lse.reshape(-1)[: q.shape[0]].numpy()
+    if tk is not None:
+        res["tail_k"], res["tail_v"] = tk.numpy(), tv.numpy()
+    return res
+
+
+def main():
+    _shim()
+    flat = _load_reference()
+    torch.manual_seed(0)
+    for c in CASES:
+        res = run_case(flat, c)
+        path = HERE / f"{c['name']}.npz"
+        np.savez_compressed(path, **res)
+        print(f"{c['name']}: q{tuple(res['q'].shape)} k{tuple(res['k'].shape)} -> {path.name}")
+
+
+if __name__ == "__main__":
+    main()

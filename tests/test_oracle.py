@@ -1,0 +1,116 @@
+"""Pins the CPU oracle (oracle/flat_oracle.py) against fixtures recorded from the reference operator
+itself (tests/golden/make_golden.py ran h3/htrc_flat.py with PROD int8 settings)."""
+import numpy as np
+import pytest
+
+from oracle import flat_oracle as O
+
+CASES = ["base", "ragged", "sink_tail", "all_exact", "no_exact", "big_tail", "leaf32", "wide"]
+
+
+def _stages(z):
+    tail = (z["tail_k"], z["tail_v"]) if "tail_k" in z else None
+    return O.flat_attention(z["q"], z["k"], z["v"], leaf=int(z["leaf"]),
+                            exact_leaves=int(z["exact_leaves"]), sink_leaves=int(z["sink_leaves"]),
+                            tail=tail, return_stages=True), tail
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_key_pack_bit_exact(golden_cases, case):
+    z = golden_cases[case]
+    k8, ks = O.pack_k(z["k"])
+    assert np.array_equal(k8, z["k8"])
+    assert np.array_equal(ks.view(np.uint32), z["ks"].view(np.uint32))
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_centres_and_leaf_state(golden_cases, case):
+    z = golden_cases[case]
+    (out, lse, st), _ = _stages(z)
+    assert np.abs(st["mu"] - z["mu"]).max() <= 1e-7 * max(1.0, np.abs(z["mu"]).max())
+    # lz / sg / vbar: float32 products of the fp64 statistics vs the reference's float32 kernels
+    assert np.abs(st["lz"] - z["lz"]).max() < 1e-5
+    assert np.abs(st["sg"] / z["sg"] - 1).max() < 1e-5
+    assert np.abs(st["vb"] - z["vb"]).max() <= 2.0 ** -8 * max(1.0, np.abs(z["vb"]).max())
+    # int8 slope codes: identical except at most 1 LSB on the rare code sitting on a .5 boundary
+    diff = np.abs(st["g8"].astype(int) - z["g8"].astype(int))
+    assert diff.max() <= 1 and (diff > 0).mean() < 1e-4
+
+
+def test_slope_pack_bit_exact_on_identical_input():
+    rng = np.random.default_rng(5)
+    g = (rng.standard_normal((64, 128)) * rng.uniform(0.01, 3, (64, 1))).astype(np.float32)
+    g8, sg = O.pack_slope(g)
+    # the formula, written out independently in float32
+    am = np.maximum(np.abs(g).max(1), np.float32(1e-30))
+    sg2 = am * np.float32(1 / 127)
+    y = g * (np.float32(127) / am)[:, None]
+    g82 = np.trunc(np.where(y >= 0, y + np.float32(0.5), y - np.float32(0.5))).astype(np.int8)
+    assert np.array_equal(g8, g82) and np.array_equal(sg, sg2)
+    assert np.abs(g8).max() <= 127
+
+
+@pytest.mark.parametrize("case", [c for c in CASES if c != "no_exact"])
+def test_rowmax_selection_and_routing(golden_cases, case):
+    z = golden_cases[case]
+    (out, lse, st), _ = _stages(z)
+    # evaluated on the reference's own state, the selection is identical up to float32 rounding
+    q8, sq, dq8, sdq = O.query_codes(st["qt"], z["mu"])
+    sel = O.rowmax_select(dq8, sdq, z["g8"], z["sg"], z["lz"])
+    assert np.abs(sel - z["sel"]).max() < 1e-4
+    assert (st["excl"] == z["excl"]).mean() >= 0.999
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_ordered_restatement_matches_reference(golden_cases, case):
+    """With the reference's own state and block order, the restated online softmax reproduces the
+    reference's output to float32 rounding."""
+    z = golden_cases[case]
+    (out, lse, st), tail = _stages(z)
+    nt = z["mu"].shape[0]
+    idx = z["idx"] if "idx" in z else np.zeros((nt, 0), np.int32)
+    q8, sq, dq8, sdq = O.query_codes(st["qt"], z["mu"])
+    o2, l2 = O.tile_attention_ordered(st["qt"], q8, sq, dq8, sdq, z["g8"], z["sg"], z["lz"], z["vb"],
+                                      z["excl"], idx, z["k8"], z["ks"], O.bf16_round(z["v"]),
+                                      int(z["leaf"]), 1 / np.sqrt(128), tail=tail)
+    n = z["q"].shape[0]
+    assert np.abs(o2[:n] - z["out"]).max() < 2e-5
+    if "lse" in z:
+        assert np.abs(l2[:n] - z["lse"]).max() < 2e-5
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_order_free_oracle_within_tolerance(golden_cases, case):
+    """The order-free oracle (the checker of the CUDA path) agrees with the reference's output to
+    well inside the parity tolerance (out max-abs 2e-2, log-Z mean-abs 1e-3)."""
+    z = golden_cases[case]
+    (out, lse, st), _ = _stages(z)
+    assert np.abs(out - z["out"]).max() < 1e-2
+    if "lse" in z:
+        assert np.abs(lse - z["lse"]).mean() < 1e-4
+
+
+def test_all_leaves_exact_is_dequantised_softmax(golden_cases):
+    """exact_leaves >= nb: the operator is softmax attention over the INT8-dequantised logits."""
+    z = golden_cases["all_exact"]
+    (out, lse, st), _ = _stages(z)
+    n = z["q"].shape[0]
+    qd = (st["q8"].astype(np.float64) * st["sq"][..., None]).reshape(-1, 128)[:n]
+    kd = st["k8"].astype(np.float64) * st["ks"][:, None]
+    s = qd @ kd.T / np.sqrt(128)
+    m = s.max(1, keepdims=True)
+    p = np.exp(s - m)
+    ref = p @ O.bf16_round(z["v"]).astype(np.float64) / p.sum(1, keepdims=True)
+    assert np.abs(out - ref).max() < 1e-2
+    assert np.abs(lse - (m[:, 0] + np.log(p.sum(1)))).max() < 1e-4
+
+
+def test_route_sink_and_ties():
+    sel = np.array([[0.0, 5.0, 5.0, 1.0, 9.0]], np.float32)
+    idx, excl = O.route(sel, 2, sink_leaves=1)
+    assert idx.tolist() == [[0, 1, 4]]
+    assert excl.tolist() == [[1, 1, 0, 0, 1]]
+    idx, excl = O.route(sel, 0)
+    assert idx.shape == (1, 0) and excl.sum() == 0
+    idx, _ = O.route(sel, 99)
+    assert idx.tolist() == [[0, 1, 2, 3, 4]]
