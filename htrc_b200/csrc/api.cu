@@ -1,0 +1,413 @@
+// extern "C" entry points of libhtrc_flat.so (include/htrc_flat.h): argument checks, workspace
+// layout, TMA tensor maps and the launch sequence of one head of the flat HTRC operator.
+#include <cmath>
+#include <cstring>
+#include <mutex>
+
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+using namespace htrc;
+
+namespace {
+
+constexpr int kDim = 128;
+constexpr int kTile = 64;
+constexpr int kLeaf = 64;
+constexpr int64_t kMaxLeaves = 8192;
+constexpr int64_t kMaxRouted = 1536;
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+bool encoder() {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  return g_encode != nullptr;
+}
+
+struct DeviceInfo {
+  bool ok = false;
+  int sms = 148;
+};
+
+DeviceInfo device_info() {
+  static DeviceInfo cache[64];
+  static bool probed[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return DeviceInfo{};
+  if (!probed[dev]) {
+    int major = 0, sms = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev].ok = (major == 10);
+    cache[dev].sms = sms > 0 ? sms : 148;
+    probed[dev] = true;
+  }
+  return cache[dev];
+}
+
+// rank-2/3 tiled map; dims innermost first, strides in bytes for dims 1..rank-1
+bool make_map(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* base, const uint64_t* dims,
+              const uint64_t* strides, const uint32_t* box, bool swizzle128) {
+  if (!encoder() || base == nullptr) return false;
+  cuuint64_t gd[3], gs[2];
+  cuuint32_t bx[3], es[3] = {1, 1, 1};
+  for (int i = 0; i < rank; ++i) {
+    gd[i] = dims[i];
+    bx[i] = box[i];
+    if (dims[i] == 0) return false;
+  }
+  for (int i = 0; i < rank - 1; ++i) gs[i] = strides[i];
+  CUresult r = g_encode(m, dt, static_cast<cuuint32_t>(rank), const_cast<void*>(base), gd, gs, bx, es,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// [rows, 128] matrix of 1- or 2-byte elements, box of `box_rows` rows x (128 B)
+bool map_rows(CUtensorMap* m, const void* base, int64_t rows, bool bf16, int box_rows) {
+  const uint64_t dims[2] = {128, static_cast<uint64_t>(rows)};
+  const uint64_t strides[1] = {bf16 ? 256u : 128u};
+  const uint32_t box[2] = {bf16 ? 64u : 128u, static_cast<uint32_t>(box_rows)};
+  return make_map(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, base, dims, strides,
+                  box, true);
+}
+
+// [tc, nb, 128] state of 1- or 2-byte elements, box (inner, box_leaves, box_tiles)
+bool map_state(CUtensorMap* m, const void* base, int64_t tc, int64_t nb, bool bf16, int box_leaves, int box_tiles) {
+  const uint64_t es = bf16 ? 2 : 1;
+  const uint64_t dims[3] = {128, static_cast<uint64_t>(nb), static_cast<uint64_t>(tc)};
+  const uint64_t strides[2] = {128 * es, static_cast<uint64_t>(nb) * 128 * es};
+  const uint32_t box[3] = {bf16 ? 64u : 128u, static_cast<uint32_t>(box_leaves), static_cast<uint32_t>(box_tiles)};
+  return make_map(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, base, dims, strides,
+                  box, true);
+}
+
+// [tc, nb] scalars (f32 or u8) with row pitch `pitch` elements, box (box_cols, 1)
+bool map_scalars(CUtensorMap* m, const void* base, int64_t tc, int64_t nb, int64_t pitch, bool f32, int box_cols) {
+  const uint64_t es = f32 ? 4 : 1;
+  const uint64_t dims[2] = {static_cast<uint64_t>(nb), static_cast<uint64_t>(tc)};
+  const uint64_t strides[1] = {static_cast<uint64_t>(pitch) * es};
+  const uint32_t box[2] = {static_cast<uint32_t>(box_cols), 1u};
+  return make_map(m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, base, dims, strides,
+                  box, false);
+}
+
+int64_t pitch_of(int64_t nb) { return (nb + 15) / 16 * 16; }
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+struct Layout {
+  int64_t n = 0, m = 0, nt = 0, nb = 0, pitch = 0, tcm = 0, kx = 0;
+  size_t status = 0, k8 = 0, ks = 0, mu = 0, mu_hi = 0, mu_lo = 0, q8 = 0, sq = 0, dq8 = 0, sdq = 0, tail = 0;
+  size_t g8 = 0, vb = 0, sg = 0, lz = 0, sel = 0, excl = 0, idx = 0, total = 0;
+};
+
+int validate(const HtrcFlatArgs* a, bool need_ptrs) {
+  if (a == nullptr) return HTRC_ERR_ARG;
+  if (a->dim != kDim || a->tile != kTile || a->leaf != kLeaf) return HTRC_ERR_UNSUPPORTED;
+  if (a->n_queries < 1 || a->n_keys < a->leaf || a->n_keys % a->leaf) return HTRC_ERR_ARG;
+  if (a->q_dtype != HTRC_DTYPE_F32 && a->q_dtype != HTRC_DTYPE_BF16) return HTRC_ERR_ARG;
+  if (a->exact_leaves < 0 || a->sink_leaves < 0 || a->n_tail < 0) return HTRC_ERR_ARG;
+  const int64_t nb = a->n_keys / a->leaf;
+  if (nb > kMaxLeaves) return HTRC_ERR_UNSUPPORTED;
+  const int64_t sink = std::min<int64_t>(a->sink_leaves, nb);
+  const int64_t kx = std::min<int64_t>(static_cast<int64_t>(a->exact_leaves) + sink, nb);
+  if (kx > kMaxRouted) return HTRC_ERR_UNSUPPORTED;
+  if (need_ptrs) {
+    if (!a->q || !a->k || !a->v || !a->out) return HTRC_ERR_ARG;
+    if (a->n_tail > 0 && (!a->tail_k || !a->tail_v)) return HTRC_ERR_ARG;
+  }
+  return HTRC_OK;
+}
+
+Layout layout_of(const HtrcFlatArgs* a) {
+  Layout L;
+  L.n = a->n_queries;
+  L.m = a->n_keys;
+  L.nt = (L.n + kTile - 1) / kTile;
+  L.nb = L.m / kLeaf;
+  L.pitch = pitch_of(L.nb);
+  const int64_t sink = std::min<int64_t>(a->sink_leaves, L.nb);
+  L.kx = std::min<int64_t>(static_cast<int64_t>(a->exact_leaves) + sink, L.nb);
+  int64_t tcm = a->tile_chunk > 0 ? std::min<int64_t>(a->tile_chunk, L.nt) : L.nt;
+  if (tcm < L.nt) tcm = std::min<int64_t>((tcm + 1) / 2 * 2, L.nt);
+  L.tcm = tcm;
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = o;
+    o = align256(o + bytes);
+    return at;
+  };
+  L.status = take(256);
+  L.k8 = take(static_cast<size_t>(L.m) * 128);
+  L.ks = take(static_cast<size_t>(L.m) * 4);
+  L.mu = take(static_cast<size_t>(L.nt) * 128 * 4);
+  L.mu_hi = take(static_cast<size_t>(L.nt) * 128 * 2);
+  L.mu_lo = take(static_cast<size_t>(L.nt) * 128 * 2);
+  L.q8 = take(static_cast<size_t>(L.nt) * 64 * 128);
+  L.sq = take(static_cast<size_t>(L.nt) * 64 * 4);
+  L.dq8 = take(static_cast<size_t>(L.nt) * 64 * 128);
+  L.sdq = take(static_cast<size_t>(L.nt) * 64 * 4);
+  L.tail = a->n_tail > 0 ? take(static_cast<size_t>(L.n) * 130 * 4) : 0;
+  L.g8 = take(static_cast<size_t>(tcm) * L.nb * 128);
+  L.vb = take(static_cast<size_t>(tcm) * L.nb * 256);
+  L.sg = take(static_cast<size_t>(tcm) * L.pitch * 4);
+  L.lz = take(static_cast<size_t>(tcm) * L.pitch * 4);
+  L.sel = take(static_cast<size_t>(tcm) * L.pitch * 4);
+  L.excl = take(static_cast<size_t>(tcm) * L.pitch);
+  L.idx = take(static_cast<size_t>(tcm) * std::max<int64_t>(L.kx, 1) * 4);
+  L.total = o;
+  return L;
+}
+
+template <typename T>
+T* at(void* base, size_t off) {
+  return reinterpret_cast<T*>(static_cast<uint8_t*>(base) + off);
+}
+
+int check_device() { return device_info().ok ? HTRC_OK : HTRC_ERR_DEVICE; }
+
+int stats_maps(LeafStatsMaps* mp, const uint16_t* mu_hi, const uint16_t* mu_lo, int64_t nt, const uint16_t* k,
+               const uint16_t* v, int64_t m, const int8_t* g8, const uint16_t* vb, int64_t tc, int64_t nb) {
+  bool ok = map_rows(&mp->mu_hi, mu_hi, nt, true, 128) && map_rows(&mp->mu_lo, mu_lo, nt, true, 128) &&
+            map_rows(&mp->k, k, m, true, 64) && map_rows(&mp->v, v, m, true, 64) &&
+            map_state(&mp->g8, g8, tc, nb, false, 1, 128) && map_state(&mp->vb, vb, tc, nb, true, 1, 128);
+  return ok ? HTRC_OK : HTRC_ERR_CUDA;
+}
+
+int rowmax_maps(RowmaxMaps* mp, const int8_t* dq8, int64_t rows, const int8_t* g8, const float* sg, const float* lz,
+                int64_t tc, int64_t nb, int64_t pitch) {
+  bool ok = map_rows(&mp->dq8, dq8, rows, false, 64) && map_state(&mp->g8, g8, tc, nb, false, 128, 1) &&
+            map_scalars(&mp->sg, sg, tc, nb, pitch, true, 128) && map_scalars(&mp->lz, lz, tc, nb, pitch, true, 128);
+  return ok ? HTRC_OK : HTRC_ERR_CUDA;
+}
+
+int tile_maps(TileMaps* mp, const int8_t* q8, const int8_t* dq8, int64_t rows, const int8_t* g8, const uint16_t* vb,
+              const float* lz, const float* sg, const uint8_t* excl, int64_t tc, int64_t nb, int64_t pitch,
+              const int8_t* k8, const uint16_t* v, int64_t m) {
+  bool ok = map_rows(&mp->q8, q8, rows, false, 64) && map_rows(&mp->dq8, dq8, rows, false, 64) &&
+            map_state(&mp->g8, g8, tc, nb, false, 64, 1) && map_state(&mp->vb, vb, tc, nb, true, 64, 1) &&
+            map_scalars(&mp->lz, lz, tc, nb, pitch, true, 64) && map_scalars(&mp->sg, sg, tc, nb, pitch, true, 64) &&
+            map_scalars(&mp->excl, excl, tc, nb, pitch, false, 64) && map_rows(&mp->k8, k8, m, false, 64) &&
+            map_rows(&mp->v, v, m, true, 64);
+  return ok ? HTRC_OK : HTRC_ERR_CUDA;
+}
+
+float scale_of(float s) { return s > 0.f ? s : 1.0f / std::sqrt(static_cast<float>(kDim)); }
+
+}  // namespace
+
+extern "C" {
+
+int64_t htrc_leaf_pitch(int64_t nb) { return pitch_of(nb); }
+
+int htrc_flat_workspace_size(const HtrcFlatArgs* args, size_t* bytes) {
+  const int rc = validate(args, false);
+  if (rc != HTRC_OK) return rc;
+  if (bytes == nullptr) return HTRC_ERR_ARG;
+  *bytes = layout_of(args).total;
+  return HTRC_OK;
+}
+
+int htrc_flat_forward(const HtrcFlatArgs* a, htrc_stream_t stream) {
+  int rc = validate(a, true);
+  if (rc != HTRC_OK) return rc;
+  if ((rc = check_device()) != HTRC_OK) return rc;
+  const Layout L = layout_of(a);
+  if (a->workspace == nullptr || a->workspace_bytes < L.total ||
+      (reinterpret_cast<uintptr_t>(a->workspace) & 255u) != 0)
+    return HTRC_ERR_WORKSPACE;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  void* ws = a->workspace;
+  int* status = at<int>(ws, L.status);
+  const float scale = scale_of(a->scale);
+  const int nb = static_cast<int>(L.nb), kx = static_cast<int>(L.kx);
+  const int sink = static_cast<int>(std::min<int64_t>(a->sink_leaves, L.nb));
+  int8_t* k8 = at<int8_t>(ws, L.k8);
+  float* ks = at<float>(ws, L.ks);
+  int8_t* q8 = at<int8_t>(ws, L.q8);
+  int8_t* dq8 = at<int8_t>(ws, L.dq8);
+  float* sq = at<float>(ws, L.sq);
+  float* sdq = at<float>(ws, L.sdq);
+  uint16_t* mu_hi = at<uint16_t>(ws, L.mu_hi);
+  uint16_t* mu_lo = at<uint16_t>(ws, L.mu_lo);
+  int8_t* g8 = at<int8_t>(ws, L.g8);
+  uint16_t* vb = at<uint16_t>(ws, L.vb);
+  float* sg = at<float>(ws, L.sg);
+  float* lz = at<float>(ws, L.lz);
+  float* sel = at<float>(ws, L.sel);
+  uint8_t* excl = at<uint8_t>(ws, L.excl);
+  int32_t* idx = at<int32_t>(ws, L.idx);
+  float* tail = a->n_tail > 0 ? at<float>(ws, L.tail) : nullptr;
+
+  launch_pack_rows(a->k, HTRC_DTYPE_BF16, L.m, HTRC_ROUND_HALF_EVEN, k8, ks, st);
+  launch_tile_prep(a->q, a->q_dtype, L.n, at<float>(ws, L.mu), mu_hi, mu_lo, q8, sq, dq8, sdq, st);
+  if (tail) launch_tail_partial(a->q, a->q_dtype, L.n, a->tail_k, a->tail_v, a->n_tail, scale, tail, st);
+  if (cudaGetLastError() != cudaSuccess) return HTRC_ERR_CUDA;
+  const bool far = kx < nb;
+  for (int64_t t0 = 0; t0 < L.nt; t0 += L.tcm) {
+    const int64_t tc = std::min<int64_t>(L.tcm, L.nt - t0);
+    if (far) {
+      LeafStatsMaps smp;
+      if ((rc = stats_maps(&smp, mu_hi, mu_lo, L.nt, a->k, a->v, L.m, g8, vb, tc, L.nb)) != HTRC_OK) return rc;
+      if ((rc = launch_leaf_stats(smp, sg, lz, L.pitch, t0, tc, nb, scale, status, device_info().sms, st)) != HTRC_OK)
+        return rc;
+      if (kx > 0) {
+        RowmaxMaps rmp;
+        if ((rc = rowmax_maps(&rmp, dq8, L.nt * 64, g8, sg, lz, tc, L.nb, L.pitch)) != HTRC_OK) return rc;
+        if ((rc = launch_rowmax(rmp, sdq, sel, L.pitch, t0, tc, nb, status, st)) != HTRC_OK) return rc;
+      }
+    }
+    if ((rc = launch_route(sel, L.pitch, tc, nb, kx, sink, idx, excl, st)) != HTRC_OK) return rc;
+    TileMaps tmp;
+    if ((rc = tile_maps(&tmp, q8, dq8, L.nt * 64, g8, vb, lz, sg, excl, tc, L.nb, L.pitch, k8, a->v, L.m)) != HTRC_OK)
+      return rc;
+    if ((rc = launch_tile_attention(tmp, sq, sdq, ks, idx, kx, nb, L.n, t0, tc, scale, tail, a->out, a->lse, status,
+                                    st)) != HTRC_OK)
+      return rc;
+  }
+  return HTRC_OK;
+}
+
+int htrc_flat_status(void* workspace, int32_t* status_out, htrc_stream_t stream) {
+  if (workspace == nullptr || status_out == nullptr) return HTRC_ERR_ARG;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  int32_t* dev = static_cast<int32_t*>(workspace);   // the status word is the first field of the layout
+  if (cudaMemcpyAsync(status_out, dev, 4, cudaMemcpyDeviceToHost, st) != cudaSuccess) return HTRC_ERR_CUDA;
+  if (cudaStreamSynchronize(st) != cudaSuccess) return HTRC_ERR_CUDA;
+  if (cudaMemsetAsync(dev, 0, 4, st) != cudaSuccess) return HTRC_ERR_CUDA;
+  return HTRC_OK;
+}
+
+int htrc_pack_int8(const void* x, int32_t dtype, int64_t rows, int32_t dim, int32_t rounding, int8_t* x8,
+                   float* scale, htrc_stream_t stream) {
+  if (!x || !x8 || !scale || rows < 1) return HTRC_ERR_ARG;
+  if (dim != kDim) return HTRC_ERR_UNSUPPORTED;
+  if (dtype != HTRC_DTYPE_F32 && dtype != HTRC_DTYPE_BF16) return HTRC_ERR_ARG;
+  if (rounding != HTRC_ROUND_HALF_EVEN && rounding != HTRC_ROUND_HALF_AWAY) return HTRC_ERR_ARG;
+  int rc = check_device();
+  if (rc != HTRC_OK) return rc;
+  launch_pack_rows(x, dtype, rows, rounding, x8, scale, reinterpret_cast<cudaStream_t>(stream));
+  return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
+}
+
+int htrc_tile_prep(const void* q, int32_t q_dtype, int64_t n_queries, int32_t dim, int32_t tile, float* mu,
+                   uint16_t* mu_hi, uint16_t* mu_lo, int8_t* q8, float* sq, int8_t* dq8, float* sdq,
+                   htrc_stream_t stream) {
+  if (!q || !mu || !mu_hi || !mu_lo || !q8 || !sq || !dq8 || !sdq || n_queries < 1) return HTRC_ERR_ARG;
+  if (dim != kDim || tile != kTile) return HTRC_ERR_UNSUPPORTED;
+  if (q_dtype != HTRC_DTYPE_F32 && q_dtype != HTRC_DTYPE_BF16) return HTRC_ERR_ARG;
+  int rc = check_device();
+  if (rc != HTRC_OK) return rc;
+  launch_tile_prep(q, q_dtype, n_queries, mu, mu_hi, mu_lo, q8, sq, dq8, sdq, reinterpret_cast<cudaStream_t>(stream));
+  return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
+}
+
+int htrc_leaf_stats(const uint16_t* mu_hi, const uint16_t* mu_lo, int64_t nt, int64_t t0, int64_t tc, const uint16_t* k,
+                    const uint16_t* v, int64_t n_keys, int32_t dim, int32_t leaf, float scale, int8_t* g8, float* sg,
+                    float* lz, uint16_t* vb, int32_t* status, htrc_stream_t stream) {
+  if (!mu_hi || !mu_lo || !k || !v || !g8 || !sg || !lz || !vb) return HTRC_ERR_ARG;
+  if (dim != kDim || leaf != kLeaf) return HTRC_ERR_UNSUPPORTED;
+  if (nt < 1 || t0 < 0 || tc < 1 || t0 + tc > nt || n_keys < leaf || n_keys % leaf) return HTRC_ERR_ARG;
+  const int64_t nb = n_keys / leaf;
+  if (nb > kMaxLeaves) return HTRC_ERR_UNSUPPORTED;
+  int rc = check_device();
+  if (rc != HTRC_OK) return rc;
+  LeafStatsMaps mp;
+  if ((rc = stats_maps(&mp, mu_hi, mu_lo, nt, k, v, n_keys, g8, vb, tc, nb)) != HTRC_OK) return rc;
+  return launch_leaf_stats(mp, sg, lz, pitch_of(nb), t0, tc, static_cast<int>(nb), scale_of(scale), status,
+                           device_info().sms, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int htrc_rowmax_select(const int8_t* dq8, const float* sdq, int64_t t0, int64_t tc, const int8_t* g8, const float* sg,
+                       const float* lz, int64_t nb, int32_t dim, float* sel, int32_t* status, htrc_stream_t stream) {
+  if (!dq8 || !sdq || !g8 || !sg || !lz || !sel || t0 < 0 || tc < 1 || nb < 1) return HTRC_ERR_ARG;
+  if (dim != kDim) return HTRC_ERR_UNSUPPORTED;
+  if (nb > kMaxLeaves) return HTRC_ERR_UNSUPPORTED;
+  int rc = check_device();
+  if (rc != HTRC_OK) return rc;
+  RowmaxMaps mp;
+  if ((rc = rowmax_maps(&mp, dq8, (t0 + tc) * 64, g8, sg, lz, tc, nb, pitch_of(nb))) != HTRC_OK) return rc;
+  return launch_rowmax(mp, sdq, sel, pitch_of(nb), t0, tc, static_cast<int>(nb), status,
+                       reinterpret_cast<cudaStream_t>(stream));
+}
+
+int htrc_route(const float* sel, int64_t tc, int64_t nb, int32_t exact_leaves, int32_t sink_leaves, int32_t* idx,
+               uint8_t* excl, htrc_stream_t stream) {
+  if (!excl || tc < 1 || nb < 1 || exact_leaves < 0 || sink_leaves < 0) return HTRC_ERR_ARG;
+  if (nb > kMaxLeaves) return HTRC_ERR_UNSUPPORTED;
+  const int64_t sink = std::min<int64_t>(sink_leaves, nb);
+  const int64_t kx = std::min<int64_t>(static_cast<int64_t>(exact_leaves) + sink, nb);
+  if (kx > 0 && kx < nb && !sel) return HTRC_ERR_ARG;
+  if (kx > 0 && !idx) return HTRC_ERR_ARG;
+  int rc = check_device();
+  if (rc != HTRC_OK) return rc;
+  return launch_route(sel, pitch_of(nb), tc, static_cast<int>(nb), static_cast<int>(kx), static_cast<int>(sink), idx,
+                      excl, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int htrc_tile_attention(const int8_t* q8, const float* sq, const int8_t* dq8, const float* sdq, int64_t n_queries,
+                        int64_t t0, int64_t tc, const int8_t* g8, const float* sg, const float* lz, const uint16_t* vb,
+                        const uint8_t* excl, const int32_t* idx, int32_t kx, int64_t nb, const int8_t* k8,
+                        const float* ks, const uint16_t* v, int64_t n_keys, int32_t dim, int32_t leaf, float scale,
+                        const float* tail_part, float* out, float* lse, int32_t* status, htrc_stream_t stream) {
+  if (!q8 || !sq || !dq8 || !sdq || !k8 || !ks || !v || !out || n_queries < 1 || t0 < 0 || tc < 1) return HTRC_ERR_ARG;
+  if (dim != kDim || leaf != kLeaf) return HTRC_ERR_UNSUPPORTED;
+  if (nb < 1 || n_keys != nb * leaf || kx < 0 || kx > nb) return HTRC_ERR_ARG;
+  if (kx > kMaxRouted || nb > kMaxLeaves) return HTRC_ERR_UNSUPPORTED;
+  if (kx < nb && (!g8 || !sg || !lz || !vb || !excl)) return HTRC_ERR_ARG;
+  if (kx > 0 && !idx) return HTRC_ERR_ARG;
+  const int64_t nt = (n_queries + 63) / 64;
+  if (t0 + tc > nt) return HTRC_ERR_ARG;
+  int rc = check_device();
+  if (rc != HTRC_OK) return rc;
+  // unused state maps (everything routed) still need a valid address: point them at the keys
+  const void* g8p = g8 ? static_cast<const void*>(g8) : static_cast<const void*>(k8);
+  const void* vbp = vb ? static_cast<const void*>(vb) : static_cast<const void*>(v);
+  const void* lzp = lz ? static_cast<const void*>(lz) : static_cast<const void*>(ks);
+  const void* sgp = sg ? static_cast<const void*>(sg) : static_cast<const void*>(ks);
+  const void* exp_ = excl ? static_cast<const void*>(excl) : static_cast<const void*>(k8);
+  TileMaps mp;
+  if ((rc = tile_maps(&mp, q8, dq8, nt * 64, static_cast<const int8_t*>(g8p), static_cast<const uint16_t*>(vbp),
+                      static_cast<const float*>(lzp), static_cast<const float*>(sgp),
+                      static_cast<const uint8_t*>(exp_), tc, nb, pitch_of(nb), k8, v, n_keys)) != HTRC_OK)
+    return rc;
+  return launch_tile_attention(mp, sq, sdq, ks, idx, kx, static_cast<int>(nb), n_queries, t0, tc, scale_of(scale),
+                               tail_part, out, lse, status, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int htrc_tail_partial(const void* q, int32_t q_dtype, int64_t n_queries, int32_t dim, const float* tail_k,
+                      const float* tail_v, int32_t n_tail, float scale, float* tail_part, htrc_stream_t stream) {
+  if (!q || !tail_k || !tail_v || !tail_part || n_queries < 1 || n_tail < 1) return HTRC_ERR_ARG;
+  if (dim != kDim) return HTRC_ERR_UNSUPPORTED;
+  if (q_dtype != HTRC_DTYPE_F32 && q_dtype != HTRC_DTYPE_BF16) return HTRC_ERR_ARG;
+  int rc = check_device();
+  if (rc != HTRC_OK) return rc;
+  launch_tail_partial(q, q_dtype, n_queries, tail_k, tail_v, n_tail, scale_of(scale), tail_part,
+                      reinterpret_cast<cudaStream_t>(stream));
+  return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
+}
+
+const char* htrc_strerror(int code) {
+  switch (code) {
+    case HTRC_OK: return "ok";
+    case HTRC_ERR_ARG: return "invalid argument";
+    case HTRC_ERR_UNSUPPORTED: return "unsupported configuration (needs dim 128, tile 64, leaf 64, <= 8192 leaves, <= 1536 routed leaves)";
+    case HTRC_ERR_WORKSPACE: return "workspace missing, misaligned or too small";
+    case HTRC_ERR_CUDA: return "CUDA runtime error";
+    case HTRC_ERR_DEVICE: return "no sm_100 device or device-side failure";
+    default: return "unknown error";
+  }
+}
+
+}  // extern "C"

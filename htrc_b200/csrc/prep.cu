@@ -1,0 +1,231 @@
+// HBM-bound preparation kernels: INT8 row packing of keys (and of any [rows, 128] matrix), tile
+// centres + query codes, and the exact tail-key partial.
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace htrc {
+
+namespace {
+constexpr float kInv127 = 1.0f / 127.0f;  // float32 of the reference's (1.0 / 127.0)
+
+template <typename T>
+__device__ __forceinline__ void load4(const T* p, float (&v)[4]);
+template <>
+__device__ __forceinline__ void load4<float>(const float* p, float (&v)[4]) {
+  float4 x = __ldg(reinterpret_cast<const float4*>(p));
+  v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+}
+template <>
+__device__ __forceinline__ void load4<uint16_t>(const uint16_t* p, float (&v)[4]) {
+  uint2 x = __ldg(reinterpret_cast<const uint2*>(p));
+  v[0] = __uint_as_float(x.x << 16); v[1] = __uint_as_float(x.x & 0xFFFF0000u);
+  v[2] = __uint_as_float(x.y << 16); v[3] = __uint_as_float(x.y & 0xFFFF0000u);
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ uint32_t pack_i8x4(int a, int b, int c, int d) {
+  return (static_cast<uint32_t>(a) & 0xFFu) | ((static_cast<uint32_t>(b) & 0xFFu) << 8) |
+         ((static_cast<uint32_t>(c) & 0xFFu) << 16) | ((static_cast<uint32_t>(d) & 0xFFu) << 24);
+}
+
+// x8 codes of 4 values given the row scale s; ROUND 0 = half-even + clamp, 1 = half-away
+template <int ROUND>
+__device__ __forceinline__ uint32_t quant4(const float (&v)[4], float s) {
+  int c[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float y = __fdiv_rn(v[i], s);
+    if (ROUND == 0) {
+      int r = static_cast<int>(rintf(y));
+      c[i] = max(-127, min(127, r));
+    } else {
+      c[i] = round_half_away_i8(y);
+    }
+  }
+  return pack_i8x4(c[0], c[1], c[2], c[3]);
+}
+}  // namespace
+
+// One warp per row of 128 values; each lane owns 4 consecutive values.
+template <typename T, int ROUND>
+__global__ void __launch_bounds__(256) pack_rows_kernel(const T* __restrict__ x, int64_t rows,
+                                                        int8_t* __restrict__ x8, float* __restrict__ scale) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  float v[4];
+  load4<T>(x + row * 128 + lane * 4, v);
+  float am = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+  am = warp_max(am);
+  const float s = fmaxf(__fmul_rn(am, kInv127), 1e-20f);
+  reinterpret_cast<uint32_t*>(x8 + row * 128)[lane] = quant4<ROUND>(v, s);
+  if (lane == 0) scale[row] = s;
+}
+
+void launch_pack_rows(const void* x, int dtype, int64_t rows, int rounding, int8_t* x8, float* scale,
+                      cudaStream_t st) {
+  const unsigned grid = static_cast<unsigned>((rows + 7) / 8);
+  if (dtype == HTRC_DTYPE_BF16) {
+    if (rounding == HTRC_ROUND_HALF_EVEN)
+      pack_rows_kernel<uint16_t, 0><<<grid, 256, 0, st>>>(static_cast<const uint16_t*>(x), rows, x8, scale);
+    else
+      pack_rows_kernel<uint16_t, 1><<<grid, 256, 0, st>>>(static_cast<const uint16_t*>(x), rows, x8, scale);
+  } else {
+    if (rounding == HTRC_ROUND_HALF_EVEN)
+      pack_rows_kernel<float, 0><<<grid, 256, 0, st>>>(static_cast<const float*>(x), rows, x8, scale);
+    else
+      pack_rows_kernel<float, 1><<<grid, 256, 0, st>>>(static_cast<const float*>(x), rows, x8, scale);
+  }
+}
+
+// One CTA (4 warps) per tile of 64 query rows.  Rows past n repeat the last query row (the
+// reference pads the last tile that way, h3/htrc_flat.py:150-152).
+template <typename T>
+__global__ void __launch_bounds__(128) tile_prep_kernel(const T* __restrict__ q, int64_t n, float* __restrict__ mu,
+                                                        uint16_t* __restrict__ mu_hi, uint16_t* __restrict__ mu_lo,
+                                                        int8_t* __restrict__ q8, float* __restrict__ sq,
+                                                        int8_t* __restrict__ dq8, float* __restrict__ sdq) {
+  __shared__ float qs[64][129];
+  __shared__ float mus[128];
+  const int t = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int64_t r0 = static_cast<int64_t>(t) * 64;
+  const int nreal = static_cast<int>(n - r0 < 64 ? n - r0 : 64);
+  // stage the tile: warp w loads rows w, w+4, ...; lane owns 4 columns
+  const int warp = tid >> 5, lane = tid & 31;
+  for (int r = warp; r < 64; r += 4) {
+    const int64_t gr = (r0 + r < n - 1) ? r0 + r : n - 1;
+    float v[4];
+    load4<T>(q + gr * 128 + lane * 4, v);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) qs[r][lane * 4 + i] = v[i];
+  }
+  __syncthreads();
+  // centre: float64 sum over the real rows, divided and rounded once
+  {
+    double s = 0.0;
+    for (int r = 0; r < nreal; ++r) s += static_cast<double>(qs[r][tid]);
+    const float m = static_cast<float>(s / static_cast<double>(nreal));
+    mus[tid] = m;
+    mu[static_cast<int64_t>(t) * 128 + tid] = m;
+    const __nv_bfloat16 hi = __float2bfloat16_rn(m);
+    const __nv_bfloat16 lo = __float2bfloat16_rn(__fsub_rn(m, __bfloat162float(hi)));
+    mu_hi[static_cast<int64_t>(t) * 128 + tid] = __bfloat16_as_ushort(hi);
+    mu_lo[static_cast<int64_t>(t) * 128 + tid] = __bfloat16_as_ushort(lo);
+  }
+  __syncthreads();
+  float m4[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) m4[i] = mus[lane * 4 + i];
+  for (int r = warp; r < 64; r += 4) {
+    float v[4], d[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      v[i] = qs[r][lane * 4 + i];
+      d[i] = __fsub_rn(v[i], m4[i]);
+    }
+    float aq = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+    float ad = fmaxf(fmaxf(fabsf(d[0]), fabsf(d[1])), fmaxf(fabsf(d[2]), fabsf(d[3])));
+    aq = warp_max(aq);
+    ad = warp_max(ad);
+    const float s_q = fmaxf(__fmul_rn(aq, kInv127), 1e-20f);
+    const float s_d = fmaxf(__fmul_rn(ad, kInv127), 1e-20f);
+    const int64_t gr = r0 + r;
+    reinterpret_cast<uint32_t*>(q8 + gr * 128)[lane] = quant4<1>(v, s_q);
+    reinterpret_cast<uint32_t*>(dq8 + gr * 128)[lane] = quant4<1>(d, s_d);
+    if (lane == 0) {
+      sq[gr] = s_q;
+      sdq[gr] = s_d;
+    }
+  }
+}
+
+void launch_tile_prep(const void* q, int dtype, int64_t n, float* mu, uint16_t* mu_hi, uint16_t* mu_lo, int8_t* q8,
+                      float* sq, int8_t* dq8, float* sdq, cudaStream_t st) {
+  const unsigned nt = static_cast<unsigned>((n + 63) / 64);
+  if (dtype == HTRC_DTYPE_BF16)
+    tile_prep_kernel<uint16_t><<<nt, 128, 0, st>>>(static_cast<const uint16_t*>(q), n, mu, mu_hi, mu_lo, q8, sq,
+                                                    dq8, sdq);
+  else
+    tile_prep_kernel<float><<<nt, 128, 0, st>>>(static_cast<const float*>(q), n, mu, mu_hi, mu_lo, q8, sq, dq8, sdq);
+}
+
+// Exact partial of each query row against the n_tail tail keys: one warp per row.
+//   n_tail <= 16: logits from bf16-rounded q and keys, P rounded to bf16 for the value product
+//                 (h3/htrc_flat_triton.py:187-207); otherwise float32 (h3/htrc_flat_triton.py:381-388).
+// Output row: acc[128], m, l  (natural-log units).
+template <typename T>
+__global__ void __launch_bounds__(256) tail_partial_kernel(const T* __restrict__ q, int64_t n,
+                                                           const float* __restrict__ tk, const float* __restrict__ tv,
+                                                           int n_tail, float scale, float* __restrict__ part) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (row >= n) return;
+  const bool small = n_tail <= 16;
+  float qv[4];
+  load4<T>(q + row * 128 + lane * 4, qv);
+  if (small) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) qv[i] = __bfloat162float(__float2bfloat16_rn(qv[i]));
+  }
+  float m = -INFINITY;
+  for (int j = 0; j < n_tail; ++j) {
+    float kv[4];
+    load4<float>(tk + static_cast<int64_t>(j) * 128 + lane * 4, kv);
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float kk = small ? __bfloat162float(__float2bfloat16_rn(kv[i])) : kv[i];
+      s = fmaf(qv[i], kk, s);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    m = fmaxf(m, s * scale);
+  }
+  float l = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int j = 0; j < n_tail; ++j) {
+    float kv[4], vv[4];
+    load4<float>(tk + static_cast<int64_t>(j) * 128 + lane * 4, kv);
+    load4<float>(tv + static_cast<int64_t>(j) * 128 + lane * 4, vv);
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float kk = small ? __bfloat162float(__float2bfloat16_rn(kv[i])) : kv[i];
+      s = fmaf(qv[i], kk, s);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const float p = expf(s * scale - m);
+    l += p;
+    const float pv = small ? __bfloat162float(__float2bfloat16_rn(p)) : p;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float vvv = small ? __bfloat162float(__float2bfloat16_rn(vv[i])) : vv[i];
+      acc[i] = fmaf(pv, vvv, acc[i]);
+    }
+  }
+  float* o = part + row * 130;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) o[lane * 4 + i] = acc[i];
+  if (lane == 0) {
+    o[128] = m;
+    o[129] = l;
+  }
+}
+
+void launch_tail_partial(const void* q, int dtype, int64_t n, const float* tk, const float* tv, int n_tail, float scale,
+                         float* part, cudaStream_t st) {
+  const unsigned grid = static_cast<unsigned>((n + 7) / 8);
+  if (dtype == HTRC_DTYPE_BF16)
+    tail_partial_kernel<uint16_t><<<grid, 256, 0, st>>>(static_cast<const uint16_t*>(q), n, tk, tv, n_tail, scale,
+                                                        part);
+  else
+    tail_partial_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(q), n, tk, tv, n_tail, scale, part);
+}
+
+}  // namespace htrc

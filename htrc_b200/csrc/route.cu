@@ -1,0 +1,136 @@
+// Per-tile top-E near-leaf routing (h3/htrc_flat.py:232-233, :250-265): the first `sink` leaves are
+// forced (selection +inf), then the kx largest selections.  One CTA of 256 threads per tile: an
+// MSB-first 8-bit radix select of the kx-th largest order-preserving key, ties at the threshold
+// broken towards the lower leaf index, then an order-preserving compaction, so idx comes out in
+// ascending leaf order.  No host synchronisation (fixed-size output).
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace htrc {
+
+namespace {
+constexpr int kThreads = 256;
+constexpr int kMaxLeaves = 8192;
+
+__device__ __forceinline__ uint32_t order_key(float f) {
+  const uint32_t b = __float_as_uint(f);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+// exclusive block-wide prefix sum of one int per thread; returns the total in *total
+__device__ __forceinline__ int block_exclusive_scan(int v, int* scratch, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) scratch[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int w = lane < kThreads / 32 ? scratch[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    if (lane < kThreads / 32) scratch[lane] = w;
+  }
+  __syncthreads();
+  const int base = warp ? scratch[warp - 1] : 0;
+  *total = scratch[kThreads / 32 - 1];
+  __syncthreads();
+  return base + x - v;
+}
+}  // namespace
+
+__global__ void __launch_bounds__(kThreads)
+    route_kernel(const float* __restrict__ sel, int64_t pitch, int nb, int kx, int sink, int32_t* __restrict__ idx,
+                 uint8_t* __restrict__ excl) {
+  __shared__ uint32_t keys[kMaxLeaves];
+  __shared__ int hist[256];
+  __shared__ int scratch[32];
+  __shared__ uint32_t s_prefix;
+  __shared__ int s_remaining;
+  const int t = blockIdx.x;
+  const int tid = threadIdx.x;
+  uint8_t* ex = excl + static_cast<int64_t>(t) * pitch;
+  int32_t* ix = idx + static_cast<int64_t>(t) * kx;
+
+  if (kx <= 0 || kx >= nb) {
+    // nothing routed / everything routed: no selection needed
+    for (int l = tid; l < static_cast<int>(pitch); l += kThreads) ex[l] = (kx > 0 && l < nb) ? 1 : 0;
+    if (kx > 0)
+      for (int l = tid; l < kx; l += kThreads) ix[l] = l;
+    return;
+  }
+  const float* row = sel + static_cast<int64_t>(t) * pitch;
+  for (int l = tid; l < nb; l += kThreads) keys[l] = l < sink ? 0xFFFFFFFFu : order_key(row[l]);
+  if (tid == 0) {
+    s_prefix = 0;
+    s_remaining = kx;
+  }
+  __syncthreads();
+  uint32_t mask = 0;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int i = tid; i < 256; i += kThreads) hist[i] = 0;
+    __syncthreads();
+    const uint32_t prefix = s_prefix;
+    for (int l = tid; l < nb; l += kThreads) {
+      const uint32_t k = keys[l];
+      if ((k & mask) == prefix) atomicAdd(&hist[(k >> shift) & 0xFF], 1);
+    }
+    __syncthreads();
+    if (tid == 0) {
+      int rem = s_remaining, above = 0, d = 255;
+      for (; d > 0; --d) {
+        if (above + hist[d] >= rem) break;
+        above += hist[d];
+      }
+      s_remaining = rem - above;
+      s_prefix = prefix | (static_cast<uint32_t>(d) << shift);
+    }
+    mask |= 0xFFu << shift;
+    __syncthreads();
+  }
+  const uint32_t thr = s_prefix;
+  const int need_eq = s_remaining;   // keys equal to thr that are taken (lowest leaf indices first)
+  // each thread owns a contiguous chunk of leaves so that the compaction keeps leaf order
+  const int chunk = (nb + kThreads - 1) / kThreads;
+  const int lo = min(nb, tid * chunk), hi = min(nb, lo + chunk);
+  int n_eq = 0;
+  for (int l = lo; l < hi; ++l) n_eq += keys[l] == thr;
+  int tot;
+  int eq_before = block_exclusive_scan(n_eq, scratch, &tot);
+  int n_take = 0;
+  {
+    int e = eq_before;
+    for (int l = lo; l < hi; ++l) {
+      const uint32_t k = keys[l];
+      const bool take = k > thr || (k == thr && e++ < need_eq);
+      n_take += take;
+    }
+  }
+  int pos = block_exclusive_scan(n_take, scratch, &tot);
+  {
+    int e = eq_before;
+    for (int l = lo; l < hi; ++l) {
+      const uint32_t k = keys[l];
+      const bool take = k > thr || (k == thr && e++ < need_eq);
+      ex[l] = take ? 1 : 0;
+      if (take && pos < kx) ix[pos++] = l;
+    }
+  }
+  for (int l = nb + tid; l < static_cast<int>(pitch); l += kThreads) ex[l] = 0;
+}
+
+int launch_route(const float* sel, int64_t pitch, int64_t tc, int nb, int kx, int sink, int32_t* idx, uint8_t* excl,
+                 cudaStream_t st) {
+  if (nb > kMaxLeaves) return HTRC_ERR_UNSUPPORTED;
+  if (tc <= 0) return HTRC_OK;
+  route_kernel<<<static_cast<unsigned>(tc), kThreads, 0, st>>>(sel, pitch, nb, kx, sink, idx, excl);
+  return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
+}
+
+}  // namespace htrc

@@ -1,0 +1,160 @@
+// Row-max near-leaf selection on tcgen05 INT8 tensor cores.
+//
+// SEL[t, l] = max_r (dq8_r . g8_{t,l}) * (sdq_r * sg_{t,l}) + lz_{t,l}     (h3/htrc_flat_triton.py:214-254)
+//
+// Computed transposed so the maximum over the 64 tile rows stays inside one thread: per block of 128
+// leaves, C = G8_block (M=128 leaves, K=128) x DQ8_tile^T (N=64 rows) into TMEM (int32); the thread
+// owning TMEM lane l reduces its 64 columns.  One CTA per tile; warp 0 loads (TMA), warp 1 issues
+// MMAs, warps 2-5 reduce.  The state is streamed once (HBM-bound).
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace htrc {
+
+namespace {
+constexpr int kStages = 3;
+constexpr uint32_t kBlkBytes = 128 * 128;          // 128 leaves x 128 B of g8
+constexpr uint32_t kParBytes = 2 * 128 * 4;         // sg[128], lz[128]
+constexpr uint32_t kStageBytes = kBlkBytes + kParBytes;
+constexpr uint32_t kOffDq = 0;                      // 64 rows x 128 B
+constexpr uint32_t kOffSdq = kOffDq + 64 * 128;     // 64 floats
+constexpr uint32_t kOffStage = kOffSdq + 1024;      // 1024-aligned
+constexpr uint32_t kOffBar = kOffStage + kStages * ((kStageBytes + 1023) / 1024 * 1024);
+constexpr uint32_t kStageStride = (kStageBytes + 1023) / 1024 * 1024;
+constexpr uint32_t kSmemBytes = kOffBar + 256 + 1024;
+constexpr uint32_t kTmemCols = 128;
+
+struct Bars {
+  uint64_t dq_full;
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint32_t tmem_base;
+  int abort_flag;
+};
+}  // namespace
+
+__global__ void __launch_bounds__(192)
+    rowmax_kernel(const __grid_constant__ CUtensorMap tm_dq8, const __grid_constant__ CUtensorMap tm_g8,
+                  const __grid_constant__ CUtensorMap tm_sg, const __grid_constant__ CUtensorMap tm_lz,
+                  const float* __restrict__ sdq, float* __restrict__ sel, int64_t pitch, int64_t t0, int nb,
+                  int* status) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Bars* bars = reinterpret_cast<Bars*>(smem + kOffBar);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tloc = blockIdx.x;
+  const int64_t tg = t0 + tloc;
+  const int nblk = (nb + 127) / 128;
+  volatile int* abort_flag = &bars->abort_flag;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->dq_full, 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], 1 + 128);   // MMA commit + the 128 reducing threads (they read sg/lz)
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bars->acc_full[b], 1);
+      mbar_init(&bars->acc_empty[b], 128);
+    }
+    bars->abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(&bars->tmem_base, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t pol_stream = policy_evict_first();
+      mbar_arrive_expect_tx(&bars->dq_full, 64 * 128 + 256);
+      tma_load_2d(smem + kOffDq, &tm_dq8, &bars->dq_full, 0, static_cast<int>(tg * 64), pol_stream);
+      bulk_load(smem + kOffSdq, sdq + tg * 64, 256, &bars->dq_full, pol_stream);
+      for (int j = 0; j < nblk; ++j) {
+        const int s = j % kStages;
+        if (j >= kStages && !mbar_wait(&bars->empty[s], ((j / kStages) - 1) & 1, status, abort_flag)) break;
+        uint8_t* st = smem + kOffStage + s * kStageStride;
+        mbar_arrive_expect_tx(&bars->full[s], kStageBytes);
+        tma_load_3d(st, &tm_g8, &bars->full[s], 0, j * 128, tloc, pol_stream);
+        tma_load_2d(st + kBlkBytes, &tm_sg, &bars->full[s], j * 128, tloc, pol_stream);
+        tma_load_2d(st + kBlkBytes + 512, &tm_lz, &bars->full[s], j * 128, tloc, pol_stream);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_i8(128, 64);
+      const uint32_t dq = smem_u32(smem + kOffDq);
+      bool ok = mbar_wait(&bars->dq_full, 0, status, abort_flag);
+      for (int j = 0; ok && j < nblk; ++j) {
+        const int s = j % kStages, b = j & 1;
+        if (!mbar_wait(&bars->full[s], (j / kStages) & 1, status, abort_flag)) break;
+        if (j >= 2 && !mbar_wait(&bars->acc_empty[b], ((j >> 1) - 1) & 1, status, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t gst = smem_u32(smem + kOffStage + s * kStageStride);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          mma_i8(tmem + 64 * b, sw128_desc(gst + kk * 32, 16, 1024), sw128_desc(dq + kk * 32, 16, 1024), idesc, kk != 0);
+        }
+        mma_commit(&bars->acc_full[b]);
+        mma_commit(&bars->empty[s]);
+      }
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;                 // leaf within the block
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const float* sdq_s = reinterpret_cast<const float*>(smem + kOffSdq);
+    if (mbar_wait(&bars->dq_full, 0, status, abort_flag)) {
+      for (int j = 0; j < nblk; ++j) {
+        const int s = j % kStages, b = j & 1;
+        if (!mbar_wait(&bars->acc_full[b], (j >> 1) & 1, status, abort_flag)) break;
+        if (!mbar_wait(&bars->full[s], (j / kStages) & 1, status, abort_flag)) break;
+        __syncwarp();
+        tc_fence_after();
+        uint32_t d0[32], d1[32];
+        tmem_ld32(tmem + lane_base + 64 * b, d0);
+        tmem_ld32(tmem + lane_base + 64 * b + 32, d1);
+        tmem_ld_wait();
+        tc_fence_before();
+        mbar_arrive(&bars->acc_empty[b]);
+        const uint8_t* st = smem + kOffStage + s * kStageStride;
+        const float sgl = reinterpret_cast<const float*>(st + kBlkBytes)[r];
+        const float lzl = reinterpret_cast<const float*>(st + kBlkBytes + 512)[r];
+        mbar_arrive(&bars->empty[s]);
+        float best = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          best = fmaxf(best, __fmul_rn(static_cast<float>(static_cast<int>(d0[i])), __fmul_rn(sdq_s[i], sgl)));
+          best = fmaxf(best, __fmul_rn(static_cast<float>(static_cast<int>(d1[i])), __fmul_rn(sdq_s[32 + i], sgl)));
+        }
+        const int leaf = j * 128 + r;
+        if (leaf < nb) sel[static_cast<int64_t>(tloc) * pitch + leaf] = __fadd_rn(best, lzl);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+}
+
+int launch_rowmax(const RowmaxMaps& maps, const float* sdq, float* sel, int64_t pitch, int64_t t0, int64_t tc, int nb,
+                  int* status, cudaStream_t st) {
+  static bool attr_done[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_done[dev]) {
+    if (cudaFuncSetAttribute(rowmax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess)
+      return HTRC_ERR_CUDA;
+    attr_done[dev] = true;
+  }
+  rowmax_kernel<<<static_cast<unsigned>(tc), 192, kSmemBytes, st>>>(maps.dq8, maps.g8, maps.sg, maps.lz, sdq, sel,
+                                                                     pitch, t0, nb, status);
+  return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
+}
+
+}  // namespace htrc

@@ -1,0 +1,269 @@
+"""Flat (tree-free) HTRC attention on B200: the host side of the operator.
+
+Mirrors the call surface of the reference's h3/htrc_flat.py (``flat_attention``, ``PROD``,
+``flat_attention_prod``) for its production path -- ``backend="triton", store="int8", dot="bf16",
+select="max", curvature="lin"`` (htrc_flat.py:99-139, :181-276, :391-399) -- and runs it through the
+C-ABI library libhtrc_flat.so (hand-written sm_100a kernels).  There is no other backend and no CPU
+fallback: configurations the kernels do not implement raise ``NotImplementedError`` and argument
+errors raise the reference's ``ValueError``s.
+
+Additions over the reference: ``return_lse=True`` also returns the log-partition per query
+(logit units, scale * q.k), and ``backend`` accepts "cuda"/"b200" as names of the same path.
+"""
+from __future__ import annotations
+
+import math
+import time
+
+import torch
+
+from . import _lib
+from ._lib import check, lib, ptr, stream_ptr
+
+DIM, TILE, LEAF = 128, 64, 64
+
+PROD = dict(tile=64, exact_leaves=256, tile_chunk=128, backend="triton", precision="tf32",
+            store="int8", dot="bf16", splits=4, kern=dict(tile_warps=4, tile_bn=64, tile_stages=2))
+"""The reference's production configuration (h3/htrc_flat.py:391-392).  The launch knobs in ``kern``
+and ``splits`` are accepted and ignored: the kernels here have their own fixed shapes."""
+
+_BACKENDS = ("triton", "cuda", "b200")
+
+
+def leaf_pitch(nb: int) -> int:
+    return int(lib().htrc_leaf_pitch(int(nb)))
+
+
+class _Tick:
+    """Stage timer with the reference's semantics (h3/htrc_flat.py:32-44): when ``prof`` is a dict,
+    synchronise and accumulate milliseconds per stage name."""
+
+    def __init__(self, prof):
+        self.prof = prof
+        if prof is not None:
+            torch.cuda.synchronize()
+            self.t = time.perf_counter()
+
+    def __call__(self, name):
+        if self.prof is not None:
+            torch.cuda.synchronize()
+            t = time.perf_counter()
+            self.prof[name] = self.prof.get(name, 0.0) + 1e3 * (t - self.t)
+            self.t = t
+
+
+def _check_args(q, k, v, tile, exact_leaves, order, curvature, leaf, select, backend, store, dot,
+                sel_stride, quant, sink_leaves, tail):
+    """The reference's argument errors (h3/htrc_flat.py:118-132, :187-212), then what this library
+    implements."""
+    if backend not in _BACKENDS and backend != "torch":
+        raise ValueError(f"unknown backend {backend}")
+    if backend == "torch":
+        if sink_leaves or tail is not None:
+            raise ValueError("sink_leaves / tail are supported by the triton backend only")
+        if select not in ("max", "bound"):
+            raise ValueError("select must be max or bound")
+        if order not in ("seq", "kmeans"):
+            raise ValueError("order must be seq or kmeans")
+        if curvature not in ("lin", "iso"):
+            raise ValueError("curvature must be lin or iso")
+        raise NotImplementedError("backend='torch' is the reference's float32 CPU specification; this library runs "
+                                  "the sm_100a INT8 production path (pass **PROD, or backend='triton', store='int8', "
+                                  "dot='bf16')")
+    if curvature != "lin":
+        raise ValueError("triton backend needs curvature='lin'")
+    m = int(k.shape[0])
+    if m % leaf:
+        raise ValueError("triton backend: key count must be a multiple of the leaf size")
+    if dot == "bf16" and store not in ("bf16", "fp8", "int8"):
+        raise ValueError("dot='bf16' needs store='bf16', 'fp8' or 'int8'")
+    if store in ("fp8", "int8") and (dot != "bf16" or select == "bound" or (quant or {}).get("state")):
+        raise ValueError("store='fp8' needs dot='bf16', select='max' and no state fake-quant")
+    if store != "int8" or dot != "bf16":
+        raise NotImplementedError("only the INT8 production path (store='int8', dot='bf16') is implemented")
+    if order != "seq":
+        raise NotImplementedError("order='kmeans' (accurate/max modes) is not implemented yet")
+    if int(tile) != TILE or int(leaf) != LEAF:
+        raise NotImplementedError(f"the kernels implement tile={TILE}, leaf={LEAF} (got tile={tile}, leaf={leaf})")
+    if int(sel_stride) != 1:
+        raise NotImplementedError("sel_stride != 1 is not implemented")
+    if quant:
+        raise NotImplementedError("fake-quant simulation (quant=...) is not implemented")
+    if q.dim() != 2 or k.dim() != 2 or v.dim() != 2 or int(q.shape[1]) != DIM or k.shape != v.shape or \
+            int(k.shape[1]) != DIM:
+        raise ValueError(f"q [N, {DIM}], k/v [M, {DIM}] expected")
+    if not (q.is_cuda and k.is_cuda and v.is_cuda):
+        raise ValueError("q, k, v must be CUDA tensors (there is no CPU path)")
+
+
+def _prep_inputs(q, k, v, tail):
+    qd = q if q.dtype in (torch.float32, torch.bfloat16) else q.float()
+    qd = qd.contiguous()
+    kb = k.to(torch.bfloat16).contiguous()
+    vb = v.to(torch.bfloat16).contiguous()
+    tk = tv = None
+    if tail is not None and tail[0] is not None and int(tail[0].shape[0]) > 0:
+        tk = tail[0].float().contiguous()
+        tv = tail[1].float().contiguous()
+    return qd, kb, vb, tk, tv
+
+
+def _args(qd, kb, vb, tk, tv, exact_leaves, sink_leaves, tile_chunk, scale, out=None, lse=None, ws=None):
+    a = _lib.HtrcFlatArgs()
+    a.q = ptr(qd)
+    a.q_dtype = _lib.DTYPE_BF16 if qd.dtype == torch.bfloat16 else _lib.DTYPE_F32
+    a.k, a.v = ptr(kb), ptr(vb)
+    a.n_queries, a.n_keys = int(qd.shape[0]), int(kb.shape[0])
+    a.dim, a.tile, a.leaf = DIM, TILE, LEAF
+    a.exact_leaves, a.sink_leaves = int(exact_leaves), int(sink_leaves)
+    a.tile_chunk = int(tile_chunk) if tile_chunk else 0
+    a.scale = float(scale) if scale is not None else 0.0
+    a.tail_k, a.tail_v = ptr(tk), ptr(tv)
+    a.n_tail = int(tk.shape[0]) if tk is not None else 0
+    a.out, a.lse = ptr(out), ptr(lse)
+    if ws is not None:
+        a.workspace, a.workspace_bytes = ptr(ws), int(ws.numel())
+    return a
+
+
+def workspace_bytes(n_queries, n_keys, exact_leaves, sink_leaves=0, tile_chunk=0, n_tail=0) -> int:
+    """Device workspace one forward call needs."""
+    a = _lib.HtrcFlatArgs()
+    a.n_queries, a.n_keys, a.dim, a.tile, a.leaf = int(n_queries), int(n_keys), DIM, TILE, LEAF
+    a.q_dtype = _lib.DTYPE_F32
+    a.exact_leaves, a.sink_leaves = int(exact_leaves), int(sink_leaves)
+    a.tile_chunk, a.n_tail = int(tile_chunk or 0), int(n_tail)
+    nbytes = ctypes_size_t()
+    check(lib().htrc_flat_workspace_size(a, nbytes), "workspace size")
+    return int(nbytes.value)
+
+
+def ctypes_size_t():
+    import ctypes
+    return ctypes.c_size_t()
+
+
+def _workspace(ws, nbytes, device):
+    """A uint8 device buffer of at least nbytes, reused through the ``ws`` dict like the reference's
+    workspace (h3/htrc_flat_triton.py:302-312)."""
+    if ws is None:
+        return torch.empty(nbytes, dtype=torch.uint8, device=device)
+    b = ws.get("workspace")
+    if b is None or b.numel() < nbytes or b.device != device:
+        b = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        ws["workspace"] = b
+    return b
+
+
+def forward_into(qd, kb, vb, tk, tv, *, exact_leaves, sink_leaves=0, tile_chunk=0, scale=None, out, lse=None,
+                 workspace, stream=None):
+    """One head through ``htrc_flat_forward`` into caller-provided buffers (no allocation; CUDA-graph
+    capturable).  qd [N, 128] f32/bf16, kb/vb [M, 128] bf16, out [N, 128] f32, lse [N] f32 or None."""
+    a = _args(qd, kb, vb, tk, tv, exact_leaves, sink_leaves, tile_chunk, scale, out, lse, workspace)
+    check(lib().htrc_flat_forward(a, stream_ptr(stream)), "htrc_flat_forward")
+
+
+def device_status(workspace, stream=None) -> int:
+    """Read and clear the device status word; raises if any failure bit is set."""
+    import ctypes
+    st = ctypes.c_int32(0)
+    check(lib().htrc_flat_status(ptr(workspace), st, stream_ptr(stream)), "htrc_flat_status")
+    if st.value:
+        bits = [name for b, name in _lib.STATUS_BITS.items() if st.value & b]
+        raise _lib.HtrcError("device status: " + ", ".join(bits))
+    return 0
+
+
+@torch.inference_mode()
+def flat_attention(q, k, v, *, tile=64, exact_leaves=64, order="seq", curvature="lin",
+                   tile_chunk=32, precision="fp32", leaf=16, scale=None, prof=None,
+                   select="max", backend="torch", store="fp32", splits=8, dot="tf32",
+                   sel_stride=1, kern=None, quant=None, sink_leaves=0, tail=None, ws=None,
+                   return_lse=False):
+    """q [N, 128], k/v [M, 128] on a CUDA device -> out [N, 128] float32 (and lse [N] with
+    return_lse).  Signature and defaults of the reference (h3/htrc_flat.py:99-103); see PROD."""
+    _check_args(q, k, v, tile, exact_leaves, order, curvature, leaf, select, backend, store, dot,
+                sel_stride, quant, sink_leaves, tail)
+    qd, kb, vb, tk, tv = _prep_inputs(q, k, v, tail)
+    if prof is not None:
+        st = run_stages(qd, kb, vb, tk, tv, exact_leaves=exact_leaves, sink_leaves=sink_leaves,
+                        tile_chunk=tile_chunk, scale=scale, prof=prof)
+        return (st["out"], st["lse"]) if return_lse else st["out"]
+    n = int(qd.shape[0])
+    out = torch.empty((n, DIM), dtype=torch.float32, device=q.device)
+    lse = torch.empty((n,), dtype=torch.float32, device=q.device) if return_lse else None
+    nbytes = workspace_bytes(n, int(kb.shape[0]), exact_leaves, sink_leaves, tile_chunk,
+                             int(tk.shape[0]) if tk is not None else 0)
+    w = _workspace(ws, nbytes, q.device)
+    forward_into(qd, kb, vb, tk, tv, exact_leaves=exact_leaves, sink_leaves=sink_leaves,
+                 tile_chunk=tile_chunk, scale=scale, out=out, lse=lse, workspace=w)
+    return (out, lse) if return_lse else out
+
+
+def flat_attention_prod(q, k, v, **over):
+    """Production configuration of the flat operator (h3/htrc_flat.py:397-399)."""
+    return flat_attention(q, k, v, **{**PROD, **over})
+
+
+@torch.inference_mode()
+def run_stages(qd, kb, vb, tk=None, tv=None, *, exact_leaves, sink_leaves=0, tile_chunk=0, scale=None,
+               prof=None, stream=None):
+    """The same operator launched stage by stage through the C ABI's stage entry points, returning
+    every intermediate (k8, ks, mu, q8, sq, dq8, sdq, g8, sg, lz, vb, sel, idx, excl, out, lse).
+    Used for stage timing (``prof``, the reference's stage names prep/stats/select/tile/finish) and
+    for per-stage parity tests.  The state of all tiles is kept (tile_chunk only sets the launch
+    granularity of the state stages)."""
+    L = lib()
+    dev = qd.device
+    s = stream_ptr(stream)
+    tick = _Tick(prof)
+    n, m = int(qd.shape[0]), int(kb.shape[0])
+    nt, nb = -(-n // TILE), m // LEAF
+    pitch = leaf_pitch(nb)
+    sink = max(0, min(int(sink_leaves), nb))
+    kx = min(int(exact_leaves) + sink, nb)
+    sc = 1.0 / math.sqrt(DIM) if scale is None else float(scale)
+    qdt = _lib.DTYPE_BF16 if qd.dtype == torch.bfloat16 else _lib.DTYPE_F32
+    e = lambda *shape, dt=torch.float32: torch.empty(shape, dtype=dt, device=dev)  # noqa: E731
+    r = dict(k8=e(m, DIM, dt=torch.int8), ks=e(m), mu=e(nt, DIM), mu_hi=e(nt, DIM, dt=torch.bfloat16),
+             mu_lo=e(nt, DIM, dt=torch.bfloat16), q8=e(nt * TILE, DIM, dt=torch.int8), sq=e(nt * TILE),
+             dq8=e(nt * TILE, DIM, dt=torch.int8), sdq=e(nt * TILE), g8=e(nt, nb, DIM, dt=torch.int8),
+             sg=e(nt, pitch), lz=e(nt, pitch), vb=e(nt, nb, DIM, dt=torch.bfloat16), sel=torch.zeros((nt, pitch),
+             dtype=torch.float32, device=dev), idx=e(nt, max(kx, 1), dt=torch.int32),
+             excl=e(nt, pitch, dt=torch.uint8), out=e(n, DIM), lse=e(n),
+             status=torch.zeros((1,), dtype=torch.int32, device=dev))
+    stp = ptr(r["status"])
+    check(L.htrc_pack_int8(ptr(kb), _lib.DTYPE_BF16, m, DIM, _lib.ROUND_HALF_EVEN, ptr(r["k8"]), ptr(r["ks"]), s),
+          "htrc_pack_int8")
+    check(L.htrc_tile_prep(ptr(qd), qdt, n, DIM, TILE, ptr(r["mu"]), ptr(r["mu_hi"]), ptr(r["mu_lo"]), ptr(r["q8"]),
+                           ptr(r["sq"]), ptr(r["dq8"]), ptr(r["sdq"]), s), "htrc_tile_prep")
+    tail_part = None
+    if tk is not None:
+        tail_part = e(n, DIM + 2)
+        check(L.htrc_tail_partial(ptr(qd), qdt, n, DIM, ptr(tk), ptr(tv), int(tk.shape[0]), sc, ptr(tail_part), s),
+              "htrc_tail_partial")
+    tick("prep")
+    chunk = nt if not tile_chunk or tile_chunk <= 0 else min(int(tile_chunk), nt)
+    far = kx < nb
+    if far:
+        for t0 in range(0, nt, chunk):
+            tc = min(chunk, nt - t0)
+            check(L.htrc_leaf_stats(ptr(r["mu_hi"]), ptr(r["mu_lo"]), nt, t0, tc, ptr(kb), ptr(vb), m, DIM, LEAF, sc,
+                                    ptr(r["g8"][t0]), ptr(r["sg"][t0]), ptr(r["lz"][t0]), ptr(r["vb"][t0]), stp, s),
+                  "htrc_leaf_stats")
+    tick("stats")
+    if far and kx > 0:
+        for t0 in range(0, nt, chunk):
+            tc = min(chunk, nt - t0)
+            check(L.htrc_rowmax_select(ptr(r["dq8"]), ptr(r["sdq"]), t0, tc, ptr(r["g8"][t0]), ptr(r["sg"][t0]),
+                                       ptr(r["lz"][t0]), nb, DIM, ptr(r["sel"][t0]), stp, s), "htrc_rowmax_select")
+    check(L.htrc_route(ptr(r["sel"]), nt, nb, int(exact_leaves), sink, ptr(r["idx"]), ptr(r["excl"]), s), "htrc_route")
+    tick("select")
+    check(L.htrc_tile_attention(ptr(r["q8"]), ptr(r["sq"]), ptr(r["dq8"]), ptr(r["sdq"]), n, 0, nt, ptr(r["g8"]),
+                                ptr(r["sg"]), ptr(r["lz"]), ptr(r["vb"]), ptr(r["excl"]), ptr(r["idx"]), kx, nb,
+                                ptr(r["k8"]), ptr(r["ks"]), ptr(vb), m, DIM, LEAF, sc, ptr(tail_part), ptr(r["out"]),
+                                ptr(r["lse"]), stp, s), "htrc_tile_attention")
+    tick("tile")
+    tick("finish")
+    r["kx"], r["nb"], r["pitch"] = kx, nb, pitch
+    return r

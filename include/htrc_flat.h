@@ -1,0 +1,142 @@
+/* C ABI of libhtrc_flat.so: the flat (tree-free) HTRC attention operator for NVIDIA B200 (sm_100a).
+ *
+ * Every pointer is a device pointer on the current CUDA device unless stated otherwise; the caller
+ * owns all memory.  No entry point allocates device memory or synchronises the stream, so a whole
+ * forward call can be captured in a CUDA graph once the library has been initialised on the device
+ * (the first call of any entry point on a device sets kernel attributes; make it before capture).
+ * Return value: HTRC_OK (0) or one of the HTRC_ERR_* codes; htrc_strerror() names them.  Errors
+ * detected on the device (a bounded wait that gave up, an out-of-range leaf index, a non-finite
+ * log-partition) are OR-ed into a status word that htrc_flat_status() reads back.
+ *
+ * Layouts (row-major, contiguous unless a pitch is given):
+ *   q [N, D] f32 or bf16;  k, v [M, D] bf16;  D = 128;  M a multiple of `leaf`.
+ *   Tiles of `tile` = 64 query rows; nt = ceil(N / 64); the last tile is padded with repeats of the
+ *   last query row.  nb = M / leaf leaves.  Per-(tile, leaf) scalars use the leaf pitch
+ *   P = htrc_leaf_pitch(nb) (nb rounded up to 16).
+ */
+#ifndef HTRC_FLAT_H_
+#define HTRC_FLAT_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* htrc_stream_t; /* a cudaStream_t; NULL is the legacy default stream */
+
+enum {
+  HTRC_OK = 0,
+  HTRC_ERR_ARG = 1,         /* invalid argument (shape, dtype, null pointer, range) */
+  HTRC_ERR_UNSUPPORTED = 2, /* valid for the reference but not implemented by this library */
+  HTRC_ERR_WORKSPACE = 3,   /* workspace missing or smaller than htrc_flat_workspace_size() */
+  HTRC_ERR_CUDA = 4,        /* a CUDA runtime call failed (launch, attribute, tensor map) */
+  HTRC_ERR_DEVICE = 5       /* no sm_100 device, or the device status word reported a failure */
+};
+
+enum { HTRC_DTYPE_F32 = 0, HTRC_DTYPE_BF16 = 1 };
+enum { HTRC_ROUND_HALF_EVEN = 0, HTRC_ROUND_HALF_AWAY = 1 };
+
+/* Device status bits (htrc_flat_status). */
+enum { HTRC_STATUS_WAIT_TIMEOUT = 1, HTRC_STATUS_BAD_INDEX = 2, HTRC_STATUS_NONFINITE = 4 };
+
+/* Arguments of one head of the operator. */
+typedef struct HtrcFlatArgs {
+  const void* q;           /* [n_queries, dim], q_dtype */
+  int32_t q_dtype;         /* HTRC_DTYPE_F32 or HTRC_DTYPE_BF16 */
+  const uint16_t* k;       /* [n_keys, dim] bf16 */
+  const uint16_t* v;       /* [n_keys, dim] bf16 */
+  int64_t n_queries;       /* N >= 1 */
+  int64_t n_keys;          /* M, a positive multiple of leaf */
+  int32_t dim;             /* D, must be 128 */
+  int32_t tile;            /* query tile rows, must be 64 */
+  int32_t leaf;            /* key leaf tokens, must be 64 */
+  int32_t exact_leaves;    /* E >= 0: leaves evaluated exactly per tile (clamped to nb) */
+  int32_t sink_leaves;     /* leading leaves always exact (clamped to nb) */
+  int32_t tile_chunk;      /* tiles per chunk of the far-field state (<= 0: all tiles at once) */
+  float scale;             /* logit scale; <= 0 selects 1/sqrt(dim) */
+  const float* tail_k;     /* [n_tail, dim] f32 keys past the last full leaf, or NULL */
+  const float* tail_v;     /* [n_tail, dim] f32 */
+  int32_t n_tail;          /* >= 0 */
+  void* workspace;         /* device workspace, 256-byte aligned */
+  size_t workspace_bytes;  /* >= htrc_flat_workspace_size(args) */
+  float* out;              /* [n_queries, dim] f32 output */
+  float* lse;              /* [n_queries] f32 log-partition (logit units), or NULL */
+} HtrcFlatArgs;
+
+/* nb rounded up to a multiple of 16: the row pitch of the per-(tile, leaf) scalar arrays. */
+int64_t htrc_leaf_pitch(int64_t nb);
+
+/* Workspace bytes one htrc_flat_forward call with these arguments needs (pointers are ignored). */
+int htrc_flat_workspace_size(const HtrcFlatArgs* args, size_t* bytes);
+
+/* The whole operator for one head: INT8 key pack, tile centres and query codes, leaf statistics,
+ * row-max selection, top-E routing, far field + near field + tail, normalised output and log-Z.
+ * Replaces flat_attention(q, k, v, backend="triton", store="int8", dot="bf16", select="max",
+ * tile=64, leaf=64, exact_leaves=E, sink_leaves=S, tail=(tk, tv)) of the reference
+ * (h3/htrc_flat.py:99-124 -> _flat_triton :181-276), plus the log-Z output the reference lacks. */
+int htrc_flat_forward(const HtrcFlatArgs* args, htrc_stream_t stream);
+
+/* Read back (synchronously) and clear the device status word inside `workspace`. */
+int htrc_flat_status(void* workspace, int32_t* status_out, htrc_stream_t stream);
+
+/* ---- stage entry points (the same kernels htrc_flat_forward launches), for parity tests ---- */
+
+/* Per-row INT8 pack of x [rows, dim]: scale = max(amax_row|x| * (1/127), 1e-20).
+ * HTRC_ROUND_HALF_EVEN: x8 = clamp(rint(x / scale), -127, 127)   (h3/htrc_flat.py:216-218, keys)
+ * HTRC_ROUND_HALF_AWAY: x8 = trunc(x / scale +- 0.5)              (h3/htrc_flat_triton.py:110-117) */
+int htrc_pack_int8(const void* x, int32_t dtype, int64_t rows, int32_t dim, int32_t rounding, int8_t* x8,
+                   float* scale, htrc_stream_t stream);
+
+/* Tile centres and query codes (h3/htrc_flat.py:142-156 `_tiles`; h3/htrc_flat_triton.py:103-117):
+ * mu [nt, dim] f32 (mean of the real rows, float64 sum rounded once); mu_hi/mu_lo [ceil(nt/128)*128,
+ * dim] bf16 with mu_hi = bf16(mu), mu_lo = bf16(mu - mu_hi) (rows past nt are zero);
+ * q8/dq8 [nt*64, dim] int8 and sq/sdq [nt*64] f32: half-away codes of q and of q - mu. */
+int htrc_tile_prep(const void* q, int32_t q_dtype, int64_t n_queries, int32_t dim, int32_t tile, float* mu,
+                   uint16_t* mu_hi, uint16_t* mu_lo, int8_t* q8, float* sq, int8_t* dq8, float* sdq,
+                   htrc_stream_t stream);
+
+/* Leaf statistics of tiles [t0, t0 + tc) (h3/htrc_flat_triton.py:41-85 `_stats_kernel`, I8 store):
+ * g8 [tc, nb, dim] int8 and sg/lz [tc, P] f32, vb [tc, nb, dim] bf16.  mu_hi/mu_lo as written by
+ * htrc_tile_prep (all nt tiles); status: device int32 word or NULL. */
+int htrc_leaf_stats(const uint16_t* mu_hi, const uint16_t* mu_lo, int64_t nt, int64_t t0, int64_t tc,
+                    const uint16_t* k, const uint16_t* v, int64_t n_keys, int32_t dim, int32_t leaf, float scale,
+                    int8_t* g8, float* sg, float* lz, uint16_t* vb, int32_t* status, htrc_stream_t stream);
+
+/* Row-max selection sel [tc, P] f32 of tiles [t0, t0 + tc) (h3/htrc_flat_triton.py:214-254
+ * `_rowmax_kernel`, I8): sel[t, l] = max_r (dq8_r . g8_l) * (sdq_r * sg_l) + lz_l over the 64 rows. */
+int htrc_rowmax_select(const int8_t* dq8, const float* sdq, int64_t t0, int64_t tc, const int8_t* g8,
+                       const float* sg, const float* lz, int64_t nb, int32_t dim, float* sel, int32_t* status,
+                       htrc_stream_t stream);
+
+/* Top-E routing of tiles [0, tc) (h3/htrc_flat.py:250-265): the first sink_leaves leaves are forced,
+ * then the largest sel; kx = min(exact_leaves + sink_leaves, nb).  idx [tc, kx] int32 in ascending
+ * leaf order (ties broken towards the lower leaf index); excl [tc, P] uint8 (1 = routed). */
+int htrc_route(const float* sel, int64_t tc, int64_t nb, int32_t exact_leaves, int32_t sink_leaves, int32_t* idx,
+               uint8_t* excl, htrc_stream_t stream);
+
+/* Far field + near field (+ tail partial) of tiles [t0, t0 + tc) merged into out/lse rows
+ * [t0*64, min(n_queries, (t0+tc)*64)) (h3/htrc_flat_triton.py:88-211 `_tile_kernel` with I8=1,
+ * merged as :257-273).  State arrays as produced by the stages above; k8/ks from htrc_pack_int8
+ * (half-even) of k; tail_part: NULL or [n_queries, dim + 2] f32 rows (acc, m, l) from the tail. */
+int htrc_tile_attention(const int8_t* q8, const float* sq, const int8_t* dq8, const float* sdq, int64_t n_queries,
+                        int64_t t0, int64_t tc, const int8_t* g8, const float* sg, const float* lz,
+                        const uint16_t* vb, const uint8_t* excl, const int32_t* idx, int32_t kx, int64_t nb,
+                        const int8_t* k8, const float* ks, const uint16_t* v, int64_t n_keys, int32_t dim,
+                        int32_t leaf, float scale, const float* tail_part, float* out, float* lse, int32_t* status,
+                        htrc_stream_t stream);
+
+/* Exact softmax partial of every query row against the tail keys (h3/htrc_flat_triton.py:187-207 for
+ * n_tail <= 16 with bf16 operands; :381-388 float32 for longer tails): tail_part [N, dim + 2]. */
+int htrc_tail_partial(const void* q, int32_t q_dtype, int64_t n_queries, int32_t dim, const float* tail_k,
+                      const float* tail_v, int32_t n_tail, float scale, float* tail_part, htrc_stream_t stream);
+
+/* Human-readable name of a return code. */
+const char* htrc_strerror(int code);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HTRC_FLAT_H_ */
