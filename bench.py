@@ -1,0 +1,420 @@
+#!/usr/bin/env python
+"""Benchmark of the flat HTRC operator on B200: milliseconds per attention layer.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload cfg3|cfg2]
+
+Workload (default cfg3): one layer = 24 heads of a 32x48x84 video latent
+(129,024 tokens), d=128, bf16 Q/K/V from the seeded smooth-field generator (htrc_b200.synth), leaf 64,
+tile 64, fast mode (256 exact leaves), INT8 store.  A step is one whole layer: every head runs the full
+operator (key pack, tile prep, leaf stats, row-max selection, routing, far+near attention).  Under
+torchrun the 24 heads are split across the N ranks and the bf16 outputs are all-gathered over NCCL on a
+side stream, overlapped with the next head.
+
+Printed JSON line (rank 0): value = ms per layer, device-resident inputs, max over ranks; e2e = the same
+through the public API (htrc_b200.forward_into) with pinned host inputs and outputs, host<->device copies
+inside the timed region; roofline of the dominant kernel from live CUDA events; cpu_baseline = the
+oracle port timed on a bounded tile sample on this host (rank 0, N=1).
+
+--impl reference times the reference's algorithm on the host CPU (the NumPy oracle port of
+h3/htrc_flat.py's production path, all host threads) on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "flat-HTRC ms per 129k-token 24-head d128 layer @1/8 B200; mean |ΔlogZ|"
+WORKLOADS = {
+    "cfg3": dict(grid=(32, 48, 84), heads=24, exact_leaves=256,
+                 name="cfg3: 129,024-token 32x48x84 latent layer, 24 heads, d128, leaf 64, tile 64, fast (E=256), INT8"),
+    "cfg2": dict(grid=(16, 32, 32), heads=24, exact_leaves=256,
+                 name="cfg2: 16,384-token 16x32x32 latent layer, 24 heads, d128, leaf 64, tile 64, fast (E=256), INT8"),
+}
+LAUNCHES_PER_HEAD = 6      # key pack, tile prep, leaf stats, row-max, route, tile attention
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="cfg3", choices=list(WORKLOADS))
+    ap.add_argument("--cpu-tiles", type=int, default=4, help="tiles of the CPU-baseline sample")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------------------------------------ helpers
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms while the timed region runs."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.rows = []
+        self.proc = None
+        self.th = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.index), "-lms", "200"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.th = threading.Thread(target=self._read, daemon=True)
+        self.th.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.th:
+            self.th.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in self.rows:
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+            except (ValueError, IndexError):
+                continue
+            for name, val in zip(names, r[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def oracle_sample(q, k, v, exact_leaves, tiles, threads):
+    """CPU oracle on a tile sample of one head: (per-head seconds, per-sample seconds, out rows, lse rows)."""
+    from threadpoolctl import threadpool_limits
+
+    from oracle import flat_oracle as O
+    with threadpool_limits(limits=threads):
+        t0 = time.perf_counter()
+        prep = O.prepare_head(q, k, v)
+        t1 = time.perf_counter()
+        out, lse = O.attention_tiles(prep, tiles, exact_leaves=exact_leaves)
+        t2 = time.perf_counter()
+    return t1 - t0, t2 - t1, out, lse
+
+
+# ------------------------------------------------------------------------------------------ reference arm
+def run_reference(a, wl, rank):
+    if rank != 0:
+        return
+    import numpy as np
+
+    from htrc_b200 import synth
+    threads = host_threads()
+    q, k, v = synth.head_inputs(wl["grid"], 128, head=0)
+    qn, kn, vn = q.float().numpy(), k.float().numpy(), v.float().numpy()
+    n = qn.shape[0]
+    nt = -(-n // 64)
+    rng = np.random.default_rng(0)
+    preps, times = [], []
+    for step in range(a.warmup + a.steps):
+        tiles = np.sort(rng.choice(nt, size=a.cpu_tiles, replace=False))
+        dp, dt, _, _ = oracle_sample(qn, kn, vn, wl["exact_leaves"], tiles, threads)
+        if step >= a.warmup:
+            preps.append(dp)
+            times.append(dt)
+    per_tile = statistics.mean(times) / a.cpu_tiles
+    ms_layer = (statistics.mean(preps) + per_tile * nt) * wl["heads"] * 1e3
+    line = {"metric": METRIC, "impl": "reference", "value": ms_layer, "unit": "ms/layer", "n_gpus": a.gpus,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms_layer, "higher_is_better": False,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8+bf16 (restated in f32/f64 on CPU)",
+            "data": "synthetic: seeded smooth-field Q/K, N(0,1) V (cfg generator), bf16",
+            "config": {"workload": wl["name"], "tokens": n, "heads": wl["heads"], "dim": 128, "leaf": 64,
+                       "tile": 64, "exact_leaves": wl["exact_leaves"]},
+            "cpu_baseline": {"value": ms_layer, "unit": "ms/layer", "cores": threads, "kind": "port",
+                             "sample": f"per step: the per-head preparation (bf16 K/V, key pack, tile centres) of "
+                                       f"head 0 plus {a.cpu_tiles} random query tiles (of {nt}); layer = "
+                                       f"{wl['heads']} x (prep + {nt} x per-tile), oracle/flat_oracle.py"},
+            "e2e": {"value": ms_layer, "unit": "ms/layer", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------------------ our arm
+def run_ours(a, wl, rank, world, local_rank):
+    import numpy as np
+    import torch
+
+    import htrc_b200
+    from htrc_b200 import flat as F
+    from htrc_b200 import synth
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+    H = wl["heads"]
+    if H % world:
+        raise SystemExit(f"{H} heads do not split over {world} ranks")
+    my_heads = list(range(rank * H // world, (rank + 1) * H // world))
+    E = wl["exact_leaves"]
+
+    # ---- inputs: pinned host copies (for e2e) and device-resident copies (for the device timing)
+    host = {}
+    for h in my_heads:
+        q, k, v = synth.head_inputs(wl["grid"], 128, head=h)
+        host[h] = tuple(t.pin_memory() for t in (q, k, v))
+    n, m = host[my_heads[0]][0].shape[0], host[my_heads[0]][1].shape[0]
+    nt, nb = -(-n // 64), m // 64
+    kx = min(E, nb)
+    dq = {h: tuple(t.to(dev, non_blocking=True) for t in host[h]) for h in my_heads}
+    out = {h: torch.empty((n, 128), dtype=torch.float32, device=dev) for h in my_heads}
+    lse = {h: torch.empty((n,), dtype=torch.float32, device=dev) for h in my_heads}
+    wsb = F.workspace_bytes(n, m, E, 0, 0, 0)
+    ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
+    comp = torch.cuda.current_stream(dev)
+    side = torch.cuda.Stream(dev)
+    gathered = None
+    obf = None
+    if world > 1:
+        obf = {h: torch.empty((n, 128), dtype=torch.bfloat16, device=dev) for h in my_heads}
+        gathered = [torch.empty((world, n, 128), dtype=torch.bfloat16, device=dev) for _ in my_heads]
+    ev_done = [torch.cuda.Event() for _ in my_heads]
+    nev = 6
+
+    def layer(stage_events=None):
+        for i, h in enumerate(my_heads):
+            evs = stage_events[i] if stage_events is not None else None
+            F.forward_into(*dq[h], None, None, exact_leaves=E, out=out[h], lse=lse[h], workspace=ws,
+                           stage_events=evs)
+            if world > 1:
+                obf[h].copy_(out[h])
+                ev_done[i].record(comp)
+                side.wait_event(ev_done[i])
+                with torch.cuda.stream(side):
+                    dist.all_gather_into_tensor(gathered[i], obf[h])
+        if world > 1:
+            comp.wait_stream(side)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    torch.cuda.synchronize(dev)
+    for _ in range(a.warmup):
+        layer()
+    barrier()
+    F.device_status(ws)
+
+    # ---- device-resident timed region, with per-stage events of every head
+    stage_evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(nev)] for _ in my_heads] for _ in range(a.steps)]
+    clocks = ClockSampler(dev.index if world == 1 else int(os.environ.get("LOCAL_RANK", 0)))
+    clocks.start()
+    barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(comp)
+    for s in range(a.steps):
+        layer(stage_evs[s])
+    t1.record(comp)
+    barrier()
+    clk = clocks.stop()
+    ms = max_over_ranks(t0.elapsed_time(t1) / a.steps)
+    F.device_status(ws)
+    stage_names = ["prep", "stats", "rowmax", "route", "tile"]
+    stage_ms = {nm: statistics.mean(stage_evs[s][i][j].elapsed_time(stage_evs[s][i][j + 1])
+                                    for s in range(a.steps) for i in range(len(my_heads)))
+                for j, nm in enumerate(stage_names)}
+
+    # ---- parity at full size on a tile sample of head 0 (rank 0): mean |dlogZ| vs the oracle
+    parity = {}
+    cpu = None
+    if rank == 0 and not a.no_cpu:
+        h0 = my_heads[0]
+        qn, kn, vn = (t.float().numpy() for t in host[h0])
+        rng = np.random.default_rng(1)
+        tiles = np.sort(rng.choice(nt, size=a.cpu_tiles, replace=False))
+        threads = host_threads()
+        dp, dt, ro, rl = oracle_sample(qn, kn, vn, E, tiles, threads)
+        rows = (tiles[:, None] * 64 + np.arange(64)[None, :]).reshape(-1)
+        valid = rows < n
+        lse_d = lse[h0].cpu().numpy()[rows[valid]]
+        out_d = out[h0].cpu().numpy()[rows[valid]]
+        parity = {"logz_mae": float(np.abs(lse_d - rl[valid]).mean()),
+                  "out_maxabs": float(np.abs(out_d - ro[valid]).max()),
+                  "sample": f"{len(tiles)} random tiles of head {h0} vs oracle/flat_oracle.py"}
+        # error of the operator against exact softmax attention on the same rows
+        qs = dq[h0][0][torch.as_tensor(rows[valid], device=dev)].float()
+        kk, vv = dq[h0][1].float(), dq[h0][2].float()
+        s_ = (qs @ kk.T) / math.sqrt(128)
+        ex = torch.softmax(s_, -1) @ vv
+        od = out[h0][torch.as_tensor(rows[valid], device=dev)]
+        parity["rel_l2_vs_exact"] = float((od - ex).norm() / ex.norm())
+        del s_
+        if world == 1:
+            per_tile = dt / len(tiles)
+            cpu_ms = (dp + per_tile * nt) * H * 1e3
+            cpu = {"value": cpu_ms, "unit": "ms/layer", "cores": threads, "kind": "port",
+                   "sample": f"head {h0}: per-head preparation + {len(tiles)} query tiles ({len(tiles) * 64} rows of "
+                             f"{n}) through oracle/flat_oracle.py; layer = {H} x (prep + {nt} x per-tile)"}
+
+    # ---- end to end through the public API with pinned host buffers
+    e2e = None
+    if not a.no_e2e:
+        qb = [torch.empty_like(dq[my_heads[0]][j]) for j in range(3) for _ in range(2)]
+        stage_in = [(qb[0], qb[2], qb[4]), (qb[1], qb[3], qb[5])]
+        stage_out = [(torch.empty((n, 128), dtype=torch.float32, device=dev),
+                      torch.empty((n,), dtype=torch.float32, device=dev)) for _ in range(2)]
+        host_out = {h: (torch.empty((n, 128), dtype=torch.float32).pin_memory(),
+                        torch.empty((n,), dtype=torch.float32).pin_memory()) for h in my_heads}
+        s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        in_done = [torch.cuda.Event() for _ in range(2)]
+        comp_done = [torch.cuda.Event() for _ in range(2)]
+        out_done = [torch.cuda.Event() for _ in range(2)]
+
+        def e2e_layer():
+            for i, h in enumerate(my_heads):
+                b = i % 2
+                if i >= 2:
+                    s_in.wait_event(comp_done[b])
+                with torch.cuda.stream(s_in):
+                    for dst, src in zip(stage_in[b], host[h]):
+                        dst.copy_(src, non_blocking=True)
+                    in_done[b].record(s_in)
+                comp.wait_event(in_done[b])
+                if i >= 2:
+                    comp.wait_event(out_done[b])
+                htrc_b200.forward_into(*stage_in[b], None, None, exact_leaves=E, out=stage_out[b][0],
+                                       lse=stage_out[b][1], workspace=ws)
+                comp_done[b].record(comp)
+                s_out.wait_event(comp_done[b])
+                with torch.cuda.stream(s_out):
+                    host_out[h][0].copy_(stage_out[b][0], non_blocking=True)
+                    host_out[h][1].copy_(stage_out[b][1], non_blocking=True)
+                    out_done[b].record(s_out)
+            comp.wait_stream(s_in)
+            comp.wait_stream(s_out)
+
+        for _ in range(a.warmup):
+            e2e_layer()
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(comp)
+        for _ in range(a.steps):
+            e2e_layer()
+        e1.record(comp)
+        barrier()
+        e2e_ms = max_over_ranks(e0.elapsed_time(e1) / a.steps)
+        h2d = sum(sum(t.numel() * t.element_size() for t in host[h]) for h in my_heads) * world
+        d2h = sum(sum(t.numel() * t.element_size() for t in host_out[h]) for h in my_heads) * world
+        same = bool(torch.equal(host_out[my_heads[0]][0].to(dev), out[my_heads[0]]))
+        e2e = {"value": e2e_ms, "unit": "ms/layer", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "api": "htrc_b200.forward_into, pinned host q/k/v in and out/lse back, copies overlapped on "
+                      "2 copy streams", "matches_device_run": same}
+
+    # ---- roofline of the dominant kernel (tile attention) from the live events
+    peaks, peak_src = measured_peaks()
+    npad = nt * 64
+    near = 2.0 * npad * (kx * 64) * 128
+    far = 2.0 * npad * (nb - kx) * 128 if kx < nb else 0.0
+    flops_bf16_equiv = (near + far) + 0.5 * (near + far)       # bf16 PV + int8 QK at half cost
+    tile_ms = stage_ms["tile"]
+    achieved = flops_bf16_equiv / (tile_ms * 1e-3) / 1e12
+    peak = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops")))
+    traffic = None
+    tp = ROOT / "profiles" / "tile_attention_traffic.json"
+    if tp.exists():
+        traffic = json.loads(tp.read_text()).get("bytes_per_launch")
+    roof = {"kernel": "tile_attention_kernel", "bound": "tensor", "achieved": achieved, "peak": peak,
+            "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
+            "peak_source": f"{peak_src} bf16_tflops_sustained", "flop_per_launch": flops_bf16_equiv,
+            "flop_count": "bf16 PV flops + int8 QK ops/2 over the routed tokens and non-routed leaves, one head",
+            "ms_per_launch": tile_ms}
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": ms, "unit": "ms/layer", "n_gpus": world, "steps": a.steps,
+                "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": False, "scaling": "strong",
+                "vs_baseline": None, "dtype": "int8 QK + bf16 PV, f32 softmax",
+                "data": "synthetic: seeded smooth-field Q/K (4x8x8 grid trilinear + 0.5 noise, RMS 3), N(0,1) V, bf16",
+                "config": {"workload": wl["name"], "tokens": n, "heads": H, "dim": 128, "leaf": 64, "tile": 64,
+                           "exact_leaves": E, "heads_per_gpu": len(my_heads),
+                           "l2": "inputs larger than L2: 2.4 GB of distinct q/k/v per layer, 1.6 GB leaf state per head",
+                           "parallelism": f"heads/{world}" + (" + bf16 output all_gather (NCCL)" if world > 1 else "")},
+                "stage_ms_per_head": stage_ms, **parity, "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
+                "gpu_launches": a.steps * len(my_heads) * LAUNCHES_PER_HEAD, "clocks": clk}
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    a = parse()
+    wl = WORKLOADS[a.workload]
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if a.impl == "reference":
+        run_reference(a, wl, rank)
+        return
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(a, wl, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

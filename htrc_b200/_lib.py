@@ -30,6 +30,7 @@ class HtrcFlatArgs(ctypes.Structure):
         ("tail_k", _p), ("tail_v", _p), ("n_tail", _i32),
         ("workspace", _p), ("workspace_bytes", ctypes.c_size_t),
         ("out", _p), ("lse", _p),
+        ("stage_events", ctypes.POINTER(_p)), ("n_stage_events", _i32),
     ]
 
 

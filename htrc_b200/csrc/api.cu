@@ -250,31 +250,44 @@ int htrc_flat_forward(const HtrcFlatArgs* a, htrc_stream_t stream) {
   int32_t* idx = at<int32_t>(ws, L.idx);
   float* tail = a->n_tail > 0 ? at<float>(ws, L.tail) : nullptr;
 
+  auto mark = [&](int i) {
+    if (a->stage_events && i < a->n_stage_events && a->stage_events[i])
+      cudaEventRecord(static_cast<cudaEvent_t>(a->stage_events[i]), st);
+  };
+  mark(0);
   launch_pack_rows(a->k, HTRC_DTYPE_BF16, L.m, HTRC_ROUND_HALF_EVEN, k8, ks, st);
   launch_tile_prep(a->q, a->q_dtype, L.n, at<float>(ws, L.mu), mu_hi, mu_lo, q8, sq, dq8, sdq, st);
   if (tail) launch_tail_partial(a->q, a->q_dtype, L.n, a->tail_k, a->tail_v, a->n_tail, scale, tail, st);
   if (cudaGetLastError() != cudaSuccess) return HTRC_ERR_CUDA;
+  mark(1);
   const bool far = kx < nb;
-  for (int64_t t0 = 0; t0 < L.nt; t0 += L.tcm) {
+  int chunk = 0;
+  for (int64_t t0 = 0; t0 < L.nt; t0 += L.tcm, ++chunk) {
     const int64_t tc = std::min<int64_t>(L.tcm, L.nt - t0);
     if (far) {
       LeafStatsMaps smp;
       if ((rc = stats_maps(&smp, mu_hi, mu_lo, L.nt, a->k, a->v, L.m, g8, vb, tc, L.nb)) != HTRC_OK) return rc;
       if ((rc = launch_leaf_stats(smp, sg, lz, L.pitch, t0, tc, nb, scale, status, device_info().sms, st)) != HTRC_OK)
         return rc;
+    }
+    mark(2 + 4 * chunk);
+    if (far) {
       if (kx > 0) {
         RowmaxMaps rmp;
         if ((rc = rowmax_maps(&rmp, dq8, L.nt * 64, g8, sg, lz, tc, L.nb, L.pitch)) != HTRC_OK) return rc;
         if ((rc = launch_rowmax(rmp, sdq, sel, L.pitch, t0, tc, nb, status, st)) != HTRC_OK) return rc;
       }
     }
+    mark(3 + 4 * chunk);
     if ((rc = launch_route(sel, L.pitch, tc, nb, kx, sink, idx, excl, st)) != HTRC_OK) return rc;
+    mark(4 + 4 * chunk);
     TileMaps tmp;
     if ((rc = tile_maps(&tmp, q8, dq8, L.nt * 64, g8, vb, lz, sg, excl, tc, L.nb, L.pitch, k8, a->v, L.m)) != HTRC_OK)
       return rc;
     if ((rc = launch_tile_attention(tmp, sq, sdq, ks, idx, kx, nb, L.n, t0, tc, scale, tail, a->out, a->lse, status,
                                     st)) != HTRC_OK)
       return rc;
+    mark(5 + 4 * chunk);
   }
   return HTRC_OK;
 }

@@ -12,6 +12,7 @@ Additions over the reference: ``return_lse=True`` also returns the log-partition
 """
 from __future__ import annotations
 
+import ctypes
 import math
 import time
 
@@ -108,7 +109,8 @@ def _prep_inputs(q, k, v, tail):
     return qd, kb, vb, tk, tv
 
 
-def _args(qd, kb, vb, tk, tv, exact_leaves, sink_leaves, tile_chunk, scale, out=None, lse=None, ws=None):
+def _args(qd, kb, vb, tk, tv, exact_leaves, sink_leaves, tile_chunk, scale, out=None, lse=None, ws=None,
+          stage_events=None):
     a = _lib.HtrcFlatArgs()
     a.q = ptr(qd)
     a.q_dtype = _lib.DTYPE_BF16 if qd.dtype == torch.bfloat16 else _lib.DTYPE_F32
@@ -123,6 +125,16 @@ def _args(qd, kb, vb, tk, tv, exact_leaves, sink_leaves, tile_chunk, scale, out=
     a.out, a.lse = ptr(out), ptr(lse)
     if ws is not None:
         a.workspace, a.workspace_bytes = ptr(ws), int(ws.numel())
+    if stage_events:
+        handles = []
+        for ev in stage_events:
+            if ev.cuda_event == 0:          # torch creates CUDA events lazily: create it now
+                ev.record()
+            handles.append(ev.cuda_event)
+        arr = (ctypes.c_void_p * len(handles))(*handles)
+        a.stage_events = ctypes.cast(arr, ctypes.POINTER(ctypes.c_void_p))
+        a.n_stage_events = len(handles)
+        a._keep = arr
     return a
 
 
@@ -133,14 +145,9 @@ def workspace_bytes(n_queries, n_keys, exact_leaves, sink_leaves=0, tile_chunk=0
     a.q_dtype = _lib.DTYPE_F32
     a.exact_leaves, a.sink_leaves = int(exact_leaves), int(sink_leaves)
     a.tile_chunk, a.n_tail = int(tile_chunk or 0), int(n_tail)
-    nbytes = ctypes_size_t()
+    nbytes = ctypes.c_size_t()
     check(lib().htrc_flat_workspace_size(a, nbytes), "workspace size")
     return int(nbytes.value)
-
-
-def ctypes_size_t():
-    import ctypes
-    return ctypes.c_size_t()
 
 
 def _workspace(ws, nbytes, device):
@@ -156,16 +163,17 @@ def _workspace(ws, nbytes, device):
 
 
 def forward_into(qd, kb, vb, tk, tv, *, exact_leaves, sink_leaves=0, tile_chunk=0, scale=None, out, lse=None,
-                 workspace, stream=None):
+                 workspace, stream=None, stage_events=None):
     """One head through ``htrc_flat_forward`` into caller-provided buffers (no allocation; CUDA-graph
-    capturable).  qd [N, 128] f32/bf16, kb/vb [M, 128] bf16, out [N, 128] f32, lse [N] f32 or None."""
-    a = _args(qd, kb, vb, tk, tv, exact_leaves, sink_leaves, tile_chunk, scale, out, lse, workspace)
+    capturable).  qd [N, 128] f32/bf16, kb/vb [M, 128] bf16, out [N, 128] f32, lse [N] f32 or None;
+    stage_events: optional list of torch.cuda.Event recorded between the stages (see
+    include/htrc_flat.h)."""
+    a = _args(qd, kb, vb, tk, tv, exact_leaves, sink_leaves, tile_chunk, scale, out, lse, workspace, stage_events)
     check(lib().htrc_flat_forward(a, stream_ptr(stream)), "htrc_flat_forward")
 
 
 def device_status(workspace, stream=None) -> int:
     """Read and clear the device status word; raises if any failure bit is set."""
-    import ctypes
     st = ctypes.c_int32(0)
     check(lib().htrc_flat_status(ptr(workspace), st, stream_ptr(stream)), "htrc_flat_status")
     if st.value:

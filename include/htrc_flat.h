@@ -63,6 +63,12 @@ typedef struct HtrcFlatArgs {
   size_t workspace_bytes;  /* >= htrc_flat_workspace_size(args) */
   float* out;              /* [n_queries, dim] f32 output */
   float* lse;              /* [n_queries] f32 log-partition (logit units), or NULL */
+  /* Optional stage timing: cudaEvent_t handles recorded on the stream at fixed points (NULL = none):
+   * [0] start, [1] after key pack + tile prep + tail, then per tile chunk c:
+   * [2+4c] after leaf stats, [3+4c] after row-max, [4+4c] after routing, [5+4c] after the tile kernel.
+   * Points past n_stage_events are not recorded. */
+  void* const* stage_events;
+  int32_t n_stage_events;
 } HtrcFlatArgs;
 
 /* nb rounded up to a multiple of 16: the row pitch of the per-(tile, leaf) scalar arrays. */
@@ -90,8 +96,8 @@ int htrc_pack_int8(const void* x, int32_t dtype, int64_t rows, int32_t dim, int3
                    float* scale, htrc_stream_t stream);
 
 /* Tile centres and query codes (h3/htrc_flat.py:142-156 `_tiles`; h3/htrc_flat_triton.py:103-117):
- * mu [nt, dim] f32 (mean of the real rows, float64 sum rounded once); mu_hi/mu_lo [ceil(nt/128)*128,
- * dim] bf16 with mu_hi = bf16(mu), mu_lo = bf16(mu - mu_hi) (rows past nt are zero);
+ * mu [nt, dim] f32 (mean of the real rows, float64 sum rounded once); mu_hi/mu_lo [nt, dim] bf16 with
+ * mu_hi = bf16(mu), mu_lo = bf16(mu - mu_hi);
  * q8/dq8 [nt*64, dim] int8 and sq/sdq [nt*64] f32: half-away codes of q and of q - mu. */
 int htrc_tile_prep(const void* q, int32_t q_dtype, int64_t n_queries, int32_t dim, int32_t tile, float* mu,
                    uint16_t* mu_hi, uint16_t* mu_lo, int8_t* q8, float* sq, int8_t* dq8, float* sdq,

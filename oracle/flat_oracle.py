@@ -41,9 +41,9 @@ EPS_SLOPE = F32(1e-30)         # slope abs-max floor (h3/htrc_flat_triton.py:75)
 # ----------------------------------------------------------------------------- bf16 helpers
 def bf16_bits(x):
     """float32 -> bfloat16 bit pattern (uint16), round to nearest even (finite inputs)."""
-    b = np.ascontiguousarray(x, dtype=F32).view(np.uint32).astype(np.uint64)
-    b = (b + 0x7FFF + ((b >> 16) & 1)) >> 16
-    return b.astype(np.uint16)
+    b = np.ascontiguousarray(x, dtype=F32).view(np.uint32)
+    lsb = (b >> np.uint32(16)) & np.uint32(1)
+    return ((b + (lsb + np.uint32(0x7FFF))) >> np.uint32(16)).astype(np.uint16)   # no overflow for finite x
 
 
 def bf16_to_f32(bits):
@@ -152,7 +152,7 @@ def query_codes(qt, mu):
 
 def rowmax_select(dq8, sdq, g8, sg, lz):
     """SEL[t, l] = max_r (dq8_r . g8_l) * (sdq_r * sg_l) + lz_l (h3/htrc_flat_triton.py:240-254)."""
-    dot = np.einsum("trd,tld->trl", dq8.astype(np.int32), g8.astype(np.int32))
+    dot = np.matmul(dq8.astype(np.float64), np.swapaxes(g8.astype(np.float64), 1, 2))
     sc = dot.astype(F32) * (sdq[:, :, None] * sg[:, None, :]).astype(F32)
     return (sc.max(1) + lz).astype(F32)
 
@@ -187,7 +187,8 @@ def tile_attention(qt, q8, sq, dq8, sdq, g8, sg, lz, vb, excl, idx, k8, ks, v, l
     near : logit = (q8 . k8_j) * (sq * ks_j * scale) over the tokens of the routed leaves, value v_j
     tail : logit = bf16(q) . bf16(tk_j) * scale (<= 16 keys) or the float32 product (> 16 keys),
            value tv_j (h3/htrc_flat_triton.py:187-207, :381-388)
-    P is rounded to bfloat16 for the value product; the normaliser sums float32 P."""
+    P is rounded to bfloat16 for the value product (not for a > 16-key tail, whose partial the
+    reference forms in float32 on the host); the normaliser sums float32 P."""
     nt, T, d = qt.shape
     nb = lz.shape[1]
     v = np.asarray(v, dtype=F32)
@@ -203,19 +204,21 @@ def tile_attention(qt, q8, sq, dq8, sdq, g8, sg, lz, vb, excl, idx, k8, ks, v, l
     else:
         tk = tv = None
     for t in range(nt):
-        parts_s, parts_v = [], []
+        parts_s, parts_v, parts_r = [], [], []
         keep = excl[t] == 0
         if keep.any():
-            dot = dq8[t].astype(np.int32) @ g8[t][keep].astype(np.int32).T
+            dot = dq8[t].astype(np.float64) @ g8[t][keep].astype(np.float64).T
             sc = dot.astype(F32) * (sdq[t][:, None] * sg[t][keep][None, :]).astype(F32) + lz[t][keep][None, :]
             parts_s.append(sc.astype(F32))
             parts_v.append(vb[t][keep])
+            parts_r.append(np.ones(sc.shape[1], bool))
         if idx.shape[1]:
             tok = (idx[t][:, None].astype(np.int64) * leaf + ar[None, :]).reshape(-1)
-            dot = q8[t].astype(np.int32) @ k8[tok].astype(np.int32).T
+            dot = q8[t].astype(np.float64) @ k8[tok].astype(np.float64).T
             sc = dot.astype(F32) * ((sq[t][:, None] * ks[tok][None, :]).astype(F32) * F32(scale)).astype(F32)
             parts_s.append(sc.astype(F32))
             parts_v.append(v[tok])
+            parts_r.append(np.ones(sc.shape[1], bool))
         if tk is not None:
             if small:
                 sc = (bf16_round(qt[t]).astype(np.float64) @ tk.astype(np.float64).T).astype(F32) * F32(scale)
@@ -223,12 +226,15 @@ def tile_attention(qt, q8, sq, dq8, sdq, g8, sg, lz, vb, excl, idx, k8, ks, v, l
                 sc = (qt[t].astype(np.float64) @ tk.astype(np.float64).T).astype(F32) * F32(scale)
             parts_s.append(sc.astype(F32))
             parts_v.append(tv)
+            parts_r.append(np.full(sc.shape[1], small))
         s = np.concatenate(parts_s, 1).astype(np.float64)
         vv = np.concatenate(parts_v, 0).astype(np.float64)
+        rnd = np.concatenate(parts_r)
         m = s.max(1, keepdims=True)
         p = np.exp(s - m)
         den = p.sum(1)
-        num = bf16_round(p.astype(F32)).astype(np.float64) @ vv
+        pq = np.where(rnd[None, :], bf16_round(p.astype(F32)).astype(np.float64), p)
+        num = pq @ vv
         out[t] = (num / np.maximum(den, 1e-30)[:, None]).astype(F32)
         lse[t] = (m[:, 0] + np.log(den)).astype(F32)
     return out.reshape(nt * T, d), lse.reshape(nt * T)
@@ -353,6 +359,47 @@ def flat_attention(q, k, v, *, tile=64, exact_leaves=256, leaf=64, scale=None, s
         return out, lse
     return out, lse, dict(k8=k8, ks=ks, qt=qt, mu=mu, g=g, g8=g8, sg=sg, lz=lz, vb=vb, q8=q8,
                           sq=sq, dq8=dq8, sdq=sdq, sel=sel, idx=idx, excl=excl)
+
+
+def prepare_head(q, k, v, *, tile=64, leaf=64):
+    """Per-head work of the production path that does not depend on the query tile: bf16 keys and
+    values, the key INT8 pack (h3/htrc_flat.py:211-219) and the tile centres (:142-156)."""
+    q = np.asarray(q, dtype=F32)
+    kb = bf16_round(np.asarray(k, dtype=F32))
+    vb = bf16_round(np.asarray(v, dtype=F32))
+    if kb.shape[0] % leaf:
+        raise ValueError("key count must be a multiple of the leaf size")
+    k8, ks = pack_rows_half_even(kb)
+    qt, mu, n = tile_centres(q, tile)
+    return dict(k=kb, v=vb, k8=k8, ks=ks, qt=qt, mu=mu, n=n, leaf=leaf)
+
+
+def attention_tiles(prep, tiles, *, exact_leaves=256, scale=None, sink_leaves=0, tail=None):
+    """The production path for a subset of query tiles of a prepared head (every tile is independent
+    given the keys): returns (out float32 [len(tiles)*T, D], lse float32 [len(tiles)*T]) for the
+    rows of those tiles, padding rows included."""
+    k, v, leaf = prep["k"], prep["v"], prep["leaf"]
+    d = k.shape[1]
+    scale = 1.0 / math.sqrt(d) if scale is None else float(scale)
+    tiles = np.asarray(tiles, dtype=np.int64)
+    qt, mu = prep["qt"][tiles], prep["mu"][tiles]
+    nb = k.shape[0] // leaf
+    g, lz, vbf = leaf_stats(mu, k, v, leaf, scale)
+    g8, sg, vb = state_int8(g, vbf)
+    q8, sq, dq8, sdq = query_codes(qt, mu)
+    sink = max(0, min(int(sink_leaves), nb))
+    kx = min(int(exact_leaves) + sink, nb)
+    sel = rowmax_select(dq8, sdq, g8, sg, lz) if kx > 0 else np.zeros((len(tiles), nb), F32)
+    idx, excl = route(sel, exact_leaves, sink)
+    return tile_attention(qt, q8, sq, dq8, sdq, g8, sg, lz, vb, excl, idx, prep["k8"], prep["ks"], v, leaf, scale,
+                          tail=tail)
+
+
+def flat_attention_tiles(q, k, v, tiles, *, tile=64, exact_leaves=256, leaf=64, scale=None, sink_leaves=0,
+                         tail=None):
+    """``prepare_head`` + ``attention_tiles`` in one call."""
+    return attention_tiles(prepare_head(q, k, v, tile=tile, leaf=leaf), tiles, exact_leaves=exact_leaves,
+                           scale=scale, sink_leaves=sink_leaves, tail=tail)
 
 
 def exact_attention(q, k, v, scale=None, tail=None):

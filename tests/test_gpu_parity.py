@@ -180,6 +180,47 @@ def test_tile_attention_on_device_state(dev, grid, seed, E, trim):
 GOLDEN64 = ["base", "ragged", "sink_tail", "all_exact", "no_exact", "big_tail", "wide"]
 
 
+def _check_against(out, lse, st, ref_out, ref_lse, ref_excl, ref_sel, n, kx, oracle_on_device_state, strict=True):
+    """Operator parity in the presence of routing: agreement >= 99.9% of (tile, leaf) pairs; every
+    disagreement a near-tie at the selection threshold; out max-abs on the tiles whose routing agrees;
+    log-Z mean-abs over all rows; and, fed the device's own stage outputs, the oracle matches every row."""
+    nb = st["nb"]
+    ex = _np(st["excl"])[:, :nb]
+    agree = (ex == ref_excl).mean()
+    assert agree >= ROUTE_AGREE, agree
+    flips = np.argwhere(ex != ref_excl)
+    if len(flips) and ref_sel is not None:
+        srt = -np.sort(-ref_sel, axis=1)
+        for t, l in flips:
+            thr = srt[t, kx - 1]
+            assert abs(ref_sel[t, l] - thr) <= 2e-2 * max(1.0, abs(thr)), (t, l, ref_sel[t, l], thr)
+    same = np.repeat((ex == ref_excl).all(1), 64)[:n]
+    o = out.cpu().numpy()
+    err = np.abs(o[same] - ref_out[same]).max(1)
+    if strict:
+        assert err.max() < OUT_TOL
+    else:
+        # independent leaf statistics: a one-LSB slope-code flip moves a far logit by up to
+        # |dq|max * |g|max / 127, so a few far-dominated rows may pass 2e-2 (see DESIGN.md)
+        assert (err < OUT_TOL).mean() >= 0.999 and err.max() < 2.5 * OUT_TOL, (err.max(), (err >= OUT_TOL).sum())
+    if ref_lse is not None:
+        assert np.abs(lse.cpu().numpy() - ref_lse).mean() < LSE_TOL
+    if oracle_on_device_state is not None:
+        o2, _ = oracle_on_device_state
+        assert np.abs(o - o2[:n]).max() < OUT_TOL
+
+
+def _oracle_on_device_state(q, v, st, tail):
+    """The oracle's far + near attention evaluated on the device's own stage outputs (identical inputs)."""
+    nb, kx, nt = st["nb"], st["kx"], st["mu"].shape[0]
+    qt, _, _ = O.tile_centres(q.float().numpy(), 64)
+    return O.tile_attention(qt, _np(st["q8"]).reshape(nt, 64, 128), _np(st["sq"]).reshape(nt, 64),
+                            _np(st["dq8"]).reshape(nt, 64, 128), _np(st["sdq"]).reshape(nt, 64), _np(st["g8"]),
+                            _np(st["sg"])[:, :nb], _np(st["lz"])[:, :nb], _np(st["vb"]), _np(st["excl"])[:, :nb],
+                            _np(st["idx"])[:, :kx], _np(st["k8"]), _np(st["ks"]), O.bf16_round(v.float().numpy()), 64,
+                            1 / math.sqrt(128), tail=tail)
+
+
 @pytest.mark.parametrize("case", GOLDEN64)
 def test_end_to_end_against_reference_fixtures(dev, golden_cases, case):
     """The whole operator against outputs recorded from the reference itself."""
@@ -193,43 +234,36 @@ def test_end_to_end_against_reference_fixtures(dev, golden_cases, case):
         tail = (torch.from_numpy(z["tail_k"]).to(dev), torch.from_numpy(z["tail_v"]).to(dev))
     cfg = {**htrc_b200.PROD, "leaf": 64, "exact_leaves": int(z["exact_leaves"]), "sink_leaves": int(z["sink_leaves"])}
     out, lse = htrc_b200.flat_attention(q, k, v, tail=tail, return_lse=True, **cfg)
-    torch.cuda.synchronize()
-    assert np.abs(out.cpu().numpy() - z["out"]).max() < OUT_TOL
-    if "lse" in z:
-        assert np.abs(lse.cpu().numpy() - z["lse"]).mean() < LSE_TOL
     st = htrc_b200.run_stages(q, k, v, tail[0] if tail else None, tail[1] if tail else None,
                               exact_leaves=cfg["exact_leaves"], sink_leaves=cfg["sink_leaves"])
     torch.cuda.synchronize()
-    nb = st["nb"]
     assert np.array_equal(_np(st["k8"]), z["k8"])
     assert np.array_equal(_np(st["ks"]).view(np.uint32), z["ks"].view(np.uint32))
-    assert (_np(st["excl"])[:, :nb] == z["excl"]).mean() >= ROUTE_AGREE
-    assert np.abs(_np(st["out"]) - z["out"]).max() < OUT_TOL
+    assert torch.equal(out, st["out"])
+    n = z["q"].shape[0]
+    _check_against(out, lse, st, z["out"], z.get("lse"), z["excl"], z.get("sel"), n, st["kx"], None)
 
 
-@pytest.mark.parametrize("grid,seed,E,sink,ntail", [((8, 32, 32), 61, 16, 0, 0), ((8, 32, 32), 62, 40, 2, 9),
-                                                     ((4, 32, 64), 63, 128, 0, 0)])
-def test_end_to_end_against_oracle(dev, grid, seed, E, sink, ntail):
+@pytest.mark.parametrize("grid,seed,E,sink,ntail,drop", [((8, 32, 32), 61, 16, 0, 0, 0), ((8, 32, 32), 62, 40, 2, 9, 64),
+                                                          ((4, 32, 64), 63, 128, 0, 0, 0), ((8, 32, 32), 64, 7, 3, 20, 128)])
+def test_end_to_end_against_oracle(dev, grid, seed, E, sink, ntail, drop):
     import htrc_b200
     q, k, v = _inputs(grid, seed)
-    tail = None
-    if ntail:
-        tk, tv = k[-ntail:].float(), v[-ntail:].float()
-        k, v = k[:-64], v[:-64]
-        tail = (tk, tv)
-    out, lse = htrc_b200.flat_attention(q.to(dev), k.to(dev), v.to(dev),
-                                        tail=(tail[0].to(dev), tail[1].to(dev)) if tail else None, return_lse=True,
-                                        **{**htrc_b200.PROD, "leaf": 64, "exact_leaves": E, "sink_leaves": sink})
+    tail = (k[-ntail:].float(), v[-ntail:].float()) if ntail else None
+    if drop:
+        k, v = k[:-drop], v[:-drop]
+    tail_d = (tail[0].to(dev), tail[1].to(dev)) if tail else None
+    cfg = {**htrc_b200.PROD, "leaf": 64, "exact_leaves": E, "sink_leaves": sink}
+    out, lse = htrc_b200.flat_attention(q.to(dev), k.to(dev), v.to(dev), tail=tail_d, return_lse=True, **cfg)
+    st = htrc_b200.run_stages(q.to(dev), k.to(dev), v.to(dev), *(tail_d or (None, None)), exact_leaves=E,
+                              sink_leaves=sink)
     torch.cuda.synchronize()
+    assert torch.equal(out, st["out"])
+    tnp = (tail[0].numpy(), tail[1].numpy()) if tail else None
     ro, rl, rst = O.flat_attention(q.float().numpy(), k.float().numpy(), v.float().numpy(), leaf=64,
-                                   exact_leaves=E, sink_leaves=sink,
-                                   tail=(tail[0].numpy(), tail[1].numpy()) if tail else None, return_stages=True)
-    assert np.abs(out.cpu().numpy() - ro).max() < OUT_TOL
-    assert np.abs(lse.cpu().numpy() - rl).mean() < LSE_TOL
-    st = htrc_b200.run_stages(q.to(dev), k.to(dev), v.to(dev), exact_leaves=E, sink_leaves=sink)
-    torch.cuda.synchronize()
-    nb = st["nb"]
-    assert (_np(st["excl"])[:, :nb] == rst["excl"]).mean() >= ROUTE_AGREE
+                                   exact_leaves=E, sink_leaves=sink, tail=tnp, return_stages=True)
+    same_state = _oracle_on_device_state(q, v, st, tnp)
+    _check_against(out, lse, st, ro, rl, rst["excl"], rst["sel"], q.shape[0], st["kx"], same_state, strict=False)
 
 
 def test_fused_forward_equals_staged(dev):
