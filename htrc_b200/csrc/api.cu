@@ -419,6 +419,7 @@ const char* htrc_strerror(int code) {
     case HTRC_ERR_WORKSPACE: return "workspace missing, misaligned or too small";
     case HTRC_ERR_CUDA: return "CUDA runtime error";
     case HTRC_ERR_DEVICE: return "no sm_100 device or device-side failure";
+    case HTRC_ERR_TOO_LARGE: return "problem needs more scratch than the 64 MiB static workspace of htrc_flat_forward_static_ws";
     default: return "unknown error";
   }
 }

@@ -32,7 +32,8 @@ enum {
   HTRC_ERR_UNSUPPORTED = 2, /* valid for the reference but not implemented by this library */
   HTRC_ERR_WORKSPACE = 3,   /* workspace missing or smaller than htrc_flat_workspace_size() */
   HTRC_ERR_CUDA = 4,        /* a CUDA runtime call failed (launch, attribute, tensor map) */
-  HTRC_ERR_DEVICE = 5       /* no sm_100 device, or the device status word reported a failure */
+  HTRC_ERR_DEVICE = 5,      /* no sm_100 device, or the device status word reported a failure */
+  HTRC_ERR_TOO_LARGE = 6    /* htrc_flat_forward_static_ws: the problem needs more than its 64 MiB */
 };
 
 enum { HTRC_DTYPE_F32 = 0, HTRC_DTYPE_BF16 = 1 };
@@ -137,6 +138,19 @@ int htrc_tile_attention(const int8_t* q8, const float* sq, const int8_t* dq8, co
  * n_tail <= 16 with bf16 operands; :381-388 float32 for longer tails): tail_part [N, dim + 2]. */
 int htrc_tail_partial(const void* q, int32_t q_dtype, int64_t n_queries, int32_t dim, const float* tail_k,
                       const float* tail_v, int32_t n_tail, float scale, float* tail_part, htrc_stream_t stream);
+
+/* The forward pass for callers that cannot allocate device memory (a plugin host that owns all device
+ * allocations and lends only input and output buffers, or an embedding whose device footprint must not
+ * grow after start-up).  Same arguments and results as htrc_flat_forward, except that args->workspace
+ * and args->workspace_bytes are ignored: the scratch lives in a 64 MiB array declared in the library
+ * (held on every GPU that uses this entry point until the process exits).  Problems whose
+ * htrc_flat_workspace_size() exceeds 64 MiB are rejected with HTRC_ERR_TOO_LARGE (about 16k queries
+ * and keys at the default routing; a smaller tile_chunk admits more).  All calls share the array: calls
+ * that overlap on the GPU race, so issue them in order on one stream.  The status word is cleared at
+ * the start of every call and is not readable through htrc_flat_status.  The first call on a device
+ * looks up the array's address; make it before any stream capture.  Allocates nothing.
+ * This entry point has no counterpart in the reference. */
+int htrc_flat_forward_static_ws(const HtrcFlatArgs* args, htrc_stream_t stream);
 
 /* Human-readable name of a return code. */
 const char* htrc_strerror(int code);
