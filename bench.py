@@ -41,6 +41,9 @@ WORKLOADS = {
                  name="cfg3: 129,024-token 32x48x84 latent layer, 24 heads, d128, leaf 64, tile 64, fast (E=256), INT8"),
     "cfg2": dict(grid=(16, 32, 32), heads=24, exact_leaves=256,
                  name="cfg2: 16,384-token 16x32x32 latent layer, 24 heads, d128, leaf 64, tile 64, fast (E=256), INT8"),
+    # profiling-sized case: one head, half of cfg3's frames (leaf state ~400 MB > L2, < 1 GB on the device)
+    "prof": dict(grid=(16, 48, 84), heads=1, exact_leaves=256,
+                 name="prof: one 64,512-token 16x48x84 head, d128, leaf 64, tile 64, fast (E=256), INT8"),
 }
 LAUNCHES_PER_HEAD = 6      # key pack, tile prep, leaf stats, row-max, route, tile attention
 

@@ -17,7 +17,7 @@ constexpr int kDim = 128;
 constexpr int kTile = 64;
 constexpr int kLeaf = 64;
 constexpr int64_t kMaxLeaves = 8192;
-constexpr int64_t kMaxRouted = 1536;
+constexpr int64_t kMaxRouted = 1024;
 
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::once_flag g_encode_once;
@@ -415,7 +415,7 @@ const char* htrc_strerror(int code) {
   switch (code) {
     case HTRC_OK: return "ok";
     case HTRC_ERR_ARG: return "invalid argument";
-    case HTRC_ERR_UNSUPPORTED: return "unsupported configuration (needs dim 128, tile 64, leaf 64, <= 8192 leaves, <= 1536 routed leaves)";
+    case HTRC_ERR_UNSUPPORTED: return "unsupported configuration (needs dim 128, tile 64, leaf 64, <= 8192 leaves, <= 1024 routed leaves)";
     case HTRC_ERR_WORKSPACE: return "workspace missing, misaligned or too small";
     case HTRC_ERR_CUDA: return "CUDA runtime error";
     case HTRC_ERR_DEVICE: return "no sm_100 device or device-side failure";

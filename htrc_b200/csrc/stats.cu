@@ -10,8 +10,10 @@
 // This is the arithmetic of h3/htrc_flat_triton.py:41-85 (_stats_kernel, I8=1); the hi/lo splits keep
 // the products at ~2^-16 relative precision (the reference uses tf32 dots).
 //
-// Warp roles (192 threads): warp 0 TMA producer, warp 1 MMA issuer (+ TMEM owner), warps 2-5 softmax
-// and epilogue (thread row = 32 * (warp % 4) + lane, the TMEM lane it may access).
+// Warp roles (320 threads): warp 0 TMA producer, warp 1 MMA issuer (+ TMEM owner), warps 2-5 softmax
+// (S -> lz, W), warps 6-9 epilogue (G, VB -> g8/sg, vbar), which drains G/VB into registers first so
+// the next leaf's MMAs overlap its quantisation and stores.  A thread's row is 32 * (warp % 4) + lane,
+// the TMEM lane it may access.
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -61,7 +63,7 @@ __device__ __forceinline__ float ex2(float x) {
 }
 }  // namespace
 
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     leaf_stats_kernel(const __grid_constant__ CUtensorMap tm_mu_hi, const __grid_constant__ CUtensorMap tm_mu_lo,
                       const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                       const __grid_constant__ CUtensorMap tm_g8, const __grid_constant__ CUtensorMap tm_vb,
@@ -184,17 +186,15 @@ __global__ void __launch_bounds__(192, 1)
         }
       }
     }
-  } else {
-    // softmax + epilogue warpgroup
+  } else if (warp < 6) {
+    // softmax warpgroup: S -> (lz, W)
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const int64_t tloc = static_cast<int64_t>(blk) * 128 + row;   // tile index within the chunk
     const bool valid = tloc < tc;
-    const int tid_wg = threadIdx.x - 64;
     const float kLog2e = 1.4426950408889634f;
     const uint32_t wh = smem_u32(smem + kOffWHi), wl = smem_u32(smem + kOffWLo);
-    const uint32_t stg = smem_u32(smem + kOffStG), stv = smem_u32(smem + kOffStV);
     for (int j = 0; j < nl; ++j) {
       const int b = j & 1;
       const int leaf = l_begin + j;
@@ -250,38 +250,66 @@ __global__ void __launch_bounds__(192, 1)
       }
       fence_proxy_async_smem();
       mbar_arrive(&bars->w_full);
-
-      // ---- epilogue of this leaf: G, VB rows -> g8/sg, vbar
+    }
+  } else {
+    // epilogue warpgroup: G, VB rows -> g8/sg, vbar (overlaps the softmax of the next leaf)
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const int64_t tloc = static_cast<int64_t>(blk) * 128 + row;   // tile index within the chunk
+    const bool valid = tloc < tc;
+    const int tid_wg = threadIdx.x - 192;
+    const uint32_t stg = smem_u32(smem + kOffStG), stv = smem_u32(smem + kOffStV);
+    for (int j = 0; j < nl; ++j) {
+      const int leaf = l_begin + j;
       if (!mbar_wait(&bars->gv_full, j & 1, status, abort_flag)) break;
       __syncwarp();
       tc_fence_after();
-      float g[128];
+      // pass 1 over G: the row's abs-max of g = scale * G
+      float am = 0.f;
 #pragma unroll
       for (int q4 = 0; q4 < 4; ++q4) {
         uint32_t r[32];
         tmem_ld32(tmem + lane_base + kColG + 32 * q4, r);
         tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) g[q4 * 32 + i] = __fmul_rn(__uint_as_float(r[i]), scale);
+        for (int i = 0; i < 32; ++i) am = fmaxf(am, fabsf(__fmul_rn(__uint_as_float(r[i]), scale)));
       }
-      float am = 0.f;
-#pragma unroll
-      for (int i = 0; i < 128; ++i) am = fmaxf(am, fabsf(g[i]));
       am = fmaxf(am, 1e-30f);
       const float sgv = __fmul_rn(am, 1.0f / 127.0f);
       const float rr = __fdiv_rn(127.0f, am);
       if (valid) sg_out[tloc * pitch + leaf] = sgv;
+      // pass 2: INT8 codes; then the vbar row as bf16 pairs
       uint32_t gw[32];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        uint32_t w = 0;
+      for (int q4 = 0; q4 < 4; ++q4) {
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_base + kColG + 32 * q4, r);
+        tmem_ld_wait();
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int cq = round_half_away_i8(__fmul_rn(g[4 * i + e], rr));
-          w |= (static_cast<uint32_t>(cq) & 0xFFu) << (8 * e);
+        for (int i = 0; i < 8; ++i) {
+          uint32_t w = 0;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float gv = __fmul_rn(__uint_as_float(r[4 * i + e]), scale);
+            const int cq = round_half_away_i8(__fmul_rn(gv, rr));
+            w |= (static_cast<uint32_t>(cq) & 0xFFu) << (8 * e);
+          }
+          gw[q4 * 8 + i] = w;
         }
-        gw[i] = w;
       }
+      uint32_t vbw[64];
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_base + kColV + 32 * q4, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) vbw[q4 * 16 + i] = pack_bf16x2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+      }
+      // G and VB are in registers: the next leaf's G/VB MMAs may start
+      tc_fence_before();
+      mbar_arrive(&bars->gv_empty);
       // previous TMA store must have finished reading the staging buffers
       if (tid_wg == 0) {
         bulk_wait_group_read0();
@@ -291,25 +319,11 @@ __global__ void __launch_bounds__(192, 1)
       __syncwarp();
 #pragma unroll
       for (int c = 0; c < 8; ++c) st_shared_v4(stg + sw128_off(row, c), gw[4 * c], gw[4 * c + 1], gw[4 * c + 2], gw[4 * c + 3]);
+      // vbar: 64 bf16 per 128-byte half row, 8 chunks of 16 B per half
 #pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) {
-        uint32_t r[32];
-        tmem_ld32(tmem + lane_base + kColV + 32 * q4, r);
-        tmem_ld_wait();
-        // 32 values = 64 bytes of bf16 = 4 chunks of 16 B; D cols [32*q4, 32*q4+32) -> half q4/2
-        const uint32_t half = stv + (q4 >> 1) * (128 * 128);
-#pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-          const int c = (q4 & 1) * 4 + cc;
-          st_shared_v4(half + sw128_off(row, c),
-                       pack_bf16x2(__uint_as_float(r[8 * cc + 0]), __uint_as_float(r[8 * cc + 1])),
-                       pack_bf16x2(__uint_as_float(r[8 * cc + 2]), __uint_as_float(r[8 * cc + 3])),
-                       pack_bf16x2(__uint_as_float(r[8 * cc + 4]), __uint_as_float(r[8 * cc + 5])),
-                       pack_bf16x2(__uint_as_float(r[8 * cc + 6]), __uint_as_float(r[8 * cc + 7])));
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(&bars->gv_empty);
+      for (int c = 0; c < 16; ++c)
+        st_shared_v4(stv + (c >> 3) * (128 * 128) + sw128_off(row, c & 7), vbw[4 * c], vbw[4 * c + 1], vbw[4 * c + 2],
+                     vbw[4 * c + 3]);
       fence_proxy_async_smem();
       mbar_arrive(&bars->stg_full);
       if (tid_wg == 0) {
@@ -343,7 +357,7 @@ int launch_leaf_stats(const LeafStatsMaps& maps, float* sg, float* lz, int64_t p
   by = min(by, nb);
   const int lpc = (nb + by - 1) / by;
   by = (nb + lpc - 1) / lpc;
-  leaf_stats_kernel<<<dim3(bx, by), 192, kSmemBytes, st>>>(maps.mu_hi, maps.mu_lo, maps.k, maps.v, maps.g8, maps.vb,
+  leaf_stats_kernel<<<dim3(bx, by), 320, kSmemBytes, st>>>(maps.mu_hi, maps.mu_lo, maps.k, maps.v, maps.g8, maps.vb,
                                                             sg, lz, pitch, t0, tc, nb, lpc, scale, status);
   return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
 }

@@ -1,53 +1,77 @@
 // Far field + near field of the flat HTRC operator, fused into one online softmax per query row,
-// on tcgen05 tensor cores (h3/htrc_flat_triton.py:88-211, `_tile_kernel` with I8=1, DOT=1; the split
-// merge of :257-273 is unnecessary because one CTA walks all leaves of its tiles).
+// on tcgen05 tensor cores (h3/htrc_flat_triton.py:88-211, `_tile_kernel` with I8=1, DOT=1, and the
+// split merge of :257-273).
 //
-// One CTA per pair of 64-row tiles (A = 2p, B = 2p+1).  Each tile is an M=64 MMA; tile A's accumulators
-// live in TMEM lanes {0..15} + 32k, tile B's at lane offset 16, so the 128 softmax threads each own one
-// query row.  Steps (64 columns each):
+// One CTA per pair of 64-row tiles (A = 2p, B = 2p+1).  Steps of 64 columns:
 //   far  (blocks of 64 leaves of the tile's own state): S = dq8 . g8^T (int8 -> int32),
 //        logit = S * (sdq_r * sg_l) + lz_l, excluded / padding leaves masked, value vbar_l (bf16);
 //   near (one routed 64-token leaf per step):           S = q8 . k8^T,
-//        logit = S * (sq_r * ks_j) * scale, value v_j (bf16).
-// P = exp(logit - m) goes to shared memory as bf16 and O += P . V runs as an M=64, N=128 bf16 MMA.
-// The running maximum is updated lazily: O and l are rescaled only when the maximum grows by more
-// than 2^8 (P <= 256 otherwise), so most steps never touch O.
+//        logit = S * (sq_r * ks_j * scale), value v_j (bf16).
+// Every MMA is M=64 per tile: tile A's rows live in TMEM lanes {0..15} + 32k, tile B's at lane offset
+// 16, so each softmax thread owns one query row of S, P and O.  P (bf16) is written back into the
+// TMEM columns of its S buffer and feeds O += P . V as the TMEM A operand; V comes from shared memory
+// as an MN-major B operand.
 //
-// Warp roles (192 threads): warp 0 TMA producer, warp 1 MMA issuer (+ TMEM owner), warps 2-5 softmax.
+// Two softmax warpgroups take alternate steps, each with its own running (max, sum) and O accumulator;
+// the two partials (and the tail partial) are merged in the epilogue.  The running maximum is updated
+// lazily: a thread rescales its O row only when its maximum grew by more than 2^8 (P <= 256 otherwise).
+//
+// Data movement: the QK operand of a step (g8 block or k8 leaf, plus its per-column parameters) goes
+// through a 4-slot ring freed as soon as the QK MMA completes; the PV operand (vbar block or v leaf)
+// through a 3-slot ring freed by the PV MMA; one producer lane fills each ring, so the QK operands run
+// ahead of the PV operands.  The MMA issuer takes PV(j), then QK(j + 4) into the S/P buffer PV(j) frees.
+// All waits block (a suspended thread takes no issue slots from the softmax warps).
+//
+// Warp roles (352 threads): warp 0 TMA producer, warp 1 MMA issuer (+ TMEM owner), warps 2-5 and 6-9
+// the two softmax warpgroups, warp 10 per-column constants (scale * log2 e, lz * log2 e or -inf).
 #include "common.cuh"
 #include "kernels.cuh"
 
 namespace htrc {
 
 namespace {
-constexpr int kStages = 3;
-constexpr uint32_t kXBytes = 64 * 128;                        // g8 block / k8 leaf: 64 rows x 128 B
-constexpr uint32_t kYBytes = 64 * 256;                        // vbar block / v leaf: 2 chunks of 64x64 bf16
-constexpr uint32_t kParBytes = 1024;                          // far: lz[64], sg[64], excl[64]; near: ks[64]
-constexpr uint32_t kTileStage = kXBytes + kYBytes + kParBytes;  // 25600
-constexpr uint32_t kStageBytes = 2 * kTileStage;              // 51200 (a multiple of 1024)
-constexpr uint32_t kOffQ8 = 0;                                // 2 tiles x 8 KB
-constexpr uint32_t kOffDq8 = 16384;                           // 2 tiles x 8 KB
-constexpr uint32_t kOffStage = 32768;
-constexpr uint32_t kOffP = kOffStage + kStages * kStageBytes;  // 2 tiles x 8 KB
-constexpr uint32_t kOffIdx = kOffP + 16384;                   // 2 tiles x kMaxKx int32
-constexpr int kMaxKx = 1536;
-constexpr uint32_t kOffBar = kOffIdx + 2 * kMaxKx * 4;
-constexpr uint32_t kSmemBytes = kOffBar + 256 + 1024;
-constexpr uint32_t kTmemCols = 256;
-constexpr uint32_t kColO = 128;
+constexpr int kThreads = 352;
+constexpr int kXSlots = 4;
+constexpr int kYSlots = 3;
+constexpr int kSBufs = 4;
+constexpr uint32_t kXBytes = 64 * 128;                          // g8 block / k8 leaf: 64 rows x 128 B
+constexpr uint32_t kYBytes = 64 * 256;                          // vbar block / v leaf: 2 chunks of 64x64 bf16
+constexpr uint32_t kParBytes = 1024;                            // far: lz[64], sg[64], excl[64]; near: ks[64]
+constexpr uint32_t kXTile = kXBytes + kParBytes;                // 9216 (a multiple of 1024)
+constexpr uint32_t kXSlot = 2 * kXTile;
+constexpr uint32_t kYSlot = 2 * kYBytes;
+constexpr uint32_t kOffQ8 = 0;                                  // 2 tiles x 8 KB
+constexpr uint32_t kOffDq8 = 16384;                             // 2 tiles x 8 KB
+constexpr uint32_t kOffX = 32768;
+constexpr uint32_t kOffY = kOffX + kXSlots * kXSlot;
+constexpr uint32_t kOffCC = kOffY + kYSlots * kYSlot;           // [X slot][tile][64] float2 constants
+constexpr uint32_t kOffEpi = kOffCC + kXSlots * 2 * 64 * 8;     // m1, l1 [128] each
+constexpr uint32_t kOffIdx = kOffEpi + 2 * 128 * 4;             // [tile][kMaxKx] uint16
+constexpr int kMaxKx = 1024;
+constexpr uint32_t kOffBar = kOffIdx + 2 * kMaxKx * 2;
+constexpr uint32_t kSmemBytes = kOffBar + 512 + 1024;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColS = 0;       // S/P buffer b (= step % 4) at 64 b; P uses its first 32 columns
+constexpr uint32_t kColO = 256;     // O[g] at 256 + 128 g (tile A / B by lane offset 0 / 16)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
-constexpr float kRescale = 8.0f;   // lazy-rescale threshold (log2 units)
+constexpr float kRescale = 8.0f;    // lazy-rescale threshold (log2 units)
+constexpr float kMagic = 12582912.0f;   // 1.5 * 2^23: int32 |x| < 2^22 -> float by an integer add
+constexpr int kMagicBits = 0x4B400000;
 
 struct Bars {
   uint64_t qd_full;
-  uint64_t st_full[kStages];
-  uint64_t st_empty[kStages];
-  uint64_t s_full[2];
-  uint64_t s_empty[2];
-  uint64_t p_full;
-  uint64_t pv_done;
+  uint64_t x_full[kXSlots];
+  uint64_t x_empty[kXSlots];    // QK MMA done (commit) + constants read (32 helper lanes)
+  uint64_t y_full[kYSlots];
+  uint64_t y_empty[kYSlots];    // PV MMA done (commit)
+  uint64_t cc_full[kXSlots];    // 32 helper lanes
+  uint64_t cc_empty[kXSlots];   // 128 softmax threads of the step's warpgroup
+  uint64_t s_full[kSBufs];      // QK done
+  uint64_t sp_empty[kSBufs];    // PV done: the S/P buffer may take the next QK
+  uint64_t p_full[kSBufs];      // 128 softmax threads wrote P into the buffer (and rescaled O if needed)
+  uint64_t pv_done[2];          // PV of warpgroup g done
+  uint64_t epi1;
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -57,9 +81,48 @@ __device__ __forceinline__ float ex2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+
+union F2 {
+  uint64_t u;
+  float2 f;
+};
+__device__ __forceinline__ float2 sub2(float2 a, float2 b) {
+  F2 x, y, z;
+  x.f = a; y.f = b;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(z.u) : "l"(x.u), "l"(y.u));
+  return z.f;
+}
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  F2 x, y, z;
+  x.f = a; y.f = b;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(z.u) : "l"(x.u), "l"(y.u));
+  return z.f;
+}
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  F2 x, y, w, z;
+  x.f = a; y.f = b; w.f = c;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(z.u) : "l"(x.u), "l"(y.u), "l"(w.u));
+  return z.f;
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  F2 x, y, z;
+  x.f = a; y.f = b;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(z.u) : "l"(x.u), "l"(y.u));
+  return z.f;
+}
+
+// O (+)= P . V with P from TMEM (M=64, K=16 per instruction)
+__device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 }  // namespace
 
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kThreads, 1)
     tile_attention_kernel(const __grid_constant__ CUtensorMap tm_q8, const __grid_constant__ CUtensorMap tm_dq8,
                           const __grid_constant__ CUtensorMap tm_g8, const __grid_constant__ CUtensorMap tm_vb,
                           const __grid_constant__ CUtensorMap tm_lz, const __grid_constant__ CUtensorMap tm_sg,
@@ -72,26 +135,34 @@ __global__ void __launch_bounds__(192, 1)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Bars* bars = reinterpret_cast<Bars*>(smem + kOffBar);
-  int32_t* idx_s = reinterpret_cast<int32_t*>(smem + kOffIdx);
+  uint16_t* idx_s = reinterpret_cast<uint16_t*>(smem + kOffIdx);
+  float2* cc = reinterpret_cast<float2*>(smem + kOffCC);
+  float* epi = reinterpret_cast<float*>(smem + kOffEpi);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tlocA = 2 * blockIdx.x;
   const int ntiles = (tlocA + 1 < tc) ? 2 : 1;
-  const int nn = kx;                 // near steps: one routed leaf per step
-  const int total = nf + nn;
+  const int total = nf + kx;        // far steps + near steps (one routed leaf per step)
   volatile int* abort_flag = &bars->abort_flag;
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->qd_full, 1);
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&bars->st_full[s], 1);
-      mbar_init(&bars->st_empty[s], 1);
+    for (int s = 0; s < kXSlots; ++s) {
+      mbar_init(&bars->x_full[s], 1);
+      mbar_init(&bars->x_empty[s], 1 + 32);
+      mbar_init(&bars->cc_full[s], 32);
+      mbar_init(&bars->cc_empty[s], 128);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int s = 0; s < kYSlots; ++s) {
+      mbar_init(&bars->y_full[s], 1);
+      mbar_init(&bars->y_empty[s], 1);
+    }
+    for (int b = 0; b < kSBufs; ++b) {
       mbar_init(&bars->s_full[b], 1);
-      mbar_init(&bars->s_empty[b], 128);
+      mbar_init(&bars->sp_empty[b], 1);
+      mbar_init(&bars->p_full[b], 128);
     }
-    mbar_init(&bars->p_full, 128);
-    mbar_init(&bars->pv_done, 1);
+    for (int g = 0; g < 2; ++g) mbar_init(&bars->pv_done[g], 1);
+    mbar_init(&bars->epi1, 128);
     bars->abort_flag = 0;
     fence_barrier_init();
   }
@@ -99,13 +170,13 @@ __global__ void __launch_bounds__(192, 1)
     // routed leaves of both tiles -> shared memory, range-checked
     for (int x = 0; x < ntiles; ++x) {
       const int32_t* src = idx + static_cast<int64_t>(tlocA + x) * kx;
-      for (int e = lane; e < nn; e += 32) {
+      for (int e = lane; e < kx; e += 32) {
         int leaf = __ldg(src + e);
         if (leaf < 0 || leaf >= nb) {
           flag_status(status, ST_BAD_INDEX);
           leaf = 0;
         }
-        idx_s[x * kMaxKx + e] = leaf;
+        idx_s[x * kMaxKx + e] = static_cast<uint16_t>(leaf);
       }
     }
   }
@@ -116,198 +187,278 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t tmem = bars->tmem_base;
 
   if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    // lane 0 fills the X ring (QK operands + parameters), lane 1 the Y ring (PV operands); each blocks
+    // on its own ring, so the QK operands run ahead of the PV operands
+    const uint64_t pol_stream = policy_evict_first();
+    const uint64_t pol_keep = policy_evict_last();
     if (lane == 0) {
-      const uint64_t pol_stream = policy_evict_first();
-      const uint64_t pol_keep = policy_evict_last();
       mbar_arrive_expect_tx(&bars->qd_full, 2 * kXBytes * ntiles);
       for (int x = 0; x < ntiles; ++x) {
         const int row = static_cast<int>((t0 + tlocA + x) * 64);
         tma_load_2d(smem + kOffQ8 + x * kXBytes, &tm_q8, &bars->qd_full, 0, row, pol_stream);
         tma_load_2d(smem + kOffDq8 + x * kXBytes, &tm_dq8, &bars->qd_full, 0, row, pol_stream);
       }
-      for (int j = 0; j < total; ++j) {
-        const int s = j % kStages;
-        if (j >= kStages && !mbar_wait(&bars->st_empty[s], ((j / kStages) - 1) & 1, status, abort_flag)) break;
-        uint8_t* st = smem + kOffStage + s * kStageBytes;
-        if (j < nf) {
-          mbar_arrive_expect_tx(&bars->st_full[s], (kXBytes + kYBytes + 256 + 256 + 64) * ntiles);
-          for (int x = 0; x < ntiles; ++x) {
-            uint8_t* tx = st + x * kTileStage;
-            const int tl = tlocA + x;
-            tma_load_3d(tx, &tm_g8, &bars->st_full[s], 0, j * 64, tl, pol_stream);
-            tma_load_3d(tx + kXBytes, &tm_vb, &bars->st_full[s], 0, j * 64, tl, pol_stream);
-            tma_load_3d(tx + kXBytes + kYBytes / 2, &tm_vb, &bars->st_full[s], 64, j * 64, tl, pol_stream);
-            tma_load_2d(tx + kXBytes + kYBytes, &tm_lz, &bars->st_full[s], j * 64, tl, pol_stream);
-            tma_load_2d(tx + kXBytes + kYBytes + 256, &tm_sg, &bars->st_full[s], j * 64, tl, pol_stream);
-            tma_load_2d(tx + kXBytes + kYBytes + 512, &tm_excl, &bars->st_full[s], j * 64, tl, pol_stream);
+      for (int nx = 0; nx < total; ++nx) {
+        {
+          if (nx >= kXSlots && !mbar_wait(&bars->x_empty[nx % kXSlots], ((nx / kXSlots) - 1) & 1, status, abort_flag))
+            break;
+          const int s = nx % kXSlots;
+          uint8_t* st = smem + kOffX + s * kXSlot;
+          if (nx < nf) {
+            mbar_arrive_expect_tx(&bars->x_full[s], (kXBytes + 256 + 256 + 64) * ntiles);
+            for (int x = 0; x < ntiles; ++x) {
+              uint8_t* tx = st + x * kXTile;
+              const int tl = tlocA + x;
+              tma_load_3d(tx, &tm_g8, &bars->x_full[s], 0, nx * 64, tl, pol_stream);
+              tma_load_2d(tx + kXBytes, &tm_lz, &bars->x_full[s], nx * 64, tl, pol_stream);
+              tma_load_2d(tx + kXBytes + 256, &tm_sg, &bars->x_full[s], nx * 64, tl, pol_stream);
+              tma_load_2d(tx + kXBytes + 512, &tm_excl, &bars->x_full[s], nx * 64, tl, pol_stream);
+            }
+          } else {
+            mbar_arrive_expect_tx(&bars->x_full[s], (kXBytes + 256) * ntiles);
+            for (int x = 0; x < ntiles; ++x) {
+              uint8_t* tx = st + x * kXTile;
+              const int leaf = idx_s[x * kMaxKx + (nx - nf)];
+              tma_load_2d(tx, &tm_k8, &bars->x_full[s], 0, leaf * 64, pol_keep);
+              bulk_load(tx + kXBytes, ks + static_cast<int64_t>(leaf) * 64, 256, &bars->x_full[s], pol_keep);
+            }
           }
-        } else {
-          const int e = j - nf;
-          mbar_arrive_expect_tx(&bars->st_full[s], (kXBytes + kYBytes + 256) * ntiles);
+        }
+      }
+    } else if (lane == 1) {
+      for (int ny = 0; ny < total; ++ny) {
+        {
+          if (ny >= kYSlots && !mbar_wait(&bars->y_empty[ny % kYSlots], ((ny / kYSlots) - 1) & 1, status, abort_flag))
+            break;
+          const int s = ny % kYSlots;
+          uint8_t* st = smem + kOffY + s * kYSlot;
+          mbar_arrive_expect_tx(&bars->y_full[s], kYBytes * ntiles);
           for (int x = 0; x < ntiles; ++x) {
-            uint8_t* tx = st + x * kTileStage;
-            const int leaf = idx_s[x * kMaxKx + e];
-            tma_load_2d(tx, &tm_k8, &bars->st_full[s], 0, leaf * 64, pol_keep);
-            tma_load_2d(tx + kXBytes, &tm_v, &bars->st_full[s], 0, leaf * 64, pol_keep);
-            tma_load_2d(tx + kXBytes + kYBytes / 2, &tm_v, &bars->st_full[s], 64, leaf * 64, pol_keep);
-            bulk_load(tx + kXBytes + kYBytes, ks + static_cast<int64_t>(leaf) * 64, 256, &bars->st_full[s], pol_keep);
+            uint8_t* ty = st + x * kYBytes;
+            if (ny < nf) {
+              const int tl = tlocA + x;
+              tma_load_3d(ty, &tm_vb, &bars->y_full[s], 0, ny * 64, tl, pol_stream);
+              tma_load_3d(ty + kYBytes / 2, &tm_vb, &bars->y_full[s], 64, ny * 64, tl, pol_stream);
+            } else {
+              const int leaf = idx_s[x * kMaxKx + (ny - nf)];
+              tma_load_2d(ty, &tm_v, &bars->y_full[s], 0, leaf * 64, pol_keep);
+              tma_load_2d(ty + kYBytes / 2, &tm_v, &bars->y_full[s], 64, leaf * 64, pol_keep);
+            }
           }
         }
       }
     }
   } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t id_qk = idesc_i8(64, 64);
-      const uint32_t id_pv = idesc_bf16(64, 128, false, true);
-      bool ok = mbar_wait(&bars->qd_full, 0, status, abort_flag);
-      for (int j = 0; ok && j <= total; ++j) {
-        if (j < total) {
-          const int s = j % kStages, b = j & 1;
-          if (!mbar_wait(&bars->st_full[s], (j / kStages) & 1, status, abort_flag)) break;
-          if (j >= 2 && !mbar_wait(&bars->s_empty[b], ((j >> 1) - 1) & 1, status, abort_flag)) break;
-          tc_fence_after();
-          const uint32_t a_base = smem_u32(smem + (j < nf ? kOffDq8 : kOffQ8));
-          const uint32_t st = smem_u32(smem + kOffStage + s * kStageBytes);
+      const uint32_t id_pv = idesc_bf16(64, 128, /*a_mn_major=*/false, /*b_mn_major=*/true);
+      // QK of step nq into S/P buffer nq % 4 (free once the PV of step nq - 4 is done)
+      auto issue_qk = [&](int nq) -> bool {
+        if (nq >= kSBufs && !mbar_wait(&bars->sp_empty[nq & 3], ((nq >> 2) - 1) & 1, status, abort_flag)) return false;
+        if (!mbar_wait(&bars->x_full[nq % kXSlots], (nq / kXSlots) & 1, status, abort_flag)) return false;
+        tc_fence_after();
+        {
+          const int b = nq & 3;
+          const uint32_t a_base = smem_u32(smem + (nq < nf ? kOffDq8 : kOffQ8));
+          const uint32_t st = smem_u32(smem + kOffX + (nq % kXSlots) * kXSlot);
           for (int x = 0; x < ntiles; ++x) {
-            const uint32_t d = tmem + (static_cast<uint32_t>(16 * x) << 16) + 64 * b;
+            const uint32_t d = tmem + (static_cast<uint32_t>(16 * x) << 16) + kColS + 64 * b;
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
               mma_i8(d, sw128_desc(a_base + x * kXBytes + kk * 32, 16, 1024),
-                     sw128_desc(st + x * kTileStage + kk * 32, 16, 1024), id_qk, kk != 0);
+                     sw128_desc(st + x * kXTile + kk * 32, 16, 1024), id_qk, kk != 0);
           }
           mma_commit(&bars->s_full[b]);
+          mma_commit(&bars->x_empty[nq % kXSlots]);
         }
-        if (j >= 1) {
-          const int jj = j - 1, s = jj % kStages;
-          if (!mbar_wait(&bars->p_full, jj & 1, status, abort_flag)) break;
+        return true;
+      };
+      bool ok = mbar_wait(&bars->qd_full, 0, status, abort_flag);
+      for (int j = 0; ok && j < total && j < kSBufs; ++j) ok = issue_qk(j);
+      for (int np = 0; ok && np < total; ++np) {
+        // PV of step np once its warpgroup wrote P and its Y slot landed; then the QK four steps ahead
+        // into the buffer that PV frees (the tensor pipe runs the MMAs in issue order anyway)
+        if (!mbar_wait(&bars->p_full[np & 3], (np >> 2) & 1, status, abort_flag)) break;
+        if (!mbar_wait(&bars->y_full[np % kYSlots], (np / kYSlots) & 1, status, abort_flag)) break;
+        {
           tc_fence_after();
-          const uint32_t st = smem_u32(smem + kOffStage + s * kStageBytes);
-          const uint32_t pb = smem_u32(smem + kOffP);
+          const int b = np & 3, g = np & 1, k = np >> 1;
+          const uint32_t st = smem_u32(smem + kOffY + (np % kYSlots) * kYSlot);
           for (int x = 0; x < ntiles; ++x) {
-            const uint32_t d = tmem + (static_cast<uint32_t>(16 * x) << 16) + kColO;
+            const uint32_t lane_off = static_cast<uint32_t>(16 * x) << 16;
+            const uint32_t d = tmem + lane_off + kColO + 128 * g;
+            const uint32_t a = tmem + lane_off + kColS + 64 * b;
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
-              mma_bf16(d, sw128_desc(pb + x * kXBytes + kk * 32, 16, 1024),
-                       sw128_desc(st + x * kTileStage + kXBytes + kk * 2048, kYBytes / 2, 1024), id_pv,
-                       (jj | kk) != 0);
+              mma_bf16_ts(d, a + 8 * kk, sw128_desc(st + x * kYBytes + kk * 2048, kYBytes / 2, 1024), id_pv,
+                          (k | kk) != 0);
           }
-          mma_commit(&bars->pv_done);
-          mma_commit(&bars->st_empty[s]);
+          mma_commit(&bars->pv_done[g]);
+          mma_commit(&bars->sp_empty[b]);
+          mma_commit(&bars->y_empty[np % kYSlots]);
         }
+        if (np + kSBufs < total) ok = issue_qk(np + kSBufs);
       }
     }
+  } else if (warp == 10) {
+    // ------------------------------------------------------------------ per-column constants
+    // far: (sg * log2 e, lz * log2 e or -inf if routed / past nb); near: (ks * scale * log2 e, 0)
+    const float near_scale = scale * kLog2e;
+    for (int j = 0; j < total; ++j) {
+      const int s = j % kXSlots;
+      if (!mbar_wait(&bars->x_full[s], (j / kXSlots) & 1, status, abort_flag)) break;
+      if (j >= kXSlots && !mbar_wait(&bars->cc_empty[s], ((j / kXSlots) - 1) & 1, status, abort_flag)) break;
+      const uint8_t* st = smem + kOffX + s * kXSlot;
+      float2* c = cc + s * 128;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int colq = q * 32 + lane;      // tile x = colq / 64, column colq % 64
+        const int x = colq >> 6, i = colq & 63;
+        const uint8_t* par = st + x * kXTile + kXBytes;
+        float2 v;
+        if (j < nf) {
+          const float lzv = reinterpret_cast<const float*>(par)[i];
+          const float sgv = reinterpret_cast<const float*>(par + 256)[i];
+          const bool masked = par[512 + i] != 0 || j * 64 + i >= nb;
+          v = make_float2(sgv * kLog2e, masked ? -INFINITY : lzv * kLog2e);
+        } else {
+          v = make_float2(reinterpret_cast<const float*>(par)[i] * near_scale, 0.f);
+        }
+        c[colq] = v;
+      }
+      mbar_arrive(&bars->x_empty[s]);      // the raw parameters of this slot have been read
+      mbar_arrive(&bars->cc_full[s]);
+    }
   } else {
-    // softmax warpgroup: thread -> (tile x, row r)
+    // ------------------------------------------------------------------ softmax warpgroups
+    const int g = (warp - 2) >> 2;            // warpgroup: 0 takes even steps, 1 odd steps
     const int quarter = warp & 3;
-    const int x = lane >> 4;
+    const int x = lane >> 4;                  // tile of this thread's query row
     const int r = quarter * 16 + (lane & 15);
+    const int col = x * 64 + r;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const bool has_tile = x < ntiles;
     const int64_t tl = tlocA + x;
     const int64_t gr = (t0 + tl) * 64 + r;
-    const bool valid = has_tile && gr < n;
     const float sq_r = has_tile ? __ldg(sq + gr) : 0.f;
     const float sdq_r = has_tile ? __ldg(sdq + gr) : 0.f;
-    const uint32_t p_row = smem_u32(smem + kOffP + x * kXBytes);
     float m_used = -INFINITY, l = 0.f;
     bool aborted = false;
-    for (int j = 0; j < total; ++j) {
-      const int b = j & 1, s = j % kStages;
-      if (!mbar_wait(&bars->s_full[b], (j >> 1) & 1, status, abort_flag)) { aborted = true; break; }
+    int kcount = 0;
+    for (int j = g; j < total; j += 2, ++kcount) {
+      const int s = j % kXSlots, b = j & 3;
+      if (!mbar_wait(&bars->s_full[b], (j >> 2) & 1, status, abort_flag)) { aborted = true; break; }
       __syncwarp();
       tc_fence_after();
       uint32_t d0[32], d1[32];
-      tmem_ld32(tmem + lane_base + 64 * b, d0);
-      tmem_ld32(tmem + lane_base + 64 * b + 32, d1);
+      tmem_ld32(tmem + lane_base + kColS + 64 * b, d0);
+      tmem_ld32(tmem + lane_base + kColS + 64 * b + 32, d1);
       tmem_ld_wait();
-      tc_fence_before();
-      mbar_arrive(&bars->s_empty[b]);
-      if (!mbar_wait(&bars->st_full[s], (j / kStages) & 1, status, abort_flag)) { aborted = true; break; }
-      const uint8_t* par = smem + kOffStage + s * kStageBytes + x * kTileStage + kXBytes + kYBytes;
+      if (!mbar_wait(&bars->cc_full[s], (j / kXSlots) & 1, status, abort_flag)) { aborted = true; break; }
+      const float2* c = cc + s * 128 + x * 64;
+      const float srow = j < nf ? sdq_r : sq_r;
+      const float2 srow2 = make_float2(srow, srow);
+      const float2 magic2 = make_float2(kMagic, kMagic);
       float lg[64];
-      if (j < nf) {
-        const float* lz_s = reinterpret_cast<const float*>(par);
-        const float* sg_s = reinterpret_cast<const float*>(par + 256);
-        const uint8_t* ex_s = par + 512;
-        const int lb = j * 64;
+      float mxa[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};   // independent chains
 #pragma unroll
-        for (int i = 0; i < 64; ++i) {
-          const int di = static_cast<int>(i < 32 ? d0[i] : d1[i - 32]);
-          const float v = __fadd_rn(__fmul_rn(static_cast<float>(di), __fmul_rn(sdq_r, sg_s[i])), lz_s[i]);
-          lg[i] = (ex_s[i] != 0 || lb + i >= nb) ? -INFINITY : v * kLog2e;
-        }
-      } else {
-        const float* ks_s = reinterpret_cast<const float*>(par);
-#pragma unroll
-        for (int i = 0; i < 64; ++i) {
-          const int di = static_cast<int>(i < 32 ? d0[i] : d1[i - 32]);
-          lg[i] = __fmul_rn(static_cast<float>(di), __fmul_rn(__fmul_rn(sq_r, ks_s[i]), scale)) * kLog2e;
-        }
+      for (int i = 0; i < 64; i += 2) {
+        const float4 cv = *reinterpret_cast<const float4*>(c + i);     // (c1_i, c2_i, c1_i+1, c2_i+1)
+        const uint32_t di0 = i < 32 ? d0[i] : d1[i - 32];
+        const uint32_t di1 = i < 32 ? d0[i + 1] : d1[i - 31];
+        const float2 xm = make_float2(__int_as_float(static_cast<int>(di0) + kMagicBits),
+                                      __int_as_float(static_cast<int>(di1) + kMagicBits));
+        const float2 fd = sub2(xm, magic2);
+        const float2 t = mul2(srow2, make_float2(cv.x, cv.z));
+        const float2 v = fma2(fd, t, make_float2(cv.y, cv.w));
+        lg[i] = v.x;
+        lg[i + 1] = v.y;
+        mxa[(i >> 1) & 3] = fmaxf(mxa[(i >> 1) & 3], fmaxf(v.x, v.y));
       }
-      float mx = -INFINITY;
-#pragma unroll
-      for (int i = 0; i < 64; ++i) mx = fmaxf(mx, lg[i]);
-      const float m_new = fmaxf(m_used, mx);
-      if (j >= 1 && !mbar_wait(&bars->pv_done, (j - 1) & 1, status, abort_flag)) { aborted = true; break; }
-      // lazy rescale; the TMEM access is warp-collective, so the whole warp joins when any lane needs it
+      const float mx = fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3]));
+      mbar_arrive(&bars->cc_empty[s]);
+      // rows of an absent tile B (odd tile count) hold stale TMEM: keep them inert
+      const float m_new = has_tile ? fmaxf(m_used, mx) : m_used;
       const bool need = m_new > m_used + kRescale;
       const float alpha = need ? ex2(m_used - m_new) : 1.0f;
       if (need) {
         l *= alpha;
         m_used = m_new;
       }
+      const bool live = has_tile && m_used != -INFINITY;
+      const float mref = live ? m_used : 0.f;
+      const float2 mref2 = make_float2(mref, mref);
+      uint32_t pw[32];
+      float2 rs2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+#pragma unroll
+      for (int i = 0; i < 64; i += 2) {
+        const float2 e = sub2(make_float2(lg[i], lg[i + 1]), mref2);
+        const float2 p = live ? make_float2(ex2(e.x), ex2(e.y)) : make_float2(0.f, 0.f);
+        rs2[(i >> 1) & 3] = add2(rs2[(i >> 1) & 3], p);
+        pw[i >> 1] = pack_bf16x2(p.x, p.y);
+      }
+      const float2 rsa = add2(add2(rs2[0], rs2[1]), add2(rs2[2], rs2[3]));
+      l += rsa.x + rsa.y;
+      // the O row is rescaled only after this warpgroup's previous PV is done; the whole warp takes
+      // part because TMEM loads and stores are warp-collective.  The wait is also taken on the
+      // warpgroup's last step: pv_done phases are otherwise skipped, and the epilogue's wait for the
+      // final PV is unambiguous only if the barrier is then at most one phase behind.
       __syncwarp();
-      if (j >= 1 && __any_sync(0xffffffffu, need)) {
+      const bool any_need = __any_sync(0xffffffffu, need);
+      if (kcount >= 1 && (any_need || j + 2 >= total)) {
+        if (!mbar_wait(&bars->pv_done[g], (kcount - 1) & 1, status, abort_flag)) { aborted = true; break; }
+      }
+      if (kcount >= 1 && any_need) {
+        __syncwarp();
         tc_fence_after();
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4) {
           uint32_t o[32];
-          tmem_ld32(tmem + lane_base + kColO + 32 * q4, o);
+          tmem_ld32(tmem + lane_base + kColO + 128 * g + 32 * q4, o);
           tmem_ld_wait();
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          tmem_st32(tmem + lane_base + kColO + 32 * q4, o);
+          tmem_st32(tmem + lane_base + kColO + 128 * g + 32 * q4, o);
         }
-        tmem_st_wait();
       }
-      const bool live = m_used != -INFINITY;
-      float rs = 0.f;
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        uint32_t w[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float p0 = live ? ex2(lg[c * 8 + 2 * e] - m_used) : 0.f;
-          const float p1 = live ? ex2(lg[c * 8 + 2 * e + 1] - m_used) : 0.f;
-          rs += p0 + p1;
-          w[e] = pack_bf16x2(p0, p1);
-        }
-        st_shared_v4(p_row + sw128_off(r, c), w[0], w[1], w[2], w[3]);
-      }
-      l += rs;
-      fence_proxy_async_smem();
+      tmem_st32(tmem + lane_base + kColS + 64 * b, pw);
+      tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&bars->p_full);
+      mbar_arrive(&bars->p_full[b]);
     }
-    if (!aborted && total > 0 && mbar_wait(&bars->pv_done, (total - 1) & 1, status, abort_flag)) {
+    // ---------------------------------------------------------------- epilogue
+    const bool last_ok =
+        !aborted && (kcount == 0 || mbar_wait(&bars->pv_done[g], (kcount - 1) & 1, status, abort_flag));
+    float* m1s = epi;
+    float* l1s = epi + 128;
+    if (g == 1) {
+      m1s[col] = kcount ? m_used : -INFINITY;
+      l1s[col] = l;
+      mbar_arrive(&bars->epi1);
+    } else if (last_ok && mbar_wait(&bars->epi1, 0, status, abort_flag)) {
+      const float m1 = m1s[col], l1 = l1s[col];
+      const float m0 = kcount ? m_used : -INFINITY;
+      const float n0 = m0 * kLn2, n1 = m1 * kLn2;           // natural-log units
+      const bool valid = has_tile && gr < n;
+      const float* tp = (tail_part != nullptr && valid) ? tail_part + gr * 130 : nullptr;
+      const float mt = tp ? tp[128] : -INFINITY, lt = tp ? tp[129] : 0.f;
+      const float mm = fmaxf(fmaxf(n0, n1), mt);
+      const float a0 = n0 == -INFINITY ? 0.f : expf(n0 - mm);
+      const float a1 = n1 == -INFINITY ? 0.f : expf(n1 - mm);
+      const float at = mt == -INFINITY ? 0.f : expf(mt - mm);
+      const float den = l * a0 + l1 * a1 + lt * at;
+      const float inv = 1.0f / fmaxf(den, 1e-30f);
+      const float c0 = a0 * inv, c1 = a1 * inv, ct = at * inv;
+      if (valid && lse != nullptr) lse[gr] = mm + logf(fmaxf(den, 1e-30f));
       __syncwarp();
       tc_fence_after();
-      // merge with the tail partial (natural-log units) and normalise
-      const float m1 = m_used * kLn2;
-      float wa = 1.f, wb = 0.f, den = l, mm = m1;
-      const float* tp = (tail_part != nullptr && valid) ? tail_part + gr * 130 : nullptr;
-      if (tp) {
-        const float mt = tp[128], lt = tp[129];
-        mm = fmaxf(m1, mt);
-        wa = expf(m1 - mm);
-        wb = expf(mt - mm);
-        den = l * wa + lt * wb;
-      }
-      const float inv = 1.0f / fmaxf(den, 1e-30f);
-#pragma unroll
+#pragma unroll 1
       for (int q4 = 0; q4 < 4; ++q4) {
-        uint32_t o[32];
-        tmem_ld32(tmem + lane_base + kColO + 32 * q4, o);
+        uint32_t o0[32], o1[32];
+        tmem_ld32(tmem + lane_base + kColO + 32 * q4, o0);
+        tmem_ld32(tmem + lane_base + kColO + 128 + 32 * q4, o1);
         tmem_ld_wait();
         if (valid) {
           float4* dst = reinterpret_cast<float4*>(out + gr * 128 + 32 * q4);
@@ -316,15 +467,16 @@ __global__ void __launch_bounds__(192, 1)
             float v[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              float a = __uint_as_float(o[4 * i + e]) * wa;
-              if (tp) a = fmaf(tp[32 * q4 + 4 * i + e], wb, a);
-              v[e] = a * inv;
+              float a = 0.f;
+              if (c0 != 0.f) a = __uint_as_float(o0[4 * i + e]) * c0;
+              if (c1 != 0.f) a = fmaf(__uint_as_float(o1[4 * i + e]), c1, a);
+              if (ct != 0.f) a = fmaf(tp[32 * q4 + 4 * i + e], ct, a);
+              v[e] = a;
             }
             dst[i] = make_float4(v[0], v[1], v[2], v[3]);
           }
         }
       }
-      if (valid && lse != nullptr) lse[gr] = mm + logf(fmaxf(den, 1e-30f));
     }
   }
   tc_fence_before();
@@ -336,7 +488,7 @@ __global__ void __launch_bounds__(192, 1)
 int launch_tile_attention(const TileMaps& maps, const float* sq, const float* sdq, const float* ks, const int32_t* idx,
                           int kx, int nb, int64_t n, int64_t t0, int64_t tc, float scale, const float* tail_part,
                           float* out, float* lse, int* status, cudaStream_t st) {
-  if (kx > kMaxKx) return HTRC_ERR_UNSUPPORTED;
+  if (kx > kMaxKx || nb > 65535) return HTRC_ERR_UNSUPPORTED;
   static bool attr_done[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -348,9 +500,9 @@ int launch_tile_attention(const TileMaps& maps, const float* sq, const float* sd
   }
   const int nf = kx >= nb ? 0 : (nb + 63) / 64;
   const unsigned grid = static_cast<unsigned>((tc + 1) / 2);
-  tile_attention_kernel<<<grid, 192, kSmemBytes, st>>>(maps.q8, maps.dq8, maps.g8, maps.vb, maps.lz, maps.sg,
-                                                        maps.excl, maps.k8, maps.v, sq, sdq, ks, idx, kx, nb, nf, n, t0,
-                                                        tc, scale, tail_part, out, lse, status);
+  tile_attention_kernel<<<grid, kThreads, kSmemBytes, st>>>(maps.q8, maps.dq8, maps.g8, maps.vb, maps.lz, maps.sg,
+                                                            maps.excl, maps.k8, maps.v, sq, sdq, ks, idx, kx, nb, nf,
+                                                            n, t0, tc, scale, tail_part, out, lse, status);
   return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
 }
 
