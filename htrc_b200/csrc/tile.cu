@@ -18,19 +18,22 @@
 //
 // Data movement: the QK operand of a step (g8 block or k8 leaf, plus its per-column parameters) goes
 // through a 4-slot ring freed as soon as the QK MMA completes; the PV operand (vbar block or v leaf)
-// through a 3-slot ring freed by the PV MMA; one producer lane fills each ring, so the QK operands run
-// ahead of the PV operands.  The MMA issuer takes PV(j), then QK(j + 4) into the S/P buffer PV(j) frees.
-// All waits block (a suspended thread takes no issue slots from the softmax warps).
+// through a 3-slot ring freed by the PV MMA.  The completion of PV(j) (one commit, pv_done[j % 4]) frees
+// S/P buffer j % 4 for QK(j + 4), Y slot j % 3 for step j + 3, and lets the warpgroup of step j + 2
+// rescale its O rows.  All waits block (a suspended thread takes no issue slots from the softmax warps).
+// The producer and issuer warps run converged and let one elected lane issue: a warp whose lanes take
+// different roles serialises them, since a lane suspended in an mbarrier wait holds up the others.
 //
-// Warp roles (352 threads): warp 0 TMA producer, warp 1 MMA issuer (+ TMEM owner), warps 2-5 and 6-9
-// the two softmax warpgroups, warp 10 per-column constants (scale * log2 e, lz * log2 e or -inf).
+// Warp roles (384 threads): warp 0 X-ring producer; warp 1 PV issuer (+ TMEM owner); warp 11 QK issuer
+// and Y-ring producer (both wait for the same PV completions); warps 2-5 and 6-9 the two softmax
+// warpgroups; warp 10 per-column constants (scale * log2 e, lz * log2 e or -inf).
 #include "common.cuh"
 #include "kernels.cuh"
 
 namespace htrc {
 
 namespace {
-constexpr int kThreads = 352;
+constexpr int kThreads = 384;
 constexpr int kXSlots = 4;
 constexpr int kYSlots = 3;
 constexpr int kSBufs = 4;
@@ -64,13 +67,11 @@ struct Bars {
   uint64_t x_full[kXSlots];
   uint64_t x_empty[kXSlots];    // QK MMA done (commit) + constants read (32 helper lanes)
   uint64_t y_full[kYSlots];
-  uint64_t y_empty[kYSlots];    // PV MMA done (commit)
   uint64_t cc_full[kXSlots];    // 32 helper lanes
   uint64_t cc_empty[kXSlots];   // 128 softmax threads of the step's warpgroup
   uint64_t s_full[kSBufs];      // QK done
-  uint64_t sp_empty[kSBufs];    // PV done: the S/P buffer may take the next QK
   uint64_t p_full[kSBufs];      // 128 softmax threads wrote P into the buffer (and rescaled O if needed)
-  uint64_t pv_done[2];          // PV of warpgroup g done
+  uint64_t pv_done[kSBufs];     // PV of the step in this buffer done
   uint64_t epi1;
   uint32_t tmem_base;
   int abort_flag;
@@ -111,15 +112,6 @@ __device__ __forceinline__ float2 add2(float2 a, float2 b) {
   return z.f;
 }
 
-// O (+)= P . V with P from TMEM (M=64, K=16 per instruction)
-__device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
-                                            uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
 }  // namespace
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -152,16 +144,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars->cc_full[s], 32);
       mbar_init(&bars->cc_empty[s], 128);
     }
-    for (int s = 0; s < kYSlots; ++s) {
-      mbar_init(&bars->y_full[s], 1);
-      mbar_init(&bars->y_empty[s], 1);
-    }
+    for (int s = 0; s < kYSlots; ++s) mbar_init(&bars->y_full[s], 1);
     for (int b = 0; b < kSBufs; ++b) {
       mbar_init(&bars->s_full[b], 1);
-      mbar_init(&bars->sp_empty[b], 1);
       mbar_init(&bars->p_full[b], 128);
+      mbar_init(&bars->pv_done[b], 1);
     }
-    for (int g = 0; g < 2; ++g) mbar_init(&bars->pv_done[g], 1);
     mbar_init(&bars->epi1, 128);
     bars->abort_flag = 0;
     fence_barrier_init();
@@ -187,22 +175,24 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = bars->tmem_base;
 
   if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer
-    // lane 0 fills the X ring (QK operands + parameters), lane 1 the Y ring (PV operands); each blocks
-    // on its own ring, so the QK operands run ahead of the PV operands
+    // ------------------------------------------------------------------ X-ring producer
+    // QK operands + per-column parameters, up to four steps ahead of the QK MMAs
     const uint64_t pol_stream = policy_evict_first();
     const uint64_t pol_keep = policy_evict_last();
-    if (lane == 0) {
-      mbar_arrive_expect_tx(&bars->qd_full, 2 * kXBytes * ntiles);
-      for (int x = 0; x < ntiles; ++x) {
-        const int row = static_cast<int>((t0 + tlocA + x) * 64);
-        tma_load_2d(smem + kOffQ8 + x * kXBytes, &tm_q8, &bars->qd_full, 0, row, pol_stream);
-        tma_load_2d(smem + kOffDq8 + x * kXBytes, &tm_dq8, &bars->qd_full, 0, row, pol_stream);
+    const uint32_t leader = elect_one();
+    {
+      if (leader) {
+        mbar_arrive_expect_tx(&bars->qd_full, 2 * kXBytes * ntiles);
+        for (int x = 0; x < ntiles; ++x) {
+          const int row = static_cast<int>((t0 + tlocA + x) * 64);
+          tma_load_2d(smem + kOffQ8 + x * kXBytes, &tm_q8, &bars->qd_full, 0, row, pol_stream);
+          tma_load_2d(smem + kOffDq8 + x * kXBytes, &tm_dq8, &bars->qd_full, 0, row, pol_stream);
+        }
       }
       for (int nx = 0; nx < total; ++nx) {
-        {
-          if (nx >= kXSlots && !mbar_wait(&bars->x_empty[nx % kXSlots], ((nx / kXSlots) - 1) & 1, status, abort_flag))
-            break;
+        if (nx >= kXSlots && !mbar_wait_warp(&bars->x_empty[nx % kXSlots], ((nx / kXSlots) - 1) & 1, status, abort_flag))
+          break;
+        if (leader) {
           const int s = nx % kXSlots;
           uint8_t* st = smem + kOffX + s * kXSlot;
           if (nx < nf) {
@@ -226,81 +216,99 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-    } else if (lane == 1) {
-      for (int ny = 0; ny < total; ++ny) {
-        {
-          if (ny >= kYSlots && !mbar_wait(&bars->y_empty[ny % kYSlots], ((ny / kYSlots) - 1) & 1, status, abort_flag))
-            break;
-          const int s = ny % kYSlots;
-          uint8_t* st = smem + kOffY + s * kYSlot;
-          mbar_arrive_expect_tx(&bars->y_full[s], kYBytes * ntiles);
-          for (int x = 0; x < ntiles; ++x) {
-            uint8_t* ty = st + x * kYBytes;
-            if (ny < nf) {
-              const int tl = tlocA + x;
-              tma_load_3d(ty, &tm_vb, &bars->y_full[s], 0, ny * 64, tl, pol_stream);
-              tma_load_3d(ty + kYBytes / 2, &tm_vb, &bars->y_full[s], 64, ny * 64, tl, pol_stream);
-            } else {
-              const int leaf = idx_s[x * kMaxKx + (ny - nf)];
-              tma_load_2d(ty, &tm_v, &bars->y_full[s], 0, leaf * 64, pol_keep);
-              tma_load_2d(ty + kYBytes / 2, &tm_v, &bars->y_full[s], 64, leaf * 64, pol_keep);
-            }
-          }
-        }
-      }
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      const uint32_t id_qk = idesc_i8(64, 64);
-      const uint32_t id_pv = idesc_bf16(64, 128, /*a_mn_major=*/false, /*b_mn_major=*/true);
-      // QK of step nq into S/P buffer nq % 4 (free once the PV of step nq - 4 is done)
-      auto issue_qk = [&](int nq) -> bool {
-        if (nq >= kSBufs && !mbar_wait(&bars->sp_empty[nq & 3], ((nq >> 2) - 1) & 1, status, abort_flag)) return false;
-        if (!mbar_wait(&bars->x_full[nq % kXSlots], (nq / kXSlots) & 1, status, abort_flag)) return false;
-        tc_fence_after();
-        {
-          const int b = nq & 3;
-          const uint32_t a_base = smem_u32(smem + (nq < nf ? kOffDq8 : kOffQ8));
-          const uint32_t st = smem_u32(smem + kOffX + (nq % kXSlots) * kXSlot);
-          for (int x = 0; x < ntiles; ++x) {
-            const uint32_t d = tmem + (static_cast<uint32_t>(16 * x) << 16) + kColS + 64 * b;
+    // ------------------------------------------------------------------ PV issuer
+    // O[g] += P . V for step np once its warpgroup wrote P and its Y slot landed; one commit per step.
+    // Descriptors are built from precomputed words: the start address is the low 14 bits.
+    const uint32_t leader = elect_one();
+    const uint32_t id_pv = idesc_bf16(64, 128, /*a_mn_major=*/false, /*b_mn_major=*/true);
+    const uint32_t hi = (1024u >> 4) | (1u << 14) | (2u << 29);          // SBO 1024, version, SWIZZLE_128B
+    const uint32_t lo0 = (smem_u32(smem + kOffY) >> 4) | ((kYBytes / 2) >> 4 << 16);   // + LBO (chunk stride)
+    int ys = 0;
+    uint32_t yph = 0;
+    for (int np = 0; np < total; ++np) {
+      if (!mbar_wait_warp(&bars->p_full[np & 3], (np >> 2) & 1, status, abort_flag)) break;
+      if (!mbar_wait_warp(&bars->y_full[ys], yph, status, abort_flag)) break;
+      tc_fence_after();
+      const uint32_t b = np & 3, g = np & 1, k = np >> 1;
+      const uint32_t lo = lo0 + ys * (kYSlot >> 4);
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              mma_i8(d, sw128_desc(a_base + x * kXBytes + kk * 32, 16, 1024),
-                     sw128_desc(st + x * kXTile + kk * 32, 16, 1024), id_qk, kk != 0);
-          }
-          mma_commit(&bars->s_full[b]);
-          mma_commit(&bars->x_empty[nq % kXSlots]);
-        }
-        return true;
-      };
-      bool ok = mbar_wait(&bars->qd_full, 0, status, abort_flag);
-      for (int j = 0; ok && j < total && j < kSBufs; ++j) ok = issue_qk(j);
-      for (int np = 0; ok && np < total; ++np) {
-        // PV of step np once its warpgroup wrote P and its Y slot landed; then the QK four steps ahead
-        // into the buffer that PV frees (the tensor pipe runs the MMAs in issue order anyway)
-        if (!mbar_wait(&bars->p_full[np & 3], (np >> 2) & 1, status, abort_flag)) break;
-        if (!mbar_wait(&bars->y_full[np % kYSlots], (np / kYSlots) & 1, status, abort_flag)) break;
-        {
-          tc_fence_after();
-          const int b = np & 3, g = np & 1, k = np >> 1;
-          const uint32_t st = smem_u32(smem + kOffY + (np % kYSlots) * kYSlot);
-          for (int x = 0; x < ntiles; ++x) {
-            const uint32_t lane_off = static_cast<uint32_t>(16 * x) << 16;
-            const uint32_t d = tmem + lane_off + kColO + 128 * g;
-            const uint32_t a = tmem + lane_off + kColS + 64 * b;
+      for (int x = 0; x < 2; ++x) {
+        if (x < ntiles) {
+          const uint32_t lane_off = static_cast<uint32_t>(16 * x) << 16;
+          const uint32_t d = tmem + lane_off + kColO + 128 * g;
+          const uint32_t a = tmem + lane_off + kColS + 64 * b;
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              mma_bf16_ts(d, a + 8 * kk, sw128_desc(st + x * kYBytes + kk * 2048, kYBytes / 2, 1024), id_pv,
-                          (k | kk) != 0);
-          }
-          mma_commit(&bars->pv_done[g]);
-          mma_commit(&bars->sp_empty[b]);
-          mma_commit(&bars->y_empty[np % kYSlots]);
+          for (int kk = 0; kk < 4; ++kk)
+            mma_bf16_ts_by(leader, d, a + 8 * kk,
+                           (static_cast<uint64_t>(hi) << 32) | (lo + ((x * kYBytes + kk * 2048) >> 4)), id_pv,
+                           (k | kk) != 0);
         }
-        if (np + kSBufs < total) ok = issue_qk(np + kSBufs);
       }
+      mma_commit_by(leader, &bars->pv_done[b]);
+      if (++ys == kYSlots) { ys = 0; yph ^= 1; }
+    }
+  } else if (warp == 11) {
+    // ------------------------------------------------------------------ QK issuer + Y-ring producer
+    // Both wait for PV(j): it frees S/P buffer j % 4 for QK(j + 4) and Y slot j % 3 for step j + 3.
+    const uint64_t pol_stream = policy_evict_first();
+    const uint64_t pol_keep = policy_evict_last();
+    const uint32_t leader = elect_one();
+    const uint32_t id_qk = idesc_i8(64, 64);
+    const uint32_t hi = (1024u >> 4) | (1u << 14) | (2u << 29);
+    const uint32_t lo_q8 = (smem_u32(smem + kOffQ8) >> 4) | (1u << 16);      // LBO 16 (unused for SW128 K-major)
+    const uint32_t lo_dq8 = (smem_u32(smem + kOffDq8) >> 4) | (1u << 16);
+    const uint32_t lo_x = (smem_u32(smem + kOffX) >> 4) | (1u << 16);
+    auto produce_y = [&](int ny) {
+      if (leader) {
+        const int s = ny % kYSlots;
+        uint8_t* st = smem + kOffY + s * kYSlot;
+        mbar_arrive_expect_tx(&bars->y_full[s], kYBytes * ntiles);
+        for (int x = 0; x < ntiles; ++x) {
+          uint8_t* ty = st + x * kYBytes;
+          if (ny < nf) {
+            const int tl = tlocA + x;
+            tma_load_3d(ty, &tm_vb, &bars->y_full[s], 0, ny * 64, tl, pol_stream);
+            tma_load_3d(ty + kYBytes / 2, &tm_vb, &bars->y_full[s], 64, ny * 64, tl, pol_stream);
+          } else {
+            const int leaf = idx_s[x * kMaxKx + (ny - nf)];
+            tma_load_2d(ty, &tm_v, &bars->y_full[s], 0, leaf * 64, pol_keep);
+            tma_load_2d(ty + kYBytes / 2, &tm_v, &bars->y_full[s], 64, leaf * 64, pol_keep);
+          }
+        }
+      }
+      __syncwarp();
+    };
+    // QK of step nq into S/P buffer nq % 4, once its X slot landed
+    auto issue_qk = [&](int nq) -> bool {
+      const int s = nq % kXSlots;
+      if (!mbar_wait_warp(&bars->x_full[s], (nq / kXSlots) & 1, status, abort_flag)) return false;
+      tc_fence_after();
+      const uint32_t b = nq & 3;
+      const uint32_t la = nq < nf ? lo_dq8 : lo_q8;
+      const uint32_t lb = lo_x + s * (kXSlot >> 4);
+#pragma unroll
+      for (int x = 0; x < 2; ++x) {
+        if (x < ntiles) {
+          const uint32_t d = tmem + (static_cast<uint32_t>(16 * x) << 16) + kColS + 64 * b;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_i8_by(leader, d, (static_cast<uint64_t>(hi) << 32) | (la + ((x * kXBytes + kk * 32) >> 4)),
+                      (static_cast<uint64_t>(hi) << 32) | (lb + ((x * kXTile + kk * 32) >> 4)), id_qk, kk != 0);
+        }
+      }
+      mma_commit_by(leader, &bars->s_full[b]);
+      mma_commit_by(leader, &bars->x_empty[s]);
+      return true;
+    };
+    bool ok = mbar_wait_warp(&bars->qd_full, 0, status, abort_flag);
+    for (int j = 0; j < total && j < kYSlots; ++j) produce_y(j);
+    for (int j = 0; ok && j < total && j < kSBufs; ++j) ok = issue_qk(j);
+    for (int j = 0; ok && j + kYSlots < total; ++j) {
+      if (!mbar_wait_warp(&bars->pv_done[j & 3], (j >> 2) & 1, status, abort_flag)) break;
+      produce_y(j + kYSlots);
+      if (j + kSBufs < total) ok = issue_qk(j + kSBufs);
     }
   } else if (warp == 10) {
     // ------------------------------------------------------------------ per-column constants
@@ -308,8 +316,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float near_scale = scale * kLog2e;
     for (int j = 0; j < total; ++j) {
       const int s = j % kXSlots;
-      if (!mbar_wait(&bars->x_full[s], (j / kXSlots) & 1, status, abort_flag)) break;
-      if (j >= kXSlots && !mbar_wait(&bars->cc_empty[s], ((j / kXSlots) - 1) & 1, status, abort_flag)) break;
+      if (!mbar_wait_warp(&bars->x_full[s], (j / kXSlots) & 1, status, abort_flag)) break;
+      if (j >= kXSlots && !mbar_wait_warp(&bars->cc_empty[s], ((j / kXSlots) - 1) & 1, status, abort_flag)) break;
       const uint8_t* st = smem + kOffX + s * kXSlot;
       float2* c = cc + s * 128;
 #pragma unroll
@@ -349,14 +357,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     int kcount = 0;
     for (int j = g; j < total; j += 2, ++kcount) {
       const int s = j % kXSlots, b = j & 3;
-      if (!mbar_wait(&bars->s_full[b], (j >> 2) & 1, status, abort_flag)) { aborted = true; break; }
+      if (!mbar_wait_warp(&bars->s_full[b], (j >> 2) & 1, status, abort_flag)) { aborted = true; break; }
       __syncwarp();
       tc_fence_after();
       uint32_t d0[32], d1[32];
       tmem_ld32(tmem + lane_base + kColS + 64 * b, d0);
       tmem_ld32(tmem + lane_base + kColS + 64 * b + 32, d1);
       tmem_ld_wait();
-      if (!mbar_wait(&bars->cc_full[s], (j / kXSlots) & 1, status, abort_flag)) { aborted = true; break; }
+      if (!mbar_wait_warp(&bars->cc_full[s], (j / kXSlots) & 1, status, abort_flag)) { aborted = true; break; }
       const float2* c = cc + s * 128 + x * 64;
       const float srow = j < nf ? sdq_r : sq_r;
       const float2 srow2 = make_float2(srow, srow);
@@ -401,16 +409,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const float2 rsa = add2(add2(rs2[0], rs2[1]), add2(rs2[2], rs2[3]));
       l += rsa.x + rsa.y;
-      // the O row is rescaled only after this warpgroup's previous PV is done; the whole warp takes
-      // part because TMEM loads and stores are warp-collective.  The wait is also taken on the
-      // warpgroup's last step: pv_done phases are otherwise skipped, and the epilogue's wait for the
-      // final PV is unambiguous only if the barrier is then at most one phase behind.
+      // the O row is rescaled only after this warpgroup's previous PV (step j - 2) is done; the whole
+      // warp takes part because TMEM loads and stores are warp-collective.  pv_done[(j - 2) % 4] is then
+      // at most one phase behind: QK(j - 2) was issued after PV(j - 6) completed.
       __syncwarp();
       const bool any_need = __any_sync(0xffffffffu, need);
-      if (kcount >= 1 && (any_need || j + 2 >= total)) {
-        if (!mbar_wait(&bars->pv_done[g], (kcount - 1) & 1, status, abort_flag)) { aborted = true; break; }
-      }
       if (kcount >= 1 && any_need) {
+        if (!mbar_wait_warp(&bars->pv_done[(j - 2) & 3], ((j - 2) >> 2) & 1, status, abort_flag)) {
+          aborted = true;
+          break;
+        }
         __syncwarp();
         tc_fence_after();
 #pragma unroll
@@ -429,15 +437,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(&bars->p_full[b]);
     }
     // ---------------------------------------------------------------- epilogue
+    const int jl = g + 2 * (kcount - 1);     // this warpgroup's last step
     const bool last_ok =
-        !aborted && (kcount == 0 || mbar_wait(&bars->pv_done[g], (kcount - 1) & 1, status, abort_flag));
+        !aborted && (kcount == 0 || mbar_wait_warp(&bars->pv_done[jl & 3], (jl >> 2) & 1, status, abort_flag));
     float* m1s = epi;
     float* l1s = epi + 128;
     if (g == 1) {
       m1s[col] = kcount ? m_used : -INFINITY;
       l1s[col] = l;
       mbar_arrive(&bars->epi1);
-    } else if (last_ok && mbar_wait(&bars->epi1, 0, status, abort_flag)) {
+    } else if (last_ok && mbar_wait_warp(&bars->epi1, 0, status, abort_flag)) {
       const float m1 = m1s[col], l1 = l1s[col];
       const float m0 = kcount ? m_used : -INFINITY;
       const float n0 = m0 * kLn2, n1 = m1 * kLn2;           // natural-log units
