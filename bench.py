@@ -188,7 +188,7 @@ def run_ours(a, wl, rank, world, local_rank):
 
     import htrc_b200
     from htrc_b200 import flat as F
-    from htrc_b200 import synth
+    from htrc_b200 import shard, synth
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
@@ -196,9 +196,10 @@ def run_ours(a, wl, rank, world, local_rank):
     if world > 1:
         import torch.distributed as dist
     H = wl["heads"]
-    if H % world:
-        raise SystemExit(f"{H} heads do not split over {world} ranks")
-    my_heads = list(range(rank * H // world, (rank + 1) * H // world))
+    try:
+        my_heads = list(shard.heads_of_rank(H, rank, world))
+    except ValueError as e:
+        raise SystemExit(str(e))
     E = wl["exact_leaves"]
 
     # ---- inputs: pinned host copies (for e2e) and device-resident copies (for the device timing)
@@ -234,7 +235,7 @@ def run_ours(a, wl, rank, world, local_rank):
                 ev_done[i].record(comp)
                 side.wait_event(ev_done[i])
                 with torch.cuda.stream(side):
-                    dist.all_gather_into_tensor(gathered[i], obf[h])
+                    shard.gather_slot(obf[h], out=gathered[i])
         if world > 1:
             comp.wait_stream(side)
 

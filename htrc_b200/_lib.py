@@ -79,8 +79,10 @@ def check(rc: int, what: str) -> None:
     if rc == HTRC_OK:
         return
     msg = f"{what}: {lib().htrc_strerror(rc).decode()}"
-    if rc in (HTRC_ERR_ARG, HTRC_ERR_UNSUPPORTED):
+    if rc == HTRC_ERR_ARG:
         raise ValueError(msg)
+    if rc == HTRC_ERR_UNSUPPORTED:
+        raise NotImplementedError(msg)
     if rc in (HTRC_ERR_WORKSPACE, HTRC_ERR_TOO_LARGE):
         raise MemoryError(msg)
     raise HtrcError(msg)

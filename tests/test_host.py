@@ -1,0 +1,162 @@
+"""Host-side checks that need no GPU: the C-ABI library loads and exports every function the header
+declares, its argument validation and error names, and the Python layer's argument errors and memory
+planning (h3/htrc_flat.py:118-132, :187-212; h3/htrc_flat_runner.py:61-84)."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+import htrc_b200
+from htrc_b200 import _lib, runner
+from htrc_b200 import flat as F
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "htrc_flat.h"
+
+
+def _declared_functions():
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    return sorted(set(re.findall(r"\b(htrc_\w+)\s*\(", text)))
+
+
+def _args(n=4096, m=4096, E=16, sink=0, dim=128, tile=64, leaf=64, chunk=0, ntail=0):
+    a = _lib.HtrcFlatArgs()
+    a.q_dtype = _lib.DTYPE_BF16
+    a.n_queries, a.n_keys = n, m
+    a.dim, a.tile, a.leaf = dim, tile, leaf
+    a.exact_leaves, a.sink_leaves, a.tile_chunk, a.n_tail = E, sink, chunk, ntail
+    return a
+
+
+def test_library_exports_every_declared_symbol():
+    names = _declared_functions()
+    assert len(names) >= 13, names
+    so = ctypes.CDLL(str(_lib.LIB_PATH))
+    missing = [n for n in names if not hasattr(so, n)]
+    assert not missing, missing
+    # and the Python binding declares a signature for each
+    assert set(names) <= set(_lib.SIGNATURES), set(names) - set(_lib.SIGNATURES)
+
+
+def test_strerror_names_every_code():
+    L = _lib.lib()
+    seen = set()
+    for code in range(7):
+        s = L.htrc_strerror(code)
+        assert isinstance(s, bytes) and s and s != b"unknown error"
+        seen.add(s)
+    assert len(seen) == 7
+    assert L.htrc_strerror(99) == b"unknown error"
+
+
+def test_leaf_pitch():
+    for nb in (1, 15, 16, 17, 2016, 8192):
+        p = F.leaf_pitch(nb)
+        assert p >= nb and p % 16 == 0 and p - nb < 16
+
+
+def test_workspace_size_validation():
+    L = _lib.lib()
+    nbytes = ctypes.c_size_t()
+    size = lambda a: L.htrc_flat_workspace_size(ctypes.byref(a), ctypes.byref(nbytes))
+    assert size(_args()) == _lib.HTRC_OK and nbytes.value > 0
+    assert size(_args(m=4096 + 32)) == _lib.HTRC_ERR_ARG            # keys not a multiple of the leaf
+    assert size(_args(n=0)) == _lib.HTRC_ERR_ARG
+    assert size(_args(dim=64)) == _lib.HTRC_ERR_UNSUPPORTED
+    assert size(_args(leaf=32)) == _lib.HTRC_ERR_UNSUPPORTED
+    assert size(_args(tile=128)) == _lib.HTRC_ERR_UNSUPPORTED
+    assert size(_args(E=-1)) == _lib.HTRC_ERR_ARG
+    assert size(_args(m=64 * 9000)) == _lib.HTRC_ERR_UNSUPPORTED      # more leaves than the route kernel handles
+    assert size(_args(m=64 * 2048, E=2000)) == _lib.HTRC_ERR_UNSUPPORTED  # more routed leaves than the tile kernel
+    assert L.htrc_flat_workspace_size(ctypes.byref(_args()), None) == _lib.HTRC_ERR_ARG
+    # chunking bounds the per-chunk leaf state, so a smaller chunk needs less
+    assert size(_args(n=65536, m=65536, E=256, chunk=64)) == _lib.HTRC_OK
+    small = nbytes.value
+    assert size(_args(n=65536, m=65536, E=256, chunk=0)) == _lib.HTRC_OK
+    assert small < nbytes.value
+    assert F.workspace_bytes(65536, 65536, 256, 0, 64, 0) == small
+
+
+def test_forward_rejects_missing_pointers_before_touching_a_device():
+    L = _lib.lib()
+    a = _args()
+    assert L.htrc_flat_forward(ctypes.byref(a), None) == _lib.HTRC_ERR_ARG
+    assert L.htrc_flat_forward(None, None) == _lib.HTRC_ERR_ARG
+
+
+def test_static_workspace_entry_rejects_oversize_without_a_device():
+    L = _lib.lib()
+    a = _args(n=65536, m=65536, E=256)
+    assert L.htrc_flat_forward_static_ws(ctypes.byref(a), None) == _lib.HTRC_ERR_TOO_LARGE
+    assert b"64 MiB" in L.htrc_strerror(_lib.HTRC_ERR_TOO_LARGE)
+    assert L.htrc_flat_forward_static_ws(None, None) == _lib.HTRC_ERR_ARG
+
+
+def test_check_maps_codes_to_python_errors():
+    _lib.check(_lib.HTRC_OK, "x")
+    with pytest.raises(ValueError):
+        _lib.check(_lib.HTRC_ERR_ARG, "x")
+    with pytest.raises(NotImplementedError):
+        _lib.check(_lib.HTRC_ERR_UNSUPPORTED, "x")
+    with pytest.raises(MemoryError):
+        _lib.check(_lib.HTRC_ERR_WORKSPACE, "x")
+    with pytest.raises(MemoryError):
+        _lib.check(_lib.HTRC_ERR_TOO_LARGE, "x")
+    with pytest.raises(_lib.HtrcError):
+        _lib.check(_lib.HTRC_ERR_CUDA, "x")
+
+
+def _qkv(n=256, m=256, dtype=torch.bfloat16):
+    g = torch.Generator().manual_seed(0)
+    return (torch.randn(n, 128, generator=g).to(dtype), torch.randn(m, 128, generator=g).to(dtype),
+            torch.randn(m, 128, generator=g).to(dtype))
+
+
+def test_flat_attention_argument_errors_match_the_reference():
+    q, k, v = _qkv()
+    cfg = dict(htrc_b200.PROD, leaf=64)
+    with pytest.raises(ValueError, match="multiple of the leaf"):
+        htrc_b200.flat_attention(q, k[:200], v[:200], **cfg)
+    with pytest.raises(ValueError, match="curvature"):
+        htrc_b200.flat_attention(q, k, v, **{**cfg, "curvature": "iso"})
+    with pytest.raises(ValueError, match="dot='bf16'"):
+        htrc_b200.flat_attention(q, k, v, **{**cfg, "store": "f32"})
+    with pytest.raises(ValueError, match="unknown backend"):
+        htrc_b200.flat_attention(q, k, v, **{**cfg, "backend": "nope"})
+    with pytest.raises(ValueError, match="store='fp8'"):
+        htrc_b200.flat_attention(q, k, v, **{**cfg, "select": "bound"})
+
+
+def test_flat_attention_unimplemented_configurations_say_so():
+    q, k, v = _qkv()
+    cfg = dict(htrc_b200.PROD, leaf=64)
+    with pytest.raises(NotImplementedError, match="kmeans"):
+        htrc_b200.flat_attention(q, k, v, **{**cfg, "order": "kmeans"})
+    with pytest.raises(NotImplementedError, match="leaf"):
+        htrc_b200.flat_attention(q, k, v, **{**cfg, "leaf": 32})
+    with pytest.raises(NotImplementedError):
+        htrc_b200.flat_attention(q, k, v, **{**cfg, "store": "bf16"})
+    with pytest.raises(NotImplementedError):
+        htrc_b200.flat_attention(q, k, v, **{**cfg, "backend": "torch"})
+
+
+def test_flat_attention_has_no_cpu_path():
+    q, k, v = _qkv()
+    with pytest.raises(ValueError, match="CUDA tensors"):
+        htrc_b200.flat_attention(q, k, v, **htrc_b200.PROD, leaf=64)
+
+
+def test_plan_chunk_takes_the_largest_chunk_that_fits():
+    keys, q = 129024, 129024
+    peaks = {c: runner.predicted_peak_mib(keys, 64, c, queries=q) for c in runner.CHUNKS}
+    # the predicted peak grows with the chunk
+    vals = [peaks[c] for c in sorted(peaks)]
+    assert vals == sorted(vals)
+    for c in runner.CHUNKS:
+        free = int(peaks[c] * 2 ** 20) + 1
+        got = runner.plan_chunk(free, keys, 64, queries=q)
+        assert got == max(x for x in runner.CHUNKS if peaks[x] * 2 ** 20 <= free)
+    with pytest.raises(MemoryError):
+        runner.plan_chunk(1 << 20, keys, 64, queries=q)
