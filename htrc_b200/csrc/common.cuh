@@ -309,4 +309,46 @@ __device__ __forceinline__ int round_half_away_i8(float y) {
   return static_cast<int>(truncf(z));
 }
 
+// ------------------------------------------------------------------------------------------------
+// paired fp32 arithmetic (one instruction for two lanes of work) and a three-input maximum
+union F2U {
+  uint64_t u;
+  float2 f;
+};
+__device__ __forceinline__ float2 sub2(float2 a, float2 b) {
+  F2U x, y, z;
+  x.f = a; y.f = b;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(z.u) : "l"(x.u), "l"(y.u));
+  return z.f;
+}
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  F2U x, y, z;
+  x.f = a; y.f = b;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(z.u) : "l"(x.u), "l"(y.u));
+  return z.f;
+}
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  F2U x, y, w, z;
+  x.f = a; y.f = b; w.f = c;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(z.u) : "l"(x.u), "l"(y.u), "l"(w.u));
+  return z.f;
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  F2U x, y, z;
+  x.f = a; y.f = b;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(z.u) : "l"(x.u), "l"(y.u));
+  return z.f;
+}
+__device__ __forceinline__ float2 add2_rz(float2 a, float2 b) {   // rounded toward zero
+  F2U x, y, z;
+  x.f = a; y.f = b;
+  asm("add.rz.f32x2 %0, %1, %2;" : "=l"(z.u) : "l"(x.u), "l"(y.u));
+  return z.f;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 }  // namespace htrc

@@ -10,16 +10,20 @@
 // This is the arithmetic of h3/htrc_flat_triton.py:41-85 (_stats_kernel, I8=1); the hi/lo splits keep
 // the products at ~2^-16 relative precision (the reference uses tf32 dots).
 //
-// Warp roles (320 threads): warp 0 TMA producer, warp 1 MMA issuer (+ TMEM owner), warps 2-5 softmax
-// (S -> lz, W), warps 6-9 epilogue (G, VB -> g8/sg, vbar), which drains G/VB into registers first so
-// the next leaf's MMAs overlap its quantisation and stores.  A thread's row is 32 * (warp % 4) + lane,
-// the TMEM lane it may access.
+// Warp roles (512 threads, one role per warpgroup so that setmaxnreg can move registers from the
+// issuing warps to the arithmetic): warpgroup 0 = warp 0 TMA producer, warp 1 S issuer (+ TMEM owner),
+// warp 2 G/VB issuer, warp 3 idle; warpgroup 1 softmax (S -> lz, W); warpgroups 2 and 3 the epilogue,
+// each for half of the 128 columns of G and VB (the two halves of a row exchange their abs-max through
+// shared memory and a named barrier), so each leaf's quantisation is spread over eight warps.  A
+// thread's row is 32 * (warp % 4) + lane, the TMEM lane it may access.  The producer and issuer warps
+// run converged and let one elected lane issue.
 #include "common.cuh"
 #include "kernels.cuh"
 
 namespace htrc {
 
 namespace {
+constexpr int kThreads = 512;
 constexpr int kStages = 2;
 constexpr uint32_t kMuBytes = 128 * 128 * 2;        // one of mu_hi / mu_lo: 128 rows x 256 B
 constexpr uint32_t kLeafBytes = 64 * 128 * 2;       // K (or V) of one 64-token leaf
@@ -32,7 +36,8 @@ constexpr uint32_t kOffWHi = kOffStage + kStages * kStageBytes;
 constexpr uint32_t kOffWLo = kOffWHi + kWBytes;
 constexpr uint32_t kOffStG = kOffWLo + kWBytes;     // g8 staging: 128 rows x 128 B
 constexpr uint32_t kOffStV = kOffStG + 128 * 128;   // vbar staging: 2 x (128 rows x 128 B)
-constexpr uint32_t kOffBar = kOffStV + 2 * 128 * 128;
+constexpr uint32_t kOffAm = kOffStV + 2 * 128 * 128;  // row abs-max halves [2 (leaf parity)][2 (half)][128]
+constexpr uint32_t kOffBar = kOffAm + 2 * 2 * 128 * 4;
 constexpr uint32_t kSmemBytes = kOffBar + 256 + 1024;  // + barriers, + alignment slack
 
 constexpr uint32_t kTmemCols = 512;
@@ -49,9 +54,9 @@ struct Bars {
   uint64_t w_full;
   uint64_t w_empty;
   uint64_t gv_full;
-  uint64_t gv_empty;
-  uint64_t stg_free;   // thread 0 of the epilogue: the previous TMA store has read the staging buffers
-  uint64_t stg_full;   // the 128 epilogue threads: this leaf's rows are staged
+  uint64_t gv_empty;   // the 256 epilogue threads drained G and VB into registers
+  uint64_t stg_free;   // thread 0 of the epilogue: the previous TMA stores have read the staging buffers
+  uint64_t stg_full;   // the 256 epilogue threads: this leaf's rows are staged
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -61,9 +66,22 @@ __device__ __forceinline__ float ex2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// INT8 codes of two values y (|y| <= 127 + rounding): trunc(y + copysign(0.5, y)) with the sum rounded to
+// float first, the reference's round-half-away-from-zero codes.  z + copysign(2^23, z) rounded toward zero
+// drops the fraction; subtracting the constant again gives trunc(z) exactly, and adding 1.5 * 2^23 puts
+// the code in the low byte of the float's bits.  Returns those bits (only the low byte is used).
+__device__ __forceinline__ uint2 half_away_codes2(float2 y) {
+  const uint32_t s0 = __float_as_uint(y.x) & 0x80000000u, s1 = __float_as_uint(y.y) & 0x80000000u;
+  const float2 z = add2(y, make_float2(__uint_as_float(s0 | 0x3F000000u), __uint_as_float(s1 | 0x3F000000u)));
+  const float2 c23 = make_float2(__uint_as_float((__float_as_uint(z.x) & 0x80000000u) | 0x4B000000u),
+                                 __uint_as_float((__float_as_uint(z.y) & 0x80000000u) | 0x4B000000u));
+  const float2 t = sub2(add2_rz(z, c23), c23);
+  const float2 b = add2(t, make_float2(12582912.0f, 12582912.0f));
+  return make_uint2(__float_as_uint(b.x), __float_as_uint(b.y));
+}
 }  // namespace
 
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(kThreads, 1)
     leaf_stats_kernel(const __grid_constant__ CUtensorMap tm_mu_hi, const __grid_constant__ CUtensorMap tm_mu_lo,
                       const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                       const __grid_constant__ CUtensorMap tm_g8, const __grid_constant__ CUtensorMap tm_vb,
@@ -93,9 +111,9 @@ __global__ void __launch_bounds__(320, 1)
     mbar_init(&bars->w_full, 128);
     mbar_init(&bars->w_empty, 1);
     mbar_init(&bars->gv_full, 1);
-    mbar_init(&bars->gv_empty, 128);
+    mbar_init(&bars->gv_empty, 256);
     mbar_init(&bars->stg_free, 1);
-    mbar_init(&bars->stg_full, 128);
+    mbar_init(&bars->stg_full, 256);
     bars->abort_flag = 0;
     fence_barrier_init();
   }
@@ -105,42 +123,52 @@ __global__ void __launch_bounds__(320, 1)
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
 
-  if (warp == 0) {
-    if (lane == 0 && nl > 0) {
-      tma_prefetch_desc(&tm_mu_hi);
-      tma_prefetch_desc(&tm_k);
-      tma_prefetch_desc(&tm_v);
-      const uint64_t pol_keep = policy_evict_last();
-      const int trow = static_cast<int>(t0) + blk * 128;
-      mbar_arrive_expect_tx(&bars->mu_full, 2 * kMuBytes);
-      for (int c = 0; c < 2; ++c) {
-        tma_load_2d(smem + kOffMuHi + c * (kMuBytes / 2), &tm_mu_hi, &bars->mu_full, 64 * c, trow, pol_keep);
-        tma_load_2d(smem + kOffMuLo + c * (kMuBytes / 2), &tm_mu_lo, &bars->mu_full, 64 * c, trow, pol_keep);
+  if (warp < 4) {
+    // one setmaxnreg per warpgroup, executed by all of its warps at the same instruction
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 64;");
+    if (warp == 0) {
+      // ------------------------------------------------------------------ TMA producer
+      const uint32_t leader = elect_one();
+      if (nl > 0) {
+        const uint64_t pol_keep = policy_evict_last();
+        if (leader) {
+          tma_prefetch_desc(&tm_mu_hi);
+          tma_prefetch_desc(&tm_k);
+          tma_prefetch_desc(&tm_v);
+          const int trow = static_cast<int>(t0) + blk * 128;
+          mbar_arrive_expect_tx(&bars->mu_full, 2 * kMuBytes);
+          for (int c = 0; c < 2; ++c) {
+            tma_load_2d(smem + kOffMuHi + c * (kMuBytes / 2), &tm_mu_hi, &bars->mu_full, 64 * c, trow, pol_keep);
+            tma_load_2d(smem + kOffMuLo + c * (kMuBytes / 2), &tm_mu_lo, &bars->mu_full, 64 * c, trow, pol_keep);
+          }
+        }
+        for (int j = 0; j < nl; ++j) {
+          const int s = j % kStages;
+          if (j >= kStages && !mbar_wait_warp(&bars->kv_empty[s], ((j / kStages) - 1) & 1, status, abort_flag)) break;
+          if (leader) {
+            uint8_t* st = smem + kOffStage + s * kStageBytes;
+            const int row = (l_begin + j) * 64;
+            mbar_arrive_expect_tx(&bars->kv_full[s], kStageBytes);
+            tma_load_2d(st, &tm_k, &bars->kv_full[s], 0, row, pol_keep);
+            tma_load_2d(st + kLeafBytes / 2, &tm_k, &bars->kv_full[s], 64, row, pol_keep);
+            tma_load_2d(st + kLeafBytes, &tm_v, &bars->kv_full[s], 0, row, pol_keep);
+            tma_load_2d(st + kLeafBytes + kLeafBytes / 2, &tm_v, &bars->kv_full[s], 64, row, pol_keep);
+          }
+          __syncwarp();
+        }
       }
-      for (int j = 0; j < nl; ++j) {
-        const int s = j % kStages;
-        if (j >= kStages && !mbar_wait(&bars->kv_empty[s], ((j / kStages) - 1) & 1, status, abort_flag)) break;
-        uint8_t* st = smem + kOffStage + s * kStageBytes;
-        const int row = (l_begin + j) * 64;
-        mbar_arrive_expect_tx(&bars->kv_full[s], kStageBytes);
-        tma_load_2d(st, &tm_k, &bars->kv_full[s], 0, row, pol_keep);
-        tma_load_2d(st + kLeafBytes / 2, &tm_k, &bars->kv_full[s], 64, row, pol_keep);
-        tma_load_2d(st + kLeafBytes, &tm_v, &bars->kv_full[s], 0, row, pol_keep);
-        tma_load_2d(st + kLeafBytes + kLeafBytes / 2, &tm_v, &bars->kv_full[s], 64, row, pol_keep);
-      }
-    }
-  } else if (warp == 1) {
-    if (lane == 0 && nl > 0) {
-      const uint32_t id_s = idesc_bf16(128, 64, false, false);
-      const uint32_t id_gv = idesc_bf16(128, 128, false, true);
-      const uint32_t mu_hi = smem_u32(smem + kOffMuHi), mu_lo = smem_u32(smem + kOffMuLo);
-      const uint32_t w_hi = smem_u32(smem + kOffWHi), w_lo = smem_u32(smem + kOffWLo);
-      bool ok = mbar_wait(&bars->mu_full, 0, status, abort_flag);
-      for (int j = 0; ok && j <= nl; ++j) {
-        if (j < nl) {
+    } else if (warp == 1) {
+      // ------------------------------------------------------------------ S issuer
+      // S(j) = mu . K_j^T into S buffer j % 2 once the K/V stage landed and the softmax released it
+      const uint32_t leader = elect_one();
+      if (nl > 0) {
+        const uint32_t id_s = idesc_bf16(128, 64, false, false);
+        const uint32_t mu_hi = smem_u32(smem + kOffMuHi), mu_lo = smem_u32(smem + kOffMuLo);
+        bool ok = mbar_wait_warp(&bars->mu_full, 0, status, abort_flag);
+        for (int j = 0; ok && j < nl; ++j) {
           const int s = j % kStages, b = j & 1;
-          if (!mbar_wait(&bars->kv_full[s], (j / kStages) & 1, status, abort_flag)) break;
-          if (j >= 2 && !mbar_wait(&bars->s_empty[b], ((j >> 1) - 1) & 1, status, abort_flag)) break;
+          if (!mbar_wait_warp(&bars->kv_full[s], (j / kStages) & 1, status, abort_flag)) break;
+          if (j >= 2 && !mbar_wait_warp(&bars->s_empty[b], ((j >> 1) - 1) & 1, status, abort_flag)) break;
           tc_fence_after();
           const uint32_t kst = smem_u32(smem + kOffStage + s * kStageBytes);
           const uint32_t d = tmem + kColS + 64 * b;
@@ -152,16 +180,25 @@ __global__ void __launch_bounds__(320, 1)
               for (int kk = 0; kk < 4; ++kk) {
                 const uint64_t a = sw128_desc((h ? mu_lo : mu_hi) + c * (kMuBytes / 2) + kk * 32, 16, 1024);
                 const uint64_t bdesc = sw128_desc(kst + c * (kLeafBytes / 2) + kk * 32, 16, 1024);
-                mma_bf16(d, a, bdesc, id_s, (h | c | kk) != 0);
+                mma_bf16_by(leader, d, a, bdesc, id_s, (h | c | kk) != 0);
               }
             }
           }
-          mma_commit(&bars->s_full[b]);
+          mma_commit_by(leader, &bars->s_full[b]);
         }
-        if (j >= 1) {
-          const int jj = j - 1, s = jj % kStages;
-          if (!mbar_wait(&bars->w_full, jj & 1, status, abort_flag)) break;
-          if (jj >= 1 && !mbar_wait(&bars->gv_empty, (jj - 1) & 1, status, abort_flag)) break;
+      }
+    } else if (warp == 2) {
+      // ------------------------------------------------------------------ G/VB issuer
+      // G(j) = W . K_j and VB(j) = W_hi . V_j once the softmax wrote W and the epilogue drained the
+      // previous G/VB; their completion also releases the K/V stage (S(j) completed before W(j) existed)
+      const uint32_t leader = elect_one();
+      if (nl > 0) {
+        const uint32_t id_gv = idesc_bf16(128, 128, false, true);
+        const uint32_t w_hi = smem_u32(smem + kOffWHi), w_lo = smem_u32(smem + kOffWLo);
+        for (int j = 0; j < nl; ++j) {
+          const int s = j % kStages;
+          if (!mbar_wait_warp(&bars->w_full, j & 1, status, abort_flag)) break;
+          if (j >= 1 && !mbar_wait_warp(&bars->gv_empty, (j - 1) & 1, status, abort_flag)) break;
           tc_fence_after();
           const uint32_t kst = smem_u32(smem + kOffStage + s * kStageBytes);
           const uint32_t vst = kst + kLeafBytes;
@@ -171,23 +208,25 @@ __global__ void __launch_bounds__(320, 1)
             for (int kk = 0; kk < 4; ++kk) {
               const uint64_t a = sw128_desc((h ? w_lo : w_hi) + kk * 32, 16, 1024);
               const uint64_t bdesc = sw128_desc(kst + kk * 2048, kLeafBytes / 2, 1024);
-              mma_bf16(tmem + kColG, a, bdesc, id_gv, (h | kk) != 0);
+              mma_bf16_by(leader, tmem + kColG, a, bdesc, id_gv, (h | kk) != 0);
             }
           }
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             const uint64_t a = sw128_desc(w_hi + kk * 32, 16, 1024);
             const uint64_t bdesc = sw128_desc(vst + kk * 2048, kLeafBytes / 2, 1024);
-            mma_bf16(tmem + kColV, a, bdesc, id_gv, kk != 0);
+            mma_bf16_by(leader, tmem + kColV, a, bdesc, id_gv, kk != 0);
           }
-          mma_commit(&bars->gv_full);
-          mma_commit(&bars->w_empty);
-          mma_commit(&bars->kv_empty[s]);
+          mma_commit_by(leader, &bars->gv_full);
+          mma_commit_by(leader, &bars->w_empty);
+          mma_commit_by(leader, &bars->kv_empty[s]);
         }
       }
     }
-  } else if (warp < 6) {
-    // softmax warpgroup: S -> (lz, W)
+    // warp 3: nothing (it completes warpgroup 0 for setmaxnreg)
+  } else if (warp < 8) {
+    // ------------------------------------------------------------------ softmax warpgroup: S -> (lz, W)
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 144;");
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
@@ -215,18 +254,27 @@ __global__ void __launch_bounds__(320, 1)
       }
       tc_fence_before();
       mbar_arrive(&bars->s_empty[b]);
-      float m = -INFINITY;
+      float mxa[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      const float2 sc2 = make_float2(scale, scale);
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        a[i] = __fmul_rn(a[i], scale);
-        m = fmaxf(m, a[i]);
+      for (int i = 0; i < 64; i += 2) {
+        const float2 v = mul2(make_float2(a[i], a[i + 1]), sc2);
+        a[i] = v.x;
+        a[i + 1] = v.y;
+        mxa[(i >> 1) & 3] = max3(mxa[(i >> 1) & 3], v.x, v.y);
       }
-      float z = 0.f;
+      const float m = fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3]));
+      float2 zs[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+      const float2 m2 = make_float2(m, m), l2e2 = make_float2(kLog2e, kLog2e);
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        a[i] = ex2(__fmul_rn(a[i] - m, kLog2e));
-        z += a[i];
+      for (int i = 0; i < 64; i += 2) {
+        const float2 e = mul2(sub2(make_float2(a[i], a[i + 1]), m2), l2e2);
+        a[i] = ex2(e.x);
+        a[i + 1] = ex2(e.y);
+        zs[(i >> 1) & 3] = add2(zs[(i >> 1) & 3], make_float2(a[i], a[i + 1]));
       }
+      const float2 zz = add2(add2(zs[0], zs[1]), add2(zs[2], zs[3]));
+      const float z = zz.x + zz.y;
       const float lz = m + logf(z);
       if (valid) {
         lz_out[tloc * pitch + leaf] = lz;
@@ -239,11 +287,10 @@ __global__ void __launch_bounds__(320, 1)
         uint32_t hi[4], lo[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float w0 = a[c * 8 + 2 * e] * rz, w1 = a[c * 8 + 2 * e + 1] * rz;
-          const __nv_bfloat16 h0 = __float2bfloat16_rn(w0), h1 = __float2bfloat16_rn(w1);
-          const float l0 = w0 - __bfloat162float(h0), l1 = w1 - __bfloat162float(h1);
-          hi[e] = static_cast<uint32_t>(__bfloat16_as_ushort(h0)) | (static_cast<uint32_t>(__bfloat16_as_ushort(h1)) << 16);
-          lo[e] = pack_bf16x2(l0, l1);
+          const float2 w = mul2(make_float2(a[c * 8 + 2 * e], a[c * 8 + 2 * e + 1]), make_float2(rz, rz));
+          hi[e] = pack_bf16x2(w.x, w.y);
+          const float2 lw = sub2(w, make_float2(__uint_as_float(hi[e] << 16), __uint_as_float(hi[e] & 0xFFFF0000u)));
+          lo[e] = pack_bf16x2(lw.x, lw.y);
         }
         st_shared_v4(wh + sw128_off(row, c), hi[0], hi[1], hi[2], hi[3]);
         st_shared_v4(wl + sw128_off(row, c), lo[0], lo[1], lo[2], lo[3]);
@@ -252,81 +299,92 @@ __global__ void __launch_bounds__(320, 1)
       mbar_arrive(&bars->w_full);
     }
   } else {
-    // epilogue warpgroup: G, VB rows -> g8/sg, vbar (overlaps the softmax of the next leaf)
+    // ------------------------------------------------------------------ epilogue: G, VB -> g8/sg, vbar
+    // warpgroup 2 takes columns 0-63 of G and VB, warpgroup 3 columns 64-127; it overlaps the softmax of
+    // the next leaf
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 144;");
+    const int half = (warp - 8) >> 2;
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const int64_t tloc = static_cast<int64_t>(blk) * 128 + row;   // tile index within the chunk
     const bool valid = tloc < tc;
-    const int tid_wg = threadIdx.x - 192;
+    const bool lead = threadIdx.x == 256;             // issues the TMA stores
     const uint32_t stg = smem_u32(smem + kOffStG), stv = smem_u32(smem + kOffStV);
+    float* amx = reinterpret_cast<float*>(smem + kOffAm);
+    const uint32_t colg = kColG + 64 * half, colv = kColV + 64 * half;
     for (int j = 0; j < nl; ++j) {
       const int leaf = l_begin + j;
       if (!mbar_wait(&bars->gv_full, j & 1, status, abort_flag)) break;
       __syncwarp();
       tc_fence_after();
-      // pass 1 over G: the row's abs-max of g = scale * G
-      float am = 0.f;
+      // pass 1 over this half of G: abs-max of g = scale * G, as scale * max |G| (scale > 0 and rounding is
+      // monotonic, so this is the maximum of the rounded products)
+      float ama[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) {
+      for (int q2 = 0; q2 < 2; ++q2) {
         uint32_t r[32];
-        tmem_ld32(tmem + lane_base + kColG + 32 * q4, r);
+        tmem_ld32(tmem + lane_base + colg + 32 * q2, r);
         tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) am = fmaxf(am, fabsf(__fmul_rn(__uint_as_float(r[i]), scale)));
+        for (int i = 0; i < 32; i += 2)
+          ama[(i >> 1) & 3] = max3(ama[(i >> 1) & 3], fabsf(__uint_as_float(r[i])), fabsf(__uint_as_float(r[i + 1])));
       }
+      float am = __fmul_rn(fmaxf(fmaxf(ama[0], ama[1]), fmaxf(ama[2], ama[3])), scale);
+      // the other half of the row: exchanged through shared memory (buffered by leaf parity)
+      amx[((j & 1) * 2 + half) * 128 + row] = am;
+      named_bar_sync(1 + quarter, 64);
+      am = fmaxf(am, amx[((j & 1) * 2 + (half ^ 1)) * 128 + row]);
       am = fmaxf(am, 1e-30f);
       const float sgv = __fmul_rn(am, 1.0f / 127.0f);
       const float rr = __fdiv_rn(127.0f, am);
-      if (valid) sg_out[tloc * pitch + leaf] = sgv;
-      // pass 2: INT8 codes; then the vbar row as bf16 pairs
-      uint32_t gw[32];
+      if (valid && half == 0) sg_out[tloc * pitch + leaf] = sgv;
+      // pass 2: INT8 codes; then the vbar half row as bf16 pairs
+      uint32_t gw[16];
 #pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) {
+      for (int q2 = 0; q2 < 2; ++q2) {
         uint32_t r[32];
-        tmem_ld32(tmem + lane_base + kColG + 32 * q4, r);
+        tmem_ld32(tmem + lane_base + colg + 32 * q2, r);
         tmem_ld_wait();
+        const float2 sc2 = make_float2(scale, scale), rr2 = make_float2(rr, rr);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          uint32_t w = 0;
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float gv = __fmul_rn(__uint_as_float(r[4 * i + e]), scale);
-            const int cq = round_half_away_i8(__fmul_rn(gv, rr));
-            w |= (static_cast<uint32_t>(cq) & 0xFFu) << (8 * e);
-          }
-          gw[q4 * 8 + i] = w;
+          const uint2 c01 = half_away_codes2(mul2(mul2(make_float2(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1])), sc2), rr2));
+          const uint2 c23 = half_away_codes2(mul2(mul2(make_float2(__uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3])), sc2), rr2));
+          gw[q2 * 8 + i] = __byte_perm(__byte_perm(c01.x, c01.y, 0x0040), __byte_perm(c23.x, c23.y, 0x0040), 0x5410);
         }
       }
-      uint32_t vbw[64];
+      uint32_t vbw[32];
 #pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) {
+      for (int q2 = 0; q2 < 2; ++q2) {
         uint32_t r[32];
-        tmem_ld32(tmem + lane_base + kColV + 32 * q4, r);
+        tmem_ld32(tmem + lane_base + colv + 32 * q2, r);
         tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 16; ++i) vbw[q4 * 16 + i] = pack_bf16x2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+        for (int i = 0; i < 16; ++i) vbw[q2 * 16 + i] = pack_bf16x2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
       }
       // G and VB are in registers: the next leaf's G/VB MMAs may start
       tc_fence_before();
       mbar_arrive(&bars->gv_empty);
-      // previous TMA store must have finished reading the staging buffers
-      if (tid_wg == 0) {
+      // the previous TMA stores must have finished reading the staging buffers
+      if (lead) {
         bulk_wait_group_read0();
         mbar_arrive(&bars->stg_free);
       }
       if (!mbar_wait(&bars->stg_free, j & 1, status, abort_flag)) break;
       __syncwarp();
+      // g8: this half is the 16-byte chunks 4 half .. 4 half + 3 of the 128-byte row
 #pragma unroll
-      for (int c = 0; c < 8; ++c) st_shared_v4(stg + sw128_off(row, c), gw[4 * c], gw[4 * c + 1], gw[4 * c + 2], gw[4 * c + 3]);
-      // vbar: 64 bf16 per 128-byte half row, 8 chunks of 16 B per half
+      for (int c = 0; c < 4; ++c)
+        st_shared_v4(stg + sw128_off(row, 4 * half + c), gw[4 * c], gw[4 * c + 1], gw[4 * c + 2], gw[4 * c + 3]);
+      // vbar: this half is the 128-byte row of staging box `half`
 #pragma unroll
-      for (int c = 0; c < 16; ++c)
-        st_shared_v4(stv + (c >> 3) * (128 * 128) + sw128_off(row, c & 7), vbw[4 * c], vbw[4 * c + 1], vbw[4 * c + 2],
+      for (int c = 0; c < 8; ++c)
+        st_shared_v4(stv + half * (128 * 128) + sw128_off(row, c), vbw[4 * c], vbw[4 * c + 1], vbw[4 * c + 2],
                      vbw[4 * c + 3]);
       fence_proxy_async_smem();
       mbar_arrive(&bars->stg_full);
-      if (tid_wg == 0) {
+      if (lead) {
         if (!mbar_wait(&bars->stg_full, j & 1, status, abort_flag)) break;
         tma_store_3d(&tm_g8, smem + kOffStG, 0, leaf, blk * 128);
         tma_store_3d(&tm_vb, smem + kOffStV, 0, leaf, blk * 128);
@@ -334,7 +392,7 @@ __global__ void __launch_bounds__(320, 1)
         bulk_commit_group();
       }
     }
-    if (tid_wg == 0) bulk_wait_group0();
+    if (lead) bulk_wait_group0();
   }
   tc_fence_before();
   __syncthreads();
@@ -357,8 +415,9 @@ int launch_leaf_stats(const LeafStatsMaps& maps, float* sg, float* lz, int64_t p
   by = min(by, nb);
   const int lpc = (nb + by - 1) / by;
   by = (nb + lpc - 1) / lpc;
-  leaf_stats_kernel<<<dim3(bx, by), 320, kSmemBytes, st>>>(maps.mu_hi, maps.mu_lo, maps.k, maps.v, maps.g8, maps.vb,
-                                                            sg, lz, pitch, t0, tc, nb, lpc, scale, status);
+  leaf_stats_kernel<<<dim3(bx, by), kThreads, kSmemBytes, st>>>(maps.mu_hi, maps.mu_lo, maps.k, maps.v, maps.g8,
+                                                                maps.vb, sg, lz, pitch, t0, tc, nb, lpc, scale,
+                                                                status);
   return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
 }
 

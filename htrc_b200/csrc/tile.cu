@@ -83,35 +83,6 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-union F2 {
-  uint64_t u;
-  float2 f;
-};
-__device__ __forceinline__ float2 sub2(float2 a, float2 b) {
-  F2 x, y, z;
-  x.f = a; y.f = b;
-  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(z.u) : "l"(x.u), "l"(y.u));
-  return z.f;
-}
-__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
-  F2 x, y, z;
-  x.f = a; y.f = b;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(z.u) : "l"(x.u), "l"(y.u));
-  return z.f;
-}
-__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
-  F2 x, y, w, z;
-  x.f = a; y.f = b; w.f = c;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(z.u) : "l"(x.u), "l"(y.u), "l"(w.u));
-  return z.f;
-}
-__device__ __forceinline__ float2 add2(float2 a, float2 b) {
-  F2 x, y, z;
-  x.f = a; y.f = b;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(z.u) : "l"(x.u), "l"(y.u));
-  return z.f;
-}
-
 }  // namespace
 
 __global__ void __launch_bounds__(kThreads, 1)
