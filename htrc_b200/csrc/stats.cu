@@ -411,7 +411,7 @@ int launch_leaf_stats(const LeafStatsMaps& maps, float* sg, float* lz, int64_t p
     attr_done[dev] = true;
   }
   const int bx = static_cast<int>((tc + 127) / 128);
-  int by = max(1, (num_sms + bx - 1) / bx);
+  int by = max(1, num_sms / bx);                    // one wave: bx * by <= SMs
   by = min(by, nb);
   const int lpc = (nb + by - 1) / by;
   by = (nb + lpc - 1) / lpc;
