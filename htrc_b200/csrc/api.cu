@@ -179,8 +179,10 @@ int check_device() { return device_info().ok ? HTRC_OK : HTRC_ERR_DEVICE; }
 
 int stats_maps(LeafStatsMaps* mp, const uint16_t* mu_hi, const uint16_t* mu_lo, int64_t nt, const uint16_t* k,
                const uint16_t* v, int64_t m, const int8_t* g8, const uint16_t* vb, int64_t tc, int64_t nb) {
-  bool ok = map_rows(&mp->mu_hi, mu_hi, nt, true, 128) && map_rows(&mp->mu_lo, mu_lo, nt, true, 128) &&
-            map_rows(&mp->k, k, m, true, 64) && map_rows(&mp->v, v, m, true, 64) &&
+  mp->mu_hi = mu_hi;
+  mp->mu_lo = mu_lo;
+  mp->nt = nt;
+  bool ok = map_rows(&mp->k, k, m, true, 64) && map_rows(&mp->v, v, m, true, 64) &&
             map_state(&mp->g8, g8, tc, nb, false, 1, 128) && map_state(&mp->vb, vb, tc, nb, true, 1, 128);
   return ok ? HTRC_OK : HTRC_ERR_CUDA;
 }

@@ -7,7 +7,9 @@
 namespace htrc {
 
 struct LeafStatsMaps {
-  CUtensorMap mu_hi, mu_lo;   // [nt, 128] bf16, box (64, 128), 128B swizzle
+  const uint16_t* mu_hi;      // [nt, 128] bf16 rows (loaded into TMEM by the kernel)
+  const uint16_t* mu_lo;
+  int64_t nt;
   CUtensorMap k, v;           // [M, 128] bf16, box (64, 64), 128B swizzle
   CUtensorMap g8;             // [tc, nb, 128] int8 (store), box (128, 1, 128), 128B swizzle
   CUtensorMap vb;             // [tc, nb, 128] bf16 (store), box (64, 1, 128), 128B swizzle

@@ -1,7 +1,9 @@
 // Leaf statistics of the flat HTRC far field on tcgen05 tensor cores.
 //
 // One CTA owns 128 tile centres (the MMA M dimension) and a contiguous range of leaves.  Per leaf:
-//   S  = mu . K_leaf^T            (M=128 centres, N=64 tokens, K=128; mu = mu_hi + mu_lo, two bf16 MMAs)
+//   S  = mu . K_leaf^T            (M=128 centres, N=64 tokens, K=128; mu = mu_hi + mu_lo, two bf16 MMAs
+//                                  with mu in TMEM as the A operand, which leaves shared memory to four
+//                                  K/V stages)
 //   softmax over the 64 tokens of each centre row (one thread per row, in registers): lz, w
 //   G  = W . K_leaf               (M=128, N=128, K=64; W = w_hi + w_lo, two bf16 MMAs, K_leaf MN-major)
 //   VB = W_hi . V_leaf            (M=128, N=128, K=64)
@@ -24,14 +26,11 @@ namespace htrc {
 
 namespace {
 constexpr int kThreads = 512;
-constexpr int kStages = 2;
-constexpr uint32_t kMuBytes = 128 * 128 * 2;        // one of mu_hi / mu_lo: 128 rows x 256 B
+constexpr int kStages = 4;
 constexpr uint32_t kLeafBytes = 64 * 128 * 2;       // K (or V) of one 64-token leaf
 constexpr uint32_t kStageBytes = 2 * kLeafBytes;    // K + V
 constexpr uint32_t kWBytes = 128 * 128;             // W_hi or W_lo: 128 rows x 64 bf16
-constexpr uint32_t kOffMuHi = 0;
-constexpr uint32_t kOffMuLo = kOffMuHi + kMuBytes;
-constexpr uint32_t kOffStage = kOffMuLo + kMuBytes;
+constexpr uint32_t kOffStage = 0;
 constexpr uint32_t kOffWHi = kOffStage + kStages * kStageBytes;
 constexpr uint32_t kOffWLo = kOffWHi + kWBytes;
 constexpr uint32_t kOffStG = kOffWLo + kWBytes;     // g8 staging: 128 rows x 128 B
@@ -44,9 +43,10 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0;      // two 64-column S buffers
 constexpr uint32_t kColG = 128;    // 128 columns
 constexpr uint32_t kColV = 256;    // 128 columns
+constexpr uint32_t kColMu = 384;   // mu_hi (64 columns of bf16 pairs), then mu_lo
 
 struct Bars {
-  uint64_t mu_full;
+  uint64_t mu_full;    // the 128 softmax threads stored their mu rows in TMEM
   uint64_t kv_full[kStages];
   uint64_t kv_empty[kStages];
   uint64_t s_full[2];
@@ -82,7 +82,7 @@ __device__ __forceinline__ uint2 half_away_codes2(float2 y) {
 }  // namespace
 
 __global__ void __launch_bounds__(kThreads, 1)
-    leaf_stats_kernel(const __grid_constant__ CUtensorMap tm_mu_hi, const __grid_constant__ CUtensorMap tm_mu_lo,
+    leaf_stats_kernel(const uint16_t* __restrict__ mu_hi_g, const uint16_t* __restrict__ mu_lo_g, int64_t nt,
                       const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                       const __grid_constant__ CUtensorMap tm_g8, const __grid_constant__ CUtensorMap tm_vb,
                       float* __restrict__ sg_out, float* __restrict__ lz_out, int64_t pitch, int64_t t0, int64_t tc,
@@ -99,7 +99,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_flag = &bars->abort_flag;
 
   if (threadIdx.x == 0) {
-    mbar_init(&bars->mu_full, 1);
+    mbar_init(&bars->mu_full, 128);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&bars->kv_full[s], 1);
       mbar_init(&bars->kv_empty[s], 1);
@@ -132,15 +132,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (nl > 0) {
         const uint64_t pol_keep = policy_evict_last();
         if (leader) {
-          tma_prefetch_desc(&tm_mu_hi);
           tma_prefetch_desc(&tm_k);
           tma_prefetch_desc(&tm_v);
-          const int trow = static_cast<int>(t0) + blk * 128;
-          mbar_arrive_expect_tx(&bars->mu_full, 2 * kMuBytes);
-          for (int c = 0; c < 2; ++c) {
-            tma_load_2d(smem + kOffMuHi + c * (kMuBytes / 2), &tm_mu_hi, &bars->mu_full, 64 * c, trow, pol_keep);
-            tma_load_2d(smem + kOffMuLo + c * (kMuBytes / 2), &tm_mu_lo, &bars->mu_full, 64 * c, trow, pol_keep);
-          }
         }
         for (int j = 0; j < nl; ++j) {
           const int s = j % kStages;
@@ -163,7 +156,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t leader = elect_one();
       if (nl > 0) {
         const uint32_t id_s = idesc_bf16(128, 64, false, false);
-        const uint32_t mu_hi = smem_u32(smem + kOffMuHi), mu_lo = smem_u32(smem + kOffMuLo);
         bool ok = mbar_wait_warp(&bars->mu_full, 0, status, abort_flag);
         for (int j = 0; ok && j < nl; ++j) {
           const int s = j % kStages, b = j & 1;
@@ -178,9 +170,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int c = 0; c < 2; ++c) {
 #pragma unroll
               for (int kk = 0; kk < 4; ++kk) {
-                const uint64_t a = sw128_desc((h ? mu_lo : mu_hi) + c * (kMuBytes / 2) + kk * 32, 16, 1024);
+                // A: mu_hi / mu_lo dims 64 c + 16 kk .. + 15 = TMEM columns (64 h + 32 c + 8 kk) .. + 7
+                const uint32_t a = tmem + kColMu + 64 * h + 32 * c + 8 * kk;
                 const uint64_t bdesc = sw128_desc(kst + c * (kLeafBytes / 2) + kk * 32, 16, 1024);
-                mma_bf16_by(leader, d, a, bdesc, id_s, (h | c | kk) != 0);
+                mma_bf16_ts_by(leader, d, a, bdesc, id_s, (h | c | kk) != 0);
               }
             }
           }
@@ -234,6 +227,29 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool valid = tloc < tc;
     const float kLog2e = 1.4426950408889634f;
     const uint32_t wh = smem_u32(smem + kOffWHi), wl = smem_u32(smem + kOffWLo);
+    if (nl > 0) {
+      // this row's centre (hi and lo parts, 128 bf16 each) -> TMEM lane `row`; rows past the end are zero
+      const int64_t grow = t0 + static_cast<int64_t>(blk) * 128 + row;
+      for (int part = 0; part < 2; ++part) {
+        const uint4* src = reinterpret_cast<const uint4*>((part ? mu_lo_g : mu_hi_g) + grow * 128);
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint32_t r[32];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const uint4 v = grow < nt ? __ldg(src + half * 8 + i) : make_uint4(0u, 0u, 0u, 0u);
+            r[4 * i] = v.x;
+            r[4 * i + 1] = v.y;
+            r[4 * i + 2] = v.z;
+            r[4 * i + 3] = v.w;
+          }
+          tmem_st32(tmem + lane_base + kColMu + 64 * part + 32 * half, r);
+        }
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&bars->mu_full);
+    }
     for (int j = 0; j < nl; ++j) {
       const int b = j & 1;
       const int leaf = l_begin + j;
@@ -415,7 +431,7 @@ int launch_leaf_stats(const LeafStatsMaps& maps, float* sg, float* lz, int64_t p
   by = min(by, nb);
   const int lpc = (nb + by - 1) / by;
   by = (nb + lpc - 1) / lpc;
-  leaf_stats_kernel<<<dim3(bx, by), kThreads, kSmemBytes, st>>>(maps.mu_hi, maps.mu_lo, maps.k, maps.v, maps.g8,
+  leaf_stats_kernel<<<dim3(bx, by), kThreads, kSmemBytes, st>>>(maps.mu_hi, maps.mu_lo, maps.nt, maps.k, maps.v, maps.g8,
                                                                 maps.vb, sg, lz, pitch, t0, tc, nb, lpc, scale,
                                                                 status);
   return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
