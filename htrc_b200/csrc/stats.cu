@@ -334,20 +334,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(&bars->gv_full, j & 1, status, abort_flag)) break;
       __syncwarp();
       tc_fence_after();
-      // pass 1 over this half of G: abs-max of g = scale * G, as scale * max |G| (scale > 0 and rounding is
-      // monotonic, so this is the maximum of the rounded products)
-      float ama[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int q2 = 0; q2 < 2; ++q2) {
+      // drain this half of G (raw) and VB (as bf16 pairs) into registers and release TMEM at once, so the
+      // next leaf's G/VB MMAs overlap the quantisation below
+      uint32_t gr[64];
+      tmem_ld32(tmem + lane_base + colg, *reinterpret_cast<uint32_t(*)[32]>(gr));
+      tmem_ld32(tmem + lane_base + colg + 32, *reinterpret_cast<uint32_t(*)[32]>(gr + 32));
+      uint32_t vbw[32];
+      {
         uint32_t r[32];
-        tmem_ld32(tmem + lane_base + colg + 32 * q2, r);
+        tmem_ld32(tmem + lane_base + colv, r);
         tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; i += 2)
-          ama[(i >> 1) & 3] = max3(ama[(i >> 1) & 3], fabsf(__uint_as_float(r[i])), fabsf(__uint_as_float(r[i + 1])));
+        for (int i = 0; i < 16; ++i) vbw[i] = pack_bf16x2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+        tmem_ld32(tmem + lane_base + colv + 32, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) vbw[16 + i] = pack_bf16x2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
       }
+      tc_fence_before();
+      mbar_arrive(&bars->gv_empty);
+      // abs-max of g = scale * G, as scale * max |G| (scale > 0 and rounding is monotonic, so this is the
+      // maximum of the rounded products); the other half of the row comes through shared memory
+      // (buffered by leaf parity)
+      float ama[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int i = 0; i < 64; i += 2)
+        ama[(i >> 1) & 3] = max3(ama[(i >> 1) & 3], fabsf(__uint_as_float(gr[i])), fabsf(__uint_as_float(gr[i + 1])));
       float am = __fmul_rn(fmaxf(fmaxf(ama[0], ama[1]), fmaxf(ama[2], ama[3])), scale);
-      // the other half of the row: exchanged through shared memory (buffered by leaf parity)
       amx[((j & 1) * 2 + half) * 128 + row] = am;
       named_bar_sync(1 + quarter, 64);
       am = fmaxf(am, amx[((j & 1) * 2 + (half ^ 1)) * 128 + row]);
@@ -355,33 +368,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float sgv = __fmul_rn(am, 1.0f / 127.0f);
       const float rr = __fdiv_rn(127.0f, am);
       if (valid && half == 0) sg_out[tloc * pitch + leaf] = sgv;
-      // pass 2: INT8 codes; then the vbar half row as bf16 pairs
+      // INT8 codes
       uint32_t gw[16];
+      const float2 sc2 = make_float2(scale, scale), rr2 = make_float2(rr, rr);
 #pragma unroll
-      for (int q2 = 0; q2 < 2; ++q2) {
-        uint32_t r[32];
-        tmem_ld32(tmem + lane_base + colg + 32 * q2, r);
-        tmem_ld_wait();
-        const float2 sc2 = make_float2(scale, scale), rr2 = make_float2(rr, rr);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const uint2 c01 = half_away_codes2(mul2(mul2(make_float2(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1])), sc2), rr2));
-          const uint2 c23 = half_away_codes2(mul2(mul2(make_float2(__uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3])), sc2), rr2));
-          gw[q2 * 8 + i] = __byte_perm(__byte_perm(c01.x, c01.y, 0x0040), __byte_perm(c23.x, c23.y, 0x0040), 0x5410);
-        }
+      for (int i = 0; i < 16; ++i) {
+        const uint2 c01 = half_away_codes2(mul2(mul2(make_float2(__uint_as_float(gr[4 * i]), __uint_as_float(gr[4 * i + 1])), sc2), rr2));
+        const uint2 c23 = half_away_codes2(mul2(mul2(make_float2(__uint_as_float(gr[4 * i + 2]), __uint_as_float(gr[4 * i + 3])), sc2), rr2));
+        gw[i] = __byte_perm(__byte_perm(c01.x, c01.y, 0x0040), __byte_perm(c23.x, c23.y, 0x0040), 0x5410);
       }
-      uint32_t vbw[32];
-#pragma unroll
-      for (int q2 = 0; q2 < 2; ++q2) {
-        uint32_t r[32];
-        tmem_ld32(tmem + lane_base + colv + 32 * q2, r);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 16; ++i) vbw[q2 * 16 + i] = pack_bf16x2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
-      }
-      // G and VB are in registers: the next leaf's G/VB MMAs may start
-      tc_fence_before();
-      mbar_arrive(&bars->gv_empty);
       // the previous TMA stores must have finished reading the staging buffers
       if (lead) {
         bulk_wait_group_read0();
