@@ -54,12 +54,12 @@ DeviceInfo device_info() {
   return cache[dev];
 }
 
-// rank-2/3 tiled map; dims innermost first, strides in bytes for dims 1..rank-1
+// rank-2..4 tiled map; dims innermost first, strides in bytes for dims 1..rank-1
 bool make_map(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* base, const uint64_t* dims,
               const uint64_t* strides, const uint32_t* box, bool swizzle128) {
-  if (!encoder() || base == nullptr) return false;
-  cuuint64_t gd[3], gs[2];
-  cuuint32_t bx[3], es[3] = {1, 1, 1};
+  if (!encoder() || base == nullptr || rank < 2 || rank > 4) return false;
+  cuuint64_t gd[4], gs[3];
+  cuuint32_t bx[4], es[4] = {1, 1, 1, 1};
   for (int i = 0; i < rank; ++i) {
     gd[i] = dims[i];
     bx[i] = box[i];
@@ -80,6 +80,24 @@ bool map_rows(CUtensorMap* m, const void* base, int64_t rows, bool bf16, int box
   const uint32_t box[2] = {bf16 ? 64u : 128u, static_cast<uint32_t>(box_rows)};
   return make_map(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, base, dims, strides,
                   box, true);
+}
+
+// [rows, 128] bf16 matrix seen as [2 halves][rows][64]: one box of `box_rows` rows lands in shared memory as
+// the 64-column half 0 followed by half 1, each a 128-byte-swizzled [box_rows][64] tile (one TMA load for a
+// whole leaf instead of one per half)
+bool map_rows_halves(CUtensorMap* m, const void* base, int64_t rows, int box_rows) {
+  const uint64_t dims[3] = {64, static_cast<uint64_t>(rows), 2};
+  const uint64_t strides[2] = {256, 128};
+  const uint32_t box[3] = {64, static_cast<uint32_t>(box_rows), 2};
+  return make_map(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, box, true);
+}
+
+// [tc, nb, 128] bf16 state seen as [tc][2 halves][nb][64], box (64, box_leaves, 2, 1): the same split per tile
+bool map_state_halves(CUtensorMap* m, const void* base, int64_t tc, int64_t nb, int box_leaves) {
+  const uint64_t dims[4] = {64, static_cast<uint64_t>(nb), 2, static_cast<uint64_t>(tc)};
+  const uint64_t strides[3] = {256, 128, static_cast<uint64_t>(nb) * 256};
+  const uint32_t box[4] = {64, static_cast<uint32_t>(box_leaves), 2, 1};
+  return make_map(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, base, dims, strides, box, true);
 }
 
 // [tc, nb, 128] state of 1- or 2-byte elements, box (inner, box_leaves, box_tiles)
@@ -182,7 +200,7 @@ int stats_maps(LeafStatsMaps* mp, const uint16_t* mu_hi, const uint16_t* mu_lo, 
   mp->mu_hi = mu_hi;
   mp->mu_lo = mu_lo;
   mp->nt = nt;
-  bool ok = map_rows(&mp->k, k, m, true, 64) && map_rows(&mp->v, v, m, true, 64) &&
+  bool ok = map_rows_halves(&mp->k, k, m, 64) && map_rows_halves(&mp->v, v, m, 64) &&
             map_state(&mp->g8, g8, tc, nb, false, 1, 128) && map_state(&mp->vb, vb, tc, nb, true, 1, 128);
   return ok ? HTRC_OK : HTRC_ERR_CUDA;
 }
@@ -198,10 +216,10 @@ int tile_maps(TileMaps* mp, const int8_t* q8, const int8_t* dq8, int64_t rows, c
               const float* lz, const float* sg, const uint8_t* excl, int64_t tc, int64_t nb, int64_t pitch,
               const int8_t* k8, const uint16_t* v, int64_t m) {
   bool ok = map_rows(&mp->q8, q8, rows, false, 64) && map_rows(&mp->dq8, dq8, rows, false, 64) &&
-            map_state(&mp->g8, g8, tc, nb, false, 64, 1) && map_state(&mp->vb, vb, tc, nb, true, 64, 1) &&
+            map_state(&mp->g8, g8, tc, nb, false, 64, 1) && map_state_halves(&mp->vb, vb, tc, nb, 64) &&
             map_scalars(&mp->lz, lz, tc, nb, pitch, true, 64) && map_scalars(&mp->sg, sg, tc, nb, pitch, true, 64) &&
             map_scalars(&mp->excl, excl, tc, nb, pitch, false, 64) && map_rows(&mp->k8, k8, m, false, 64) &&
-            map_rows(&mp->v, v, m, true, 64);
+            map_rows_halves(&mp->v, v, m, 64);
   return ok ? HTRC_OK : HTRC_ERR_CUDA;
 }
 

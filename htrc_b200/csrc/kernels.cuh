@@ -10,7 +10,7 @@ struct LeafStatsMaps {
   const uint16_t* mu_hi;      // [nt, 128] bf16 rows (loaded into TMEM by the kernel)
   const uint16_t* mu_lo;
   int64_t nt;
-  CUtensorMap k, v;           // [M, 128] bf16, box (64, 64), 128B swizzle
+  CUtensorMap k, v;           // [M, 128] bf16 as [2][M][64], box (64, 64, 2), 128B swizzle
   CUtensorMap g8;             // [tc, nb, 128] int8 (store), box (128, 1, 128), 128B swizzle
   CUtensorMap vb;             // [tc, nb, 128] bf16 (store), box (64, 1, 128), 128B swizzle
 };
@@ -24,11 +24,11 @@ struct RowmaxMaps {
 struct TileMaps {
   CUtensorMap q8, dq8;        // [nt*64, 128] int8, box (128, 64), 128B swizzle
   CUtensorMap g8;             // [tc, nb, 128] int8, box (128, 64, 1), 128B swizzle
-  CUtensorMap vb;             // [tc, nb, 128] bf16, box (64, 64, 1), 128B swizzle
+  CUtensorMap vb;             // [tc, nb, 128] bf16 as [tc][2][nb][64], box (64, 64, 2, 1), 128B swizzle
   CUtensorMap lz, sg;         // [tc, nb] f32 (row pitch P), box (64, 1)
   CUtensorMap excl;           // [tc, nb] u8 (row pitch P), box (64, 1)
   CUtensorMap k8;             // [M, 128] int8, box (128, 64), 128B swizzle
-  CUtensorMap v;              // [M, 128] bf16, box (64, 64), 128B swizzle
+  CUtensorMap v;              // [M, 128] bf16 as [2][M][64], box (64, 64, 2), 128B swizzle
 };
 
 void launch_pack_rows(const void* x, int dtype, int64_t rows, int rounding, int8_t* x8, float* scale, cudaStream_t st);

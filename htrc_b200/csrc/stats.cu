@@ -142,10 +142,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint8_t* st = smem + kOffStage + s * kStageBytes;
             const int row = (l_begin + j) * 64;
             mbar_arrive_expect_tx(&bars->kv_full[s], kStageBytes);
-            tma_load_2d(st, &tm_k, &bars->kv_full[s], 0, row, pol_keep);
-            tma_load_2d(st + kLeafBytes / 2, &tm_k, &bars->kv_full[s], 64, row, pol_keep);
-            tma_load_2d(st + kLeafBytes, &tm_v, &bars->kv_full[s], 0, row, pol_keep);
-            tma_load_2d(st + kLeafBytes + kLeafBytes / 2, &tm_v, &bars->kv_full[s], 64, row, pol_keep);
+            tma_load_3d(st, &tm_k, &bars->kv_full[s], 0, row, 0, pol_keep);        // both 64-column halves
+            tma_load_3d(st + kLeafBytes, &tm_v, &bars->kv_full[s], 0, row, 0, pol_keep);
           }
           __syncwarp();
         }

@@ -238,15 +238,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive_expect_tx(&bars->y_full[s], kYBytes * ntiles);
         for (int x = 0; x < ntiles; ++x) {
           uint8_t* ty = st + x * kYBytes;
-          if (ny < nf) {
-            const int tl = tlocA + x;
-            tma_load_3d(ty, &tm_vb, &bars->y_full[s], 0, ny * 64, tl, pol_stream);
-            tma_load_3d(ty + kYBytes / 2, &tm_vb, &bars->y_full[s], 64, ny * 64, tl, pol_stream);
-          } else {
-            const int leaf = idx_s[x * kMaxKx + (ny - nf)];
-            tma_load_2d(ty, &tm_v, &bars->y_full[s], 0, leaf * 64, pol_keep);
-            tma_load_2d(ty + kYBytes / 2, &tm_v, &bars->y_full[s], 64, leaf * 64, pol_keep);
-          }
+          // both 64-column halves in one load: [half][64 rows][64] at ty, ty + kYBytes / 2
+          if (ny < nf)
+            tma_load_4d(ty, &tm_vb, &bars->y_full[s], 0, ny * 64, 0, tlocA + x, pol_stream);
+          else
+            tma_load_3d(ty, &tm_v, &bars->y_full[s], 0, idx_s[x * kMaxKx + (ny - nf)] * 64, 0, pol_keep);
         }
       }
       __syncwarp();
