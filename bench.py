@@ -376,7 +376,7 @@ def run_ours(a, wl, rank, world, local_rank):
     traffic = None
     tp = ROOT / "profiles" / "tile_attention_traffic.json"
     if tp.exists():
-        traffic = json.loads(tp.read_text()).get("bytes_per_launch")
+        traffic = json.loads(tp.read_text()).get("bytes_per_launch", {}).get(a.workload)
     roof = {"kernel": "tile_attention_kernel", "bound": "tensor", "achieved": achieved, "peak": peak,
             "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
             "peak_source": f"{peak_src} bf16_tflops_sustained", "flop_per_launch": flops_bf16_equiv,
