@@ -124,11 +124,16 @@ int64_t pitch_of(int64_t nb) { return (nb + 15) / 16 * 16; }
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
+// Workspace of one forward call.  Centre rows (mu, and the far-field state, routing and exclusion
+// rows) are per group of `group` tiles; a chunk holds gcm groups = gcm * group tiles.
 struct Layout {
-  int64_t n = 0, m = 0, nt = 0, nb = 0, pitch = 0, tcm = 0, kx = 0;
+  int64_t n = 0, m = 0, nt = 0, nb = 0, pitch = 0, kx = 0, group = 1, ng = 0, gcm = 0, tcm = 0;
+  bool kmeans = false;
   size_t status = 0, k8 = 0, ks = 0, mu = 0, mu_hi = 0, mu_lo = 0, q8 = 0, sq = 0, dq8 = 0, sdq = 0, tail = 0;
-  size_t g8 = 0, vb = 0, sg = 0, lz = 0, sel = 0, excl = 0, idx = 0, total = 0;
+  size_t g8 = 0, vb = 0, sg = 0, lz = 0, sel = 0, excl = 0, idx = 0, perm = 0, km = 0, total = 0;
 };
+
+constexpr int kMaxGroup = 65536;
 
 int validate(const HtrcFlatArgs* a, bool need_ptrs) {
   if (a == nullptr) return HTRC_ERR_ARG;
@@ -136,6 +141,9 @@ int validate(const HtrcFlatArgs* a, bool need_ptrs) {
   if (a->n_queries < 1 || a->n_keys < a->leaf || a->n_keys % a->leaf) return HTRC_ERR_ARG;
   if (a->q_dtype != HTRC_DTYPE_F32 && a->q_dtype != HTRC_DTYPE_BF16) return HTRC_ERR_ARG;
   if (a->exact_leaves < 0 || a->sink_leaves < 0 || a->n_tail < 0) return HTRC_ERR_ARG;
+  if (a->group > kMaxGroup) return HTRC_ERR_ARG;
+  if (a->order != HTRC_ORDER_SEQ && a->order != HTRC_ORDER_KMEANS) return HTRC_ERR_ARG;
+  if (a->n_queries > (int64_t(1) << 31) - 1) return HTRC_ERR_UNSUPPORTED;
   const int64_t nb = a->n_keys / a->leaf;
   if (nb > kMaxLeaves) return HTRC_ERR_UNSUPPORTED;
   const int64_t sink = std::min<int64_t>(a->sink_leaves, nb);
@@ -157,9 +165,17 @@ Layout layout_of(const HtrcFlatArgs* a) {
   L.pitch = pitch_of(L.nb);
   const int64_t sink = std::min<int64_t>(a->sink_leaves, L.nb);
   L.kx = std::min<int64_t>(static_cast<int64_t>(a->exact_leaves) + sink, L.nb);
-  int64_t tcm = a->tile_chunk > 0 ? std::min<int64_t>(a->tile_chunk, L.nt) : L.nt;
-  if (tcm < L.nt) tcm = std::min<int64_t>((tcm + 1) / 2 * 2, L.nt);
-  L.tcm = tcm;
+  L.group = a->group > 1 ? a->group : 1;
+  L.ng = (L.nt + L.group - 1) / L.group;
+  L.kmeans = a->order == HTRC_ORDER_KMEANS;
+  // groups per chunk: tile_chunk // group (the reference's gstep, h3/htrc_flat.py:238), made even in
+  // tiles when the state is chunked so that no tile pair of the tile kernel straddles two chunks
+  int64_t gcm = a->tile_chunk > 0 ? std::max<int64_t>(1, a->tile_chunk / L.group) : L.ng;
+  gcm = std::min<int64_t>(gcm, L.ng);
+  if (gcm < L.ng && (gcm * L.group) % 2) gcm = std::min<int64_t>(gcm + 1, L.ng);
+  L.gcm = gcm;
+  L.tcm = std::min<int64_t>(gcm * L.group, L.nt);
+  const int64_t gcm_rows = gcm;
   size_t o = 0;
   auto take = [&](size_t bytes) {
     const size_t at = o;
@@ -169,21 +185,25 @@ Layout layout_of(const HtrcFlatArgs* a) {
   L.status = take(256);
   L.k8 = take(static_cast<size_t>(L.m) * 128);
   L.ks = take(static_cast<size_t>(L.m) * 4);
-  L.mu = take(static_cast<size_t>(L.nt) * 128 * 4);
-  L.mu_hi = take(static_cast<size_t>(L.nt) * 128 * 2);
-  L.mu_lo = take(static_cast<size_t>(L.nt) * 128 * 2);
+  L.mu = take(static_cast<size_t>(L.ng) * 128 * 4);
+  L.mu_hi = take(static_cast<size_t>(L.ng) * 128 * 2);
+  L.mu_lo = take(static_cast<size_t>(L.ng) * 128 * 2);
   L.q8 = take(static_cast<size_t>(L.nt) * 64 * 128);
   L.sq = take(static_cast<size_t>(L.nt) * 64 * 4);
   L.dq8 = take(static_cast<size_t>(L.nt) * 64 * 128);
   L.sdq = take(static_cast<size_t>(L.nt) * 64 * 4);
   L.tail = a->n_tail > 0 ? take(static_cast<size_t>(L.n) * 130 * 4) : 0;
-  L.g8 = take(static_cast<size_t>(tcm) * L.nb * 128);
-  L.vb = take(static_cast<size_t>(tcm) * L.nb * 256);
-  L.sg = take(static_cast<size_t>(tcm) * L.pitch * 4);
-  L.lz = take(static_cast<size_t>(tcm) * L.pitch * 4);
-  L.sel = take(static_cast<size_t>(tcm) * L.pitch * 4);
-  L.excl = take(static_cast<size_t>(tcm) * L.pitch);
-  L.idx = take(static_cast<size_t>(tcm) * std::max<int64_t>(L.kx, 1) * 4);
+  L.g8 = take(static_cast<size_t>(gcm_rows) * L.nb * 128);
+  L.vb = take(static_cast<size_t>(gcm_rows) * L.nb * 256);
+  L.sg = take(static_cast<size_t>(gcm_rows) * L.pitch * 4);
+  L.lz = take(static_cast<size_t>(gcm_rows) * L.pitch * 4);
+  L.sel = take(static_cast<size_t>(L.tcm) * L.pitch * 4);
+  L.excl = take(static_cast<size_t>(gcm_rows) * L.pitch);
+  L.idx = take(static_cast<size_t>(gcm_rows) * std::max<int64_t>(L.kx, 1) * 4);
+  if (L.kmeans) {
+    L.perm = take(static_cast<size_t>(L.n) * 4);
+    L.km = take(kmeans_scratch_bytes(L.n));
+  }
   L.total = o;
   return L;
 }
@@ -269,6 +289,8 @@ int htrc_flat_forward(const HtrcFlatArgs* a, htrc_stream_t stream) {
   uint8_t* excl = at<uint8_t>(ws, L.excl);
   int32_t* idx = at<int32_t>(ws, L.idx);
   float* tail = a->n_tail > 0 ? at<float>(ws, L.tail) : nullptr;
+  int32_t* perm = L.kmeans ? at<int32_t>(ws, L.perm) : nullptr;
+  const int group = static_cast<int>(L.group);
 
   auto mark = [&](int i) {
     if (a->stage_events && i < a->n_stage_events && a->stage_events[i])
@@ -276,36 +298,39 @@ int htrc_flat_forward(const HtrcFlatArgs* a, htrc_stream_t stream) {
   };
   mark(0);
   launch_pack_rows(a->k, HTRC_DTYPE_BF16, L.m, HTRC_ROUND_HALF_EVEN, k8, ks, st);
-  launch_tile_prep(a->q, a->q_dtype, L.n, at<float>(ws, L.mu), mu_hi, mu_lo, q8, sq, dq8, sdq, st);
+  if (perm && (rc = launch_kmeans_order(a->q, a->q_dtype, L.n, perm, at<void>(ws, L.km), st)) != HTRC_OK) return rc;
+  launch_tile_prep(a->q, a->q_dtype, L.n, perm, group, at<float>(ws, L.mu), mu_hi, mu_lo, q8, sq, dq8, sdq, st);
   if (tail) launch_tail_partial(a->q, a->q_dtype, L.n, a->tail_k, a->tail_v, a->n_tail, scale, tail, st);
   if (cudaGetLastError() != cudaSuccess) return HTRC_ERR_CUDA;
   mark(1);
   const bool far = kx < nb;
   int chunk = 0;
-  for (int64_t t0 = 0; t0 < L.nt; t0 += L.tcm, ++chunk) {
-    const int64_t tc = std::min<int64_t>(L.tcm, L.nt - t0);
+  for (int64_t g0 = 0; g0 < L.ng; g0 += L.gcm, ++chunk) {
+    const int64_t gc = std::min<int64_t>(L.gcm, L.ng - g0);     // centre rows of this chunk
+    const int64_t t0 = g0 * L.group;
+    const int64_t tc = std::min<int64_t>(gc * L.group, L.nt - t0);
     if (far) {
       LeafStatsMaps smp;
-      if ((rc = stats_maps(&smp, mu_hi, mu_lo, L.nt, a->k, a->v, L.m, g8, vb, tc, L.nb)) != HTRC_OK) return rc;
-      if ((rc = launch_leaf_stats(smp, sg, lz, L.pitch, t0, tc, nb, scale, status, device_info().sms, st)) != HTRC_OK)
+      if ((rc = stats_maps(&smp, mu_hi, mu_lo, L.ng, a->k, a->v, L.m, g8, vb, gc, L.nb)) != HTRC_OK) return rc;
+      if ((rc = launch_leaf_stats(smp, sg, lz, L.pitch, g0, gc, nb, scale, status, device_info().sms, st)) != HTRC_OK)
         return rc;
     }
     mark(2 + 4 * chunk);
     if (far) {
       if (kx > 0) {
         RowmaxMaps rmp;
-        if ((rc = rowmax_maps(&rmp, dq8, L.nt * 64, g8, sg, lz, tc, L.nb, L.pitch)) != HTRC_OK) return rc;
-        if ((rc = launch_rowmax(rmp, sdq, sel, L.pitch, t0, tc, nb, status, st)) != HTRC_OK) return rc;
+        if ((rc = rowmax_maps(&rmp, dq8, L.nt * 64, g8, sg, lz, gc, L.nb, L.pitch)) != HTRC_OK) return rc;
+        if ((rc = launch_rowmax(rmp, sdq, sel, L.pitch, t0, tc, nb, group, status, st)) != HTRC_OK) return rc;
       }
     }
     mark(3 + 4 * chunk);
-    if ((rc = launch_route(sel, L.pitch, tc, nb, kx, sink, idx, excl, st)) != HTRC_OK) return rc;
+    if ((rc = launch_route(sel, L.pitch, tc, group, nb, kx, sink, idx, excl, st)) != HTRC_OK) return rc;
     mark(4 + 4 * chunk);
     TileMaps tmp;
-    if ((rc = tile_maps(&tmp, q8, dq8, L.nt * 64, g8, vb, lz, sg, excl, tc, L.nb, L.pitch, k8, a->v, L.m)) != HTRC_OK)
+    if ((rc = tile_maps(&tmp, q8, dq8, L.nt * 64, g8, vb, lz, sg, excl, gc, L.nb, L.pitch, k8, a->v, L.m)) != HTRC_OK)
       return rc;
-    if ((rc = launch_tile_attention(tmp, sq, sdq, ks, idx, kx, nb, L.n, t0, tc, scale, tail, a->out, a->lse, status,
-                                    st)) != HTRC_OK)
+    if ((rc = launch_tile_attention(tmp, sq, sdq, ks, idx, kx, nb, L.n, t0, tc, group, scale, tail, perm, a->out,
+                                    a->lse, status, st)) != HTRC_OK)
       return rc;
     mark(5 + 4 * chunk);
   }
@@ -334,16 +359,38 @@ int htrc_pack_int8(const void* x, int32_t dtype, int64_t rows, int32_t dim, int3
   return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
 }
 
-int htrc_tile_prep(const void* q, int32_t q_dtype, int64_t n_queries, int32_t dim, int32_t tile, float* mu,
-                   uint16_t* mu_hi, uint16_t* mu_lo, int8_t* q8, float* sq, int8_t* dq8, float* sdq,
-                   htrc_stream_t stream) {
+int htrc_tile_prep(const void* q, int32_t q_dtype, int64_t n_queries, int32_t dim, int32_t tile, const int32_t* perm,
+                   int32_t group, float* mu, uint16_t* mu_hi, uint16_t* mu_lo, int8_t* q8, float* sq, int8_t* dq8,
+                   float* sdq, htrc_stream_t stream) {
   if (!q || !mu || !mu_hi || !mu_lo || !q8 || !sq || !dq8 || !sdq || n_queries < 1) return HTRC_ERR_ARG;
   if (dim != kDim || tile != kTile) return HTRC_ERR_UNSUPPORTED;
   if (q_dtype != HTRC_DTYPE_F32 && q_dtype != HTRC_DTYPE_BF16) return HTRC_ERR_ARG;
+  if (group > kMaxGroup) return HTRC_ERR_ARG;
   int rc = check_device();
   if (rc != HTRC_OK) return rc;
-  launch_tile_prep(q, q_dtype, n_queries, mu, mu_hi, mu_lo, q8, sq, dq8, sdq, reinterpret_cast<cudaStream_t>(stream));
+  launch_tile_prep(q, q_dtype, n_queries, perm, group, mu, mu_hi, mu_lo, q8, sq, dq8, sdq,
+                   reinterpret_cast<cudaStream_t>(stream));
   return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
+}
+
+int htrc_kmeans_scratch_size(int64_t n_queries, size_t* bytes) {
+  if (n_queries < 1 || bytes == nullptr) return HTRC_ERR_ARG;
+  *bytes = kmeans_scratch_bytes(n_queries);
+  return HTRC_OK;
+}
+
+int htrc_kmeans_order(const void* q, int32_t q_dtype, int64_t n_queries, int32_t dim, int32_t* perm, void* scratch,
+                      size_t scratch_bytes, htrc_stream_t stream) {
+  if (!q || !perm || n_queries < 1) return HTRC_ERR_ARG;
+  if (dim != kDim) return HTRC_ERR_UNSUPPORTED;
+  if (q_dtype != HTRC_DTYPE_F32 && q_dtype != HTRC_DTYPE_BF16) return HTRC_ERR_ARG;
+  if (n_queries > (int64_t(1) << 31) - 1) return HTRC_ERR_UNSUPPORTED;
+  if (scratch == nullptr || scratch_bytes < kmeans_scratch_bytes(n_queries) ||
+      (reinterpret_cast<uintptr_t>(scratch) & 255u) != 0)
+    return HTRC_ERR_WORKSPACE;
+  int rc = check_device();
+  if (rc != HTRC_OK) return rc;
+  return launch_kmeans_order(q, q_dtype, n_queries, perm, scratch, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int htrc_leaf_stats(const uint16_t* mu_hi, const uint16_t* mu_lo, int64_t nt, int64_t t0, int64_t tc, const uint16_t* k,
@@ -362,22 +409,26 @@ int htrc_leaf_stats(const uint16_t* mu_hi, const uint16_t* mu_lo, int64_t nt, in
                            device_info().sms, reinterpret_cast<cudaStream_t>(stream));
 }
 
-int htrc_rowmax_select(const int8_t* dq8, const float* sdq, int64_t t0, int64_t tc, const int8_t* g8, const float* sg,
-                       const float* lz, int64_t nb, int32_t dim, float* sel, int32_t* status, htrc_stream_t stream) {
+int htrc_rowmax_select(const int8_t* dq8, const float* sdq, int64_t t0, int64_t tc, int32_t group, const int8_t* g8,
+                       const float* sg, const float* lz, int64_t nb, int32_t dim, float* sel, int32_t* status,
+                       htrc_stream_t stream) {
   if (!dq8 || !sdq || !g8 || !sg || !lz || !sel || t0 < 0 || tc < 1 || nb < 1) return HTRC_ERR_ARG;
+  const int64_t g = group > 1 ? group : 1;
+  if (g > kMaxGroup || t0 % g) return HTRC_ERR_ARG;
   if (dim != kDim) return HTRC_ERR_UNSUPPORTED;
   if (nb > kMaxLeaves) return HTRC_ERR_UNSUPPORTED;
   int rc = check_device();
   if (rc != HTRC_OK) return rc;
   RowmaxMaps mp;
-  if ((rc = rowmax_maps(&mp, dq8, (t0 + tc) * 64, g8, sg, lz, tc, nb, pitch_of(nb))) != HTRC_OK) return rc;
-  return launch_rowmax(mp, sdq, sel, pitch_of(nb), t0, tc, static_cast<int>(nb), status,
+  if ((rc = rowmax_maps(&mp, dq8, (t0 + tc) * 64, g8, sg, lz, (tc + g - 1) / g, nb, pitch_of(nb))) != HTRC_OK)
+    return rc;
+  return launch_rowmax(mp, sdq, sel, pitch_of(nb), t0, tc, static_cast<int>(nb), static_cast<int>(g), status,
                        reinterpret_cast<cudaStream_t>(stream));
 }
 
-int htrc_route(const float* sel, int64_t tc, int64_t nb, int32_t exact_leaves, int32_t sink_leaves, int32_t* idx,
-               uint8_t* excl, htrc_stream_t stream) {
-  if (!excl || tc < 1 || nb < 1 || exact_leaves < 0 || sink_leaves < 0) return HTRC_ERR_ARG;
+int htrc_route(const float* sel, int64_t tc, int64_t nb, int32_t exact_leaves, int32_t sink_leaves, int32_t group,
+               int32_t* idx, uint8_t* excl, htrc_stream_t stream) {
+  if (!excl || tc < 1 || nb < 1 || exact_leaves < 0 || sink_leaves < 0 || group > kMaxGroup) return HTRC_ERR_ARG;
   if (nb > kMaxLeaves) return HTRC_ERR_UNSUPPORTED;
   const int64_t sink = std::min<int64_t>(sink_leaves, nb);
   const int64_t kx = std::min<int64_t>(static_cast<int64_t>(exact_leaves) + sink, nb);
@@ -385,16 +436,19 @@ int htrc_route(const float* sel, int64_t tc, int64_t nb, int32_t exact_leaves, i
   if (kx > 0 && !idx) return HTRC_ERR_ARG;
   int rc = check_device();
   if (rc != HTRC_OK) return rc;
-  return launch_route(sel, pitch_of(nb), tc, static_cast<int>(nb), static_cast<int>(kx), static_cast<int>(sink), idx,
-                      excl, reinterpret_cast<cudaStream_t>(stream));
+  return launch_route(sel, pitch_of(nb), tc, group, static_cast<int>(nb), static_cast<int>(kx), static_cast<int>(sink),
+                      idx, excl, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int htrc_tile_attention(const int8_t* q8, const float* sq, const int8_t* dq8, const float* sdq, int64_t n_queries,
-                        int64_t t0, int64_t tc, const int8_t* g8, const float* sg, const float* lz, const uint16_t* vb,
-                        const uint8_t* excl, const int32_t* idx, int32_t kx, int64_t nb, const int8_t* k8,
-                        const float* ks, const uint16_t* v, int64_t n_keys, int32_t dim, int32_t leaf, float scale,
-                        const float* tail_part, float* out, float* lse, int32_t* status, htrc_stream_t stream) {
+                        int64_t t0, int64_t tc, int32_t group, const int8_t* g8, const float* sg, const float* lz,
+                        const uint16_t* vb, const uint8_t* excl, const int32_t* idx, int32_t kx, int64_t nb,
+                        const int8_t* k8, const float* ks, const uint16_t* v, int64_t n_keys, int32_t dim, int32_t leaf,
+                        float scale, const float* tail_part, const int32_t* perm, float* out, float* lse,
+                        int32_t* status, htrc_stream_t stream) {
   if (!q8 || !sq || !dq8 || !sdq || !k8 || !ks || !v || !out || n_queries < 1 || t0 < 0 || tc < 1) return HTRC_ERR_ARG;
+  const int64_t g = group > 1 ? group : 1;
+  if (g > kMaxGroup || t0 % g) return HTRC_ERR_ARG;
   if (dim != kDim || leaf != kLeaf) return HTRC_ERR_UNSUPPORTED;
   if (nb < 1 || n_keys != nb * leaf || kx < 0 || kx > nb) return HTRC_ERR_ARG;
   if (kx > kMaxRouted || nb > kMaxLeaves) return HTRC_ERR_UNSUPPORTED;
@@ -413,10 +467,11 @@ int htrc_tile_attention(const int8_t* q8, const float* sq, const int8_t* dq8, co
   TileMaps mp;
   if ((rc = tile_maps(&mp, q8, dq8, nt * 64, static_cast<const int8_t*>(g8p), static_cast<const uint16_t*>(vbp),
                       static_cast<const float*>(lzp), static_cast<const float*>(sgp),
-                      static_cast<const uint8_t*>(exp_), tc, nb, pitch_of(nb), k8, v, n_keys)) != HTRC_OK)
+                      static_cast<const uint8_t*>(exp_), (tc + g - 1) / g, nb, pitch_of(nb), k8, v, n_keys)) != HTRC_OK)
     return rc;
-  return launch_tile_attention(mp, sq, sdq, ks, idx, kx, static_cast<int>(nb), n_queries, t0, tc, scale_of(scale),
-                               tail_part, out, lse, status, reinterpret_cast<cudaStream_t>(stream));
+  return launch_tile_attention(mp, sq, sdq, ks, idx, kx, static_cast<int>(nb), n_queries, t0, tc, static_cast<int>(g),
+                               scale_of(scale), tail_part, perm, out, lse, status,
+                               reinterpret_cast<cudaStream_t>(stream));
 }
 
 int htrc_tail_partial(const void* q, int32_t q_dtype, int64_t n_queries, int32_t dim, const float* tail_k,

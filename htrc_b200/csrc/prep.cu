@@ -83,10 +83,51 @@ void launch_pack_rows(const void* x, int dtype, int64_t rows, int rounding, int8
   }
 }
 
-// One CTA (4 warps) per tile of 64 query rows.  Rows past n repeat the last query row (the
-// reference pads the last tile that way, h3/htrc_flat.py:150-152).
+// Row of q that tile row `row` holds: rows past n repeat the last row (the reference pads the last
+// tile that way, h3/htrc_flat.py:150-152), after the optional k-means permutation (:146-147).
+__device__ __forceinline__ int64_t source_row(const int32_t* perm, int64_t n, int64_t row) {
+  const int64_t r = row < n - 1 ? row : n - 1;
+  return perm ? static_cast<int64_t>(__ldg(perm + r)) : r;
+}
+
+__device__ __forceinline__ void store_centre(int64_t c, int col, float m, float* mu, uint16_t* mu_hi,
+                                             uint16_t* mu_lo) {
+  mu[c * 128 + col] = m;
+  const __nv_bfloat16 hi = __float2bfloat16_rn(m);
+  const __nv_bfloat16 lo = __float2bfloat16_rn(__fsub_rn(m, __bfloat162float(hi)));
+  mu_hi[c * 128 + col] = __bfloat16_as_ushort(hi);
+  mu_lo[c * 128 + col] = __bfloat16_as_ushort(lo);
+}
+
+// Centres of groups of G > 1 consecutive tiles (h3/htrc_flat.py:223-231): the mean of all G * 64 rows
+// of the padded tiles -- the last tile's rows past n repeat the last row and the tiles that fill the
+// last group repeat the last tile.  One CTA per group, thread = column; float64 sum rounded once.
 template <typename T>
-__global__ void __launch_bounds__(128) tile_prep_kernel(const T* __restrict__ q, int64_t n, float* __restrict__ mu,
+__global__ void __launch_bounds__(128) group_centre_kernel(const T* __restrict__ q, const int32_t* __restrict__ perm,
+                                                           int64_t n, int64_t nt, int group, float* __restrict__ mu,
+                                                           uint16_t* __restrict__ mu_hi, uint16_t* __restrict__ mu_lo) {
+  const int64_t g = blockIdx.x;
+  const int col = threadIdx.x;
+  double s = 0.0;
+  for (int x = 0; x < group; ++x) {
+    const int64_t t = g * group + x < nt ? g * group + x : nt - 1;
+#pragma unroll 8
+    for (int r = 0; r < 64; ++r) {
+      const int64_t src = source_row(perm, n, t * 64 + r);
+      if constexpr (sizeof(T) == 4)
+        s += static_cast<double>(__ldg(reinterpret_cast<const float*>(q) + src * 128 + col));
+      else
+        s += static_cast<double>(__uint_as_float(static_cast<uint32_t>(__ldg(q + src * 128 + col)) << 16));
+    }
+  }
+  store_centre(g, col, static_cast<float>(s / static_cast<double>(group * 64)), mu, mu_hi, mu_lo);
+}
+
+// One CTA (4 warps) per tile of 64 query rows: the tile's centre (group 1; else the group centre
+// written by group_centre_kernel) and the codes of its rows and of their offsets from the centre.
+template <typename T>
+__global__ void __launch_bounds__(128) tile_prep_kernel(const T* __restrict__ q, const int32_t* __restrict__ perm,
+                                                        int64_t n, int group, float* __restrict__ mu,
                                                         uint16_t* __restrict__ mu_hi, uint16_t* __restrict__ mu_lo,
                                                         int8_t* __restrict__ q8, float* __restrict__ sq,
                                                         int8_t* __restrict__ dq8, float* __restrict__ sdq) {
@@ -99,24 +140,21 @@ __global__ void __launch_bounds__(128) tile_prep_kernel(const T* __restrict__ q,
   // stage the tile: warp w loads rows w, w+4, ...; lane owns 4 columns
   const int warp = tid >> 5, lane = tid & 31;
   for (int r = warp; r < 64; r += 4) {
-    const int64_t gr = (r0 + r < n - 1) ? r0 + r : n - 1;
     float v[4];
-    load4<T>(q + gr * 128 + lane * 4, v);
+    load4<T>(q + source_row(perm, n, r0 + r) * 128 + lane * 4, v);
 #pragma unroll
     for (int i = 0; i < 4; ++i) qs[r][lane * 4 + i] = v[i];
   }
   __syncthreads();
-  // centre: float64 sum over the real rows, divided and rounded once
-  {
+  if (group <= 1) {
+    // centre: float64 sum over the real rows, divided and rounded once
     double s = 0.0;
     for (int r = 0; r < nreal; ++r) s += static_cast<double>(qs[r][tid]);
     const float m = static_cast<float>(s / static_cast<double>(nreal));
     mus[tid] = m;
-    mu[static_cast<int64_t>(t) * 128 + tid] = m;
-    const __nv_bfloat16 hi = __float2bfloat16_rn(m);
-    const __nv_bfloat16 lo = __float2bfloat16_rn(__fsub_rn(m, __bfloat162float(hi)));
-    mu_hi[static_cast<int64_t>(t) * 128 + tid] = __bfloat16_as_ushort(hi);
-    mu_lo[static_cast<int64_t>(t) * 128 + tid] = __bfloat16_as_ushort(lo);
+    store_centre(t, tid, m, mu, mu_hi, mu_lo);
+  } else {
+    mus[tid] = mu[static_cast<int64_t>(t / group) * 128 + tid];
   }
   __syncthreads();
   float m4[4];
@@ -145,14 +183,22 @@ __global__ void __launch_bounds__(128) tile_prep_kernel(const T* __restrict__ q,
   }
 }
 
-void launch_tile_prep(const void* q, int dtype, int64_t n, float* mu, uint16_t* mu_hi, uint16_t* mu_lo, int8_t* q8,
-                      float* sq, int8_t* dq8, float* sdq, cudaStream_t st) {
-  const unsigned nt = static_cast<unsigned>((n + 63) / 64);
-  if (dtype == HTRC_DTYPE_BF16)
-    tile_prep_kernel<uint16_t><<<nt, 128, 0, st>>>(static_cast<const uint16_t*>(q), n, mu, mu_hi, mu_lo, q8, sq,
-                                                    dq8, sdq);
-  else
-    tile_prep_kernel<float><<<nt, 128, 0, st>>>(static_cast<const float*>(q), n, mu, mu_hi, mu_lo, q8, sq, dq8, sdq);
+void launch_tile_prep(const void* q, int dtype, int64_t n, const int32_t* perm, int group, float* mu, uint16_t* mu_hi,
+                      uint16_t* mu_lo, int8_t* q8, float* sq, int8_t* dq8, float* sdq, cudaStream_t st) {
+  const int64_t nt = (n + 63) / 64;
+  const int g = group > 1 ? group : 1;
+  const unsigned ng = static_cast<unsigned>((nt + g - 1) / g);
+  if (dtype == HTRC_DTYPE_BF16) {
+    const uint16_t* qb = static_cast<const uint16_t*>(q);
+    if (g > 1) group_centre_kernel<uint16_t><<<ng, 128, 0, st>>>(qb, perm, n, nt, g, mu, mu_hi, mu_lo);
+    tile_prep_kernel<uint16_t><<<static_cast<unsigned>(nt), 128, 0, st>>>(qb, perm, n, g, mu, mu_hi, mu_lo, q8, sq,
+                                                                         dq8, sdq);
+  } else {
+    const float* qf = static_cast<const float*>(q);
+    if (g > 1) group_centre_kernel<float><<<ng, 128, 0, st>>>(qf, perm, n, nt, g, mu, mu_hi, mu_lo);
+    tile_prep_kernel<float><<<static_cast<unsigned>(nt), 128, 0, st>>>(qf, perm, n, g, mu, mu_hi, mu_lo, q8, sq, dq8,
+                                                                      sdq);
+  }
 }
 
 // Exact partial of each query row against the n_tail tail keys: one warp per row.

@@ -1,5 +1,8 @@
 // Per-tile top-E near-leaf routing (h3/htrc_flat.py:232-233, :250-265): the first `sink` leaves are
-// forced (selection +inf), then the kx largest selections.  One CTA of 256 threads per tile: an
+// forced (selection +inf), then the kx largest selections.  With groups of G tiles (:223-231) a group's
+// selection is the maximum over its tiles' rows (the reference's row-max runs over all G * 64 rows of
+// the group; the repeats of the last tile that pad the last group add nothing to a maximum) and one
+// routing serves the whole group.  One CTA of 256 threads per group: an
 // MSB-first 8-bit radix select of the kx-th largest order-preserving key, ties at the threshold
 // broken towards the lower leaf index, then an order-preserving compaction, so idx comes out in
 // ascending leaf order.  No host synchronisation (fixed-size output).
@@ -46,8 +49,8 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* scratch, int* to
 }  // namespace
 
 __global__ void __launch_bounds__(kThreads)
-    route_kernel(const float* __restrict__ sel, int64_t pitch, int nb, int kx, int sink, int32_t* __restrict__ idx,
-                 uint8_t* __restrict__ excl) {
+    route_kernel(const float* __restrict__ sel, int64_t pitch, int64_t tc, int group, int nb, int kx, int sink,
+                 int32_t* __restrict__ idx, uint8_t* __restrict__ excl) {
   __shared__ uint32_t keys[kMaxLeaves];
   __shared__ int hist[256];
   __shared__ int scratch[32];
@@ -65,8 +68,13 @@ __global__ void __launch_bounds__(kThreads)
       for (int l = tid; l < kx; l += kThreads) ix[l] = l;
     return;
   }
-  const float* row = sel + static_cast<int64_t>(t) * pitch;
-  for (int l = tid; l < nb; l += kThreads) keys[l] = l < sink ? 0xFFFFFFFFu : order_key(row[l]);
+  const int64_t ta = static_cast<int64_t>(t) * group;
+  const int64_t tb = ta + group < tc ? ta + group : tc;
+  for (int l = tid; l < nb; l += kThreads) {
+    float s = sel[ta * pitch + l];
+    for (int64_t x = ta + 1; x < tb; ++x) s = fmaxf(s, sel[x * pitch + l]);
+    keys[l] = l < sink ? 0xFFFFFFFFu : order_key(s);
+  }
   if (tid == 0) {
     s_prefix = 0;
     s_remaining = kx;
@@ -125,11 +133,13 @@ __global__ void __launch_bounds__(kThreads)
   for (int l = nb + tid; l < static_cast<int>(pitch); l += kThreads) ex[l] = 0;
 }
 
-int launch_route(const float* sel, int64_t pitch, int64_t tc, int nb, int kx, int sink, int32_t* idx, uint8_t* excl,
-                 cudaStream_t st) {
+int launch_route(const float* sel, int64_t pitch, int64_t tc, int group, int nb, int kx, int sink, int32_t* idx,
+                 uint8_t* excl, cudaStream_t st) {
   if (nb > kMaxLeaves) return HTRC_ERR_UNSUPPORTED;
   if (tc <= 0) return HTRC_OK;
-  route_kernel<<<static_cast<unsigned>(tc), kThreads, 0, st>>>(sel, pitch, nb, kx, sink, idx, excl);
+  const int g = group > 1 ? group : 1;
+  const unsigned ng = static_cast<unsigned>((tc + g - 1) / g);
+  route_kernel<<<ng, kThreads, 0, st>>>(sel, pitch, tc, g, nb, kx, sink, idx, excl);
   return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
 }
 

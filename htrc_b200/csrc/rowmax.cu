@@ -5,7 +5,9 @@
 // Computed transposed so the maximum over the 64 tile rows stays inside one thread: per block of 128
 // leaves, C = G8_block (M=128 leaves, K=128) x DQ8_tile^T (N=64 rows) into TMEM (int32); the thread
 // owning TMEM lane l reduces its 64 columns.  One CTA per tile; warp 0 loads (TMA), warp 1 issues
-// MMAs, warps 2-5 reduce.  The state is streamed once (HBM-bound).
+// MMAs, warps 2-5 reduce.  The state is streamed once (HBM-bound).  With groups of G tiles sharing one
+// state row (h3/htrc_flat.py:223-231) the CTA of tile t reads state row t / G and writes its own sel row;
+// the maximum over the group's tiles is taken by the routing kernel.
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -39,12 +41,13 @@ __global__ void __launch_bounds__(192)
     rowmax_kernel(const __grid_constant__ CUtensorMap tm_dq8, const __grid_constant__ CUtensorMap tm_g8,
                   const __grid_constant__ CUtensorMap tm_sg, const __grid_constant__ CUtensorMap tm_lz,
                   const float* __restrict__ sdq, float* __restrict__ sel, int64_t pitch, int64_t t0, int nb,
-                  int* status) {
+                  int group, int* status) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Bars* bars = reinterpret_cast<Bars*>(smem + kOffBar);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tloc = blockIdx.x;
+  const int srow = tloc / group;             // state row of this tile
   const int64_t tg = t0 + tloc;
   const int nblk = (nb + 127) / 128;
   volatile int* abort_flag = &bars->abort_flag;
@@ -79,9 +82,9 @@ __global__ void __launch_bounds__(192)
         if (j >= kStages && !mbar_wait(&bars->empty[s], ((j / kStages) - 1) & 1, status, abort_flag)) break;
         uint8_t* st = smem + kOffStage + s * kStageStride;
         mbar_arrive_expect_tx(&bars->full[s], kStageBytes);
-        tma_load_3d(st, &tm_g8, &bars->full[s], 0, j * 128, tloc, pol_stream);
-        tma_load_2d(st + kBlkBytes, &tm_sg, &bars->full[s], j * 128, tloc, pol_stream);
-        tma_load_2d(st + kBlkBytes + 512, &tm_lz, &bars->full[s], j * 128, tloc, pol_stream);
+        tma_load_3d(st, &tm_g8, &bars->full[s], 0, j * 128, srow, pol_stream);
+        tma_load_2d(st + kBlkBytes, &tm_sg, &bars->full[s], j * 128, srow, pol_stream);
+        tma_load_2d(st + kBlkBytes + 512, &tm_lz, &bars->full[s], j * 128, srow, pol_stream);
       }
     }
   } else if (warp == 1) {
@@ -143,7 +146,7 @@ __global__ void __launch_bounds__(192)
 }
 
 int launch_rowmax(const RowmaxMaps& maps, const float* sdq, float* sel, int64_t pitch, int64_t t0, int64_t tc, int nb,
-                  int* status, cudaStream_t st) {
+                  int group, int* status, cudaStream_t st) {
   static bool attr_done[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -153,7 +156,7 @@ int launch_rowmax(const RowmaxMaps& maps, const float* sdq, float* sel, int64_t 
     attr_done[dev] = true;
   }
   rowmax_kernel<<<static_cast<unsigned>(tc), 192, kSmemBytes, st>>>(maps.dq8, maps.g8, maps.sg, maps.lz, sdq, sel,
-                                                                     pitch, t0, nb, status);
+                                                                     pitch, t0, nb, group > 1 ? group : 1, status);
   return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
 }
 

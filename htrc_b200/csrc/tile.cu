@@ -24,6 +24,10 @@
 // The producer and issuer warps run converged and let one elected lane issue: a warp whose lanes take
 // different roles serialises them, since a lane suspended in an mbarrier wait holds up the others.
 //
+// Groups (h3/htrc_flat.py:223-231): G consecutive tiles share one far-field state row and one routing;
+// tile t of the chunk reads state row t / G.  k-means order (:146-147, :159-165): tile row i is query
+// perm[i], so the epilogue writes out/lse row perm[i] (and reads the tail partial of that row).
+//
 // Warp roles (384 threads): warp 0 X-ring producer; warp 1 PV issuer (+ TMEM owner); warp 11 QK issuer
 // and Y-ring producer (both wait for the same PV completions); warps 2-5 and 6-9 the two softmax
 // warpgroups; warp 10 per-column constants (scale * log2 e, lz * log2 e or -inf).
@@ -92,9 +96,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                           const __grid_constant__ CUtensorMap tm_excl, const __grid_constant__ CUtensorMap tm_k8,
                           const __grid_constant__ CUtensorMap tm_v, const float* __restrict__ sq,
                           const float* __restrict__ sdq, const float* __restrict__ ks, const int32_t* __restrict__ idx,
-                          int kx, int nb, int nf, int64_t n, int64_t t0, int64_t tc, float scale,
-                          const float* __restrict__ tail_part, float* __restrict__ out, float* __restrict__ lse,
-                          int* status) {
+                          int kx, int nb, int nf, int64_t n, int64_t t0, int64_t tc, int group, float scale,
+                          const float* __restrict__ tail_part, const int32_t* __restrict__ perm,
+                          float* __restrict__ out, float* __restrict__ lse, int* status) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Bars* bars = reinterpret_cast<Bars*>(smem + kOffBar);
@@ -104,6 +108,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tlocA = 2 * blockIdx.x;
   const int ntiles = (tlocA + 1 < tc) ? 2 : 1;
+  const int srow[2] = {tlocA / group, (tlocA + 1) / group};     // state rows of tiles A and B
   const int total = nf + kx;        // far steps + near steps (one routed leaf per step)
   volatile int* abort_flag = &bars->abort_flag;
 
@@ -128,7 +133,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // routed leaves of both tiles -> shared memory, range-checked
     for (int x = 0; x < ntiles; ++x) {
-      const int32_t* src = idx + static_cast<int64_t>(tlocA + x) * kx;
+      const int32_t* src = idx + static_cast<int64_t>(srow[x]) * kx;
       for (int e = lane; e < kx; e += 32) {
         int leaf = __ldg(src + e);
         if (leaf < 0 || leaf >= nb) {
@@ -170,7 +175,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_arrive_expect_tx(&bars->x_full[s], (kXBytes + 256 + 256 + 64) * ntiles);
             for (int x = 0; x < ntiles; ++x) {
               uint8_t* tx = st + x * kXTile;
-              const int tl = tlocA + x;
+              const int tl = srow[x];
               tma_load_3d(tx, &tm_g8, &bars->x_full[s], 0, nx * 64, tl, pol_stream);
               tma_load_2d(tx + kXBytes, &tm_lz, &bars->x_full[s], nx * 64, tl, pol_stream);
               tma_load_2d(tx + kXBytes + 256, &tm_sg, &bars->x_full[s], nx * 64, tl, pol_stream);
@@ -240,7 +245,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* ty = st + x * kYBytes;
           // both 64-column halves in one load: [half][64 rows][64] at ty, ty + kYBytes / 2
           if (ny < nf)
-            tma_load_4d(ty, &tm_vb, &bars->y_full[s], 0, ny * 64, 0, tlocA + x, pol_stream);
+            tma_load_4d(ty, &tm_vb, &bars->y_full[s], 0, ny * 64, 0, srow[x], pol_stream);
           else
             tma_load_3d(ty, &tm_v, &bars->y_full[s], 0, idx_s[x * kMaxKx + (ny - nf)] * 64, 0, pol_keep);
         }
@@ -418,7 +423,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float m0 = kcount ? m_used : -INFINITY;
       const float n0 = m0 * kLn2, n1 = m1 * kLn2;           // natural-log units
       const bool valid = has_tile && gr < n;
-      const float* tp = (tail_part != nullptr && valid) ? tail_part + gr * 130 : nullptr;
+      const int64_t orow = (perm != nullptr && valid) ? static_cast<int64_t>(__ldg(perm + gr)) : gr;
+      const float* tp = (tail_part != nullptr && valid) ? tail_part + orow * 130 : nullptr;
       const float mt = tp ? tp[128] : -INFINITY, lt = tp ? tp[129] : 0.f;
       const float mm = fmaxf(fmaxf(n0, n1), mt);
       const float a0 = n0 == -INFINITY ? 0.f : expf(n0 - mm);
@@ -427,7 +433,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float den = l * a0 + l1 * a1 + lt * at;
       const float inv = 1.0f / fmaxf(den, 1e-30f);
       const float c0 = a0 * inv, c1 = a1 * inv, ct = at * inv;
-      if (valid && lse != nullptr) lse[gr] = mm + logf(fmaxf(den, 1e-30f));
+      if (valid && lse != nullptr) lse[orow] = mm + logf(fmaxf(den, 1e-30f));
       __syncwarp();
       tc_fence_after();
 #pragma unroll 1
@@ -437,7 +443,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld32(tmem + lane_base + kColO + 128 + 32 * q4, o1);
         tmem_ld_wait();
         if (valid) {
-          float4* dst = reinterpret_cast<float4*>(out + gr * 128 + 32 * q4);
+          float4* dst = reinterpret_cast<float4*>(out + orow * 128 + 32 * q4);
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             float v[4];
@@ -462,8 +468,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 int launch_tile_attention(const TileMaps& maps, const float* sq, const float* sdq, const float* ks, const int32_t* idx,
-                          int kx, int nb, int64_t n, int64_t t0, int64_t tc, float scale, const float* tail_part,
-                          float* out, float* lse, int* status, cudaStream_t st) {
+                          int kx, int nb, int64_t n, int64_t t0, int64_t tc, int group, float scale,
+                          const float* tail_part, const int32_t* perm, float* out, float* lse, int* status,
+                          cudaStream_t st) {
   if (kx > kMaxKx || nb > 65535) return HTRC_ERR_UNSUPPORTED;
   static bool attr_done[64] = {};
   int dev = 0;
@@ -478,7 +485,8 @@ int launch_tile_attention(const TileMaps& maps, const float* sq, const float* sd
   const unsigned grid = static_cast<unsigned>((tc + 1) / 2);
   tile_attention_kernel<<<grid, kThreads, kSmemBytes, st>>>(maps.q8, maps.dq8, maps.g8, maps.vb, maps.lz, maps.sg,
                                                             maps.excl, maps.k8, maps.v, sq, sdq, ks, idx, kx, nb, nf,
-                                                            n, t0, tc, scale, tail_part, out, lse, status);
+                                                            n, t0, tc, group > 1 ? group : 1, scale, tail_part,
+                                                            perm, out, lse, status);
   return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
 }
 

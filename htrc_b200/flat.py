@@ -7,6 +7,11 @@ C-ABI library libhtrc_flat.so (hand-written sm_100a kernels).  There is no other
 fallback: configurations the kernels do not implement raise ``NotImplementedError`` and argument
 errors raise the reference's ``ValueError``s.
 
+Query order and groups: ``order="kmeans"`` (the accurate/max modes) reorders the queries on the device
+by the reference's k-means permutation before tiling and writes the output back in the caller's order
+(h3/htrc_flat.py:47-65, :146-147, :159-165); ``kern={"group": G}`` lets G consecutive tiles share one
+expansion centre, far-field state and routing (:223-231).
+
 Additions over the reference: ``return_lse=True`` also returns the log-partition per query
 (logit units, scale * q.k), and ``backend`` accepts "cuda"/"b200" as names of the same path.
 """
@@ -82,8 +87,6 @@ def _check_args(q, k, v, tile, exact_leaves, order, curvature, leaf, select, bac
         raise ValueError("store='fp8' needs dot='bf16', select='max' and no state fake-quant")
     if store != "int8" or dot != "bf16":
         raise NotImplementedError("only the INT8 production path (store='int8', dot='bf16') is implemented")
-    if order != "seq":
-        raise NotImplementedError("order='kmeans' (accurate/max modes) is not implemented yet")
     if int(tile) != TILE or int(leaf) != LEAF:
         raise NotImplementedError(f"the kernels implement tile={TILE}, leaf={LEAF} (got tile={tile}, leaf={leaf})")
     if int(sel_stride) != 1:
@@ -109,8 +112,20 @@ def _prep_inputs(q, k, v, tail):
     return qd, kb, vb, tk, tv
 
 
+def group_of(kern) -> int:
+    """G consecutive tiles per centre: the reference's ``max(1, int(kern.get("group", 1)))``
+    (h3/htrc_flat.py:223)."""
+    return max(1, int((kern or {}).get("group", 1)))
+
+
+def order_code(order) -> int:
+    """The triton path permutes for order == "kmeans" and keeps the sequence otherwise
+    (h3/htrc_flat.py:146)."""
+    return _lib.ORDER_KMEANS if order == "kmeans" else _lib.ORDER_SEQ
+
+
 def _args(qd, kb, vb, tk, tv, exact_leaves, sink_leaves, tile_chunk, scale, out=None, lse=None, ws=None,
-          stage_events=None):
+          stage_events=None, group=1, order=_lib.ORDER_SEQ):
     a = _lib.HtrcFlatArgs()
     a.q = ptr(qd)
     a.q_dtype = _lib.DTYPE_BF16 if qd.dtype == torch.bfloat16 else _lib.DTYPE_F32
@@ -123,6 +138,7 @@ def _args(qd, kb, vb, tk, tv, exact_leaves, sink_leaves, tile_chunk, scale, out=
     a.tail_k, a.tail_v = ptr(tk), ptr(tv)
     a.n_tail = int(tk.shape[0]) if tk is not None else 0
     a.out, a.lse = ptr(out), ptr(lse)
+    a.group, a.order = int(group), int(order)
     if ws is not None:
         a.workspace, a.workspace_bytes = ptr(ws), int(ws.numel())
     if stage_events:
@@ -138,13 +154,15 @@ def _args(qd, kb, vb, tk, tv, exact_leaves, sink_leaves, tile_chunk, scale, out=
     return a
 
 
-def workspace_bytes(n_queries, n_keys, exact_leaves, sink_leaves=0, tile_chunk=0, n_tail=0) -> int:
+def workspace_bytes(n_queries, n_keys, exact_leaves, sink_leaves=0, tile_chunk=0, n_tail=0, group=1,
+                    order=_lib.ORDER_SEQ) -> int:
     """Device workspace one forward call needs."""
     a = _lib.HtrcFlatArgs()
     a.n_queries, a.n_keys, a.dim, a.tile, a.leaf = int(n_queries), int(n_keys), DIM, TILE, LEAF
     a.q_dtype = _lib.DTYPE_F32
     a.exact_leaves, a.sink_leaves = int(exact_leaves), int(sink_leaves)
     a.tile_chunk, a.n_tail = int(tile_chunk or 0), int(n_tail)
+    a.group, a.order = int(group), int(order)
     nbytes = ctypes.c_size_t()
     check(lib().htrc_flat_workspace_size(a, nbytes), "workspace size")
     return int(nbytes.value)
@@ -163,12 +181,13 @@ def _workspace(ws, nbytes, device):
 
 
 def forward_into(qd, kb, vb, tk, tv, *, exact_leaves, sink_leaves=0, tile_chunk=0, scale=None, out, lse=None,
-                 workspace, stream=None, stage_events=None):
+                 workspace, stream=None, stage_events=None, group=1, order=_lib.ORDER_SEQ):
     """One head through ``htrc_flat_forward`` into caller-provided buffers (no allocation; CUDA-graph
     capturable).  qd [N, 128] f32/bf16, kb/vb [M, 128] bf16, out [N, 128] f32, lse [N] f32 or None;
     stage_events: optional list of torch.cuda.Event recorded between the stages (see
-    include/htrc_flat.h)."""
-    a = _args(qd, kb, vb, tk, tv, exact_leaves, sink_leaves, tile_chunk, scale, out, lse, workspace, stage_events)
+    include/htrc_flat.h); group / order: ``group_of(kern)`` / ``order_code(order)``."""
+    a = _args(qd, kb, vb, tk, tv, exact_leaves, sink_leaves, tile_chunk, scale, out, lse, workspace, stage_events,
+              group, order)
     check(lib().htrc_flat_forward(a, stream_ptr(stream)), "htrc_flat_forward")
 
 
@@ -193,18 +212,19 @@ def flat_attention(q, k, v, *, tile=64, exact_leaves=64, order="seq", curvature=
     _check_args(q, k, v, tile, exact_leaves, order, curvature, leaf, select, backend, store, dot,
                 sel_stride, quant, sink_leaves, tail)
     qd, kb, vb, tk, tv = _prep_inputs(q, k, v, tail)
+    grp, oc = group_of(kern), order_code(order)
     if prof is not None:
         st = run_stages(qd, kb, vb, tk, tv, exact_leaves=exact_leaves, sink_leaves=sink_leaves,
-                        tile_chunk=tile_chunk, scale=scale, prof=prof)
+                        tile_chunk=tile_chunk, scale=scale, prof=prof, group=grp, order=oc)
         return (st["out"], st["lse"]) if return_lse else st["out"]
     n = int(qd.shape[0])
     out = torch.empty((n, DIM), dtype=torch.float32, device=q.device)
     lse = torch.empty((n,), dtype=torch.float32, device=q.device) if return_lse else None
     nbytes = workspace_bytes(n, int(kb.shape[0]), exact_leaves, sink_leaves, tile_chunk,
-                             int(tk.shape[0]) if tk is not None else 0)
+                             int(tk.shape[0]) if tk is not None else 0, grp, oc)
     w = _workspace(ws, nbytes, q.device)
     forward_into(qd, kb, vb, tk, tv, exact_leaves=exact_leaves, sink_leaves=sink_leaves,
-                 tile_chunk=tile_chunk, scale=scale, out=out, lse=lse, workspace=w)
+                 tile_chunk=tile_chunk, scale=scale, out=out, lse=lse, workspace=w, group=grp, order=oc)
     return (out, lse) if return_lse else out
 
 
@@ -215,63 +235,72 @@ def flat_attention_prod(q, k, v, **over):
 
 @torch.inference_mode()
 def run_stages(qd, kb, vb, tk=None, tv=None, *, exact_leaves, sink_leaves=0, tile_chunk=0, scale=None,
-               prof=None, stream=None):
+               prof=None, stream=None, group=1, order=_lib.ORDER_SEQ):
     """The same operator launched stage by stage through the C ABI's stage entry points, returning
-    every intermediate (k8, ks, mu, q8, sq, dq8, sdq, g8, sg, lz, vb, sel, idx, excl, out, lse).
+    every intermediate (perm, k8, ks, mu, q8, sq, dq8, sdq, g8, sg, lz, vb, sel, idx, excl, out, lse).
     Used for stage timing (``prof``, the reference's stage names prep/stats/select/tile/finish) and
-    for per-stage parity tests.  The state of all tiles is kept (tile_chunk only sets the launch
-    granularity of the state stages)."""
+    for per-stage parity tests.  The state of all centre rows is kept (tile_chunk only sets the launch
+    granularity of the state stages, in groups of ``group`` tiles)."""
     L = lib()
     dev = qd.device
     s = stream_ptr(stream)
     tick = _Tick(prof)
     n, m = int(qd.shape[0]), int(kb.shape[0])
     nt, nb = -(-n // TILE), m // LEAF
+    grp = max(1, int(group))
+    ng = -(-nt // grp)
     pitch = leaf_pitch(nb)
     sink = max(0, min(int(sink_leaves), nb))
     kx = min(int(exact_leaves) + sink, nb)
     sc = 1.0 / math.sqrt(DIM) if scale is None else float(scale)
     qdt = _lib.DTYPE_BF16 if qd.dtype == torch.bfloat16 else _lib.DTYPE_F32
     e = lambda *shape, dt=torch.float32: torch.empty(shape, dtype=dt, device=dev)  # noqa: E731
-    r = dict(k8=e(m, DIM, dt=torch.int8), ks=e(m), mu=e(nt, DIM), mu_hi=e(nt, DIM, dt=torch.bfloat16),
-             mu_lo=e(nt, DIM, dt=torch.bfloat16), q8=e(nt * TILE, DIM, dt=torch.int8), sq=e(nt * TILE),
-             dq8=e(nt * TILE, DIM, dt=torch.int8), sdq=e(nt * TILE), g8=e(nt, nb, DIM, dt=torch.int8),
-             sg=e(nt, pitch), lz=e(nt, pitch), vb=e(nt, nb, DIM, dt=torch.bfloat16), sel=torch.zeros((nt, pitch),
-             dtype=torch.float32, device=dev), idx=e(nt, max(kx, 1), dt=torch.int32),
-             excl=e(nt, pitch, dt=torch.uint8), out=e(n, DIM), lse=e(n),
-             status=torch.zeros((1,), dtype=torch.int32, device=dev))
+    r = dict(k8=e(m, DIM, dt=torch.int8), ks=e(m), mu=e(ng, DIM), mu_hi=e(ng, DIM, dt=torch.bfloat16),
+             mu_lo=e(ng, DIM, dt=torch.bfloat16), q8=e(nt * TILE, DIM, dt=torch.int8), sq=e(nt * TILE),
+             dq8=e(nt * TILE, DIM, dt=torch.int8), sdq=e(nt * TILE), g8=e(ng, nb, DIM, dt=torch.int8),
+             sg=e(ng, pitch), lz=e(ng, pitch), vb=e(ng, nb, DIM, dt=torch.bfloat16), sel=torch.zeros((nt, pitch),
+             dtype=torch.float32, device=dev), idx=e(ng, max(kx, 1), dt=torch.int32),
+             excl=e(ng, pitch, dt=torch.uint8), out=e(n, DIM), lse=e(n),
+             status=torch.zeros((1,), dtype=torch.int32, device=dev), perm=None)
     stp = ptr(r["status"])
     check(L.htrc_pack_int8(ptr(kb), _lib.DTYPE_BF16, m, DIM, _lib.ROUND_HALF_EVEN, ptr(r["k8"]), ptr(r["ks"]), s),
           "htrc_pack_int8")
-    check(L.htrc_tile_prep(ptr(qd), qdt, n, DIM, TILE, ptr(r["mu"]), ptr(r["mu_hi"]), ptr(r["mu_lo"]), ptr(r["q8"]),
-                           ptr(r["sq"]), ptr(r["dq8"]), ptr(r["sdq"]), s), "htrc_tile_prep")
+    if order == _lib.ORDER_KMEANS:
+        r["perm"] = e(n, dt=torch.int32)
+        nbytes = ctypes.c_size_t()
+        check(L.htrc_kmeans_scratch_size(n, nbytes), "htrc_kmeans_scratch_size")
+        scratch = torch.empty(int(nbytes.value), dtype=torch.uint8, device=dev)
+        check(L.htrc_kmeans_order(ptr(qd), qdt, n, DIM, ptr(r["perm"]), ptr(scratch), int(nbytes.value), s),
+              "htrc_kmeans_order")
+    perm = ptr(r["perm"])
+    check(L.htrc_tile_prep(ptr(qd), qdt, n, DIM, TILE, perm, grp, ptr(r["mu"]), ptr(r["mu_hi"]), ptr(r["mu_lo"]),
+                           ptr(r["q8"]), ptr(r["sq"]), ptr(r["dq8"]), ptr(r["sdq"]), s), "htrc_tile_prep")
     tail_part = None
     if tk is not None:
         tail_part = e(n, DIM + 2)
         check(L.htrc_tail_partial(ptr(qd), qdt, n, DIM, ptr(tk), ptr(tv), int(tk.shape[0]), sc, ptr(tail_part), s),
               "htrc_tail_partial")
     tick("prep")
-    chunk = nt if not tile_chunk or tile_chunk <= 0 else min(int(tile_chunk), nt)
+    gstep = ng if not tile_chunk or tile_chunk <= 0 else min(max(1, int(tile_chunk) // grp), ng)
     far = kx < nb
     if far:
-        for t0 in range(0, nt, chunk):
-            tc = min(chunk, nt - t0)
-            check(L.htrc_leaf_stats(ptr(r["mu_hi"]), ptr(r["mu_lo"]), nt, t0, tc, ptr(kb), ptr(vb), m, DIM, LEAF, sc,
-                                    ptr(r["g8"][t0]), ptr(r["sg"][t0]), ptr(r["lz"][t0]), ptr(r["vb"][t0]), stp, s),
+        for g0 in range(0, ng, gstep):
+            gc = min(gstep, ng - g0)
+            check(L.htrc_leaf_stats(ptr(r["mu_hi"]), ptr(r["mu_lo"]), ng, g0, gc, ptr(kb), ptr(vb), m, DIM, LEAF, sc,
+                                    ptr(r["g8"][g0]), ptr(r["sg"][g0]), ptr(r["lz"][g0]), ptr(r["vb"][g0]), stp, s),
                   "htrc_leaf_stats")
     tick("stats")
     if far and kx > 0:
-        for t0 in range(0, nt, chunk):
-            tc = min(chunk, nt - t0)
-            check(L.htrc_rowmax_select(ptr(r["dq8"]), ptr(r["sdq"]), t0, tc, ptr(r["g8"][t0]), ptr(r["sg"][t0]),
-                                       ptr(r["lz"][t0]), nb, DIM, ptr(r["sel"][t0]), stp, s), "htrc_rowmax_select")
-    check(L.htrc_route(ptr(r["sel"]), nt, nb, int(exact_leaves), sink, ptr(r["idx"]), ptr(r["excl"]), s), "htrc_route")
+        check(L.htrc_rowmax_select(ptr(r["dq8"]), ptr(r["sdq"]), 0, nt, grp, ptr(r["g8"]), ptr(r["sg"]), ptr(r["lz"]),
+                                   nb, DIM, ptr(r["sel"]), stp, s), "htrc_rowmax_select")
+    check(L.htrc_route(ptr(r["sel"]), nt, nb, int(exact_leaves), sink, grp, ptr(r["idx"]), ptr(r["excl"]), s),
+          "htrc_route")
     tick("select")
-    check(L.htrc_tile_attention(ptr(r["q8"]), ptr(r["sq"]), ptr(r["dq8"]), ptr(r["sdq"]), n, 0, nt, ptr(r["g8"]),
+    check(L.htrc_tile_attention(ptr(r["q8"]), ptr(r["sq"]), ptr(r["dq8"]), ptr(r["sdq"]), n, 0, nt, grp, ptr(r["g8"]),
                                 ptr(r["sg"]), ptr(r["lz"]), ptr(r["vb"]), ptr(r["excl"]), ptr(r["idx"]), kx, nb,
-                                ptr(r["k8"]), ptr(r["ks"]), ptr(vb), m, DIM, LEAF, sc, ptr(tail_part), ptr(r["out"]),
-                                ptr(r["lse"]), stp, s), "htrc_tile_attention")
+                                ptr(r["k8"]), ptr(r["ks"]), ptr(vb), m, DIM, LEAF, sc, ptr(tail_part), perm,
+                                ptr(r["out"]), ptr(r["lse"]), stp, s), "htrc_tile_attention")
     tick("tile")
     tick("finish")
-    r["kx"], r["nb"], r["pitch"] = kx, nb, pitch
+    r["kx"], r["nb"], r["pitch"], r["group"] = kx, nb, pitch, grp
     return r

@@ -30,34 +30,37 @@ MODES = {
 CHUNKS = (1024, 512, 256, 128, 64, 32, 16)
 
 STATIC_MIB = 0.0      # graph runner's static q (fp32) / k / v (bf16) copies, added per call below
-KMEANS_MIB = 65.0     # reserved for the k-means ordering of the accurate/max modes
+KMEANS_MIB = 0.0      # the k-means ordering's scratch is part of the library workspace (order="kmeans")
 
 
 def predicted_peak_mib(keys: int, tile: int, tile_chunk: int, splits: int = 8, leaf: int = 64,
                        dim: int = 128, order: str = "seq", graph: bool = True, queries: int = 0,
-                       exact_leaves: int = 256) -> float:
+                       exact_leaves: int = 256, group: int = 1) -> float:
     """Device memory of one head above the caller's q/k/v, in MiB: this library's workspace
-    (htrc_flat_workspace_size) for the chunk size, plus the static graph copies.  Same signature as
-    the reference's model (h3/htrc_flat_runner.py:61-68); ``splits`` is accepted and unused."""
+    (htrc_flat_workspace_size: codes, per-chunk state, k-means scratch) for the chunk size, plus the
+    static graph copies.  Same signature as the reference's model (h3/htrc_flat_runner.py:61-68);
+    ``splits`` is accepted and unused."""
     q = int(queries) if queries else int(tile) * max(1, int(tile_chunk))
-    ws = _flat.workspace_bytes(q, int(keys), int(exact_leaves), 0, int(tile_chunk), 0)
+    ws = _flat.workspace_bytes(q, int(keys), int(exact_leaves), 0, int(tile_chunk), 0, int(group),
+                               _flat.order_code(order))
     static = (q * dim * 4 + 2 * keys * dim * 2 + q * (dim + 1) * 4) if graph else 0
     kmeans = KMEANS_MIB if order == "kmeans" else 0.0
     return (ws + static) / 2 ** 20 + kmeans
 
 
 def plan_chunk(free_bytes: int, keys: int, tile: int, splits: int = 8, order: str = "seq",
-               graph: bool = True, queries: int = 0, leaf: int = 64, exact_leaves: int = 256) -> int:
+               graph: bool = True, queries: int = 0, leaf: int = 64, exact_leaves: int = 256,
+               group: int = 1) -> int:
     """Largest tile chunk whose predicted peak fits in ``free_bytes`` (h3/htrc_flat_runner.py:71-84);
     raises MemoryError when even the smallest chunk does not fit."""
     nt = -(-int(queries) // int(tile)) if queries else 0
     for c in CHUNKS:
         eff = min(c, nt) if nt else c
         if predicted_peak_mib(keys, tile, eff, splits, leaf, order=order, graph=graph, queries=queries,
-                              exact_leaves=exact_leaves) * 2 ** 20 <= free_bytes:
+                              exact_leaves=exact_leaves, group=group) * 2 ** 20 <= free_bytes:
             return c
     need = predicted_peak_mib(keys, tile, CHUNKS[-1], splits, leaf, order=order, graph=graph, queries=queries,
-                              exact_leaves=exact_leaves)
+                              exact_leaves=exact_leaves, group=group)
     raise MemoryError(f"flat HTRC needs ~{need:.0f} MiB at the smallest chunk, {int(free_bytes) >> 20} MiB free")
 
 
@@ -83,17 +86,20 @@ class FlatRunner:
         self.tail_rows = int(tail_rows)
         self.want_lse = bool(lse)
         self.queries, self.keys, self.dim = int(queries), int(keys), int(dim)
+        self.group = _flat.group_of(base.get("kern"))
+        self.order = _flat.order_code(base["order"])
         if tile_chunk is None:
             if free_bytes is not None:
                 tile_chunk = plan_chunk(free_bytes, keys, base["tile"], base.get("splits", 8), base["order"],
-                                        use_graph, queries=int(queries), exact_leaves=base["exact_leaves"])
+                                        use_graph, queries=int(queries), exact_leaves=base["exact_leaves"],
+                                        group=self.group)
             else:
                 tile_chunk = base["tile_chunk"]
         base["tile_chunk"] = int(tile_chunk)
         self.cfg = base
         self.predicted_mib = predicted_peak_mib(keys, base["tile"], base["tile_chunk"], base.get("splits", 8),
                                                 order=base["order"], graph=use_graph, queries=int(queries),
-                                                exact_leaves=base["exact_leaves"])
+                                                exact_leaves=base["exact_leaves"], group=self.group)
         self.ws = {}
         self.graph = None
         self.graph_error = None
@@ -137,10 +143,11 @@ class FlatRunner:
             self._so = torch.empty((self.queries, self.dim), device=dev, dtype=torch.float32)
             self._sl = torch.empty((self.queries,), device=dev, dtype=torch.float32)
             nbytes = _flat.workspace_bytes(self.queries, self.keys, c["exact_leaves"], c["sink_leaves"],
-                                           c["tile_chunk"], self.tail_rows)
+                                           c["tile_chunk"], self.tail_rows, self.group, self.order)
             self._w = torch.empty(nbytes, dtype=torch.uint8, device=dev)
             kw = dict(exact_leaves=c["exact_leaves"], sink_leaves=c["sink_leaves"], tile_chunk=c["tile_chunk"],
-                      scale=c.get("scale"), out=self._so, lse=self._sl, workspace=self._w)
+                      scale=c.get("scale"), out=self._so, lse=self._sl, workspace=self._w, group=self.group,
+                      order=self.order)
             self._capturing = True
             try:
                 side = torch.cuda.Stream()

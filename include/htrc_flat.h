@@ -13,6 +13,11 @@
  *   Tiles of `tile` = 64 query rows; nt = ceil(N / 64); the last tile is padded with repeats of the
  *   last query row.  nb = M / leaf leaves.  Per-(tile, leaf) scalars use the leaf pitch
  *   P = htrc_leaf_pitch(nb) (nb rounded up to 16).
+ *   Groups: G consecutive tiles share one expansion centre, one far-field state row and one routing
+ *   (G = 1 by default); ng = ceil(nt / G) state rows.  The per-(tile, leaf) arrays below are then
+ *   per-(group, leaf).
+ *   Order: with HTRC_ORDER_KMEANS the query rows are first reordered by a k-means permutation perm
+ *   (tile row i holds query perm[i]) and the output is written back in the caller's row order.
  */
 #ifndef HTRC_FLAT_H_
 #define HTRC_FLAT_H_
@@ -37,6 +42,7 @@ enum {
 };
 
 enum { HTRC_DTYPE_F32 = 0, HTRC_DTYPE_BF16 = 1 };
+enum { HTRC_ORDER_SEQ = 0, HTRC_ORDER_KMEANS = 1 };
 enum { HTRC_ROUND_HALF_EVEN = 0, HTRC_ROUND_HALF_AWAY = 1 };
 
 /* Device status bits (htrc_flat_status). */
@@ -70,6 +76,10 @@ typedef struct HtrcFlatArgs {
    * Points past n_stage_events are not recorded. */
   void* const* stage_events;
   int32_t n_stage_events;
+  int32_t group;           /* G consecutive tiles share one centre, state and routing (<= 1: one tile;
+                              the reference's kern["group"], h3/htrc_flat.py:223-231) */
+  int32_t order;           /* HTRC_ORDER_SEQ, or HTRC_ORDER_KMEANS: query rows grouped by a k-means
+                              permutation first (order="kmeans", h3/htrc_flat.py:47-65, :146-147) */
 } HtrcFlatArgs;
 
 /* nb rounded up to a multiple of 16: the row pitch of the per-(tile, leaf) scalar arrays. */
@@ -81,8 +91,9 @@ int htrc_flat_workspace_size(const HtrcFlatArgs* args, size_t* bytes);
 /* The whole operator for one head: INT8 key pack, tile centres and query codes, leaf statistics,
  * row-max selection, top-E routing, far field + near field + tail, normalised output and log-Z.
  * Replaces flat_attention(q, k, v, backend="triton", store="int8", dot="bf16", select="max",
- * tile=64, leaf=64, exact_leaves=E, sink_leaves=S, tail=(tk, tv)) of the reference
- * (h3/htrc_flat.py:99-124 -> _flat_triton :181-276), plus the log-Z output the reference lacks. */
+ * tile=64, leaf=64, exact_leaves=E, sink_leaves=S, tail=(tk, tv), order="seq"|"kmeans",
+ * kern={"group": G}) of the reference (h3/htrc_flat.py:99-124 -> _flat_triton :181-276), plus the
+ * log-Z output the reference lacks. */
 int htrc_flat_forward(const HtrcFlatArgs* args, htrc_stream_t stream);
 
 /* Read back (synchronously) and clear the device status word inside `workspace`. */
@@ -96,43 +107,63 @@ int htrc_flat_status(void* workspace, int32_t* status_out, htrc_stream_t stream)
 int htrc_pack_int8(const void* x, int32_t dtype, int64_t rows, int32_t dim, int32_t rounding, int8_t* x8,
                    float* scale, htrc_stream_t stream);
 
-/* Tile centres and query codes (h3/htrc_flat.py:142-156 `_tiles`; h3/htrc_flat_triton.py:103-117):
- * mu [nt, dim] f32 (mean of the real rows, float64 sum rounded once); mu_hi/mu_lo [nt, dim] bf16 with
- * mu_hi = bf16(mu), mu_lo = bf16(mu - mu_hi);
- * q8/dq8 [nt*64, dim] int8 and sq/sdq [nt*64] f32: half-away codes of q and of q - mu. */
-int htrc_tile_prep(const void* q, int32_t q_dtype, int64_t n_queries, int32_t dim, int32_t tile, float* mu,
-                   uint16_t* mu_hi, uint16_t* mu_lo, int8_t* q8, float* sq, int8_t* dq8, float* sdq,
-                   htrc_stream_t stream);
+/* Tile centres and query codes (h3/htrc_flat.py:142-156 `_tiles`, :223-231 groups;
+ * h3/htrc_flat_triton.py:103-117):
+ * mu [ng, dim] f32; group 1: the mean of the tile's real rows; group G > 1: the mean of all G*64 rows of
+ * the group, the last tile's padding rows and the repeats of the last tile that fill the last group
+ * included (float64 sum rounded once); mu_hi/mu_lo [ng, dim] bf16 with mu_hi = bf16(mu),
+ * mu_lo = bf16(mu - mu_hi);
+ * q8/dq8 [nt*64, dim] int8 and sq/sdq [nt*64] f32: half-away codes of q and of q - mu[tile / G].
+ * perm: NULL, or [n_queries] int32 (tile row i reads query row perm[i]). */
+int htrc_tile_prep(const void* q, int32_t q_dtype, int64_t n_queries, int32_t dim, int32_t tile, const int32_t* perm,
+                   int32_t group, float* mu, uint16_t* mu_hi, uint16_t* mu_lo, int8_t* q8, float* sq, int8_t* dq8,
+                   float* sdq, htrc_stream_t stream);
 
-/* Leaf statistics of tiles [t0, t0 + tc) (h3/htrc_flat_triton.py:41-85 `_stats_kernel`, I8 store):
+/* k-means query order (h3/htrc_flat.py:47-65 `kmeans_order`: 32 clusters, Lloyd's iterations x 8 on
+ * the rows round(linspace(0, N-1, min(4096, N))) seeded with sample rows round(linspace(0, S-1, 32)),
+ * then the nearest centre of every row and a stable sort of the rows by centre): perm [n_queries]
+ * int32.  Distances are exact float32 sums of squared differences (the reference's torch.cdist expands
+ * |x|^2 - 2 x.c + |c|^2), ties go to the lower centre.  scratch: htrc_kmeans_scratch_size() bytes,
+ * 256-byte aligned. */
+int htrc_kmeans_scratch_size(int64_t n_queries, size_t* bytes);
+int htrc_kmeans_order(const void* q, int32_t q_dtype, int64_t n_queries, int32_t dim, int32_t* perm, void* scratch,
+                      size_t scratch_bytes, htrc_stream_t stream);
+
+/* Leaf statistics of centre rows [t0, t0 + tc) (h3/htrc_flat_triton.py:41-85 `_stats_kernel`, I8 store):
  * g8 [tc, nb, dim] int8 and sg/lz [tc, P] f32, vb [tc, nb, dim] bf16.  mu_hi/mu_lo as written by
- * htrc_tile_prep (all nt tiles); status: device int32 word or NULL. */
+ * htrc_tile_prep (all nt centre rows: tiles, or groups of tiles); status: device int32 word or NULL. */
 int htrc_leaf_stats(const uint16_t* mu_hi, const uint16_t* mu_lo, int64_t nt, int64_t t0, int64_t tc,
                     const uint16_t* k, const uint16_t* v, int64_t n_keys, int32_t dim, int32_t leaf, float scale,
                     int8_t* g8, float* sg, float* lz, uint16_t* vb, int32_t* status, htrc_stream_t stream);
 
 /* Row-max selection sel [tc, P] f32 of tiles [t0, t0 + tc) (h3/htrc_flat_triton.py:214-254
- * `_rowmax_kernel`, I8): sel[t, l] = max_r (dq8_r . g8_l) * (sdq_r * sg_l) + lz_l over the 64 rows. */
-int htrc_rowmax_select(const int8_t* dq8, const float* sdq, int64_t t0, int64_t tc, const int8_t* g8,
+ * `_rowmax_kernel`, I8): sel[t, l] = max_r (dq8_r . g8_l) * (sdq_r * sg_l) + lz_l over the tile's 64
+ * rows, with the state row (t - t0) / group of g8/sg/lz (t0 a multiple of group).  The maximum over a
+ * group's tiles is taken by htrc_route. */
+int htrc_rowmax_select(const int8_t* dq8, const float* sdq, int64_t t0, int64_t tc, int32_t group, const int8_t* g8,
                        const float* sg, const float* lz, int64_t nb, int32_t dim, float* sel, int32_t* status,
                        htrc_stream_t stream);
 
-/* Top-E routing of tiles [0, tc) (h3/htrc_flat.py:250-265): the first sink_leaves leaves are forced,
- * then the largest sel; kx = min(exact_leaves + sink_leaves, nb).  idx [tc, kx] int32 in ascending
- * leaf order (ties broken towards the lower leaf index); excl [tc, P] uint8 (1 = routed). */
-int htrc_route(const float* sel, int64_t tc, int64_t nb, int32_t exact_leaves, int32_t sink_leaves, int32_t* idx,
-               uint8_t* excl, htrc_stream_t stream);
+/* Top-E routing of the groups of tiles [0, tc) (h3/htrc_flat.py:250-265): a group's selection is the
+ * maximum of its tiles' sel rows (the reference's row-max over all G*64 rows); the first sink_leaves
+ * leaves are forced, then the largest; kx = min(exact_leaves + sink_leaves, nb).  idx [ceil(tc/G), kx]
+ * int32 in ascending leaf order (ties broken towards the lower leaf index); excl [ceil(tc/G), P] uint8
+ * (1 = routed). */
+int htrc_route(const float* sel, int64_t tc, int64_t nb, int32_t exact_leaves, int32_t sink_leaves, int32_t group,
+               int32_t* idx, uint8_t* excl, htrc_stream_t stream);
 
 /* Far field + near field (+ tail partial) of tiles [t0, t0 + tc) merged into out/lse rows
  * [t0*64, min(n_queries, (t0+tc)*64)) (h3/htrc_flat_triton.py:88-211 `_tile_kernel` with I8=1,
- * merged as :257-273).  State arrays as produced by the stages above; k8/ks from htrc_pack_int8
- * (half-even) of k; tail_part: NULL or [n_queries, dim + 2] f32 rows (acc, m, l) from the tail. */
+ * merged as :257-273).  State arrays as produced by the stages above (state row (t - t0) / group; t0 a
+ * multiple of group); k8/ks from htrc_pack_int8 (half-even) of k; tail_part: NULL or
+ * [n_queries, dim + 2] f32 rows (acc, m, l) from the tail, in the caller's row order; perm: NULL, or the
+ * permutation given to htrc_tile_prep (tile row i is written to out/lse row perm[i]). */
 int htrc_tile_attention(const int8_t* q8, const float* sq, const int8_t* dq8, const float* sdq, int64_t n_queries,
-                        int64_t t0, int64_t tc, const int8_t* g8, const float* sg, const float* lz,
+                        int64_t t0, int64_t tc, int32_t group, const int8_t* g8, const float* sg, const float* lz,
                         const uint16_t* vb, const uint8_t* excl, const int32_t* idx, int32_t kx, int64_t nb,
                         const int8_t* k8, const float* ks, const uint16_t* v, int64_t n_keys, int32_t dim,
-                        int32_t leaf, float scale, const float* tail_part, float* out, float* lse, int32_t* status,
-                        htrc_stream_t stream);
+                        int32_t leaf, float scale, const float* tail_part, const int32_t* perm, float* out, float* lse,
+                        int32_t* status, htrc_stream_t stream);
 
 /* Exact softmax partial of every query row against the tail keys (h3/htrc_flat_triton.py:187-207 for
  * n_tail <= 16 with bf16 operands; :381-388 float32 for longer tails): tail_part [N, dim + 2]. */

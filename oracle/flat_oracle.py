@@ -9,7 +9,9 @@ It restates, step by step, the arithmetic of the reference operator
 dot="bf16", select="max", curvature="lin"``:
 
   K INT8 pack ............ h3/htrc_flat.py:213-219       (round-half-even, IEEE divide by the scale)
+  k-means query order .... h3/htrc_flat.py:47-65         (order="kmeans": Lloyd on a sample, stable sort)
   tile centres ........... h3/htrc_flat.py:142-156       (mean over the tile's real rows)
+  group centres .......... h3/htrc_flat.py:223-231       (kern group G: mean over G padded tiles)
   leaf statistics ........ h3/htrc_flat_triton.py:41-85  (lz, g -> g8/sg half-away, vbar -> bf16)
   row-max selection ...... h3/htrc_flat_triton.py:214-254 (dq8 . g8 * sdq * sg, max over rows, + lz)
   top-E routing .......... h3/htrc_flat.py:232-265       (sink leaves forced, topk, exclusion mask)
@@ -95,6 +97,67 @@ def pack_slope(g):
 
 
 # ----------------------------------------------------------------------------- stages
+def linspace_f32(hi, steps):
+    """torch.linspace(0, hi, steps) in float32 on the CPU: step = hi / (steps - 1) in float32, the first
+    half step * i, the second half hi - step * (steps - 1 - i) rounded once (checked against
+    torch.linspace in tests/test_oracle.py)."""
+    if steps <= 1:
+        return np.zeros(max(steps, 0), F32)
+    step = F32(F32(hi) / F32(steps - 1))
+    i = np.arange(steps)
+    up = (np.float64(step) * i).astype(F32)
+    dn = (np.float64(F32(hi)) - np.float64(step) * (steps - 1 - i)).astype(F32)
+    return np.where(i < steps // 2, up, dn).astype(F32)
+
+
+def _round_index(x):
+    """torch's .round().long(): half to even."""
+    return np.rint(x.astype(np.float64)).astype(np.int64)
+
+
+def _nearest(x, c):
+    """Index of the nearest centre per row (first minimum), distances in float64."""
+    x = np.asarray(x, np.float64)
+    c = np.asarray(c, np.float64)
+    d = (x * x).sum(1)[:, None] - 2.0 * (x @ c.T) + (c * c).sum(1)[None, :]
+    return d.argmin(1)
+
+
+def kmeans_order(q, clusters=32, sample=4096, iters=8, return_labels=False):
+    """Permutation grouping queries by k-means (h3/htrc_flat.py:47-65): Lloyd's iterations on the
+    rows round(linspace(0, n-1, min(sample, n))), seeded with the sample rows
+    round(linspace(0, S-1, clusters)); an empty cluster keeps its centre; then every row's nearest
+    centre and a stable sort by it.  Distances here are float64 (the reference's torch.cdist works in
+    float32 through |x|^2 - 2 x.c + |c|^2), so assignments can differ at near-ties only."""
+    x = np.asarray(q, dtype=F32)
+    n = x.shape[0]
+    sidx = _round_index(linspace_f32(n - 1, min(sample, n)))
+    s = x[sidx]
+    c = s[_round_index(linspace_f32(s.shape[0] - 1, clusters))].copy()
+    for _ in range(iters):
+        a = _nearest(s, c)
+        sums = np.zeros((clusters, x.shape[1]), np.float64)
+        np.add.at(sums, a, s.astype(np.float64))
+        cnt = np.bincount(a, minlength=clusters)
+        nz = cnt > 0
+        c[nz] = (sums[nz] / cnt[nz][:, None]).astype(F32)
+    assign = _nearest(x, c)
+    perm = np.argsort(assign, kind="stable").astype(np.int64)
+    return (perm, assign) if return_labels else perm
+
+
+def group_centres(qt, group):
+    """Centres of groups of `group` consecutive tiles (h3/htrc_flat.py:223-231): the tiles are padded
+    with repeats of the last tile to a multiple of the group and each centre is the mean of all
+    group * T rows (the last tile's padding rows included); float64 mean rounded once."""
+    qt = np.asarray(qt, dtype=F32)
+    nt, t, d = qt.shape
+    ntp = -(-nt // group) * group
+    if ntp > nt:
+        qt = np.concatenate([qt, np.repeat(qt[-1:], ntp - nt, 0)], 0)
+    return qt.reshape(ntp // group, group * t, d).astype(np.float64).mean(1).astype(F32)
+
+
 def tile_centres(q, tile):
     """(qt float32 [nt, T, D], mu float32 [nt, D], n) with the last tile padded by repeats of the
     last row and its centre taken over its real rows (h3/htrc_flat.py:142-156).  The mean is
@@ -150,11 +213,19 @@ def query_codes(qt, mu):
     return q8, sq, dq8, sdq
 
 
-def rowmax_select(dq8, sdq, g8, sg, lz):
-    """SEL[t, l] = max_r (dq8_r . g8_l) * (sdq_r * sg_l) + lz_l (h3/htrc_flat_triton.py:240-254)."""
-    dot = np.matmul(dq8.astype(np.float64), np.swapaxes(g8.astype(np.float64), 1, 2))
-    sc = dot.astype(F32) * (sdq[:, :, None] * sg[:, None, :]).astype(F32)
-    return (sc.max(1) + lz).astype(F32)
+def rowmax_select(dq8, sdq, g8, sg, lz, group=1):
+    """SEL[t, l] = max_r (dq8_r . g8_l) * (sdq_r * sg_l) + lz_l (h3/htrc_flat_triton.py:240-254); with
+    groups the rows are all G * T rows of a group (the reference calls the kernel with
+    T = G * tile, h3/htrc_flat.py:243-249) and the state row is the group's: returns [ng, nb]."""
+    nt = dq8.shape[0]
+    st = np.arange(nt) // group
+    dot = np.matmul(dq8.astype(np.float64), np.swapaxes(g8[st].astype(np.float64), 1, 2))
+    sc = dot.astype(F32) * (sdq[:, :, None] * sg[st][:, None, :]).astype(F32)
+    per_tile = (sc.max(1) + lz[st]).astype(F32)
+    ng = -(-nt // group)
+    out = np.full((ng, per_tile.shape[1]), -np.inf, F32)
+    np.maximum.at(out, st, per_tile)
+    return out
 
 
 def route(sel, exact_leaves, sink_leaves=0):
@@ -179,7 +250,7 @@ def route(sel, exact_leaves, sink_leaves=0):
 
 
 def tile_attention(qt, q8, sq, dq8, sdq, g8, sg, lz, vb, excl, idx, k8, ks, v, leaf, scale,
-                   tail=None):
+                   tail=None, group=1):
     """Far field + near field + tail of every tile, merged; returns (out float32 [nt*T, D],
     lse float32 [nt*T]) (h3/htrc_flat_triton.py:88-211, merge :257-273).
 
@@ -188,7 +259,8 @@ def tile_attention(qt, q8, sq, dq8, sdq, g8, sg, lz, vb, excl, idx, k8, ks, v, l
     tail : logit = bf16(q) . bf16(tk_j) * scale (<= 16 keys) or the float32 product (> 16 keys),
            value tv_j (h3/htrc_flat_triton.py:187-207, :381-388)
     P is rounded to bfloat16 for the value product (not for a > 16-key tail, whose partial the
-    reference forms in float32 on the host); the normaliser sums float32 P."""
+    reference forms in float32 on the host); the normaliser sums float32 P.  Tile t uses the state,
+    exclusion and routing rows of its group t // group (h3/htrc_flat_triton.py:102)."""
     nt, T, d = qt.shape
     nb = lz.shape[1]
     v = np.asarray(v, dtype=F32)
@@ -204,16 +276,17 @@ def tile_attention(qt, q8, sq, dq8, sdq, g8, sg, lz, vb, excl, idx, k8, ks, v, l
     else:
         tk = tv = None
     for t in range(nt):
+        gt = t // group
         parts_s, parts_v, parts_r = [], [], []
-        keep = excl[t] == 0
+        keep = excl[gt] == 0
         if keep.any():
-            dot = dq8[t].astype(np.float64) @ g8[t][keep].astype(np.float64).T
-            sc = dot.astype(F32) * (sdq[t][:, None] * sg[t][keep][None, :]).astype(F32) + lz[t][keep][None, :]
+            dot = dq8[t].astype(np.float64) @ g8[gt][keep].astype(np.float64).T
+            sc = dot.astype(F32) * (sdq[t][:, None] * sg[gt][keep][None, :]).astype(F32) + lz[gt][keep][None, :]
             parts_s.append(sc.astype(F32))
-            parts_v.append(vb[t][keep])
+            parts_v.append(vb[gt][keep])
             parts_r.append(np.ones(sc.shape[1], bool))
         if idx.shape[1]:
-            tok = (idx[t][:, None].astype(np.int64) * leaf + ar[None, :]).reshape(-1)
+            tok = (idx[gt][:, None].astype(np.int64) * leaf + ar[None, :]).reshape(-1)
             dot = q8[t].astype(np.float64) @ k8[tok].astype(np.float64).T
             sc = dot.astype(F32) * ((sq[t][:, None] * ks[tok][None, :]).astype(F32) * F32(scale)).astype(F32)
             parts_s.append(sc.astype(F32))
@@ -247,7 +320,7 @@ def _split(n, ns, bn):
 
 
 def tile_attention_ordered(qt, q8, sq, dq8, sdq, g8, sg, lz, vb, excl, idx, k8, ks, v, leaf, scale,
-                           tail=None, splits=4, bn=64):
+                           tail=None, splits=4, bn=64, group=1):
     """Same operator evaluated in the reference kernel's exact order: ``splits`` split programs per
     tile, blocks of ``bn`` leaves / tokens, float32 online softmax with P rounded to bfloat16
     against the running maximum, then the split merge (h3/htrc_flat_triton.py:118-211, :257-273).
@@ -278,6 +351,7 @@ def tile_attention_ordered(qt, q8, sq, dq8, sdq, g8, sg, lz, vb, excl, idx, k8, 
         return mn, l, acc
 
     for t in range(nt):
+        gt = t // group
         pms, pls, paccs = [], [], []
         for sp in range(splits):
             m = np.full(T, -np.inf, F32)
@@ -286,14 +360,14 @@ def tile_attention_ordered(qt, q8, sq, dq8, sdq, g8, sg, lz, vb, excl, idx, k8, 
             lo, hi = sp * lps, min(nb, sp * lps + lps)
             for n0 in range(lo, hi, bn):
                 c = np.arange(n0, min(n0 + bn, hi))
-                dot = dq8[t].astype(np.int32) @ g8[t][c].astype(np.int32).T
-                sc = (dot.astype(F32) * (sdq[t][:, None] * sg[t][c][None, :]).astype(F32) + lz[t][c][None, :]).astype(F32)
-                sc = np.where((excl[t][c] == 0)[None, :], sc, F32(-np.inf))
-                m, l, acc = step(m, l, acc, sc, vb[t][c])
+                dot = dq8[t].astype(np.int32) @ g8[gt][c].astype(np.int32).T
+                sc = (dot.astype(F32) * (sdq[t][:, None] * sg[gt][c][None, :]).astype(F32) + lz[gt][c][None, :]).astype(F32)
+                sc = np.where((excl[gt][c] == 0)[None, :], sc, F32(-np.inf))
+                m, l, acc = step(m, l, acc, sc, vb[gt][c])
             e_lo, e_hi = sp * eps, min(e_n, sp * eps + eps)
             for e0 in range(e_lo, e_hi, bn):
                 j = np.arange(e0, min(e0 + bn, e_hi))
-                tok = idx[t][j // leaf].astype(np.int64) * leaf + j % leaf
+                tok = idx[gt][j // leaf].astype(np.int64) * leaf + j % leaf
                 dot = q8[t].astype(np.int32) @ k8[tok].astype(np.int32).T
                 sc = (dot.astype(F32) * ((sq[t][:, None] * ks[tok][None, :]).astype(F32) * scale)).astype(F32)
                 m, l, acc = step(m, l, acc, sc, v[tok])
@@ -327,11 +401,21 @@ def pack_k(k):
 
 
 def flat_attention(q, k, v, *, tile=64, exact_leaves=256, leaf=64, scale=None, sink_leaves=0,
-                   tail=None, return_stages=False):
+                   tail=None, return_stages=False, group=1, order="seq", perm=None):
     """The whole production path for one head: q [N, D], k/v [M, D] (float32 arrays holding the
     caller's values; k and v are rounded to bfloat16 as the reference's bf16 path stores them).
+    group: G tiles per centre (kern["group"]); order "kmeans" permutes the queries first (``perm``
+    overrides the permutation, e.g. with the device's, to check the stages after it).
     Returns (out float32 [N, D], lse float32 [N]) and, with return_stages, a dict of every stage."""
     q = np.asarray(q, dtype=F32)
+    group = max(1, int(group))
+    if order == "kmeans" and perm is None:
+        perm = kmeans_order(q)
+    if order != "kmeans":
+        perm = None
+    q_caller = q
+    if perm is not None:
+        q = q[np.asarray(perm, np.int64)]
     k = bf16_round(np.asarray(k, dtype=F32))
     v = bf16_round(np.asarray(v, dtype=F32))
     n, d = q.shape
@@ -341,24 +425,30 @@ def flat_attention(q, k, v, *, tile=64, exact_leaves=256, leaf=64, scale=None, s
     scale = 1.0 / math.sqrt(d) if scale is None else float(scale)
     k8, ks = pack_rows_half_even(k)
     qt, mu, _ = tile_centres(q, tile)
+    if group > 1:
+        mu = group_centres(qt, group)
     g, lz, vbf = leaf_stats(mu, k, v, leaf, scale)
     g8, sg, vb = state_int8(g, vbf)
-    q8, sq, dq8, sdq = query_codes(qt, mu)
+    q8, sq, dq8, sdq = query_codes(qt, mu[np.arange(qt.shape[0]) // group])
     nb = m // leaf
     sink = max(0, min(int(sink_leaves), nb))
     kx = min(int(exact_leaves) + sink, nb)
     if kx > 0:
-        sel = rowmax_select(dq8, sdq, g8, sg, lz)
+        sel = rowmax_select(dq8, sdq, g8, sg, lz, group)
     else:
-        sel = np.zeros((qt.shape[0], nb), F32)
+        sel = np.zeros((mu.shape[0], nb), F32)
     idx, excl = route(sel, exact_leaves, sink)
     out, lse = tile_attention(qt, q8, sq, dq8, sdq, g8, sg, lz, vb, excl, idx, k8, ks, v, leaf,
-                              scale, tail=tail)
+                              scale, tail=tail, group=group)
     out, lse = out[:n], lse[:n]
+    if perm is not None:
+        full, full_l = np.empty_like(out), np.empty_like(lse)
+        full[perm], full_l[perm] = out, lse
+        out, lse = full, full_l
     if not return_stages:
         return out, lse
     return out, lse, dict(k8=k8, ks=ks, qt=qt, mu=mu, g=g, g8=g8, sg=sg, lz=lz, vb=vb, q8=q8,
-                          sq=sq, dq8=dq8, sdq=sdq, sel=sel, idx=idx, excl=excl)
+                          sq=sq, dq8=dq8, sdq=sdq, sel=sel, idx=idx, excl=excl, perm=perm, q=q_caller)
 
 
 def prepare_head(q, k, v, *, tile=64, leaf=64):

@@ -3,7 +3,7 @@
 Run once, in a container that has the reference checkout (default ``/root/reference``; override
 with ``HTRC_REFERENCE``):
 
-    TRITON_INTERPRET=1 python tests/golden/make_golden.py
+    TRITON_INTERPRET=1 python tests/golden/make_golden.py [case ...]
 
 It imports the reference's ``h3/htrc_flat.py`` unmodified and calls
 ``flat_attention(q, k, v, **PROD, leaf=L, exact_leaves=E, ...)`` on CPU tensors with Triton's
@@ -87,9 +87,17 @@ def _load_reference():
 
 
 def _recorder(flat):
-    """Wrap the reference's kernel wrappers to record what flows between them."""
+    """Wrap the reference's kernel wrappers (and its k-means order) to record what flows between them."""
     tri = flat._load_triton()
-    rec = {"stats": [], "sel": [], "tile": []}
+    rec = {"stats": [], "sel": [], "tile": [], "perm": []}
+    o_km = flat.kmeans_order
+
+    def kmeans_order(q, *a, **kw):
+        perm = o_km(q, *a, **kw)
+        rec["perm"].append(perm.clone())
+        return perm
+
+    flat.kmeans_order = kmeans_order
     o_stats, o_sel, o_tile = tri.leaf_stats, tri.rowmax_select, tri.tile_attention
 
     def leaf_stats(mu, kf, vf, nb, scale, **kw):
@@ -132,6 +140,14 @@ CASES = [
     dict(name="big_tail", grid=(2, 16, 16), leaf=64, E=2, sink=0, tail=20, trim=0, seed=16),
     dict(name="leaf32", grid=(2, 16, 16), leaf=32, E=4, sink=0, tail=0, trim=0, seed=17),
     dict(name="wide", grid=(4, 16, 32), leaf=64, E=4, sink=0, tail=0, trim=0, seed=18),
+    # groups of tiles sharing one centre (kern group) and the k-means query order (order="kmeans")
+    dict(name="group2", grid=(2, 16, 16), leaf=64, E=2, sink=0, tail=0, trim=37, seed=19, group=2),
+    dict(name="group4", grid=(2, 16, 20), leaf=64, E=2, sink=1, tail=0, trim=0, seed=20, group=4),
+    dict(name="kmeans", grid=(2, 16, 16), leaf=64, E=2, sink=0, tail=0, trim=21, seed=21, order="kmeans"),
+    dict(name="kmeans_g2_tail", grid=(2, 16, 16), leaf=64, E=2, sink=0, tail=5, trim=0, seed=22, order="kmeans",
+         group=2),
+    dict(name="kmeans_sampled", grid=(4, 32, 33), leaf=64, E=4, sink=0, tail=0, trim=67, seed=23, order="kmeans",
+         slim=True, keys=1024),
 ]
 
 
@@ -146,15 +162,21 @@ def run_case(flat, c):
         k, v = k[:keep].contiguous(), v[:keep].contiguous()
     if c["trim"]:
         q = q[: -c["trim"]].contiguous()
+    if c.get("keys"):
+        k, v = k[: c["keys"]].contiguous(), v[: c["keys"]].contiguous()
     rec = _recorder(flat)
     ws = {}
     cfg = dict(flat.PROD)
-    cfg.update(leaf=c["leaf"], exact_leaves=c["E"], sink_leaves=c["sink"], tile_chunk=4096)
+    cfg.update(leaf=c["leaf"], exact_leaves=c["E"], sink_leaves=c["sink"], tile_chunk=4096,
+               order=c.get("order", "seq"))
+    if c.get("group", 1) > 1:
+        cfg["kern"] = {**cfg["kern"], "group": c["group"]}
     out = flat.flat_attention(q, k, v, tail=(tk, tv) if tk is not None else None, ws=ws, **cfg)
     st = rec["stats"]
     ti = rec["tile"]
     res = dict(q=q.float().numpy(), k=k.float().numpy(), v=v.float().numpy(),
                leaf=np.int64(c["leaf"]), exact_leaves=np.int64(c["E"]), sink_leaves=np.int64(c["sink"]),
+               group=np.int64(c.get("group", 1)),
                mu=_cat(st, "mu").numpy(), g8=_cat(st, "g8").numpy(), sg=_cat(st, "sg").numpy(),
                lz=_cat(st, "lz").numpy(), vb=_cat(st, "vb").float().numpy(),
                excl=_cat(ti, "excl").numpy().astype(np.uint8), k8=ti[0]["k8"].numpy(),
@@ -167,9 +189,23 @@ def run_case(flat, c):
         pm, pl = _cat(ti, "pm").double(), _cat(ti, "pl").double()
         mm = pm.amax(1, keepdim=True)
         lse = (mm[:, 0] + torch.log((pl * torch.exp(pm - mm)).sum(1))).float()
-        res["lse"] = lse.reshape(-1)[: q.shape[0]].numpy()
+        lse = lse.reshape(-1)[: q.shape[0]]
+        if rec["perm"]:                            # tile order -> the caller's row order
+            full = torch.empty_like(lse)
+            full[rec["perm"][0]] = lse
+            lse = full
+        res["lse"] = lse.numpy()
     if tk is not None:
         res["tail_k"], res["tail_v"] = tk.numpy(), tv.numpy()
+    if rec["perm"]:
+        res["perm"] = rec["perm"][0].numpy().astype(np.int64)
+    if c.get("slim"):
+        # large case: inputs as bfloat16 bit patterns, no per-(tile, leaf) state (the tests recompute it)
+        for name, t in (("q", q), ("k", k), ("v", v)):
+            res.pop(name)
+            res[name + "16"] = t.to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+        for name in ("g8", "vb", "sg", "lz", "sel", "k8"):
+            res.pop(name, None)
     return res
 
 
@@ -177,11 +213,15 @@ def main():
     _shim()
     flat = _load_reference()
     torch.manual_seed(0)
+    only = set(sys.argv[1:])
     for c in CASES:
+        if only and c["name"] not in only:
+            continue
         res = run_case(flat, c)
         path = HERE / f"{c['name']}.npz"
         np.savez_compressed(path, **res)
-        print(f"{c['name']}: q{tuple(res['q'].shape)} k{tuple(res['k'].shape)} -> {path.name}")
+        qs, ks = res.get("q", res.get("q16")).shape, res.get("k", res.get("k16")).shape
+        print(f"{c['name']}: q{tuple(qs)} k{tuple(ks)} -> {path.name}")
 
 
 if __name__ == "__main__":

@@ -143,7 +143,7 @@ def test_route_sink_and_ties(dev):
         kx = min(E + sink, nb)
         idx = torch.full((3, max(kx, 1)), -1, dtype=torch.int32, device=dev)
         excl = torch.full((3, pitch), 9, dtype=torch.uint8, device=dev)
-        _lib.check(lib().htrc_route(ptr(sel.to(dev)), 3, nb, E, sink, ptr(idx), ptr(excl), stream_ptr()), "route")
+        _lib.check(lib().htrc_route(ptr(sel.to(dev)), 3, nb, E, sink, 1, ptr(idx), ptr(excl), stream_ptr()), "route")
         torch.cuda.synchronize()
         ridx, rex = O.route(sel[:, :nb].numpy(), E, sink)
         assert np.array_equal(excl.cpu().numpy()[:, :nb], rex), (E, sink)

@@ -132,14 +132,51 @@ def test_flat_attention_argument_errors_match_the_reference():
 def test_flat_attention_unimplemented_configurations_say_so():
     q, k, v = _qkv()
     cfg = dict(htrc_b200.PROD, leaf=64)
-    with pytest.raises(NotImplementedError, match="kmeans"):
-        htrc_b200.flat_attention(q, k, v, **{**cfg, "order": "kmeans"})
+    with pytest.raises(NotImplementedError, match="tile=64"):
+        htrc_b200.flat_attention(q, k, v, **{**cfg, "order": "kmeans", "tile": 32})   # the "max" mode
     with pytest.raises(NotImplementedError, match="leaf"):
         htrc_b200.flat_attention(q, k, v, **{**cfg, "leaf": 32})
     with pytest.raises(NotImplementedError):
         htrc_b200.flat_attention(q, k, v, **{**cfg, "store": "bf16"})
     with pytest.raises(NotImplementedError):
         htrc_b200.flat_attention(q, k, v, **{**cfg, "backend": "torch"})
+
+
+def test_orders_and_groups_need_no_cpu_path_either():
+    q, k, v = _qkv()
+    cfg = dict(htrc_b200.PROD, leaf=64)
+    for over in ({"order": "kmeans"}, {"kern": {"group": 2}}, {"order": "kmeans", "kern": {"group": 4}}):
+        with pytest.raises(ValueError, match="CUDA tensors"):
+            htrc_b200.flat_attention(q, k, v, **{**cfg, **over})
+
+
+def test_group_and_order_validation_and_workspace():
+    L = _lib.lib()
+    nbytes = ctypes.c_size_t()
+    a = _args(n=65536, m=65536, E=256, chunk=64)
+    assert L.htrc_flat_workspace_size(ctypes.byref(a), ctypes.byref(nbytes)) == _lib.HTRC_OK
+    base = nbytes.value
+    a.group = 2                                     # half the centre rows: less far-field state per chunk
+    assert L.htrc_flat_workspace_size(ctypes.byref(a), ctypes.byref(nbytes)) == _lib.HTRC_OK
+    assert nbytes.value < base
+    a.group, a.order = 1, _lib.ORDER_KMEANS         # the permutation and the k-means scratch
+    assert L.htrc_flat_workspace_size(ctypes.byref(a), ctypes.byref(nbytes)) == _lib.HTRC_OK
+    km = ctypes.c_size_t()
+    assert L.htrc_kmeans_scratch_size(65536, ctypes.byref(km)) == _lib.HTRC_OK
+    assert nbytes.value >= base + km.value + 65536 * 4
+    a.order = 7
+    assert L.htrc_flat_workspace_size(ctypes.byref(a), ctypes.byref(nbytes)) == _lib.HTRC_ERR_ARG
+    a.order, a.group = 0, 1 << 20
+    assert L.htrc_flat_workspace_size(ctypes.byref(a), ctypes.byref(nbytes)) == _lib.HTRC_ERR_ARG
+    assert L.htrc_kmeans_scratch_size(0, ctypes.byref(km)) == _lib.HTRC_ERR_ARG
+    assert L.htrc_kmeans_order(None, 0, 16, 128, None, None, 0, None) == _lib.HTRC_ERR_ARG
+
+
+def test_group_and_order_of_the_reference_arguments():
+    assert F.group_of(None) == 1 and F.group_of({}) == 1 and F.group_of({"group": 0}) == 1
+    assert F.group_of({"group": 4, "tile_bn": 64}) == 4
+    assert F.order_code("kmeans") == _lib.ORDER_KMEANS
+    assert F.order_code("seq") == _lib.ORDER_SEQ and F.order_code("other") == _lib.ORDER_SEQ
 
 
 def test_flat_attention_has_no_cpu_path():

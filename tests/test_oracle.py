@@ -5,17 +5,33 @@ import pytest
 
 from oracle import flat_oracle as O
 
-CASES = ["base", "ragged", "sink_tail", "all_exact", "no_exact", "big_tail", "leaf32", "wide"]
+CASES = ["base", "ragged", "sink_tail", "all_exact", "no_exact", "big_tail", "leaf32", "wide",
+         "group2", "group4", "kmeans", "kmeans_g2_tail", "kmeans_sampled"]
+SLIM = {"kmeans_sampled"}                      # no recorded per-(tile, leaf) state
+STATE_CASES = [c for c in CASES if c not in SLIM]
+KMEANS_CASES = ["kmeans", "kmeans_g2_tail", "kmeans_sampled"]
+
+
+def _group(z):
+    return int(z["group"]) if "group" in z else 1
 
 
 def _stages(z):
+    """The oracle on a fixture's inputs; a k-means case uses the reference's recorded permutation
+    (the oracle's own is checked separately)."""
     tail = (z["tail_k"], z["tail_v"]) if "tail_k" in z else None
+    order = "kmeans" if "perm" in z else "seq"
     return O.flat_attention(z["q"], z["k"], z["v"], leaf=int(z["leaf"]),
                             exact_leaves=int(z["exact_leaves"]), sink_leaves=int(z["sink_leaves"]),
-                            tail=tail, return_stages=True), tail
+                            tail=tail, return_stages=True, group=_group(z), order=order,
+                            perm=z.get("perm")), tail
 
 
-@pytest.mark.parametrize("case", CASES)
+def _tile_mu(z, nt):
+    return z["mu"][np.arange(nt) // _group(z)]
+
+
+@pytest.mark.parametrize("case", STATE_CASES)
 def test_key_pack_bit_exact(golden_cases, case):
     z = golden_cases[case]
     k8, ks = O.pack_k(z["k"])
@@ -24,6 +40,15 @@ def test_key_pack_bit_exact(golden_cases, case):
 
 
 @pytest.mark.parametrize("case", CASES)
+def test_centres(golden_cases, case):
+    """Tile centres (group 1: over the real rows) and group centres (all G * 64 padded rows)."""
+    z = golden_cases[case]
+    (out, lse, st), _ = _stages(z)
+    assert st["mu"].shape == z["mu"].shape
+    assert np.abs(st["mu"] - z["mu"]).max() <= 1e-7 * max(1.0, np.abs(z["mu"]).max())
+
+
+@pytest.mark.parametrize("case", STATE_CASES)
 def test_centres_and_leaf_state(golden_cases, case):
     z = golden_cases[case]
     (out, lse, st), _ = _stages(z)
@@ -50,33 +75,38 @@ def test_slope_pack_bit_exact_on_identical_input():
     assert np.abs(g8).max() <= 127
 
 
-@pytest.mark.parametrize("case", [c for c in CASES if c != "no_exact"])
+@pytest.mark.parametrize("case", [c for c in STATE_CASES if c != "no_exact"])
 def test_rowmax_selection_and_routing(golden_cases, case):
     z = golden_cases[case]
     (out, lse, st), _ = _stages(z)
     # evaluated on the reference's own state, the selection is identical up to float32 rounding
-    q8, sq, dq8, sdq = O.query_codes(st["qt"], z["mu"])
-    sel = O.rowmax_select(dq8, sdq, z["g8"], z["sg"], z["lz"])
+    q8, sq, dq8, sdq = O.query_codes(st["qt"], _tile_mu(z, st["qt"].shape[0]))
+    sel = O.rowmax_select(dq8, sdq, z["g8"], z["sg"], z["lz"], _group(z))
     assert np.abs(sel - z["sel"]).max() < 1e-4
     assert (st["excl"] == z["excl"]).mean() >= 0.999
 
 
-@pytest.mark.parametrize("case", CASES)
+@pytest.mark.parametrize("case", STATE_CASES)
 def test_ordered_restatement_matches_reference(golden_cases, case):
     """With the reference's own state and block order, the restated online softmax reproduces the
     reference's output to float32 rounding."""
     z = golden_cases[case]
     (out, lse, st), tail = _stages(z)
-    nt = z["mu"].shape[0]
-    idx = z["idx"] if "idx" in z else np.zeros((nt, 0), np.int32)
-    q8, sq, dq8, sdq = O.query_codes(st["qt"], z["mu"])
+    ng = z["mu"].shape[0]
+    idx = z["idx"] if "idx" in z else np.zeros((ng, 0), np.int32)
+    q8, sq, dq8, sdq = O.query_codes(st["qt"], _tile_mu(z, st["qt"].shape[0]))
     o2, l2 = O.tile_attention_ordered(st["qt"], q8, sq, dq8, sdq, z["g8"], z["sg"], z["lz"], z["vb"],
                                       z["excl"], idx, z["k8"], z["ks"], O.bf16_round(z["v"]),
-                                      int(z["leaf"]), 1 / np.sqrt(128), tail=tail)
+                                      int(z["leaf"]), 1 / np.sqrt(128), tail=tail, group=_group(z))
     n = z["q"].shape[0]
-    assert np.abs(o2[:n] - z["out"]).max() < 2e-5
+    o2, l2 = o2[:n], l2[:n]
+    if "perm" in z:                                      # tile order -> the caller's row order
+        full, full_l = np.empty_like(o2), np.empty_like(l2)
+        full[z["perm"]], full_l[z["perm"]] = o2, l2
+        o2, l2 = full, full_l
+    assert np.abs(o2 - z["out"]).max() < 2e-5
     if "lse" in z:
-        assert np.abs(l2[:n] - z["lse"]).max() < 2e-5
+        assert np.abs(l2 - z["lse"]).max() < 2e-5
 
 
 @pytest.mark.parametrize("case", CASES)
@@ -103,6 +133,46 @@ def test_all_leaves_exact_is_dequantised_softmax(golden_cases):
     ref = p @ O.bf16_round(z["v"]).astype(np.float64) / p.sum(1, keepdims=True)
     assert np.abs(out - ref).max() < 1e-2
     assert np.abs(lse - (m[:, 0] + np.log(p.sum(1)))).max() < 1e-4
+
+
+@pytest.mark.parametrize("case", KMEANS_CASES)
+def test_kmeans_order_matches_reference(golden_cases, case):
+    """The restated k-means order reproduces the reference's permutation (sampled Lloyd + stable
+    sort; the last case has more rows than the 4096-row sample)."""
+    z = golden_cases[case]
+    assert np.array_equal(O.kmeans_order(z["q"]), z["perm"])
+
+
+def test_linspace_matches_torch():
+    """The float32 linspace formula behind the k-means sample and seed rows."""
+    torch = pytest.importorskip("torch")
+    for n in list(range(1, 200)) + [4095, 4096, 4097, 40759, 129024, 245952, 1000003]:
+        s = min(4096, n)
+        assert np.array_equal(O.linspace_f32(n - 1, s), torch.linspace(0, n - 1, s).numpy()), n
+        assert np.array_equal(O.linspace_f32(s - 1, 32), torch.linspace(0, s - 1, 32).numpy()), n
+
+
+def test_groups_of_three_restate_the_rule():
+    """G = 3 is outside what the reference's kernels compile for (tl.arange needs a power of two
+    rows); the oracle applies the same rule: the centre of a group is the mean of its padded tiles,
+    its selection the maximum over its tiles and every tile of a group uses one state row."""
+    rng = np.random.default_rng(3)
+    q = rng.standard_normal((7 * 64 - 5, 128)).astype(np.float32)
+    k = rng.standard_normal((512, 128)).astype(np.float32)
+    v = rng.standard_normal((512, 128)).astype(np.float32)
+    out, lse, st = O.flat_attention(q, k, v, exact_leaves=2, group=3, return_stages=True)
+    assert st["mu"].shape == (3, 128) and st["idx"].shape == (3, 2)
+    qt = st["qt"]
+    pad = np.concatenate([qt, qt[-1:], qt[-1:]], 0)             # 7 tiles -> 9 = 3 groups of 3
+    assert np.allclose(st["mu"], pad.reshape(3, 192, 128).mean(1), atol=1e-6)
+    gt = np.arange(7) // 3
+    per_tile = O.rowmax_select(st["dq8"], st["sdq"], st["g8"][gt], st["sg"][gt], st["lz"][gt])
+    for g in range(3):
+        assert np.array_equal(st["sel"][g], per_tile[3 * g:3 * g + 3].max(0))
+    # with every leaf exact the grouping of the centres does not matter
+    o3 = O.flat_attention(q, k, v, exact_leaves=99, group=3)[0]
+    o1 = O.flat_attention(q, k, v, exact_leaves=99, group=1)[0]
+    assert np.array_equal(o3, o1)
 
 
 def test_route_sink_and_ties():
