@@ -214,7 +214,7 @@ def run_ours(a, wl, rank, world, local_rank):
     out = {h: torch.empty((n, 128), dtype=torch.float32, device=dev) for h in my_heads}
     lse = {h: torch.empty((n,), dtype=torch.float32, device=dev) for h in my_heads}
     wsb = F.workspace_bytes(n, m, E, 0, 0, 0)
-    ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
+    ws = F.new_workspace(wsb, dev)
     comp = torch.cuda.current_stream(dev)
     side = torch.cuda.Stream(dev)
     gathered = None

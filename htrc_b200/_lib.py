@@ -49,8 +49,8 @@ SIGNATURES = {
     "htrc_leaf_stats": (ctypes.c_int, [_p, _p, _i64, _i64, _i64, _p, _p, _i64, _i32, _i32, _f32, _p, _p, _p, _p, _p, _p]),
     "htrc_rowmax_select": (ctypes.c_int, [_p, _p, _i64, _i64, _i32, _p, _p, _p, _i64, _i32, _p, _p, _p]),
     "htrc_route": (ctypes.c_int, [_p, _i64, _i64, _i32, _i32, _i32, _p, _p, _p]),
-    "htrc_tile_attention": (ctypes.c_int, [_p, _p, _p, _p, _i64, _i64, _i64, _i32, _p, _p, _p, _p, _p, _p, _i32, _i64,
-                                           _p, _p, _p, _i64, _i32, _i32, _f32, _p, _p, _p, _p, _p, _p]),
+    "htrc_tile_attention": (ctypes.c_int, [_p, _p, _p, _p, _i64, _i32, _i64, _i64, _i32, _p, _p, _p, _p, _p, _p, _i32,
+                                           _i64, _p, _p, _p, _i64, _i32, _i32, _f32, _p, _p, _p, _p, _p, _p]),
     "htrc_tail_partial": (ctypes.c_int, [_p, _i32, _i64, _i32, _p, _p, _i32, _f32, _p, _p]),
     "htrc_flat_forward_static_ws": (ctypes.c_int, [ctypes.POINTER(HtrcFlatArgs), _p]),
     "htrc_strerror": (ctypes.c_char_p, [ctypes.c_int]),

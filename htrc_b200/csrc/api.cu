@@ -14,7 +14,7 @@ using namespace htrc;
 namespace {
 
 constexpr int kDim = 128;
-constexpr int kTile = 64;
+constexpr int kTile = 64;        // rows of a tile as the kernels hold it (a 32-row tile is padded to 64)
 constexpr int kLeaf = 64;
 constexpr int64_t kMaxLeaves = 8192;
 constexpr int64_t kMaxRouted = 1024;
@@ -127,7 +127,7 @@ size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 // Workspace of one forward call.  Centre rows (mu, and the far-field state, routing and exclusion
 // rows) are per group of `group` tiles; a chunk holds gcm groups = gcm * group tiles.
 struct Layout {
-  int64_t n = 0, m = 0, nt = 0, nb = 0, pitch = 0, kx = 0, group = 1, ng = 0, gcm = 0, tcm = 0;
+  int64_t n = 0, m = 0, nt = 0, nb = 0, pitch = 0, kx = 0, group = 1, ng = 0, gcm = 0, tcm = 0, trows = 64;
   bool kmeans = false;
   size_t status = 0, k8 = 0, ks = 0, mu = 0, mu_hi = 0, mu_lo = 0, q8 = 0, sq = 0, dq8 = 0, sdq = 0, tail = 0;
   size_t g8 = 0, vb = 0, sg = 0, lz = 0, sel = 0, excl = 0, idx = 0, perm = 0, km = 0, total = 0;
@@ -137,7 +137,7 @@ constexpr int kMaxGroup = 65536;
 
 int validate(const HtrcFlatArgs* a, bool need_ptrs) {
   if (a == nullptr) return HTRC_ERR_ARG;
-  if (a->dim != kDim || a->tile != kTile || a->leaf != kLeaf) return HTRC_ERR_UNSUPPORTED;
+  if (a->dim != kDim || (a->tile != kTile && a->tile != kTile / 2) || a->leaf != kLeaf) return HTRC_ERR_UNSUPPORTED;
   if (a->n_queries < 1 || a->n_keys < a->leaf || a->n_keys % a->leaf) return HTRC_ERR_ARG;
   if (a->q_dtype != HTRC_DTYPE_F32 && a->q_dtype != HTRC_DTYPE_BF16) return HTRC_ERR_ARG;
   if (a->exact_leaves < 0 || a->sink_leaves < 0 || a->n_tail < 0) return HTRC_ERR_ARG;
@@ -160,7 +160,8 @@ Layout layout_of(const HtrcFlatArgs* a) {
   Layout L;
   L.n = a->n_queries;
   L.m = a->n_keys;
-  L.nt = (L.n + kTile - 1) / kTile;
+  L.trows = a->tile;
+  L.nt = (L.n + L.trows - 1) / L.trows;
   L.nb = L.m / kLeaf;
   L.pitch = pitch_of(L.nb);
   const int64_t sink = std::min<int64_t>(a->sink_leaves, L.nb);
@@ -299,7 +300,8 @@ int htrc_flat_forward(const HtrcFlatArgs* a, htrc_stream_t stream) {
   mark(0);
   launch_pack_rows(a->k, HTRC_DTYPE_BF16, L.m, HTRC_ROUND_HALF_EVEN, k8, ks, st);
   if (perm && (rc = launch_kmeans_order(a->q, a->q_dtype, L.n, perm, at<void>(ws, L.km), st)) != HTRC_OK) return rc;
-  launch_tile_prep(a->q, a->q_dtype, L.n, perm, group, at<float>(ws, L.mu), mu_hi, mu_lo, q8, sq, dq8, sdq, st);
+  const int trows = static_cast<int>(L.trows);
+  launch_tile_prep(a->q, a->q_dtype, L.n, trows, perm, group, at<float>(ws, L.mu), mu_hi, mu_lo, q8, sq, dq8, sdq, st);
   if (tail) launch_tail_partial(a->q, a->q_dtype, L.n, a->tail_k, a->tail_v, a->n_tail, scale, tail, st);
   if (cudaGetLastError() != cudaSuccess) return HTRC_ERR_CUDA;
   mark(1);
@@ -329,8 +331,8 @@ int htrc_flat_forward(const HtrcFlatArgs* a, htrc_stream_t stream) {
     TileMaps tmp;
     if ((rc = tile_maps(&tmp, q8, dq8, L.nt * 64, g8, vb, lz, sg, excl, gc, L.nb, L.pitch, k8, a->v, L.m)) != HTRC_OK)
       return rc;
-    if ((rc = launch_tile_attention(tmp, sq, sdq, ks, idx, kx, nb, L.n, t0, tc, group, scale, tail, perm, a->out,
-                                    a->lse, status, st)) != HTRC_OK)
+    if ((rc = launch_tile_attention(tmp, sq, sdq, ks, idx, kx, nb, L.n, trows, t0, tc, group, scale, tail, perm,
+                                    a->out, a->lse, status, st)) != HTRC_OK)
       return rc;
     mark(5 + 4 * chunk);
   }
@@ -363,12 +365,12 @@ int htrc_tile_prep(const void* q, int32_t q_dtype, int64_t n_queries, int32_t di
                    int32_t group, float* mu, uint16_t* mu_hi, uint16_t* mu_lo, int8_t* q8, float* sq, int8_t* dq8,
                    float* sdq, htrc_stream_t stream) {
   if (!q || !mu || !mu_hi || !mu_lo || !q8 || !sq || !dq8 || !sdq || n_queries < 1) return HTRC_ERR_ARG;
-  if (dim != kDim || tile != kTile) return HTRC_ERR_UNSUPPORTED;
+  if (dim != kDim || (tile != kTile && tile != kTile / 2)) return HTRC_ERR_UNSUPPORTED;
   if (q_dtype != HTRC_DTYPE_F32 && q_dtype != HTRC_DTYPE_BF16) return HTRC_ERR_ARG;
   if (group > kMaxGroup) return HTRC_ERR_ARG;
   int rc = check_device();
   if (rc != HTRC_OK) return rc;
-  launch_tile_prep(q, q_dtype, n_queries, perm, group, mu, mu_hi, mu_lo, q8, sq, dq8, sdq,
+  launch_tile_prep(q, q_dtype, n_queries, tile, perm, group, mu, mu_hi, mu_lo, q8, sq, dq8, sdq,
                    reinterpret_cast<cudaStream_t>(stream));
   return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
 }
@@ -441,20 +443,20 @@ int htrc_route(const float* sel, int64_t tc, int64_t nb, int32_t exact_leaves, i
 }
 
 int htrc_tile_attention(const int8_t* q8, const float* sq, const int8_t* dq8, const float* sdq, int64_t n_queries,
-                        int64_t t0, int64_t tc, int32_t group, const int8_t* g8, const float* sg, const float* lz,
-                        const uint16_t* vb, const uint8_t* excl, const int32_t* idx, int32_t kx, int64_t nb,
-                        const int8_t* k8, const float* ks, const uint16_t* v, int64_t n_keys, int32_t dim, int32_t leaf,
-                        float scale, const float* tail_part, const int32_t* perm, float* out, float* lse,
+                        int32_t tile, int64_t t0, int64_t tc, int32_t group, const int8_t* g8, const float* sg,
+                        const float* lz, const uint16_t* vb, const uint8_t* excl, const int32_t* idx, int32_t kx,
+                        int64_t nb, const int8_t* k8, const float* ks, const uint16_t* v, int64_t n_keys, int32_t dim,
+                        int32_t leaf, float scale, const float* tail_part, const int32_t* perm, float* out, float* lse,
                         int32_t* status, htrc_stream_t stream) {
   if (!q8 || !sq || !dq8 || !sdq || !k8 || !ks || !v || !out || n_queries < 1 || t0 < 0 || tc < 1) return HTRC_ERR_ARG;
   const int64_t g = group > 1 ? group : 1;
   if (g > kMaxGroup || t0 % g) return HTRC_ERR_ARG;
-  if (dim != kDim || leaf != kLeaf) return HTRC_ERR_UNSUPPORTED;
+  if (dim != kDim || leaf != kLeaf || (tile != kTile && tile != kTile / 2)) return HTRC_ERR_UNSUPPORTED;
   if (nb < 1 || n_keys != nb * leaf || kx < 0 || kx > nb) return HTRC_ERR_ARG;
   if (kx > kMaxRouted || nb > kMaxLeaves) return HTRC_ERR_UNSUPPORTED;
   if (kx < nb && (!g8 || !sg || !lz || !vb || !excl)) return HTRC_ERR_ARG;
   if (kx > 0 && !idx) return HTRC_ERR_ARG;
-  const int64_t nt = (n_queries + 63) / 64;
+  const int64_t nt = (n_queries + tile - 1) / tile;
   if (t0 + tc > nt) return HTRC_ERR_ARG;
   int rc = check_device();
   if (rc != HTRC_OK) return rc;
@@ -469,7 +471,7 @@ int htrc_tile_attention(const int8_t* q8, const float* sq, const int8_t* dq8, co
                       static_cast<const float*>(lzp), static_cast<const float*>(sgp),
                       static_cast<const uint8_t*>(exp_), (tc + g - 1) / g, nb, pitch_of(nb), k8, v, n_keys)) != HTRC_OK)
     return rc;
-  return launch_tile_attention(mp, sq, sdq, ks, idx, kx, static_cast<int>(nb), n_queries, t0, tc, static_cast<int>(g),
+  return launch_tile_attention(mp, sq, sdq, ks, idx, kx, static_cast<int>(nb), n_queries, tile, t0, tc, static_cast<int>(g),
                                scale_of(scale), tail_part, perm, out, lse, status,
                                reinterpret_cast<cudaStream_t>(stream));
 }
@@ -490,7 +492,7 @@ const char* htrc_strerror(int code) {
   switch (code) {
     case HTRC_OK: return "ok";
     case HTRC_ERR_ARG: return "invalid argument";
-    case HTRC_ERR_UNSUPPORTED: return "unsupported configuration (needs dim 128, tile 64, leaf 64, <= 8192 leaves, <= 1024 routed leaves)";
+    case HTRC_ERR_UNSUPPORTED: return "unsupported configuration (needs dim 128, tile 64 or 32, leaf 64, <= 8192 leaves, <= 1024 routed leaves)";
     case HTRC_ERR_WORKSPACE: return "workspace missing, misaligned or too small";
     case HTRC_ERR_CUDA: return "CUDA runtime error";
     case HTRC_ERR_DEVICE: return "no sm_100 device or device-side failure";

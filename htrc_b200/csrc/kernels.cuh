@@ -33,8 +33,8 @@ struct TileMaps {
 };
 
 void launch_pack_rows(const void* x, int dtype, int64_t rows, int rounding, int8_t* x8, float* scale, cudaStream_t st);
-void launch_tile_prep(const void* q, int dtype, int64_t n, const int32_t* perm, int group, float* mu, uint16_t* mu_hi,
-                      uint16_t* mu_lo, int8_t* q8, float* sq, int8_t* dq8, float* sdq, cudaStream_t st);
+void launch_tile_prep(const void* q, int dtype, int64_t n, int tile_rows, const int32_t* perm, int group, float* mu,
+                      uint16_t* mu_hi, uint16_t* mu_lo, int8_t* q8, float* sq, int8_t* dq8, float* sdq, cudaStream_t st);
 size_t kmeans_scratch_bytes(int64_t n);
 int launch_kmeans_order(const void* q, int dtype, int64_t n, int32_t* perm, void* scratch, cudaStream_t st);
 void launch_tail_partial(const void* q, int dtype, int64_t n, const float* tk, const float* tv, int n_tail, float scale,
@@ -46,7 +46,7 @@ int launch_rowmax(const RowmaxMaps& maps, const float* sdq, float* sel, int64_t 
 int launch_route(const float* sel, int64_t pitch, int64_t tc, int group, int nb, int kx, int sink, int32_t* idx,
                  uint8_t* excl, cudaStream_t st);
 int launch_tile_attention(const TileMaps& maps, const float* sq, const float* sdq, const float* ks, const int32_t* idx,
-                          int kx, int nb, int64_t n, int64_t t0, int64_t tc, int group, float scale,
+                          int kx, int nb, int64_t n, int tile_rows, int64_t t0, int64_t tc, int group, float scale,
                           const float* tail_part, const int32_t* perm, float* out, float* lse, int* status,
                           cudaStream_t st);
 

@@ -83,11 +83,15 @@ void launch_pack_rows(const void* x, int dtype, int64_t rows, int rounding, int8
   }
 }
 
-// Row of q that tile row `row` holds: rows past n repeat the last row (the reference pads the last
-// tile that way, h3/htrc_flat.py:150-152), after the optional k-means permutation (:146-147).
-__device__ __forceinline__ int64_t source_row(const int32_t* perm, int64_t n, int64_t row) {
-  const int64_t r = row < n - 1 ? row : n - 1;
-  return perm ? static_cast<int64_t>(__ldg(perm + r)) : r;
+// Row of q that row r of tile t holds.  Tiles of T = 64 or 32 query rows are held as 64 rows: a 32-row
+// tile's rows 32..63 repeat its row 31, which changes no centre (taken over the real rows), no row
+// maximum and no output (only rows < T are written).  Rows past n repeat the last row (the reference
+// pads the last tile that way, h3/htrc_flat.py:150-152), after the optional k-means permutation
+// (:146-147).
+__device__ __forceinline__ int64_t source_row(const int32_t* perm, int64_t n, int trows, int64_t t, int r) {
+  const int64_t li = t * trows + (r < trows ? r : trows - 1);
+  const int64_t c = li < n - 1 ? li : n - 1;
+  return perm ? static_cast<int64_t>(__ldg(perm + c)) : c;
 }
 
 __device__ __forceinline__ void store_centre(int64_t c, int col, float m, float* mu, uint16_t* mu_hi,
@@ -99,35 +103,37 @@ __device__ __forceinline__ void store_centre(int64_t c, int col, float m, float*
   mu_lo[c * 128 + col] = __bfloat16_as_ushort(lo);
 }
 
-// Centres of groups of G > 1 consecutive tiles (h3/htrc_flat.py:223-231): the mean of all G * 64 rows
+// Centres of groups of G > 1 consecutive tiles (h3/htrc_flat.py:223-231): the mean of all G * T rows
 // of the padded tiles -- the last tile's rows past n repeat the last row and the tiles that fill the
 // last group repeat the last tile.  One CTA per group, thread = column; float64 sum rounded once.
 template <typename T>
 __global__ void __launch_bounds__(128) group_centre_kernel(const T* __restrict__ q, const int32_t* __restrict__ perm,
-                                                           int64_t n, int64_t nt, int group, float* __restrict__ mu,
-                                                           uint16_t* __restrict__ mu_hi, uint16_t* __restrict__ mu_lo) {
+                                                           int64_t n, int trows, int64_t nt, int group,
+                                                           float* __restrict__ mu, uint16_t* __restrict__ mu_hi,
+                                                           uint16_t* __restrict__ mu_lo) {
   const int64_t g = blockIdx.x;
   const int col = threadIdx.x;
   double s = 0.0;
   for (int x = 0; x < group; ++x) {
     const int64_t t = g * group + x < nt ? g * group + x : nt - 1;
 #pragma unroll 8
-    for (int r = 0; r < 64; ++r) {
-      const int64_t src = source_row(perm, n, t * 64 + r);
+    for (int r = 0; r < trows; ++r) {
+      const int64_t src = source_row(perm, n, trows, t, r);
       if constexpr (sizeof(T) == 4)
         s += static_cast<double>(__ldg(reinterpret_cast<const float*>(q) + src * 128 + col));
       else
         s += static_cast<double>(__uint_as_float(static_cast<uint32_t>(__ldg(q + src * 128 + col)) << 16));
     }
   }
-  store_centre(g, col, static_cast<float>(s / static_cast<double>(group * 64)), mu, mu_hi, mu_lo);
+  store_centre(g, col, static_cast<float>(s / static_cast<double>(group * trows)), mu, mu_hi, mu_lo);
 }
 
-// One CTA (4 warps) per tile of 64 query rows: the tile's centre (group 1; else the group centre
-// written by group_centre_kernel) and the codes of its rows and of their offsets from the centre.
+// One CTA (4 warps) per tile of T query rows (held as 64 rows): the tile's centre (group 1; else the
+// group centre written by group_centre_kernel) and the codes of its rows and of their offsets from
+// the centre.
 template <typename T>
 __global__ void __launch_bounds__(128) tile_prep_kernel(const T* __restrict__ q, const int32_t* __restrict__ perm,
-                                                        int64_t n, int group, float* __restrict__ mu,
+                                                        int64_t n, int trows, int group, float* __restrict__ mu,
                                                         uint16_t* __restrict__ mu_hi, uint16_t* __restrict__ mu_lo,
                                                         int8_t* __restrict__ q8, float* __restrict__ sq,
                                                         int8_t* __restrict__ dq8, float* __restrict__ sdq) {
@@ -135,13 +141,14 @@ __global__ void __launch_bounds__(128) tile_prep_kernel(const T* __restrict__ q,
   __shared__ float mus[128];
   const int t = blockIdx.x;
   const int tid = threadIdx.x;
-  const int64_t r0 = static_cast<int64_t>(t) * 64;
-  const int nreal = static_cast<int>(n - r0 < 64 ? n - r0 : 64);
+  const int64_t r0 = static_cast<int64_t>(t) * 64;              // first of the tile's 64 held rows
+  const int64_t first = static_cast<int64_t>(t) * trows;         // its first query (in tile order)
+  const int nreal = static_cast<int>(n - first < trows ? n - first : trows);
   // stage the tile: warp w loads rows w, w+4, ...; lane owns 4 columns
   const int warp = tid >> 5, lane = tid & 31;
   for (int r = warp; r < 64; r += 4) {
     float v[4];
-    load4<T>(q + source_row(perm, n, r0 + r) * 128 + lane * 4, v);
+    load4<T>(q + source_row(perm, n, trows, t, r) * 128 + lane * 4, v);
 #pragma unroll
     for (int i = 0; i < 4; ++i) qs[r][lane * 4 + i] = v[i];
   }
@@ -183,21 +190,22 @@ __global__ void __launch_bounds__(128) tile_prep_kernel(const T* __restrict__ q,
   }
 }
 
-void launch_tile_prep(const void* q, int dtype, int64_t n, const int32_t* perm, int group, float* mu, uint16_t* mu_hi,
-                      uint16_t* mu_lo, int8_t* q8, float* sq, int8_t* dq8, float* sdq, cudaStream_t st) {
-  const int64_t nt = (n + 63) / 64;
+void launch_tile_prep(const void* q, int dtype, int64_t n, int tile_rows, const int32_t* perm, int group, float* mu,
+                      uint16_t* mu_hi, uint16_t* mu_lo, int8_t* q8, float* sq, int8_t* dq8, float* sdq, cudaStream_t st) {
+  const int tr = tile_rows == 32 ? 32 : 64;
+  const int64_t nt = (n + tr - 1) / tr;
   const int g = group > 1 ? group : 1;
   const unsigned ng = static_cast<unsigned>((nt + g - 1) / g);
   if (dtype == HTRC_DTYPE_BF16) {
     const uint16_t* qb = static_cast<const uint16_t*>(q);
-    if (g > 1) group_centre_kernel<uint16_t><<<ng, 128, 0, st>>>(qb, perm, n, nt, g, mu, mu_hi, mu_lo);
-    tile_prep_kernel<uint16_t><<<static_cast<unsigned>(nt), 128, 0, st>>>(qb, perm, n, g, mu, mu_hi, mu_lo, q8, sq,
-                                                                         dq8, sdq);
+    if (g > 1) group_centre_kernel<uint16_t><<<ng, 128, 0, st>>>(qb, perm, n, tr, nt, g, mu, mu_hi, mu_lo);
+    tile_prep_kernel<uint16_t><<<static_cast<unsigned>(nt), 128, 0, st>>>(qb, perm, n, tr, g, mu, mu_hi, mu_lo, q8,
+                                                                         sq, dq8, sdq);
   } else {
     const float* qf = static_cast<const float*>(q);
-    if (g > 1) group_centre_kernel<float><<<ng, 128, 0, st>>>(qf, perm, n, nt, g, mu, mu_hi, mu_lo);
-    tile_prep_kernel<float><<<static_cast<unsigned>(nt), 128, 0, st>>>(qf, perm, n, g, mu, mu_hi, mu_lo, q8, sq, dq8,
-                                                                      sdq);
+    if (g > 1) group_centre_kernel<float><<<ng, 128, 0, st>>>(qf, perm, n, tr, nt, g, mu, mu_hi, mu_lo);
+    tile_prep_kernel<float><<<static_cast<unsigned>(nt), 128, 0, st>>>(qf, perm, n, tr, g, mu, mu_hi, mu_lo, q8, sq,
+                                                                      dq8, sdq);
   }
 }
 

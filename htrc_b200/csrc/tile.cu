@@ -24,6 +24,9 @@
 // The producer and issuer warps run converged and let one elected lane issue: a warp whose lanes take
 // different roles serialises them, since a lane suspended in an mbarrier wait holds up the others.
 //
+// Tiles of 32 rows (the "max" mode, h3/htrc_flat_runner.py:52) are held as 64 rows whose rows 32..63
+// repeat row 31; only rows < 32 are written.
+//
 // Groups (h3/htrc_flat.py:223-231): G consecutive tiles share one far-field state row and one routing;
 // tile t of the chunk reads state row t / G.  k-means order (:146-147, :159-165): tile row i is query
 // perm[i], so the epilogue writes out/lse row perm[i] (and reads the tail partial of that row).
@@ -96,7 +99,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                           const __grid_constant__ CUtensorMap tm_excl, const __grid_constant__ CUtensorMap tm_k8,
                           const __grid_constant__ CUtensorMap tm_v, const float* __restrict__ sq,
                           const float* __restrict__ sdq, const float* __restrict__ ks, const int32_t* __restrict__ idx,
-                          int kx, int nb, int nf, int64_t n, int64_t t0, int64_t tc, int group, float scale,
+                          int kx, int nb, int nf, int64_t n, int trows, int64_t t0, int64_t tc, int group,
+                          float scale,
                           const float* __restrict__ tail_part, const int32_t* __restrict__ perm,
                           float* __restrict__ out, float* __restrict__ lse, int* status) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -422,8 +426,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float m1 = m1s[col], l1 = l1s[col];
       const float m0 = kcount ? m_used : -INFINITY;
       const float n0 = m0 * kLn2, n1 = m1 * kLn2;           // natural-log units
-      const bool valid = has_tile && gr < n;
-      const int64_t orow = (perm != nullptr && valid) ? static_cast<int64_t>(__ldg(perm + gr)) : gr;
+      const int64_t li = (t0 + tl) * trows + r;                  // query index in tile order
+      const bool valid = has_tile && r < trows && li < n;
+      const int64_t orow = (perm != nullptr && valid) ? static_cast<int64_t>(__ldg(perm + li)) : li;
       const float* tp = (tail_part != nullptr && valid) ? tail_part + orow * 130 : nullptr;
       const float mt = tp ? tp[128] : -INFINITY, lt = tp ? tp[129] : 0.f;
       const float mm = fmaxf(fmaxf(n0, n1), mt);
@@ -468,7 +473,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 int launch_tile_attention(const TileMaps& maps, const float* sq, const float* sdq, const float* ks, const int32_t* idx,
-                          int kx, int nb, int64_t n, int64_t t0, int64_t tc, int group, float scale,
+                          int kx, int nb, int64_t n, int tile_rows, int64_t t0, int64_t tc, int group, float scale,
                           const float* tail_part, const int32_t* perm, float* out, float* lse, int* status,
                           cudaStream_t st) {
   if (kx > kMaxKx || nb > 65535) return HTRC_ERR_UNSUPPORTED;
@@ -485,7 +490,8 @@ int launch_tile_attention(const TileMaps& maps, const float* sq, const float* sd
   const unsigned grid = static_cast<unsigned>((tc + 1) / 2);
   tile_attention_kernel<<<grid, kThreads, kSmemBytes, st>>>(maps.q8, maps.dq8, maps.g8, maps.vb, maps.lz, maps.sg,
                                                             maps.excl, maps.k8, maps.v, sq, sdq, ks, idx, kx, nb, nf,
-                                                            n, t0, tc, group > 1 ? group : 1, scale, tail_part,
+                                                            n, tile_rows == 32 ? 32 : 64, t0, tc,
+                                                            group > 1 ? group : 1, scale, tail_part,
                                                             perm, out, lse, status);
   return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
 }

@@ -27,6 +27,7 @@ from . import _lib
 from ._lib import check, lib, ptr, stream_ptr
 
 DIM, TILE, LEAF = 128, 64, 64
+TILES = (64, 32)          # query tile rows the kernels take (32: the "max" mode, held as 64 rows)
 
 PROD = dict(tile=64, exact_leaves=256, tile_chunk=128, backend="triton", precision="tf32",
             store="int8", dot="bf16", splits=4, kern=dict(tile_warps=4, tile_bn=64, tile_stages=2))
@@ -87,8 +88,8 @@ def _check_args(q, k, v, tile, exact_leaves, order, curvature, leaf, select, bac
         raise ValueError("store='fp8' needs dot='bf16', select='max' and no state fake-quant")
     if store != "int8" or dot != "bf16":
         raise NotImplementedError("only the INT8 production path (store='int8', dot='bf16') is implemented")
-    if int(tile) != TILE or int(leaf) != LEAF:
-        raise NotImplementedError(f"the kernels implement tile={TILE}, leaf={LEAF} (got tile={tile}, leaf={leaf})")
+    if int(tile) not in TILES or int(leaf) != LEAF:
+        raise NotImplementedError(f"the kernels implement tile=64 or 32, leaf={LEAF} (got tile={tile}, leaf={leaf})")
     if int(sel_stride) != 1:
         raise NotImplementedError("sel_stride != 1 is not implemented")
     if quant:
@@ -125,13 +126,13 @@ def order_code(order) -> int:
 
 
 def _args(qd, kb, vb, tk, tv, exact_leaves, sink_leaves, tile_chunk, scale, out=None, lse=None, ws=None,
-          stage_events=None, group=1, order=_lib.ORDER_SEQ):
+          stage_events=None, group=1, order=_lib.ORDER_SEQ, tile=TILE):
     a = _lib.HtrcFlatArgs()
     a.q = ptr(qd)
     a.q_dtype = _lib.DTYPE_BF16 if qd.dtype == torch.bfloat16 else _lib.DTYPE_F32
     a.k, a.v = ptr(kb), ptr(vb)
     a.n_queries, a.n_keys = int(qd.shape[0]), int(kb.shape[0])
-    a.dim, a.tile, a.leaf = DIM, TILE, LEAF
+    a.dim, a.tile, a.leaf = DIM, int(tile), LEAF
     a.exact_leaves, a.sink_leaves = int(exact_leaves), int(sink_leaves)
     a.tile_chunk = int(tile_chunk) if tile_chunk else 0
     a.scale = float(scale) if scale is not None else 0.0
@@ -155,10 +156,10 @@ def _args(qd, kb, vb, tk, tv, exact_leaves, sink_leaves, tile_chunk, scale, out=
 
 
 def workspace_bytes(n_queries, n_keys, exact_leaves, sink_leaves=0, tile_chunk=0, n_tail=0, group=1,
-                    order=_lib.ORDER_SEQ) -> int:
+                    order=_lib.ORDER_SEQ, tile=TILE) -> int:
     """Device workspace one forward call needs."""
     a = _lib.HtrcFlatArgs()
-    a.n_queries, a.n_keys, a.dim, a.tile, a.leaf = int(n_queries), int(n_keys), DIM, TILE, LEAF
+    a.n_queries, a.n_keys, a.dim, a.tile, a.leaf = int(n_queries), int(n_keys), DIM, int(tile), LEAF
     a.q_dtype = _lib.DTYPE_F32
     a.exact_leaves, a.sink_leaves = int(exact_leaves), int(sink_leaves)
     a.tile_chunk, a.n_tail = int(tile_chunk or 0), int(n_tail)
@@ -168,26 +169,34 @@ def workspace_bytes(n_queries, n_keys, exact_leaves, sink_leaves=0, tile_chunk=0
     return int(nbytes.value)
 
 
+def new_workspace(nbytes, device):
+    """A device workspace of nbytes for ``forward_into``: its device status word (the first 256 bytes)
+    starts at zero; the rest needs no initialisation."""
+    w = torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+    w[:256].zero_()
+    return w
+
+
 def _workspace(ws, nbytes, device):
     """A uint8 device buffer of at least nbytes, reused through the ``ws`` dict like the reference's
     workspace (h3/htrc_flat_triton.py:302-312)."""
     if ws is None:
-        return torch.empty(nbytes, dtype=torch.uint8, device=device)
+        return new_workspace(nbytes, device)
     b = ws.get("workspace")
     if b is None or b.numel() < nbytes or b.device != device:
-        b = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        b = new_workspace(nbytes, device)
         ws["workspace"] = b
     return b
 
 
 def forward_into(qd, kb, vb, tk, tv, *, exact_leaves, sink_leaves=0, tile_chunk=0, scale=None, out, lse=None,
-                 workspace, stream=None, stage_events=None, group=1, order=_lib.ORDER_SEQ):
+                 workspace, stream=None, stage_events=None, group=1, order=_lib.ORDER_SEQ, tile=TILE):
     """One head through ``htrc_flat_forward`` into caller-provided buffers (no allocation; CUDA-graph
     capturable).  qd [N, 128] f32/bf16, kb/vb [M, 128] bf16, out [N, 128] f32, lse [N] f32 or None;
     stage_events: optional list of torch.cuda.Event recorded between the stages (see
-    include/htrc_flat.h); group / order: ``group_of(kern)`` / ``order_code(order)``."""
+    include/htrc_flat.h); group / order: ``group_of(kern)`` / ``order_code(order)``; tile: 64 or 32."""
     a = _args(qd, kb, vb, tk, tv, exact_leaves, sink_leaves, tile_chunk, scale, out, lse, workspace, stage_events,
-              group, order)
+              group, order, tile)
     check(lib().htrc_flat_forward(a, stream_ptr(stream)), "htrc_flat_forward")
 
 
@@ -197,6 +206,9 @@ def device_status(workspace, stream=None) -> int:
     check(lib().htrc_flat_status(ptr(workspace), st, stream_ptr(stream)), "htrc_flat_status")
     if st.value:
         bits = [name for b, name in _lib.STATUS_BITS.items() if st.value & b]
+        other = st.value & ~sum(_lib.STATUS_BITS)
+        if other:
+            bits.append(f"unknown bits {other:#x} (a workspace whose status word was not zeroed?)")
         raise _lib.HtrcError("device status: " + ", ".join(bits))
     return 0
 
@@ -215,16 +227,16 @@ def flat_attention(q, k, v, *, tile=64, exact_leaves=64, order="seq", curvature=
     grp, oc = group_of(kern), order_code(order)
     if prof is not None:
         st = run_stages(qd, kb, vb, tk, tv, exact_leaves=exact_leaves, sink_leaves=sink_leaves,
-                        tile_chunk=tile_chunk, scale=scale, prof=prof, group=grp, order=oc)
+                        tile_chunk=tile_chunk, scale=scale, prof=prof, group=grp, order=oc, tile=tile)
         return (st["out"], st["lse"]) if return_lse else st["out"]
     n = int(qd.shape[0])
     out = torch.empty((n, DIM), dtype=torch.float32, device=q.device)
     lse = torch.empty((n,), dtype=torch.float32, device=q.device) if return_lse else None
     nbytes = workspace_bytes(n, int(kb.shape[0]), exact_leaves, sink_leaves, tile_chunk,
-                             int(tk.shape[0]) if tk is not None else 0, grp, oc)
+                             int(tk.shape[0]) if tk is not None else 0, grp, oc, tile)
     w = _workspace(ws, nbytes, q.device)
     forward_into(qd, kb, vb, tk, tv, exact_leaves=exact_leaves, sink_leaves=sink_leaves,
-                 tile_chunk=tile_chunk, scale=scale, out=out, lse=lse, workspace=w, group=grp, order=oc)
+                 tile_chunk=tile_chunk, scale=scale, out=out, lse=lse, workspace=w, group=grp, order=oc, tile=tile)
     return (out, lse) if return_lse else out
 
 
@@ -235,7 +247,7 @@ def flat_attention_prod(q, k, v, **over):
 
 @torch.inference_mode()
 def run_stages(qd, kb, vb, tk=None, tv=None, *, exact_leaves, sink_leaves=0, tile_chunk=0, scale=None,
-               prof=None, stream=None, group=1, order=_lib.ORDER_SEQ):
+               prof=None, stream=None, group=1, order=_lib.ORDER_SEQ, tile=TILE):
     """The same operator launched stage by stage through the C ABI's stage entry points, returning
     every intermediate (perm, k8, ks, mu, q8, sq, dq8, sdq, g8, sg, lz, vb, sel, idx, excl, out, lse).
     Used for stage timing (``prof``, the reference's stage names prep/stats/select/tile/finish) and
@@ -246,7 +258,8 @@ def run_stages(qd, kb, vb, tk=None, tv=None, *, exact_leaves, sink_leaves=0, til
     s = stream_ptr(stream)
     tick = _Tick(prof)
     n, m = int(qd.shape[0]), int(kb.shape[0])
-    nt, nb = -(-n // TILE), m // LEAF
+    tile = int(tile)
+    nt, nb = -(-n // tile), m // LEAF
     grp = max(1, int(group))
     ng = -(-nt // grp)
     pitch = leaf_pitch(nb)
@@ -273,7 +286,7 @@ def run_stages(qd, kb, vb, tk=None, tv=None, *, exact_leaves, sink_leaves=0, til
         check(L.htrc_kmeans_order(ptr(qd), qdt, n, DIM, ptr(r["perm"]), ptr(scratch), int(nbytes.value), s),
               "htrc_kmeans_order")
     perm = ptr(r["perm"])
-    check(L.htrc_tile_prep(ptr(qd), qdt, n, DIM, TILE, perm, grp, ptr(r["mu"]), ptr(r["mu_hi"]), ptr(r["mu_lo"]),
+    check(L.htrc_tile_prep(ptr(qd), qdt, n, DIM, tile, perm, grp, ptr(r["mu"]), ptr(r["mu_hi"]), ptr(r["mu_lo"]),
                            ptr(r["q8"]), ptr(r["sq"]), ptr(r["dq8"]), ptr(r["sdq"]), s), "htrc_tile_prep")
     tail_part = None
     if tk is not None:
@@ -296,11 +309,12 @@ def run_stages(qd, kb, vb, tk=None, tv=None, *, exact_leaves, sink_leaves=0, til
     check(L.htrc_route(ptr(r["sel"]), nt, nb, int(exact_leaves), sink, grp, ptr(r["idx"]), ptr(r["excl"]), s),
           "htrc_route")
     tick("select")
-    check(L.htrc_tile_attention(ptr(r["q8"]), ptr(r["sq"]), ptr(r["dq8"]), ptr(r["sdq"]), n, 0, nt, grp, ptr(r["g8"]),
+    check(L.htrc_tile_attention(ptr(r["q8"]), ptr(r["sq"]), ptr(r["dq8"]), ptr(r["sdq"]), n, tile, 0, nt, grp,
+                                ptr(r["g8"]),
                                 ptr(r["sg"]), ptr(r["lz"]), ptr(r["vb"]), ptr(r["excl"]), ptr(r["idx"]), kx, nb,
                                 ptr(r["k8"]), ptr(r["ks"]), ptr(vb), m, DIM, LEAF, sc, ptr(tail_part), perm,
                                 ptr(r["out"]), ptr(r["lse"]), stp, s), "htrc_tile_attention")
     tick("tile")
     tick("finish")
-    r["kx"], r["nb"], r["pitch"], r["group"] = kx, nb, pitch, grp
+    r["kx"], r["nb"], r["pitch"], r["group"], r["tile"] = kx, nb, pitch, grp, tile
     return r

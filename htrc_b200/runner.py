@@ -42,7 +42,7 @@ def predicted_peak_mib(keys: int, tile: int, tile_chunk: int, splits: int = 8, l
     ``splits`` is accepted and unused."""
     q = int(queries) if queries else int(tile) * max(1, int(tile_chunk))
     ws = _flat.workspace_bytes(q, int(keys), int(exact_leaves), 0, int(tile_chunk), 0, int(group),
-                               _flat.order_code(order))
+                               _flat.order_code(order), int(tile))
     static = (q * dim * 4 + 2 * keys * dim * 2 + q * (dim + 1) * 4) if graph else 0
     kmeans = KMEANS_MIB if order == "kmeans" else 0.0
     return (ws + static) / 2 ** 20 + kmeans
@@ -143,11 +143,11 @@ class FlatRunner:
             self._so = torch.empty((self.queries, self.dim), device=dev, dtype=torch.float32)
             self._sl = torch.empty((self.queries,), device=dev, dtype=torch.float32)
             nbytes = _flat.workspace_bytes(self.queries, self.keys, c["exact_leaves"], c["sink_leaves"],
-                                           c["tile_chunk"], self.tail_rows, self.group, self.order)
-            self._w = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+                                           c["tile_chunk"], self.tail_rows, self.group, self.order, c["tile"])
+            self._w = _flat.new_workspace(nbytes, dev)
             kw = dict(exact_leaves=c["exact_leaves"], sink_leaves=c["sink_leaves"], tile_chunk=c["tile_chunk"],
                       scale=c.get("scale"), out=self._so, lse=self._sl, workspace=self._w, group=self.group,
-                      order=self.order)
+                      order=self.order, tile=c["tile"])
             self._capturing = True
             try:
                 side = torch.cuda.Stream()

@@ -10,8 +10,9 @@
  *
  * Layouts (row-major, contiguous unless a pitch is given):
  *   q [N, D] f32 or bf16;  k, v [M, D] bf16;  D = 128;  M a multiple of `leaf`.
- *   Tiles of `tile` = 64 query rows; nt = ceil(N / 64); the last tile is padded with repeats of the
- *   last query row.  nb = M / leaf leaves.  Per-(tile, leaf) scalars use the leaf pitch
+ *   Tiles of `tile` = 64 (or 32) query rows; nt = ceil(N / tile); the last tile is padded with repeats
+ *   of the last query row.  Every tile is held as 64 rows (q8/dq8/sq/sdq [nt*64, ...]); a 32-row tile's
+ *   rows 32..63 repeat its row 31.  nb = M / leaf leaves.  Per-(tile, leaf) scalars use the leaf pitch
  *   P = htrc_leaf_pitch(nb) (nb rounded up to 16).
  *   Groups: G consecutive tiles share one expansion centre, one far-field state row and one routing
  *   (G = 1 by default); ng = ceil(nt / G) state rows.  The per-(tile, leaf) arrays below are then
@@ -57,7 +58,8 @@ typedef struct HtrcFlatArgs {
   int64_t n_queries;       /* N >= 1 */
   int64_t n_keys;          /* M, a positive multiple of leaf */
   int32_t dim;             /* D, must be 128 */
-  int32_t tile;            /* query tile rows, must be 64 */
+  int32_t tile;            /* query tile rows: 64, or 32 (the "max" mode; held as 64 rows, rows 32..63
+                              repeating row 31) */
   int32_t leaf;            /* key leaf tokens, must be 64 */
   int32_t exact_leaves;    /* E >= 0: leaves evaluated exactly per tile (clamped to nb) */
   int32_t sink_leaves;     /* leading leaves always exact (clamped to nb) */
@@ -66,7 +68,8 @@ typedef struct HtrcFlatArgs {
   const float* tail_k;     /* [n_tail, dim] f32 keys past the last full leaf, or NULL */
   const float* tail_v;     /* [n_tail, dim] f32 */
   int32_t n_tail;          /* >= 0 */
-  void* workspace;         /* device workspace, 256-byte aligned */
+  void* workspace;         /* device workspace, 256-byte aligned; its first 256 bytes (the status word)
+                              must be zero when first used -- htrc_flat_status() clears them */
   size_t workspace_bytes;  /* >= htrc_flat_workspace_size(args) */
   float* out;              /* [n_queries, dim] f32 output */
   float* lse;              /* [n_queries] f32 log-partition (logit units), or NULL */
@@ -91,7 +94,7 @@ int htrc_flat_workspace_size(const HtrcFlatArgs* args, size_t* bytes);
 /* The whole operator for one head: INT8 key pack, tile centres and query codes, leaf statistics,
  * row-max selection, top-E routing, far field + near field + tail, normalised output and log-Z.
  * Replaces flat_attention(q, k, v, backend="triton", store="int8", dot="bf16", select="max",
- * tile=64, leaf=64, exact_leaves=E, sink_leaves=S, tail=(tk, tv), order="seq"|"kmeans",
+ * tile=64|32, leaf=64, exact_leaves=E, sink_leaves=S, tail=(tk, tv), order="seq"|"kmeans",
  * kern={"group": G}) of the reference (h3/htrc_flat.py:99-124 -> _flat_triton :181-276), plus the
  * log-Z output the reference lacks. */
 int htrc_flat_forward(const HtrcFlatArgs* args, htrc_stream_t stream);
@@ -109,12 +112,12 @@ int htrc_pack_int8(const void* x, int32_t dtype, int64_t rows, int32_t dim, int3
 
 /* Tile centres and query codes (h3/htrc_flat.py:142-156 `_tiles`, :223-231 groups;
  * h3/htrc_flat_triton.py:103-117):
- * mu [ng, dim] f32; group 1: the mean of the tile's real rows; group G > 1: the mean of all G*64 rows of
+ * mu [ng, dim] f32; group 1: the mean of the tile's real rows; group G > 1: the mean of all G*tile rows of
  * the group, the last tile's padding rows and the repeats of the last tile that fill the last group
  * included (float64 sum rounded once); mu_hi/mu_lo [ng, dim] bf16 with mu_hi = bf16(mu),
  * mu_lo = bf16(mu - mu_hi);
  * q8/dq8 [nt*64, dim] int8 and sq/sdq [nt*64] f32: half-away codes of q and of q - mu[tile / G].
- * perm: NULL, or [n_queries] int32 (tile row i reads query row perm[i]). */
+ * tile: 64 or 32; perm: NULL, or [n_queries] int32 (query i in tile order is row perm[i] of q). */
 int htrc_tile_prep(const void* q, int32_t q_dtype, int64_t n_queries, int32_t dim, int32_t tile, const int32_t* perm,
                    int32_t group, float* mu, uint16_t* mu_hi, uint16_t* mu_lo, int8_t* q8, float* sq, int8_t* dq8,
                    float* sdq, htrc_stream_t stream);
@@ -157,9 +160,11 @@ int htrc_route(const float* sel, int64_t tc, int64_t nb, int32_t exact_leaves, i
  * merged as :257-273).  State arrays as produced by the stages above (state row (t - t0) / group; t0 a
  * multiple of group); k8/ks from htrc_pack_int8 (half-even) of k; tail_part: NULL or
  * [n_queries, dim + 2] f32 rows (acc, m, l) from the tail, in the caller's row order; perm: NULL, or the
- * permutation given to htrc_tile_prep (tile row i is written to out/lse row perm[i]). */
+ * permutation given to htrc_tile_prep (query i in tile order is written to out/lse row perm[i]); tile: the
+ * tile rows given to htrc_tile_prep. */
 int htrc_tile_attention(const int8_t* q8, const float* sq, const int8_t* dq8, const float* sdq, int64_t n_queries,
-                        int64_t t0, int64_t tc, int32_t group, const int8_t* g8, const float* sg, const float* lz,
+                        int32_t tile, int64_t t0, int64_t tc, int32_t group, const int8_t* g8, const float* sg,
+                        const float* lz,
                         const uint16_t* vb, const uint8_t* excl, const int32_t* idx, int32_t kx, int64_t nb,
                         const int8_t* k8, const float* ks, const uint16_t* v, int64_t n_keys, int32_t dim,
                         int32_t leaf, float scale, const float* tail_part, const int32_t* perm, float* out, float* lse,

@@ -148,6 +148,10 @@ CASES = [
          group=2),
     dict(name="kmeans_sampled", grid=(4, 32, 33), leaf=64, E=4, sink=0, tail=0, trim=67, seed=23, order="kmeans",
          slim=True, keys=1024),
+    # 32-row tiles (the "max" mode: k-means order, tile 32)
+    dict(name="tile32", grid=(2, 16, 16), leaf=64, E=2, sink=1, tail=5, trim=19, seed=24, tile=32),
+    dict(name="max_mode", grid=(2, 16, 16), leaf=64, E=3, sink=0, tail=0, trim=0, seed=25, tile=32, order="kmeans"),
+    dict(name="tile32_g2", grid=(2, 16, 16), leaf=64, E=2, sink=0, tail=0, trim=45, seed=26, tile=32, group=2),
 ]
 
 
@@ -168,7 +172,7 @@ def run_case(flat, c):
     ws = {}
     cfg = dict(flat.PROD)
     cfg.update(leaf=c["leaf"], exact_leaves=c["E"], sink_leaves=c["sink"], tile_chunk=4096,
-               order=c.get("order", "seq"))
+               order=c.get("order", "seq"), tile=c.get("tile", 64))
     if c.get("group", 1) > 1:
         cfg["kern"] = {**cfg["kern"], "group": c["group"]}
     out = flat.flat_attention(q, k, v, tail=(tk, tv) if tk is not None else None, ws=ws, **cfg)
@@ -176,7 +180,7 @@ def run_case(flat, c):
     ti = rec["tile"]
     res = dict(q=q.float().numpy(), k=k.float().numpy(), v=v.float().numpy(),
                leaf=np.int64(c["leaf"]), exact_leaves=np.int64(c["E"]), sink_leaves=np.int64(c["sink"]),
-               group=np.int64(c.get("group", 1)),
+               group=np.int64(c.get("group", 1)), tile=np.int64(c.get("tile", 64)),
                mu=_cat(st, "mu").numpy(), g8=_cat(st, "g8").numpy(), sg=_cat(st, "sg").numpy(),
                lz=_cat(st, "lz").numpy(), vb=_cat(st, "vb").float().numpy(),
                excl=_cat(ti, "excl").numpy().astype(np.uint8), k8=ti[0]["k8"].numpy(),

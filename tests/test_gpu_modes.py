@@ -4,7 +4,8 @@ reference's fixtures, through the C ABI:
 * ``order="kmeans"`` (accurate / max modes, h3/htrc_flat.py:47-65, :146-147, :159-165): the device
   permutation against the reference's recorded one and the oracle's, then every stage after it;
 * ``kern={"group": G}`` (h3/htrc_flat.py:223-231): G consecutive tiles share one centre, far-field
-  state row and routing.
+  state row and routing;
+* ``tile=32`` (the max mode, h3/htrc_flat_runner.py:52): 32-row tiles, held as 64 rows.
 """
 import ctypes
 import math
@@ -56,8 +57,13 @@ def _device_perm(q, dtype):
     return perm.cpu().numpy().astype(np.int64)
 
 
-KMEANS_FIXTURES = ["kmeans", "kmeans_g2_tail", "kmeans_sampled"]
+KMEANS_FIXTURES = ["kmeans", "kmeans_g2_tail", "kmeans_sampled", "max_mode"]
 GROUP_FIXTURES = ["group2", "group4"]
+TILE32_FIXTURES = ["tile32", "tile32_g2"]
+
+
+def _tile(z):
+    return int(z["tile"]) if "tile" in z else 64
 
 
 @pytest.mark.parametrize("case", KMEANS_FIXTURES)
@@ -84,12 +90,12 @@ def test_kmeans_order_against_oracle(dev, grid, seed):
     assert bad.sum() <= max(2, n // 10000), bad.sum()
 
 
-def _check(out, lse, excl_dev, z_out, z_lse, z_excl, n, group, perm):
+def _check(out, lse, excl_dev, z_out, z_lse, z_excl, n, group, perm, tile=64):
     """Routing agreement >= 99.9% of (group, leaf) pairs; out max-abs on the rows of groups whose
     routing agrees (rows mapped through the permutation); log-Z mean-abs over all rows."""
     agree = (excl_dev == z_excl).mean()
     assert agree >= ROUTE_AGREE, agree
-    same_tile_rows = np.repeat((excl_dev == z_excl).all(1), 64 * group)[:n]
+    same_tile_rows = np.repeat((excl_dev == z_excl).all(1), tile * group)[:n]
     rows = np.arange(n) if perm is None else np.asarray(perm)[:n]
     o = out.cpu().numpy()
     err = np.abs(o[rows[same_tile_rows]] - z_out[rows[same_tile_rows]]).max()
@@ -98,7 +104,7 @@ def _check(out, lse, excl_dev, z_out, z_lse, z_excl, n, group, perm):
         assert np.abs(lse.cpu().numpy() - z_lse).mean() < LSE_TOL
 
 
-@pytest.mark.parametrize("case", GROUP_FIXTURES + KMEANS_FIXTURES)
+@pytest.mark.parametrize("case", GROUP_FIXTURES + KMEANS_FIXTURES + TILE32_FIXTURES)
 def test_end_to_end_against_reference_fixtures(dev, golden_cases, case):
     """The whole operator with kern group / order="kmeans" against outputs recorded from the reference."""
     import htrc_b200
@@ -112,11 +118,11 @@ def test_end_to_end_against_reference_fixtures(dev, golden_cases, case):
     g = int(z["group"])
     order = "kmeans" if "perm" in z else "seq"
     cfg = {**htrc_b200.PROD, "leaf": 64, "exact_leaves": int(z["exact_leaves"]), "sink_leaves": int(z["sink_leaves"]),
-           "order": order, "kern": {**htrc_b200.PROD["kern"], "group": g}}
+           "order": order, "kern": {**htrc_b200.PROD["kern"], "group": g}, "tile": _tile(z)}
     out, lse = htrc_b200.flat_attention(q, k, v, tail=tail, return_lse=True, **cfg)
     st = htrc_b200.run_stages(q, k, v, tail[0] if tail else None, tail[1] if tail else None,
                               exact_leaves=cfg["exact_leaves"], sink_leaves=cfg["sink_leaves"], group=g,
-                              order=htrc_b200.flat.order_code(order))
+                              order=htrc_b200.flat.order_code(order), tile=_tile(z))
     torch.cuda.synchronize()
     assert torch.equal(out, st["out"]) and torch.equal(lse, st["lse"])
     assert int(st["status"].item()) == 0
@@ -126,19 +132,25 @@ def test_end_to_end_against_reference_fixtures(dev, golden_cases, case):
         perm = _np(st["perm"]).astype(np.int64)
         assert np.array_equal(perm, z["perm"])
     nb = st["nb"]
-    _check(out, lse, _np(st["excl"])[:, :nb], z["out"], z.get("lse"), z["excl"], n, g, perm)
+    _check(out, lse, _np(st["excl"])[:, :nb], z["out"], z.get("lse"), z["excl"], n, g, perm, _tile(z))
 
 
-def _oracle_on_device_state(q, v, st, group, perm, tail=None):
+def _held(x, nt, tile):
+    """Device rows [nt * 64, ...] -> the oracle's [nt, tile, ...] (a 32-row tile is held as 64 rows)."""
+    x = _np(x)
+    return x.reshape(nt, 64, *x.shape[1:])[:, :tile]
+
+
+def _oracle_on_device_state(q, v, st, group, perm, tail=None, tile=64):
     """The oracle's far + near attention on the device's own stage outputs, in the caller's row order."""
     nb, kx = st["nb"], st["kx"]
     qf = q.float().numpy()
     if perm is not None:
         qf = qf[perm]
-    qt, _, n = O.tile_centres(qf, 64)
+    qt, _, n = O.tile_centres(qf, tile)
     nt = qt.shape[0]
-    out, lse = O.tile_attention(qt, _np(st["q8"]).reshape(nt, 64, 128), _np(st["sq"]).reshape(nt, 64),
-                                _np(st["dq8"]).reshape(nt, 64, 128), _np(st["sdq"]).reshape(nt, 64), _np(st["g8"]),
+    out, lse = O.tile_attention(qt, _held(st["q8"], nt, tile), _held(st["sq"], nt, tile),
+                                _held(st["dq8"], nt, tile), _held(st["sdq"], nt, tile), _np(st["g8"]),
                                 _np(st["sg"])[:, :nb], _np(st["lz"])[:, :nb], _np(st["vb"]), _np(st["excl"])[:, :nb],
                                 _np(st["idx"])[:, :kx], _np(st["k8"]), _np(st["ks"]), O.bf16_round(v.float().numpy()),
                                 64, 1 / math.sqrt(128), tail=tail, group=group)
@@ -150,10 +162,12 @@ def _oracle_on_device_state(q, v, st, group, perm, tail=None):
     return out, lse
 
 
-@pytest.mark.parametrize("grid,seed,E,group,trim,order", [
-    ((4, 16, 32), 91, 6, 2, 0, "seq"), ((4, 16, 32), 92, 6, 3, 70, "seq"), ((4, 16, 32), 93, 9, 4, 0, "seq"),
-    ((4, 16, 32), 94, 5, 1, 13, "kmeans"), ((4, 16, 32), 95, 8, 2, 0, "kmeans")])
-def test_stages_on_device_state(dev, grid, seed, E, group, trim, order):
+@pytest.mark.parametrize("grid,seed,E,group,trim,order,tile", [
+    ((4, 16, 32), 91, 6, 2, 0, "seq", 64), ((4, 16, 32), 92, 6, 3, 70, "seq", 64),
+    ((4, 16, 32), 93, 9, 4, 0, "seq", 64), ((4, 16, 32), 94, 5, 1, 13, "kmeans", 64),
+    ((4, 16, 32), 95, 8, 2, 0, "kmeans", 64), ((4, 16, 32), 96, 6, 1, 11, "seq", 32),
+    ((4, 16, 32), 97, 7, 2, 40, "kmeans", 32)])
+def test_stages_on_device_state(dev, grid, seed, E, group, trim, order, tile):
     """Group centres and query codes bit-exact; fed the device's own state, selection and routing equal
     the oracle's formulas bit for bit and far + near attention matches the oracle."""
     import htrc_b200
@@ -161,21 +175,24 @@ def test_stages_on_device_state(dev, grid, seed, E, group, trim, order):
     if trim:
         q = q[:-trim]
     oc = htrc_b200.flat.order_code(order)
-    st = htrc_b200.run_stages(q.to(dev), k.to(dev), v.to(dev), exact_leaves=E, group=group, order=oc)
+    st = htrc_b200.run_stages(q.to(dev), k.to(dev), v.to(dev), exact_leaves=E, group=group, order=oc, tile=tile)
     torch.cuda.synchronize()
     assert int(st["status"].item()) == 0
     perm = _np(st["perm"]).astype(np.int64) if order == "kmeans" else None
     if perm is not None:
         assert np.array_equal(np.sort(perm), np.arange(q.shape[0]))
     qf = q.float().numpy() if perm is None else q.float().numpy()[perm]
-    qt, mu1, _ = O.tile_centres(qf, 64)
+    qt, mu1, _ = O.tile_centres(qf, tile)
     mu = O.group_centres(qt, group) if group > 1 else mu1
     assert np.array_equal(_np(st["mu"]).view(np.uint32), mu.view(np.uint32))
     nt, nb = qt.shape[0], st["nb"]
     q8, sq, dq8, sdq = O.query_codes(qt, mu[np.arange(nt) // group])
-    assert np.array_equal(_np(st["q8"]).reshape(nt, 64, 128), q8)
-    assert np.array_equal(_np(st["dq8"]).reshape(nt, 64, 128), dq8)
-    assert np.array_equal(_np(st["sdq"]).reshape(nt, 64).view(np.uint32), sdq.view(np.uint32))
+    assert np.array_equal(_held(st["q8"], nt, tile), q8)
+    assert np.array_equal(_held(st["dq8"], nt, tile), dq8)
+    assert np.array_equal(_held(st["sdq"], nt, tile).view(np.uint32), sdq.view(np.uint32))
+    if tile == 32:                                   # held rows 32..63 repeat row 31
+        held = _np(st["dq8"]).reshape(nt, 64, 128)
+        assert (held[:, 32:] == held[:, 31:32]).all()
     gt = np.arange(nt) // group
     g8, sg, lz = _np(st["g8"]), _np(st["sg"])[:, :nb], _np(st["lz"])[:, :nb]
     per_tile = O.rowmax_select(dq8, sdq, g8[gt], sg[gt], lz[gt])
@@ -184,43 +201,48 @@ def test_stages_on_device_state(dev, grid, seed, E, group, trim, order):
     idx, excl = O.route(sel, E)
     assert np.array_equal(_np(st["idx"])[:, :idx.shape[1]], idx)
     assert np.array_equal(_np(st["excl"])[:, :nb], excl)
-    out, lse = _oracle_on_device_state(q, v, st, group, perm)
+    out, lse = _oracle_on_device_state(q, v, st, group, perm, tile=tile)
     assert np.abs(_np(st["out"]) - out).max() < OUT_TOL
     assert np.abs(_np(st["lse"]) - lse).mean() < LSE_TOL
 
 
-@pytest.mark.parametrize("group,order,chunk", [(2, "seq", 6), (3, "seq", 7), (1, "kmeans", 10), (4, "kmeans", 9)])
-def test_chunked_forward_equals_staged(dev, group, order, chunk):
+@pytest.mark.parametrize("group,order,chunk,tile", [(2, "seq", 6, 64), (3, "seq", 7, 64), (1, "kmeans", 10, 64),
+                                                     (4, "kmeans", 9, 64), (1, "seq", 5, 32), (2, "kmeans", 8, 32)])
+def test_chunked_forward_equals_staged(dev, group, order, chunk, tile):
     """The single-call forward with chunked state (groups per chunk = tile_chunk // G) equals the staged
     path; the tail partial is read in the caller's row order."""
     import htrc_b200
     q, k, v = _inputs((4, 16, 40), 101)
     tk, tv = k[-9:].float().to(dev), v[-9:].float().to(dev)
     qd, kd, vd = q.to(dev), k[:-64].to(dev), v[:-64].to(dev)
-    cfg = {**htrc_b200.PROD, "leaf": 64, "exact_leaves": 5, "order": order,
+    cfg = {**htrc_b200.PROD, "leaf": 64, "exact_leaves": 5, "order": order, "tile": tile,
            "kern": {**htrc_b200.PROD["kern"], "group": group}}
     a, la = htrc_b200.flat_attention(qd, kd, vd, tail=(tk, tv), return_lse=True, **{**cfg, "tile_chunk": 0})
     b, lb = htrc_b200.flat_attention(qd, kd, vd, tail=(tk, tv), return_lse=True, **{**cfg, "tile_chunk": chunk})
-    st = htrc_b200.run_stages(qd, kd, vd, tk, tv, exact_leaves=5, group=group, order=htrc_b200.flat.order_code(order))
+    st = htrc_b200.run_stages(qd, kd, vd, tk, tv, exact_leaves=5, group=group, order=htrc_b200.flat.order_code(order),
+                              tile=tile)
     torch.cuda.synchronize()
     assert torch.equal(a, b) and torch.equal(la, lb)
     assert torch.equal(a, st["out"]) and torch.equal(la, st["lse"])
     perm = _np(st["perm"]).astype(np.int64) if order == "kmeans" else None
-    out, lse = _oracle_on_device_state(q, v[:-64], st, group, perm, tail=(tk.cpu().numpy(), tv.cpu().numpy()))
+    out, lse = _oracle_on_device_state(q, v[:-64], st, group, perm, tail=(tk.cpu().numpy(), tv.cpu().numpy()),
+                                       tile=tile)
     assert np.abs(a.cpu().numpy() - out).max() < OUT_TOL
 
 
-def test_runner_accurate_mode(dev):
-    """FlatRunner(mode="accurate"): k-means order with 1024 routed leaves, captured in a CUDA graph."""
+@pytest.mark.parametrize("mode", ["accurate", "max"])
+def test_runner_kmeans_modes(dev, mode):
+    """FlatRunner(mode="accurate" / "max"): k-means order with 1024 routed leaves (tile 64 / 32),
+    captured in a CUDA graph."""
     import htrc_b200
     from htrc_b200 import runner
     q, k, v = _inputs((8, 32, 48), 111)
     n = q.shape[0]
-    r = runner.FlatRunner(n, n, mode="accurate", lse=True)
+    r = runner.FlatRunner(n, n, mode=mode, lse=True)
     assert r.graph is not None, r.graph_error
     out, lse = r.head(q.to(dev), k.to(dev), v.to(dev))
     ref, rl = htrc_b200.flat_attention(q.to(dev), k.to(dev), v.to(dev), return_lse=True,
-                                       **{**htrc_b200.PROD, **runner.MODES["accurate"], "leaf": 64})
+                                       **{**htrc_b200.PROD, **runner.MODES[mode], "leaf": 64})
     torch.cuda.synchronize()
     assert torch.equal(out, ref) and torch.equal(lse, rl)
     r.check_status()

@@ -67,6 +67,8 @@ def test_workspace_size_validation():
     assert size(_args(dim=64)) == _lib.HTRC_ERR_UNSUPPORTED
     assert size(_args(leaf=32)) == _lib.HTRC_ERR_UNSUPPORTED
     assert size(_args(tile=128)) == _lib.HTRC_ERR_UNSUPPORTED
+    assert size(_args(tile=16)) == _lib.HTRC_ERR_UNSUPPORTED
+    assert size(_args(tile=32)) == _lib.HTRC_OK                        # the "max" mode
     assert size(_args(E=-1)) == _lib.HTRC_ERR_ARG
     assert size(_args(m=64 * 9000)) == _lib.HTRC_ERR_UNSUPPORTED      # more leaves than the route kernel handles
     assert size(_args(m=64 * 2048, E=2000)) == _lib.HTRC_ERR_UNSUPPORTED  # more routed leaves than the tile kernel
@@ -132,8 +134,8 @@ def test_flat_attention_argument_errors_match_the_reference():
 def test_flat_attention_unimplemented_configurations_say_so():
     q, k, v = _qkv()
     cfg = dict(htrc_b200.PROD, leaf=64)
-    with pytest.raises(NotImplementedError, match="tile=64"):
-        htrc_b200.flat_attention(q, k, v, **{**cfg, "order": "kmeans", "tile": 32})   # the "max" mode
+    with pytest.raises(NotImplementedError, match="tile=64 or 32"):
+        htrc_b200.flat_attention(q, k, v, **{**cfg, "tile": 16})
     with pytest.raises(NotImplementedError, match="leaf"):
         htrc_b200.flat_attention(q, k, v, **{**cfg, "leaf": 32})
     with pytest.raises(NotImplementedError):
@@ -145,7 +147,8 @@ def test_flat_attention_unimplemented_configurations_say_so():
 def test_orders_and_groups_need_no_cpu_path_either():
     q, k, v = _qkv()
     cfg = dict(htrc_b200.PROD, leaf=64)
-    for over in ({"order": "kmeans"}, {"kern": {"group": 2}}, {"order": "kmeans", "kern": {"group": 4}}):
+    for over in ({"order": "kmeans"}, {"kern": {"group": 2}}, {"order": "kmeans", "kern": {"group": 4}},
+                 {"order": "kmeans", "tile": 32}):
         with pytest.raises(ValueError, match="CUDA tensors"):
             htrc_b200.flat_attention(q, k, v, **{**cfg, **over})
 

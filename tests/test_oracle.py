@@ -6,10 +6,10 @@ import pytest
 from oracle import flat_oracle as O
 
 CASES = ["base", "ragged", "sink_tail", "all_exact", "no_exact", "big_tail", "leaf32", "wide",
-         "group2", "group4", "kmeans", "kmeans_g2_tail", "kmeans_sampled"]
+         "group2", "group4", "kmeans", "kmeans_g2_tail", "kmeans_sampled", "tile32", "max_mode", "tile32_g2"]
 SLIM = {"kmeans_sampled"}                      # no recorded per-(tile, leaf) state
 STATE_CASES = [c for c in CASES if c not in SLIM]
-KMEANS_CASES = ["kmeans", "kmeans_g2_tail", "kmeans_sampled"]
+KMEANS_CASES = ["kmeans", "kmeans_g2_tail", "kmeans_sampled", "max_mode"]
 
 
 def _group(z):
@@ -24,7 +24,7 @@ def _stages(z):
     return O.flat_attention(z["q"], z["k"], z["v"], leaf=int(z["leaf"]),
                             exact_leaves=int(z["exact_leaves"]), sink_leaves=int(z["sink_leaves"]),
                             tail=tail, return_stages=True, group=_group(z), order=order,
-                            perm=z.get("perm")), tail
+                            perm=z.get("perm"), tile=int(z["tile"]) if "tile" in z else 64), tail
 
 
 def _tile_mu(z, nt):
