@@ -58,6 +58,7 @@ def parse():
     ap.add_argument("--cpu-tiles", type=int, default=4, help="tiles of the CPU-baseline sample")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-modes", action="store_true", help="skip the per-mode head timings")
     return ap.parse_args()
 
 
@@ -364,6 +365,55 @@ def run_ours(a, wl, rank, world, local_rank):
                "api": "htrc_b200.forward_into, pinned host q/k/v in and out/lse back, copies overlapped on "
                       "2 copy streams", "matches_device_run": same}
 
+    # ---- the reference runner's modes on head 0 (rank 0, one GPU): ms per head through FlatRunner's
+    # CUDA graph (static-buffer copies included), and the k-means ordering alone
+    modes = None
+    if rank == 0 and world == 1 and not a.no_modes:
+        from htrc_b200 import runner as R
+        h0 = my_heads[0]
+        modes = {}
+        for mode in R.MODES:
+            r = R.FlatRunner(n, m, mode=mode, device=dev)
+            if r.graph is None:
+                modes[mode] = f"graph capture failed: {r.graph_error}"
+                continue
+            for _ in range(2):
+                r.head(*dq[h0])
+            torch.cuda.synchronize(dev)
+            m0, m1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            m0.record(comp)
+            for _ in range(3):
+                r.head(*dq[h0])
+            m1.record(comp)
+            torch.cuda.synchronize(dev)
+            r.check_status()
+            modes[mode] = m0.elapsed_time(m1) / 3
+            r.close()
+            del r
+        import ctypes
+
+        from htrc_b200 import _lib
+        kb = ctypes.c_size_t()
+        _lib.check(_lib.lib().htrc_kmeans_scratch_size(n, kb), "kmeans scratch")
+        kscr = torch.empty(int(kb.value), dtype=torch.uint8, device=dev)
+        perm = torch.empty((n,), dtype=torch.int32, device=dev)
+
+        def km():
+            _lib.check(_lib.lib().htrc_kmeans_order(_lib.ptr(dq[h0][0]), _lib.DTYPE_BF16, n, 128, _lib.ptr(perm),
+                                                    _lib.ptr(kscr), int(kb.value), _lib.stream_ptr()), "kmeans")
+        km()
+        torch.cuda.synchronize(dev)
+        k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        k0.record(comp)
+        for _ in range(5):
+            km()
+        k1.record(comp)
+        torch.cuda.synchronize(dev)
+        modes = {"ms_per_head": modes, "kmeans_order_ms": k0.elapsed_time(k1) / 5,
+                 "note": "head 0 of the workload through FlatRunner (CUDA graph) per mode of "
+                         "h3/htrc_flat_runner.py:48-53: fast E=256, balanced E=512, accurate E=1024 + k-means, "
+                         "max E=1024 + k-means + 32-row tiles"}
+
     # ---- roofline of the dominant kernel (tile attention) from the live events
     peaks, peak_src = measured_peaks()
     npad = nt * 64
@@ -392,7 +442,8 @@ def run_ours(a, wl, rank, world, local_rank):
                            "exact_leaves": E, "heads_per_gpu": len(my_heads),
                            "l2": "inputs larger than L2: 2.4 GB of distinct q/k/v per layer, 1.6 GB leaf state per head",
                            "parallelism": f"heads/{world}" + (" + bf16 output all_gather (NCCL)" if world > 1 else "")},
-                "stage_ms_per_head": stage_ms, **parity, "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
+                "stage_ms_per_head": stage_ms, "modes": modes, **parity, "roofline": roof, "cpu_baseline": cpu,
+                "e2e": e2e,
                 "gpu_launches": a.steps * len(my_heads) * LAUNCHES_PER_HEAD, "clocks": clk}
         print(json.dumps(line), flush=True)
 

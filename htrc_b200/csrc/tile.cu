@@ -25,7 +25,8 @@
 // different roles serialises them, since a lane suspended in an mbarrier wait holds up the others.
 //
 // Tiles of 32 rows (the "max" mode, h3/htrc_flat_runner.py:52) are held as 64 rows whose rows 32..63
-// repeat row 31; only rows < 32 are written.
+// repeat row 31; only rows < 32 are written, and the softmax warps that own only such rows skip the
+// arithmetic (they keep their place in the barrier protocol and leave P = 0).
 //
 // Groups (h3/htrc_flat.py:223-231): G consecutive tiles share one far-field state row and one routing;
 // tile t of the chunk reads state row t / G.  k-means order (:146-147, :159-165): tile row i is query
@@ -92,6 +93,7 @@ __device__ __forceinline__ float ex2(float x) {
 
 }  // namespace
 
+template <int TROWS>
 __global__ void __launch_bounds__(kThreads, 1)
     tile_attention_kernel(const __grid_constant__ CUtensorMap tm_q8, const __grid_constant__ CUtensorMap tm_dq8,
                           const __grid_constant__ CUtensorMap tm_g8, const __grid_constant__ CUtensorMap tm_vb,
@@ -99,7 +101,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                           const __grid_constant__ CUtensorMap tm_excl, const __grid_constant__ CUtensorMap tm_k8,
                           const __grid_constant__ CUtensorMap tm_v, const float* __restrict__ sq,
                           const float* __restrict__ sdq, const float* __restrict__ ks, const int32_t* __restrict__ idx,
-                          int kx, int nb, int nf, int64_t n, int trows, int64_t t0, int64_t tc, int group,
+                          int kx, int nb, int nf, int64_t n, int64_t t0, int64_t tc, int group,
                           float scale,
                           const float* __restrict__ tail_part, const int32_t* __restrict__ perm,
                           float* __restrict__ out, float* __restrict__ lse, int* status) {
@@ -324,6 +326,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int col = x * 64 + r;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const bool has_tile = x < ntiles;
+    const bool warp_rows = quarter * 16 < TROWS;   // warp-uniform: false for the held copies of row 31
     const int64_t tl = tlocA + x;
     const int64_t gr = (t0 + tl) * 64 + r;
     const float sq_r = has_tile ? __ldg(sq + gr) : 0.f;
@@ -336,6 +339,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait_warp(&bars->s_full[b], (j >> 2) & 1, status, abort_flag)) { aborted = true; break; }
       __syncwarp();
       tc_fence_after();
+      if (TROWS < 64 && !warp_rows) {
+        // held copies only: consume the step's constants in order and write P = 0 after QK(j)
+        if (!mbar_wait_warp(&bars->cc_full[s], (j / kXSlots) & 1, status, abort_flag)) { aborted = true; break; }
+        mbar_arrive(&bars->cc_empty[s]);
+        uint32_t z[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) z[i] = 0u;
+        tmem_st32(tmem + lane_base + kColS + 64 * b, z);
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&bars->p_full[b]);
+        continue;
+      }
       uint32_t d0[32], d1[32];
       tmem_ld32(tmem + lane_base + kColS + 64 * b, d0);
       tmem_ld32(tmem + lane_base + kColS + 64 * b + 32, d1);
@@ -426,8 +442,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float m1 = m1s[col], l1 = l1s[col];
       const float m0 = kcount ? m_used : -INFINITY;
       const float n0 = m0 * kLn2, n1 = m1 * kLn2;           // natural-log units
-      const int64_t li = (t0 + tl) * trows + r;                  // query index in tile order
-      const bool valid = has_tile && r < trows && li < n;
+      const int64_t li = (t0 + tl) * TROWS + r;                  // query index in tile order
+      const bool valid = has_tile && r < TROWS && li < n;
       const int64_t orow = (perm != nullptr && valid) ? static_cast<int64_t>(__ldg(perm + li)) : li;
       const float* tp = (tail_part != nullptr && valid) ? tail_part + orow * 130 : nullptr;
       const float mt = tp ? tp[128] : -INFINITY, lt = tp ? tp[129] : 0.f;
@@ -481,18 +497,19 @@ int launch_tile_attention(const TileMaps& maps, const float* sq, const float* sd
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr_done[dev]) {
-    if (cudaFuncSetAttribute(tile_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
-        cudaSuccess)
+    if (cudaFuncSetAttribute(tile_attention_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(tile_attention_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
+            cudaSuccess)
       return HTRC_ERR_CUDA;
     attr_done[dev] = true;
   }
   const int nf = kx >= nb ? 0 : (nb + 63) / 64;
   const unsigned grid = static_cast<unsigned>((tc + 1) / 2);
-  tile_attention_kernel<<<grid, kThreads, kSmemBytes, st>>>(maps.q8, maps.dq8, maps.g8, maps.vb, maps.lz, maps.sg,
-                                                            maps.excl, maps.k8, maps.v, sq, sdq, ks, idx, kx, nb, nf,
-                                                            n, tile_rows == 32 ? 32 : 64, t0, tc,
-                                                            group > 1 ? group : 1, scale, tail_part,
-                                                            perm, out, lse, status);
+  auto kernel = tile_rows == 32 ? tile_attention_kernel<32> : tile_attention_kernel<64>;
+  kernel<<<grid, kThreads, kSmemBytes, st>>>(maps.q8, maps.dq8, maps.g8, maps.vb, maps.lz, maps.sg, maps.excl, maps.k8,
+                                             maps.v, sq, sdq, ks, idx, kx, nb, nf, n, t0, tc, group > 1 ? group : 1,
+                                             scale, tail_part, perm, out, lse, status);
   return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
 }
 

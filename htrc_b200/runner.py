@@ -54,7 +54,10 @@ def plan_chunk(free_bytes: int, keys: int, tile: int, splits: int = 8, order: st
     """Largest tile chunk whose predicted peak fits in ``free_bytes`` (h3/htrc_flat_runner.py:71-84);
     raises MemoryError when even the smallest chunk does not fit."""
     nt = -(-int(queries) // int(tile)) if queries else 0
-    for c in CHUNKS:
+    # the whole sequence in one chunk first: one launch per stage, and the tile kernel's grid covers every
+    # SM (a chunk of 128 tiles is 64 CTAs on 148 SMs)
+    cands = ((nt,) if nt > CHUNKS[0] else ()) + CHUNKS
+    for c in cands:
         eff = min(c, nt) if nt else c
         if predicted_peak_mib(keys, tile, eff, splits, leaf, order=order, graph=graph, queries=queries,
                               exact_leaves=exact_leaves, group=group) * 2 ** 20 <= free_bytes:
@@ -89,6 +92,10 @@ class FlatRunner:
         self.group = _flat.group_of(base.get("kern"))
         self.order = _flat.order_code(base["order"])
         if tile_chunk is None:
+            if free_bytes is None and self.device.type == "cuda" and torch.cuda.is_available():
+                # plan from the device's free memory (the reference falls back to PROD's 128-tile chunk,
+                # sized for a 16 GB card; the chunk size changes no result)
+                free_bytes = int(torch.cuda.mem_get_info(self.device)[0] * 0.8)
             if free_bytes is not None:
                 tile_chunk = plan_chunk(free_bytes, keys, base["tile"], base.get("splits", 8), base["order"],
                                         use_graph, queries=int(queries), exact_leaves=base["exact_leaves"],

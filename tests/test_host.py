@@ -200,3 +200,6 @@ def test_plan_chunk_takes_the_largest_chunk_that_fits():
         assert got == max(x for x in runner.CHUNKS if peaks[x] * 2 ** 20 <= free)
     with pytest.raises(MemoryError):
         runner.plan_chunk(1 << 20, keys, 64, queries=q)
+    # with room for it, the whole sequence is one chunk (2016 tiles: every SM busy in one launch)
+    assert runner.plan_chunk(1 << 40, keys, 64, queries=q) == -(-q // 64)
+    assert runner.plan_chunk(1 << 40, 4096, 64, queries=4096) == 1024       # <= 1024 tiles: as the reference
