@@ -33,20 +33,33 @@ __device__ __forceinline__ uint32_t pack_i8x4(int a, int b, int c, int d) {
          ((static_cast<uint32_t>(c) & 0xFFu) << 16) | ((static_cast<uint32_t>(d) & 0xFFu) << 24);
 }
 
-// x8 codes of 4 values given the row scale s; ROUND 0 = half-even + clamp, 1 = half-away
+// INT8 code of v / s (s > 0, |v / s| <= 127 + rounding): ROUND 1 = the reference's half-away
+// trunc(fl(fl(v / s) +- 0.5)), ROUND 0 = half-even rint(fl(v / s)) clamped to +-127.  The quotient is
+// taken as v * r with r = 1/s correctly rounded (within 2^-22 relative of v / s, so within 4e-5 of it
+// for |v / s| < 128) and the code is read from it, unless it lies within 2^-12 of a rounding boundary
+// k + 1/2, where the correctly rounded quotient and the reference's formula decide.  Away from the
+// boundaries both rounding modes give the nearest integer.  No transcendental-unit instruction on the
+// fast path: floor and nearest integer come from adding 2^23 (toward zero / to nearest).
 template <int ROUND>
-__device__ __forceinline__ uint32_t quant4(const float (&v)[4], float s) {
+__device__ __forceinline__ int quant_code(float v, float s, float r) {
+  const float ya = __fmul_rn(v, r);
+  const float h = __fadd_rn(fabsf(ya), 0.5f);                          // boundaries -> integers
+  const float n = __fsub_rn(__fadd_rn(h, 12582912.0f), 12582912.0f);   // nearest integer to h
+  if (fabsf(__fsub_rn(h, n)) < 2.44140625e-4f) {
+    const float y = __fdiv_rn(v, s);
+    if (ROUND == 0) return max(-127, min(127, static_cast<int>(rintf(y))));
+    return round_half_away_i8(y);
+  }
+  const int k = min(127, __float_as_int(__fadd_rz(h, 8388608.0f)) - 0x4B000000);   // floor(h)
+  return ya < 0.f ? -k : k;
+}
+
+// x8 codes of 4 values given the row scale s and its reciprocal r
+template <int ROUND>
+__device__ __forceinline__ uint32_t quant4(const float (&v)[4], float s, float r) {
   int c[4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    float y = __fdiv_rn(v[i], s);
-    if (ROUND == 0) {
-      int r = static_cast<int>(rintf(y));
-      c[i] = max(-127, min(127, r));
-    } else {
-      c[i] = round_half_away_i8(y);
-    }
-  }
+  for (int i = 0; i < 4; ++i) c[i] = quant_code<ROUND>(v[i], s, r);
   return pack_i8x4(c[0], c[1], c[2], c[3]);
 }
 }  // namespace
@@ -63,7 +76,7 @@ __global__ void __launch_bounds__(256) pack_rows_kernel(const T* __restrict__ x,
   float am = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
   am = warp_max(am);
   const float s = fmaxf(__fmul_rn(am, kInv127), 1e-20f);
-  reinterpret_cast<uint32_t*>(x8 + row * 128)[lane] = quant4<ROUND>(v, s);
+  reinterpret_cast<uint32_t*>(x8 + row * 128)[lane] = quant4<ROUND>(v, s, __frcp_rn(s));
   if (lane == 0) scale[row] = s;
 }
 
@@ -144,13 +157,19 @@ __global__ void __launch_bounds__(128) tile_prep_kernel(const T* __restrict__ q,
   const int64_t r0 = static_cast<int64_t>(t) * 64;              // first of the tile's 64 held rows
   const int64_t first = static_cast<int64_t>(t) * trows;         // its first query (in tile order)
   const int nreal = static_cast<int>(n - first < trows ? n - first : trows);
-  // stage the tile: warp w loads rows w, w+4, ...; lane owns 4 columns
+  // stage the tile: warp w loads rows w, w+4, ...; lane owns 4 columns; all 16 loads of a warp in flight
   const int warp = tid >> 5, lane = tid & 31;
-  for (int r = warp; r < 64; r += 4) {
-    float v[4];
-    load4<T>(q + source_row(perm, n, trows, t, r) * 128 + lane * 4, v);
+  {
+    int64_t src[16];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) qs[r][lane * 4 + i] = v[i];
+    for (int i = 0; i < 16; ++i) src[i] = source_row(perm, n, trows, t, warp + 4 * i);
+    float v[16][4];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) load4<T>(q + src[i] * 128 + lane * 4, v[i]);
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) qs[warp + 4 * i][lane * 4 + c] = v[i][c];
   }
   __syncthreads();
   if (group <= 1) {
@@ -167,6 +186,7 @@ __global__ void __launch_bounds__(128) tile_prep_kernel(const T* __restrict__ q,
   float m4[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) m4[i] = mus[lane * 4 + i];
+#pragma unroll 4
   for (int r = warp; r < 64; r += 4) {
     float v[4], d[4];
 #pragma unroll
@@ -181,8 +201,8 @@ __global__ void __launch_bounds__(128) tile_prep_kernel(const T* __restrict__ q,
     const float s_q = fmaxf(__fmul_rn(aq, kInv127), 1e-20f);
     const float s_d = fmaxf(__fmul_rn(ad, kInv127), 1e-20f);
     const int64_t gr = r0 + r;
-    reinterpret_cast<uint32_t*>(q8 + gr * 128)[lane] = quant4<1>(v, s_q);
-    reinterpret_cast<uint32_t*>(dq8 + gr * 128)[lane] = quant4<1>(d, s_d);
+    reinterpret_cast<uint32_t*>(q8 + gr * 128)[lane] = quant4<1>(v, s_q, __frcp_rn(s_q));
+    reinterpret_cast<uint32_t*>(dq8 + gr * 128)[lane] = quant4<1>(d, s_d, __frcp_rn(s_d));
     if (lane == 0) {
       sq[gr] = s_q;
       sdq[gr] = s_d;

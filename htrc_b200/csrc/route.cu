@@ -12,7 +12,7 @@
 namespace htrc {
 
 namespace {
-constexpr int kThreads = 256;
+constexpr int kThreads = 256;       // also the number of radix bins (one per thread)
 constexpr int kMaxLeaves = 8192;
 
 __device__ __forceinline__ uint32_t order_key(float f) {
@@ -82,7 +82,7 @@ __global__ void __launch_bounds__(kThreads)
   __syncthreads();
   uint32_t mask = 0;
   for (int shift = 24; shift >= 0; shift -= 8) {
-    for (int i = tid; i < 256; i += kThreads) hist[i] = 0;
+    hist[tid] = 0;                                   // kThreads == 256 bins
     __syncthreads();
     const uint32_t prefix = s_prefix;
     for (int l = tid; l < nb; l += kThreads) {
@@ -90,14 +90,15 @@ __global__ void __launch_bounds__(kThreads)
       if ((k & mask) == prefix) atomicAdd(&hist[(k >> shift) & 0xFF], 1);
     }
     __syncthreads();
-    if (tid == 0) {
-      int rem = s_remaining, above = 0, d = 255;
-      for (; d > 0; --d) {
-        if (above + hist[d] >= rem) break;
-        above += hist[d];
-      }
+    // thread t holds digit 255 - t: an inclusive scan gives the count of candidates with a digit >= it;
+    // the digit of the kx-th largest is the one where that count first reaches the remaining rank
+    const int rem = s_remaining;
+    const int c = hist[255 - tid];
+    int tot;
+    const int above = block_exclusive_scan(c, scratch, &tot);      // candidates with a larger digit
+    if (above < rem && above + c >= rem) {
       s_remaining = rem - above;
-      s_prefix = prefix | (static_cast<uint32_t>(d) << shift);
+      s_prefix = prefix | (static_cast<uint32_t>(255 - tid) << shift);
     }
     mask |= 0xFFu << shift;
     __syncthreads();
