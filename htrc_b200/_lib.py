@@ -13,6 +13,7 @@ LIB_PATH = Path(__file__).with_name("libhtrc_flat.so")
 HTRC_OK, HTRC_ERR_ARG, HTRC_ERR_UNSUPPORTED, HTRC_ERR_WORKSPACE, HTRC_ERR_CUDA, HTRC_ERR_DEVICE, HTRC_ERR_TOO_LARGE = range(7)
 DTYPE_F32, DTYPE_BF16 = 0, 1
 ORDER_SEQ, ORDER_KMEANS = 0, 1
+FQ_FORMATS = {"int8": 1, "int4": 2, "fp8": 3, "fp4": 4}
 ROUND_HALF_EVEN, ROUND_HALF_AWAY = 0, 1
 STATUS_BITS = {1: "bounded wait gave up", 2: "routed leaf index out of range", 4: "non-finite log-partition"}
 
@@ -53,6 +54,8 @@ SIGNATURES = {
                                            _i64, _p, _p, _p, _i64, _i32, _i32, _f32, _p, _p, _p, _p, _p, _p]),
     "htrc_tail_partial": (ctypes.c_int, [_p, _i32, _i64, _i32, _p, _p, _i32, _f32, _p, _p]),
     "htrc_flat_forward_static_ws": (ctypes.c_int, [ctypes.POINTER(HtrcFlatArgs), _p]),
+    "htrc_fake_quant": (ctypes.c_int, [_p, _i32, _i64, _i32, _i32, _i32, _p, _i32, _p]),
+    "htrc_dequant_rows": (ctypes.c_int, [_p, _i64, _p, _i64, _i64, _i32, _p, _p]),
     "htrc_strerror": (ctypes.c_char_p, [ctypes.c_int]),
 }
 

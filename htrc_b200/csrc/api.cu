@@ -488,6 +488,32 @@ int htrc_tail_partial(const void* q, int32_t q_dtype, int64_t n_queries, int32_t
   return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
 }
 
+int htrc_fake_quant(const void* x, int32_t x_dtype, int64_t rows, int32_t dim, int32_t fmt, int32_t group, void* out,
+                    int32_t out_dtype, htrc_stream_t stream) {
+  if (!x || !out || rows < 1 || group < 0) return HTRC_ERR_ARG;
+  if (fmt < HTRC_FQ_INT8 || fmt > HTRC_FQ_FP4) return HTRC_ERR_ARG;
+  if (x_dtype != HTRC_DTYPE_F32 && x_dtype != HTRC_DTYPE_BF16) return HTRC_ERR_ARG;
+  if (out_dtype != HTRC_DTYPE_F32 && out_dtype != HTRC_DTYPE_BF16) return HTRC_ERR_ARG;
+  if (dim != kDim) return HTRC_ERR_UNSUPPORTED;
+  const int gsz = group == 0 ? (fmt == HTRC_FQ_FP4 ? 16 : dim) : group;
+  if (gsz > dim || dim % gsz || (gsz & (gsz - 1))) return HTRC_ERR_ARG;   // the reference: group divides D
+  int rc = check_device();
+  if (rc != HTRC_OK) return rc;
+  launch_fake_quant(x, x_dtype, rows, fmt, gsz, out, out_dtype, reinterpret_cast<cudaStream_t>(stream));
+  return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
+}
+
+int htrc_dequant_rows(const uint8_t* x8, int64_t stride_x, const float* scale, int64_t stride_s, int64_t rows,
+                      int32_t dim, uint16_t* out, htrc_stream_t stream) {
+  if (!x8 || !scale || !out || rows < 1 || stride_x < dim || stride_s < 0) return HTRC_ERR_ARG;
+  if (dim != kDim) return HTRC_ERR_UNSUPPORTED;
+  if ((stride_x & 3) || (reinterpret_cast<uintptr_t>(x8) & 3)) return HTRC_ERR_ARG;
+  int rc = check_device();
+  if (rc != HTRC_OK) return rc;
+  launch_dequant_rows(x8, stride_x, scale, stride_s, rows, out, reinterpret_cast<cudaStream_t>(stream));
+  return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
+}
+
 const char* htrc_strerror(int code) {
   switch (code) {
     case HTRC_OK: return "ok";

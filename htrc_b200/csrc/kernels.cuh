@@ -37,6 +37,10 @@ void launch_tile_prep(const void* q, int dtype, int64_t n, int tile_rows, const 
                       uint16_t* mu_hi, uint16_t* mu_lo, int8_t* q8, float* sq, int8_t* dq8, float* sdq, cudaStream_t st);
 size_t kmeans_scratch_bytes(int64_t n);
 int launch_kmeans_order(const void* q, int dtype, int64_t n, int32_t* perm, void* scratch, cudaStream_t st);
+void launch_fake_quant(const void* x, int x_dtype, int64_t rows, int fmt, int gsz, void* out, int out_dtype,
+                       cudaStream_t st);
+void launch_dequant_rows(const uint8_t* x8, int64_t stride_x, const float* scale, int64_t stride_s, int64_t rows,
+                         uint16_t* out, cudaStream_t st);
 void launch_tail_partial(const void* q, int dtype, int64_t n, const float* tk, const float* tv, int n_tail, float scale,
                          float* part, cudaStream_t st);
 int launch_leaf_stats(const LeafStatsMaps& maps, float* sg, float* lz, int64_t pitch, int64_t t0, int64_t tc, int nb,

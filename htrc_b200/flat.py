@@ -92,8 +92,9 @@ def _check_args(q, k, v, tile, exact_leaves, order, curvature, leaf, select, bac
         raise NotImplementedError(f"the kernels implement tile=64 or 32, leaf={LEAF} (got tile={tile}, leaf={leaf})")
     if int(sel_stride) != 1:
         raise NotImplementedError("sel_stride != 1 is not implemented")
-    if quant:
-        raise NotImplementedError("fake-quant simulation (quant=...) is not implemented")
+    for key in ("kv", "q"):
+        if (quant or {}).get(key) and quant[key] not in _lib.FQ_FORMATS:
+            raise ValueError(f"unknown quant format {quant[key]}")
     if q.dim() != 2 or k.dim() != 2 or v.dim() != 2 or int(q.shape[1]) != DIM or k.shape != v.shape or \
             int(k.shape[1]) != DIM:
         raise ValueError(f"q [N, {DIM}], k/v [M, {DIM}] expected")
@@ -101,7 +102,51 @@ def _check_args(q, k, v, tile, exact_leaves, order, curvature, leaf, select, bac
         raise ValueError("q, k, v must be CUDA tensors (there is no CPU path)")
 
 
-def _prep_inputs(q, k, v, tail):
+def fake_quant(x, fmt, group=0, out_dtype=torch.float32):
+    """Round-trip x [..., 128] (CUDA, f32 or bf16) through a low-bit format with symmetric per-group
+    scales (group 0: one scale per row; fp4: 16) -- h3/htrc_flat.py:68-97, on the device.  fmt: int8,
+    int4, fp8 (e4m3), fp4 (e2m1).  Returns float32 like the reference (or ``out_dtype``)."""
+    if fmt not in _lib.FQ_FORMATS:
+        raise ValueError(f"unknown quant format {fmt}")
+    d = int(x.shape[-1])
+    gsz = int(group) if group else (16 if fmt == "fp4" else d)
+    if d % gsz:
+        raise ValueError("quant group must divide the feature size")
+    if not x.is_cuda:
+        raise ValueError("fake_quant runs on the device (there is no CPU path)")
+    xs = x if x.dtype in (torch.float32, torch.bfloat16) else x.float()
+    xs = xs.reshape(-1, d).contiguous()
+    out = torch.empty(xs.shape, dtype=out_dtype, device=x.device)
+    dt = lambda t: _lib.DTYPE_BF16 if t == torch.bfloat16 else _lib.DTYPE_F32  # noqa: E731
+    check(lib().htrc_fake_quant(ptr(xs), dt(xs.dtype), int(xs.shape[0]), d, _lib.FQ_FORMATS[fmt], int(group), ptr(out),
+                                dt(out_dtype), stream_ptr()), "htrc_fake_quant")
+    return out.reshape(x.shape)
+
+
+def dequant_rows(x8, scale, out):
+    """out[r, :] = x8[r, :] * scale[r] (fp8 e4m3 codes -> bf16), h3/htrc_flat_triton.py:287-294; x8 [rows, 128]
+    and scale [rows] may be strided views, out [rows, 128] bf16 contiguous."""
+    rows, d = int(x8.shape[0]), int(x8.shape[1])
+    if x8.element_size() != 1 or x8.stride(1) != 1 or out.dtype != torch.bfloat16 or not out.is_contiguous():
+        raise ValueError("dequant_rows: x8 [rows, D] one-byte codes with unit column stride, out bf16 contiguous")
+    sc = scale if scale.dtype == torch.float32 else scale.float()
+    check(lib().htrc_dequant_rows(ptr(x8), int(x8.stride(0)), ptr(sc), int(sc.stride(0)), rows, d, ptr(out),
+                                  stream_ptr()), "htrc_dequant_rows")
+    return out
+
+
+def _prep_inputs(q, k, v, tail, quant=None):
+    """Device inputs of the kernels: q f32/bf16, k/v bf16.  With ``quant`` (kv / q formats and a group,
+    h3/htrc_flat.py:190-195) k, v and q are fake-quantised first; the near field then sees the
+    quantised keys rounded to bf16, as the reference's bf16 path does (its leaf statistics see them
+    unrounded)."""
+    quant = quant or {}
+    qg = int(quant.get("group", 0))
+    if quant.get("kv"):
+        k = fake_quant(k, quant["kv"], qg, out_dtype=torch.bfloat16)
+        v = fake_quant(v, quant["kv"], qg, out_dtype=torch.bfloat16)
+    if quant.get("q"):
+        q = fake_quant(q, quant["q"], qg)
     qd = q if q.dtype in (torch.float32, torch.bfloat16) else q.float()
     qd = qd.contiguous()
     kb = k.to(torch.bfloat16).contiguous()
@@ -223,7 +268,7 @@ def flat_attention(q, k, v, *, tile=64, exact_leaves=64, order="seq", curvature=
     return_lse).  Signature and defaults of the reference (h3/htrc_flat.py:99-103); see PROD."""
     _check_args(q, k, v, tile, exact_leaves, order, curvature, leaf, select, backend, store, dot,
                 sel_stride, quant, sink_leaves, tail)
-    qd, kb, vb, tk, tv = _prep_inputs(q, k, v, tail)
+    qd, kb, vb, tk, tv = _prep_inputs(q, k, v, tail, quant)
     grp, oc = group_of(kern), order_code(order)
     if prof is not None:
         st = run_stages(qd, kb, vb, tk, tv, exact_leaves=exact_leaves, sink_leaves=sink_leaves,

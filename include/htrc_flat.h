@@ -45,6 +45,7 @@ enum {
 enum { HTRC_DTYPE_F32 = 0, HTRC_DTYPE_BF16 = 1 };
 enum { HTRC_ORDER_SEQ = 0, HTRC_ORDER_KMEANS = 1 };
 enum { HTRC_ROUND_HALF_EVEN = 0, HTRC_ROUND_HALF_AWAY = 1 };
+enum { HTRC_FQ_INT8 = 1, HTRC_FQ_INT4 = 2, HTRC_FQ_FP8 = 3, HTRC_FQ_FP4 = 4 }; /* htrc_fake_quant formats */
 
 /* Device status bits (htrc_flat_status). */
 enum { HTRC_STATUS_WAIT_TIMEOUT = 1, HTRC_STATUS_BAD_INDEX = 2, HTRC_STATUS_NONFINITE = 4 };
@@ -187,6 +188,22 @@ int htrc_tail_partial(const void* q, int32_t q_dtype, int64_t n_queries, int32_t
  * looks up the array's address; make it before any stream capture.  Allocates nothing.
  * This entry point has no counterpart in the reference. */
 int htrc_flat_forward_static_ws(const HtrcFlatArgs* args, htrc_stream_t stream);
+
+/* Low-bit round trip of x [rows, dim] (h3/htrc_flat.py:68-97 `fake_quant`, a simulation of quantised
+ * inputs): every group of `group` consecutive values of a row (0: the whole row; HTRC_FQ_FP4 with 0:
+ * 16; else a power of two dividing dim) is rounded through the format with the symmetric scale
+ * s = max(amax, 1e-20) / qmax and written back as s * code: INT8 / INT4 clamp(rint(x / s), +-qmax),
+ * qmax 127 / 7; FP8 nearest-even e4m3 of clamp(x / s, +-448); FP4 the e2m1 grid value of |x / s|
+ * chosen by the reference's thresholds, times sign(x).  x f32 or bf16; out f32 or bf16 (rounded
+ * to nearest even). */
+int htrc_fake_quant(const void* x, int32_t x_dtype, int64_t rows, int32_t dim, int32_t fmt, int32_t group, void* out,
+                    int32_t out_dtype, htrc_stream_t stream);
+
+/* out[r, :] = bf16(float(x8[r, :]) * scale[r]) for e4m3 codes x8 (h3/htrc_flat_triton.py:276-294
+ * `dequant_rows`, the fp8 cache read path); row strides in elements (x8: multiple of 4, so rows stay
+ * 4-byte aligned), out [rows, dim] contiguous. */
+int htrc_dequant_rows(const uint8_t* x8, int64_t stride_x, const float* scale, int64_t stride_s, int64_t rows,
+                      int32_t dim, uint16_t* out, htrc_stream_t stream);
 
 /* Human-readable name of a return code. */
 const char* htrc_strerror(int code);

@@ -96,6 +96,55 @@ def pack_slope(g):
     return _round_half_away_i8(g * r[..., None]), sg
 
 
+# ----------------------------------------------------------------------------- low-bit simulation
+FP4_GRID = np.array([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0], F32)      # e2m1 magnitudes
+FP4_THR = np.array([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0], F32)         # bucket boundaries (h3/htrc_flat.py:66)
+
+
+def e4m3_round(t):
+    """Nearest-even float8 e4m3fn value of t (|t| <= 448): 3 mantissa bits, exponent bias 7,
+    subnormal quantum 2^-9."""
+    t = np.asarray(t, np.float64)
+    a = np.abs(t)
+    e = np.floor(np.log2(np.maximum(a, 2.0 ** -9)))
+    quantum = np.where(a < 2.0 ** -6, 2.0 ** -9, 2.0 ** (e - 3))
+    r = np.rint(a / quantum) * quantum                  # half-even on the exact quotient (a power of 2)
+    return (np.sign(t) * np.minimum(r, 448.0)).astype(F32)
+
+
+def fake_quant(x, fmt, group=0):
+    """Low-bit round trip with symmetric per-group scales (h3/htrc_flat.py:68-97): float32 result."""
+    x = np.asarray(x, F32)
+    d = x.shape[-1]
+    if fmt == "fp4" and not group:
+        group = 16
+    gsz = d if not group else int(group)
+    if d % gsz:
+        raise ValueError("quant group must divide the feature size")
+    y = x.reshape(*x.shape[:-1], d // gsz, gsz)
+    amax = np.maximum(np.abs(y).max(-1, keepdims=True), F32(1e-20))
+    if fmt in ("int8", "int4"):
+        qmax = F32(127.0 if fmt == "int8" else 7.0)
+        sc = (amax / qmax).astype(F32)
+        out = (np.clip(np.rint((y / sc).astype(F32)), -qmax, qmax) * sc).astype(F32)
+    elif fmt == "fp8":
+        sc = (amax / F32(448.0)).astype(F32)
+        out = (e4m3_round(np.clip((y / sc).astype(F32), -448.0, 448.0)) * sc).astype(F32)
+    elif fmt == "fp4":
+        sc = (amax / F32(6.0)).astype(F32)
+        a = np.abs((y / sc).astype(F32))
+        idx = (a[..., None] > FP4_THR).sum(-1)
+        out = ((np.sign(y).astype(F32) * FP4_GRID[idx]).astype(F32) * sc).astype(F32)
+    else:
+        raise ValueError(f"unknown quant format {fmt}")
+    return out.reshape(x.shape)
+
+
+def dequant_rows(x8_values, scale):
+    """bf16(x8 * scale) per row (h3/htrc_flat_triton.py:276-294), x8 given as its float values."""
+    return bf16_round((np.asarray(x8_values, F32) * np.asarray(scale, F32)[:, None]).astype(F32))
+
+
 # ----------------------------------------------------------------------------- stages
 def linspace_f32(hi, steps):
     """torch.linspace(0, hi, steps) in float32 on the CPU: step = hi / (steps - 1) in float32, the first
@@ -401,7 +450,8 @@ def pack_k(k):
 
 
 def flat_attention(q, k, v, *, tile=64, exact_leaves=256, leaf=64, scale=None, sink_leaves=0,
-                   tail=None, return_stages=False, group=1, order="seq", perm=None):
+                   tail=None, return_stages=False, group=1, order="seq", perm=None, quant=None,
+                   stats_bf16=False):
     """The whole production path for one head: q [N, D], k/v [M, D] (float32 arrays holding the
     caller's values; k and v are rounded to bfloat16 as the reference's bf16 path stores them).
     group: G tiles per centre (kern["group"]); order "kmeans" permutes the queries first (``perm``
@@ -409,6 +459,19 @@ def flat_attention(q, k, v, *, tile=64, exact_leaves=256, leaf=64, scale=None, s
     Returns (out float32 [N, D], lse float32 [N]) and, with return_stages, a dict of every stage."""
     q = np.asarray(q, dtype=F32)
     group = max(1, int(group))
+    k_stats = v_stats = None
+    if quant:
+        # h3/htrc_flat.py:190-195: inputs fake-quantised first (float32 results); the bf16 near field
+        # rounds the quantised keys/values to bf16 while the leaf statistics use them unrounded
+        # (stats_bf16=True models a device that reads bf16 keys for the statistics too)
+        qg = int(quant.get("group", 0))
+        if quant.get("kv"):
+            k = fake_quant(k, quant["kv"], qg)
+            v = fake_quant(v, quant["kv"], qg)
+            if not stats_bf16:
+                k_stats, v_stats = k, v
+        if quant.get("q"):
+            q = fake_quant(q, quant["q"], qg)
     if order == "kmeans" and perm is None:
         perm = kmeans_order(q)
     if order != "kmeans":
@@ -427,7 +490,7 @@ def flat_attention(q, k, v, *, tile=64, exact_leaves=256, leaf=64, scale=None, s
     qt, mu, _ = tile_centres(q, tile)
     if group > 1:
         mu = group_centres(qt, group)
-    g, lz, vbf = leaf_stats(mu, k, v, leaf, scale)
+    g, lz, vbf = leaf_stats(mu, k if k_stats is None else k_stats, v if v_stats is None else v_stats, leaf, scale)
     g8, sg, vb = state_int8(g, vbf)
     q8, sq, dq8, sdq = query_codes(qt, mu[np.arange(qt.shape[0]) // group])
     nb = m // leaf

@@ -152,6 +152,9 @@ CASES = [
     dict(name="tile32", grid=(2, 16, 16), leaf=64, E=2, sink=1, tail=5, trim=19, seed=24, tile=32),
     dict(name="max_mode", grid=(2, 16, 16), leaf=64, E=3, sink=0, tail=0, trim=0, seed=25, tile=32, order="kmeans"),
     dict(name="tile32_g2", grid=(2, 16, 16), leaf=64, E=2, sink=0, tail=0, trim=45, seed=26, tile=32, group=2),
+    # low-bit simulation of the inputs (quant=): k/v int4 and q int8 with groups of 32
+    dict(name="quant_kv_q", grid=(2, 16, 16), leaf=64, E=2, sink=0, tail=0, trim=0, seed=27,
+         quant={"kv": "int4", "q": "int8", "group": 32}),
 ]
 
 
@@ -175,6 +178,8 @@ def run_case(flat, c):
                order=c.get("order", "seq"), tile=c.get("tile", 64))
     if c.get("group", 1) > 1:
         cfg["kern"] = {**cfg["kern"], "group": c["group"]}
+    if c.get("quant"):
+        cfg["quant"] = dict(c["quant"])
     out = flat.flat_attention(q, k, v, tail=(tk, tv) if tk is not None else None, ws=ws, **cfg)
     st = rec["stats"]
     ti = rec["tile"]
@@ -203,6 +208,9 @@ def run_case(flat, c):
         res["tail_k"], res["tail_v"] = tk.numpy(), tv.numpy()
     if rec["perm"]:
         res["perm"] = rec["perm"][0].numpy().astype(np.int64)
+    if c.get("quant"):
+        res["quant_kv"], res["quant_q"] = np.array(c["quant"]["kv"]), np.array(c["quant"]["q"])
+        res["quant_group"] = np.int64(c["quant"]["group"])
     if c.get("slim"):
         # large case: inputs as bfloat16 bit patterns, no per-(tile, leaf) state (the tests recompute it)
         for name, t in (("q", q), ("k", k), ("v", v)):
@@ -213,11 +221,37 @@ def run_case(flat, c):
     return res
 
 
+def fake_quant_fixture(flat):
+    """The reference's fake_quant (h3/htrc_flat.py:68-97) on rows of varied scale, and its dequant_rows
+    (h3/htrc_flat_triton.py:276-294) on e4m3 codes."""
+    g = torch.Generator().manual_seed(31)
+    x = torch.randn(64, 128, generator=g) * torch.rand(64, 1, generator=g).pow(3) * 20
+    x[5] = 0.0
+    x[6, :7] = 1e-30
+    xb = x.to(torch.bfloat16)                        # bf16 inputs (the kv path)
+    res = {"x": x.numpy(), "xb": xb.float().numpy()}
+    for fmt in ("int8", "int4", "fp8", "fp4"):
+        for grp in (0, 16, 32):
+            res[f"y_{fmt}_{grp}"] = flat.fake_quant(x, fmt, grp).numpy()
+            res[f"yb_{fmt}_{grp}"] = flat.fake_quant(xb, fmt, grp).numpy()
+    codes = torch.randint(0, 256, (64, 128), generator=g, dtype=torch.uint8)
+    codes[(codes & 0x7F) == 0x7F] = 0x3C               # no NaN codes
+    sc = torch.rand(64, generator=g) * 3 + 1e-3
+    tri = flat._load_triton()
+    out = torch.empty(64, 128, dtype=torch.bfloat16)
+    tri.dequant_rows(codes.view(torch.float8_e4m3fn), sc, out)
+    res.update(codes=codes.numpy(), dq_scale=sc.numpy(), dq_out=out.float().numpy())
+    return res
+
+
 def main():
     _shim()
     flat = _load_reference()
     torch.manual_seed(0)
     only = set(sys.argv[1:])
+    if not only or "fake_quant" in only:
+        np.savez_compressed(HERE / "fake_quant.npz", **fake_quant_fixture(flat))
+        print("fake_quant -> fake_quant.npz")
     for c in CASES:
         if only and c["name"] not in only:
             continue

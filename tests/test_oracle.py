@@ -6,7 +6,8 @@ import pytest
 from oracle import flat_oracle as O
 
 CASES = ["base", "ragged", "sink_tail", "all_exact", "no_exact", "big_tail", "leaf32", "wide",
-         "group2", "group4", "kmeans", "kmeans_g2_tail", "kmeans_sampled", "tile32", "max_mode", "tile32_g2"]
+         "group2", "group4", "kmeans", "kmeans_g2_tail", "kmeans_sampled", "tile32", "max_mode", "tile32_g2",
+         "quant_kv_q"]
 SLIM = {"kmeans_sampled"}                      # no recorded per-(tile, leaf) state
 STATE_CASES = [c for c in CASES if c not in SLIM]
 KMEANS_CASES = ["kmeans", "kmeans_g2_tail", "kmeans_sampled", "max_mode"]
@@ -14,6 +15,12 @@ KMEANS_CASES = ["kmeans", "kmeans_g2_tail", "kmeans_sampled", "max_mode"]
 
 def _group(z):
     return int(z["group"]) if "group" in z else 1
+
+
+def _quant(z):
+    if "quant_kv" not in z:
+        return None
+    return {"kv": str(z["quant_kv"]), "q": str(z["quant_q"]), "group": int(z["quant_group"])}
 
 
 def _stages(z):
@@ -24,7 +31,13 @@ def _stages(z):
     return O.flat_attention(z["q"], z["k"], z["v"], leaf=int(z["leaf"]),
                             exact_leaves=int(z["exact_leaves"]), sink_leaves=int(z["sink_leaves"]),
                             tail=tail, return_stages=True, group=_group(z), order=order,
-                            perm=z.get("perm"), tile=int(z["tile"]) if "tile" in z else 64), tail
+                            perm=z.get("perm"), tile=int(z["tile"]) if "tile" in z else 64,
+                            quant=_quant(z)), tail
+
+
+def _v_used(z):
+    q = _quant(z)
+    return O.fake_quant(z["v"], q["kv"], q["group"]) if q else z["v"]
 
 
 def _tile_mu(z, nt):
@@ -34,7 +47,8 @@ def _tile_mu(z, nt):
 @pytest.mark.parametrize("case", STATE_CASES)
 def test_key_pack_bit_exact(golden_cases, case):
     z = golden_cases[case]
-    k8, ks = O.pack_k(z["k"])
+    q = _quant(z)
+    k8, ks = O.pack_k(O.fake_quant(z["k"], q["kv"], q["group"]) if q else z["k"])
     assert np.array_equal(k8, z["k8"])
     assert np.array_equal(ks.view(np.uint32), z["ks"].view(np.uint32))
 
@@ -96,7 +110,7 @@ def test_ordered_restatement_matches_reference(golden_cases, case):
     idx = z["idx"] if "idx" in z else np.zeros((ng, 0), np.int32)
     q8, sq, dq8, sdq = O.query_codes(st["qt"], _tile_mu(z, st["qt"].shape[0]))
     o2, l2 = O.tile_attention_ordered(st["qt"], q8, sq, dq8, sdq, z["g8"], z["sg"], z["lz"], z["vb"],
-                                      z["excl"], idx, z["k8"], z["ks"], O.bf16_round(z["v"]),
+                                      z["excl"], idx, z["k8"], z["ks"], O.bf16_round(_v_used(z)),
                                       int(z["leaf"]), 1 / np.sqrt(128), tail=tail, group=_group(z))
     n = z["q"].shape[0]
     o2, l2 = o2[:n], l2[:n]
@@ -173,6 +187,32 @@ def test_groups_of_three_restate_the_rule():
     o3 = O.flat_attention(q, k, v, exact_leaves=99, group=3)[0]
     o1 = O.flat_attention(q, k, v, exact_leaves=99, group=1)[0]
     assert np.array_equal(o3, o1)
+
+
+def test_fake_quant_bit_exact_against_reference(golden_cases):
+    """h3/htrc_flat.py:68-97 on float32 and bf16 rows of varied scale (a zero row, tiny values)."""
+    z = golden_cases["fake_quant"]
+    for fmt in ("int8", "int4", "fp8", "fp4"):
+        for grp in (0, 16, 32):
+            for xk, yk in (("x", "y"), ("xb", "yb")):
+                got = O.fake_quant(z[xk], fmt, grp)
+                assert np.array_equal(got, z[f"{yk}_{fmt}_{grp}"]), (fmt, grp, xk)
+
+
+def test_e4m3_rounding_matches_torch():
+    torch = pytest.importorskip("torch")
+    rng = np.random.default_rng(0)
+    t = np.concatenate([rng.uniform(-448, 448, 20000),
+                        rng.uniform(-1, 1, 20000) * 2.0 ** rng.integers(-12, 0, 20000)]).astype(np.float32)
+    ref = torch.from_numpy(t).to(torch.float8_e4m3fn).float().numpy()
+    assert np.array_equal(O.e4m3_round(t), ref)
+
+
+def test_dequant_rows_against_reference(golden_cases):
+    import torch
+    z = golden_cases["fake_quant"]
+    vals = torch.from_numpy(z["codes"]).view(torch.float8_e4m3fn).float().numpy()
+    assert np.array_equal(O.dequant_rows(vals, z["dq_scale"]), z["dq_out"])
 
 
 def test_route_sink_and_ties():
