@@ -372,8 +372,9 @@ def run_ours(a, wl, rank, world, local_rank):
         from htrc_b200 import runner as R
         h0 = my_heads[0]
         modes = {}
-        for mode in R.MODES:
-            r = R.FlatRunner(n, m, mode=mode, device=dev)
+        for mode in list(R.MODES) + ["fast+iso"]:
+            extra = dict(backend="cuda", curvature="iso") if mode == "fast+iso" else {}
+            r = R.FlatRunner(n, m, mode=mode.split("+")[0], device=dev, **extra)
             if r.graph is None:
                 modes[mode] = f"graph capture failed: {r.graph_error}"
                 continue
@@ -412,7 +413,7 @@ def run_ours(a, wl, rank, world, local_rank):
         modes = {"ms_per_head": modes, "kmeans_order_ms": k0.elapsed_time(k1) / 5,
                  "note": "head 0 of the workload through FlatRunner (CUDA graph) per mode of "
                          "h3/htrc_flat_runner.py:48-53: fast E=256, balanced E=512, accurate E=1024 + k-means, "
-                         "max E=1024 + k-means + 32-row tiles"}
+                         "max E=1024 + k-means + 32-row tiles; fast+iso: fast with the isotropic curvature term"}
 
     # ---- roofline of the dominant kernel (tile attention) from the live events
     peaks, peak_src = measured_peaks()
@@ -433,6 +434,21 @@ def run_ours(a, wl, rank, world, local_rank):
             "flop_count": "bf16 PV flops + int8 QK ops/2 over the routed tokens and non-routed leaves, one head",
             "ms_per_launch": tile_ms}
 
+    # ---- every stage against its binding roofline (algorithmic bytes or flop per head / stage time)
+    hbm = float(peaks.get("hbm_gbs", 6650.0))
+    pitch = -(-nb // 16) * 16
+    stage_bytes = {
+        "prep": m * (2 * 128 + 128 + 4) + n * 2 * 128 + npad * (2 * 128 + 8),   # k pack + q codes (bf16 q)
+        "stats": nt * nb * (128 + 256) + 2 * nt * pitch * 4,                    # g8 + vbar + sg/lz written
+        "rowmax": nt * nb * 128 + 2 * nt * pitch * 4 + nt * pitch * 4,          # g8 + sg/lz read, sel written
+        "route": nt * pitch * 4 + nt * (pitch + kx * 4),                        # sel read, excl/idx written
+    }
+    stage_roof = {nm: {"bound": "hbm", "bytes": b_, "achieved_gbs": b_ / (stage_ms[nm] * 1e-3) / 1e9,
+                       "frac": b_ / (stage_ms[nm] * 1e-3) / 1e9 / hbm}
+                  for nm, b_ in stage_bytes.items()}
+    stage_roof["stats"]["tensor_frac"] = (6.0 * nt * m * 128 / (stage_ms["stats"] * 1e-3) / 1e12) / peak
+    stage_roof["tile"] = {"bound": "tensor", "frac": roof["frac"]}
+
     if rank == 0:
         line = {"metric": METRIC, "value": ms, "unit": "ms/layer", "n_gpus": world, "steps": a.steps,
                 "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": False, "scaling": "strong",
@@ -442,7 +458,8 @@ def run_ours(a, wl, rank, world, local_rank):
                            "exact_leaves": E, "heads_per_gpu": len(my_heads),
                            "l2": "inputs larger than L2: 2.4 GB of distinct q/k/v per layer, 1.6 GB leaf state per head",
                            "parallelism": f"heads/{world}" + (" + bf16 output all_gather (NCCL)" if world > 1 else "")},
-                "stage_ms_per_head": stage_ms, "modes": modes, **parity, "roofline": roof, "cpu_baseline": cpu,
+                "stage_ms_per_head": stage_ms, "stage_roofline": stage_roof, "modes": modes, **parity,
+                "roofline": roof, "cpu_baseline": cpu,
                 "e2e": e2e,
                 "gpu_launches": a.steps * len(my_heads) * LAUNCHES_PER_HEAD, "clocks": clk}
         print(json.dumps(line), flush=True)

@@ -131,6 +131,8 @@ struct Layout {
   bool kmeans = false;
   size_t status = 0, k8 = 0, ks = 0, mu = 0, mu_hi = 0, mu_lo = 0, q8 = 0, sq = 0, dq8 = 0, sdq = 0, tail = 0;
   size_t g8 = 0, vb = 0, sg = 0, lz = 0, sel = 0, excl = 0, idx = 0, perm = 0, km = 0, total = 0;
+  bool iso = false;
+  size_t kn2 = 0, dd = 0, cv = 0;           // iso curvature: key norms, row offsets, coefficients
 };
 
 constexpr int kMaxGroup = 65536;
@@ -143,6 +145,7 @@ int validate(const HtrcFlatArgs* a, bool need_ptrs) {
   if (a->exact_leaves < 0 || a->sink_leaves < 0 || a->n_tail < 0) return HTRC_ERR_ARG;
   if (a->group > kMaxGroup) return HTRC_ERR_ARG;
   if (a->order != HTRC_ORDER_SEQ && a->order != HTRC_ORDER_KMEANS) return HTRC_ERR_ARG;
+  if (a->curvature != HTRC_CURV_LIN && a->curvature != HTRC_CURV_ISO) return HTRC_ERR_ARG;
   if (a->n_queries > (int64_t(1) << 31) - 1) return HTRC_ERR_UNSUPPORTED;
   const int64_t nb = a->n_keys / a->leaf;
   if (nb > kMaxLeaves) return HTRC_ERR_UNSUPPORTED;
@@ -201,6 +204,12 @@ Layout layout_of(const HtrcFlatArgs* a) {
   L.sel = take(static_cast<size_t>(L.tcm) * L.pitch * 4);
   L.excl = take(static_cast<size_t>(gcm_rows) * L.pitch);
   L.idx = take(static_cast<size_t>(gcm_rows) * std::max<int64_t>(L.kx, 1) * 4);
+  L.iso = a->curvature == HTRC_CURV_ISO;
+  if (L.iso) {
+    L.kn2 = take(static_cast<size_t>(L.m) * 4);
+    L.dd = take(static_cast<size_t>(L.nt) * 64 * 4);
+    L.cv = take(static_cast<size_t>(gcm_rows) * L.pitch * 4);
+  }
   if (L.kmeans) {
     L.perm = take(static_cast<size_t>(L.n) * 4);
     L.km = take(kmeans_scratch_bytes(L.n));
@@ -227,20 +236,21 @@ int stats_maps(LeafStatsMaps* mp, const uint16_t* mu_hi, const uint16_t* mu_lo, 
 }
 
 int rowmax_maps(RowmaxMaps* mp, const int8_t* dq8, int64_t rows, const int8_t* g8, const float* sg, const float* lz,
-                int64_t tc, int64_t nb, int64_t pitch) {
+                const float* cv, int64_t tc, int64_t nb, int64_t pitch) {
   bool ok = map_rows(&mp->dq8, dq8, rows, false, 64) && map_state(&mp->g8, g8, tc, nb, false, 128, 1) &&
-            map_scalars(&mp->sg, sg, tc, nb, pitch, true, 128) && map_scalars(&mp->lz, lz, tc, nb, pitch, true, 128);
+            map_scalars(&mp->sg, sg, tc, nb, pitch, true, 128) && map_scalars(&mp->lz, lz, tc, nb, pitch, true, 128) &&
+            map_scalars(&mp->cv, cv ? cv : sg, tc, nb, pitch, true, 128);
   return ok ? HTRC_OK : HTRC_ERR_CUDA;
 }
 
 int tile_maps(TileMaps* mp, const int8_t* q8, const int8_t* dq8, int64_t rows, const int8_t* g8, const uint16_t* vb,
-              const float* lz, const float* sg, const uint8_t* excl, int64_t tc, int64_t nb, int64_t pitch,
-              const int8_t* k8, const uint16_t* v, int64_t m) {
+              const float* lz, const float* sg, const float* cv, const uint8_t* excl, int64_t tc, int64_t nb,
+              int64_t pitch, const int8_t* k8, const uint16_t* v, int64_t m) {
   bool ok = map_rows(&mp->q8, q8, rows, false, 64) && map_rows(&mp->dq8, dq8, rows, false, 64) &&
             map_state(&mp->g8, g8, tc, nb, false, 64, 1) && map_state_halves(&mp->vb, vb, tc, nb, 64) &&
             map_scalars(&mp->lz, lz, tc, nb, pitch, true, 64) && map_scalars(&mp->sg, sg, tc, nb, pitch, true, 64) &&
             map_scalars(&mp->excl, excl, tc, nb, pitch, false, 64) && map_rows(&mp->k8, k8, m, false, 64) &&
-            map_rows_halves(&mp->v, v, m, 64);
+            map_rows_halves(&mp->v, v, m, 64) && map_scalars(&mp->cv, cv ? cv : sg, tc, nb, pitch, true, 64);
   return ok ? HTRC_OK : HTRC_ERR_CUDA;
 }
 
@@ -298,10 +308,14 @@ int htrc_flat_forward(const HtrcFlatArgs* a, htrc_stream_t stream) {
       cudaEventRecord(static_cast<cudaEvent_t>(a->stage_events[i]), st);
   };
   mark(0);
-  launch_pack_rows(a->k, HTRC_DTYPE_BF16, L.m, HTRC_ROUND_HALF_EVEN, k8, ks, st);
+  float* kn2 = L.iso ? at<float>(ws, L.kn2) : nullptr;
+  float* dd = L.iso ? at<float>(ws, L.dd) : nullptr;
+  float* cv = L.iso ? at<float>(ws, L.cv) : nullptr;
+  launch_pack_rows(a->k, HTRC_DTYPE_BF16, L.m, HTRC_ROUND_HALF_EVEN, k8, ks, kn2, st);
   if (perm && (rc = launch_kmeans_order(a->q, a->q_dtype, L.n, perm, at<void>(ws, L.km), st)) != HTRC_OK) return rc;
   const int trows = static_cast<int>(L.trows);
-  launch_tile_prep(a->q, a->q_dtype, L.n, trows, perm, group, at<float>(ws, L.mu), mu_hi, mu_lo, q8, sq, dq8, sdq, st);
+  launch_tile_prep(a->q, a->q_dtype, L.n, trows, perm, group, at<float>(ws, L.mu), mu_hi, mu_lo, q8, sq, dq8, sdq, dd,
+                   st);
   if (tail) launch_tail_partial(a->q, a->q_dtype, L.n, a->tail_k, a->tail_v, a->n_tail, scale, tail, st);
   if (cudaGetLastError() != cudaSuccess) return HTRC_ERR_CUDA;
   mark(1);
@@ -314,25 +328,27 @@ int htrc_flat_forward(const HtrcFlatArgs* a, htrc_stream_t stream) {
     if (far) {
       LeafStatsMaps smp;
       if ((rc = stats_maps(&smp, mu_hi, mu_lo, L.ng, a->k, a->v, L.m, g8, vb, gc, L.nb)) != HTRC_OK) return rc;
-      if ((rc = launch_leaf_stats(smp, sg, lz, L.pitch, g0, gc, nb, scale, status, device_info().sms, st)) != HTRC_OK)
+      if ((rc = launch_leaf_stats(smp, sg, lz, L.pitch, g0, gc, nb, scale, kn2, cv, status, device_info().sms, st)) !=
+          HTRC_OK)
         return rc;
     }
     mark(2 + 4 * chunk);
     if (far) {
       if (kx > 0) {
         RowmaxMaps rmp;
-        if ((rc = rowmax_maps(&rmp, dq8, L.nt * 64, g8, sg, lz, gc, L.nb, L.pitch)) != HTRC_OK) return rc;
-        if ((rc = launch_rowmax(rmp, sdq, sel, L.pitch, t0, tc, nb, group, status, st)) != HTRC_OK) return rc;
+        if ((rc = rowmax_maps(&rmp, dq8, L.nt * 64, g8, sg, lz, cv, gc, L.nb, L.pitch)) != HTRC_OK) return rc;
+        if ((rc = launch_rowmax(rmp, sdq, dd, sel, L.pitch, t0, tc, nb, group, status, st)) != HTRC_OK) return rc;
       }
     }
     mark(3 + 4 * chunk);
     if ((rc = launch_route(sel, L.pitch, tc, group, nb, kx, sink, idx, excl, st)) != HTRC_OK) return rc;
     mark(4 + 4 * chunk);
     TileMaps tmp;
-    if ((rc = tile_maps(&tmp, q8, dq8, L.nt * 64, g8, vb, lz, sg, excl, gc, L.nb, L.pitch, k8, a->v, L.m)) != HTRC_OK)
+    if ((rc = tile_maps(&tmp, q8, dq8, L.nt * 64, g8, vb, lz, sg, cv, excl, gc, L.nb, L.pitch, k8, a->v, L.m)) !=
+        HTRC_OK)
       return rc;
     if ((rc = launch_tile_attention(tmp, sq, sdq, ks, idx, kx, nb, L.n, trows, t0, tc, group, scale, tail, perm,
-                                    a->out, a->lse, status, st)) != HTRC_OK)
+                                    dd, a->out, a->lse, status, st)) != HTRC_OK)
       return rc;
     mark(5 + 4 * chunk);
   }
@@ -350,27 +366,27 @@ int htrc_flat_status(void* workspace, int32_t* status_out, htrc_stream_t stream)
 }
 
 int htrc_pack_int8(const void* x, int32_t dtype, int64_t rows, int32_t dim, int32_t rounding, int8_t* x8,
-                   float* scale, htrc_stream_t stream) {
+                   float* scale, float* sqnorm, htrc_stream_t stream) {
   if (!x || !x8 || !scale || rows < 1) return HTRC_ERR_ARG;
   if (dim != kDim) return HTRC_ERR_UNSUPPORTED;
   if (dtype != HTRC_DTYPE_F32 && dtype != HTRC_DTYPE_BF16) return HTRC_ERR_ARG;
   if (rounding != HTRC_ROUND_HALF_EVEN && rounding != HTRC_ROUND_HALF_AWAY) return HTRC_ERR_ARG;
   int rc = check_device();
   if (rc != HTRC_OK) return rc;
-  launch_pack_rows(x, dtype, rows, rounding, x8, scale, reinterpret_cast<cudaStream_t>(stream));
+  launch_pack_rows(x, dtype, rows, rounding, x8, scale, sqnorm, reinterpret_cast<cudaStream_t>(stream));
   return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
 }
 
 int htrc_tile_prep(const void* q, int32_t q_dtype, int64_t n_queries, int32_t dim, int32_t tile, const int32_t* perm,
                    int32_t group, float* mu, uint16_t* mu_hi, uint16_t* mu_lo, int8_t* q8, float* sq, int8_t* dq8,
-                   float* sdq, htrc_stream_t stream) {
+                   float* sdq, float* dd, htrc_stream_t stream) {
   if (!q || !mu || !mu_hi || !mu_lo || !q8 || !sq || !dq8 || !sdq || n_queries < 1) return HTRC_ERR_ARG;
   if (dim != kDim || (tile != kTile && tile != kTile / 2)) return HTRC_ERR_UNSUPPORTED;
   if (q_dtype != HTRC_DTYPE_F32 && q_dtype != HTRC_DTYPE_BF16) return HTRC_ERR_ARG;
   if (group > kMaxGroup) return HTRC_ERR_ARG;
   int rc = check_device();
   if (rc != HTRC_OK) return rc;
-  launch_tile_prep(q, q_dtype, n_queries, tile, perm, group, mu, mu_hi, mu_lo, q8, sq, dq8, sdq,
+  launch_tile_prep(q, q_dtype, n_queries, tile, perm, group, mu, mu_hi, mu_lo, q8, sq, dq8, sdq, dd,
                    reinterpret_cast<cudaStream_t>(stream));
   return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
 }
@@ -397,8 +413,9 @@ int htrc_kmeans_order(const void* q, int32_t q_dtype, int64_t n_queries, int32_t
 
 int htrc_leaf_stats(const uint16_t* mu_hi, const uint16_t* mu_lo, int64_t nt, int64_t t0, int64_t tc, const uint16_t* k,
                     const uint16_t* v, int64_t n_keys, int32_t dim, int32_t leaf, float scale, int8_t* g8, float* sg,
-                    float* lz, uint16_t* vb, int32_t* status, htrc_stream_t stream) {
+                    float* lz, uint16_t* vb, const float* kn2, float* cv, int32_t* status, htrc_stream_t stream) {
   if (!mu_hi || !mu_lo || !k || !v || !g8 || !sg || !lz || !vb) return HTRC_ERR_ARG;
+  if ((kn2 == nullptr) != (cv == nullptr)) return HTRC_ERR_ARG;
   if (dim != kDim || leaf != kLeaf) return HTRC_ERR_UNSUPPORTED;
   if (nt < 1 || t0 < 0 || tc < 1 || t0 + tc > nt || n_keys < leaf || n_keys % leaf) return HTRC_ERR_ARG;
   const int64_t nb = n_keys / leaf;
@@ -407,14 +424,15 @@ int htrc_leaf_stats(const uint16_t* mu_hi, const uint16_t* mu_lo, int64_t nt, in
   if (rc != HTRC_OK) return rc;
   LeafStatsMaps mp;
   if ((rc = stats_maps(&mp, mu_hi, mu_lo, nt, k, v, n_keys, g8, vb, tc, nb)) != HTRC_OK) return rc;
-  return launch_leaf_stats(mp, sg, lz, pitch_of(nb), t0, tc, static_cast<int>(nb), scale_of(scale), status,
+  return launch_leaf_stats(mp, sg, lz, pitch_of(nb), t0, tc, static_cast<int>(nb), scale_of(scale), kn2, cv, status,
                            device_info().sms, reinterpret_cast<cudaStream_t>(stream));
 }
 
-int htrc_rowmax_select(const int8_t* dq8, const float* sdq, int64_t t0, int64_t tc, int32_t group, const int8_t* g8,
-                       const float* sg, const float* lz, int64_t nb, int32_t dim, float* sel, int32_t* status,
-                       htrc_stream_t stream) {
+int htrc_rowmax_select(const int8_t* dq8, const float* sdq, const float* dd, int64_t t0, int64_t tc, int32_t group,
+                       const int8_t* g8, const float* sg, const float* lz, const float* cv, int64_t nb, int32_t dim,
+                       float* sel, int32_t* status, htrc_stream_t stream) {
   if (!dq8 || !sdq || !g8 || !sg || !lz || !sel || t0 < 0 || tc < 1 || nb < 1) return HTRC_ERR_ARG;
+  if ((dd == nullptr) != (cv == nullptr)) return HTRC_ERR_ARG;
   const int64_t g = group > 1 ? group : 1;
   if (g > kMaxGroup || t0 % g) return HTRC_ERR_ARG;
   if (dim != kDim) return HTRC_ERR_UNSUPPORTED;
@@ -422,9 +440,9 @@ int htrc_rowmax_select(const int8_t* dq8, const float* sdq, int64_t t0, int64_t 
   int rc = check_device();
   if (rc != HTRC_OK) return rc;
   RowmaxMaps mp;
-  if ((rc = rowmax_maps(&mp, dq8, (t0 + tc) * 64, g8, sg, lz, (tc + g - 1) / g, nb, pitch_of(nb))) != HTRC_OK)
+  if ((rc = rowmax_maps(&mp, dq8, (t0 + tc) * 64, g8, sg, lz, cv, (tc + g - 1) / g, nb, pitch_of(nb))) != HTRC_OK)
     return rc;
-  return launch_rowmax(mp, sdq, sel, pitch_of(nb), t0, tc, static_cast<int>(nb), static_cast<int>(g), status,
+  return launch_rowmax(mp, sdq, dd, sel, pitch_of(nb), t0, tc, static_cast<int>(nb), static_cast<int>(g), status,
                        reinterpret_cast<cudaStream_t>(stream));
 }
 
@@ -446,9 +464,10 @@ int htrc_tile_attention(const int8_t* q8, const float* sq, const int8_t* dq8, co
                         int32_t tile, int64_t t0, int64_t tc, int32_t group, const int8_t* g8, const float* sg,
                         const float* lz, const uint16_t* vb, const uint8_t* excl, const int32_t* idx, int32_t kx,
                         int64_t nb, const int8_t* k8, const float* ks, const uint16_t* v, int64_t n_keys, int32_t dim,
-                        int32_t leaf, float scale, const float* tail_part, const int32_t* perm, float* out, float* lse,
-                        int32_t* status, htrc_stream_t stream) {
+                        int32_t leaf, float scale, const float* tail_part, const int32_t* perm, const float* cv,
+                        const float* dd, float* out, float* lse, int32_t* status, htrc_stream_t stream) {
   if (!q8 || !sq || !dq8 || !sdq || !k8 || !ks || !v || !out || n_queries < 1 || t0 < 0 || tc < 1) return HTRC_ERR_ARG;
+  if ((dd == nullptr) != (cv == nullptr)) return HTRC_ERR_ARG;
   const int64_t g = group > 1 ? group : 1;
   if (g > kMaxGroup || t0 % g) return HTRC_ERR_ARG;
   if (dim != kDim || leaf != kLeaf || (tile != kTile && tile != kTile / 2)) return HTRC_ERR_UNSUPPORTED;
@@ -468,11 +487,11 @@ int htrc_tile_attention(const int8_t* q8, const float* sq, const int8_t* dq8, co
   const void* exp_ = excl ? static_cast<const void*>(excl) : static_cast<const void*>(k8);
   TileMaps mp;
   if ((rc = tile_maps(&mp, q8, dq8, nt * 64, static_cast<const int8_t*>(g8p), static_cast<const uint16_t*>(vbp),
-                      static_cast<const float*>(lzp), static_cast<const float*>(sgp),
+                      static_cast<const float*>(lzp), static_cast<const float*>(sgp), cv,
                       static_cast<const uint8_t*>(exp_), (tc + g - 1) / g, nb, pitch_of(nb), k8, v, n_keys)) != HTRC_OK)
     return rc;
   return launch_tile_attention(mp, sq, sdq, ks, idx, kx, static_cast<int>(nb), n_queries, tile, t0, tc, static_cast<int>(g),
-                               scale_of(scale), tail_part, perm, out, lse, status,
+                               scale_of(scale), tail_part, perm, cv ? dd : nullptr, out, lse, status,
                                reinterpret_cast<cudaStream_t>(stream));
 }
 

@@ -28,6 +28,14 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// sum of squares of a 128-value row held four values per lane (fp32, lane products then a tree)
+__device__ __forceinline__ float row_sqnorm(const float (&v)[4]) {
+  float s = __fmaf_rn(v[3], v[3], __fmaf_rn(v[2], v[2], __fmaf_rn(v[1], v[1], __fmul_rn(v[0], v[0]))));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+  return s;
+}
+
 __device__ __forceinline__ uint32_t pack_i8x4(int a, int b, int c, int d) {
   return (static_cast<uint32_t>(a) & 0xFFu) | ((static_cast<uint32_t>(b) & 0xFFu) << 8) |
          ((static_cast<uint32_t>(c) & 0xFFu) << 16) | ((static_cast<uint32_t>(d) & 0xFFu) << 24);
@@ -67,7 +75,8 @@ __device__ __forceinline__ uint32_t quant4(const float (&v)[4], float s, float r
 // One warp per row of 128 values; each lane owns 4 consecutive values.
 template <typename T, int ROUND>
 __global__ void __launch_bounds__(256) pack_rows_kernel(const T* __restrict__ x, int64_t rows,
-                                                        int8_t* __restrict__ x8, float* __restrict__ scale) {
+                                                        int8_t* __restrict__ x8, float* __restrict__ scale,
+                                                        float* __restrict__ sqnorm) {
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -78,21 +87,25 @@ __global__ void __launch_bounds__(256) pack_rows_kernel(const T* __restrict__ x,
   const float s = fmaxf(__fmul_rn(am, kInv127), 1e-20f);
   reinterpret_cast<uint32_t*>(x8 + row * 128)[lane] = quant4<ROUND>(v, s, __frcp_rn(s));
   if (lane == 0) scale[row] = s;
+  if (sqnorm != nullptr) {                 // |x_row|^2 (the iso curvature's key norms)
+    const float n2 = row_sqnorm(v);
+    if (lane == 0) sqnorm[row] = n2;
+  }
 }
 
 void launch_pack_rows(const void* x, int dtype, int64_t rows, int rounding, int8_t* x8, float* scale,
-                      cudaStream_t st) {
+                      float* sqnorm, cudaStream_t st) {
   const unsigned grid = static_cast<unsigned>((rows + 7) / 8);
   if (dtype == HTRC_DTYPE_BF16) {
     if (rounding == HTRC_ROUND_HALF_EVEN)
-      pack_rows_kernel<uint16_t, 0><<<grid, 256, 0, st>>>(static_cast<const uint16_t*>(x), rows, x8, scale);
+      pack_rows_kernel<uint16_t, 0><<<grid, 256, 0, st>>>(static_cast<const uint16_t*>(x), rows, x8, scale, sqnorm);
     else
-      pack_rows_kernel<uint16_t, 1><<<grid, 256, 0, st>>>(static_cast<const uint16_t*>(x), rows, x8, scale);
+      pack_rows_kernel<uint16_t, 1><<<grid, 256, 0, st>>>(static_cast<const uint16_t*>(x), rows, x8, scale, sqnorm);
   } else {
     if (rounding == HTRC_ROUND_HALF_EVEN)
-      pack_rows_kernel<float, 0><<<grid, 256, 0, st>>>(static_cast<const float*>(x), rows, x8, scale);
+      pack_rows_kernel<float, 0><<<grid, 256, 0, st>>>(static_cast<const float*>(x), rows, x8, scale, sqnorm);
     else
-      pack_rows_kernel<float, 1><<<grid, 256, 0, st>>>(static_cast<const float*>(x), rows, x8, scale);
+      pack_rows_kernel<float, 1><<<grid, 256, 0, st>>>(static_cast<const float*>(x), rows, x8, scale, sqnorm);
   }
 }
 
@@ -149,7 +162,8 @@ __global__ void __launch_bounds__(128) tile_prep_kernel(const T* __restrict__ q,
                                                         int64_t n, int trows, int group, float* __restrict__ mu,
                                                         uint16_t* __restrict__ mu_hi, uint16_t* __restrict__ mu_lo,
                                                         int8_t* __restrict__ q8, float* __restrict__ sq,
-                                                        int8_t* __restrict__ dq8, float* __restrict__ sdq) {
+                                                        int8_t* __restrict__ dq8, float* __restrict__ sdq,
+                                                        float* __restrict__ dd) {
   __shared__ float qs[64][129];
   __shared__ float mus[128];
   const int t = blockIdx.x;
@@ -207,11 +221,16 @@ __global__ void __launch_bounds__(128) tile_prep_kernel(const T* __restrict__ q,
       sq[gr] = s_q;
       sdq[gr] = s_d;
     }
+    if (dd != nullptr) {                     // |q - mu|^2 in float32 (the iso curvature's offsets)
+      const float n2 = row_sqnorm(d);
+      if (lane == 0) dd[gr] = n2;
+    }
   }
 }
 
 void launch_tile_prep(const void* q, int dtype, int64_t n, int tile_rows, const int32_t* perm, int group, float* mu,
-                      uint16_t* mu_hi, uint16_t* mu_lo, int8_t* q8, float* sq, int8_t* dq8, float* sdq, cudaStream_t st) {
+                      uint16_t* mu_hi, uint16_t* mu_lo, int8_t* q8, float* sq, int8_t* dq8, float* sdq, float* dd,
+                      cudaStream_t st) {
   const int tr = tile_rows == 32 ? 32 : 64;
   const int64_t nt = (n + tr - 1) / tr;
   const int g = group > 1 ? group : 1;
@@ -220,12 +239,12 @@ void launch_tile_prep(const void* q, int dtype, int64_t n, int tile_rows, const 
     const uint16_t* qb = static_cast<const uint16_t*>(q);
     if (g > 1) group_centre_kernel<uint16_t><<<ng, 128, 0, st>>>(qb, perm, n, tr, nt, g, mu, mu_hi, mu_lo);
     tile_prep_kernel<uint16_t><<<static_cast<unsigned>(nt), 128, 0, st>>>(qb, perm, n, tr, g, mu, mu_hi, mu_lo, q8,
-                                                                         sq, dq8, sdq);
+                                                                         sq, dq8, sdq, dd);
   } else {
     const float* qf = static_cast<const float*>(q);
     if (g > 1) group_centre_kernel<float><<<ng, 128, 0, st>>>(qf, perm, n, tr, nt, g, mu, mu_hi, mu_lo);
     tile_prep_kernel<float><<<static_cast<unsigned>(nt), 128, 0, st>>>(qf, perm, n, tr, g, mu, mu_hi, mu_lo, q8, sq,
-                                                                      dq8, sdq);
+                                                                      dq8, sdq, dd);
   }
 }
 

@@ -7,7 +7,8 @@
 // owning TMEM lane l reduces its 64 columns.  One CTA per tile; warp 0 loads (TMA), warp 1 issues
 // MMAs, warps 2-5 reduce.  The state is streamed once (HBM-bound).  With groups of G tiles sharing one
 // state row (h3/htrc_flat.py:223-231) the CTA of tile t reads state row t / G and writes its own sel row;
-// the maximum over the group's tiles is taken by the routing kernel.
+// the maximum over the group's tiles is taken by the routing kernel.  ISO adds the isotropic curvature
+// term c_l * |q_r - mu|^2 to every logit before the maximum (h3/htrc_flat.py:331-333).
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -16,10 +17,10 @@ namespace htrc {
 namespace {
 constexpr int kStages = 3;
 constexpr uint32_t kBlkBytes = 128 * 128;          // 128 leaves x 128 B of g8
-constexpr uint32_t kParBytes = 2 * 128 * 4;         // sg[128], lz[128]
+constexpr uint32_t kParBytes = 3 * 128 * 4;         // sg[128], lz[128], cv[128] (ISO)
 constexpr uint32_t kStageBytes = kBlkBytes + kParBytes;
 constexpr uint32_t kOffDq = 0;                      // 64 rows x 128 B
-constexpr uint32_t kOffSdq = kOffDq + 64 * 128;     // 64 floats
+constexpr uint32_t kOffSdq = kOffDq + 64 * 128;     // 64 floats, then dd[64] (ISO)
 constexpr uint32_t kOffStage = kOffSdq + 1024;      // 1024-aligned
 constexpr uint32_t kOffBar = kOffStage + kStages * ((kStageBytes + 1023) / 1024 * 1024);
 constexpr uint32_t kStageStride = (kStageBytes + 1023) / 1024 * 1024;
@@ -37,10 +38,12 @@ struct Bars {
 };
 }  // namespace
 
+template <bool ISO>
 __global__ void __launch_bounds__(192)
     rowmax_kernel(const __grid_constant__ CUtensorMap tm_dq8, const __grid_constant__ CUtensorMap tm_g8,
                   const __grid_constant__ CUtensorMap tm_sg, const __grid_constant__ CUtensorMap tm_lz,
-                  const float* __restrict__ sdq, float* __restrict__ sel, int64_t pitch, int64_t t0, int nb,
+                  const __grid_constant__ CUtensorMap tm_cv, const float* __restrict__ sdq,
+                  const float* __restrict__ dd, float* __restrict__ sel, int64_t pitch, int64_t t0, int nb,
                   int group, int* status) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -74,17 +77,19 @@ __global__ void __launch_bounds__(192)
   if (warp == 0) {
     if (lane == 0) {
       const uint64_t pol_stream = policy_evict_first();
-      mbar_arrive_expect_tx(&bars->dq_full, 64 * 128 + 256);
+      mbar_arrive_expect_tx(&bars->dq_full, 64 * 128 + 256 + (ISO ? 256 : 0));
       tma_load_2d(smem + kOffDq, &tm_dq8, &bars->dq_full, 0, static_cast<int>(tg * 64), pol_stream);
       bulk_load(smem + kOffSdq, sdq + tg * 64, 256, &bars->dq_full, pol_stream);
+      if (ISO) bulk_load(smem + kOffSdq + 256, dd + tg * 64, 256, &bars->dq_full, pol_stream);
       for (int j = 0; j < nblk; ++j) {
         const int s = j % kStages;
         if (j >= kStages && !mbar_wait(&bars->empty[s], ((j / kStages) - 1) & 1, status, abort_flag)) break;
         uint8_t* st = smem + kOffStage + s * kStageStride;
-        mbar_arrive_expect_tx(&bars->full[s], kStageBytes);
+        mbar_arrive_expect_tx(&bars->full[s], kBlkBytes + 1024 + (ISO ? 512 : 0));
         tma_load_3d(st, &tm_g8, &bars->full[s], 0, j * 128, srow, pol_stream);
         tma_load_2d(st + kBlkBytes, &tm_sg, &bars->full[s], j * 128, srow, pol_stream);
         tma_load_2d(st + kBlkBytes + 512, &tm_lz, &bars->full[s], j * 128, srow, pol_stream);
+        if (ISO) tma_load_2d(st + kBlkBytes + 1024, &tm_cv, &bars->full[s], j * 128, srow, pol_stream);
       }
     }
   } else if (warp == 1) {
@@ -111,6 +116,7 @@ __global__ void __launch_bounds__(192)
     const int r = quarter * 32 + lane;                 // leaf within the block
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const float* sdq_s = reinterpret_cast<const float*>(smem + kOffSdq);
+    const float* dd_s = sdq_s + 64;
     if (mbar_wait(&bars->dq_full, 0, status, abort_flag)) {
       for (int j = 0; j < nblk; ++j) {
         const int s = j % kStages, b = j & 1;
@@ -127,12 +133,18 @@ __global__ void __launch_bounds__(192)
         const uint8_t* st = smem + kOffStage + s * kStageStride;
         const float sgl = reinterpret_cast<const float*>(st + kBlkBytes)[r];
         const float lzl = reinterpret_cast<const float*>(st + kBlkBytes + 512)[r];
+        const float cvl = ISO ? reinterpret_cast<const float*>(st + kBlkBytes + 1024)[r] : 0.f;
         mbar_arrive(&bars->empty[s]);
         float best = -INFINITY;
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          best = fmaxf(best, __fmul_rn(static_cast<float>(static_cast<int>(d0[i])), __fmul_rn(sdq_s[i], sgl)));
-          best = fmaxf(best, __fmul_rn(static_cast<float>(static_cast<int>(d1[i])), __fmul_rn(sdq_s[32 + i], sgl)));
+          float a = __fmul_rn(static_cast<float>(static_cast<int>(d0[i])), __fmul_rn(sdq_s[i], sgl));
+          float b = __fmul_rn(static_cast<float>(static_cast<int>(d1[i])), __fmul_rn(sdq_s[32 + i], sgl));
+          if (ISO) {
+            a = __fadd_rn(a, __fmul_rn(cvl, dd_s[i]));
+            b = __fadd_rn(b, __fmul_rn(cvl, dd_s[32 + i]));
+          }
+          best = fmaxf(best, fmaxf(a, b));
         }
         const int leaf = j * 128 + r;
         if (leaf < nb) sel[static_cast<int64_t>(tloc) * pitch + leaf] = __fadd_rn(best, lzl);
@@ -145,18 +157,21 @@ __global__ void __launch_bounds__(192)
   if (warp == 1) tmem_dealloc(tmem, kTmemCols);
 }
 
-int launch_rowmax(const RowmaxMaps& maps, const float* sdq, float* sel, int64_t pitch, int64_t t0, int64_t tc, int nb,
-                  int group, int* status, cudaStream_t st) {
+int launch_rowmax(const RowmaxMaps& maps, const float* sdq, const float* dd, float* sel, int64_t pitch, int64_t t0,
+                  int64_t tc, int nb, int group, int* status, cudaStream_t st) {
   static bool attr_done[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr_done[dev]) {
-    if (cudaFuncSetAttribute(rowmax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess)
+    if (cudaFuncSetAttribute(rowmax_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(rowmax_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess)
       return HTRC_ERR_CUDA;
     attr_done[dev] = true;
   }
-  rowmax_kernel<<<static_cast<unsigned>(tc), 192, kSmemBytes, st>>>(maps.dq8, maps.g8, maps.sg, maps.lz, sdq, sel,
-                                                                     pitch, t0, nb, group > 1 ? group : 1, status);
+  auto kernel = dd != nullptr ? rowmax_kernel<true> : rowmax_kernel<false>;
+  kernel<<<static_cast<unsigned>(tc), 192, kSmemBytes, st>>>(maps.dq8, maps.g8, maps.sg, maps.lz, maps.cv, sdq, dd, sel,
+                                                             pitch, t0, nb, group > 1 ? group : 1, status);
   return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
 }
 

@@ -11,6 +11,10 @@
 //   g8/vbar rows staged in shared memory and written by TMA stores, lz/sg by plain stores.
 // This is the arithmetic of h3/htrc_flat_triton.py:41-85 (_stats_kernel, I8=1); the hi/lo splits keep
 // the products at ~2^-16 relative precision (the reference uses tf32 dots).
+// ISO adds the isotropic curvature of each (centre, leaf) (h3/htrc_flat.py:331-333, the torch
+// backend's curvature="iso"): c = 0.5 / D * max(tr, 0), tr = scale^2 (sum_s w_s |k_s|^2 - |sum_s w_s k_s|^2);
+// the softmax warps form sum_s w_s |k_s|^2 from the key norms staged with K/V, the epilogue |G|^2 from
+// its G columns (the two halves exchange partial sums with their abs-maxima).
 //
 // Warp roles (512 threads, one role per warpgroup so that setmaxnreg can move registers from the
 // issuing warps to the arithmetic): warpgroup 0 = warp 0 TMA producer, warp 1 S issuer (+ TMEM owner),
@@ -36,7 +40,10 @@ constexpr uint32_t kOffWLo = kOffWHi + kWBytes;
 constexpr uint32_t kOffStG = kOffWLo + kWBytes;     // g8 staging: 128 rows x 128 B
 constexpr uint32_t kOffStV = kOffStG + 128 * 128;   // vbar staging: 2 x (128 rows x 128 B)
 constexpr uint32_t kOffAm = kOffStV + 2 * 128 * 128;  // row abs-max halves [2 (leaf parity)][2 (half)][128]
-constexpr uint32_t kOffBar = kOffAm + 2 * 2 * 128 * 4;
+constexpr uint32_t kOffB2 = kOffAm + 2 * 2 * 128 * 4;   // ISO: |G|^2 halves [2][2][128]
+constexpr uint32_t kOffAw = kOffB2 + 2 * 2 * 128 * 4;   // ISO: sum_s w_s |k_s|^2 [2 (leaf parity)][128]
+constexpr uint32_t kOffKn = kOffAw + 2 * 128 * 4;       // ISO: key norms of each K/V stage [kStages][64]
+constexpr uint32_t kOffBar = kOffKn + kStages * 64 * 4;
 constexpr uint32_t kSmemBytes = kOffBar + 256 + 1024;  // + barriers, + alignment slack
 
 constexpr uint32_t kTmemCols = 512;
@@ -81,12 +88,14 @@ __device__ __forceinline__ uint2 half_away_codes2(float2 y) {
 }
 }  // namespace
 
+template <bool ISO>
 __global__ void __launch_bounds__(kThreads, 1)
     leaf_stats_kernel(const uint16_t* __restrict__ mu_hi_g, const uint16_t* __restrict__ mu_lo_g, int64_t nt,
                       const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                       const __grid_constant__ CUtensorMap tm_g8, const __grid_constant__ CUtensorMap tm_vb,
                       float* __restrict__ sg_out, float* __restrict__ lz_out, int64_t pitch, int64_t t0, int64_t tc,
-                      int nb, int leaves_per_cta, float scale, int* status) {
+                      int nb, int leaves_per_cta, float scale, const float* __restrict__ kn2,
+                      float* __restrict__ cv_out, int* status) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Bars* bars = reinterpret_cast<Bars*>(smem + kOffBar);
@@ -141,9 +150,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (leader) {
             uint8_t* st = smem + kOffStage + s * kStageBytes;
             const int row = (l_begin + j) * 64;
-            mbar_arrive_expect_tx(&bars->kv_full[s], kStageBytes);
+            mbar_arrive_expect_tx(&bars->kv_full[s], kStageBytes + (ISO ? 256 : 0));
             tma_load_3d(st, &tm_k, &bars->kv_full[s], 0, row, 0, pol_keep);        // both 64-column halves
             tma_load_3d(st + kLeafBytes, &tm_v, &bars->kv_full[s], 0, row, 0, pol_keep);
+            if (ISO) bulk_load(smem + kOffKn + s * 256, kn2 + row, 256, &bars->kv_full[s], pol_keep);
           }
           __syncwarp();
         }
@@ -290,12 +300,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float2 zz = add2(add2(zs[0], zs[1]), add2(zs[2], zs[3]));
       const float z = zz.x + zz.y;
       const float lz = m + logf(z);
+      float kw = 0.f;                           // ISO: sum_s e_s |k_s|^2 (divided by z below)
+      if (ISO) {
+        const float4* kn = reinterpret_cast<const float4*>(smem + kOffKn + (j % kStages) * 256);
+        float2 acc2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float4 c = kn[i];
+          acc2[i & 1] = fma2(make_float2(a[4 * i], a[4 * i + 1]), make_float2(c.x, c.y), acc2[i & 1]);
+          acc2[i & 1] = fma2(make_float2(a[4 * i + 2], a[4 * i + 3]), make_float2(c.z, c.w), acc2[i & 1]);
+        }
+        const float2 t = add2(acc2[0], acc2[1]);
+        kw = t.x + t.y;
+      }
       if (valid) {
         lz_out[tloc * pitch + leaf] = lz;
         if (!isfinite(lz)) flag_status(status, ST_NONFINITE);
       }
       const float rz = 1.0f / z;
       if (j >= 1 && !mbar_wait(&bars->w_empty, (j - 1) & 1, status, abort_flag)) break;
+      // after w_empty(j - 1): the epilogue read this parity's value (for leaf j - 2) before G/VB(j - 1) began
+      if (ISO) reinterpret_cast<float*>(smem + kOffAw)[(j & 1) * 128 + row] = kw * rz;
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         uint32_t hi[4], lo[4];
@@ -349,6 +374,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 16; ++i) vbw[16 + i] = pack_bf16x2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
       }
+      float aw = 0.f, b2 = 0.f;                 // ISO: sum w |k|^2 of this row, this half's |G|^2
+      if (ISO) {
+        aw = reinterpret_cast<const float*>(smem + kOffAw)[(j & 1) * 128 + row];
+        float2 s2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+#pragma unroll
+        for (int i = 0; i < 64; i += 2) {
+          const float2 gg = make_float2(__uint_as_float(gr[i]), __uint_as_float(gr[i + 1]));
+          s2[(i >> 1) & 1] = fma2(gg, gg, s2[(i >> 1) & 1]);
+        }
+        const float2 t = add2(s2[0], s2[1]);
+        b2 = t.x + t.y;
+      }
       tc_fence_before();
       mbar_arrive(&bars->gv_empty);
       // abs-max of g = scale * G, as scale * max |G| (scale > 0 and rounding is monotonic, so this is the
@@ -360,8 +397,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         ama[(i >> 1) & 3] = max3(ama[(i >> 1) & 3], fabsf(__uint_as_float(gr[i])), fabsf(__uint_as_float(gr[i + 1])));
       float am = __fmul_rn(fmaxf(fmaxf(ama[0], ama[1]), fmaxf(ama[2], ama[3])), scale);
       amx[((j & 1) * 2 + half) * 128 + row] = am;
+      if (ISO) reinterpret_cast<float*>(smem + kOffB2)[((j & 1) * 2 + half) * 128 + row] = b2;
       named_bar_sync(1 + quarter, 64);
       am = fmaxf(am, amx[((j & 1) * 2 + (half ^ 1)) * 128 + row]);
+      if (ISO && half == 0) {
+        const float gg = b2 + reinterpret_cast<const float*>(smem + kOffB2)[((j & 1) * 2 + 1) * 128 + row];
+        const float tr = __fmul_rn(__fmul_rn(scale, scale), __fsub_rn(aw, gg));
+        if (valid) cv_out[tloc * pitch + leaf] = __fmul_rn(0.5f / 128.0f, fmaxf(tr, 0.f));
+      }
       am = fmaxf(am, 1e-30f);
       const float sgv = __fmul_rn(am, 1.0f / 127.0f);
       const float rr = __fdiv_rn(127.0f, am);
@@ -410,12 +453,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 int launch_leaf_stats(const LeafStatsMaps& maps, float* sg, float* lz, int64_t pitch, int64_t t0, int64_t tc, int nb,
-                      float scale, int* status, int num_sms, cudaStream_t st) {
+                      float scale, const float* kn2, float* cv, int* status, int num_sms, cudaStream_t st) {
   static bool attr_done[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr_done[dev]) {
-    if (cudaFuncSetAttribute(leaf_stats_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess)
+    if (cudaFuncSetAttribute(leaf_stats_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(leaf_stats_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
+            cudaSuccess)
       return HTRC_ERR_CUDA;
     attr_done[dev] = true;
   }
@@ -424,9 +470,9 @@ int launch_leaf_stats(const LeafStatsMaps& maps, float* sg, float* lz, int64_t p
   by = min(by, nb);
   const int lpc = (nb + by - 1) / by;
   by = (nb + lpc - 1) / lpc;
-  leaf_stats_kernel<<<dim3(bx, by), kThreads, kSmemBytes, st>>>(maps.mu_hi, maps.mu_lo, maps.nt, maps.k, maps.v, maps.g8,
-                                                                maps.vb, sg, lz, pitch, t0, tc, nb, lpc, scale,
-                                                                status);
+  auto kernel = cv != nullptr ? leaf_stats_kernel<true> : leaf_stats_kernel<false>;
+  kernel<<<dim3(bx, by), kThreads, kSmemBytes, st>>>(maps.mu_hi, maps.mu_lo, maps.nt, maps.k, maps.v, maps.g8, maps.vb,
+                                                     sg, lz, pitch, t0, tc, nb, lpc, scale, kn2, cv, status);
   return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
 }
 

@@ -28,6 +28,9 @@
 // repeat row 31; only rows < 32 are written, and the softmax warps that own only such rows skip the
 // arithmetic (they keep their place in the barrier protocol and leave P = 0).
 //
+// ISO adds the isotropic curvature term c_l * |q_r - mu|^2 to every far logit (h3/htrc_flat.py:331-333,
+// the torch backend's curvature="iso"; c_l from the leaf statistics, |q_r - mu|^2 from the tile prep).
+//
 // Groups (h3/htrc_flat.py:223-231): G consecutive tiles share one far-field state row and one routing;
 // tile t of the chunk reads state row t / G.  k-means order (:146-147, :159-165): tile row i is query
 // perm[i], so the epilogue writes out/lse row perm[i] (and reads the tail partial of that row).
@@ -47,7 +50,7 @@ constexpr int kYSlots = 3;
 constexpr int kSBufs = 4;
 constexpr uint32_t kXBytes = 64 * 128;                          // g8 block / k8 leaf: 64 rows x 128 B
 constexpr uint32_t kYBytes = 64 * 256;                          // vbar block / v leaf: 2 chunks of 64x64 bf16
-constexpr uint32_t kParBytes = 1024;                            // far: lz[64], sg[64], excl[64]; near: ks[64]
+constexpr uint32_t kParBytes = 1024;                            // far: lz[64], sg[64], excl[64], cv[64]; near: ks[64]
 constexpr uint32_t kXTile = kXBytes + kParBytes;                // 9216 (a multiple of 1024)
 constexpr uint32_t kXSlot = 2 * kXTile;
 constexpr uint32_t kYSlot = 2 * kYBytes;
@@ -59,7 +62,8 @@ constexpr uint32_t kOffCC = kOffY + kYSlots * kYSlot;           // [X slot][tile
 constexpr uint32_t kOffEpi = kOffCC + kXSlots * 2 * 64 * 8;     // m1, l1 [128] each
 constexpr uint32_t kOffIdx = kOffEpi + 2 * 128 * 4;             // [tile][kMaxKx] uint16
 constexpr int kMaxKx = 1024;
-constexpr uint32_t kOffBar = kOffIdx + 2 * kMaxKx * 2;
+constexpr uint32_t kOffCC3 = kOffIdx + 2 * kMaxKx * 2;          // ISO: [X slot][tile][64] c * log2 e (0 for near)
+constexpr uint32_t kOffBar = kOffCC3 + kXSlots * 2 * 64 * 4;
 constexpr uint32_t kSmemBytes = kOffBar + 512 + 1024;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0;       // S/P buffer b (= step % 4) at 64 b; P uses its first 32 columns
@@ -93,13 +97,14 @@ __device__ __forceinline__ float ex2(float x) {
 
 }  // namespace
 
-template <int TROWS>
+template <int TROWS, bool ISO>
 __global__ void __launch_bounds__(kThreads, 1)
     tile_attention_kernel(const __grid_constant__ CUtensorMap tm_q8, const __grid_constant__ CUtensorMap tm_dq8,
                           const __grid_constant__ CUtensorMap tm_g8, const __grid_constant__ CUtensorMap tm_vb,
                           const __grid_constant__ CUtensorMap tm_lz, const __grid_constant__ CUtensorMap tm_sg,
                           const __grid_constant__ CUtensorMap tm_excl, const __grid_constant__ CUtensorMap tm_k8,
-                          const __grid_constant__ CUtensorMap tm_v, const float* __restrict__ sq,
+                          const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_cv,
+                          const float* __restrict__ dd, const float* __restrict__ sq,
                           const float* __restrict__ sdq, const float* __restrict__ ks, const int32_t* __restrict__ idx,
                           int kx, int nb, int nf, int64_t n, int64_t t0, int64_t tc, int group,
                           float scale,
@@ -178,7 +183,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int s = nx % kXSlots;
           uint8_t* st = smem + kOffX + s * kXSlot;
           if (nx < nf) {
-            mbar_arrive_expect_tx(&bars->x_full[s], (kXBytes + 256 + 256 + 64) * ntiles);
+            mbar_arrive_expect_tx(&bars->x_full[s], (kXBytes + 256 + 256 + 64 + (ISO ? 256 : 0)) * ntiles);
             for (int x = 0; x < ntiles; ++x) {
               uint8_t* tx = st + x * kXTile;
               const int tl = srow[x];
@@ -186,6 +191,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               tma_load_2d(tx + kXBytes, &tm_lz, &bars->x_full[s], nx * 64, tl, pol_stream);
               tma_load_2d(tx + kXBytes + 256, &tm_sg, &bars->x_full[s], nx * 64, tl, pol_stream);
               tma_load_2d(tx + kXBytes + 512, &tm_excl, &bars->x_full[s], nx * 64, tl, pol_stream);
+              if (ISO) tma_load_2d(tx + kXBytes + 768, &tm_cv, &bars->x_full[s], nx * 64, tl, pol_stream);
             }
           } else {
             mbar_arrive_expect_tx(&bars->x_full[s], (kXBytes + 256) * ntiles);
@@ -309,8 +315,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float sgv = reinterpret_cast<const float*>(par + 256)[i];
           const bool masked = par[512 + i] != 0 || j * 64 + i >= nb;
           v = make_float2(sgv * kLog2e, masked ? -INFINITY : lzv * kLog2e);
+          if (ISO) reinterpret_cast<float*>(smem + kOffCC3)[s * 128 + colq] =
+              reinterpret_cast<const float*>(par + 768)[i] * kLog2e;
         } else {
           v = make_float2(reinterpret_cast<const float*>(par)[i] * near_scale, 0.f);
+          if (ISO) reinterpret_cast<float*>(smem + kOffCC3)[s * 128 + colq] = 0.f;
         }
         c[colq] = v;
       }
@@ -331,6 +340,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int64_t gr = (t0 + tl) * 64 + r;
     const float sq_r = has_tile ? __ldg(sq + gr) : 0.f;
     const float sdq_r = has_tile ? __ldg(sdq + gr) : 0.f;
+    const float dd_r = (ISO && has_tile) ? __ldg(dd + gr) : 0.f;
     float m_used = -INFINITY, l = 0.f;
     bool aborted = false;
     int kcount = 0;
@@ -358,6 +368,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld_wait();
       if (!mbar_wait_warp(&bars->cc_full[s], (j / kXSlots) & 1, status, abort_flag)) { aborted = true; break; }
       const float2* c = cc + s * 128 + x * 64;
+      const float* c3 = reinterpret_cast<const float*>(smem + kOffCC3) + s * 128 + x * 64;
+      const float2 dd2 = make_float2(dd_r, dd_r);
       const float srow = j < nf ? sdq_r : sq_r;
       const float2 srow2 = make_float2(srow, srow);
       const float2 magic2 = make_float2(kMagic, kMagic);
@@ -372,7 +384,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                                       __int_as_float(static_cast<int>(di1) + kMagicBits));
         const float2 fd = sub2(xm, magic2);
         const float2 t = mul2(srow2, make_float2(cv.x, cv.z));
-        const float2 v = fma2(fd, t, make_float2(cv.y, cv.w));
+        float2 v = fma2(fd, t, make_float2(cv.y, cv.w));
+        if (ISO) v = fma2(*reinterpret_cast<const float2*>(c3 + i), dd2, v);
         lg[i] = v.x;
         lg[i + 1] = v.y;
         mxa[(i >> 1) & 3] = fmaxf(mxa[(i >> 1) & 3], fmaxf(v.x, v.y));
@@ -490,26 +503,28 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 int launch_tile_attention(const TileMaps& maps, const float* sq, const float* sdq, const float* ks, const int32_t* idx,
                           int kx, int nb, int64_t n, int tile_rows, int64_t t0, int64_t tc, int group, float scale,
-                          const float* tail_part, const int32_t* perm, float* out, float* lse, int* status,
-                          cudaStream_t st) {
+                          const float* tail_part, const int32_t* perm, const float* dd, float* out, float* lse,
+                          int* status, cudaStream_t st) {
   if (kx > kMaxKx || nb > 65535) return HTRC_ERR_UNSUPPORTED;
   static bool attr_done[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr_done[dev]) {
-    if (cudaFuncSetAttribute(tile_attention_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
-            cudaSuccess ||
-        cudaFuncSetAttribute(tile_attention_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
-            cudaSuccess)
-      return HTRC_ERR_CUDA;
+    bool ok = true;
+    for (auto k : {tile_attention_kernel<64, false>, tile_attention_kernel<32, false>, tile_attention_kernel<64, true>,
+                   tile_attention_kernel<32, true>})
+      ok = ok && cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) == cudaSuccess;
+    if (!ok) return HTRC_ERR_CUDA;
     attr_done[dev] = true;
   }
   const int nf = kx >= nb ? 0 : (nb + 63) / 64;
   const unsigned grid = static_cast<unsigned>((tc + 1) / 2);
-  auto kernel = tile_rows == 32 ? tile_attention_kernel<32> : tile_attention_kernel<64>;
+  const bool iso = dd != nullptr;
+  auto kernel = tile_rows == 32 ? (iso ? tile_attention_kernel<32, true> : tile_attention_kernel<32, false>)
+                                : (iso ? tile_attention_kernel<64, true> : tile_attention_kernel<64, false>);
   kernel<<<grid, kThreads, kSmemBytes, st>>>(maps.q8, maps.dq8, maps.g8, maps.vb, maps.lz, maps.sg, maps.excl, maps.k8,
-                                             maps.v, sq, sdq, ks, idx, kx, nb, nf, n, t0, tc, group > 1 ? group : 1,
-                                             scale, tail_part, perm, out, lse, status);
+                                             maps.v, maps.cv, dd, sq, sdq, ks, idx, kx, nb, nf, n, t0, tc,
+                                             group > 1 ? group : 1, scale, tail_part, perm, out, lse, status);
   return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
 }
 

@@ -7,6 +7,10 @@ C-ABI library libhtrc_flat.so (hand-written sm_100a kernels).  There is no other
 fallback: configurations the kernels do not implement raise ``NotImplementedError`` and argument
 errors raise the reference's ``ValueError``s.
 
+Curvature: ``curvature="iso"`` with ``backend="cuda"`` (or "b200") adds the isotropic second-order far-field
+term of the reference's torch backend (h3/htrc_flat.py:331-333) to the INT8 production path; the
+reference's triton backend rejects it, and so does ``backend="triton"`` here.
+
 Query order and groups: ``order="kmeans"`` (the accurate/max modes) reorders the queries on the device
 by the reference's k-means permutation before tiling and writes the output back in the caller's order
 (h3/htrc_flat.py:47-65, :146-147, :159-165); ``kern={"group": G}`` lets G consecutive tiles share one
@@ -77,8 +81,9 @@ def _check_args(q, k, v, tile, exact_leaves, order, curvature, leaf, select, bac
         raise NotImplementedError("backend='torch' is the reference's float32 CPU specification; this library runs "
                                   "the sm_100a INT8 production path (pass **PROD, or backend='triton', store='int8', "
                                   "dot='bf16')")
-    if curvature != "lin":
-        raise ValueError("triton backend needs curvature='lin'")
+    if curvature != "lin" and (backend == "triton" or curvature != "iso"):
+        raise ValueError("triton backend needs curvature='lin'" if backend == "triton" else
+                         "curvature must be lin or iso")
     m = int(k.shape[0])
     if m % leaf:
         raise ValueError("triton backend: key count must be a multiple of the leaf size")
@@ -170,8 +175,12 @@ def order_code(order) -> int:
     return _lib.ORDER_KMEANS if order == "kmeans" else _lib.ORDER_SEQ
 
 
+def curvature_code(curvature) -> int:
+    return _lib.CURV_ISO if curvature == "iso" else _lib.CURV_LIN
+
+
 def _args(qd, kb, vb, tk, tv, exact_leaves, sink_leaves, tile_chunk, scale, out=None, lse=None, ws=None,
-          stage_events=None, group=1, order=_lib.ORDER_SEQ, tile=TILE):
+          stage_events=None, group=1, order=_lib.ORDER_SEQ, tile=TILE, curvature=_lib.CURV_LIN):
     a = _lib.HtrcFlatArgs()
     a.q = ptr(qd)
     a.q_dtype = _lib.DTYPE_BF16 if qd.dtype == torch.bfloat16 else _lib.DTYPE_F32
@@ -184,7 +193,7 @@ def _args(qd, kb, vb, tk, tv, exact_leaves, sink_leaves, tile_chunk, scale, out=
     a.tail_k, a.tail_v = ptr(tk), ptr(tv)
     a.n_tail = int(tk.shape[0]) if tk is not None else 0
     a.out, a.lse = ptr(out), ptr(lse)
-    a.group, a.order = int(group), int(order)
+    a.group, a.order, a.curvature = int(group), int(order), int(curvature)
     if ws is not None:
         a.workspace, a.workspace_bytes = ptr(ws), int(ws.numel())
     if stage_events:
@@ -201,14 +210,14 @@ def _args(qd, kb, vb, tk, tv, exact_leaves, sink_leaves, tile_chunk, scale, out=
 
 
 def workspace_bytes(n_queries, n_keys, exact_leaves, sink_leaves=0, tile_chunk=0, n_tail=0, group=1,
-                    order=_lib.ORDER_SEQ, tile=TILE) -> int:
+                    order=_lib.ORDER_SEQ, tile=TILE, curvature=_lib.CURV_LIN) -> int:
     """Device workspace one forward call needs."""
     a = _lib.HtrcFlatArgs()
     a.n_queries, a.n_keys, a.dim, a.tile, a.leaf = int(n_queries), int(n_keys), DIM, int(tile), LEAF
     a.q_dtype = _lib.DTYPE_F32
     a.exact_leaves, a.sink_leaves = int(exact_leaves), int(sink_leaves)
     a.tile_chunk, a.n_tail = int(tile_chunk or 0), int(n_tail)
-    a.group, a.order = int(group), int(order)
+    a.group, a.order, a.curvature = int(group), int(order), int(curvature)
     nbytes = ctypes.c_size_t()
     check(lib().htrc_flat_workspace_size(a, nbytes), "workspace size")
     return int(nbytes.value)
@@ -235,13 +244,14 @@ def _workspace(ws, nbytes, device):
 
 
 def forward_into(qd, kb, vb, tk, tv, *, exact_leaves, sink_leaves=0, tile_chunk=0, scale=None, out, lse=None,
-                 workspace, stream=None, stage_events=None, group=1, order=_lib.ORDER_SEQ, tile=TILE):
+                 workspace, stream=None, stage_events=None, group=1, order=_lib.ORDER_SEQ, tile=TILE,
+                 curvature=_lib.CURV_LIN):
     """One head through ``htrc_flat_forward`` into caller-provided buffers (no allocation; CUDA-graph
     capturable).  qd [N, 128] f32/bf16, kb/vb [M, 128] bf16, out [N, 128] f32, lse [N] f32 or None;
     stage_events: optional list of torch.cuda.Event recorded between the stages (see
     include/htrc_flat.h); group / order: ``group_of(kern)`` / ``order_code(order)``; tile: 64 or 32."""
     a = _args(qd, kb, vb, tk, tv, exact_leaves, sink_leaves, tile_chunk, scale, out, lse, workspace, stage_events,
-              group, order, tile)
+              group, order, tile, curvature)
     check(lib().htrc_flat_forward(a, stream_ptr(stream)), "htrc_flat_forward")
 
 
@@ -269,19 +279,20 @@ def flat_attention(q, k, v, *, tile=64, exact_leaves=64, order="seq", curvature=
     _check_args(q, k, v, tile, exact_leaves, order, curvature, leaf, select, backend, store, dot,
                 sel_stride, quant, sink_leaves, tail)
     qd, kb, vb, tk, tv = _prep_inputs(q, k, v, tail, quant)
-    grp, oc = group_of(kern), order_code(order)
+    grp, oc, cc = group_of(kern), order_code(order), curvature_code(curvature)
     if prof is not None:
         st = run_stages(qd, kb, vb, tk, tv, exact_leaves=exact_leaves, sink_leaves=sink_leaves,
-                        tile_chunk=tile_chunk, scale=scale, prof=prof, group=grp, order=oc, tile=tile)
+                        tile_chunk=tile_chunk, scale=scale, prof=prof, group=grp, order=oc, tile=tile, curvature=cc)
         return (st["out"], st["lse"]) if return_lse else st["out"]
     n = int(qd.shape[0])
     out = torch.empty((n, DIM), dtype=torch.float32, device=q.device)
     lse = torch.empty((n,), dtype=torch.float32, device=q.device) if return_lse else None
     nbytes = workspace_bytes(n, int(kb.shape[0]), exact_leaves, sink_leaves, tile_chunk,
-                             int(tk.shape[0]) if tk is not None else 0, grp, oc, tile)
+                             int(tk.shape[0]) if tk is not None else 0, grp, oc, tile, cc)
     w = _workspace(ws, nbytes, q.device)
     forward_into(qd, kb, vb, tk, tv, exact_leaves=exact_leaves, sink_leaves=sink_leaves,
-                 tile_chunk=tile_chunk, scale=scale, out=out, lse=lse, workspace=w, group=grp, order=oc, tile=tile)
+                 tile_chunk=tile_chunk, scale=scale, out=out, lse=lse, workspace=w, group=grp, order=oc, tile=tile,
+                 curvature=cc)
     return (out, lse) if return_lse else out
 
 
@@ -292,7 +303,7 @@ def flat_attention_prod(q, k, v, **over):
 
 @torch.inference_mode()
 def run_stages(qd, kb, vb, tk=None, tv=None, *, exact_leaves, sink_leaves=0, tile_chunk=0, scale=None,
-               prof=None, stream=None, group=1, order=_lib.ORDER_SEQ, tile=TILE):
+               prof=None, stream=None, group=1, order=_lib.ORDER_SEQ, tile=TILE, curvature=_lib.CURV_LIN):
     """The same operator launched stage by stage through the C ABI's stage entry points, returning
     every intermediate (perm, k8, ks, mu, q8, sq, dq8, sdq, g8, sg, lz, vb, sel, idx, excl, out, lse).
     Used for stage timing (``prof``, the reference's stage names prep/stats/select/tile/finish) and
@@ -320,9 +331,11 @@ def run_stages(qd, kb, vb, tk=None, tv=None, *, exact_leaves, sink_leaves=0, til
              dtype=torch.float32, device=dev), idx=e(ng, max(kx, 1), dt=torch.int32),
              excl=e(ng, pitch, dt=torch.uint8), out=e(n, DIM), lse=e(n),
              status=torch.zeros((1,), dtype=torch.int32, device=dev), perm=None)
+    iso = curvature == _lib.CURV_ISO
+    r.update(kn2=e(m) if iso else None, dd=e(nt * TILE) if iso else None, cv=e(ng, pitch) if iso else None)
     stp = ptr(r["status"])
-    check(L.htrc_pack_int8(ptr(kb), _lib.DTYPE_BF16, m, DIM, _lib.ROUND_HALF_EVEN, ptr(r["k8"]), ptr(r["ks"]), s),
-          "htrc_pack_int8")
+    check(L.htrc_pack_int8(ptr(kb), _lib.DTYPE_BF16, m, DIM, _lib.ROUND_HALF_EVEN, ptr(r["k8"]), ptr(r["ks"]),
+                           ptr(r["kn2"]), s), "htrc_pack_int8")
     if order == _lib.ORDER_KMEANS:
         r["perm"] = e(n, dt=torch.int32)
         nbytes = ctypes.c_size_t()
@@ -332,7 +345,7 @@ def run_stages(qd, kb, vb, tk=None, tv=None, *, exact_leaves, sink_leaves=0, til
               "htrc_kmeans_order")
     perm = ptr(r["perm"])
     check(L.htrc_tile_prep(ptr(qd), qdt, n, DIM, tile, perm, grp, ptr(r["mu"]), ptr(r["mu_hi"]), ptr(r["mu_lo"]),
-                           ptr(r["q8"]), ptr(r["sq"]), ptr(r["dq8"]), ptr(r["sdq"]), s), "htrc_tile_prep")
+                           ptr(r["q8"]), ptr(r["sq"]), ptr(r["dq8"]), ptr(r["sdq"]), ptr(r["dd"]), s), "htrc_tile_prep")
     tail_part = None
     if tk is not None:
         tail_part = e(n, DIM + 2)
@@ -345,12 +358,12 @@ def run_stages(qd, kb, vb, tk=None, tv=None, *, exact_leaves, sink_leaves=0, til
         for g0 in range(0, ng, gstep):
             gc = min(gstep, ng - g0)
             check(L.htrc_leaf_stats(ptr(r["mu_hi"]), ptr(r["mu_lo"]), ng, g0, gc, ptr(kb), ptr(vb), m, DIM, LEAF, sc,
-                                    ptr(r["g8"][g0]), ptr(r["sg"][g0]), ptr(r["lz"][g0]), ptr(r["vb"][g0]), stp, s),
-                  "htrc_leaf_stats")
+                                    ptr(r["g8"][g0]), ptr(r["sg"][g0]), ptr(r["lz"][g0]), ptr(r["vb"][g0]),
+                                    ptr(r["kn2"]), ptr(r["cv"][g0]) if iso else None, stp, s), "htrc_leaf_stats")
     tick("stats")
     if far and kx > 0:
-        check(L.htrc_rowmax_select(ptr(r["dq8"]), ptr(r["sdq"]), 0, nt, grp, ptr(r["g8"]), ptr(r["sg"]), ptr(r["lz"]),
-                                   nb, DIM, ptr(r["sel"]), stp, s), "htrc_rowmax_select")
+        check(L.htrc_rowmax_select(ptr(r["dq8"]), ptr(r["sdq"]), ptr(r["dd"]), 0, nt, grp, ptr(r["g8"]), ptr(r["sg"]),
+                                   ptr(r["lz"]), ptr(r["cv"]), nb, DIM, ptr(r["sel"]), stp, s), "htrc_rowmax_select")
     check(L.htrc_route(ptr(r["sel"]), nt, nb, int(exact_leaves), sink, grp, ptr(r["idx"]), ptr(r["excl"]), s),
           "htrc_route")
     tick("select")
@@ -358,7 +371,7 @@ def run_stages(qd, kb, vb, tk=None, tv=None, *, exact_leaves, sink_leaves=0, til
                                 ptr(r["g8"]),
                                 ptr(r["sg"]), ptr(r["lz"]), ptr(r["vb"]), ptr(r["excl"]), ptr(r["idx"]), kx, nb,
                                 ptr(r["k8"]), ptr(r["ks"]), ptr(vb), m, DIM, LEAF, sc, ptr(tail_part), perm,
-                                ptr(r["out"]), ptr(r["lse"]), stp, s), "htrc_tile_attention")
+                                ptr(r["cv"]), ptr(r["dd"]), ptr(r["out"]), ptr(r["lse"]), stp, s), "htrc_tile_attention")
     tick("tile")
     tick("finish")
     r["kx"], r["nb"], r["pitch"], r["group"], r["tile"] = kx, nb, pitch, grp, tile

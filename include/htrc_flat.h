@@ -44,6 +44,7 @@ enum {
 
 enum { HTRC_DTYPE_F32 = 0, HTRC_DTYPE_BF16 = 1 };
 enum { HTRC_ORDER_SEQ = 0, HTRC_ORDER_KMEANS = 1 };
+enum { HTRC_CURV_LIN = 0, HTRC_CURV_ISO = 1 };
 enum { HTRC_ROUND_HALF_EVEN = 0, HTRC_ROUND_HALF_AWAY = 1 };
 enum { HTRC_FQ_INT8 = 1, HTRC_FQ_INT4 = 2, HTRC_FQ_FP8 = 3, HTRC_FQ_FP4 = 4 }; /* htrc_fake_quant formats */
 
@@ -84,6 +85,10 @@ typedef struct HtrcFlatArgs {
                               the reference's kern["group"], h3/htrc_flat.py:223-231) */
   int32_t order;           /* HTRC_ORDER_SEQ, or HTRC_ORDER_KMEANS: query rows grouped by a k-means
                               permutation first (order="kmeans", h3/htrc_flat.py:47-65, :146-147) */
+  int32_t curvature;       /* HTRC_CURV_LIN (the production far field lz + g.dq), or HTRC_CURV_ISO: plus
+                              the isotropic second-order term 0.5/D max(tr, 0) |q - mu|^2 with
+                              tr = scale^2 (sum w |k|^2 - |sum w k|^2) per (centre, leaf) -- the torch
+                              backend's curvature="iso" (h3/htrc_flat.py:331-333) on the INT8 path */
 } HtrcFlatArgs;
 
 /* nb rounded up to a multiple of 16: the row pitch of the per-(tile, leaf) scalar arrays. */
@@ -109,7 +114,7 @@ int htrc_flat_status(void* workspace, int32_t* status_out, htrc_stream_t stream)
  * HTRC_ROUND_HALF_EVEN: x8 = clamp(rint(x / scale), -127, 127)   (h3/htrc_flat.py:216-218, keys)
  * HTRC_ROUND_HALF_AWAY: x8 = trunc(x / scale +- 0.5)              (h3/htrc_flat_triton.py:110-117) */
 int htrc_pack_int8(const void* x, int32_t dtype, int64_t rows, int32_t dim, int32_t rounding, int8_t* x8,
-                   float* scale, htrc_stream_t stream);
+                   float* scale, float* sqnorm, htrc_stream_t stream);   /* sqnorm: NULL or [rows] |x_row|^2 */
 
 /* Tile centres and query codes (h3/htrc_flat.py:142-156 `_tiles`, :223-231 groups;
  * h3/htrc_flat_triton.py:103-117):
@@ -121,7 +126,7 @@ int htrc_pack_int8(const void* x, int32_t dtype, int64_t rows, int32_t dim, int3
  * tile: 64 or 32; perm: NULL, or [n_queries] int32 (query i in tile order is row perm[i] of q). */
 int htrc_tile_prep(const void* q, int32_t q_dtype, int64_t n_queries, int32_t dim, int32_t tile, const int32_t* perm,
                    int32_t group, float* mu, uint16_t* mu_hi, uint16_t* mu_lo, int8_t* q8, float* sq, int8_t* dq8,
-                   float* sdq, htrc_stream_t stream);
+                   float* sdq, float* dd, htrc_stream_t stream);   /* dd: NULL or [nt*64] |q - mu|^2 (f32) */
 
 /* k-means query order (h3/htrc_flat.py:47-65 `kmeans_order`: 32 clusters, Lloyd's iterations x 8 on
  * the rows round(linspace(0, N-1, min(4096, N))) seeded with sample rows round(linspace(0, S-1, 32)),
@@ -138,15 +143,19 @@ int htrc_kmeans_order(const void* q, int32_t q_dtype, int64_t n_queries, int32_t
  * htrc_tile_prep (all nt centre rows: tiles, or groups of tiles); status: device int32 word or NULL. */
 int htrc_leaf_stats(const uint16_t* mu_hi, const uint16_t* mu_lo, int64_t nt, int64_t t0, int64_t tc,
                     const uint16_t* k, const uint16_t* v, int64_t n_keys, int32_t dim, int32_t leaf, float scale,
-                    int8_t* g8, float* sg, float* lz, uint16_t* vb, int32_t* status, htrc_stream_t stream);
+                    int8_t* g8, float* sg, float* lz, uint16_t* vb, const float* kn2, float* cv, int32_t* status,
+                    htrc_stream_t stream);
+/* kn2 / cv: both NULL, or the key norms |k|^2 [n_keys] (htrc_pack_int8's sqnorm) and the iso curvature
+ * coefficients cv [tc, P] f32 = 0.5/D max(tr, 0) to write. */
 
 /* Row-max selection sel [tc, P] f32 of tiles [t0, t0 + tc) (h3/htrc_flat_triton.py:214-254
  * `_rowmax_kernel`, I8): sel[t, l] = max_r (dq8_r . g8_l) * (sdq_r * sg_l) + lz_l over the tile's 64
  * rows, with the state row (t - t0) / group of g8/sg/lz (t0 a multiple of group).  The maximum over a
  * group's tiles is taken by htrc_route. */
-int htrc_rowmax_select(const int8_t* dq8, const float* sdq, int64_t t0, int64_t tc, int32_t group, const int8_t* g8,
-                       const float* sg, const float* lz, int64_t nb, int32_t dim, float* sel, int32_t* status,
-                       htrc_stream_t stream);
+int htrc_rowmax_select(const int8_t* dq8, const float* sdq, const float* dd, int64_t t0, int64_t tc, int32_t group,
+                       const int8_t* g8, const float* sg, const float* lz, const float* cv, int64_t nb, int32_t dim,
+                       float* sel, int32_t* status, htrc_stream_t stream);
+/* dd / cv: both NULL, or the iso curvature inputs: each logit gains cv_l * dd_r before the maximum. */
 
 /* Top-E routing of the groups of tiles [0, tc) (h3/htrc_flat.py:250-265): a group's selection is the
  * maximum of its tiles' sel rows (the reference's row-max over all G*64 rows); the first sink_leaves
@@ -168,8 +177,9 @@ int htrc_tile_attention(const int8_t* q8, const float* sq, const int8_t* dq8, co
                         const float* lz,
                         const uint16_t* vb, const uint8_t* excl, const int32_t* idx, int32_t kx, int64_t nb,
                         const int8_t* k8, const float* ks, const uint16_t* v, int64_t n_keys, int32_t dim,
-                        int32_t leaf, float scale, const float* tail_part, const int32_t* perm, float* out, float* lse,
-                        int32_t* status, htrc_stream_t stream);
+                        int32_t leaf, float scale, const float* tail_part, const int32_t* perm, const float* cv,
+                        const float* dd, float* out, float* lse, int32_t* status, htrc_stream_t stream);
+/* cv / dd: both NULL, or the iso curvature inputs (each far logit gains cv_l * dd_r). */
 
 /* Exact softmax partial of every query row against the tail keys (h3/htrc_flat_triton.py:187-207 for
  * n_tail <= 16 with bf16 operands; :381-388 float32 for longer tails): tail_part [N, dim + 2]. */

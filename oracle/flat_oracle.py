@@ -245,6 +245,30 @@ def leaf_stats(mu, k, v, leaf, scale):
     return g.astype(F32), lz.astype(F32), vb.astype(F32)
 
 
+def iso_coeff(mu, k, leaf, scale):
+    """Isotropic curvature coefficient per (centre, leaf) (h3/htrc_flat.py:331-333, the torch backend's
+    curvature="iso"): 0.5 / D * max(tr, 0), tr = scale^2 (sum_s w_s |k_s|^2 - |sum_s w_s k_s|^2), in
+    float64 rounded once."""
+    mu = np.asarray(mu, dtype=np.float64)
+    k = np.asarray(k, dtype=np.float64)
+    nb = k.shape[0] // leaf
+    d = k.shape[1]
+    k3 = k[: nb * leaf].reshape(nb, leaf, d)
+    a = np.einsum("td,lsd->tls", mu, k3) * float(scale)
+    w = np.exp(a - a.max(-1, keepdims=True))
+    w /= w.sum(-1, keepdims=True)
+    kn2 = (k3 * k3).sum(-1)                                   # [nb, leaf]
+    mean = np.einsum("tls,lsd->tld", w, k3)
+    tr = float(scale) ** 2 * ((w * kn2[None]).sum(-1) - (mean * mean).sum(-1))
+    return (0.5 / d * np.maximum(tr, 0.0)).astype(F32)
+
+
+def offset_sqnorm(qt, mu):
+    """|q_r - mu|^2 per tile row, from the float32 offsets (the iso term's row factor)."""
+    dq = (np.asarray(qt, F32) - np.asarray(mu, F32)[:, None, :]).astype(F32)
+    return (dq.astype(np.float64) ** 2).sum(-1).astype(F32)
+
+
 def state_int8(g, vb):
     """The stored far-field state: (g8, sg, vbar as bf16-rounded float32)
     (h3/htrc_flat_triton.py:73-81)."""
@@ -262,7 +286,7 @@ def query_codes(qt, mu):
     return q8, sq, dq8, sdq
 
 
-def rowmax_select(dq8, sdq, g8, sg, lz, group=1):
+def rowmax_select(dq8, sdq, g8, sg, lz, group=1, cv=None, dd=None):
     """SEL[t, l] = max_r (dq8_r . g8_l) * (sdq_r * sg_l) + lz_l (h3/htrc_flat_triton.py:240-254); with
     groups the rows are all G * T rows of a group (the reference calls the kernel with
     T = G * tile, h3/htrc_flat.py:243-249) and the state row is the group's: returns [ng, nb]."""
@@ -270,6 +294,8 @@ def rowmax_select(dq8, sdq, g8, sg, lz, group=1):
     st = np.arange(nt) // group
     dot = np.matmul(dq8.astype(np.float64), np.swapaxes(g8[st].astype(np.float64), 1, 2))
     sc = dot.astype(F32) * (sdq[:, :, None] * sg[st][:, None, :]).astype(F32)
+    if cv is not None:                                        # iso curvature: + c_l |q_r - mu|^2
+        sc = (sc + (cv[st][:, None, :] * dd[:, :, None]).astype(F32)).astype(F32)
     per_tile = (sc.max(1) + lz[st]).astype(F32)
     ng = -(-nt // group)
     out = np.full((ng, per_tile.shape[1]), -np.inf, F32)
@@ -299,7 +325,7 @@ def route(sel, exact_leaves, sink_leaves=0):
 
 
 def tile_attention(qt, q8, sq, dq8, sdq, g8, sg, lz, vb, excl, idx, k8, ks, v, leaf, scale,
-                   tail=None, group=1):
+                   tail=None, group=1, cv=None, dd=None):
     """Far field + near field + tail of every tile, merged; returns (out float32 [nt*T, D],
     lse float32 [nt*T]) (h3/htrc_flat_triton.py:88-211, merge :257-273).
 
@@ -331,6 +357,8 @@ def tile_attention(qt, q8, sq, dq8, sdq, g8, sg, lz, vb, excl, idx, k8, ks, v, l
         if keep.any():
             dot = dq8[t].astype(np.float64) @ g8[gt][keep].astype(np.float64).T
             sc = dot.astype(F32) * (sdq[t][:, None] * sg[gt][keep][None, :]).astype(F32) + lz[gt][keep][None, :]
+            if cv is not None:
+                sc = sc + (cv[gt][keep][None, :] * dd[t][:, None]).astype(F32)
             parts_s.append(sc.astype(F32))
             parts_v.append(vb[gt][keep])
             parts_r.append(np.ones(sc.shape[1], bool))
@@ -451,7 +479,7 @@ def pack_k(k):
 
 def flat_attention(q, k, v, *, tile=64, exact_leaves=256, leaf=64, scale=None, sink_leaves=0,
                    tail=None, return_stages=False, group=1, order="seq", perm=None, quant=None,
-                   stats_bf16=False):
+                   stats_bf16=False, curvature="lin"):
     """The whole production path for one head: q [N, D], k/v [M, D] (float32 arrays holding the
     caller's values; k and v are rounded to bfloat16 as the reference's bf16 path stores them).
     group: G tiles per centre (kern["group"]); order "kmeans" permutes the queries first (``perm``
@@ -492,17 +520,22 @@ def flat_attention(q, k, v, *, tile=64, exact_leaves=256, leaf=64, scale=None, s
         mu = group_centres(qt, group)
     g, lz, vbf = leaf_stats(mu, k if k_stats is None else k_stats, v if v_stats is None else v_stats, leaf, scale)
     g8, sg, vb = state_int8(g, vbf)
-    q8, sq, dq8, sdq = query_codes(qt, mu[np.arange(qt.shape[0]) // group])
+    mu_t = mu[np.arange(qt.shape[0]) // group]
+    q8, sq, dq8, sdq = query_codes(qt, mu_t)
+    cv = dd = None
+    if curvature == "iso":
+        cv = iso_coeff(mu, k if k_stats is None else k_stats, leaf, scale)
+        dd = offset_sqnorm(qt, mu_t)
     nb = m // leaf
     sink = max(0, min(int(sink_leaves), nb))
     kx = min(int(exact_leaves) + sink, nb)
     if kx > 0:
-        sel = rowmax_select(dq8, sdq, g8, sg, lz, group)
+        sel = rowmax_select(dq8, sdq, g8, sg, lz, group, cv, dd)
     else:
         sel = np.zeros((mu.shape[0], nb), F32)
     idx, excl = route(sel, exact_leaves, sink)
     out, lse = tile_attention(qt, q8, sq, dq8, sdq, g8, sg, lz, vb, excl, idx, k8, ks, v, leaf,
-                              scale, tail=tail, group=group)
+                              scale, tail=tail, group=group, cv=cv, dd=dd)
     out, lse = out[:n], lse[:n]
     if perm is not None:
         full, full_l = np.empty_like(out), np.empty_like(lse)
@@ -511,7 +544,7 @@ def flat_attention(q, k, v, *, tile=64, exact_leaves=256, leaf=64, scale=None, s
     if not return_stages:
         return out, lse
     return out, lse, dict(k8=k8, ks=ks, qt=qt, mu=mu, g=g, g8=g8, sg=sg, lz=lz, vb=vb, q8=q8,
-                          sq=sq, dq8=dq8, sdq=sdq, sel=sel, idx=idx, excl=excl, perm=perm, q=q_caller)
+                          sq=sq, dq8=dq8, sdq=sdq, sel=sel, idx=idx, excl=excl, perm=perm, q=q_caller, cv=cv, dd=dd)
 
 
 def prepare_head(q, k, v, *, tile=64, leaf=64):
@@ -553,6 +586,59 @@ def flat_attention_tiles(q, k, v, tiles, *, tile=64, exact_leaves=256, leaf=64, 
     """``prepare_head`` + ``attention_tiles`` in one call."""
     return attention_tiles(prepare_head(q, k, v, tile=tile, leaf=leaf), tiles, exact_leaves=exact_leaves,
                            scale=scale, sink_leaves=sink_leaves, tail=tail)
+
+
+def flat_attention_f32(q, k, v, *, tile=64, exact_leaves=64, leaf=16, scale=None, curvature="lin"):
+    """The reference's float32 specification of the operator (the torch backend, h3/htrc_flat.py:279-388),
+    evaluated in float64: exact leaf cumulants at the tile centres (real rows only), far logits
+    lz + dq.g (+ the isotropic curvature 0.5/D max(tr, 0) |dq|^2 with curvature="iso", :331-333), the
+    exact_leaves leaves with the largest row-maximum logit evaluated exactly, both parts merged.  No INT8
+    and no bf16 rounding (the production path's quantisation is not part of this specification)."""
+    q = np.asarray(q, np.float64)
+    k = np.asarray(k, np.float64)
+    v = np.asarray(v, np.float64)
+    n, d = q.shape
+    scale = 1.0 / math.sqrt(d) if scale is None else float(scale)
+    nb = k.shape[0] // leaf
+    k3 = k[: nb * leaf].reshape(nb, leaf, d)
+    v3 = v[: nb * leaf].reshape(nb, leaf, d)
+    nt = -(-n // tile)
+    qs = np.concatenate([q, np.repeat(q[-1:], nt * tile - n, 0)], 0) if nt * tile > n else q
+    qt = qs.reshape(nt, tile, d)
+    out = np.zeros((nt, tile, d))
+    kx = min(int(exact_leaves), nb)
+    for t in range(nt):
+        real = min(tile, n - t * tile)
+        mu = qt[t, :real].mean(0)
+        a = np.einsum("d,lsd->ls", mu, k3) * scale
+        m = a.max(-1, keepdims=True)
+        w = np.exp(a - m)
+        z = w.sum(-1, keepdims=True)
+        w /= z
+        lz = (m + np.log(z))[:, 0]
+        g = np.einsum("ls,lsd->ld", w, k3) * scale
+        vb = np.einsum("ls,lsd->ld", w, v3)
+        dq = qt[t] - mu[None, :]
+        lg = dq @ g.T + lz[None, :]
+        if curvature == "iso":
+            tr = (w * (k3 * k3).sum(-1)).sum(-1) * scale * scale - (g * g).sum(-1)
+            lg = lg + 0.5 / d * np.maximum(tr, 0.0)[None, :] * (dq * dq).sum(-1)[:, None]
+        parts_s, parts_v = [], []
+        keep = np.ones(nb, bool)
+        if kx > 0:
+            idx = np.argsort(-lg.max(0), kind="stable")[:kx]
+            keep[idx] = False
+            tok = (idx[:, None] * leaf + np.arange(leaf)[None, :]).reshape(-1)
+            parts_s.append(qt[t] @ k[tok].T * scale)
+            parts_v.append(v[tok])
+        if keep.any():
+            parts_s.append(lg[:, keep])
+            parts_v.append(vb[keep])
+        s_ = np.concatenate(parts_s, 1)
+        vv = np.concatenate(parts_v, 0)
+        p_ = np.exp(s_ - s_.max(1, keepdims=True))
+        out[t] = p_ @ vv / p_.sum(1, keepdims=True)
+    return out.reshape(nt * tile, d)[:n].astype(F32)
 
 
 def exact_attention(q, k, v, scale=None, tail=None):

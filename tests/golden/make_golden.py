@@ -244,11 +244,28 @@ def fake_quant_fixture(flat):
     return res
 
 
+def torch_spec_fixture(flat):
+    """The reference's float32 torch backend (h3/htrc_flat.py:279-388) with curvature lin and iso: the
+    specification the INT8 path approximates, and the only place the reference defines the iso term."""
+    q, k, v = synth.head_inputs((2, 16, 16), 128, base_seed=41)
+    q = q[:-21].contiguous()
+    res = {name + "16": t.view(torch.int16).numpy().view(np.uint16) for name, t in (("q", q), ("k", k), ("v", v))}
+    for curv in ("lin", "iso"):
+        for e in (0, 3, 8):
+            out = flat.flat_attention(q, k, v, backend="torch", curvature=curv, leaf=64, exact_leaves=e, tile=64,
+                                      tile_chunk=64, precision="fp32")
+            res[f"out_{curv}_{e}"] = out.numpy()
+    return res
+
+
 def main():
     _shim()
     flat = _load_reference()
     torch.manual_seed(0)
     only = set(sys.argv[1:])
+    if not only or "torch_spec" in only:
+        np.savez_compressed(HERE / "torch_spec.npz", **torch_spec_fixture(flat))
+        print("torch_spec -> torch_spec.npz")
     if not only or "fake_quant" in only:
         np.savez_compressed(HERE / "fake_quant.npz", **fake_quant_fixture(flat))
         print("fake_quant -> fake_quant.npz")

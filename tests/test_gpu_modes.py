@@ -251,3 +251,84 @@ def test_runner_kmeans_modes(dev, mode):
     assert np.abs(out.cpu().numpy() - ro).max() < OUT_TOL
     assert np.abs(lse.cpu().numpy() - rl).mean() < LSE_TOL
     r.close()
+
+
+@pytest.mark.parametrize("grid,seed,E,group,order,tile", [((4, 16, 32), 121, 6, 1, "seq", 64),
+                                                          ((4, 16, 32), 122, 5, 2, "kmeans", 64),
+                                                          ((4, 16, 32), 123, 7, 1, "seq", 32)])
+def test_iso_curvature_on_device_state(dev, grid, seed, E, group, order, tile):
+    """curvature="iso" (the torch backend's isotropic second-order far-field term, on the INT8 path): key
+    norms, row offsets and curvature coefficients against the oracle; fed the device's own state, the
+    selection and routing bit for bit and far + near attention within the tolerance."""
+    import htrc_b200
+    from htrc_b200 import _lib
+    q, k, v = _inputs(grid, seed)
+    st = htrc_b200.run_stages(q.to(dev), k.to(dev), v.to(dev), exact_leaves=E, group=group,
+                              order=htrc_b200.flat.order_code(order), tile=tile, curvature=_lib.CURV_ISO)
+    torch.cuda.synchronize()
+    assert int(st["status"].item()) == 0
+    perm = _np(st["perm"]).astype(np.int64) if order == "kmeans" else None
+    kb = O.bf16_round(k.float().numpy())
+    assert np.allclose(_np(st["kn2"]), (kb.astype(np.float64) ** 2).sum(1), rtol=1e-6)
+    qf = q.float().numpy() if perm is None else q.float().numpy()[perm]
+    qt, mu1, _ = O.tile_centres(qf, tile)
+    mu = O.group_centres(qt, group) if group > 1 else mu1
+    nt, nb = qt.shape[0], st["nb"]
+    mu_t = mu[np.arange(nt) // group]
+    assert np.allclose(_held(st["dd"], nt, tile), O.offset_sqnorm(qt, mu_t), rtol=1e-5, atol=1e-6)
+    cv = _np(st["cv"])[:, :nb]
+    want = O.iso_coeff(mu, kb, 64, 1 / math.sqrt(128))
+    assert np.allclose(cv, want, rtol=2e-3, atol=2e-5), np.abs(cv - want).max()
+    dq8 = _held(st["dq8"], nt, tile)
+    sdq = _held(st["sdq"], nt, tile)
+    dd = _held(st["dd"], nt, tile)
+    gt = np.arange(nt) // group
+    g8, sg, lz = _np(st["g8"]), _np(st["sg"])[:, :nb], _np(st["lz"])[:, :nb]
+    per_tile = O.rowmax_select(dq8, sdq, g8[gt], sg[gt], lz[gt], 1, cv[gt], dd)
+    assert np.array_equal(_np(st["sel"])[:nt, :nb].view(np.uint32), per_tile.view(np.uint32))
+    idx, excl = O.route(O.rowmax_select(dq8, sdq, g8, sg, lz, group, cv, dd), E)
+    assert np.array_equal(_np(st["idx"])[:, :idx.shape[1]], idx)
+    assert np.array_equal(_np(st["excl"])[:, :nb], excl)
+    out, lse = O.tile_attention(qt, _held(st["q8"], nt, tile), _held(st["sq"], nt, tile), dq8, sdq, g8, sg, lz,
+                                _np(st["vb"]), excl, idx, _np(st["k8"]), _np(st["ks"]),
+                                O.bf16_round(v.float().numpy()), 64, 1 / math.sqrt(128), group=group, cv=cv, dd=dd)
+    n = q.shape[0]
+    out, lse = out[:n], lse[:n]
+    if perm is not None:
+        fo, fl = np.empty_like(out), np.empty_like(lse)
+        fo[perm], fl[perm] = out, lse
+        out, lse = fo, fl
+    assert np.abs(_np(st["out"]) - out).max() < OUT_TOL
+    assert np.abs(_np(st["lse"]) - lse).mean() < LSE_TOL
+
+
+def test_iso_curvature_end_to_end(dev):
+    """flat_attention(backend="cuda", curvature="iso") and FlatRunner against the oracle computing its own
+    statistics (routing agreement, output and log-Z tolerances); backend="triton" rejects it like the
+    reference."""
+    import htrc_b200
+    from htrc_b200 import runner
+    q, k, v = _inputs((8, 32, 32), 131)
+    qd, kd, vd = q.to(dev), k.to(dev), v.to(dev)
+    cfg = {**htrc_b200.PROD, "leaf": 64, "exact_leaves": 24, "backend": "cuda", "curvature": "iso"}
+    out, lse = htrc_b200.flat_attention(qd, kd, vd, return_lse=True, **cfg)
+    with pytest.raises(ValueError, match="curvature='lin'"):
+        htrc_b200.flat_attention(qd, kd, vd, **{**cfg, "backend": "triton"})
+    r = runner.FlatRunner(q.shape[0], k.shape[0], mode="fast", backend="cuda", curvature="iso", lse=True,
+                          exact_leaves=24)
+    assert r.graph is not None, r.graph_error
+    o2, l2 = r.head(qd, kd, vd)
+    torch.cuda.synchronize()
+    assert torch.equal(o2, out) and torch.equal(l2, lse)
+    ro, rl, rst = O.flat_attention(q.float().numpy(), k.float().numpy(), v.float().numpy(), exact_leaves=24,
+                                   curvature="iso", return_stages=True)
+    st = htrc_b200.run_stages(qd, kd, vd, exact_leaves=24, curvature=htrc_b200.flat.curvature_code("iso"))
+    torch.cuda.synchronize()
+    nb = st["nb"]
+    ex = _np(st["excl"])[:, :nb]
+    assert (ex == rst["excl"]).mean() >= ROUTE_AGREE
+    same = np.repeat((ex == rst["excl"]).all(1), 64)[:q.shape[0]]
+    err = np.abs(out.cpu().numpy()[same] - ro[same]).max(1)
+    assert (err < OUT_TOL).mean() >= 0.999 and err.max() < 2.5 * OUT_TOL
+    assert np.abs(lse.cpu().numpy() - rl).mean() < LSE_TOL
+    r.close()

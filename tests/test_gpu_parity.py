@@ -45,12 +45,14 @@ def test_key_pack_bit_exact(dev):
     kd = k.to(dev)
     k8 = torch.empty((4096, 128), dtype=torch.int8, device=dev)
     ks = torch.empty((4096,), dtype=torch.float32, device=dev)
+    kn2 = torch.empty((4096,), dtype=torch.float32, device=dev)
     _lib.check(lib().htrc_pack_int8(ptr(kd), _lib.DTYPE_BF16, 4096, 128, _lib.ROUND_HALF_EVEN, ptr(k8), ptr(ks),
-                                    stream_ptr()), "pack")
+                                    ptr(kn2), stream_ptr()), "pack")
     torch.cuda.synchronize()
     rk8, rks = O.pack_rows_half_even(k.float().numpy())
     assert np.array_equal(k8.cpu().numpy(), rk8)
     assert np.array_equal(ks.cpu().numpy().view(np.uint32), rks.view(np.uint32))
+    assert np.allclose(kn2.cpu().numpy(), (k.double().numpy() ** 2).sum(1), rtol=1e-6)   # the iso key norms
 
 
 def test_half_away_pack_bit_exact(dev):
@@ -63,7 +65,7 @@ def test_half_away_pack_bit_exact(dev):
     xd = x.to(dev)
     x8 = torch.empty((2048, 128), dtype=torch.int8, device=dev)
     s = torch.empty((2048,), dtype=torch.float32, device=dev)
-    _lib.check(lib().htrc_pack_int8(ptr(xd), _lib.DTYPE_F32, 2048, 128, _lib.ROUND_HALF_AWAY, ptr(x8), ptr(s),
+    _lib.check(lib().htrc_pack_int8(ptr(xd), _lib.DTYPE_F32, 2048, 128, _lib.ROUND_HALF_AWAY, ptr(x8), ptr(s), None,
                                     stream_ptr()), "pack")
     torch.cuda.synchronize()
     r8, rs = O.pack_rows_half_away(x.numpy())

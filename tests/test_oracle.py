@@ -215,6 +215,32 @@ def test_dequant_rows_against_reference(golden_cases):
     assert np.array_equal(O.dequant_rows(vals, z["dq_scale"]), z["dq_out"])
 
 
+@pytest.mark.parametrize("curv", ["lin", "iso"])
+@pytest.mark.parametrize("e", [0, 3, 8])
+def test_f32_specification_matches_reference_torch_backend(golden_cases, curv, e):
+    """The reference's float32 torch backend, including the isotropic curvature term it alone defines."""
+    z = golden_cases["torch_spec"]
+    got = O.flat_attention_f32(z["q"], z["k"], z["v"], exact_leaves=e, leaf=64, curvature=curv)
+    assert np.abs(got - z[f"out_{curv}_{e}"]).max() < 1e-4
+
+
+def test_iso_term_properties():
+    """On the INT8 path: the curvature coefficients are non-negative, the term changes only the far
+    field (every leaf exact -> identical to lin), and with far leaves it changes the output."""
+    rng = np.random.default_rng(7)
+    q = rng.standard_normal((300, 128)).astype(np.float32)
+    k = rng.standard_normal((512, 128)).astype(np.float32)
+    v = rng.standard_normal((512, 128)).astype(np.float32)
+    o_iso, _, st = O.flat_attention(q, k, v, exact_leaves=2, curvature="iso", return_stages=True)
+    assert (st["cv"] >= 0).all() and st["cv"].max() > 0
+    assert np.allclose(st["dd"], ((st["qt"] - st["mu"][:, None, :]) ** 2).sum(-1), rtol=1e-5)
+    o_lin, _ = O.flat_attention(q, k, v, exact_leaves=2)
+    assert np.abs(o_iso - o_lin).max() > 1e-3
+    a, _ = O.flat_attention(q, k, v, exact_leaves=99, curvature="iso")
+    b, _ = O.flat_attention(q, k, v, exact_leaves=99)
+    assert np.array_equal(a, b)
+
+
 def test_route_sink_and_ties():
     sel = np.array([[0.0, 5.0, 5.0, 1.0, 9.0]], np.float32)
     idx, excl = O.route(sel, 2, sink_leaves=1)
