@@ -101,6 +101,12 @@ class ClockSampler:
             return
         self.th = threading.Thread(target=self._read, daemon=True)
         self.th.start()
+        # the first query initialises NVML, which can stall the GPU for a while: let it finish before the
+        # caller's timed region starts
+        t0 = time.time()
+        while not self.rows and time.time() - t0 < 10.0 and self.proc.poll() is None:
+            time.sleep(0.05)
+        self.rows.clear()
 
     def _read(self):
         for line in self.proc.stdout:
