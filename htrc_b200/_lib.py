@@ -58,6 +58,7 @@ SIGNATURES = {
     "htrc_flat_forward_static_ws": (ctypes.c_int, [ctypes.POINTER(HtrcFlatArgs), _p]),
     "htrc_fake_quant": (ctypes.c_int, [_p, _i32, _i64, _i32, _i32, _i32, _p, _i32, _p]),
     "htrc_dequant_rows": (ctypes.c_int, [_p, _i64, _p, _i64, _i64, _i32, _p, _p]),
+    "htrc_selftest_wait_timeout": (ctypes.c_int, [_p, _i64, _p]),
     "htrc_strerror": (ctypes.c_char_p, [ctypes.c_int]),
 }
 

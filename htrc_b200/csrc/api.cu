@@ -258,6 +258,22 @@ float scale_of(float s) { return s > 0.f ? s : 1.0f / std::sqrt(static_cast<floa
 
 }  // namespace
 
+// Self-test of the failure path every kernel shares: a CTA waits on an mbarrier nothing arrives at, with
+// the kernels' own bounded wait given a short limit; the wait gives up, flags the status word and the
+// kernel returns (no trap, no fault; the context stays usable).
+__global__ void __launch_bounds__(32) wait_selftest_kernel(int* status, long long limit) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait_for(&bar, 0, status, &abort_flag, limit);   // no arrival: runs out
+  __syncthreads();
+}
+
 extern "C" {
 
 int64_t htrc_leaf_pitch(int64_t nb) { return pitch_of(nb); }
@@ -530,6 +546,14 @@ int htrc_dequant_rows(const uint8_t* x8, int64_t stride_x, const float* scale, i
   int rc = check_device();
   if (rc != HTRC_OK) return rc;
   launch_dequant_rows(x8, stride_x, scale, stride_s, rows, out, reinterpret_cast<cudaStream_t>(stream));
+  return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
+}
+
+int htrc_selftest_wait_timeout(int32_t* status, int64_t limit_cycles, htrc_stream_t stream) {
+  if (!status || limit_cycles < 1 || limit_cycles > (int64_t(1) << 34)) return HTRC_ERR_ARG;
+  int rc = check_device();
+  if (rc != HTRC_OK) return rc;
+  wait_selftest_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(status, limit_cycles);
   return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
 }
 

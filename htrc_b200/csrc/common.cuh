@@ -59,20 +59,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 // Wait for the phase with the given parity to complete.  Returns false (and flags the status
-// word) when the bound is exceeded or when another thread already flagged a failure.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status,
-                                          volatile int* abort_flag) {
+// word) when `limit` clock cycles pass or when another thread already flagged a failure.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, int* status, volatile int* abort_flag,
+                                              long long limit) {
   if (mbar_try_wait(bar, parity)) return true;
   long long t0 = clock64();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (clock64() - t0 > kWaitCycles) {
+    if (clock64() - t0 > limit) {
       *abort_flag = 1;
       flag_status(status, ST_WAIT_TIMEOUT);
       return false;
     }
   }
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status,
+                                          volatile int* abort_flag) {
+  return mbar_wait_for(bar, parity, status, abort_flag, kWaitCycles);
 }
 
 // The same, for a warp whose lanes all wait: the lanes agree on the outcome, so the warp leaves its

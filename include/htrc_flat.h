@@ -215,6 +215,12 @@ int htrc_fake_quant(const void* x, int32_t x_dtype, int64_t rows, int32_t dim, i
 int htrc_dequant_rows(const uint8_t* x8, int64_t stride_x, const float* scale, int64_t stride_s, int64_t rows,
                       int32_t dim, uint16_t* out, htrc_stream_t stream);
 
+/* Self-test of the device failure path (no reference counterpart): one CTA waits on a barrier nothing
+ * arrives at, with the kernels' bounded wait given `limit_cycles` (at most 2^34) clock cycles; the wait
+ * gives up and ORs HTRC_STATUS_WAIT_TIMEOUT into *status (a device int32 word), then the kernel returns.
+ * Nothing faults or traps and the context stays usable. */
+int htrc_selftest_wait_timeout(int32_t* status, int64_t limit_cycles, htrc_stream_t stream);
+
 /* Human-readable name of a return code. */
 const char* htrc_strerror(int code);
 

@@ -280,3 +280,24 @@ def test_fused_forward_equals_staged(dev):
     torch.cuda.synchronize()
     assert torch.equal(a, b) and torch.equal(la, lb)
     assert torch.equal(a, st["out"]) and torch.equal(la, st["lse"])
+
+
+def test_bounded_wait_runs_out_and_reports(dev):
+    """The failure path every kernel shares, made to run out on purpose without a fault: a wait on a
+    barrier nothing arrives at gives up after its bound, the status word reports it (and the library's
+    status reader raises), and the context still runs the operator afterwards."""
+    import htrc_b200
+    from htrc_b200 import _lib
+    from htrc_b200 import flat as F
+    from htrc_b200._lib import lib, ptr, stream_ptr
+    ws = F.new_workspace(4096, dev)                     # the status word is the workspace's first word
+    _lib.check(lib().htrc_selftest_wait_timeout(ptr(ws), 2_000_000, stream_ptr()), "selftest")
+    torch.cuda.synchronize()
+    assert int(ws[:4].view(torch.int32).item()) == 1     # HTRC_STATUS_WAIT_TIMEOUT
+    with pytest.raises(_lib.HtrcError, match="bounded wait"):
+        F.device_status(ws)
+    F.device_status(ws)                                   # read and cleared: no bit left
+    q, k, v = _inputs((2, 16, 16), 141)
+    out = htrc_b200.flat_attention(q.to(dev), k.to(dev), v.to(dev), **{**htrc_b200.PROD, "leaf": 64, "exact_leaves": 2})
+    torch.cuda.synchronize()
+    assert torch.isfinite(out).all()
