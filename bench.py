@@ -232,18 +232,18 @@ def run_ours(a, wl, rank, world, local_rank):
     ev_done = [torch.cuda.Event() for _ in my_heads]
     nev = 6
 
-    def layer(stage_events=None):
+    def layer(stage_events=None, gather=True):
         for i, h in enumerate(my_heads):
             evs = stage_events[i] if stage_events is not None else None
             F.forward_into(*dq[h], None, None, exact_leaves=E, out=out[h], lse=lse[h], workspace=ws,
                            stage_events=evs)
-            if world > 1:
+            if world > 1 and gather:
                 obf[h].copy_(out[h])
                 ev_done[i].record(comp)
                 side.wait_event(ev_done[i])
                 with torch.cuda.stream(side):
                     shard.gather_slot(obf[h], out=gathered[i])
-        if world > 1:
+        if world > 1 and gather:
             comp.wait_stream(side)
 
     def barrier():
@@ -278,6 +278,22 @@ def run_ours(a, wl, rank, world, local_rank):
     barrier()
     clk = clocks.stop()
     ms = max_over_ranks(t0.elapsed_time(t1) / a.steps)
+    gather_info = None
+    if world > 1:
+        # the same layer without the output gathers: the gathers' exposed (not overlapped) time
+        barrier()
+        g0 = torch.cuda.Event(enable_timing=True)
+        g1 = torch.cuda.Event(enable_timing=True)
+        g0.record(comp)
+        for _ in range(a.steps):
+            layer(gather=False)
+        g1.record(comp)
+        barrier()
+        ms_nog = max_over_ranks(g0.elapsed_time(g1) / a.steps)
+        gather_info = {"compute_only_ms": ms_nog, "exposed_ms": ms - ms_nog,
+                       "bytes_per_rank_per_step": len(my_heads) * world * n * 128 * 2,
+                       "how": "bf16 outputs all-gathered (NCCL) per local head on a side stream, overlapped with the "
+                              "next head; exposed = layer time - the same layer without the gathers"}
     F.device_status(ws)
     stage_names = ["prep", "stats", "rowmax", "route", "tile"]
     stage_ms = {nm: statistics.mean(stage_evs[s][i][j].elapsed_time(stage_evs[s][i][j + 1])
@@ -464,7 +480,8 @@ def run_ours(a, wl, rank, world, local_rank):
                            "exact_leaves": E, "heads_per_gpu": len(my_heads),
                            "l2": "inputs larger than L2: 2.4 GB of distinct q/k/v per layer, 1.6 GB leaf state per head",
                            "parallelism": f"heads/{world}" + (" + bf16 output all_gather (NCCL)" if world > 1 else "")},
-                "stage_ms_per_head": stage_ms, "stage_roofline": stage_roof, "modes": modes, **parity,
+                "stage_ms_per_head": stage_ms, "stage_roofline": stage_roof, "gather": gather_info, "modes": modes,
+                **parity,
                 "roofline": roof, "cpu_baseline": cpu,
                 "e2e": e2e,
                 "gpu_launches": a.steps * len(my_heads) * LAUNCHES_PER_HEAD, "clocks": clk}
