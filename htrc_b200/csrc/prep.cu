@@ -22,12 +22,6 @@ __device__ __forceinline__ void load4<uint16_t>(const uint16_t* p, float (&v)[4]
   v[2] = __uint_as_float(x.y << 16); v[3] = __uint_as_float(x.y & 0xFFFF0000u);
 }
 
-__device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  return v;
-}
-
 // sum of squares of a 128-value row held four values per lane (fp32, lane products then a tree)
 __device__ __forceinline__ float row_sqnorm(const float (&v)[4]) {
   float s = __fmaf_rn(v[3], v[3], __fmaf_rn(v[2], v[2], __fmaf_rn(v[1], v[1], __fmul_rn(v[0], v[0]))));
@@ -62,12 +56,32 @@ __device__ __forceinline__ int quant_code(float v, float s, float r) {
   return ya < 0.f ? -k : k;
 }
 
-// x8 codes of 4 values given the row scale s and its reciprocal r
+// x8 codes of 4 values given the row scale s and its reciprocal r: the fast path of quant_code on pairs
+// (paired fp32 arithmetic), the exact quotient only for the values near a rounding boundary (rare: the
+// whole warp takes that branch only when one of its lanes needs it)
 template <int ROUND>
 __device__ __forceinline__ uint32_t quant4(const float (&v)[4], float s, float r) {
+  const float2 r2 = make_float2(r, r);
+  const float2 m2 = make_float2(12582912.0f, 12582912.0f);
   int c[4];
+  bool near = false;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) c[i] = quant_code<ROUND>(v[i], s, r);
+  for (int p = 0; p < 2; ++p) {
+    const float2 ya = mul2(make_float2(v[2 * p], v[2 * p + 1]), r2);
+    const float2 h = make_float2(__fadd_rn(fabsf(ya.x), 0.5f), __fadd_rn(fabsf(ya.y), 0.5f));
+    const float2 t = add2(h, m2);                 // nearest integer of h in the low mantissa bits
+    const float2 nn = sub2(t, m2);
+    const float2 e = sub2(h, nn);
+    near |= (fabsf(e.x) < 2.44140625e-4f) | (fabsf(e.y) < 2.44140625e-4f);
+    const int k0 = (__float_as_int(t.x) - 0x4B400000) - (h.x < nn.x);      // floor(h)
+    const int k1 = (__float_as_int(t.y) - 0x4B400000) - (h.y < nn.y);
+    c[2 * p] = ya.x < 0.f ? -k0 : k0;
+    c[2 * p + 1] = ya.y < 0.f ? -k1 : k1;
+  }
+  if (__any_sync(0xffffffffu, near)) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) c[i] = quant_code<ROUND>(v[i], s, r);
+  }
   return pack_i8x4(c[0], c[1], c[2], c[3]);
 }
 }  // namespace
@@ -83,7 +97,7 @@ __global__ void __launch_bounds__(256) pack_rows_kernel(const T* __restrict__ x,
   float v[4];
   load4<T>(x + row * 128 + lane * 4, v);
   float am = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
-  am = warp_max(am);
+  am = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(am)));   // non-negative: uint order
   const float s = fmaxf(__fmul_rn(am, kInv127), 1e-20f);
   reinterpret_cast<uint32_t*>(x8 + row * 128)[lane] = quant4<ROUND>(v, s, __frcp_rn(s));
   if (lane == 0) scale[row] = s;
@@ -210,8 +224,8 @@ __global__ void __launch_bounds__(128) tile_prep_kernel(const T* __restrict__ q,
     }
     float aq = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
     float ad = fmaxf(fmaxf(fabsf(d[0]), fabsf(d[1])), fmaxf(fabsf(d[2]), fabsf(d[3])));
-    aq = warp_max(aq);
-    ad = warp_max(ad);
+    aq = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(aq)));
+    ad = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(ad)));
     const float s_q = fmaxf(__fmul_rn(aq, kInv127), 1e-20f);
     const float s_d = fmaxf(__fmul_rn(ad, kInv127), 1e-20f);
     const int64_t gr = r0 + r;
