@@ -472,6 +472,198 @@ def tile_attention_ordered(qt, q8, sq, dq8, sdq, g8, sg, lz, vb, excl, idx, k8, 
     return out.reshape(nt * T, d), lse.reshape(nt * T)
 
 
+# ----------------------------------------------------------------------------- fp8 (e4m3) state
+INV448 = F32(1.0 / 448.0)      # the constant (1.0 / 448.0) the reference multiplies by, as float32
+
+
+def f16_round(x):
+    """Nearest-even float16 value of float32 x, as float32."""
+    return np.asarray(x, F32).astype(np.float16).astype(F32)
+
+
+def e4m3_codes(vals):
+    """e4m3fn code bytes of values already on the e4m3 grid (|v| <= 448); -0 for negative zeros."""
+    x = np.asarray(vals, np.float64)
+    a = np.abs(x)
+    sub = a < 2.0 ** -6
+    er = np.floor(np.log2(np.maximum(a, 2.0 ** -6)))
+    code = np.where(sub, np.rint(a / 2.0 ** -9), (er + 7) * 8 + np.rint((a / 2.0 ** er - 1.0) * 8))
+    return (code.astype(np.uint8) | (np.signbit(x).astype(np.uint8) << 7)).astype(np.uint8)
+
+
+def e4m3_values(codes):
+    """Float32 values of e4m3fn code bytes."""
+    c = np.asarray(codes, np.uint8).astype(np.int64)
+    sign = np.where(c & 0x80, -1.0, 1.0)
+    e = (c >> 3) & 0xF
+    m = c & 7
+    v = np.where(e == 0, m * 2.0 ** -9, (1.0 + m / 8.0) * 2.0 ** (e - 7.0))
+    return (sign * v).astype(F32)
+
+
+def state_fp8(g, vb):
+    """The fp8 far-field state (h3/htrc_flat_triton.py:65-72): per (centre, leaf) row scales
+    sg = max(amax|g| * (1/448), 1e-30), sv likewise for vbar, and the e4m3 values of g / sg and
+    vbar / sv (nearest even, saturating at 448).  Returns (g values, sg, vbar values, sv)."""
+    g = np.asarray(g, F32)
+    vb = np.asarray(vb, F32)
+    sg = np.maximum((np.abs(g).max(-1) * INV448).astype(F32), F32(1e-30)).astype(F32)
+    sv = np.maximum((np.abs(vb).max(-1) * INV448).astype(F32), F32(1e-30)).astype(F32)
+    gq = e4m3_round(np.clip((g / sg[..., None]).astype(F32), -448.0, 448.0))
+    vq = e4m3_round(np.clip((vb / sv[..., None]).astype(F32), -448.0, 448.0))
+    return gq, sg, vq, sv
+
+
+def query_codes_fp8(qt, mu):
+    """The fp8 path's query operands (h3/htrc_flat_triton.py:103-109): bf16(q) for the near field and
+    fp16(q - mu) for the far field (float32 offsets rounded once)."""
+    qt = np.asarray(qt, F32)
+    dq = (qt - np.asarray(mu, F32)[:, None, :]).astype(F32)
+    return bf16_round(qt), f16_round(dq)
+
+
+def rowmax_select_fp8(dqh, gq, sg, lz, group=1):
+    """SEL[t, l] = max_r (fp16(dq_r) . g_l) * sg_l + lz_l (h3/htrc_flat_triton.py:240-254, FP8=1): float32
+    products of fp16 operands; groups as rowmax_select."""
+    nt = dqh.shape[0]
+    st = np.arange(nt) // group
+    dot = np.matmul(dqh.astype(np.float64), np.swapaxes(gq[st].astype(np.float64), 1, 2)).astype(F32)
+    per_tile = ((dot * sg[st][:, None, :]).astype(F32).max(1) + lz[st]).astype(F32)
+    ng = -(-nt // group)
+    out = np.full((ng, per_tile.shape[1]), -np.inf, F32)
+    np.maximum.at(out, st, per_tile)
+    return out
+
+
+def tile_attention_fp8(qt, qb, dqh, gq, sg, lz, vq, sv, excl, idx, kb, vbf, leaf, scale, tail=None, group=1):
+    """Far + near (+ tail) of every tile with the fp8 state (h3/htrc_flat_triton.py:118-211, FP8=1, DOT=1),
+    order-free: far logit = (fp16 dq . g) * sg + lz, value weight fp16(p * sv) on the e4m3 values of vbar;
+    near logit = (bf16 q . bf16 k) * scale, weight bf16(p); the normaliser sums float32 p.
+    Returns (out [nt*T, D], lse [nt*T])."""
+    nt, T, d = qt.shape
+    out = np.zeros((nt, T, d), F32)
+    lse = np.zeros((nt, T), F32)
+    ar = np.arange(leaf)
+    vbf = np.asarray(vbf, F32)
+    small_tail = tail is not None and 0 < tail[0].shape[0] <= 16
+    for t in range(nt):
+        gt = t // group
+        ss, vs, ws = [], [], []          # scores, values, (kind, column multiplier)
+        keep = excl[gt] == 0
+        if keep.any():
+            sc = (dqh[t].astype(np.float64) @ gq[gt][keep].astype(np.float64).T).astype(F32)
+            ss.append((sc * sg[gt][keep][None, :]).astype(F32) + lz[gt][keep][None, :])
+            vs.append(vq[gt][keep])
+            ws.append(("f16", sv[gt][keep]))
+        if idx.shape[1]:
+            tok = (idx[gt][:, None].astype(np.int64) * leaf + ar[None, :]).reshape(-1)
+            sc = (qb[t].astype(np.float64) @ kb[tok].astype(np.float64).T).astype(F32)
+            ss.append((sc * F32(scale)).astype(F32))
+            vs.append(vbf[tok])
+            ws.append(("bf16", None))
+        if tail is not None and tail[0].shape[0]:
+            tk = np.asarray(tail[0], F32)
+            tv = np.asarray(tail[1], F32)
+            if small_tail:
+                sc = (bf16_round(qt[t]).astype(np.float64) @ bf16_round(tk).astype(np.float64).T).astype(F32)
+                ss.append((sc * F32(scale)).astype(F32))
+                vs.append(bf16_round(tv))
+                ws.append(("bf16", None))
+            else:
+                sc = (qt[t].astype(np.float64) @ tk.astype(np.float64).T).astype(F32)
+                ss.append((sc * F32(scale)).astype(F32))
+                vs.append(tv)
+                ws.append(("none", None))
+        m = np.max([x.max(1) for x in ss], axis=0)
+        den = np.zeros(T)
+        num = np.zeros((T, d))
+        for sc, vv, (kind, mult) in zip(ss, vs, ws):
+            pr = np.exp(sc.astype(np.float64) - m[:, None])
+            den += pr.sum(1)
+            if kind == "f16":
+                w = f16_round((pr * mult[None, :]).astype(F32)).astype(np.float64)
+            elif kind == "bf16":
+                w = bf16_round(pr.astype(F32)).astype(np.float64)
+            else:
+                w = pr
+            num += w @ vv.astype(np.float64)
+        out[t] = (num / np.maximum(den, 1e-30)[:, None]).astype(F32)
+        lse[t] = (m + np.log(den)).astype(F32)
+    return out.reshape(nt * T, d), lse.reshape(nt * T)
+
+
+def tile_attention_fp8_ordered(qt, qb, dqh, gq, sg, lz, vq, sv, excl, idx, kb, vbf, leaf, scale, tail=None,
+                               splits=4, bn=64, group=1):
+    """The fp8 tile attention in the reference kernel's own order (splits, blocks of bn, float32 online
+    softmax, weights rounded against the running maximum, split merge); idx in the reference's order.
+    Pins the restatement against fixtures recorded from the reference."""
+    nt, T, d = qt.shape
+    nb = lz.shape[1]
+    kx = idx.shape[1]
+    lps = _split(nb, splits, bn)
+    e_n = kx * leaf
+    eps = _split(e_n, splits, bn)
+    vbf = np.asarray(vbf, F32)
+    scale = F32(scale)
+    small_tail = tail is not None and 0 < tail[0].shape[0] <= 16
+    out = np.zeros((nt, T, d), F32)
+    lse = np.zeros((nt, T), F32)
+
+    def step(m, l, acc, sc, vals, weight):
+        mn = np.maximum(m, sc.max(1))
+        ms = np.where(mn == -np.inf, F32(0), mn).astype(F32)
+        p = np.exp(sc - ms[:, None]).astype(F32)
+        al = np.exp(m - ms).astype(F32)
+        l = (l * al + p.sum(1)).astype(F32)
+        acc = (acc * al[:, None] + (weight(p).astype(np.float64) @ vals.astype(np.float64))).astype(F32)
+        return mn, l, acc
+
+    for t in range(nt):
+        gt = t // group
+        pms, pls, paccs = [], [], []
+        for sp in range(splits):
+            m = np.full(T, -np.inf, F32)
+            l = np.zeros(T, F32)
+            acc = np.zeros((T, d), F32)
+            lo, hi = sp * lps, min(nb, sp * lps + lps)
+            for n0 in range(lo, hi, bn):
+                c = np.arange(n0, min(n0 + bn, hi))
+                sc = (dqh[t].astype(np.float64) @ gq[gt][c].astype(np.float64).T).astype(F32)
+                sc = ((sc * sg[gt][c][None, :]).astype(F32) + lz[gt][c][None, :]).astype(F32)
+                sc = np.where((excl[gt][c] == 0)[None, :], sc, F32(-np.inf))
+                svc = sv[gt][c]
+                m, l, acc = step(m, l, acc, sc, vq[gt][c], lambda p, svc=svc: f16_round((p * svc[None, :]).astype(F32)))
+            e_lo, e_hi = sp * eps, min(e_n, sp * eps + eps)
+            for e0 in range(e_lo, e_hi, bn):
+                j = np.arange(e0, min(e0 + bn, e_hi))
+                tok = idx[gt][j // leaf].astype(np.int64) * leaf + j % leaf
+                sc = ((qb[t].astype(np.float64) @ kb[tok].astype(np.float64).T).astype(F32) * scale).astype(F32)
+                m, l, acc = step(m, l, acc, sc, vbf[tok], bf16_round)
+            if small_tail and sp == splits - 1:
+                tk, tv = bf16_round(tail[0]), bf16_round(tail[1])
+                sc = ((bf16_round(qt[t]).astype(np.float64) @ tk.astype(np.float64).T).astype(F32) * scale).astype(F32)
+                m, l, acc = step(m, l, acc, sc, tv, bf16_round)
+            pms.append(m)
+            pls.append(l)
+            paccs.append(acc)
+        if tail is not None and tail[0].shape[0] > 16:
+            tk32 = np.asarray(tail[0], F32)
+            lg = (qt[t].astype(np.float64) @ tk32.astype(np.float64).T).astype(F32) * scale
+            tm = lg.max(1)
+            te = np.exp(lg - tm[:, None]).astype(F32)
+            pms.append(tm.astype(F32))
+            pls.append(te.sum(1).astype(F32))
+            paccs.append((te.astype(np.float64) @ np.asarray(tail[1], np.float64)).astype(F32))
+        pm, pl, pa = np.array(pms), np.array(pls), np.array(paccs)
+        mm = pm.max(0)
+        mm = np.where(mm == -np.inf, F32(0), mm)
+        w = np.exp(pm - mm).astype(F32)
+        den = (pl * w).sum(0)
+        out[t] = ((pa * w[:, :, None]).sum(0) / np.maximum(den, F32(1e-30))[:, None]).astype(F32)
+        lse[t] = (mm + np.log(np.maximum(den, F32(1e-30)))).astype(F32)
+    return out.reshape(nt * T, d), lse.reshape(nt * T)
+
+
 def pack_k(k):
     """Near-field key pack of bf16 keys: (k8, ks) (h3/htrc_flat.py:211-219)."""
     return pack_rows_half_even(bf16_round(np.asarray(k, dtype=F32)))
@@ -479,7 +671,7 @@ def pack_k(k):
 
 def flat_attention(q, k, v, *, tile=64, exact_leaves=256, leaf=64, scale=None, sink_leaves=0,
                    tail=None, return_stages=False, group=1, order="seq", perm=None, quant=None,
-                   stats_bf16=False, curvature="lin"):
+                   stats_bf16=False, curvature="lin", store="int8"):
     """The whole production path for one head: q [N, D], k/v [M, D] (float32 arrays holding the
     caller's values; k and v are rounded to bfloat16 as the reference's bf16 path stores them).
     group: G tiles per centre (kern["group"]); order "kmeans" permutes the queries first (``perm``
@@ -519,6 +711,9 @@ def flat_attention(q, k, v, *, tile=64, exact_leaves=256, leaf=64, scale=None, s
     if group > 1:
         mu = group_centres(qt, group)
     g, lz, vbf = leaf_stats(mu, k if k_stats is None else k_stats, v if v_stats is None else v_stats, leaf, scale)
+    if store == "fp8":
+        return _flat_fp8(qt, mu, g, lz, vbf, k, v, n, leaf, scale, exact_leaves, sink_leaves, tail, group, perm,
+                         return_stages)
     g8, sg, vb = state_int8(g, vbf)
     mu_t = mu[np.arange(qt.shape[0]) // group]
     q8, sq, dq8, sdq = query_codes(qt, mu_t)
@@ -545,6 +740,29 @@ def flat_attention(q, k, v, *, tile=64, exact_leaves=256, leaf=64, scale=None, s
         return out, lse
     return out, lse, dict(k8=k8, ks=ks, qt=qt, mu=mu, g=g, g8=g8, sg=sg, lz=lz, vb=vb, q8=q8,
                           sq=sq, dq8=dq8, sdq=sdq, sel=sel, idx=idx, excl=excl, perm=perm, q=q_caller, cv=cv, dd=dd)
+
+
+def _flat_fp8(qt, mu, g, lz, vbf, kb, vb, n, leaf, scale, exact_leaves, sink_leaves, tail, group, perm, return_stages):
+    """store="fp8" after the leaf statistics: e4m3 state, fp16 far field, bf16 near field."""
+    gq, sg, vq, sv = state_fp8(g, vbf)
+    mu_t = mu[np.arange(qt.shape[0]) // group]
+    qb, dqh = query_codes_fp8(qt, mu_t)
+    nb = kb.shape[0] // leaf
+    sink = max(0, min(int(sink_leaves), nb))
+    kx = min(int(exact_leaves) + sink, nb)
+    sel = rowmax_select_fp8(dqh, gq, sg, lz, group) if kx > 0 else np.zeros((mu.shape[0], nb), F32)
+    idx, excl = route(sel, exact_leaves, sink)
+    out, lse = tile_attention_fp8(qt, qb, dqh, gq, sg, lz, vq, sv, excl, idx, kb, vb, leaf, scale, tail=tail,
+                                  group=group)
+    out, lse = out[:n], lse[:n]
+    if perm is not None:
+        full, full_l = np.empty_like(out), np.empty_like(lse)
+        full[perm], full_l[perm] = out, lse
+        out, lse = full, full_l
+    if not return_stages:
+        return out, lse
+    return out, lse, dict(qt=qt, mu=mu, g=g, gq=gq, sg=sg, lz=lz, vq=vq, sv=sv, qb=qb, dqh=dqh, sel=sel, idx=idx,
+                          excl=excl, perm=perm)
 
 
 def prepare_head(q, k, v, *, tile=64, leaf=64):

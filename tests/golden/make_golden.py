@@ -16,7 +16,8 @@ Triton 3.6's interpreter has two defects on this path, fixed here by a harness-s
 reference is not modified):
   1. ``create_dot`` multiplies bfloat16 operands as their raw uint16 bit patterns -> the shim widens
      bfloat16 operands to float32 before the product;
-  2. float32 -> bfloat16 casts truncate -> the shim rounds to nearest even, as the GPU does.
+  2. float32 -> bfloat16, float16 and float8 (e4m3) casts truncate -> the shim rounds to nearest even
+     (float8 saturating at +-448), as the GPU does.
 The interpreter also evaluates ``tl.dot(..., input_precision="tf32")`` in float32 and ``/`` as
 IEEE division; the fixtures therefore pin the reference's arithmetic at float32 precision.
 """
@@ -63,15 +64,39 @@ def _shim():
         bits = ((x + 0x7FFF + ((x >> 16) & 1)) >> 16).astype(np.uint16)
         return itp.TensorHandle(bits, dst_type.scalar)
 
-    def cast_impl(self, src, dst_type):
+    def to_f16(src, dst_type):
+        x = np.ascontiguousarray(src.data, dtype=np.float32)
+        return itp.TensorHandle(x.astype(np.float16), dst_type.scalar)      # numpy rounds to nearest even
+
+    def to_e4m3(src, dst_type):
+        # nearest-even e4m3fn with saturation at +-448 (the GPU's cvt.rn.satfinite), as code bytes
+        x = np.ascontiguousarray(src.data, dtype=np.float32).astype(np.float64)
+        a = np.minimum(np.abs(x), 448.0)
+        e = np.floor(np.log2(np.maximum(a, 2.0 ** -9)))
+        quantum = np.where(a < 2.0 ** -6, 2.0 ** -9, 2.0 ** (e - 3))
+        r = np.minimum(np.rint(a / quantum) * quantum, 448.0)
+        sub = r < 2.0 ** -6
+        er = np.floor(np.log2(np.maximum(r, 2.0 ** -6)))
+        code = np.where(sub, np.rint(r / 2.0 ** -9), (er + 7) * 8 + np.rint((r / 2.0 ** er - 1.0) * 8))
+        sign = np.signbit(x).astype(np.uint8) << 7
+        return itp.TensorHandle((code.astype(np.uint8) | sign).astype(np.uint8), dst_type.scalar)
+
+    def narrow(src, dst_type):
         if src.dtype.scalar == tl.float32 and dst_type.scalar == tl.bfloat16:
             return to_bf16(src, dst_type)
-        return orig_cast(self, src, dst_type)
+        if src.dtype.scalar == tl.float32 and dst_type.scalar == tl.float16:
+            return to_f16(src, dst_type)
+        if src.dtype.scalar == tl.float32 and dst_type.scalar == tl.float8e4nv:
+            return to_e4m3(src, dst_type)
+        return None
+
+    def cast_impl(self, src, dst_type):
+        r = narrow(src, dst_type)
+        return r if r is not None else orig_cast(self, src, dst_type)
 
     def create_fp_to_fp(self, src, dst_type, rounding_mode):
-        if src.dtype.scalar == tl.float32 and dst_type.scalar == tl.bfloat16:
-            return to_bf16(src, dst_type)
-        return orig_fp2fp(self, src, dst_type, rounding_mode)
+        r = narrow(src, dst_type)
+        return r if r is not None else orig_fp2fp(self, src, dst_type, rounding_mode)
 
     B.create_dot = create_dot
     B.cast_impl = cast_impl
@@ -102,7 +127,10 @@ def _recorder(flat):
 
     def leaf_stats(mu, kf, vf, nb, scale, **kw):
         g, lz, vb, sg, sv = o_stats(mu, kf, vf, nb, scale, **kw)
-        rec["stats"].append(dict(mu=mu.clone(), g8=g.clone(), lz=lz.clone(), vb=vb.clone(), sg=sg.clone()))
+        ent = dict(mu=mu.clone(), g8=g.clone(), lz=lz.clone(), vb=vb.clone(), sg=sg.clone())
+        if sv is not None:                         # fp8 store: value row scales too
+            ent["sv"] = sv.clone()
+        rec["stats"].append(ent)
         return g, lz, vb, sg, sv
 
     def rowmax_select(*a, **kw):
@@ -113,8 +141,9 @@ def _recorder(flat):
     def tile_attention(q_c, mu_c, g, lz, vb, excl, idx, k_ex, v_ex, scale, **kw):
         ws = kw.get("ws")
         res = o_tile(q_c, mu_c, g, lz, vb, excl, idx, k_ex, v_ex, scale, **kw)
-        ent = dict(q_c=q_c.clone(), excl=excl.clone(), k8=k_ex.clone(), ks=kw["ks"].clone(),
-                   out=res.clone())
+        ent = dict(q_c=q_c.clone(), excl=excl.clone(), k8=k_ex.clone(), out=res.clone())
+        if kw.get("ks") is not None:
+            ent["ks"] = kw["ks"].clone()
         if idx is not None:
             ent["idx"] = idx.clone()
         if ws is not None:
@@ -155,6 +184,9 @@ CASES = [
     # low-bit simulation of the inputs (quant=): k/v int4 and q int8 with groups of 32
     dict(name="quant_kv_q", grid=(2, 16, 16), leaf=64, E=2, sink=0, tail=0, trim=0, seed=27,
          quant={"kv": "int4", "q": "int8", "group": 32}),
+    # the fp8 (e4m3) leaf state with row scales (store="fp8"): fp16 far-field dots, bf16 near field
+    dict(name="fp8_state", grid=(2, 16, 16), leaf=64, E=2, sink=0, tail=0, trim=23, seed=28, store="fp8"),
+    dict(name="fp8_sink_tail", grid=(2, 16, 16), leaf=64, E=3, sink=1, tail=5, trim=0, seed=29, store="fp8"),
 ]
 
 
@@ -175,7 +207,7 @@ def run_case(flat, c):
     ws = {}
     cfg = dict(flat.PROD)
     cfg.update(leaf=c["leaf"], exact_leaves=c["E"], sink_leaves=c["sink"], tile_chunk=4096,
-               order=c.get("order", "seq"), tile=c.get("tile", 64))
+               order=c.get("order", "seq"), tile=c.get("tile", 64), store=c.get("store", "int8"))
     if c.get("group", 1) > 1:
         cfg["kern"] = {**cfg["kern"], "group": c["group"]}
     if c.get("quant"):
@@ -183,13 +215,19 @@ def run_case(flat, c):
     out = flat.flat_attention(q, k, v, tail=(tk, tv) if tk is not None else None, ws=ws, **cfg)
     st = rec["stats"]
     ti = rec["tile"]
+    fp8 = c.get("store") == "fp8"
     res = dict(q=q.float().numpy(), k=k.float().numpy(), v=v.float().numpy(),
                leaf=np.int64(c["leaf"]), exact_leaves=np.int64(c["E"]), sink_leaves=np.int64(c["sink"]),
                group=np.int64(c.get("group", 1)), tile=np.int64(c.get("tile", 64)),
-               mu=_cat(st, "mu").numpy(), g8=_cat(st, "g8").numpy(), sg=_cat(st, "sg").numpy(),
-               lz=_cat(st, "lz").numpy(), vb=_cat(st, "vb").float().numpy(),
-               excl=_cat(ti, "excl").numpy().astype(np.uint8), k8=ti[0]["k8"].numpy(),
-               ks=ti[0]["ks"].numpy(), out=out.float().numpy())
+               mu=_cat(st, "mu").numpy(), sg=_cat(st, "sg").numpy(), lz=_cat(st, "lz").numpy(),
+               excl=_cat(ti, "excl").numpy().astype(np.uint8), out=out.float().numpy())
+    if fp8:
+        # e4m3 state as its codes (bytes), with the row scales of g and vbar; no INT8 keys
+        res.update(store=np.array("fp8"), g_e4m3=_cat(st, "g8").view(torch.uint8).numpy(),
+                   vb_e4m3=_cat(st, "vb").view(torch.uint8).numpy(), sv=_cat(st, "sv").numpy())
+    else:
+        res.update(g8=_cat(st, "g8").numpy(), vb=_cat(st, "vb").float().numpy(), k8=ti[0]["k8"].numpy(),
+                   ks=ti[0]["ks"].numpy())
     if rec["sel"]:
         res["sel"] = torch.cat(rec["sel"], 0).numpy()
     if "idx" in ti[0]:

@@ -250,3 +250,63 @@ def test_route_sink_and_ties():
     assert idx.shape == (1, 0) and excl.sum() == 0
     idx, _ = O.route(sel, 99)
     assert idx.tolist() == [[0, 1, 2, 3, 4]]
+
+
+FP8_CASES = ["fp8_state", "fp8_sink_tail"]
+
+
+def _fp8(z):
+    tail = (z["tail_k"], z["tail_v"]) if "tail_k" in z else None
+    out, lse, st = O.flat_attention(z["q"], z["k"], z["v"], leaf=int(z["leaf"]),
+                                    exact_leaves=int(z["exact_leaves"]), sink_leaves=int(z["sink_leaves"]),
+                                    tail=tail, return_stages=True, store="fp8")
+    return out, lse, st, tail
+
+
+@pytest.mark.parametrize("case", FP8_CASES)
+def test_fp8_state_bit_exact(golden_cases, case):
+    """store="fp8": the e4m3 codes of g / sg and vbar / sv are the reference's, byte for byte, and the
+    row scales agree to float32 rounding of the leaf statistics."""
+    z = golden_cases[case]
+    out, lse, st, _ = _fp8(z)
+    assert np.array_equal(O.e4m3_codes(st["gq"]), z["g_e4m3"])
+    assert np.array_equal(O.e4m3_codes(st["vq"]), z["vb_e4m3"])
+    assert np.array_equal(O.e4m3_values(z["g_e4m3"]), st["gq"])
+    assert np.allclose(st["sg"], z["sg"], rtol=2e-6, atol=0)
+    assert np.allclose(st["sv"], z["sv"], rtol=2e-6, atol=0)
+    assert np.allclose(st["sel"], z["sel"], rtol=0, atol=1e-4)
+    assert np.array_equal(st["excl"], z["excl"])
+    assert np.array_equal(np.sort(st["idx"], 1), np.sort(z["idx"], 1))
+
+
+@pytest.mark.parametrize("case", FP8_CASES)
+def test_fp8_ordered_restatement_matches_reference(golden_cases, case):
+    """The fp8 tile attention in the reference kernel's order, fed the reference's own state, reproduces
+    its output to float32 accumulation-order error."""
+    z = golden_cases[case]
+    out, lse, st, tail = _fp8(z)
+    gq, vq = O.e4m3_values(z["g_e4m3"]), O.e4m3_values(z["vb_e4m3"])
+    qb, dqh = O.query_codes_fp8(st["qt"], z["mu"])
+    assert np.allclose(O.rowmax_select_fp8(dqh, gq, z["sg"], z["lz"]), z["sel"], rtol=0, atol=2e-5)
+    o, l = O.tile_attention_fp8_ordered(st["qt"], qb, dqh, gq, z["sg"], z["lz"], vq, z["sv"], z["excl"], z["idx"],
+                                        O.bf16_round(z["k"]), O.bf16_round(z["v"]), int(z["leaf"]),
+                                        1.0 / np.sqrt(z["q"].shape[1]), tail=tail)
+    n = z["q"].shape[0]
+    assert np.abs(o[:n] - z["out"]).max() < 5e-5
+    assert np.abs(l[:n] - z["lse"]).max() < 5e-5
+
+
+@pytest.mark.parametrize("case", FP8_CASES)
+def test_fp8_order_free_oracle_within_tolerance(golden_cases, case):
+    """The order-free fp8 oracle (weights rounded against the row's final maximum) stays within the
+    fp16-weight rounding of the reference."""
+    z = golden_cases[case]
+    out, lse, _, _ = _fp8(z)
+    assert np.abs(out - z["out"]).max() < 1e-2
+    assert np.abs(lse - z["lse"]).max() < 1e-4
+
+
+def test_e4m3_codes_round_trip():
+    c = np.arange(256, dtype=np.uint8)
+    c = c[(c & 0x7F) != 0x7F]                       # 0x7F / 0xFF are NaN in e4m3fn
+    assert np.array_equal(O.e4m3_codes(O.e4m3_values(c)), c)
