@@ -14,6 +14,8 @@ HTRC_OK, HTRC_ERR_ARG, HTRC_ERR_UNSUPPORTED, HTRC_ERR_WORKSPACE, HTRC_ERR_CUDA, 
 DTYPE_F32, DTYPE_BF16 = 0, 1
 ORDER_SEQ, ORDER_KMEANS = 0, 1
 CURV_LIN, CURV_ISO = 0, 1
+STORE_INT8, STORE_FP8 = 0, 1
+STORES = {"int8": STORE_INT8, "fp8": STORE_FP8}
 FQ_FORMATS = {"int8": 1, "int4": 2, "fp8": 3, "fp4": 4}
 ROUND_HALF_EVEN, ROUND_HALF_AWAY = 0, 1
 STATUS_BITS = {1: "bounded wait gave up", 2: "routed leaf index out of range", 4: "non-finite log-partition"}
@@ -34,7 +36,7 @@ class HtrcFlatArgs(ctypes.Structure):
         ("workspace", _p), ("workspace_bytes", ctypes.c_size_t),
         ("out", _p), ("lse", _p),
         ("stage_events", ctypes.POINTER(_p)), ("n_stage_events", _i32),
-        ("group", _i32), ("order", _i32), ("curvature", _i32),
+        ("group", _i32), ("order", _i32), ("curvature", _i32), ("store", _i32),
     ]
 
 
@@ -55,6 +57,12 @@ SIGNATURES = {
     "htrc_tile_attention": (ctypes.c_int, [_p, _p, _p, _p, _i64, _i32, _i64, _i64, _i32, _p, _p, _p, _p, _p, _p, _i32,
                                            _i64, _p, _p, _p, _i64, _i32, _i32, _f32, _p, _p, _p, _p, _p, _p, _p, _p]),
     "htrc_tail_partial": (ctypes.c_int, [_p, _i32, _i64, _i32, _p, _p, _i32, _f32, _p, _p]),
+    "htrc_tile_prep_fp8": (ctypes.c_int, [_p, _i32, _i64, _i32, _i32, _p, _i32, _p, _p, _p, _p, _p, _p]),
+    "htrc_leaf_stats_fp8": (ctypes.c_int, [_p, _p, _i64, _i64, _i64, _p, _p, _i64, _i32, _i32, _f32, _p, _p, _p, _p, _p,
+                                           _p, _p]),
+    "htrc_rowmax_select_fp8": (ctypes.c_int, [_p, _i64, _i64, _i32, _p, _p, _p, _i64, _i32, _p, _p, _p]),
+    "htrc_tile_attention_fp8": (ctypes.c_int, [_p, _p, _i64, _i32, _i64, _i64, _i32, _p, _p, _p, _p, _p, _p, _p, _i32,
+                                               _i64, _p, _p, _i64, _i32, _i32, _f32, _p, _p, _p, _p, _p, _p]),
     "htrc_flat_forward_static_ws": (ctypes.c_int, [ctypes.POINTER(HtrcFlatArgs), _p]),
     "htrc_fake_quant": (ctypes.c_int, [_p, _i32, _i64, _i32, _i32, _i32, _p, _i32, _p]),
     "htrc_dequant_rows": (ctypes.c_int, [_p, _i64, _p, _i64, _i64, _i32, _p, _p]),

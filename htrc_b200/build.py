@@ -17,7 +17,7 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libhtrc_flat.so"
-SOURCES = ["api.cu", "prep.cu", "stats.cu", "rowmax.cu", "route.cu", "tile.cu", "kmeans.cu", "quant.cu", "static_ws.cu"]
+SOURCES = ["api.cu", "prep.cu", "stats.cu", "rowmax.cu", "route.cu", "tile.cu", "kmeans.cu", "quant.cu", "static_ws.cu", "fp8.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -110,6 +110,14 @@ bool map_state(CUtensorMap* m, const void* base, int64_t tc, int64_t nb, bool bf
                   box, true);
 }
 
+// [tc, nb, 128] one-byte codes without swizzle (staged as plain 128-byte rows), box (128, box_leaves, 1)
+bool map_codes(CUtensorMap* m, const void* base, int64_t tc, int64_t nb, int box_leaves) {
+  const uint64_t dims[3] = {128, static_cast<uint64_t>(nb), static_cast<uint64_t>(tc)};
+  const uint64_t strides[2] = {128, static_cast<uint64_t>(nb) * 128};
+  const uint32_t box[3] = {128u, static_cast<uint32_t>(box_leaves), 1u};
+  return make_map(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, base, dims, strides, box, false);
+}
+
 // [tc, nb] scalars (f32 or u8) with row pitch `pitch` elements, box (box_cols, 1)
 bool map_scalars(CUtensorMap* m, const void* base, int64_t tc, int64_t nb, int64_t pitch, bool f32, int box_cols) {
   const uint64_t es = f32 ? 4 : 1;
@@ -133,6 +141,8 @@ struct Layout {
   size_t g8 = 0, vb = 0, sg = 0, lz = 0, sel = 0, excl = 0, idx = 0, perm = 0, km = 0, total = 0;
   bool iso = false;
   size_t kn2 = 0, dd = 0, cv = 0;           // iso curvature: key norms, row offsets, coefficients
+  bool fp8 = false;                         // fp8 state: q8 / dq8 hold bf16 / fp16 rows, vb the vbar codes
+  size_t sv = 0;
 };
 
 constexpr int kMaxGroup = 65536;
@@ -146,6 +156,8 @@ int validate(const HtrcFlatArgs* a, bool need_ptrs) {
   if (a->group > kMaxGroup) return HTRC_ERR_ARG;
   if (a->order != HTRC_ORDER_SEQ && a->order != HTRC_ORDER_KMEANS) return HTRC_ERR_ARG;
   if (a->curvature != HTRC_CURV_LIN && a->curvature != HTRC_CURV_ISO) return HTRC_ERR_ARG;
+  if (a->store != HTRC_STORE_INT8 && a->store != HTRC_STORE_FP8) return HTRC_ERR_ARG;
+  if (a->store == HTRC_STORE_FP8 && a->curvature != HTRC_CURV_LIN) return HTRC_ERR_UNSUPPORTED;
   if (a->n_queries > (int64_t(1) << 31) - 1) return HTRC_ERR_UNSUPPORTED;
   const int64_t nb = a->n_keys / a->leaf;
   if (nb > kMaxLeaves) return HTRC_ERR_UNSUPPORTED;
@@ -186,19 +198,26 @@ Layout layout_of(const HtrcFlatArgs* a) {
     o = align256(o + bytes);
     return at;
   };
+  L.fp8 = a->store == HTRC_STORE_FP8;
+  const size_t qes = L.fp8 ? 2 : 1;         // bytes per value of the query operands
   L.status = take(256);
-  L.k8 = take(static_cast<size_t>(L.m) * 128);
-  L.ks = take(static_cast<size_t>(L.m) * 4);
+  if (!L.fp8) {
+    L.k8 = take(static_cast<size_t>(L.m) * 128);
+    L.ks = take(static_cast<size_t>(L.m) * 4);
+  }
   L.mu = take(static_cast<size_t>(L.ng) * 128 * 4);
   L.mu_hi = take(static_cast<size_t>(L.ng) * 128 * 2);
   L.mu_lo = take(static_cast<size_t>(L.ng) * 128 * 2);
-  L.q8 = take(static_cast<size_t>(L.nt) * 64 * 128);
-  L.sq = take(static_cast<size_t>(L.nt) * 64 * 4);
-  L.dq8 = take(static_cast<size_t>(L.nt) * 64 * 128);
-  L.sdq = take(static_cast<size_t>(L.nt) * 64 * 4);
+  L.q8 = take(static_cast<size_t>(L.nt) * 64 * 128 * qes);
+  L.dq8 = take(static_cast<size_t>(L.nt) * 64 * 128 * qes);
+  if (!L.fp8) {
+    L.sq = take(static_cast<size_t>(L.nt) * 64 * 4);
+    L.sdq = take(static_cast<size_t>(L.nt) * 64 * 4);
+  }
   L.tail = a->n_tail > 0 ? take(static_cast<size_t>(L.n) * 130 * 4) : 0;
   L.g8 = take(static_cast<size_t>(gcm_rows) * L.nb * 128);
-  L.vb = take(static_cast<size_t>(gcm_rows) * L.nb * 256);
+  L.vb = take(static_cast<size_t>(gcm_rows) * L.nb * (L.fp8 ? 128 : 256));
+  if (L.fp8) L.sv = take(static_cast<size_t>(gcm_rows) * L.pitch * 4);
   L.sg = take(static_cast<size_t>(gcm_rows) * L.pitch * 4);
   L.lz = take(static_cast<size_t>(gcm_rows) * L.pitch * 4);
   L.sel = take(static_cast<size_t>(L.tcm) * L.pitch * 4);
@@ -226,12 +245,31 @@ T* at(void* base, size_t off) {
 int check_device() { return device_info().ok ? HTRC_OK : HTRC_ERR_DEVICE; }
 
 int stats_maps(LeafStatsMaps* mp, const uint16_t* mu_hi, const uint16_t* mu_lo, int64_t nt, const uint16_t* k,
-               const uint16_t* v, int64_t m, const int8_t* g8, const uint16_t* vb, int64_t tc, int64_t nb) {
+               const uint16_t* v, int64_t m, const void* g8, const void* vb, int64_t tc, int64_t nb, bool fp8) {
   mp->mu_hi = mu_hi;
   mp->mu_lo = mu_lo;
   mp->nt = nt;
   bool ok = map_rows_halves(&mp->k, k, m, 64) && map_rows_halves(&mp->v, v, m, 64) &&
-            map_state(&mp->g8, g8, tc, nb, false, 1, 128) && map_state(&mp->vb, vb, tc, nb, true, 1, 128);
+            map_state(&mp->g8, g8, tc, nb, false, 1, 128) && map_state(&mp->vb, vb, tc, nb, !fp8, 1, 128);
+  return ok ? HTRC_OK : HTRC_ERR_CUDA;
+}
+
+int rowmax_fp8_maps(RowmaxFp8Maps* mp, const uint16_t* dqh, int64_t rows, const uint8_t* g8, const float* sg,
+                    const float* lz, int64_t tc, int64_t nb, int64_t pitch) {
+  bool ok = map_rows_halves(&mp->dqh, dqh, rows, 64) && map_codes(&mp->graw, g8, tc, nb, 128) &&
+            map_scalars(&mp->sg, sg, tc, nb, pitch, true, 128) && map_scalars(&mp->lz, lz, tc, nb, pitch, true, 128);
+  return ok ? HTRC_OK : HTRC_ERR_CUDA;
+}
+
+int tile_fp8_maps(TileFp8Maps* mp, const uint16_t* qb, const uint16_t* dqh, int64_t rows, const uint8_t* g8,
+                  const uint8_t* vb8, const float* lz, const float* sg, const float* sv, const uint8_t* excl, int64_t tc,
+                  int64_t nb, int64_t pitch, const uint16_t* k, const uint16_t* v, int64_t m) {
+  bool ok = map_rows_halves(&mp->qb, qb, rows, 64) && map_rows_halves(&mp->dqh, dqh, rows, 64) &&
+            map_codes(&mp->graw, g8, tc, nb, 64) && map_codes(&mp->vraw, vb8, tc, nb, 64) &&
+            map_scalars(&mp->lz, lz, tc, nb, pitch, true, 64) && map_scalars(&mp->sg, sg, tc, nb, pitch, true, 64) &&
+            map_scalars(&mp->sv, sv, tc, nb, pitch, true, 64) &&
+            map_scalars(&mp->excl, excl, tc, nb, pitch, false, 64) && map_rows_halves(&mp->k, k, m, 64) &&
+            map_rows_halves(&mp->v, v, m, 64);
   return ok ? HTRC_OK : HTRC_ERR_CUDA;
 }
 
@@ -327,11 +365,12 @@ int htrc_flat_forward(const HtrcFlatArgs* a, htrc_stream_t stream) {
   float* kn2 = L.iso ? at<float>(ws, L.kn2) : nullptr;
   float* dd = L.iso ? at<float>(ws, L.dd) : nullptr;
   float* cv = L.iso ? at<float>(ws, L.cv) : nullptr;
-  launch_pack_rows(a->k, HTRC_DTYPE_BF16, L.m, HTRC_ROUND_HALF_EVEN, k8, ks, kn2, st);
+  float* sv = L.fp8 ? at<float>(ws, L.sv) : nullptr;
+  if (!L.fp8) launch_pack_rows(a->k, HTRC_DTYPE_BF16, L.m, HTRC_ROUND_HALF_EVEN, k8, ks, kn2, st);
   if (perm && (rc = launch_kmeans_order(a->q, a->q_dtype, L.n, perm, at<void>(ws, L.km), st)) != HTRC_OK) return rc;
   const int trows = static_cast<int>(L.trows);
   launch_tile_prep(a->q, a->q_dtype, L.n, trows, perm, group, at<float>(ws, L.mu), mu_hi, mu_lo, q8, sq, dq8, sdq, dd,
-                   st);
+                   L.fp8, st);
   if (tail) launch_tail_partial(a->q, a->q_dtype, L.n, a->tail_k, a->tail_v, a->n_tail, scale, tail, st);
   if (cudaGetLastError() != cudaSuccess) return HTRC_ERR_CUDA;
   mark(1);
@@ -343,13 +382,21 @@ int htrc_flat_forward(const HtrcFlatArgs* a, htrc_stream_t stream) {
     const int64_t tc = std::min<int64_t>(gc * L.group, L.nt - t0);
     if (far) {
       LeafStatsMaps smp;
-      if ((rc = stats_maps(&smp, mu_hi, mu_lo, L.ng, a->k, a->v, L.m, g8, vb, gc, L.nb)) != HTRC_OK) return rc;
-      if ((rc = launch_leaf_stats(smp, sg, lz, L.pitch, g0, gc, nb, scale, kn2, cv, status, device_info().sms, st)) !=
-          HTRC_OK)
+      if ((rc = stats_maps(&smp, mu_hi, mu_lo, L.ng, a->k, a->v, L.m, g8, vb, gc, L.nb, L.fp8)) != HTRC_OK) return rc;
+      if ((rc = launch_leaf_stats(smp, sg, lz, L.pitch, g0, gc, nb, scale, kn2, cv, sv, status, device_info().sms,
+                                  st)) != HTRC_OK)
         return rc;
     }
     mark(2 + 4 * chunk);
-    if (far) {
+    if (far && L.fp8) {
+      if (kx > 0) {
+        RowmaxFp8Maps rmp;
+        if ((rc = rowmax_fp8_maps(&rmp, reinterpret_cast<const uint16_t*>(dq8), L.nt * 64,
+                                  reinterpret_cast<const uint8_t*>(g8), sg, lz, gc, L.nb, L.pitch)) != HTRC_OK)
+          return rc;
+        if ((rc = launch_rowmax_fp8(rmp, sel, L.pitch, t0, tc, nb, group, status, st)) != HTRC_OK) return rc;
+      }
+    } else if (far) {
       if (kx > 0) {
         RowmaxMaps rmp;
         if ((rc = rowmax_maps(&rmp, dq8, L.nt * 64, g8, sg, lz, cv, gc, L.nb, L.pitch)) != HTRC_OK) return rc;
@@ -359,6 +406,18 @@ int htrc_flat_forward(const HtrcFlatArgs* a, htrc_stream_t stream) {
     mark(3 + 4 * chunk);
     if ((rc = launch_route(sel, L.pitch, tc, group, nb, kx, sink, idx, excl, st)) != HTRC_OK) return rc;
     mark(4 + 4 * chunk);
+    if (L.fp8) {
+      TileFp8Maps tmp;
+      if ((rc = tile_fp8_maps(&tmp, reinterpret_cast<const uint16_t*>(q8), reinterpret_cast<const uint16_t*>(dq8),
+                              L.nt * 64, reinterpret_cast<const uint8_t*>(g8), reinterpret_cast<const uint8_t*>(vb), lz,
+                              sg, sv, excl, gc, L.nb, L.pitch, a->k, a->v, L.m)) != HTRC_OK)
+        return rc;
+      if ((rc = launch_tile_fp8(tmp, idx, kx, nb, L.n, trows, t0, tc, group, scale, tail, perm, a->out, a->lse, status,
+                                st)) != HTRC_OK)
+        return rc;
+      mark(5 + 4 * chunk);
+      continue;
+    }
     TileMaps tmp;
     if ((rc = tile_maps(&tmp, q8, dq8, L.nt * 64, g8, vb, lz, sg, cv, excl, gc, L.nb, L.pitch, k8, a->v, L.m)) !=
         HTRC_OK)
@@ -402,7 +461,7 @@ int htrc_tile_prep(const void* q, int32_t q_dtype, int64_t n_queries, int32_t di
   if (group > kMaxGroup) return HTRC_ERR_ARG;
   int rc = check_device();
   if (rc != HTRC_OK) return rc;
-  launch_tile_prep(q, q_dtype, n_queries, tile, perm, group, mu, mu_hi, mu_lo, q8, sq, dq8, sdq, dd,
+  launch_tile_prep(q, q_dtype, n_queries, tile, perm, group, mu, mu_hi, mu_lo, q8, sq, dq8, sdq, dd, false,
                    reinterpret_cast<cudaStream_t>(stream));
   return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
 }
@@ -439,9 +498,88 @@ int htrc_leaf_stats(const uint16_t* mu_hi, const uint16_t* mu_lo, int64_t nt, in
   int rc = check_device();
   if (rc != HTRC_OK) return rc;
   LeafStatsMaps mp;
-  if ((rc = stats_maps(&mp, mu_hi, mu_lo, nt, k, v, n_keys, g8, vb, tc, nb)) != HTRC_OK) return rc;
-  return launch_leaf_stats(mp, sg, lz, pitch_of(nb), t0, tc, static_cast<int>(nb), scale_of(scale), kn2, cv, status,
-                           device_info().sms, reinterpret_cast<cudaStream_t>(stream));
+  if ((rc = stats_maps(&mp, mu_hi, mu_lo, nt, k, v, n_keys, g8, vb, tc, nb, false)) != HTRC_OK) return rc;
+  return launch_leaf_stats(mp, sg, lz, pitch_of(nb), t0, tc, static_cast<int>(nb), scale_of(scale), kn2, cv, nullptr,
+                           status, device_info().sms, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int htrc_tile_prep_fp8(const void* q, int32_t q_dtype, int64_t n_queries, int32_t dim, int32_t tile,
+                       const int32_t* perm, int32_t group, float* mu, uint16_t* mu_hi, uint16_t* mu_lo, uint16_t* qb,
+                       uint16_t* dqh, htrc_stream_t stream) {
+  if (!q || !mu || !mu_hi || !mu_lo || !qb || !dqh || n_queries < 1) return HTRC_ERR_ARG;
+  if (dim != kDim || (tile != kTile && tile != kTile / 2)) return HTRC_ERR_UNSUPPORTED;
+  if (q_dtype != HTRC_DTYPE_F32 && q_dtype != HTRC_DTYPE_BF16) return HTRC_ERR_ARG;
+  if (group > kMaxGroup) return HTRC_ERR_ARG;
+  int rc = check_device();
+  if (rc != HTRC_OK) return rc;
+  launch_tile_prep(q, q_dtype, n_queries, tile, perm, group, mu, mu_hi, mu_lo, reinterpret_cast<int8_t*>(qb), nullptr,
+                   reinterpret_cast<int8_t*>(dqh), nullptr, nullptr, true, reinterpret_cast<cudaStream_t>(stream));
+  return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
+}
+
+int htrc_leaf_stats_fp8(const uint16_t* mu_hi, const uint16_t* mu_lo, int64_t nt, int64_t t0, int64_t tc,
+                        const uint16_t* k, const uint16_t* v, int64_t n_keys, int32_t dim, int32_t leaf, float scale,
+                        uint8_t* g8, float* sg, float* lz, uint8_t* vb8, float* sv, int32_t* status,
+                        htrc_stream_t stream) {
+  if (!mu_hi || !mu_lo || !k || !v || !g8 || !sg || !lz || !vb8 || !sv) return HTRC_ERR_ARG;
+  if (dim != kDim || leaf != kLeaf) return HTRC_ERR_UNSUPPORTED;
+  if (nt < 1 || t0 < 0 || tc < 1 || t0 + tc > nt || n_keys < leaf || n_keys % leaf) return HTRC_ERR_ARG;
+  const int64_t nb = n_keys / leaf;
+  if (nb > kMaxLeaves) return HTRC_ERR_UNSUPPORTED;
+  int rc = check_device();
+  if (rc != HTRC_OK) return rc;
+  LeafStatsMaps mp;
+  if ((rc = stats_maps(&mp, mu_hi, mu_lo, nt, k, v, n_keys, g8, vb8, tc, nb, true)) != HTRC_OK) return rc;
+  return launch_leaf_stats(mp, sg, lz, pitch_of(nb), t0, tc, static_cast<int>(nb), scale_of(scale), nullptr, nullptr,
+                           sv, status, device_info().sms, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int htrc_rowmax_select_fp8(const uint16_t* dqh, int64_t t0, int64_t tc, int32_t group, const uint8_t* g8,
+                           const float* sg, const float* lz, int64_t nb, int32_t dim, float* sel, int32_t* status,
+                           htrc_stream_t stream) {
+  if (!dqh || !g8 || !sg || !lz || !sel || t0 < 0 || tc < 1 || nb < 1) return HTRC_ERR_ARG;
+  const int64_t g = group > 1 ? group : 1;
+  if (g > kMaxGroup || t0 % g) return HTRC_ERR_ARG;
+  if (dim != kDim) return HTRC_ERR_UNSUPPORTED;
+  if (nb > kMaxLeaves) return HTRC_ERR_UNSUPPORTED;
+  int rc = check_device();
+  if (rc != HTRC_OK) return rc;
+  RowmaxFp8Maps mp;
+  if ((rc = rowmax_fp8_maps(&mp, dqh, (t0 + tc) * 64, g8, sg, lz, (tc + g - 1) / g, nb, pitch_of(nb))) != HTRC_OK)
+    return rc;
+  return launch_rowmax_fp8(mp, sel, pitch_of(nb), t0, tc, static_cast<int>(nb), static_cast<int>(g), status,
+                           reinterpret_cast<cudaStream_t>(stream));
+}
+
+int htrc_tile_attention_fp8(const uint16_t* qb, const uint16_t* dqh, int64_t n_queries, int32_t tile, int64_t t0,
+                            int64_t tc, int32_t group, const uint8_t* g8, const float* sg, const float* lz,
+                            const uint8_t* vb8, const float* sv, const uint8_t* excl, const int32_t* idx, int32_t kx,
+                            int64_t nb, const uint16_t* k, const uint16_t* v, int64_t n_keys, int32_t dim,
+                            int32_t leaf, float scale, const float* tail_part, const int32_t* perm, float* out,
+                            float* lse, int32_t* status, htrc_stream_t stream) {
+  if (!qb || !dqh || !k || !v || !out || n_queries < 1 || t0 < 0 || tc < 1) return HTRC_ERR_ARG;
+  const int64_t g = group > 1 ? group : 1;
+  if (g > kMaxGroup || t0 % g) return HTRC_ERR_ARG;
+  if (dim != kDim || leaf != kLeaf || (tile != kTile && tile != kTile / 2)) return HTRC_ERR_UNSUPPORTED;
+  if (nb < 1 || n_keys != nb * leaf || kx < 0 || kx > nb) return HTRC_ERR_ARG;
+  if (kx > kMaxRouted || nb > kMaxLeaves) return HTRC_ERR_UNSUPPORTED;
+  if (kx < nb && (!g8 || !sg || !lz || !vb8 || !sv || !excl)) return HTRC_ERR_ARG;
+  if (kx > 0 && !idx) return HTRC_ERR_ARG;
+  const int64_t nt = (n_queries + tile - 1) / tile;
+  if (t0 + tc > nt) return HTRC_ERR_ARG;
+  int rc = check_device();
+  if (rc != HTRC_OK) return rc;
+  // unused state maps (everything routed) still need a valid address: point them at the keys
+  const void* kp = static_cast<const void*>(k);
+  TileFp8Maps mp;
+  if ((rc = tile_fp8_maps(&mp, qb, dqh, nt * 64, static_cast<const uint8_t*>(g8 ? g8 : kp),
+                          static_cast<const uint8_t*>(vb8 ? vb8 : kp), lz ? lz : static_cast<const float*>(kp),
+                          sg ? sg : static_cast<const float*>(kp), sv ? sv : static_cast<const float*>(kp),
+                          excl ? excl : static_cast<const uint8_t*>(kp), (tc + g - 1) / g, nb, pitch_of(nb), k, v,
+                          n_keys)) != HTRC_OK)
+    return rc;
+  return launch_tile_fp8(mp, idx, kx, static_cast<int>(nb), n_queries, tile, t0, tc, static_cast<int>(g),
+                         scale_of(scale), tail_part, perm, out, lse, status, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int htrc_rowmax_select(const int8_t* dq8, const float* sdq, const float* dd, int64_t t0, int64_t tc, int32_t group,

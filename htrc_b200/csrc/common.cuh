@@ -6,6 +6,7 @@
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include "../../include/htrc_flat.h"
@@ -308,6 +309,12 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool a_mn_major,
          | ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
          (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
+// Instruction descriptor, kind::f16 with fp16 inputs and f32 accumulate.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool a_mn_major, bool b_mn_major) {
+  return (1u << 4)                    // D format f32 (A and B format 0: fp16)
+         | ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
+         (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
 // Instruction descriptor, kind::i8 with signed int8 inputs and s32 accumulate (both K-major).
 __host__ __device__ constexpr uint32_t idesc_i8(int M, int N) {
   return (2u << 4)                    // D format s32
@@ -322,6 +329,24 @@ __device__ __forceinline__ uint32_t sw128_off(uint32_t r, uint32_t c) { return r
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// e4m3 (fp8) codes: two bytes -> two fp16 values (byte 0 -> low half; exact, e4m3 is a subset of fp16),
+// and two float32 values -> two codes, nearest even, saturating at +-448 (lo -> byte 0)
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t two_codes) {
+  uint32_t h;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h) : "h"(static_cast<uint16_t>(two_codes & 0xFFFFu)));
+  return h;
+}
+__device__ __forceinline__ uint32_t f32x2_to_e4m3x2(float lo, float hi) {
+  uint16_t b;
+  asm("{\n\t.reg .b16 r;\n\tcvt.rn.satfinite.e4m3x2.f32 r, %1, %2;\n\tmov.b16 %0, r;\n\t}" : "=h"(b) : "f"(hi), "f"(lo));
+  return b;
 }
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {

@@ -12,7 +12,7 @@ struct LeafStatsMaps {
   int64_t nt;
   CUtensorMap k, v;           // [M, 128] bf16 as [2][M][64], box (64, 64, 2), 128B swizzle
   CUtensorMap g8;             // [tc, nb, 128] int8 (store), box (128, 1, 128), 128B swizzle
-  CUtensorMap vb;             // [tc, nb, 128] bf16 (store), box (64, 1, 128), 128B swizzle
+  CUtensorMap vb;             // [tc, nb, 128] bf16 (store), box (64, 1, 128), 128B swizzle; fp8: codes as g8
 };
 
 // state arrays hold one row per centre: per tile, or per group of tiles (rows [tc] below)
@@ -34,11 +34,26 @@ struct TileMaps {
   CUtensorMap cv;             // iso curvature coefficients [tc, nb] f32 (row pitch P), box (64, 1); any valid map
 };
 
+// fp8 (e4m3) state path
+struct RowmaxFp8Maps {
+  CUtensorMap dqh;            // [nt*64, 128] fp16 as [2][rows][64], box (64, 64, 2), 128B swizzle
+  CUtensorMap graw;           // [tc, nb, 128] e4m3 codes, box (128, 128, 1), no swizzle
+  CUtensorMap sg, lz;         // [tc, nb] f32 (row pitch P), box (128, 1)
+};
+
+struct TileFp8Maps {
+  CUtensorMap qb, dqh;        // [nt*64, 128] bf16 / fp16 as [2][rows][64], box (64, 64, 2), 128B swizzle
+  CUtensorMap graw, vraw;     // [tc, nb, 128] e4m3 codes of g / vbar, box (128, 64, 1), no swizzle
+  CUtensorMap lz, sg, sv;     // [tc, nb] f32 (row pitch P), box (64, 1)
+  CUtensorMap excl;           // [tc, nb] u8 (row pitch P), box (64, 1)
+  CUtensorMap k, v;           // [M, 128] bf16 as [2][M][64], box (64, 64, 2), 128B swizzle
+};
+
 void launch_pack_rows(const void* x, int dtype, int64_t rows, int rounding, int8_t* x8, float* scale, float* sqnorm,
                       cudaStream_t st);
 void launch_tile_prep(const void* q, int dtype, int64_t n, int tile_rows, const int32_t* perm, int group, float* mu,
                       uint16_t* mu_hi, uint16_t* mu_lo, int8_t* q8, float* sq, int8_t* dq8, float* sdq, float* dd,
-                      cudaStream_t st);
+                      bool fp8, cudaStream_t st);
 size_t kmeans_scratch_bytes(int64_t n);
 int launch_kmeans_order(const void* q, int dtype, int64_t n, int32_t* perm, void* scratch, cudaStream_t st);
 void launch_fake_quant(const void* x, int x_dtype, int64_t rows, int fmt, int gsz, void* out, int out_dtype,
@@ -48,7 +63,7 @@ void launch_dequant_rows(const uint8_t* x8, int64_t stride_x, const float* scale
 void launch_tail_partial(const void* q, int dtype, int64_t n, const float* tk, const float* tv, int n_tail, float scale,
                          float* part, cudaStream_t st);
 int launch_leaf_stats(const LeafStatsMaps& maps, float* sg, float* lz, int64_t pitch, int64_t t0, int64_t tc, int nb,
-                      float scale, const float* kn2, float* cv, int* status, int num_sms, cudaStream_t st);
+                      float scale, const float* kn2, float* cv, float* sv, int* status, int num_sms, cudaStream_t st);
 int launch_rowmax(const RowmaxMaps& maps, const float* sdq, const float* dd, float* sel, int64_t pitch, int64_t t0,
                   int64_t tc, int nb, int group, int* status, cudaStream_t st);
 int launch_route(const float* sel, int64_t pitch, int64_t tc, int group, int nb, int kx, int sink, int32_t* idx,
@@ -57,5 +72,10 @@ int launch_tile_attention(const TileMaps& maps, const float* sq, const float* sd
                           int kx, int nb, int64_t n, int tile_rows, int64_t t0, int64_t tc, int group, float scale,
                           const float* tail_part, const int32_t* perm, const float* dd, float* out, float* lse,
                           int* status, cudaStream_t st);
+int launch_rowmax_fp8(const RowmaxFp8Maps& maps, float* sel, int64_t pitch, int64_t t0, int64_t tc, int nb, int group,
+                      int* status, cudaStream_t st);
+int launch_tile_fp8(const TileFp8Maps& maps, const int32_t* idx, int kx, int nb, int64_t n, int tile_rows, int64_t t0,
+                    int64_t tc, int group, float scale, const float* tail_part, const int32_t* perm, float* out,
+                    float* lse, int* status, cudaStream_t st);
 
 }  // namespace htrc

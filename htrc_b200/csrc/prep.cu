@@ -170,8 +170,10 @@ __global__ void __launch_bounds__(128) group_centre_kernel(const T* __restrict__
 
 // One CTA (4 warps) per tile of T query rows (held as 64 rows): the tile's centre (group 1; else the
 // group centre written by group_centre_kernel) and the codes of its rows and of their offsets from
-// the centre.
-template <typename T>
+// the centre.  FP8 (the fp8 state path, h3/htrc_flat_triton.py:103-109) writes instead the rows as bf16
+// (q8 holds uint16 bf16 rows) and the float32 offsets rounded once to fp16 (dq8 holds uint16 fp16 rows);
+// sq / sdq are not written.
+template <typename T, bool FP8>
 __global__ void __launch_bounds__(128) tile_prep_kernel(const T* __restrict__ q, const int32_t* __restrict__ perm,
                                                         int64_t n, int trows, int group, float* __restrict__ mu,
                                                         uint16_t* __restrict__ mu_hi, uint16_t* __restrict__ mu_lo,
@@ -222,13 +224,18 @@ __global__ void __launch_bounds__(128) tile_prep_kernel(const T* __restrict__ q,
       v[i] = qs[r][lane * 4 + i];
       d[i] = __fsub_rn(v[i], m4[i]);
     }
+    const int64_t gr = r0 + r;
+    if constexpr (FP8) {
+      reinterpret_cast<uint2*>(q8 + gr * 256)[lane] = make_uint2(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]));
+      reinterpret_cast<uint2*>(dq8 + gr * 256)[lane] = make_uint2(pack_f16x2(d[0], d[1]), pack_f16x2(d[2], d[3]));
+      continue;
+    }
     float aq = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
     float ad = fmaxf(fmaxf(fabsf(d[0]), fabsf(d[1])), fmaxf(fabsf(d[2]), fabsf(d[3])));
     aq = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(aq)));
     ad = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(ad)));
     const float s_q = fmaxf(__fmul_rn(aq, kInv127), 1e-20f);
     const float s_d = fmaxf(__fmul_rn(ad, kInv127), 1e-20f);
-    const int64_t gr = r0 + r;
     reinterpret_cast<uint32_t*>(q8 + gr * 128)[lane] = quant4<1>(v, s_q, __frcp_rn(s_q));
     reinterpret_cast<uint32_t*>(dq8 + gr * 128)[lane] = quant4<1>(d, s_d, __frcp_rn(s_d));
     if (lane == 0) {
@@ -244,7 +251,7 @@ __global__ void __launch_bounds__(128) tile_prep_kernel(const T* __restrict__ q,
 
 void launch_tile_prep(const void* q, int dtype, int64_t n, int tile_rows, const int32_t* perm, int group, float* mu,
                       uint16_t* mu_hi, uint16_t* mu_lo, int8_t* q8, float* sq, int8_t* dq8, float* sdq, float* dd,
-                      cudaStream_t st) {
+                      bool fp8, cudaStream_t st) {
   const int tr = tile_rows == 32 ? 32 : 64;
   const int64_t nt = (n + tr - 1) / tr;
   const int g = group > 1 ? group : 1;
@@ -252,13 +259,13 @@ void launch_tile_prep(const void* q, int dtype, int64_t n, int tile_rows, const 
   if (dtype == HTRC_DTYPE_BF16) {
     const uint16_t* qb = static_cast<const uint16_t*>(q);
     if (g > 1) group_centre_kernel<uint16_t><<<ng, 128, 0, st>>>(qb, perm, n, tr, nt, g, mu, mu_hi, mu_lo);
-    tile_prep_kernel<uint16_t><<<static_cast<unsigned>(nt), 128, 0, st>>>(qb, perm, n, tr, g, mu, mu_hi, mu_lo, q8,
-                                                                         sq, dq8, sdq, dd);
+    auto k = fp8 ? tile_prep_kernel<uint16_t, true> : tile_prep_kernel<uint16_t, false>;
+    k<<<static_cast<unsigned>(nt), 128, 0, st>>>(qb, perm, n, tr, g, mu, mu_hi, mu_lo, q8, sq, dq8, sdq, dd);
   } else {
     const float* qf = static_cast<const float*>(q);
     if (g > 1) group_centre_kernel<float><<<ng, 128, 0, st>>>(qf, perm, n, tr, nt, g, mu, mu_hi, mu_lo);
-    tile_prep_kernel<float><<<static_cast<unsigned>(nt), 128, 0, st>>>(qf, perm, n, tr, g, mu, mu_hi, mu_lo, q8, sq,
-                                                                      dq8, sdq, dd);
+    auto k = fp8 ? tile_prep_kernel<float, true> : tile_prep_kernel<float, false>;
+    k<<<static_cast<unsigned>(nt), 128, 0, st>>>(qf, perm, n, tr, g, mu, mu_hi, mu_lo, q8, sq, dq8, sdq, dd);
   }
 }
 

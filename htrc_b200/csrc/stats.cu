@@ -15,6 +15,9 @@
 // backend's curvature="iso"): c = 0.5 / D * max(tr, 0), tr = scale^2 (sum_s w_s |k_s|^2 - |sum_s w_s k_s|^2);
 // the softmax warps form sum_s w_s |k_s|^2 from the key norms staged with K/V, the epilogue |G|^2 from
 // its G columns (the two halves exchange partial sums with their abs-maxima).
+// FP8 stores the state as e4m3 codes with per-(centre, leaf) row scales instead (h3/htrc_flat_triton.py:65-72,
+// store="fp8"): sg = max(amax|g| * (1/448), 1e-30), g codes = e4m3(g / sg) rounded to nearest even and
+// saturated at 448, and the same for vbar with sv (vbar from the full W . V, both W halves).
 //
 // Warp roles (512 threads, one role per warpgroup so that setmaxnreg can move registers from the
 // issuing warps to the arithmetic): warpgroup 0 = warp 0 TMA producer, warp 1 S issuer (+ TMEM owner),
@@ -88,14 +91,14 @@ __device__ __forceinline__ uint2 half_away_codes2(float2 y) {
 }
 }  // namespace
 
-template <bool ISO>
+template <bool ISO, bool FP8>
 __global__ void __launch_bounds__(kThreads, 1)
     leaf_stats_kernel(const uint16_t* __restrict__ mu_hi_g, const uint16_t* __restrict__ mu_lo_g, int64_t nt,
                       const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                       const __grid_constant__ CUtensorMap tm_g8, const __grid_constant__ CUtensorMap tm_vb,
                       float* __restrict__ sg_out, float* __restrict__ lz_out, int64_t pitch, int64_t t0, int64_t tc,
                       int nb, int leaves_per_cta, float scale, const float* __restrict__ kn2,
-                      float* __restrict__ cv_out, int* status) {
+                      float* __restrict__ cv_out, float* __restrict__ sv_out, int* status) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Bars* bars = reinterpret_cast<Bars*>(smem + kOffBar);
@@ -213,10 +216,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t a = sw128_desc(w_hi + kk * 32, 16, 1024);
-            const uint64_t bdesc = sw128_desc(vst + kk * 2048, kLeafBytes / 2, 1024);
-            mma_bf16_by(leader, tmem + kColV, a, bdesc, id_gv, kk != 0);
+          for (int h = 0; h < (FP8 ? 2 : 1); ++h) {
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint64_t a = sw128_desc((h ? w_lo : w_hi) + kk * 32, 16, 1024);
+              const uint64_t bdesc = sw128_desc(vst + kk * 2048, kLeafBytes / 2, 1024);
+              mma_bf16_by(leader, tmem + kColV, a, bdesc, id_gv, (h | kk) != 0);
+            }
           }
           mma_commit_by(leader, &bars->gv_full);
           mma_commit_by(leader, &bars->w_empty);
@@ -357,6 +363,88 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(&bars->gv_full, j & 1, status, abort_flag)) break;
       __syncwarp();
       tc_fence_after();
+      if constexpr (FP8) {
+        // this half of G and its abs-max, then the abs-max of this half of VB (read twice from TMEM, so that
+        // only G stays in registers); the halves of a row exchange both through shared memory
+        uint32_t gr[64];
+        tmem_ld32(tmem + lane_base + colg, *reinterpret_cast<uint32_t(*)[32]>(gr));
+        tmem_ld32(tmem + lane_base + colg + 32, *reinterpret_cast<uint32_t(*)[32]>(gr + 32));
+        tmem_ld_wait();
+        float ama[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int i = 0; i < 64; i += 2)
+          ama[(i >> 1) & 3] = max3(ama[(i >> 1) & 3], fabsf(__uint_as_float(gr[i])), fabsf(__uint_as_float(gr[i + 1])));
+        float am = __fmul_rn(fmaxf(fmaxf(ama[0], ama[1]), fmaxf(ama[2], ama[3])), scale);
+        float vam = 0.f;
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tmem + lane_base + colv + 32 * c, r);
+          tmem_ld_wait();
+          float vm[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int i = 0; i < 32; i += 2)
+            vm[(i >> 1) & 3] = max3(vm[(i >> 1) & 3], fabsf(__uint_as_float(r[i])), fabsf(__uint_as_float(r[i + 1])));
+          vam = fmaxf(vam, fmaxf(fmaxf(vm[0], vm[1]), fmaxf(vm[2], vm[3])));
+        }
+        float* amv = reinterpret_cast<float*>(smem + kOffB2);
+        amx[((j & 1) * 2 + half) * 128 + row] = am;
+        amv[((j & 1) * 2 + half) * 128 + row] = vam;
+        named_bar_sync(1 + quarter, 64);
+        am = fmaxf(am, amx[((j & 1) * 2 + (half ^ 1)) * 128 + row]);
+        vam = fmaxf(vam, amv[((j & 1) * 2 + (half ^ 1)) * 128 + row]);
+        const float sgv = fmaxf(__fmul_rn(am, 1.0f / 448.0f), 1e-30f);
+        const float svv = fmaxf(__fmul_rn(vam, 1.0f / 448.0f), 1e-30f);
+        if (valid && half == 0) {
+          sg_out[tloc * pitch + leaf] = sgv;
+          sv_out[tloc * pitch + leaf] = svv;
+        }
+        const float2 sc2 = make_float2(scale, scale);
+        const float rg = __frcp_rn(sgv), rv = __frcp_rn(svv);
+        const float2 rg2 = make_float2(rg, rg), rv2 = make_float2(rv, rv);
+        uint32_t gw[16], vw[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float2 a = mul2(mul2(make_float2(__uint_as_float(gr[4 * i]), __uint_as_float(gr[4 * i + 1])), sc2), rg2);
+          const float2 b = mul2(mul2(make_float2(__uint_as_float(gr[4 * i + 2]), __uint_as_float(gr[4 * i + 3])), sc2), rg2);
+          gw[i] = f32x2_to_e4m3x2(a.x, a.y) | (f32x2_to_e4m3x2(b.x, b.y) << 16);
+        }
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tmem + lane_base + colv + 32 * c, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float2 a = mul2(make_float2(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1])), rv2);
+            const float2 b = mul2(make_float2(__uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3])), rv2);
+            vw[8 * c + i] = f32x2_to_e4m3x2(a.x, a.y) | (f32x2_to_e4m3x2(b.x, b.y) << 16);
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&bars->gv_empty);
+        if (lead) {
+          bulk_wait_group_read0();
+          mbar_arrive(&bars->stg_free);
+        }
+        if (!mbar_wait(&bars->stg_free, j & 1, status, abort_flag)) break;
+        __syncwarp();
+        // this half is the 16-byte chunks 4 half .. 4 half + 3 of the 128-byte code rows of g and vbar
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          st_shared_v4(stg + sw128_off(row, 4 * half + c), gw[4 * c], gw[4 * c + 1], gw[4 * c + 2], gw[4 * c + 3]);
+          st_shared_v4(stv + sw128_off(row, 4 * half + c), vw[4 * c], vw[4 * c + 1], vw[4 * c + 2], vw[4 * c + 3]);
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&bars->stg_full);
+        if (lead) {
+          if (!mbar_wait(&bars->stg_full, j & 1, status, abort_flag)) break;
+          tma_store_3d(&tm_g8, smem + kOffStG, 0, leaf, blk * 128);
+          tma_store_3d(&tm_vb, smem + kOffStV, 0, leaf, blk * 128);
+          bulk_commit_group();
+        }
+        continue;
+      }
       // drain this half of G (raw) and VB (as bf16 pairs) into registers and release TMEM at once, so the
       // next leaf's G/VB MMAs overlap the quantisation below
       uint32_t gr[64];
@@ -453,26 +541,27 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 int launch_leaf_stats(const LeafStatsMaps& maps, float* sg, float* lz, int64_t pitch, int64_t t0, int64_t tc, int nb,
-                      float scale, const float* kn2, float* cv, int* status, int num_sms, cudaStream_t st) {
+                      float scale, const float* kn2, float* cv, float* sv, int* status, int num_sms, cudaStream_t st) {
   static bool attr_done[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr_done[dev]) {
-    if (cudaFuncSetAttribute(leaf_stats_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
-            cudaSuccess ||
-        cudaFuncSetAttribute(leaf_stats_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
-            cudaSuccess)
-      return HTRC_ERR_CUDA;
+    bool ok = true;
+    for (auto k : {leaf_stats_kernel<false, false>, leaf_stats_kernel<true, false>, leaf_stats_kernel<false, true>})
+      ok = ok && cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) == cudaSuccess;
+    if (!ok) return HTRC_ERR_CUDA;
     attr_done[dev] = true;
   }
+  if (sv != nullptr && cv != nullptr) return HTRC_ERR_UNSUPPORTED;
   const int bx = static_cast<int>((tc + 127) / 128);
   int by = max(1, num_sms / bx);                    // one wave: bx * by <= SMs
   by = min(by, nb);
   const int lpc = (nb + by - 1) / by;
   by = (nb + lpc - 1) / lpc;
-  auto kernel = cv != nullptr ? leaf_stats_kernel<true> : leaf_stats_kernel<false>;
+  auto kernel = sv != nullptr ? leaf_stats_kernel<false, true>
+                               : (cv != nullptr ? leaf_stats_kernel<true, false> : leaf_stats_kernel<false, false>);
   kernel<<<dim3(bx, by), kThreads, kSmemBytes, st>>>(maps.mu_hi, maps.mu_lo, maps.nt, maps.k, maps.v, maps.g8, maps.vb,
-                                                     sg, lz, pitch, t0, tc, nb, lpc, scale, kn2, cv, status);
+                                                     sg, lz, pitch, t0, tc, nb, lpc, scale, kn2, cv, sv, status);
   return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
 }
 

@@ -7,6 +7,10 @@ C-ABI library libhtrc_flat.so (hand-written sm_100a kernels).  There is no other
 fallback: configurations the kernels do not implement raise ``NotImplementedError`` and argument
 errors raise the reference's ``ValueError``s.
 
+State format: ``store="int8"`` (the production path) or ``store="fp8"``: the reference's e4m3 far-field
+state with per-(centre, leaf) row scales, fp16 far-field dots and a bf16 near field
+(h3/htrc_flat_triton.py FP8=1), on its own sm_100a kernels.
+
 Curvature: ``curvature="iso"`` with ``backend="cuda"`` (or "b200") adds the isotropic second-order far-field
 term of the reference's torch backend (h3/htrc_flat.py:331-333) to the INT8 production path; the
 reference's triton backend rejects it, and so does ``backend="triton"`` here.
@@ -91,8 +95,11 @@ def _check_args(q, k, v, tile, exact_leaves, order, curvature, leaf, select, bac
         raise ValueError("dot='bf16' needs store='bf16', 'fp8' or 'int8'")
     if store in ("fp8", "int8") and (dot != "bf16" or select == "bound" or (quant or {}).get("state")):
         raise ValueError("store='fp8' needs dot='bf16', select='max' and no state fake-quant")
-    if store != "int8" or dot != "bf16":
-        raise NotImplementedError("only the INT8 production path (store='int8', dot='bf16') is implemented")
+    if store not in _lib.STORES or dot != "bf16":
+        raise NotImplementedError("only the dot='bf16' paths with store='int8' (production) or store='fp8' are "
+                                  "implemented")
+    if store == "fp8" and curvature != "lin":
+        raise NotImplementedError("curvature='iso' is implemented on the INT8 path only")
     if int(tile) not in TILES or int(leaf) != LEAF:
         raise NotImplementedError(f"the kernels implement tile=64 or 32, leaf={LEAF} (got tile={tile}, leaf={leaf})")
     if int(sel_stride) != 1:
@@ -180,7 +187,8 @@ def curvature_code(curvature) -> int:
 
 
 def _args(qd, kb, vb, tk, tv, exact_leaves, sink_leaves, tile_chunk, scale, out=None, lse=None, ws=None,
-          stage_events=None, group=1, order=_lib.ORDER_SEQ, tile=TILE, curvature=_lib.CURV_LIN):
+          stage_events=None, group=1, order=_lib.ORDER_SEQ, tile=TILE, curvature=_lib.CURV_LIN,
+          store=_lib.STORE_INT8):
     a = _lib.HtrcFlatArgs()
     a.q = ptr(qd)
     a.q_dtype = _lib.DTYPE_BF16 if qd.dtype == torch.bfloat16 else _lib.DTYPE_F32
@@ -193,7 +201,7 @@ def _args(qd, kb, vb, tk, tv, exact_leaves, sink_leaves, tile_chunk, scale, out=
     a.tail_k, a.tail_v = ptr(tk), ptr(tv)
     a.n_tail = int(tk.shape[0]) if tk is not None else 0
     a.out, a.lse = ptr(out), ptr(lse)
-    a.group, a.order, a.curvature = int(group), int(order), int(curvature)
+    a.group, a.order, a.curvature, a.store = int(group), int(order), int(curvature), int(store)
     if ws is not None:
         a.workspace, a.workspace_bytes = ptr(ws), int(ws.numel())
     if stage_events:
@@ -210,14 +218,14 @@ def _args(qd, kb, vb, tk, tv, exact_leaves, sink_leaves, tile_chunk, scale, out=
 
 
 def workspace_bytes(n_queries, n_keys, exact_leaves, sink_leaves=0, tile_chunk=0, n_tail=0, group=1,
-                    order=_lib.ORDER_SEQ, tile=TILE, curvature=_lib.CURV_LIN) -> int:
+                    order=_lib.ORDER_SEQ, tile=TILE, curvature=_lib.CURV_LIN, store=_lib.STORE_INT8) -> int:
     """Device workspace one forward call needs."""
     a = _lib.HtrcFlatArgs()
     a.n_queries, a.n_keys, a.dim, a.tile, a.leaf = int(n_queries), int(n_keys), DIM, int(tile), LEAF
     a.q_dtype = _lib.DTYPE_F32
     a.exact_leaves, a.sink_leaves = int(exact_leaves), int(sink_leaves)
     a.tile_chunk, a.n_tail = int(tile_chunk or 0), int(n_tail)
-    a.group, a.order, a.curvature = int(group), int(order), int(curvature)
+    a.group, a.order, a.curvature, a.store = int(group), int(order), int(curvature), int(store)
     nbytes = ctypes.c_size_t()
     check(lib().htrc_flat_workspace_size(a, nbytes), "workspace size")
     return int(nbytes.value)
@@ -245,13 +253,14 @@ def _workspace(ws, nbytes, device):
 
 def forward_into(qd, kb, vb, tk, tv, *, exact_leaves, sink_leaves=0, tile_chunk=0, scale=None, out, lse=None,
                  workspace, stream=None, stage_events=None, group=1, order=_lib.ORDER_SEQ, tile=TILE,
-                 curvature=_lib.CURV_LIN):
+                 curvature=_lib.CURV_LIN, store=_lib.STORE_INT8):
     """One head through ``htrc_flat_forward`` into caller-provided buffers (no allocation; CUDA-graph
     capturable).  qd [N, 128] f32/bf16, kb/vb [M, 128] bf16, out [N, 128] f32, lse [N] f32 or None;
     stage_events: optional list of torch.cuda.Event recorded between the stages (see
-    include/htrc_flat.h); group / order: ``group_of(kern)`` / ``order_code(order)``; tile: 64 or 32."""
+    include/htrc_flat.h); group / order: ``group_of(kern)`` / ``order_code(order)``; tile: 64 or 32;
+    store: ``_lib.STORES[store]``."""
     a = _args(qd, kb, vb, tk, tv, exact_leaves, sink_leaves, tile_chunk, scale, out, lse, workspace, stage_events,
-              group, order, tile, curvature)
+              group, order, tile, curvature, store)
     check(lib().htrc_flat_forward(a, stream_ptr(stream)), "htrc_flat_forward")
 
 
@@ -279,20 +288,21 @@ def flat_attention(q, k, v, *, tile=64, exact_leaves=64, order="seq", curvature=
     _check_args(q, k, v, tile, exact_leaves, order, curvature, leaf, select, backend, store, dot,
                 sel_stride, quant, sink_leaves, tail)
     qd, kb, vb, tk, tv = _prep_inputs(q, k, v, tail, quant)
-    grp, oc, cc = group_of(kern), order_code(order), curvature_code(curvature)
+    grp, oc, cc, sc = group_of(kern), order_code(order), curvature_code(curvature), _lib.STORES[store]
     if prof is not None:
         st = run_stages(qd, kb, vb, tk, tv, exact_leaves=exact_leaves, sink_leaves=sink_leaves,
-                        tile_chunk=tile_chunk, scale=scale, prof=prof, group=grp, order=oc, tile=tile, curvature=cc)
+                        tile_chunk=tile_chunk, scale=scale, prof=prof, group=grp, order=oc, tile=tile, curvature=cc,
+                        store=sc)
         return (st["out"], st["lse"]) if return_lse else st["out"]
     n = int(qd.shape[0])
     out = torch.empty((n, DIM), dtype=torch.float32, device=q.device)
     lse = torch.empty((n,), dtype=torch.float32, device=q.device) if return_lse else None
     nbytes = workspace_bytes(n, int(kb.shape[0]), exact_leaves, sink_leaves, tile_chunk,
-                             int(tk.shape[0]) if tk is not None else 0, grp, oc, tile, cc)
+                             int(tk.shape[0]) if tk is not None else 0, grp, oc, tile, cc, sc)
     w = _workspace(ws, nbytes, q.device)
     forward_into(qd, kb, vb, tk, tv, exact_leaves=exact_leaves, sink_leaves=sink_leaves,
                  tile_chunk=tile_chunk, scale=scale, out=out, lse=lse, workspace=w, group=grp, order=oc, tile=tile,
-                 curvature=cc)
+                 curvature=cc, store=sc)
     return (out, lse) if return_lse else out
 
 
@@ -303,9 +313,11 @@ def flat_attention_prod(q, k, v, **over):
 
 @torch.inference_mode()
 def run_stages(qd, kb, vb, tk=None, tv=None, *, exact_leaves, sink_leaves=0, tile_chunk=0, scale=None,
-               prof=None, stream=None, group=1, order=_lib.ORDER_SEQ, tile=TILE, curvature=_lib.CURV_LIN):
+               prof=None, stream=None, group=1, order=_lib.ORDER_SEQ, tile=TILE, curvature=_lib.CURV_LIN,
+               store=_lib.STORE_INT8):
     """The same operator launched stage by stage through the C ABI's stage entry points, returning
-    every intermediate (perm, k8, ks, mu, q8, sq, dq8, sdq, g8, sg, lz, vb, sel, idx, excl, out, lse).
+    every intermediate (perm, k8, ks, mu, q8, sq, dq8, sdq, g8, sg, lz, vb, sel, idx, excl, out, lse; with
+    store=STORE_FP8: perm, mu, qb, dqh, g8 / vb8 e4m3 codes, sg, sv, lz, sel, idx, excl, out, lse).
     Used for stage timing (``prof``, the reference's stage names prep/stats/select/tile/finish) and
     for per-stage parity tests.  The state of all centre rows is kept (tile_chunk only sets the launch
     granularity of the state stages, in groups of ``group`` tiles)."""
@@ -324,6 +336,12 @@ def run_stages(qd, kb, vb, tk=None, tv=None, *, exact_leaves, sink_leaves=0, til
     sc = 1.0 / math.sqrt(DIM) if scale is None else float(scale)
     qdt = _lib.DTYPE_BF16 if qd.dtype == torch.bfloat16 else _lib.DTYPE_F32
     e = lambda *shape, dt=torch.float32: torch.empty(shape, dtype=dt, device=dev)  # noqa: E731
+    if store == _lib.STORE_FP8:
+        if curvature != _lib.CURV_LIN:
+            raise NotImplementedError("curvature='iso' is implemented on the INT8 path only")
+        return _run_stages_fp8(qd, kb, vb, tk, tv, n=n, m=m, nt=nt, nb=nb, ng=ng, grp=grp, pitch=pitch, sink=sink,
+                               kx=kx, sc=sc, qdt=qdt, tile=tile, tile_chunk=tile_chunk, exact_leaves=exact_leaves,
+                               order=order, s=s, tick=tick, e=e)
     r = dict(k8=e(m, DIM, dt=torch.int8), ks=e(m), mu=e(ng, DIM), mu_hi=e(ng, DIM, dt=torch.bfloat16),
              mu_lo=e(ng, DIM, dt=torch.bfloat16), q8=e(nt * TILE, DIM, dt=torch.int8), sq=e(nt * TILE),
              dq8=e(nt * TILE, DIM, dt=torch.int8), sdq=e(nt * TILE), g8=e(ng, nb, DIM, dt=torch.int8),
@@ -372,6 +390,60 @@ def run_stages(qd, kb, vb, tk=None, tv=None, *, exact_leaves, sink_leaves=0, til
                                 ptr(r["sg"]), ptr(r["lz"]), ptr(r["vb"]), ptr(r["excl"]), ptr(r["idx"]), kx, nb,
                                 ptr(r["k8"]), ptr(r["ks"]), ptr(vb), m, DIM, LEAF, sc, ptr(tail_part), perm,
                                 ptr(r["cv"]), ptr(r["dd"]), ptr(r["out"]), ptr(r["lse"]), stp, s), "htrc_tile_attention")
+    tick("tile")
+    tick("finish")
+    r["kx"], r["nb"], r["pitch"], r["group"], r["tile"] = kx, nb, pitch, grp, tile
+    return r
+
+
+def _run_stages_fp8(qd, kb, vb, tk, tv, *, n, m, nt, nb, ng, grp, pitch, sink, kx, sc, qdt, tile, tile_chunk,
+                    exact_leaves, order, s, tick, e):
+    """run_stages for the fp8 state (store="fp8"): tile prep with bf16 rows and fp16 offsets, e4m3 leaf
+    statistics, fp8 row-max selection, routing and the fp8 tile kernel."""
+    L = lib()
+    dev = qd.device
+    r = dict(mu=e(ng, DIM), mu_hi=e(ng, DIM, dt=torch.bfloat16), mu_lo=e(ng, DIM, dt=torch.bfloat16),
+             qb=e(nt * TILE, DIM, dt=torch.bfloat16), dqh=e(nt * TILE, DIM, dt=torch.float16),
+             g8=e(ng, nb, DIM, dt=torch.uint8), vb8=e(ng, nb, DIM, dt=torch.uint8), sg=e(ng, pitch), sv=e(ng, pitch),
+             lz=e(ng, pitch), sel=torch.zeros((nt, pitch), dtype=torch.float32, device=dev),
+             idx=e(ng, max(kx, 1), dt=torch.int32), excl=e(ng, pitch, dt=torch.uint8), out=e(n, DIM), lse=e(n),
+             status=torch.zeros((1,), dtype=torch.int32, device=dev), perm=None)
+    stp = ptr(r["status"])
+    if order == _lib.ORDER_KMEANS:
+        r["perm"] = e(n, dt=torch.int32)
+        nbytes = ctypes.c_size_t()
+        check(L.htrc_kmeans_scratch_size(n, nbytes), "htrc_kmeans_scratch_size")
+        scratch = torch.empty(int(nbytes.value), dtype=torch.uint8, device=dev)
+        check(L.htrc_kmeans_order(ptr(qd), qdt, n, DIM, ptr(r["perm"]), ptr(scratch), int(nbytes.value), s),
+              "htrc_kmeans_order")
+    perm = ptr(r["perm"])
+    check(L.htrc_tile_prep_fp8(ptr(qd), qdt, n, DIM, tile, perm, grp, ptr(r["mu"]), ptr(r["mu_hi"]), ptr(r["mu_lo"]),
+                               ptr(r["qb"]), ptr(r["dqh"]), s), "htrc_tile_prep_fp8")
+    tail_part = None
+    if tk is not None:
+        tail_part = e(n, DIM + 2)
+        check(L.htrc_tail_partial(ptr(qd), qdt, n, DIM, ptr(tk), ptr(tv), int(tk.shape[0]), sc, ptr(tail_part), s),
+              "htrc_tail_partial")
+    tick("prep")
+    gstep = ng if not tile_chunk or tile_chunk <= 0 else min(max(1, int(tile_chunk) // grp), ng)
+    far = kx < nb
+    if far:
+        for g0 in range(0, ng, gstep):
+            gc = min(gstep, ng - g0)
+            check(L.htrc_leaf_stats_fp8(ptr(r["mu_hi"]), ptr(r["mu_lo"]), ng, g0, gc, ptr(kb), ptr(vb), m, DIM, LEAF,
+                                        sc, ptr(r["g8"][g0]), ptr(r["sg"][g0]), ptr(r["lz"][g0]), ptr(r["vb8"][g0]),
+                                        ptr(r["sv"][g0]), stp, s), "htrc_leaf_stats_fp8")
+    tick("stats")
+    if far and kx > 0:
+        check(L.htrc_rowmax_select_fp8(ptr(r["dqh"]), 0, nt, grp, ptr(r["g8"]), ptr(r["sg"]), ptr(r["lz"]), nb, DIM,
+                                       ptr(r["sel"]), stp, s), "htrc_rowmax_select_fp8")
+    check(L.htrc_route(ptr(r["sel"]), nt, nb, int(exact_leaves), sink, grp, ptr(r["idx"]), ptr(r["excl"]), s),
+          "htrc_route")
+    tick("select")
+    check(L.htrc_tile_attention_fp8(ptr(r["qb"]), ptr(r["dqh"]), n, tile, 0, nt, grp, ptr(r["g8"]), ptr(r["sg"]),
+                                    ptr(r["lz"]), ptr(r["vb8"]), ptr(r["sv"]), ptr(r["excl"]), ptr(r["idx"]), kx, nb,
+                                    ptr(kb), ptr(vb), m, DIM, LEAF, sc, ptr(tail_part), perm, ptr(r["out"]),
+                                    ptr(r["lse"]), stp, s), "htrc_tile_attention_fp8")
     tick("tile")
     tick("finish")
     r["kx"], r["nb"], r["pitch"], r["group"], r["tile"] = kx, nb, pitch, grp, tile

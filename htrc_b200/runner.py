@@ -18,6 +18,7 @@ from __future__ import annotations
 
 import torch
 
+from . import _lib
 from . import flat as _flat
 
 MODES = {
@@ -92,6 +93,7 @@ class FlatRunner:
         self.group = _flat.group_of(base.get("kern"))
         self.order = _flat.order_code(base["order"])
         self.curvature = _flat.curvature_code(base.get("curvature", "lin"))
+        self.store = _lib.STORES.get(base.get("store", "int8"), _lib.STORE_INT8)
         if tile_chunk is None:
             if free_bytes is None and self.device.type == "cuda" and torch.cuda.is_available():
                 # plan from the device's free memory (the reference falls back to PROD's 128-tile chunk,
@@ -152,11 +154,11 @@ class FlatRunner:
             self._sl = torch.empty((self.queries,), device=dev, dtype=torch.float32)
             nbytes = _flat.workspace_bytes(self.queries, self.keys, c["exact_leaves"], c["sink_leaves"],
                                            c["tile_chunk"], self.tail_rows, self.group, self.order, c["tile"],
-                                           self.curvature)
+                                           self.curvature, self.store)
             self._w = _flat.new_workspace(nbytes, dev)
             kw = dict(exact_leaves=c["exact_leaves"], sink_leaves=c["sink_leaves"], tile_chunk=c["tile_chunk"],
                       scale=c.get("scale"), out=self._so, lse=self._sl, workspace=self._w, group=self.group,
-                      order=self.order, tile=c["tile"], curvature=self.curvature)
+                      order=self.order, tile=c["tile"], curvature=self.curvature, store=self.store)
             self._capturing = True
             try:
                 side = torch.cuda.Stream()

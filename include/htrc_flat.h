@@ -47,6 +47,7 @@ enum { HTRC_ORDER_SEQ = 0, HTRC_ORDER_KMEANS = 1 };
 enum { HTRC_CURV_LIN = 0, HTRC_CURV_ISO = 1 };
 enum { HTRC_ROUND_HALF_EVEN = 0, HTRC_ROUND_HALF_AWAY = 1 };
 enum { HTRC_FQ_INT8 = 1, HTRC_FQ_INT4 = 2, HTRC_FQ_FP8 = 3, HTRC_FQ_FP4 = 4 }; /* htrc_fake_quant formats */
+enum { HTRC_STORE_INT8 = 0, HTRC_STORE_FP8 = 1 };                             /* far-field state format */
 
 /* Device status bits (htrc_flat_status). */
 enum { HTRC_STATUS_WAIT_TIMEOUT = 1, HTRC_STATUS_BAD_INDEX = 2, HTRC_STATUS_NONFINITE = 4 };
@@ -89,6 +90,9 @@ typedef struct HtrcFlatArgs {
                               the isotropic second-order term 0.5/D max(tr, 0) |q - mu|^2 with
                               tr = scale^2 (sum w |k|^2 - |sum w k|^2) per (centre, leaf) -- the torch
                               backend's curvature="iso" (h3/htrc_flat.py:331-333) on the INT8 path */
+  int32_t store;           /* HTRC_STORE_INT8 (store="int8": INT8 state and INT8 query/key codes), or
+                              HTRC_STORE_FP8 (store="fp8", h3/htrc_flat_triton.py FP8=1: e4m3 state codes with
+                              row scales, fp16 far-field dots, bf16 near field; needs HTRC_CURV_LIN) */
 } HtrcFlatArgs;
 
 /* nb rounded up to a multiple of 16: the row pitch of the per-(tile, leaf) scalar arrays. */
@@ -98,8 +102,9 @@ int64_t htrc_leaf_pitch(int64_t nb);
 int htrc_flat_workspace_size(const HtrcFlatArgs* args, size_t* bytes);
 
 /* The whole operator for one head: INT8 key pack, tile centres and query codes, leaf statistics,
- * row-max selection, top-E routing, far field + near field + tail, normalised output and log-Z.
- * Replaces flat_attention(q, k, v, backend="triton", store="int8", dot="bf16", select="max",
+ * row-max selection, top-E routing, far field + near field + tail, normalised output and log-Z
+ * (store HTRC_STORE_FP8: the fp8 stage entry points below instead of the INT8 ones, no key pack).
+ * Replaces flat_attention(q, k, v, backend="triton", store="int8"|"fp8", dot="bf16", select="max",
  * tile=64|32, leaf=64, exact_leaves=E, sink_leaves=S, tail=(tk, tv), order="seq"|"kmeans",
  * kern={"group": G}) of the reference (h3/htrc_flat.py:99-124 -> _flat_triton :181-276), plus the
  * log-Z output the reference lacks. */
@@ -185,6 +190,41 @@ int htrc_tile_attention(const int8_t* q8, const float* sq, const int8_t* dq8, co
  * n_tail <= 16 with bf16 operands; :381-388 float32 for longer tails): tail_part [N, dim + 2]. */
 int htrc_tail_partial(const void* q, int32_t q_dtype, int64_t n_queries, int32_t dim, const float* tail_k,
                       const float* tail_v, int32_t n_tail, float scale, float* tail_part, htrc_stream_t stream);
+
+/* ---- stage entry points of the fp8 state path (HTRC_STORE_FP8) ---- */
+
+/* Tile centres as htrc_tile_prep, with the fp8 path's query operands (h3/htrc_flat_triton.py:103-109):
+ * qb [nt*64, dim] bf16 rows of q and dqh [nt*64, dim] fp16 = fp16(q - mu[tile / G]) (float32 offsets
+ * rounded once). */
+int htrc_tile_prep_fp8(const void* q, int32_t q_dtype, int64_t n_queries, int32_t dim, int32_t tile,
+                       const int32_t* perm, int32_t group, float* mu, uint16_t* mu_hi, uint16_t* mu_lo, uint16_t* qb,
+                       uint16_t* dqh, htrc_stream_t stream);
+
+/* Leaf statistics of centre rows [t0, t0 + tc) with the fp8 state (h3/htrc_flat_triton.py:41-85, FP8=1):
+ * g8 [tc, nb, dim] e4m3 codes of g / sg, sg = max(amax|g| * (1/448), 1e-30); vb8 [tc, nb, dim] e4m3 codes
+ * of vbar / sv with sv likewise; lz, sg, sv [tc, P] f32.  Codes are nearest even, saturated at 448. */
+int htrc_leaf_stats_fp8(const uint16_t* mu_hi, const uint16_t* mu_lo, int64_t nt, int64_t t0, int64_t tc,
+                        const uint16_t* k, const uint16_t* v, int64_t n_keys, int32_t dim, int32_t leaf, float scale,
+                        uint8_t* g8, float* sg, float* lz, uint8_t* vb8, float* sv, int32_t* status,
+                        htrc_stream_t stream);
+
+/* Row-max selection with the fp8 state (h3/htrc_flat_triton.py:214-254, FP8=1):
+ * sel[t, l] = max_r (dqh_r . g_l) * sg_l + lz_l over the tile's 64 rows (fp16 operands, float32 sums);
+ * state row (t - t0) / group as htrc_rowmax_select. */
+int htrc_rowmax_select_fp8(const uint16_t* dqh, int64_t t0, int64_t tc, int32_t group, const uint8_t* g8,
+                           const float* sg, const float* lz, int64_t nb, int32_t dim, float* sel, int32_t* status,
+                           htrc_stream_t stream);
+
+/* Far field + near field (+ tail partial) with the fp8 state (h3/htrc_flat_triton.py:88-211, FP8=1, DOT=1,
+ * merged as :257-273): far logit (dqh . g) * sg + lz with value weight fp16(p * sv) on the vbar codes,
+ * near logit (qb . bf16 k) * scale with weight bf16(p) on v; one float32 softmax per row.  Other arguments
+ * as htrc_tile_attention (k, v: the bf16 keys and values). */
+int htrc_tile_attention_fp8(const uint16_t* qb, const uint16_t* dqh, int64_t n_queries, int32_t tile, int64_t t0,
+                            int64_t tc, int32_t group, const uint8_t* g8, const float* sg, const float* lz,
+                            const uint8_t* vb8, const float* sv, const uint8_t* excl, const int32_t* idx, int32_t kx,
+                            int64_t nb, const uint16_t* k, const uint16_t* v, int64_t n_keys, int32_t dim,
+                            int32_t leaf, float scale, const float* tail_part, const int32_t* perm, float* out,
+                            float* lse, int32_t* status, htrc_stream_t stream);
 
 /* The forward pass for callers that cannot allocate device memory (a plugin host that owns all device
  * allocations and lends only input and output buffers, or an embedding whose device footprint must not

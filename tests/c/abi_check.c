@@ -12,7 +12,7 @@ static int fail(const char* what) {
 
 int main(void) {
   HtrcFlatArgs a;
-  size_t need = 0, need_chunked = 0, need_iso = 0;
+  size_t need = 0, need_chunked = 0, need_iso = 0, need_fp8 = 0;
   memset(&a, 0, sizeof(a));
   a.q_dtype = HTRC_DTYPE_BF16;
   a.n_queries = 129024;
@@ -30,6 +30,13 @@ int main(void) {
   a.tile_chunk = 0;
   a.curvature = HTRC_CURV_ISO;
   if (htrc_flat_workspace_size(&a, &need_iso) != HTRC_OK || need_iso <= need) return fail("iso size");
+  a.store = HTRC_STORE_FP8;
+  if (htrc_flat_workspace_size(&a, &need_iso) != HTRC_ERR_UNSUPPORTED) return fail("fp8 state with iso curvature");
+  a.curvature = HTRC_CURV_LIN;
+  if (htrc_flat_workspace_size(&a, &need_fp8) != HTRC_OK || need_fp8 >= need) return fail("fp8 size");
+  a.store = 5;
+  if (htrc_flat_workspace_size(&a, &need_fp8) != HTRC_ERR_ARG) return fail("bad store");
+  a.store = HTRC_STORE_INT8;
   a.curvature = 7;
   if (htrc_flat_workspace_size(&a, &need) != HTRC_ERR_ARG) return fail("bad curvature");
   a.curvature = HTRC_CURV_LIN;
@@ -42,6 +49,6 @@ int main(void) {
   if (htrc_flat_forward(&a, NULL) != HTRC_ERR_ARG) return fail("forward without pointers");
   if (htrc_leaf_pitch(2016) != 2016 || htrc_leaf_pitch(2017) != 2032) return fail("leaf pitch");
   if (strcmp(htrc_strerror(HTRC_OK), "ok") != 0) return fail("strerror");
-  printf("ok %zu %zu %zu\n", need_chunked, need, need_iso);
+  printf("ok %zu %zu %zu %zu\n", need_chunked, need, need_iso, sizeof(HtrcFlatArgs));
   return 0;
 }

@@ -25,3 +25,6 @@ def test_c_host_compiles_links_and_runs(tmp_path):
     r = subprocess.run([str(exe)], capture_output=True, text=True, env=env, timeout=120)
     assert r.returncode == 0, r.stderr
     assert r.stdout.startswith("ok ")
+    # the ctypes mirror of the argument struct has the C layout's size
+    import ctypes
+    assert int(r.stdout.split()[-1]) == ctypes.sizeof(_lib.HtrcFlatArgs)

@@ -1,0 +1,194 @@
+"""GPU parity of the fp8 state path (store="fp8": e4m3 far-field state with row scales, fp16 far-field
+dots, bf16 near field -- h3/htrc_flat_triton.py FP8=1) against the CPU oracle and against fixtures
+recorded from the reference, through the C ABI's fp8 stage entry points and the whole operator.
+Tolerances: output max-abs 2e-2 and log-Z mean-abs 1e-3 end to end, routing agreement >= 99.9%; the
+e4m3 codes agree with the oracle's except where the device's float32 statistics sit on the other side
+of an e4m3 rounding boundary (then by one step of the code grid)."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+from oracle import flat_oracle as O  # noqa: E402
+
+OUT_TOL = 2e-2
+LSE_TOL = 1e-3
+ROUTE_AGREE = 0.999
+SCALE = 1.0 / math.sqrt(128)
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from htrc_b200 import _lib
+    _lib.lib()
+    return torch.device("cuda:0")
+
+
+def _np(t):
+    return t.detach().float().cpu().numpy() if t.dtype in (torch.bfloat16, torch.float16) else t.detach().cpu().numpy()
+
+
+def _stages(dev, q, k, v, E, sink=0, tail=None, **kw):
+    import htrc_b200
+    from htrc_b200 import _lib
+    tk = tv = None
+    if tail is not None:
+        tk = torch.from_numpy(np.asarray(tail[0], np.float32)).to(dev)
+        tv = torch.from_numpy(np.asarray(tail[1], np.float32)).to(dev)
+    st = htrc_b200.run_stages(torch.from_numpy(q).to(dev), torch.from_numpy(k).to(torch.bfloat16).to(dev),
+                              torch.from_numpy(v).to(torch.bfloat16).to(dev), tk, tv, exact_leaves=E, sink_leaves=sink,
+                              store=_lib.STORE_FP8, **kw)
+    torch.cuda.synchronize()
+    assert int(st["status"].item()) == 0
+    return st
+
+
+def _codes_close(dev_codes, ref_codes):
+    """Codes equal except rarely, and then one step apart on the e4m3 grid."""
+    a = O.e4m3_values(dev_codes).astype(np.float64)
+    b = O.e4m3_values(ref_codes).astype(np.float64)
+    diff = np.abs(a - b)
+    step = np.maximum(np.abs(b), 2.0 ** -6) * 2.0 ** -3
+    assert (diff <= step * 1.0001).all(), float((diff / step).max())
+    assert (dev_codes != ref_codes).mean() < 5e-3
+
+
+def _state_oracle(st, leaf=64):
+    """The device's own fp8 state as oracle arrays."""
+    nb = st["nb"]
+    return (O.e4m3_values(_np(st["g8"])[:, :nb]), _np(st["sg"])[:, :nb], _np(st["lz"])[:, :nb],
+            O.e4m3_values(_np(st["vb8"])[:, :nb]), _np(st["sv"])[:, :nb])
+
+
+@pytest.mark.parametrize("case", ["fp8_state", "fp8_sink_tail"])
+def test_fp8_path_against_reference_fixture(dev, golden_cases, case):
+    z = golden_cases[case]
+    tail = (z["tail_k"], z["tail_v"]) if "tail_k" in z else None
+    E, sink = int(z["exact_leaves"]), int(z["sink_leaves"])
+    st = _stages(dev, z["q"], z["k"], z["v"], E, sink, tail)
+    nb = st["nb"]
+    # tile prep: the centres and the operand rows
+    assert np.allclose(_np(st["mu"]), z["mu"], rtol=0, atol=2e-6)
+    qt, _, _ = O.tile_centres(z["q"], 64)
+    qb, dqh = O.query_codes_fp8(qt, _np(st["mu"]))
+    nt = qt.shape[0]
+    assert np.array_equal(_np(st["qb"]).reshape(nt, 64, 128), qb)
+    assert np.array_equal(_np(st["dqh"]).reshape(nt, 64, 128), dqh)
+    # state
+    _codes_close(_np(st["g8"])[:, :nb], z["g_e4m3"])
+    _codes_close(_np(st["vb8"])[:, :nb], z["vb_e4m3"])
+    assert np.allclose(_np(st["sg"])[:, :nb], z["sg"], rtol=2e-3, atol=0)
+    assert np.allclose(_np(st["sv"])[:, :nb], z["sv"], rtol=2e-3, atol=0)
+    assert np.abs(_np(st["lz"])[:, :nb] - z["lz"]).max() < 2e-4
+    # selection and routing
+    assert np.abs(_np(st["sel"])[:, :nb] - z["sel"]).max() < 1e-2 * max(1.0, np.abs(z["sel"]).max())
+    assert (_np(st["excl"])[:, :nb] == z["excl"]).mean() >= ROUTE_AGREE
+    # output
+    out, lse = _np(st["out"]), _np(st["lse"])
+    assert np.abs(out - z["out"]).max() < OUT_TOL
+    assert np.abs(lse - z["lse"]).mean() < LSE_TOL
+
+
+@pytest.mark.parametrize("case", ["fp8_state", "fp8_sink_tail"])
+def test_fp8_operator_end_to_end(dev, golden_cases, case):
+    """flat_attention(**PROD, store="fp8") against the reference's recorded output."""
+    import htrc_b200
+    z = golden_cases[case]
+    tail = None
+    if "tail_k" in z:
+        tail = (torch.from_numpy(z["tail_k"]).to(dev), torch.from_numpy(z["tail_v"]).to(dev))
+    q = torch.from_numpy(z["q"]).to(dev)
+    k = torch.from_numpy(z["k"]).to(torch.bfloat16).to(dev)
+    v = torch.from_numpy(z["v"]).to(torch.bfloat16).to(dev)
+    cfg = {**htrc_b200.PROD, "leaf": 64, "store": "fp8", "exact_leaves": int(z["exact_leaves"]),
+           "sink_leaves": int(z["sink_leaves"])}
+    out, lse = htrc_b200.flat_attention(q, k, v, tail=tail, return_lse=True, **cfg)
+    torch.cuda.synchronize()
+    assert np.abs(out.cpu().numpy() - z["out"]).max() < OUT_TOL
+    assert np.abs(lse.cpu().numpy() - z["lse"]).mean() < LSE_TOL
+
+
+def _synthetic(n, m, seed):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(n, 128, generator=g) * 2.0
+    k = torch.randn(m, 128, generator=g) * 2.0
+    # smooth structure: nearby tokens share a direction, so leaves carry real far-field mass
+    base = torch.randn(max(1, m // 64), 128, generator=g) * 2.5
+    k += base.repeat_interleave(64, 0)[:m]
+    q += base.repeat_interleave(64, 0)[torch.arange(n) * max(1, m // 64) // n]
+    v = torch.randn(m, 128, generator=g)
+    return q.numpy().astype(np.float32), O.bf16_round(k.numpy()), O.bf16_round(v.numpy())
+
+
+@pytest.mark.parametrize("n,m,E,sink,n_tail", [(4096, 8192, 16, 1, 0),     # 2 far steps + 17 near: 19 steps
+                                               (3000, 32768, 61, 2, 5),    # 8 far blocks, ragged tiles, tail
+                                               (1024, 64 * 130, 0, 0, 0),  # far field only (3 far steps)
+                                               (640, 4096, 64, 0, 0)])     # everything routed: near only
+def test_fp8_tile_kernel_on_device_state(dev, n, m, E, sink, n_tail):
+    """Fed the device's own state and routing, the fp8 tile kernel reproduces the oracle's fp8 tile
+    attention (weights rounded against the row's final maximum) within the fp16-weight rounding, and
+    selection / routing equal the oracle's formulas on that state."""
+    q, k, v = _synthetic(n, m, 100 + n_tail)
+    tail = None
+    if n_tail:
+        g = np.random.default_rng(7)
+        tail = (g.standard_normal((n_tail, 128)).astype(np.float32), g.standard_normal((n_tail, 128)).astype(np.float32))
+    st = _stages(dev, q, k, v, E, sink, tail)
+    nb = st["nb"]
+    qt, _, _ = O.tile_centres(q, 64)
+    nt = qt.shape[0]
+    qb, dqh = _np(st["qb"]).reshape(nt, 64, 128), _np(st["dqh"]).reshape(nt, 64, 128)
+    gq, sg, lz, vq, sv = _state_oracle(st)
+    kx = st["kx"]
+    if 0 < kx < nb:
+        sel = O.rowmax_select_fp8(dqh, gq, sg, lz)
+        sel_d = _np(st["sel"])[:, :nb]
+        assert np.abs(sel_d - sel).max() <= 1e-4 * max(1.0, np.abs(sel).max())
+        idx, excl = O.route(sel_d, E, min(sink, nb))
+        assert np.array_equal(_np(st["excl"])[:, :nb], excl)
+        assert np.array_equal(np.sort(_np(st["idx"])[:, :kx], 1), np.sort(idx, 1))
+    excl_d = _np(st["excl"])[:, :nb]
+    idx_d = _np(st["idx"])[:, :kx] if kx else np.zeros((nt, 0), np.int32)
+    o, l = O.tile_attention_fp8(qt, qb, dqh, gq, sg, lz, vq, sv, excl_d, idx_d, k, v, 64, SCALE, tail=tail)
+    out, lse = _np(st["out"]), _np(st["lse"])
+    assert np.abs(out - o[:n]).max() < 1e-2
+    assert np.abs(lse - l[:n]).max() < 1e-3
+
+
+@pytest.mark.parametrize("over", [{"kern": {"group": 2}}, {"order": "kmeans"}, {"tile": 32},
+                                  {"order": "kmeans", "tile": 32, "kern": {"group": 4}}])
+def test_fp8_modes_against_oracle(dev, over):
+    """Groups, the k-means order and 32-row tiles on the fp8 path, end to end against the oracle run on
+    the same inputs (the k-means permutation is the device's, checked elsewhere against the reference)."""
+    import htrc_b200
+    q, k, v = _synthetic(2048, 16384, 55)
+    cfg = {**htrc_b200.PROD, "leaf": 64, "store": "fp8", "exact_leaves": 24, "sink_leaves": 1, **over}
+    st = htrc_b200.run_stages(torch.from_numpy(q).cuda(), torch.from_numpy(k).to(torch.bfloat16).cuda(),
+                              torch.from_numpy(v).to(torch.bfloat16).cuda(), exact_leaves=24, sink_leaves=1,
+                              store=1, group=htrc_b200.flat.group_of(cfg.get("kern")),
+                              order=htrc_b200.flat.order_code(cfg["order"]), tile=cfg["tile"])
+    torch.cuda.synchronize()
+    perm = _np(st["perm"]) if st["perm"] is not None else None
+    ro, rl, rst = O.flat_attention(q, k, v, exact_leaves=24, sink_leaves=1, tile=cfg["tile"],
+                                   group=htrc_b200.flat.group_of(cfg.get("kern")), order=cfg["order"], perm=perm,
+                                   store="fp8", return_stages=True)
+    nb = st["nb"]
+    assert (_np(st["excl"])[:, :nb] == rst["excl"]).mean() >= ROUTE_AGREE
+    out, lse = htrc_b200.flat_attention(torch.from_numpy(q).cuda(), torch.from_numpy(k).to(torch.bfloat16).cuda(),
+                                        torch.from_numpy(v).to(torch.bfloat16).cuda(), return_lse=True, **cfg)
+    torch.cuda.synchronize()
+    # caller rows whose group's routing agrees (tile-order row i: tile i // T, state row tile // G)
+    agree = (_np(st["excl"])[:, :nb] == rst["excl"]).all(1)
+    i = np.arange(q.shape[0])
+    same = agree[(i // cfg["tile"]) // htrc_b200.flat.group_of(cfg.get("kern"))]
+    o = out.cpu().numpy()
+    rows = i if perm is None else perm.astype(np.int64)
+    ok_rows = rows[same]
+    assert np.abs(o[ok_rows] - ro[ok_rows]).max() < OUT_TOL
+    assert np.abs(lse.cpu().numpy() - rl).mean() < LSE_TOL
+    assert np.array_equal(o, _np(st["out"]))            # the fused forward and the stage launches agree

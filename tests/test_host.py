@@ -144,6 +144,38 @@ def test_flat_attention_unimplemented_configurations_say_so():
         htrc_b200.flat_attention(q, k, v, **{**cfg, "backend": "torch"})
 
 
+def test_fp8_state_option_is_accepted_and_checked():
+    """store='fp8' (the reference's e4m3 far-field state) passes the argument checks and then needs CUDA
+    tensors like every other path; the iso curvature is refused on it; its workspace drops the INT8 key
+    codes and halves the vbar state."""
+    q, k, v = _qkv()
+    cfg = dict(htrc_b200.PROD, leaf=64, store="fp8")
+    for over in ({}, {"order": "kmeans"}, {"kern": {"group": 2}}, {"tile": 32}, {"sink_leaves": 1},
+                 {"quant": {"kv": "int4", "q": "int8", "group": 32}}):
+        with pytest.raises(ValueError, match="CUDA tensors"):
+            htrc_b200.flat_attention(q, k, v, **{**cfg, **over})
+    with pytest.raises(ValueError, match="store='fp8'"):
+        htrc_b200.flat_attention(q, k, v, **{**cfg, "quant": {"state": "int8"}})
+    with pytest.raises(NotImplementedError, match="iso"):
+        htrc_b200.flat_attention(q, k, v, **{**cfg, "backend": "cuda", "curvature": "iso"})
+    from htrc_b200 import flat as F
+    n = m = 16384
+    i8 = F.workspace_bytes(n, m, 256, store=_lib.STORE_INT8)
+    f8 = F.workspace_bytes(n, m, 256, store=_lib.STORE_FP8)
+    nt, nb = n // 64, m // 64
+    # no k8/ks (m * 132), bf16 + fp16 query rows instead of two code rows and two scales (+ 512 - 264 bytes per
+    # held row), vbar codes instead of bf16 (- nt*nb*128), plus sv (nt * pitch * 4); alignment slack
+    want = i8 - m * 132 + nt * 64 * (512 - 264) - nt * nb * 128 + nt * F.leaf_pitch(nb) * 4
+    assert abs(f8 - want) <= 8 * 256
+    a = _lib.HtrcFlatArgs()
+    a.n_queries, a.n_keys, a.dim, a.tile, a.leaf, a.exact_leaves = n, m, 128, 64, 64, 256
+    a.store, a.curvature = _lib.STORE_FP8, _lib.CURV_ISO
+    nbytes = ctypes.c_size_t()
+    assert _lib.lib().htrc_flat_workspace_size(ctypes.byref(a), ctypes.byref(nbytes)) == _lib.HTRC_ERR_UNSUPPORTED
+    a.store = 3
+    assert _lib.lib().htrc_flat_workspace_size(ctypes.byref(a), ctypes.byref(nbytes)) == _lib.HTRC_ERR_ARG
+
+
 def test_orders_and_groups_need_no_cpu_path_either():
     q, k, v = _qkv()
     cfg = dict(htrc_b200.PROD, leaf=64)
