@@ -416,8 +416,8 @@ def run_ours(a, wl, rank, world, local_rank):
         from htrc_b200 import runner as R
         h0 = my_heads[0]
         modes = {}
-        for mode in list(R.MODES) + ["fast+iso"]:
-            extra = dict(backend="cuda", curvature="iso") if mode == "fast+iso" else {}
+        for mode in list(R.MODES) + ["fast+iso", "fast+fp8"]:
+            extra = {"fast+iso": dict(backend="cuda", curvature="iso"), "fast+fp8": dict(store="fp8")}.get(mode, {})
             r = R.FlatRunner(n, m, mode=mode.split("+")[0], device=dev, **extra)
             if r.graph is None:
                 modes[mode] = f"graph capture failed: {r.graph_error}"
@@ -457,7 +457,8 @@ def run_ours(a, wl, rank, world, local_rank):
         modes = {"ms_per_head": modes, "kmeans_order_ms": k0.elapsed_time(k1) / 5,
                  "note": "head 0 of the workload through FlatRunner (CUDA graph) per mode of "
                          "h3/htrc_flat_runner.py:48-53: fast E=256, balanced E=512, accurate E=1024 + k-means, "
-                         "max E=1024 + k-means + 32-row tiles; fast+iso: fast with the isotropic curvature term"}
+                         "max E=1024 + k-means + 32-row tiles; fast+iso: fast with the isotropic curvature term; "
+                         "fast+fp8: fast with the e4m3 far-field state (store='fp8')"}
 
     # ---- roofline of the dominant kernel (tile attention) from the live events
     peaks, peak_src = measured_peaks()

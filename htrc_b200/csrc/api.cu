@@ -142,7 +142,7 @@ struct Layout {
   bool iso = false;
   size_t kn2 = 0, dd = 0, cv = 0;           // iso curvature: key norms, row offsets, coefficients
   bool fp8 = false;                         // fp8 state: q8 / dq8 hold bf16 / fp16 rows, vb the vbar codes
-  size_t sv = 0;
+  size_t sv = 0, fpart = 0;
 };
 
 constexpr int kMaxGroup = 65536;
@@ -217,7 +217,10 @@ Layout layout_of(const HtrcFlatArgs* a) {
   L.tail = a->n_tail > 0 ? take(static_cast<size_t>(L.n) * 130 * 4) : 0;
   L.g8 = take(static_cast<size_t>(gcm_rows) * L.nb * 128);
   L.vb = take(static_cast<size_t>(gcm_rows) * L.nb * (L.fp8 ? 128 : 256));
-  if (L.fp8) L.sv = take(static_cast<size_t>(gcm_rows) * L.pitch * 4);
+  if (L.fp8) {
+    L.sv = take(static_cast<size_t>(gcm_rows) * L.pitch * 4);
+    if (L.kx < L.nb) L.fpart = take(static_cast<size_t>(L.n) * 130 * 4);   // far-field partial rows
+  }
   L.sg = take(static_cast<size_t>(gcm_rows) * L.pitch * 4);
   L.lz = take(static_cast<size_t>(gcm_rows) * L.pitch * 4);
   L.sel = take(static_cast<size_t>(L.tcm) * L.pitch * 4);
@@ -412,8 +415,9 @@ int htrc_flat_forward(const HtrcFlatArgs* a, htrc_stream_t stream) {
                               L.nt * 64, reinterpret_cast<const uint8_t*>(g8), reinterpret_cast<const uint8_t*>(vb), lz,
                               sg, sv, excl, gc, L.nb, L.pitch, a->k, a->v, L.m)) != HTRC_OK)
         return rc;
-      if ((rc = launch_tile_fp8(tmp, idx, kx, nb, L.n, trows, t0, tc, group, scale, tail, perm, a->out, a->lse, status,
-                                st)) != HTRC_OK)
+      float* fpart = L.fpart ? at<float>(ws, L.fpart) : nullptr;
+      if ((rc = launch_tile_fp8(tmp, idx, kx, nb, L.n, trows, t0, tc, group, scale, tail, perm, fpart, a->out, a->lse,
+                                status, st)) != HTRC_OK)
         return rc;
       mark(5 + 4 * chunk);
       continue;
@@ -555,15 +559,15 @@ int htrc_tile_attention_fp8(const uint16_t* qb, const uint16_t* dqh, int64_t n_q
                             int64_t tc, int32_t group, const uint8_t* g8, const float* sg, const float* lz,
                             const uint8_t* vb8, const float* sv, const uint8_t* excl, const int32_t* idx, int32_t kx,
                             int64_t nb, const uint16_t* k, const uint16_t* v, int64_t n_keys, int32_t dim,
-                            int32_t leaf, float scale, const float* tail_part, const int32_t* perm, float* out,
-                            float* lse, int32_t* status, htrc_stream_t stream) {
+                            int32_t leaf, float scale, const float* tail_part, const int32_t* perm,
+                            float* far_part, float* out, float* lse, int32_t* status, htrc_stream_t stream) {
   if (!qb || !dqh || !k || !v || !out || n_queries < 1 || t0 < 0 || tc < 1) return HTRC_ERR_ARG;
   const int64_t g = group > 1 ? group : 1;
   if (g > kMaxGroup || t0 % g) return HTRC_ERR_ARG;
   if (dim != kDim || leaf != kLeaf || (tile != kTile && tile != kTile / 2)) return HTRC_ERR_UNSUPPORTED;
   if (nb < 1 || n_keys != nb * leaf || kx < 0 || kx > nb) return HTRC_ERR_ARG;
   if (kx > kMaxRouted || nb > kMaxLeaves) return HTRC_ERR_UNSUPPORTED;
-  if (kx < nb && (!g8 || !sg || !lz || !vb8 || !sv || !excl)) return HTRC_ERR_ARG;
+  if (kx < nb && (!g8 || !sg || !lz || !vb8 || !sv || !excl || !far_part)) return HTRC_ERR_ARG;
   if (kx > 0 && !idx) return HTRC_ERR_ARG;
   const int64_t nt = (n_queries + tile - 1) / tile;
   if (t0 + tc > nt) return HTRC_ERR_ARG;
@@ -579,7 +583,8 @@ int htrc_tile_attention_fp8(const uint16_t* qb, const uint16_t* dqh, int64_t n_q
                           n_keys)) != HTRC_OK)
     return rc;
   return launch_tile_fp8(mp, idx, kx, static_cast<int>(nb), n_queries, tile, t0, tc, static_cast<int>(g),
-                         scale_of(scale), tail_part, perm, out, lse, status, reinterpret_cast<cudaStream_t>(stream));
+                         scale_of(scale), tail_part, perm, far_part, out, lse, status,
+                         reinterpret_cast<cudaStream_t>(stream));
 }
 
 int htrc_rowmax_select(const int8_t* dq8, const float* sdq, const float* dd, int64_t t0, int64_t tc, int32_t group,

@@ -4,7 +4,8 @@
 // The far-field state is e4m3 codes with per-(centre, leaf) row scales: g codes with sg, vbar codes with sv
 // (written by the leaf-statistics kernel).  e4m3 values are exact in fp16, so the kernels stage the codes
 // by TMA, convert them on chip into fp16 operands in the 128-byte-swizzled UMMA layout (one cvt per pair
-// of codes) and run kind::f16 MMAs with float32 accumulation:
+// of codes; measured faster here than placing the code bits into fp16 position with integer ops) and run
+// kind::f16 MMAs with float32 accumulation:
 //   selection (:214-254):  SEL[t, l] = max_r (fp16(q_r - mu) . g_l) * sg_l + lz_l
 //   far field (:118-160):  logit = (fp16(q_r - mu) . g_l) * sg_l + lz_l, value weight fp16(p * sv_l) on g's
 //                          vbar codes (the normaliser sums p, not p * sv)
@@ -49,14 +50,15 @@ __device__ __forceinline__ void codes_to_f16(const uint8_t* raw, uint32_t dst, i
 // Groups of G tiles read state row t / G (the routing kernel takes the maximum over the group's rows).
 namespace {
 namespace rmx {
-constexpr int kStages = 2;
+constexpr int kStages = 6;                              // raw code stages: the HBM stream in flight
+constexpr int kOpStages = 2;                            // converted fp16 blocks
 constexpr uint32_t kRawBytes = 128 * 128;               // 128 leaves x 128 codes
 constexpr uint32_t kRawStage = kRawBytes + 1024;        // + sg[128], lz[128]
 constexpr uint32_t kOpBytes = 2 * 128 * 128;            // fp16 g block: 2 halves x 128 rows x 128 B
 constexpr uint32_t kOffDq = 0;                          // fp16 offsets of the tile: 2 halves x 64 rows x 128 B
 constexpr uint32_t kOffRaw = 16384;
 constexpr uint32_t kOffOp = kOffRaw + kStages * kRawStage;
-constexpr uint32_t kOffBar = kOffOp + kStages * kOpBytes;
+constexpr uint32_t kOffBar = kOffOp + kOpStages * kOpBytes;
 constexpr uint32_t kSmemBytes = kOffBar + 256 + 1024;
 constexpr uint32_t kTmemCols = 128;
 static_assert(kOffOp % 1024 == 0, "swizzled operands need 1024-byte alignment");
@@ -65,8 +67,8 @@ struct Bars {
   uint64_t dq_full;
   uint64_t raw_full[kStages];    // TMA: codes, sg, lz
   uint64_t raw_empty[kStages];   // the 128 converting threads read them
-  uint64_t op_full[kStages];     // the 128 converting threads wrote the fp16 block
-  uint64_t op_empty[kStages];    // MMA commit
+  uint64_t op_full[kOpStages];   // the 128 converting threads wrote the fp16 block
+  uint64_t op_empty[kOpStages];  // MMA commit
   uint64_t acc_full[2];
   uint64_t acc_empty[2];         // the 128 reducing threads drained the accumulator
   uint32_t tmem_base;
@@ -95,6 +97,8 @@ __global__ void __launch_bounds__(192)
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&bars->raw_full[s], 1);
       mbar_init(&bars->raw_empty[s], 128);
+    }
+    for (int s = 0; s < kOpStages; ++s) {
       mbar_init(&bars->op_full[s], 128);
       mbar_init(&bars->op_empty[s], 1);
     }
@@ -132,11 +136,11 @@ __global__ void __launch_bounds__(192)
       const uint32_t dq = smem_u32(smem + kOffDq);
       bool ok = mbar_wait(&bars->dq_full, 0, status, abort_flag);
       for (int j = 0; ok && j < nblk; ++j) {
-        const int s = j % kStages, b = j & 1;
-        if (!mbar_wait(&bars->op_full[s], (j / kStages) & 1, status, abort_flag)) break;
+        const int s = j % kOpStages, b = j & 1;
+        if (!mbar_wait(&bars->op_full[s], (j / kOpStages) & 1, status, abort_flag)) break;
         if (j >= 2 && !mbar_wait(&bars->acc_empty[b], ((j >> 1) - 1) & 1, status, abort_flag)) break;
         tc_fence_after();
-        const uint32_t op = smem_u32(smem + kOffOp + s * kOpBytes);
+        const uint32_t op = smem_u32(smem + kOffOp + s * kOpBytes);   // s: the op stage
 #pragma unroll
         for (int h = 0; h < 2; ++h)
 #pragma unroll
@@ -157,15 +161,16 @@ __global__ void __launch_bounds__(192)
     for (int j = 0; j <= nblk; ++j) {
       float sg_cur = 0.f, lz_cur = 0.f;
       if (j < nblk) {
-        const int s = j % kStages;
+        const int s = j % kStages, o = j % kOpStages;
         if (!mbar_wait_warp(&bars->raw_full[s], (j / kStages) & 1, status, abort_flag)) break;
-        if (j >= kStages && !mbar_wait_warp(&bars->op_empty[s], ((j / kStages) - 1) & 1, status, abort_flag)) break;
+        if (j >= kOpStages && !mbar_wait_warp(&bars->op_empty[o], ((j / kOpStages) - 1) & 1, status, abort_flag))
+          break;
         const uint8_t* st = smem + kOffRaw + s * kRawStage;
-        codes_to_f16<128, 128>(st, smem_u32(smem + kOffOp + s * kOpBytes), tid);
+        codes_to_f16<128, 128>(st, smem_u32(smem + kOffOp + o * kOpBytes), tid);
         sg_cur = reinterpret_cast<const float*>(st + kRawBytes)[r];
         lz_cur = reinterpret_cast<const float*>(st + kRawBytes + 512)[r];
         fence_proxy_async_smem();
-        mbar_arrive(&bars->op_full[s]);
+        mbar_arrive(&bars->op_full[o]);
         mbar_arrive(&bars->raw_empty[s]);
       }
       if (j >= 1) {
@@ -221,61 +226,69 @@ int launch_rowmax_fp8(const RowmaxFp8Maps& maps, float* sel, int64_t pitch, int6
 }
 
 // ================================================================================================
-// Tile attention.  One CTA per 64-row tile; steps of 64 columns as in the INT8 kernel (far blocks of 64
-// leaves of the tile's state, then one routed 64-token leaf per step), taken in pairs: the MMAs of steps
-// 2p and 2p + 1 are M=64 each, step 2p in TMEM lanes {0..15} + 32k and step 2p + 1 at lane offset 16, so
-// every softmax thread owns one (query row, step parity) of S, P and O and all 128 threads of a
-// warpgroup work on every pair.  Two warpgroups take alternate pairs, each with its own O accumulator
-// (two per row: one per step parity) and running (max, sum); the four partials of a row and its tail
-// partial are merged in the epilogue.  The running maximum is updated lazily (rescale when it grew by
-// more than 2^8), as in the INT8 kernel.
+// Tile attention, in two passes over the tiles of a chunk that share one kernel body:
+//   FAR:  the far field alone (blocks of 64 leaves of the tile's state, fp16 from the codes), written as one
+//         partial (acc[128], m, l) per query row, like the tail partial;
+//   NEAR: the routed leaves (bf16 keys and values, by TMA), merged in the epilogue with the far partial and
+//         the tail partial into the normalised output and log-Z.
+// Splitting keeps each pass's shared memory for its own rings: FAR stages the codes four steps ahead and
+// converts them, NEAR holds three pairs of keys and of values in flight.  The merge is the exact
+// (max, sum) combination the reference applies to its splits (:257-273).
 //
-// Operands (16 KB each, fp16 / bf16 in two 128-byte-swizzled halves): the tile's bf16 rows and fp16
-// offsets (loaded once), per step an X operand (far: g converted from codes; near: the keys of the
-// routed leaf, by TMA) and a Y operand (far: vbar converted from codes; near: the leaf's values, by TMA).
-// X and Y rings hold two pairs each; the codes land in two-slot raw rings and two converter warps per
-// ring turn them into fp16.
+// Within a pass: one CTA per 64-row tile; steps of 64 columns taken in pairs: the MMAs of steps 2p and
+// 2p + 1 are M=64 each, step 2p in TMEM lanes {0..15} + 32k and step 2p + 1 at lane offset 16, so every
+// softmax thread owns one (query row, step parity) of S, P and O and all 128 threads of a warpgroup work
+// on every pair.  Two warpgroups take alternate pairs, each with its own O accumulator (two per row: one
+// per step parity) and running (max, sum); the lazy maximum is rescaled only when it grew by more than 2^8.
+// The FAR pass pads its steps to an even count (the extra block lies past nb and is masked).
 //
-// Warp roles (512 threads, warpgroup-aligned for setmaxnreg): warp 0 X producer (tile rows, far
-// parameters and raw g codes, near keys); warp 1 PV issuer (+ TMEM owner); warp 2 QK issuer and Y
-// producer (raw vbar codes, near values); warp 3 per-column constants; warps 4-7 and 8-11 the two
-// softmax warpgroups; warps 12-13 convert g codes, warps 14-15 vbar codes.
+// Warp roles.  Both passes: warp 0 X producer (tile rows; FAR: block parameters and raw g codes, NEAR:
+// routed keys), warp 1 PV issuer (+ TMEM owner), warp 2 QK issuer, warps 4-7 and 8-11 the softmax
+// warpgroups.  FAR: warp 3 per-column constants, warps 12-13 convert g codes, warps 14-15 load and convert
+// vbar codes (512 threads, warpgroup-aligned setmaxnreg).  NEAR: warp 3 loads the routed values (384
+// threads).
 namespace {
 namespace tfx {
-constexpr int kThreads = 512;
 constexpr uint32_t kOpBytes = 16384;                     // 2 halves x 64 rows x 128 B
-constexpr uint32_t kParBytes = 1024;                     // far: lz[64], sg[64], sv[64], excl[64]
-constexpr uint32_t kXSub = kOpBytes + kParBytes;
 constexpr uint32_t kRawBytes = 64 * 128;                 // 64 leaves x 128 codes
-constexpr uint32_t kOffQb = 0;
-constexpr uint32_t kOffDqh = kOpBytes;
-constexpr uint32_t kOffX = 2 * kOpBytes;                 // [pair slot][step parity] x kXSub
-constexpr uint32_t kOffY = kOffX + 4 * kXSub;            // [pair slot][step parity] x kOpBytes
-constexpr uint32_t kOffRawG = kOffY + 4 * kOpBytes;      // [step parity] x kRawBytes
-constexpr uint32_t kOffRawV = kOffRawG + 2 * kRawBytes;
-constexpr uint32_t kOffCC = kOffRawV + 2 * kRawBytes;    // [pair slot][parity][64] float2 (c1, c2)
-constexpr uint32_t kOffCS = kOffCC + 4 * 64 * 8;         // [pair slot][parity][64] sv (far weights)
-constexpr uint32_t kOffEpi = kOffCS + 4 * 64 * 4;        // m, l of warpgroup 1 [parity][64] each
-constexpr uint32_t kOffIdx = kOffEpi + 2 * 128 * 4;      // [kMaxKx] uint16
 constexpr int kMaxKx = 1024;
-constexpr uint32_t kOffBar = kOffIdx + kMaxKx * 2;
-constexpr uint32_t kSmemBytes = kOffBar + 512 + 1024;
-constexpr uint32_t kTmemCols = 512;
+constexpr float kRescale = 8.0f;
 constexpr uint32_t kColS = 0;       // S/P buffer b (= pair % 4) at 64 b; P uses its first 32 columns
 constexpr uint32_t kColO = 256;     // O[g] at 256 + 128 g (step parity by lane offset 0 / 16)
-constexpr float kRescale = 8.0f;
-static_assert(kOffX % 1024 == 0 && kXSub % 1024 == 0 && kOffY % 1024 == 0, "swizzled operands need 1024-byte alignment");
-static_assert(kSmemBytes <= 232448, "shared memory per CTA");
+constexpr uint32_t kTmemCols = 512;
+
+template <bool FAR>
+struct Cfg {
+  static constexpr int kThreads = FAR ? 512 : 384;
+  static constexpr int kXP = FAR ? 2 : 3;                // X ring: pairs
+  static constexpr int kYP = FAR ? 2 : 3;                // Y ring: pairs
+  static constexpr int kRG = FAR ? 4 : 0;                // raw g code slots (steps)
+  static constexpr int kRV = FAR ? 4 : 0;                // raw vbar code slots (steps)
+  static constexpr uint32_t kXSub = kOpBytes + (FAR ? 1024 : 0);   // far: + lz[64], sg[64], sv[64], excl[64]
+  static constexpr uint32_t kOffQ = 0;                   // FAR: fp16 offsets; NEAR: bf16 rows
+  static constexpr uint32_t kOffX = kOpBytes;            // [pair slot][step parity] x kXSub
+  static constexpr uint32_t kOffY = kOffX + 2 * kXP * kXSub;
+  static constexpr uint32_t kOffRawG = kOffY + 2 * kYP * kOpBytes;
+  static constexpr uint32_t kOffRawV = kOffRawG + kRG * kRawBytes;
+  static constexpr uint32_t kOffCC = kOffRawV + kRV * kRawBytes;   // FAR: [warpgroup][parity][64] float2
+  static constexpr uint32_t kOffCS = kOffCC + (FAR ? 4 * 64 * 8 : 0);   // FAR: sv
+  static constexpr uint32_t kOffEpi = kOffCS + (FAR ? 4 * 64 * 4 : 0);  // m, l of warpgroup 1
+  static constexpr uint32_t kOffIdx = kOffEpi + 2 * 128 * 4;           // NEAR: [kMaxKx] uint16
+  static constexpr uint32_t kOffBar = kOffIdx + (FAR ? 0 : kMaxKx * 2);
+  static constexpr uint32_t kSmemBytes = kOffBar + 512 + 1024;
+  static_assert(kOffX % 1024 == 0 && kXSub % 1024 == 0 && kOffY % 1024 == 0, "swizzled operands: 1024-byte alignment");
+  static_assert(kSmemBytes <= 232448, "shared memory per CTA");
+};
 
 struct Bars {
   uint64_t qd_full;
-  uint64_t x_full[2];     // X producer (arrive + bytes) + 64 g converter threads
-  uint64_t x_empty[2];    // QK commit + 32 constant lanes
-  uint64_t y_full[2];     // Y producer (arrive + bytes) + 64 vbar converter threads
-  uint64_t rg_full[2];
-  uint64_t rg_empty[2];   // 64 g converter threads
-  uint64_t rv_full[2];
-  uint64_t rv_empty[2];   // 64 vbar converter threads
+  uint64_t x_full[3];     // X producer (arrive + bytes) [+ 64 g converter threads]
+  uint64_t x_empty[3];    // QK commit [+ 32 constant lanes]
+  uint64_t y_full[3];     // NEAR: Y producer (arrive + bytes); FAR: 64 vbar converter threads
+  uint64_t rg_full[4];
+  uint64_t rg_empty[4];   // 64 g converter threads
+  uint64_t rv_full[4];
+  uint64_t rv_empty[4];   // 64 vbar converter threads
   uint64_t cc_full[2];    // 32 constant lanes
   uint64_t cc_empty[2];   // 128 softmax threads of the pair's warpgroup
   uint64_t s_full[4];     // QK of the pair done
@@ -285,68 +298,53 @@ struct Bars {
   uint32_t tmem_base;
   int abort_flag;
 };
-
-// P of one step from its 64 log2-unit logits: far steps weight p by sv and round to fp16, near steps round
-// p to bf16 (KIND 0 near, 1 far, 2 per-lane choice); returns the float32 sum of p
-template <int KIND>
-__device__ __forceinline__ float make_p(const float (&lg)[64], const float* sv, float mref, bool live, bool far,
-                                        uint32_t (&pw)[32]) {
-  const float2 mref2 = make_float2(mref, mref);
-  float2 rs2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-#pragma unroll
-  for (int i = 0; i < 64; i += 2) {
-    const float2 e = sub2(make_float2(lg[i], lg[i + 1]), mref2);
-    const float2 p = live ? make_float2(ex2(e.x), ex2(e.y)) : make_float2(0.f, 0.f);
-    rs2[(i >> 1) & 3] = add2(rs2[(i >> 1) & 3], p);
-    if (KIND == 0) {
-      pw[i >> 1] = pack_bf16x2(p.x, p.y);
-    } else {
-      const float2 w = mul2(p, *reinterpret_cast<const float2*>(sv + i));
-      const uint32_t h = pack_f16x2(w.x, w.y);
-      pw[i >> 1] = KIND == 1 ? h : (far ? h : pack_bf16x2(p.x, p.y));
-    }
-  }
-  const float2 rsa = add2(add2(rs2[0], rs2[1]), add2(rs2[2], rs2[3]));
-  return rsa.x + rsa.y;
-}
+static_assert(sizeof(Bars) <= 512, "barrier block");
 }  // namespace tfx
 }  // namespace
 
-template <int TROWS>
-__global__ void __launch_bounds__(tfx::kThreads, 1)
-    tile_fp8_kernel(const __grid_constant__ CUtensorMap tm_qb, const __grid_constant__ CUtensorMap tm_dqh,
-                    const __grid_constant__ CUtensorMap tm_graw, const __grid_constant__ CUtensorMap tm_vraw,
-                    const __grid_constant__ CUtensorMap tm_lz, const __grid_constant__ CUtensorMap tm_sg,
-                    const __grid_constant__ CUtensorMap tm_sv, const __grid_constant__ CUtensorMap tm_excl,
-                    const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
-                    const int32_t* __restrict__ idx, int kx, int nb, int nf, int64_t n, int64_t t0, int group,
-                    float scale, const float* __restrict__ tail_part, const int32_t* __restrict__ perm,
-                    float* __restrict__ out, float* __restrict__ lse, int* status) {
+template <int TROWS, bool FAR>
+__global__ void __launch_bounds__(tfx::Cfg<FAR>::kThreads, 1)
+    tile_fp8_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_graw,
+                    const __grid_constant__ CUtensorMap tm_vraw, const __grid_constant__ CUtensorMap tm_lz,
+                    const __grid_constant__ CUtensorMap tm_sg, const __grid_constant__ CUtensorMap tm_sv,
+                    const __grid_constant__ CUtensorMap tm_excl, const __grid_constant__ CUtensorMap tm_k,
+                    const __grid_constant__ CUtensorMap tm_v, const int32_t* __restrict__ idx, int kx, int nb,
+                    int64_t n, int64_t t0, int group, float scale, const float* __restrict__ tail_part,
+                    const int32_t* __restrict__ perm, float* __restrict__ far_part, float* __restrict__ out,
+                    float* __restrict__ lse, int* status) {
   using namespace tfx;
+  using C = Cfg<FAR>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  Bars* bars = reinterpret_cast<Bars*>(smem + kOffBar);
-  uint16_t* idx_s = reinterpret_cast<uint16_t*>(smem + kOffIdx);
-  float2* cc = reinterpret_cast<float2*>(smem + kOffCC);
-  float* cs = reinterpret_cast<float*>(smem + kOffCS);
-  float* epi = reinterpret_cast<float*>(smem + kOffEpi);
+  Bars* bars = reinterpret_cast<Bars*>(smem + C::kOffBar);
+  uint16_t* idx_s = reinterpret_cast<uint16_t*>(smem + C::kOffIdx);
+  float2* cc = reinterpret_cast<float2*>(smem + C::kOffCC);
+  float* cs = reinterpret_cast<float*>(smem + C::kOffCS);
+  float* epi = reinterpret_cast<float*>(smem + C::kOffEpi);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tloc = blockIdx.x;
   const int srow = tloc / group;            // state row of this tile
-  const int total = nf + kx;                // far steps + near steps
+  // FAR: blocks of 64 leaves, padded to an even count; NEAR: the routed leaves
+  const int total = FAR ? ((nb + 127) / 128) * 2 : kx;
   const int np = (total + 1) / 2;           // pairs of steps
   volatile int* abort_flag = &bars->abort_flag;
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->qd_full, 1);
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&bars->x_full[s], 1 + 64);
-      mbar_init(&bars->x_empty[s], 1 + 32);
-      mbar_init(&bars->y_full[s], 1 + 64);
+    for (int s = 0; s < C::kXP; ++s) {
+      mbar_init(&bars->x_full[s], FAR ? 1 + 64 : 1);
+      mbar_init(&bars->x_empty[s], FAR ? 1 + 32 : 1);
+    }
+    for (int s = 0; s < C::kYP; ++s) mbar_init(&bars->y_full[s], FAR ? 64 : 1);
+    for (int s = 0; s < C::kRG; ++s) {
       mbar_init(&bars->rg_full[s], 1);
       mbar_init(&bars->rg_empty[s], 64);
+    }
+    for (int s = 0; s < C::kRV; ++s) {
       mbar_init(&bars->rv_full[s], 1);
       mbar_init(&bars->rv_empty[s], 64);
+    }
+    for (int s = 0; s < 2; ++s) {
       mbar_init(&bars->cc_full[s], 32);
       mbar_init(&bars->cc_empty[s], 128);
     }
@@ -359,7 +357,7 @@ __global__ void __launch_bounds__(tfx::kThreads, 1)
     bars->abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 0) {
+  if (!FAR && warp == 0) {
     // routed leaves of the tile's state row -> shared memory, range-checked
     const int32_t* src = idx + static_cast<int64_t>(srow) * kx;
     for (int e = lane; e < kx; e += 32) {
@@ -376,50 +374,55 @@ __global__ void __launch_bounds__(tfx::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
+  auto xsub = [&](int p, int x) { return smem + C::kOffX + ((p % C::kXP) * 2 + x) * C::kXSub; };
+  auto ysub = [&](int p, int x) { return smem + C::kOffY + ((p % C::kYP) * 2 + x) * kOpBytes; };
 
   if (warp < 4) {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 64;");
+    if constexpr (FAR) asm volatile("setmaxnreg.dec.sync.aligned.u32 64;");
     const uint32_t leader = elect_one();
     if (warp == 0) {
       // ---------------------------------------------------------------- X producer
       const uint64_t pol_stream = policy_evict_first();
       const uint64_t pol_keep = policy_evict_last();
       if (leader) {
-        const int row = static_cast<int>((t0 + tloc) * 64);
-        mbar_arrive_expect_tx(&bars->qd_full, 2 * kOpBytes);
-        tma_load_3d(smem + kOffQb, &tm_qb, &bars->qd_full, 0, row, 0, pol_stream);
-        tma_load_3d(smem + kOffDqh, &tm_dqh, &bars->qd_full, 0, row, 0, pol_stream);
+        mbar_arrive_expect_tx(&bars->qd_full, kOpBytes);
+        tma_load_3d(smem + C::kOffQ, &tm_q, &bars->qd_full, 0, static_cast<int>((t0 + tloc) * 64), 0, pol_stream);
       }
+      int jr = 0;                               // FAR: next block whose raw g codes are to be loaded
       for (int p = 0; p < np; ++p) {
-        const int ps = p & 1;
-        if (p >= 2 && !mbar_wait_warp(&bars->x_empty[ps], ((p >> 1) - 1) & 1, status, abort_flag)) break;
-        bool ok = true;
-        for (int x = 0; x < 2 && ok; ++x) {     // raw g slots of the pair's far steps (slot = step parity)
-          const int j = 2 * p + x;
-          if (j < total && j < nf && j >= 2)
-            ok = mbar_wait_warp(&bars->rg_empty[x], ((j >> 1) - 1) & 1, status, abort_flag);
+        if constexpr (FAR) {
+          // raw g codes up to kRG blocks ahead of this pair (slot j % kRG, freed by the g converters)
+          bool ok = true;
+          for (; ok && jr < total && jr < 2 * p + C::kRG; ++jr) {
+            const int rs = jr % C::kRG;
+            if (jr >= C::kRG) ok = mbar_wait_warp(&bars->rg_empty[rs], ((jr / C::kRG) - 1) & 1, status, abort_flag);
+            if (ok && leader) {
+              mbar_arrive_expect_tx(&bars->rg_full[rs], kRawBytes);
+              tma_load_3d(smem + C::kOffRawG + rs * kRawBytes, &tm_graw, &bars->rg_full[rs], 0, jr * 64, srow,
+                          pol_stream);
+            }
+            __syncwarp();
+          }
+          if (!ok) break;
         }
-        if (!ok) break;
+        const int xs = p % C::kXP;
+        if (p >= C::kXP && !mbar_wait_warp(&bars->x_empty[xs], ((p / C::kXP) - 1) & 1, status, abort_flag)) break;
         if (leader) {
           uint32_t tx = 0;
-          for (int x = 0; x < 2; ++x) {
-            const int j = 2 * p + x;
-            if (j < total) tx += j < nf ? 3 * 256 + 64 : kOpBytes;
-          }
-          mbar_arrive_expect_tx(&bars->x_full[ps], tx);
+          for (int x = 0; x < 2; ++x)
+            if (2 * p + x < total) tx += FAR ? 3 * 256 + 64 : kOpBytes;
+          mbar_arrive_expect_tx(&bars->x_full[xs], tx);
           for (int x = 0; x < 2; ++x) {
             const int j = 2 * p + x;
             if (j >= total) continue;
-            uint8_t* xs = smem + kOffX + (ps * 2 + x) * kXSub;
-            if (j < nf) {
-              mbar_arrive_expect_tx(&bars->rg_full[x], kRawBytes);
-              tma_load_3d(smem + kOffRawG + x * kRawBytes, &tm_graw, &bars->rg_full[x], 0, j * 64, srow, pol_stream);
-              tma_load_2d(xs + kOpBytes, &tm_lz, &bars->x_full[ps], j * 64, srow, pol_stream);
-              tma_load_2d(xs + kOpBytes + 256, &tm_sg, &bars->x_full[ps], j * 64, srow, pol_stream);
-              tma_load_2d(xs + kOpBytes + 512, &tm_sv, &bars->x_full[ps], j * 64, srow, pol_stream);
-              tma_load_2d(xs + kOpBytes + 768, &tm_excl, &bars->x_full[ps], j * 64, srow, pol_stream);
+            uint8_t* xp = xsub(p, x);
+            if constexpr (FAR) {
+              tma_load_2d(xp + kOpBytes, &tm_lz, &bars->x_full[xs], j * 64, srow, pol_stream);
+              tma_load_2d(xp + kOpBytes + 256, &tm_sg, &bars->x_full[xs], j * 64, srow, pol_stream);
+              tma_load_2d(xp + kOpBytes + 512, &tm_sv, &bars->x_full[xs], j * 64, srow, pol_stream);
+              tma_load_2d(xp + kOpBytes + 768, &tm_excl, &bars->x_full[xs], j * 64, srow, pol_stream);
             } else {
-              tma_load_3d(xs, &tm_k, &bars->x_full[ps], 0, idx_s[j - nf] * 64, 0, pol_keep);
+              tma_load_3d(xp, &tm_k, &bars->x_full[xs], 0, idx_s[j] * 64, 0, pol_keep);
             }
           }
         }
@@ -427,149 +430,118 @@ __global__ void __launch_bounds__(tfx::kThreads, 1)
       }
     } else if (warp == 1) {
       // ---------------------------------------------------------------- PV issuer
-      const uint32_t id_far = idesc_f16(64, 128, false, true), id_near = idesc_bf16(64, 128, false, true);
+      const uint32_t idesc = FAR ? idesc_f16(64, 128, false, true) : idesc_bf16(64, 128, false, true);
       for (int p = 0; p < np; ++p) {
-        const int b = p & 3, g = p & 1, ys = p & 1;
+        const int b = p & 3, g = p & 1, ys = p % C::kYP;
         if (!mbar_wait_warp(&bars->p_full[b], (p >> 2) & 1, status, abort_flag)) break;
-        if (!mbar_wait_warp(&bars->y_full[ys], (p >> 1) & 1, status, abort_flag)) break;
+        if (!mbar_wait_warp(&bars->y_full[ys], (p / C::kYP) & 1, status, abort_flag)) break;
         tc_fence_after();
 #pragma unroll
         for (int x = 0; x < 2; ++x) {
-          const int j = 2 * p + x;
-          if (j < total) {
+          if (2 * p + x < total) {
             const uint32_t lane_off = static_cast<uint32_t>(16 * x) << 16;
             const uint32_t d = tmem + lane_off + kColO + 128 * g;
             const uint32_t a = tmem + lane_off + kColS + 64 * b;
-            const uint32_t ysub = smem_u32(smem + kOffY + (ys * 2 + x) * kOpBytes);
+            const uint32_t yb = smem_u32(ysub(p, x));
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
-              mma_bf16_ts_by(leader, d, a + 8 * kk, sw128_desc(ysub + kk * 2048, kOpBytes / 2, 1024),
-                             j < nf ? id_far : id_near, ((p >> 1) | kk) != 0);
+              mma_bf16_ts_by(leader, d, a + 8 * kk, sw128_desc(yb + kk * 2048, kOpBytes / 2, 1024), idesc,
+                             ((p >> 1) | kk) != 0);
           }
         }
         mma_commit_by(leader, &bars->pv_done[b]);
       }
     } else if (warp == 2) {
-      // ---------------------------------------------------------------- QK issuer + Y producer
-      // Both wait for PV(p): it frees S/P buffer p % 4 for QK(p + 4) and the Y slot of pair p for p + 2.
-      const uint64_t pol_stream = policy_evict_first();
-      const uint64_t pol_keep = policy_evict_last();
-      const uint32_t id_far = idesc_f16(64, 64, false, false), id_near = idesc_bf16(64, 64, false, false);
-      auto produce_y = [&](int p) -> bool {
-        const int ys = p & 1;
-        for (int x = 0; x < 2; ++x) {          // raw vbar slots of the pair's far steps
-          const int j = 2 * p + x;
-          if (j < total && j < nf && j >= 2 &&
-              !mbar_wait_warp(&bars->rv_empty[x], ((j >> 1) - 1) & 1, status, abort_flag))
-            return false;
-        }
-        if (leader) {
-          uint32_t tx = 0;
-          for (int x = 0; x < 2; ++x) {
-            const int j = 2 * p + x;
-            if (j < total && j >= nf) tx += kOpBytes;
-          }
-          mbar_arrive_expect_tx(&bars->y_full[ys], tx);
-          for (int x = 0; x < 2; ++x) {
-            const int j = 2 * p + x;
-            if (j >= total) continue;
-            if (j < nf) {
-              mbar_arrive_expect_tx(&bars->rv_full[x], kRawBytes);
-              tma_load_3d(smem + kOffRawV + x * kRawBytes, &tm_vraw, &bars->rv_full[x], 0, j * 64, srow, pol_stream);
-            } else {
-              tma_load_3d(smem + kOffY + (ys * 2 + x) * kOpBytes, &tm_v, &bars->y_full[ys], 0, idx_s[j - nf] * 64, 0,
-                          pol_keep);
-            }
-          }
-        }
-        __syncwarp();
-        return true;
-      };
-      auto issue_qk = [&](int p) -> bool {
-        const int ps = p & 1;
-        if (!mbar_wait_warp(&bars->x_full[ps], (p >> 1) & 1, status, abort_flag)) return false;
+      // ---------------------------------------------------------------- QK issuer
+      // QK(p) into S/P buffer p % 4 once PV(p - 4) freed it and the pair's X slot landed
+      const uint32_t idesc = FAR ? idesc_f16(64, 64, false, false) : idesc_bf16(64, 64, false, false);
+      const uint32_t a0 = smem_u32(smem + C::kOffQ);
+      bool ok = mbar_wait_warp(&bars->qd_full, 0, status, abort_flag);
+      for (int p = 0; ok && p < np; ++p) {
+        const int xs = p % C::kXP;
+        if (p >= 4 && !mbar_wait_warp(&bars->pv_done[p & 3], ((p - 4) >> 2) & 1, status, abort_flag)) break;
+        if (!mbar_wait_warp(&bars->x_full[xs], (p / C::kXP) & 1, status, abort_flag)) break;
         tc_fence_after();
         const uint32_t b = p & 3;
 #pragma unroll
         for (int x = 0; x < 2; ++x) {
-          const int j = 2 * p + x;
-          if (j < total) {
-            const bool far = j < nf;
-            const uint32_t a0 = smem_u32(smem + (far ? kOffDqh : kOffQb));
-            const uint32_t b0 = smem_u32(smem + kOffX + (ps * 2 + x) * kXSub);
+          if (2 * p + x < total) {
+            const uint32_t b0 = smem_u32(xsub(p, x));
             const uint32_t d = tmem + (static_cast<uint32_t>(16 * x) << 16) + kColS + 64 * b;
 #pragma unroll
             for (int h = 0; h < 2; ++h)
 #pragma unroll
               for (int kk = 0; kk < 4; ++kk)
                 mma_bf16_by(leader, d, sw128_desc(a0 + h * (kOpBytes / 2) + kk * 32, 16, 1024),
-                            sw128_desc(b0 + h * (kOpBytes / 2) + kk * 32, 16, 1024), far ? id_far : id_near,
-                            (h | kk) != 0);
+                            sw128_desc(b0 + h * (kOpBytes / 2) + kk * 32, 16, 1024), idesc, (h | kk) != 0);
           }
         }
         mma_commit_by(leader, &bars->s_full[b]);
-        mma_commit_by(leader, &bars->x_empty[ps]);
-        return true;
-      };
-      bool ok = mbar_wait_warp(&bars->qd_full, 0, status, abort_flag);
-      for (int p = 0; ok && p < np && p < 2; ++p) ok = produce_y(p);
-      for (int p = 0; ok && p < np && p < 4; ++p) ok = issue_qk(p);
-      for (int p = 0; ok && p + 2 < np; ++p) {
-        if (!mbar_wait_warp(&bars->pv_done[p & 3], (p >> 2) & 1, status, abort_flag)) break;
-        ok = produce_y(p + 2);
-        if (ok && p + 4 < np) ok = issue_qk(p + 4);
+        mma_commit_by(leader, &bars->x_empty[xs]);
       }
-    } else {
-      // ---------------------------------------------------------------- per-column constants
-      // far: (sg * log2 e, lz * log2 e or -inf if routed / past nb) and sv; near: (scale * log2 e, 0)
-      const float near_c1 = scale * kLog2e;
+    } else if constexpr (FAR) {
+      // ---------------------------------------------------------------- per-column constants (FAR)
+      // (sg * log2 e, lz * log2 e or -inf if routed / past nb) and sv
       for (int p = 0; p < np; ++p) {
-        const int ps = p & 1;
-        if (!mbar_wait_warp(&bars->x_full[ps], (p >> 1) & 1, status, abort_flag)) break;
-        if (p >= 2 && !mbar_wait_warp(&bars->cc_empty[ps], ((p >> 1) - 1) & 1, status, abort_flag)) break;
+        const int xs = p % C::kXP, cs_slot = p & 1;
+        if (!mbar_wait_warp(&bars->x_full[xs], (p / C::kXP) & 1, status, abort_flag)) break;
+        if (p >= 2 && !mbar_wait_warp(&bars->cc_empty[cs_slot], ((p >> 1) - 1) & 1, status, abort_flag)) break;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const int colq = q * 32 + lane;      // step parity x = colq / 64, column colq % 64
           const int x = colq >> 6, i = colq & 63;
           const int j = 2 * p + x;
-          const uint8_t* par = smem + kOffX + (ps * 2 + x) * kXSub + kOpBytes;
-          float2 c = make_float2(near_c1, 0.f);
-          float svv = 1.f;
-          if (j < nf) {
-            const float* pf = reinterpret_cast<const float*>(par);
-            const bool masked = par[768 + i] != 0 || j * 64 + i >= nb;
-            c = make_float2(pf[64 + i] * kLog2e, masked ? -INFINITY : pf[i] * kLog2e);
-            svv = pf[128 + i];
-          }
-          cc[(ps * 2 + x) * 64 + i] = c;
-          cs[(ps * 2 + x) * 64 + i] = svv;
+          const uint8_t* par = xsub(p, x) + kOpBytes;
+          const float* pf = reinterpret_cast<const float*>(par);
+          const bool masked = j >= total || par[768 + i] != 0 || j * 64 + i >= nb;
+          cc[(cs_slot * 2 + x) * 64 + i] = make_float2(pf[64 + i] * kLog2e, masked ? -INFINITY : pf[i] * kLog2e);
+          cs[(cs_slot * 2 + x) * 64 + i] = masked ? 0.f : pf[128 + i];
         }
-        mbar_arrive(&bars->x_empty[ps]);      // the raw parameters of this slot have been read
-        mbar_arrive(&bars->cc_full[ps]);
+        mbar_arrive(&bars->x_empty[xs]);      // the raw parameters of this slot have been read
+        mbar_arrive(&bars->cc_full[cs_slot]);
+      }
+    } else {
+      // ---------------------------------------------------------------- Y producer (NEAR)
+      // the values of the pair's routed leaves once PV(p - kYP) freed its Y slot
+      const uint64_t pol_keep = policy_evict_last();
+      for (int p = 0; p < np; ++p) {
+        const int ys = p % C::kYP;
+        if (p >= C::kYP &&
+            !mbar_wait_warp(&bars->pv_done[(p - C::kYP) & 3], ((p - C::kYP) >> 2) & 1, status, abort_flag))
+          break;
+        if (leader) {
+          mbar_arrive_expect_tx(&bars->y_full[ys], (2 * p + 1 < total ? 2 : 1) * kOpBytes);
+          for (int x = 0; x < 2; ++x)
+            if (2 * p + x < total)
+              tma_load_3d(ysub(p, x), &tm_v, &bars->y_full[ys], 0, idx_s[2 * p + x] * 64, 0, pol_keep);
+        }
+        __syncwarp();
       }
     }
   } else if (warp < 12) {
     // ------------------------------------------------------------------ softmax warpgroups
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 184;");
+    if constexpr (FAR) asm volatile("setmaxnreg.inc.sync.aligned.u32 184;");
     const int g = (warp - 4) >> 2;            // warpgroup: 0 takes even pairs, 1 odd pairs
     const int quarter = warp & 3;
     const int x = lane >> 4;                  // step parity of this thread
     const int r = quarter * 16 + (lane & 15); // query row
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const bool warp_rows = quarter * 16 < TROWS;   // warp-uniform: false for the held copies of row 31
+    const float c_near = scale * kLog2e;
     float m_used = -INFINITY, l = 0.f;
     bool aborted = false;
     int kcount = 0;
     for (int p = g; p < np; p += 2, ++kcount) {
-      const int b = p & 3, ps = p & 1;
-      const int j = 2 * p + x;
-      const bool has = j < total, far = j < nf;
+      const int b = p & 3;
+      const bool has = 2 * p + x < total;
       if (!mbar_wait_warp(&bars->s_full[b], (p >> 2) & 1, status, abort_flag)) { aborted = true; break; }
       __syncwarp();
       tc_fence_after();
       if (TROWS < 64 && !warp_rows) {
-        if (!mbar_wait_warp(&bars->cc_full[ps], (p >> 1) & 1, status, abort_flag)) { aborted = true; break; }
-        mbar_arrive(&bars->cc_empty[ps]);
+        if (FAR) {
+          if (!mbar_wait_warp(&bars->cc_full[g], (p >> 1) & 1, status, abort_flag)) { aborted = true; break; }
+          mbar_arrive(&bars->cc_empty[g]);
+        }
         uint32_t z[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) z[i] = 0u;
@@ -583,18 +555,23 @@ __global__ void __launch_bounds__(tfx::kThreads, 1)
       tmem_ld32(tmem + lane_base + kColS + 64 * b, d0);
       tmem_ld32(tmem + lane_base + kColS + 64 * b + 32, d1);
       tmem_ld_wait();
-      if (!mbar_wait_warp(&bars->cc_full[ps], (p >> 1) & 1, status, abort_flag)) { aborted = true; break; }
-      const float2* c = cc + (ps * 2 + x) * 64;
-      const float* sv = cs + (ps * 2 + x) * 64;
+      const float2* c = cc + (g * 2 + x) * 64;
+      const float* sv = cs + (g * 2 + x) * 64;
+      if (FAR && !mbar_wait_warp(&bars->cc_full[g], (p >> 1) & 1, status, abort_flag)) { aborted = true; break; }
       float lg[64];
       float mxa[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
       for (int i = 0; i < 64; i += 2) {
-        const float4 cv = *reinterpret_cast<const float4*>(c + i);     // (c1_i, c2_i, c1_i+1, c2_i+1)
         const uint32_t di0 = i < 32 ? d0[i] : d1[i - 32];
         const uint32_t di1 = i < 32 ? d0[i + 1] : d1[i - 31];
-        const float2 v = fma2(make_float2(__uint_as_float(di0), __uint_as_float(di1)), make_float2(cv.x, cv.z),
-                              make_float2(cv.y, cv.w));
+        float2 v;
+        if constexpr (FAR) {
+          const float4 cv = *reinterpret_cast<const float4*>(c + i);     // (c1_i, c2_i, c1_i+1, c2_i+1)
+          v = fma2(make_float2(__uint_as_float(di0), __uint_as_float(di1)), make_float2(cv.x, cv.z),
+                   make_float2(cv.y, cv.w));
+        } else {
+          v = mul2(make_float2(__uint_as_float(di0), __uint_as_float(di1)), make_float2(c_near, c_near));
+        }
         lg[i] = v.x;
         lg[i + 1] = v.y;
         mxa[(i >> 1) & 3] = fmaxf(mxa[(i >> 1) & 3], fmaxf(v.x, v.y));
@@ -609,15 +586,25 @@ __global__ void __launch_bounds__(tfx::kThreads, 1)
         m_used = m_new;
       }
       const bool live = has && m_used != -INFINITY;
-      const float mref = live ? m_used : 0.f;
+      const float2 mref2 = make_float2(live ? m_used : 0.f, live ? m_used : 0.f);
       uint32_t pw[32];
-      const bool all_far = __all_sync(0xffffffffu, far || !has), all_near = __all_sync(0xffffffffu, !far);
-      float rsum;
-      if (all_far) rsum = make_p<1>(lg, sv, mref, live, far, pw);
-      else if (all_near) rsum = make_p<0>(lg, sv, mref, live, far, pw);
-      else rsum = make_p<2>(lg, sv, mref, live, far, pw);
-      mbar_arrive(&bars->cc_empty[ps]);
-      l += rsum;
+      float2 rs2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+#pragma unroll
+      for (int i = 0; i < 64; i += 2) {
+        const float2 e = sub2(make_float2(lg[i], lg[i + 1]), mref2);
+        const float2 pp = live ? make_float2(ex2(e.x), ex2(e.y)) : make_float2(0.f, 0.f);
+        rs2[(i >> 1) & 3] = add2(rs2[(i >> 1) & 3], pp);
+        if constexpr (FAR) {
+          // far weights fp16(p * sv), as the reference's (p * sv).to(fp16) on the vbar codes
+          const float2 w = mul2(pp, *reinterpret_cast<const float2*>(sv + i));
+          pw[i >> 1] = pack_f16x2(w.x, w.y);
+        } else {
+          pw[i >> 1] = pack_bf16x2(pp.x, pp.y);
+        }
+      }
+      if (FAR) mbar_arrive(&bars->cc_empty[g]);
+      const float2 rsa = add2(add2(rs2[0], rs2[1]), add2(rs2[2], rs2[3]));
+      l += rsa.x + rsa.y;
       // the O rows are rescaled only after this warpgroup's previous PV (pair p - 2) is done; the whole warp
       // takes part because TMEM loads and stores are warp-collective
       __syncwarp();
@@ -661,20 +648,33 @@ __global__ void __launch_bounds__(tfx::kThreads, 1)
       const int64_t li = (t0 + tloc) * TROWS + r;                // query index in tile order
       const bool valid = r < TROWS && li < n;
       const int64_t orow = (perm != nullptr && valid) ? static_cast<int64_t>(__ldg(perm + li)) : li;
-      const float* tp = (tail_part != nullptr && valid) ? tail_part + orow * 130 : nullptr;
+      // NEAR: the far and tail partials of the row join the merge
+      const float* fp = (!FAR && far_part != nullptr && valid) ? far_part + orow * 130 : nullptr;
+      const float* tp = (!FAR && tail_part != nullptr && valid) ? tail_part + orow * 130 : nullptr;
+      const float mf = fp ? fp[128] : -INFINITY, lf = fp ? fp[129] : 0.f;
       const float mt = tp ? tp[128] : -INFINITY, lt = tp ? tp[129] : 0.f;
       const float mh = fmaxf(n0, n1);
-      const float mm = fmaxf(fmaxf(mh, __shfl_xor_sync(0xffffffffu, mh, 16)), mt);
+      const float mm = fmaxf(fmaxf(mh, __shfl_xor_sync(0xffffffffu, mh, 16)), fmaxf(mf, mt));
       const float a0 = n0 == -INFINITY ? 0.f : expf(n0 - mm);
       const float a1 = n1 == -INFINITY ? 0.f : expf(n1 - mm);
+      const float af = mf == -INFINITY ? 0.f : expf(mf - mm);
       const float at = mt == -INFINITY ? 0.f : expf(mt - mm);
       const float dh = l * a0 + l1 * a1;
-      const float den = dh + __shfl_xor_sync(0xffffffffu, dh, 16) + lt * at;
-      const float inv = 1.0f / fmaxf(den, 1e-30f);
-      const float c0 = a0 * inv, c1 = a1 * inv, ct = at * inv;
-      if (valid && x == 0 && lse != nullptr) lse[orow] = mm + logf(fmaxf(den, 1e-30f));
+      const float den = dh + __shfl_xor_sync(0xffffffffu, dh, 16) + lf * af + lt * at;
+      // FAR keeps the row unnormalised (acc relative to mm, with l = den) for the NEAR merge
+      const float inv = FAR ? 1.0f : 1.0f / fmaxf(den, 1e-30f);
+      const float c0 = a0 * inv, c1 = a1 * inv, cf = af * inv, ct = at * inv;
+      if (valid && x == 0) {
+        if (FAR) {
+          far_part[orow * 130 + 128] = mm;
+          far_part[orow * 130 + 129] = den;
+        } else if (lse != nullptr) {
+          lse[orow] = mm + logf(fmaxf(den, 1e-30f));
+        }
+      }
       __syncwarp();
       tc_fence_after();
+      float* dst_row = FAR ? far_part + orow * 130 : out + orow * 128;
 #pragma unroll 1
       for (int q4 = 0; q4 < 4; ++q4) {
         uint32_t o0[32], o1[32];
@@ -690,61 +690,85 @@ __global__ void __launch_bounds__(tfx::kThreads, 1)
           a[i] = v + __shfl_xor_sync(0xffffffffu, v, 16);      // + the other step parity of the row
         }
         if (valid && x == (q4 >> 1)) {
-          float4* dst = reinterpret_cast<float4*>(out + orow * 128 + 32 * q4);
+          float4* dst = reinterpret_cast<float4*>(dst_row + 32 * q4);
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             float v[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) v[e] = ct != 0.f ? fmaf(tp[32 * q4 + 4 * i + e], ct, a[4 * i + e]) : a[4 * i + e];
-            dst[i] = make_float4(v[0], v[1], v[2], v[3]);
+            for (int e = 0; e < 4; ++e) {
+              float t = a[4 * i + e];
+              if (cf != 0.f) t = fmaf(fp[32 * q4 + 4 * i + e], cf, t);
+              if (ct != 0.f) t = fmaf(tp[32 * q4 + 4 * i + e], ct, t);
+              v[e] = t;
+            }
+            if (FAR) {      // 130-float rows are only 8-byte aligned
+              reinterpret_cast<float2*>(dst_row + 32 * q4)[2 * i] = make_float2(v[0], v[1]);
+              reinterpret_cast<float2*>(dst_row + 32 * q4)[2 * i + 1] = make_float2(v[2], v[3]);
+            } else {
+              dst[i] = make_float4(v[0], v[1], v[2], v[3]);
+            }
           }
         }
       }
     }
-  } else {
-    // ------------------------------------------------------------------ code converters
+  } else if constexpr (FAR) {
+    // ------------------------------------------------------------------ code converters (FAR)
     asm volatile("setmaxnreg.dec.sync.aligned.u32 72;");
+    const uint64_t pol_stream = policy_evict_first();
     if (warp < 14) {
-      // g codes of far steps -> fp16 X operand
+      // g codes -> fp16 X operand of each block
       const int tid = threadIdx.x - 384;
       for (int p = 0; p < np; ++p) {
-        const int ps = p & 1;
-        if (p >= 2 && !mbar_wait_warp(&bars->x_empty[ps], ((p >> 1) - 1) & 1, status, abort_flag)) break;
+        const int xs = p % C::kXP;
+        if (p >= C::kXP && !mbar_wait_warp(&bars->x_empty[xs], ((p / C::kXP) - 1) & 1, status, abort_flag)) break;
         bool ok = true;
         for (int x = 0; x < 2 && ok; ++x) {
-          const int j = 2 * p + x;
-          if (j < total && j < nf) {
-            ok = mbar_wait_warp(&bars->rg_full[x], (j >> 1) & 1, status, abort_flag);
-            if (ok) {
-              codes_to_f16<64, 64>(smem + kOffRawG + x * kRawBytes, smem_u32(smem + kOffX + (ps * 2 + x) * kXSub), tid);
-              mbar_arrive(&bars->rg_empty[x]);
-            }
+          const int j = 2 * p + x, rs = j % C::kRG;
+          ok = mbar_wait_warp(&bars->rg_full[rs], (j / C::kRG) & 1, status, abort_flag);
+          if (ok) {
+            codes_to_f16<64, 64>(smem + C::kOffRawG + rs * kRawBytes, smem_u32(xsub(p, x)), tid);
+            mbar_arrive(&bars->rg_empty[rs]);
           }
         }
         if (!ok) break;
         fence_proxy_async_smem();        // the fp16 operand is read by the tensor cores (async proxy)
-        mbar_arrive(&bars->x_full[ps]);
+        mbar_arrive(&bars->x_full[xs]);
       }
     } else {
-      // vbar codes of far steps -> fp16 Y operand, once PV(p - 2) freed the pair's Y slot
+      // raw vbar codes kRV blocks ahead (TMA), converted into the pair's Y slot once PV(p - kYP) freed it
       const int tid = threadIdx.x - 448;
-      for (int p = 0; p < np; ++p) {
-        const int ys = p & 1;
-        if (p >= 2 && !mbar_wait_warp(&bars->pv_done[(p - 2) & 3], ((p - 2) >> 2) & 1, status, abort_flag)) break;
-        bool ok = true;
+      const uint32_t leader = elect_one() && warp == 14;      // one issuing lane for the two warps
+      int jr = 0;
+      bool ok = true;
+      auto load_raw = [&](int upto) {
+        for (; ok && jr < total && jr < upto; ++jr) {
+          const int rs = jr % C::kRV;
+          if (jr >= C::kRV) ok = mbar_wait_warp(&bars->rv_empty[rs], ((jr / C::kRV) - 1) & 1, status, abort_flag);
+          if (ok && leader) {
+            mbar_arrive_expect_tx(&bars->rv_full[rs], kRawBytes);
+            tma_load_3d(smem + C::kOffRawV + rs * kRawBytes, &tm_vraw, &bars->rv_full[rs], 0, jr * 64, srow,
+                        pol_stream);
+          }
+          __syncwarp();
+        }
+      };
+      for (int p = 0; ok && p < np; ++p) {
+        load_raw(2 * p + C::kRV);
+        if (!ok) break;
+        if (p >= C::kYP &&
+            !mbar_wait_warp(&bars->pv_done[(p - C::kYP) & 3], ((p - C::kYP) >> 2) & 1, status, abort_flag))
+          break;
         for (int x = 0; x < 2 && ok; ++x) {
-          const int j = 2 * p + x;
-          if (j < total && j < nf) {
-            ok = mbar_wait_warp(&bars->rv_full[x], (j >> 1) & 1, status, abort_flag);
-            if (ok) {
-              codes_to_f16<64, 64>(smem + kOffRawV + x * kRawBytes, smem_u32(smem + kOffY + (ys * 2 + x) * kOpBytes), tid);
-              mbar_arrive(&bars->rv_empty[x]);
-            }
+          const int j = 2 * p + x, rs = j % C::kRV;
+          ok = mbar_wait_warp(&bars->rv_full[rs], (j / C::kRV) & 1, status, abort_flag);
+          if (ok) {
+            codes_to_f16<64, 64>(smem + C::kOffRawV + rs * kRawBytes, smem_u32(ysub(p, x)), tid);
+            mbar_arrive(&bars->rv_empty[rs]);
           }
         }
         if (!ok) break;
         fence_proxy_async_smem();
-        mbar_arrive(&bars->y_full[ys]);
+        mbar_arrive(&bars->y_full[p % C::kYP]);
       }
     }
   }
@@ -754,25 +778,44 @@ __global__ void __launch_bounds__(tfx::kThreads, 1)
   if (warp == 1) tmem_dealloc(tmem, kTmemCols);
 }
 
+namespace {
+template <bool FAR>
+int set_tile_attr() {
+  using C = tfx::Cfg<FAR>;
+  bool ok = cudaFuncSetAttribute(tile_fp8_kernel<64, FAR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 C::kSmemBytes) == cudaSuccess &&
+            cudaFuncSetAttribute(tile_fp8_kernel<32, FAR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 C::kSmemBytes) == cudaSuccess;
+  return ok ? HTRC_OK : HTRC_ERR_CUDA;
+}
+}  // namespace
+
 int launch_tile_fp8(const TileFp8Maps& maps, const int32_t* idx, int kx, int nb, int64_t n, int tile_rows, int64_t t0,
-                    int64_t tc, int group, float scale, const float* tail_part, const int32_t* perm, float* out,
-                    float* lse, int* status, cudaStream_t st) {
+                    int64_t tc, int group, float scale, const float* tail_part, const int32_t* perm, float* far_part,
+                    float* out, float* lse, int* status, cudaStream_t st) {
   if (kx > tfx::kMaxKx || nb > 65535) return HTRC_ERR_UNSUPPORTED;
+  if (kx < nb && far_part == nullptr) return HTRC_ERR_ARG;
   static bool attr_done[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr_done[dev]) {
-    bool ok = true;
-    for (auto k : {tile_fp8_kernel<64>, tile_fp8_kernel<32>})
-      ok = ok && cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, tfx::kSmemBytes) == cudaSuccess;
-    if (!ok) return HTRC_ERR_CUDA;
+    if (set_tile_attr<true>() != HTRC_OK || set_tile_attr<false>() != HTRC_OK) return HTRC_ERR_CUDA;
     attr_done[dev] = true;
   }
-  const int nf = kx >= nb ? 0 : (nb + 63) / 64;
-  auto kernel = tile_rows == 32 ? tile_fp8_kernel<32> : tile_fp8_kernel<64>;
-  kernel<<<static_cast<unsigned>(tc), tfx::kThreads, tfx::kSmemBytes, st>>>(
-      maps.qb, maps.dqh, maps.graw, maps.vraw, maps.lz, maps.sg, maps.sv, maps.excl, maps.k, maps.v, idx, kx, nb, nf, n,
-      t0, group > 1 ? group : 1, scale, tail_part, perm, out, lse, status);
+  const int g = group > 1 ? group : 1;
+  const unsigned grid = static_cast<unsigned>(tc);
+  if (kx < nb) {
+    // the far field (all leaves not routed) first, as per-row partials
+    auto kf = tile_rows == 32 ? tile_fp8_kernel<32, true> : tile_fp8_kernel<64, true>;
+    kf<<<grid, tfx::Cfg<true>::kThreads, tfx::Cfg<true>::kSmemBytes, st>>>(
+        maps.dqh, maps.graw, maps.vraw, maps.lz, maps.sg, maps.sv, maps.excl, maps.k, maps.v, idx, kx, nb, n, t0, g,
+        scale, nullptr, perm, far_part, nullptr, nullptr, status);
+    if (cudaGetLastError() != cudaSuccess) return HTRC_ERR_CUDA;
+  }
+  auto kn = tile_rows == 32 ? tile_fp8_kernel<32, false> : tile_fp8_kernel<64, false>;
+  kn<<<grid, tfx::Cfg<false>::kThreads, tfx::Cfg<false>::kSmemBytes, st>>>(
+      maps.qb, maps.graw, maps.vraw, maps.lz, maps.sg, maps.sv, maps.excl, maps.k, maps.v, idx, kx, nb, n, t0, g, scale,
+      tail_part, perm, kx < nb ? far_part : nullptr, out, lse, status);
   return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
 }
 

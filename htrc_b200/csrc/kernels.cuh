@@ -75,7 +75,7 @@ int launch_tile_attention(const TileMaps& maps, const float* sq, const float* sd
 int launch_rowmax_fp8(const RowmaxFp8Maps& maps, float* sel, int64_t pitch, int64_t t0, int64_t tc, int nb, int group,
                       int* status, cudaStream_t st);
 int launch_tile_fp8(const TileFp8Maps& maps, const int32_t* idx, int kx, int nb, int64_t n, int tile_rows, int64_t t0,
-                    int64_t tc, int group, float scale, const float* tail_part, const int32_t* perm, float* out,
-                    float* lse, int* status, cudaStream_t st);
+                    int64_t tc, int group, float scale, const float* tail_part, const int32_t* perm, float* far_part,
+                    float* out, float* lse, int* status, cudaStream_t st);
 
 }  // namespace htrc

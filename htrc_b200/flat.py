@@ -440,10 +440,11 @@ def _run_stages_fp8(qd, kb, vb, tk, tv, *, n, m, nt, nb, ng, grp, pitch, sink, k
     check(L.htrc_route(ptr(r["sel"]), nt, nb, int(exact_leaves), sink, grp, ptr(r["idx"]), ptr(r["excl"]), s),
           "htrc_route")
     tick("select")
+    r["far_part"] = e(n, DIM + 2) if far else None
     check(L.htrc_tile_attention_fp8(ptr(r["qb"]), ptr(r["dqh"]), n, tile, 0, nt, grp, ptr(r["g8"]), ptr(r["sg"]),
                                     ptr(r["lz"]), ptr(r["vb8"]), ptr(r["sv"]), ptr(r["excl"]), ptr(r["idx"]), kx, nb,
-                                    ptr(kb), ptr(vb), m, DIM, LEAF, sc, ptr(tail_part), perm, ptr(r["out"]),
-                                    ptr(r["lse"]), stp, s), "htrc_tile_attention_fp8")
+                                    ptr(kb), ptr(vb), m, DIM, LEAF, sc, ptr(tail_part), perm, ptr(r["far_part"]),
+                                    ptr(r["out"]), ptr(r["lse"]), stp, s), "htrc_tile_attention_fp8")
     tick("tile")
     tick("finish")
     r["kx"], r["nb"], r["pitch"], r["group"], r["tile"] = kx, nb, pitch, grp, tile

@@ -217,14 +217,16 @@ int htrc_rowmax_select_fp8(const uint16_t* dqh, int64_t t0, int64_t tc, int32_t 
 
 /* Far field + near field (+ tail partial) with the fp8 state (h3/htrc_flat_triton.py:88-211, FP8=1, DOT=1,
  * merged as :257-273): far logit (dqh . g) * sg + lz with value weight fp16(p * sv) on the vbar codes,
- * near logit (qb . bf16 k) * scale with weight bf16(p) on v; one float32 softmax per row.  Other arguments
- * as htrc_tile_attention (k, v: the bf16 keys and values). */
+ * near logit (qb . bf16 k) * scale with weight bf16(p) on v.  Two launches: the far field writes one
+ * partial row (acc, m, l) per query into far_part [n_queries, dim + 2] f32 (scratch; NULL only when
+ * kx == nb), the near field merges it with the tail partial into out/lse.  Other arguments as
+ * htrc_tile_attention (k, v: the bf16 keys and values). */
 int htrc_tile_attention_fp8(const uint16_t* qb, const uint16_t* dqh, int64_t n_queries, int32_t tile, int64_t t0,
                             int64_t tc, int32_t group, const uint8_t* g8, const float* sg, const float* lz,
                             const uint8_t* vb8, const float* sv, const uint8_t* excl, const int32_t* idx, int32_t kx,
                             int64_t nb, const uint16_t* k, const uint16_t* v, int64_t n_keys, int32_t dim,
-                            int32_t leaf, float scale, const float* tail_part, const int32_t* perm, float* out,
-                            float* lse, int32_t* status, htrc_stream_t stream);
+                            int32_t leaf, float scale, const float* tail_part, const int32_t* perm,
+                            float* far_part, float* out, float* lse, int32_t* status, htrc_stream_t stream);
 
 /* The forward pass for callers that cannot allocate device memory (a plugin host that owns all device
  * allocations and lends only input and output buffers, or an embedding whose device footprint must not

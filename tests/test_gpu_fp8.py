@@ -171,11 +171,11 @@ def test_fp8_modes_against_oracle(dev, over):
     st = htrc_b200.run_stages(torch.from_numpy(q).cuda(), torch.from_numpy(k).to(torch.bfloat16).cuda(),
                               torch.from_numpy(v).to(torch.bfloat16).cuda(), exact_leaves=24, sink_leaves=1,
                               store=1, group=htrc_b200.flat.group_of(cfg.get("kern")),
-                              order=htrc_b200.flat.order_code(cfg["order"]), tile=cfg["tile"])
+                              order=htrc_b200.flat.order_code(cfg.get("order", "seq")), tile=cfg["tile"])
     torch.cuda.synchronize()
     perm = _np(st["perm"]) if st["perm"] is not None else None
     ro, rl, rst = O.flat_attention(q, k, v, exact_leaves=24, sink_leaves=1, tile=cfg["tile"],
-                                   group=htrc_b200.flat.group_of(cfg.get("kern")), order=cfg["order"], perm=perm,
+                                   group=htrc_b200.flat.group_of(cfg.get("kern")), order=cfg.get("order", "seq"), perm=perm,
                                    store="fp8", return_stages=True)
     nb = st["nb"]
     assert (_np(st["excl"])[:, :nb] == rst["excl"]).mean() >= ROUTE_AGREE

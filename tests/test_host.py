@@ -167,6 +167,11 @@ def test_fp8_state_option_is_accepted_and_checked():
     # held row), vbar codes instead of bf16 (- nt*nb*128), plus sv (nt * pitch * 4); alignment slack
     want = i8 - m * 132 + nt * 64 * (512 - 264) - nt * nb * 128 + nt * F.leaf_pitch(nb) * 4
     assert abs(f8 - want) <= 8 * 256
+    # with a far field the fp8 path also keeps one far partial row (dim + 2 floats) per query
+    i8 = F.workspace_bytes(n, m, 64, store=_lib.STORE_INT8)
+    f8 = F.workspace_bytes(n, m, 64, store=_lib.STORE_FP8)
+    want = i8 - m * 132 + nt * 64 * (512 - 264) - nt * nb * 128 + nt * F.leaf_pitch(nb) * 4 + n * 130 * 4
+    assert abs(f8 - want) <= 8 * 256
     a = _lib.HtrcFlatArgs()
     a.n_queries, a.n_keys, a.dim, a.tile, a.leaf, a.exact_leaves = n, m, 128, 64, 64, 256
     a.store, a.curvature = _lib.STORE_FP8, _lib.CURV_ISO
