@@ -59,6 +59,9 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-modes", action="store_true", help="skip the per-mode head timings")
+    ap.add_argument("--store", default="int8", choices=["int8", "fp8"],
+                    help="far-field state: int8 (the production path, the headline) or fp8 (e4m3 state, store='fp8'; "
+                         "no oracle sample)")
     ap.add_argument("--streams", type=int, default=1, choices=[1, 2],
                     help="heads of a layer alternate over this many streams, each with its own workspace (2: "
                          "-1.7%% device-resident, +2%% end to end, and the per-stage events then overlap)")
@@ -223,7 +226,10 @@ def run_ours(a, wl, rank, world, local_rank):
     dq = {h: tuple(t.to(dev, non_blocking=True) for t in host[h]) for h in my_heads}
     out = {h: torch.empty((n, 128), dtype=torch.float32, device=dev) for h in my_heads}
     lse = {h: torch.empty((n,), dtype=torch.float32, device=dev) for h in my_heads}
-    wsb = F.workspace_bytes(n, m, E, 0, 0, 0)
+    from htrc_b200 import _lib as _L
+    store = _L.STORES[a.store]
+    fp8 = store == _L.STORE_FP8
+    wsb = F.workspace_bytes(n, m, E, 0, 0, 0, store=store)
     ws = F.new_workspace(wsb, dev)
     comp = torch.cuda.current_stream(dev)
     side = torch.cuda.Stream(dev)
@@ -247,7 +253,7 @@ def run_ours(a, wl, rank, world, local_rank):
             hs = head_streams[i % len(head_streams)]
             with torch.cuda.stream(hs):
                 F.forward_into(*dq[h], None, None, exact_leaves=E, out=out[h], lse=lse[h],
-                               workspace=head_ws[i % len(head_ws)], stage_events=evs, stream=hs)
+                               workspace=head_ws[i % len(head_ws)], stage_events=evs, stream=hs, store=store)
                 if world > 1 and gather:
                     obf[h].copy_(out[h])
                     ev_done[i].record(hs)
@@ -319,7 +325,7 @@ def run_ours(a, wl, rank, world, local_rank):
     # ---- parity at full size on a tile sample of head 0 (rank 0): mean |dlogZ| vs the oracle
     parity = {}
     cpu = None
-    if rank == 0 and not a.no_cpu:
+    if rank == 0 and not a.no_cpu and not fp8:
         h0 = my_heads[0]
         qn, kn, vn = (t.float().numpy() for t in host[h0])
         rng = np.random.default_rng(1)
@@ -378,7 +384,7 @@ def run_ours(a, wl, rank, world, local_rank):
                 if i >= 2:
                     hs.wait_event(out_done[b])
                 with torch.cuda.stream(hs):
-                    htrc_b200.forward_into(*stage_in[b], None, None, exact_leaves=E, out=stage_out[b][0],
+                    htrc_b200.forward_into(*stage_in[b], None, None, exact_leaves=E, store=store, out=stage_out[b][0],
                                            lse=stage_out[b][1], workspace=head_ws[i % len(head_ws)], stream=hs)
                 comp_done[b].record(hs)
                 s_out.wait_event(comp_done[b])
@@ -465,18 +471,21 @@ def run_ours(a, wl, rank, world, local_rank):
     npad = nt * 64
     near = 2.0 * npad * (kx * 64) * 128
     far = 2.0 * npad * (nb - kx) * 128 if kx < nb else 0.0
-    flops_bf16_equiv = (near + far) + 0.5 * (near + far)       # bf16 PV + int8 QK at half cost
+    # INT8: bf16 PV + int8 QK at half cost; fp8: fp16 / bf16 QK and PV at full cost
+    flops_bf16_equiv = 2.0 * (near + far) if fp8 else (near + far) + 0.5 * (near + far)
     tile_ms = stage_ms["tile"]
     achieved = flops_bf16_equiv / (tile_ms * 1e-3) / 1e12
     peak = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops")))
     traffic = None
     tp = ROOT / "profiles" / "tile_attention_traffic.json"
-    if tp.exists():
+    if tp.exists() and not fp8:
         traffic = json.loads(tp.read_text()).get("bytes_per_launch", {}).get(a.workload)
-    roof = {"kernel": "tile_attention_kernel", "bound": "tensor", "achieved": achieved, "peak": peak,
+    roof = {"kernel": "tile_fp8_kernel (far + near passes)" if fp8 else "tile_attention_kernel", "bound": "tensor",
+            "achieved": achieved, "peak": peak,
             "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
             "peak_source": f"{peak_src} bf16_tflops_sustained", "flop_per_launch": flops_bf16_equiv,
-            "flop_count": "bf16 PV flops + int8 QK ops/2 over the routed tokens and non-routed leaves, one head",
+            "flop_count": ("fp16/bf16 QK + PV flops" if fp8 else "bf16 PV flops + int8 QK ops/2") +
+                          " over the routed tokens and non-routed leaves, one head",
             "ms_per_launch": tile_ms}
 
     # ---- every stage against its binding roofline (algorithmic bytes or flop per head / stage time)
@@ -488,6 +497,9 @@ def run_ours(a, wl, rank, world, local_rank):
         "rowmax": nt * nb * 128 + 2 * nt * pitch * 4 + nt * pitch * 4,          # g8 + sg/lz read, sel written
         "route": nt * pitch * 4 + nt * (pitch + kx * 4),                        # sel read, excl/idx written
     }
+    if fp8:
+        stage_bytes["prep"] = n * 2 * 128 + npad * 2 * 2 * 128                  # bf16 q read; bf16 + fp16 rows
+        stage_bytes["stats"] = nt * nb * (128 + 128) + 3 * nt * pitch * 4       # g + vbar codes, sg/sv/lz
     stage_roof = {nm: {"bound": "hbm", "bytes": b_, "achieved_gbs": b_ / (stage_ms[nm] * 1e-3) / 1e9,
                        "frac": b_ / (stage_ms[nm] * 1e-3) / 1e9 / hbm}
                   for nm, b_ in stage_bytes.items()}
@@ -497,11 +509,16 @@ def run_ours(a, wl, rank, world, local_rank):
     if rank == 0:
         line = {"metric": METRIC, "value": ms, "unit": "ms/layer", "n_gpus": world, "steps": a.steps,
                 "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": False, "scaling": "strong",
-                "vs_baseline": None, "dtype": "int8 QK + bf16 PV, f32 softmax",
+                "vs_baseline": None,
+                "dtype": ("fp8 (e4m3) state; fp16 far / bf16 near QK and PV, f32 softmax" if fp8 else
+                          "int8 QK + bf16 PV, f32 softmax"),
                 "data": "synthetic: seeded smooth-field Q/K (4x8x8 grid trilinear + 0.5 noise, RMS 3), N(0,1) V, bf16",
-                "config": {"workload": wl["name"], "tokens": n, "heads": H, "dim": 128, "leaf": 64, "tile": 64,
+                "config": {"workload": wl["name"].replace("INT8", "fp8 (e4m3) state") if fp8 else wl["name"],
+                           "tokens": n, "heads": H,
+                           "dim": 128, "leaf": 64, "tile": 64, "store": a.store,
                            "exact_leaves": E, "heads_per_gpu": len(my_heads), "head_streams": a.streams,
-                           "l2": "inputs larger than L2: 2.4 GB of distinct q/k/v per layer, 1.6 GB leaf state per head",
+                           "l2": "inputs larger than L2: 2.4 GB of distinct q/k/v per layer, "
+                                 + ("1.0" if fp8 else "1.6") + " GB leaf state per head",
                            "parallelism": f"heads/{world}" + (" + bf16 output all_gather (NCCL)" if world > 1 else "")},
                 "stage_ms_per_head": stage_ms, "stage_roofline": stage_roof, "gather": gather_info, "modes": modes,
                 **parity,
