@@ -46,12 +46,15 @@ __device__ __forceinline__ void codes_to_f16(const uint8_t* raw, uint32_t dst, i
 // ================================================================================================
 // Row-max selection.  Per block of 128 leaves: C = G_block (M=128 leaves, K=128, fp16 from the codes) x
 // DQ_tile^T (N=64 rows, fp16) into TMEM; the thread owning TMEM lane l reduces its 64 columns.  One CTA per
-// tile; warp 0 loads (TMA), warp 1 issues the MMAs, warps 2-5 convert block j + 1 and reduce block j.
+// tile, two CTAs per SM; warp 0 loads (TMA), warp 1 issues the MMAs, warps 2-5 reduce block j while eight
+// warps convert the next block.
 // Groups of G tiles read state row t / G (the routing kernel takes the maximum over the group's rows).
 namespace {
 namespace rmx {
-constexpr int kStages = 6;                              // raw code stages: the HBM stream in flight
-constexpr int kOpStages = 2;                            // converted fp16 blocks
+constexpr int kStages = 3;                              // raw code stages: the HBM stream in flight
+constexpr int kOpStages = 1;                            // converted fp16 blocks (two CTAs share an SM)
+constexpr int kConv = 256;                              // converting threads (warps 6 ..)
+constexpr int kThreads = 192 + kConv;
 constexpr uint32_t kRawBytes = 128 * 128;               // 128 leaves x 128 codes
 constexpr uint32_t kRawStage = kRawBytes + 1024;        // + sg[128], lz[128]
 constexpr uint32_t kOpBytes = 2 * 128 * 128;            // fp16 g block: 2 halves x 128 rows x 128 B
@@ -66,8 +69,8 @@ static_assert(kOffOp % 1024 == 0, "swizzled operands need 1024-byte alignment");
 struct Bars {
   uint64_t dq_full;
   uint64_t raw_full[kStages];    // TMA: codes, sg, lz
-  uint64_t raw_empty[kStages];   // the 128 converting threads read them
-  uint64_t op_full[kOpStages];   // the 128 converting threads wrote the fp16 block
+  uint64_t raw_empty[kStages];   // the converting threads read the codes, the 128 reducing threads sg / lz
+  uint64_t op_full[kOpStages];   // the converting threads wrote the fp16 block
   uint64_t op_empty[kOpStages];  // MMA commit
   uint64_t acc_full[2];
   uint64_t acc_empty[2];         // the 128 reducing threads drained the accumulator
@@ -77,7 +80,7 @@ struct Bars {
 }  // namespace rmx
 }  // namespace
 
-__global__ void __launch_bounds__(192)
+__global__ void __launch_bounds__(rmx::kThreads, 2)
     rowmax_fp8_kernel(const __grid_constant__ CUtensorMap tm_dqh, const __grid_constant__ CUtensorMap tm_graw,
                       const __grid_constant__ CUtensorMap tm_sg, const __grid_constant__ CUtensorMap tm_lz,
                       float* __restrict__ sel, int64_t pitch, int64_t t0, int nb, int group, int* status) {
@@ -96,10 +99,10 @@ __global__ void __launch_bounds__(192)
     mbar_init(&bars->dq_full, 1);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&bars->raw_full[s], 1);
-      mbar_init(&bars->raw_empty[s], 128);
+      mbar_init(&bars->raw_empty[s], kConv + 128);
     }
     for (int s = 0; s < kOpStages; ++s) {
-      mbar_init(&bars->op_full[s], 128);
+      mbar_init(&bars->op_full[s], kConv);
       mbar_init(&bars->op_empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -151,55 +154,52 @@ __global__ void __launch_bounds__(192)
         mma_commit(&bars->op_empty[s]);
       }
     }
-  } else {
-    // convert block j, then reduce block j - 1 (its MMA overlaps the conversion)
-    const int tid = threadIdx.x - 64;
+  } else if (warp < 6) {
+    // reduce block j: sel over the tile's 64 rows for the leaf of this thread's TMEM lane
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;                 // leaf within the block (TMEM lane)
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-    float sg_prev = 0.f, lz_prev = 0.f;
-    for (int j = 0; j <= nblk; ++j) {
-      float sg_cur = 0.f, lz_cur = 0.f;
-      if (j < nblk) {
-        const int s = j % kStages, o = j % kOpStages;
-        if (!mbar_wait_warp(&bars->raw_full[s], (j / kStages) & 1, status, abort_flag)) break;
-        if (j >= kOpStages && !mbar_wait_warp(&bars->op_empty[o], ((j / kOpStages) - 1) & 1, status, abort_flag))
-          break;
-        const uint8_t* st = smem + kOffRaw + s * kRawStage;
-        codes_to_f16<128, 128>(st, smem_u32(smem + kOffOp + o * kOpBytes), tid);
-        sg_cur = reinterpret_cast<const float*>(st + kRawBytes)[r];
-        lz_cur = reinterpret_cast<const float*>(st + kRawBytes + 512)[r];
-        fence_proxy_async_smem();
-        mbar_arrive(&bars->op_full[o]);
-        mbar_arrive(&bars->raw_empty[s]);
-      }
-      if (j >= 1) {
-        const int jb = j - 1, b = jb & 1;
-        if (!mbar_wait_warp(&bars->acc_full[b], (jb >> 1) & 1, status, abort_flag)) break;
-        __syncwarp();
-        tc_fence_after();
-        uint32_t d0[32], d1[32];
-        tmem_ld32(tmem + lane_base + 64 * b, d0);
-        tmem_ld32(tmem + lane_base + 64 * b + 32, d1);
-        tmem_ld_wait();
-        tc_fence_before();
-        mbar_arrive(&bars->acc_empty[b]);
-        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-        const float2 s2 = make_float2(sg_prev, sg_prev);
+    for (int j = 0; j < nblk; ++j) {
+      const int s = j % kStages, b = j & 1;
+      if (!mbar_wait_warp(&bars->raw_full[s], (j / kStages) & 1, status, abort_flag)) break;
+      const uint8_t* st = smem + kOffRaw + s * kRawStage;
+      const float sgl = reinterpret_cast<const float*>(st + kRawBytes)[r];
+      const float lzl = reinterpret_cast<const float*>(st + kRawBytes + 512)[r];
+      mbar_arrive(&bars->raw_empty[s]);
+      if (!mbar_wait_warp(&bars->acc_full[b], (j >> 1) & 1, status, abort_flag)) break;
+      __syncwarp();
+      tc_fence_after();
+      uint32_t d0[32], d1[32];
+      tmem_ld32(tmem + lane_base + 64 * b, d0);
+      tmem_ld32(tmem + lane_base + 64 * b + 32, d1);
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(&bars->acc_empty[b]);
+      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      const float2 s2 = make_float2(sgl, sgl);
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const float2 a = mul2(make_float2(__uint_as_float(d0[i]), __uint_as_float(d0[i + 1])), s2);
-          const float2 c = mul2(make_float2(__uint_as_float(d1[i]), __uint_as_float(d1[i + 1])), s2);
-          mx[(i >> 1) & 1] = max3(mx[(i >> 1) & 1], a.x, a.y);
-          mx[2 + ((i >> 1) & 1)] = max3(mx[2 + ((i >> 1) & 1)], c.x, c.y);
-        }
-        const int leaf = jb * 128 + r;
-        if (leaf < nb)
-          sel[static_cast<int64_t>(tloc) * pitch + leaf] =
-              __fadd_rn(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), lz_prev);
+      for (int i = 0; i < 32; i += 2) {
+        const float2 a = mul2(make_float2(__uint_as_float(d0[i]), __uint_as_float(d0[i + 1])), s2);
+        const float2 c = mul2(make_float2(__uint_as_float(d1[i]), __uint_as_float(d1[i + 1])), s2);
+        mx[(i >> 1) & 1] = max3(mx[(i >> 1) & 1], a.x, a.y);
+        mx[2 + ((i >> 1) & 1)] = max3(mx[2 + ((i >> 1) & 1)], c.x, c.y);
       }
-      sg_prev = sg_cur;
-      lz_prev = lz_cur;
+      const int leaf = j * 128 + r;
+      if (leaf < nb)
+        sel[static_cast<int64_t>(tloc) * pitch + leaf] = __fadd_rn(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), lzl);
+    }
+  } else {
+    // convert the codes of block j into the fp16 operand of stage j % kOpStages
+    const int tid = threadIdx.x - 192;
+    for (int j = 0; j < nblk; ++j) {
+      const int s = j % kStages, o = j % kOpStages;
+      if (!mbar_wait_warp(&bars->raw_full[s], (j / kStages) & 1, status, abort_flag)) break;
+      if (j >= kOpStages && !mbar_wait_warp(&bars->op_empty[o], ((j / kOpStages) - 1) & 1, status, abort_flag))
+        break;
+      codes_to_f16<128, kConv>(smem + kOffRaw + s * kRawStage, smem_u32(smem + kOffOp + o * kOpBytes), tid);
+      fence_proxy_async_smem();
+      mbar_arrive(&bars->op_full[o]);
+      mbar_arrive(&bars->raw_empty[s]);
     }
   }
   tc_fence_before();
@@ -219,7 +219,7 @@ int launch_rowmax_fp8(const RowmaxFp8Maps& maps, float* sel, int64_t pitch, int6
       return HTRC_ERR_CUDA;
     attr_done[dev] = true;
   }
-  rowmax_fp8_kernel<<<static_cast<unsigned>(tc), 192, rmx::kSmemBytes, st>>>(maps.dqh, maps.graw, maps.sg, maps.lz, sel,
+  rowmax_fp8_kernel<<<static_cast<unsigned>(tc), rmx::kThreads, rmx::kSmemBytes, st>>>(maps.dqh, maps.graw, maps.sg, maps.lz, sel,
                                                                              pitch, t0, nb, group > 1 ? group : 1,
                                                                              status);
   return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;

@@ -192,3 +192,49 @@ def test_fp8_modes_against_oracle(dev, over):
     assert np.abs(o[ok_rows] - ro[ok_rows]).max() < OUT_TOL
     assert np.abs(lse.cpu().numpy() - rl).mean() < LSE_TOL
     assert np.array_equal(o, _np(st["out"]))            # the fused forward and the stage launches agree
+
+
+@pytest.mark.parametrize("chunk,group", [(8, 1), (6, 2), (4, 4)])
+def test_fp8_chunked_state_matches_one_chunk(dev, chunk, group):
+    """tile_chunk smaller than the tile count: the fp8 statistics, row-max and both tile passes run per
+    chunk of centre rows (t0 > 0, chunk-local state rows); every row equals the single-chunk result."""
+    import htrc_b200
+    q, k, v = _synthetic(2000, 8192, 77)
+    qd = torch.from_numpy(q).cuda()
+    kd = torch.from_numpy(k).to(torch.bfloat16).cuda()
+    vd = torch.from_numpy(v).to(torch.bfloat16).cuda()
+    base = {**htrc_b200.PROD, "leaf": 64, "store": "fp8", "exact_leaves": 12, "sink_leaves": 1,
+            "kern": {"group": group}}
+    o1, l1 = htrc_b200.flat_attention(qd, kd, vd, return_lse=True, **{**base, "tile_chunk": 0})
+    oc, lc = htrc_b200.flat_attention(qd, kd, vd, return_lse=True, **{**base, "tile_chunk": chunk})
+    torch.cuda.synchronize()
+    assert torch.equal(o1, oc) and torch.equal(l1, lc)
+
+
+def test_fp8_with_input_fake_quant(dev):
+    """store="fp8" with quant={"kv", "q", "group"}: the device rounds k, v (to bf16) and q through the formats
+    first; against the oracle modelling the same inputs."""
+    import htrc_b200
+    q, k, v = _synthetic(1024, 8192, 78)
+    quant = {"kv": "int4", "q": "int8", "group": 32}
+    cfg = {**htrc_b200.PROD, "leaf": 64, "store": "fp8", "exact_leaves": 16, "quant": quant}
+    out, lse = htrc_b200.flat_attention(torch.from_numpy(q).cuda(), torch.from_numpy(k).to(torch.bfloat16).cuda(),
+                                        torch.from_numpy(v).to(torch.bfloat16).cuda(), return_lse=True, **cfg)
+    torch.cuda.synchronize()
+    ro, rl, rst = O.flat_attention(q, k, v, exact_leaves=16, quant=quant, stats_bf16=True, store="fp8",
+                                   return_stages=True)
+    o = out.cpu().numpy()
+    assert np.abs(lse.cpu().numpy() - rl).mean() < LSE_TOL
+    # rows of tiles whose routing the oracle reproduces are within the output tolerance
+    st = htrc_b200.run_stages(htrc_b200.flat.fake_quant(torch.from_numpy(q).cuda(), "int8", 32),
+                              htrc_b200.flat.fake_quant(torch.from_numpy(k).cuda(), "int4", 32,
+                                                        out_dtype=torch.bfloat16),
+                              htrc_b200.flat.fake_quant(torch.from_numpy(v).cuda(), "int4", 32,
+                                                        out_dtype=torch.bfloat16),
+                              exact_leaves=16, store=1)
+    torch.cuda.synchronize()
+    nb = st["nb"]
+    same = np.repeat((_np(st["excl"])[:, :nb] == rst["excl"]).all(1), 64)[: q.shape[0]]
+    assert same.mean() > 0.9
+    assert np.abs(o[same] - ro[same]).max() < OUT_TOL
+    assert np.array_equal(o, _np(st["out"]))
