@@ -110,12 +110,12 @@ bool map_state(CUtensorMap* m, const void* base, int64_t tc, int64_t nb, bool bf
                   box, true);
 }
 
-// [tc, nb, 128] one-byte codes without swizzle (staged as plain 128-byte rows), box (128, box_leaves, 1)
-bool map_codes(CUtensorMap* m, const void* base, int64_t tc, int64_t nb, int box_leaves) {
+// [tc, nb, 128] one-byte codes staged as 128-byte rows (plain, or 128-byte swizzled), box (128, box_leaves, 1)
+bool map_codes(CUtensorMap* m, const void* base, int64_t tc, int64_t nb, int box_leaves, bool swizzle) {
   const uint64_t dims[3] = {128, static_cast<uint64_t>(nb), static_cast<uint64_t>(tc)};
   const uint64_t strides[2] = {128, static_cast<uint64_t>(nb) * 128};
   const uint32_t box[3] = {128u, static_cast<uint32_t>(box_leaves), 1u};
-  return make_map(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, base, dims, strides, box, false);
+  return make_map(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, base, dims, strides, box, swizzle);
 }
 
 // [tc, nb] scalars (f32 or u8) with row pitch `pitch` elements, box (box_cols, 1)
@@ -259,7 +259,7 @@ int stats_maps(LeafStatsMaps* mp, const uint16_t* mu_hi, const uint16_t* mu_lo, 
 
 int rowmax_fp8_maps(RowmaxFp8Maps* mp, const uint16_t* dqh, int64_t rows, const uint8_t* g8, const float* sg,
                     const float* lz, int64_t tc, int64_t nb, int64_t pitch) {
-  bool ok = map_rows_halves(&mp->dqh, dqh, rows, 64) && map_codes(&mp->graw, g8, tc, nb, 128) &&
+  bool ok = map_rows_halves(&mp->dqh, dqh, rows, 64) && map_codes(&mp->graw, g8, tc, nb, 128, false) &&
             map_scalars(&mp->sg, sg, tc, nb, pitch, true, 128) && map_scalars(&mp->lz, lz, tc, nb, pitch, true, 128);
   return ok ? HTRC_OK : HTRC_ERR_CUDA;
 }
@@ -268,7 +268,7 @@ int tile_fp8_maps(TileFp8Maps* mp, const uint16_t* qb, const uint16_t* dqh, int6
                   const uint8_t* vb8, const float* lz, const float* sg, const float* sv, const uint8_t* excl, int64_t tc,
                   int64_t nb, int64_t pitch, const uint16_t* k, const uint16_t* v, int64_t m) {
   bool ok = map_rows_halves(&mp->qb, qb, rows, 64) && map_rows_halves(&mp->dqh, dqh, rows, 64) &&
-            map_codes(&mp->graw, g8, tc, nb, 64) && map_codes(&mp->vraw, vb8, tc, nb, 64) &&
+            map_codes(&mp->graw, g8, tc, nb, 64, true) && map_codes(&mp->vraw, vb8, tc, nb, 64, true) &&
             map_scalars(&mp->lz, lz, tc, nb, pitch, true, 64) && map_scalars(&mp->sg, sg, tc, nb, pitch, true, 64) &&
             map_scalars(&mp->sv, sv, tc, nb, pitch, true, 64) &&
             map_scalars(&mp->excl, excl, tc, nb, pitch, false, 64) && map_rows_halves(&mp->k, k, m, 64) &&

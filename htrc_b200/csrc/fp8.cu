@@ -41,6 +41,32 @@ __device__ __forceinline__ void codes_to_f16(const uint8_t* raw, uint32_t dst, i
                  e4m3x2_to_f16x2(w.x >> 16), e4m3x2_to_f16x2(w.y), e4m3x2_to_f16x2(w.y >> 16));
   }
 }
+// In place: 64 rows x 128 e4m3 codes landed by TMA with the 128-byte swizzle in the upper half of a 16 KB
+// operand (row r's 16-byte chunk k at dst + 8192 + 128 r + 16 (k ^ (r & 7))) -> fp16 values as two
+// 128-byte-swizzled halves [2][64][64] at dst.  Thread `row` converts its row: it reads the whole row of
+// codes first, so its writes to half 1 (the same 128 bytes) cannot overwrite codes not yet read, and no
+// other thread reads them.
+__device__ __forceinline__ void codes_to_f16_in_place(uint32_t dst, int row) {
+  const uint32_t sw = static_cast<uint32_t>(row & 7);
+  const uint32_t raw = dst + 8192 + static_cast<uint32_t>(row) * 128;
+  uint32_t c[8][4];
+#pragma unroll
+  for (int k = 0; k < 8; ++k)
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(c[k][0]), "=r"(c[k][1]), "=r"(c[k][2]), "=r"(c[k][3])
+                 : "r"(raw + ((static_cast<uint32_t>(k) ^ sw) << 4))
+                 : "memory");
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    // codes 16k .. 16k + 15 are dims 16k .. 16k + 15: half k / 4, 16-byte chunks 2 (k % 4) and 2 (k % 4) + 1
+    const uint32_t base = dst + static_cast<uint32_t>(k >> 2) * 8192 + static_cast<uint32_t>(row) * 128;
+    const uint32_t c0 = 2u * static_cast<uint32_t>(k & 3);
+    st_shared_v4(base + ((c0 ^ sw) << 4), e4m3x2_to_f16x2(c[k][0]), e4m3x2_to_f16x2(c[k][0] >> 16),
+                 e4m3x2_to_f16x2(c[k][1]), e4m3x2_to_f16x2(c[k][1] >> 16));
+    st_shared_v4(base + (((c0 + 1) ^ sw) << 4), e4m3x2_to_f16x2(c[k][2]), e4m3x2_to_f16x2(c[k][2] >> 16),
+                 e4m3x2_to_f16x2(c[k][3]), e4m3x2_to_f16x2(c[k][3] >> 16));
+  }
+}
 }  // namespace
 
 // ================================================================================================
@@ -231,8 +257,9 @@ int launch_rowmax_fp8(const RowmaxFp8Maps& maps, float* sel, int64_t pitch, int6
 //         partial (acc[128], m, l) per query row, like the tail partial;
 //   NEAR: the routed leaves (bf16 keys and values, by TMA), merged in the epilogue with the far partial and
 //         the tail partial into the normalised output and log-Z.
-// Splitting keeps each pass's shared memory for its own rings: FAR stages the codes four steps ahead and
-// converts them, NEAR holds three pairs of keys and of values in flight.  The merge is the exact
+// Splitting keeps each pass's shared memory for its own rings: FAR lands the codes of a block in the upper
+// half of its fp16 operand slot and converts them in place, three pairs of g and of vbar blocks in flight;
+// NEAR holds three pairs of keys and of values in flight.  The merge is the exact
 // (max, sum) combination the reference applies to its splits (:257-273).
 //
 // Within a pass: one CTA per 64-row tile; steps of 64 columns taken in pairs: the MMAs of steps 2p and
@@ -242,11 +269,11 @@ int launch_rowmax_fp8(const RowmaxFp8Maps& maps, float* sel, int64_t pitch, int6
 // per step parity) and running (max, sum); the lazy maximum is rescaled only when it grew by more than 2^8.
 // The FAR pass pads its steps to an even count (the extra block lies past nb and is masked).
 //
-// Warp roles.  Both passes: warp 0 X producer (tile rows; FAR: block parameters and raw g codes, NEAR:
+// Warp roles.  Both passes: warp 0 X producer (tile rows; FAR: block parameters and g codes, NEAR:
 // routed keys), warp 1 PV issuer (+ TMEM owner), warp 2 QK issuer, warps 4-7 and 8-11 the softmax
-// warpgroups.  FAR: warp 3 per-column constants, warps 12-13 convert g codes, warps 14-15 load and convert
-// vbar codes (512 threads, warpgroup-aligned setmaxnreg).  NEAR: warp 3 loads the routed values (384
-// threads).
+// warpgroups.  FAR: warp 3 per-column constants, warps 12-13 convert g codes, warps 14-15 load (two pairs
+// ahead) and convert vbar codes (512 threads, warpgroup-aligned setmaxnreg).  NEAR: warp 3 loads the
+// routed values (384 threads).
 namespace {
 namespace tfx {
 constexpr uint32_t kOpBytes = 16384;                     // 2 halves x 64 rows x 128 B
@@ -260,17 +287,13 @@ constexpr uint32_t kTmemCols = 512;
 template <bool FAR>
 struct Cfg {
   static constexpr int kThreads = FAR ? 512 : 384;
-  static constexpr int kXP = FAR ? 2 : 3;                // X ring: pairs
-  static constexpr int kYP = FAR ? 2 : 3;                // Y ring: pairs
-  static constexpr int kRG = FAR ? 4 : 0;                // raw g code slots (steps)
-  static constexpr int kRV = FAR ? 4 : 0;                // raw vbar code slots (steps)
+  static constexpr int kXP = 3;                          // X ring: pairs
+  static constexpr int kYP = 3;                          // Y ring: pairs
   static constexpr uint32_t kXSub = kOpBytes + (FAR ? 1024 : 0);   // far: + lz[64], sg[64], sv[64], excl[64]
   static constexpr uint32_t kOffQ = 0;                   // FAR: fp16 offsets; NEAR: bf16 rows
   static constexpr uint32_t kOffX = kOpBytes;            // [pair slot][step parity] x kXSub
   static constexpr uint32_t kOffY = kOffX + 2 * kXP * kXSub;
-  static constexpr uint32_t kOffRawG = kOffY + 2 * kYP * kOpBytes;
-  static constexpr uint32_t kOffRawV = kOffRawG + kRG * kRawBytes;
-  static constexpr uint32_t kOffCC = kOffRawV + kRV * kRawBytes;   // FAR: [warpgroup][parity][64] float2
+  static constexpr uint32_t kOffCC = kOffY + 2 * kYP * kOpBytes;  // FAR: [warpgroup][parity][64] float2
   static constexpr uint32_t kOffCS = kOffCC + (FAR ? 4 * 64 * 8 : 0);   // FAR: sv
   static constexpr uint32_t kOffEpi = kOffCS + (FAR ? 4 * 64 * 4 : 0);  // m, l of warpgroup 1
   static constexpr uint32_t kOffIdx = kOffEpi + 2 * 128 * 4;           // NEAR: [kMaxKx] uint16
@@ -282,13 +305,11 @@ struct Cfg {
 
 struct Bars {
   uint64_t qd_full;
-  uint64_t x_full[3];     // X producer (arrive + bytes) [+ 64 g converter threads]
+  uint64_t x_full[3];     // NEAR: X producer (arrive + bytes); FAR: 64 g converter threads
   uint64_t x_empty[3];    // QK commit [+ 32 constant lanes]
   uint64_t y_full[3];     // NEAR: Y producer (arrive + bytes); FAR: 64 vbar converter threads
-  uint64_t rg_full[4];
-  uint64_t rg_empty[4];   // 64 g converter threads
-  uint64_t rv_full[4];
-  uint64_t rv_empty[4];   // 64 vbar converter threads
+  uint64_t xr_full[3];    // FAR: g codes and block parameters landed (X producer: arrive + bytes)
+  uint64_t yr_full[3];    // FAR: vbar codes landed (vbar loader: arrive + bytes)
   uint64_t cc_full[2];    // 32 constant lanes
   uint64_t cc_empty[2];   // 128 softmax threads of the pair's warpgroup
   uint64_t s_full[4];     // QK of the pair done
@@ -332,17 +353,13 @@ __global__ void __launch_bounds__(tfx::Cfg<FAR>::kThreads, 1)
   if (threadIdx.x == 0) {
     mbar_init(&bars->qd_full, 1);
     for (int s = 0; s < C::kXP; ++s) {
-      mbar_init(&bars->x_full[s], FAR ? 1 + 64 : 1);
+      mbar_init(&bars->x_full[s], FAR ? 64 : 1);
       mbar_init(&bars->x_empty[s], FAR ? 1 + 32 : 1);
+      mbar_init(&bars->xr_full[s], 1);
     }
-    for (int s = 0; s < C::kYP; ++s) mbar_init(&bars->y_full[s], FAR ? 64 : 1);
-    for (int s = 0; s < C::kRG; ++s) {
-      mbar_init(&bars->rg_full[s], 1);
-      mbar_init(&bars->rg_empty[s], 64);
-    }
-    for (int s = 0; s < C::kRV; ++s) {
-      mbar_init(&bars->rv_full[s], 1);
-      mbar_init(&bars->rv_empty[s], 64);
+    for (int s = 0; s < C::kYP; ++s) {
+      mbar_init(&bars->y_full[s], FAR ? 64 : 1);
+      mbar_init(&bars->yr_full[s], 1);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bars->cc_full[s], 32);
@@ -388,39 +405,26 @@ __global__ void __launch_bounds__(tfx::Cfg<FAR>::kThreads, 1)
         mbar_arrive_expect_tx(&bars->qd_full, kOpBytes);
         tma_load_3d(smem + C::kOffQ, &tm_q, &bars->qd_full, 0, static_cast<int>((t0 + tloc) * 64), 0, pol_stream);
       }
-      int jr = 0;                               // FAR: next block whose raw g codes are to be loaded
       for (int p = 0; p < np; ++p) {
-        if constexpr (FAR) {
-          // raw g codes up to kRG blocks ahead of this pair (slot j % kRG, freed by the g converters)
-          bool ok = true;
-          for (; ok && jr < total && jr < 2 * p + C::kRG; ++jr) {
-            const int rs = jr % C::kRG;
-            if (jr >= C::kRG) ok = mbar_wait_warp(&bars->rg_empty[rs], ((jr / C::kRG) - 1) & 1, status, abort_flag);
-            if (ok && leader) {
-              mbar_arrive_expect_tx(&bars->rg_full[rs], kRawBytes);
-              tma_load_3d(smem + C::kOffRawG + rs * kRawBytes, &tm_graw, &bars->rg_full[rs], 0, jr * 64, srow,
-                          pol_stream);
-            }
-            __syncwarp();
-          }
-          if (!ok) break;
-        }
         const int xs = p % C::kXP;
         if (p >= C::kXP && !mbar_wait_warp(&bars->x_empty[xs], ((p / C::kXP) - 1) & 1, status, abort_flag)) break;
         if (leader) {
           uint32_t tx = 0;
           for (int x = 0; x < 2; ++x)
-            if (2 * p + x < total) tx += FAR ? 3 * 256 + 64 : kOpBytes;
-          mbar_arrive_expect_tx(&bars->x_full[xs], tx);
+            if (2 * p + x < total) tx += FAR ? kRawBytes + 3 * 256 + 64 : kOpBytes;
+          uint64_t* bar = FAR ? &bars->xr_full[xs] : &bars->x_full[xs];
+          mbar_arrive_expect_tx(bar, tx);
           for (int x = 0; x < 2; ++x) {
             const int j = 2 * p + x;
             if (j >= total) continue;
             uint8_t* xp = xsub(p, x);
             if constexpr (FAR) {
-              tma_load_2d(xp + kOpBytes, &tm_lz, &bars->x_full[xs], j * 64, srow, pol_stream);
-              tma_load_2d(xp + kOpBytes + 256, &tm_sg, &bars->x_full[xs], j * 64, srow, pol_stream);
-              tma_load_2d(xp + kOpBytes + 512, &tm_sv, &bars->x_full[xs], j * 64, srow, pol_stream);
-              tma_load_2d(xp + kOpBytes + 768, &tm_excl, &bars->x_full[xs], j * 64, srow, pol_stream);
+              // the block's g codes into the upper half of its operand slot (converted there in place)
+              tma_load_3d(xp + kOpBytes / 2, &tm_graw, bar, 0, j * 64, srow, pol_stream);
+              tma_load_2d(xp + kOpBytes, &tm_lz, bar, j * 64, srow, pol_stream);
+              tma_load_2d(xp + kOpBytes + 256, &tm_sg, bar, j * 64, srow, pol_stream);
+              tma_load_2d(xp + kOpBytes + 512, &tm_sv, bar, j * 64, srow, pol_stream);
+              tma_load_2d(xp + kOpBytes + 768, &tm_excl, bar, j * 64, srow, pol_stream);
             } else {
               tma_load_3d(xp, &tm_k, &bars->x_full[xs], 0, idx_s[j] * 64, 0, pol_keep);
             }
@@ -484,7 +488,7 @@ __global__ void __launch_bounds__(tfx::Cfg<FAR>::kThreads, 1)
       // (sg * log2 e, lz * log2 e or -inf if routed / past nb) and sv
       for (int p = 0; p < np; ++p) {
         const int xs = p % C::kXP, cs_slot = p & 1;
-        if (!mbar_wait_warp(&bars->x_full[xs], (p / C::kXP) & 1, status, abort_flag)) break;
+        if (!mbar_wait_warp(&bars->xr_full[xs], (p / C::kXP) & 1, status, abort_flag)) break;
         if (p >= 2 && !mbar_wait_warp(&bars->cc_empty[cs_slot], ((p >> 1) - 1) & 1, status, abort_flag)) break;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -714,61 +718,47 @@ __global__ void __launch_bounds__(tfx::Cfg<FAR>::kThreads, 1)
   } else if constexpr (FAR) {
     // ------------------------------------------------------------------ code converters (FAR)
     asm volatile("setmaxnreg.dec.sync.aligned.u32 72;");
-    const uint64_t pol_stream = policy_evict_first();
     if (warp < 14) {
-      // g codes -> fp16 X operand of each block
-      const int tid = threadIdx.x - 384;
+      // g codes -> fp16 X operand of each block, in place, once they landed
+      const int row = threadIdx.x - 384;
       for (int p = 0; p < np; ++p) {
         const int xs = p % C::kXP;
-        if (p >= C::kXP && !mbar_wait_warp(&bars->x_empty[xs], ((p / C::kXP) - 1) & 1, status, abort_flag)) break;
-        bool ok = true;
-        for (int x = 0; x < 2 && ok; ++x) {
-          const int j = 2 * p + x, rs = j % C::kRG;
-          ok = mbar_wait_warp(&bars->rg_full[rs], (j / C::kRG) & 1, status, abort_flag);
-          if (ok) {
-            codes_to_f16<64, 64>(smem + C::kOffRawG + rs * kRawBytes, smem_u32(xsub(p, x)), tid);
-            mbar_arrive(&bars->rg_empty[rs]);
-          }
-        }
-        if (!ok) break;
+        if (!mbar_wait_warp(&bars->xr_full[xs], (p / C::kXP) & 1, status, abort_flag)) break;
+        codes_to_f16_in_place(smem_u32(xsub(p, 0)), row);
+        codes_to_f16_in_place(smem_u32(xsub(p, 1)), row);
         fence_proxy_async_smem();        // the fp16 operand is read by the tensor cores (async proxy)
         mbar_arrive(&bars->x_full[xs]);
       }
     } else {
-      // raw vbar codes kRV blocks ahead (TMA), converted into the pair's Y slot once PV(p - kYP) freed it
-      const int tid = threadIdx.x - 448;
+      // vbar codes into the upper halves of the pair's Y slots, issued two pairs ahead (the slot of pair
+      // p + 2 is freed by PV(p - 1)), then converted in place
+      const int row = threadIdx.x - 448;
       const uint32_t leader = elect_one() && warp == 14;      // one issuing lane for the two warps
-      int jr = 0;
-      bool ok = true;
-      auto load_raw = [&](int upto) {
-        for (; ok && jr < total && jr < upto; ++jr) {
-          const int rs = jr % C::kRV;
-          if (jr >= C::kRV) ok = mbar_wait_warp(&bars->rv_empty[rs], ((jr / C::kRV) - 1) & 1, status, abort_flag);
-          if (ok && leader) {
-            mbar_arrive_expect_tx(&bars->rv_full[rs], kRawBytes);
-            tma_load_3d(smem + C::kOffRawV + rs * kRawBytes, &tm_vraw, &bars->rv_full[rs], 0, jr * 64, srow,
-                        pol_stream);
-          }
-          __syncwarp();
-        }
-      };
-      for (int p = 0; ok && p < np; ++p) {
-        load_raw(2 * p + C::kRV);
-        if (!ok) break;
+      const uint64_t pol_stream = policy_evict_first();
+      auto load = [&](int p) -> bool {
+        if (p >= np) return true;
+        const int ys = p % C::kYP;
         if (p >= C::kYP &&
             !mbar_wait_warp(&bars->pv_done[(p - C::kYP) & 3], ((p - C::kYP) >> 2) & 1, status, abort_flag))
-          break;
-        for (int x = 0; x < 2 && ok; ++x) {
-          const int j = 2 * p + x, rs = j % C::kRV;
-          ok = mbar_wait_warp(&bars->rv_full[rs], (j / C::kRV) & 1, status, abort_flag);
-          if (ok) {
-            codes_to_f16<64, 64>(smem + C::kOffRawV + rs * kRawBytes, smem_u32(ysub(p, x)), tid);
-            mbar_arrive(&bars->rv_empty[rs]);
-          }
+          return false;
+        if (leader) {
+          mbar_arrive_expect_tx(&bars->yr_full[ys], 2 * kRawBytes);
+          for (int x = 0; x < 2; ++x)
+            tma_load_3d(ysub(p, x) + kOpBytes / 2, &tm_vraw, &bars->yr_full[ys], 0, (2 * p + x) * 64, srow,
+                        pol_stream);
         }
-        if (!ok) break;
+        __syncwarp();
+        return true;
+      };
+      bool ok = load(0) && load(1);
+      for (int p = 0; ok && p < np; ++p) {
+        if (!load(p + 2)) break;
+        const int ys = p % C::kYP;
+        if (!mbar_wait_warp(&bars->yr_full[ys], (p / C::kYP) & 1, status, abort_flag)) break;
+        codes_to_f16_in_place(smem_u32(ysub(p, 0)), row);
+        codes_to_f16_in_place(smem_u32(ysub(p, 1)), row);
         fence_proxy_async_smem();
-        mbar_arrive(&bars->y_full[p % C::kYP]);
+        mbar_arrive(&bars->y_full[ys]);
       }
     }
   }

@@ -43,7 +43,7 @@ struct RowmaxFp8Maps {
 
 struct TileFp8Maps {
   CUtensorMap qb, dqh;        // [nt*64, 128] bf16 / fp16 as [2][rows][64], box (64, 64, 2), 128B swizzle
-  CUtensorMap graw, vraw;     // [tc, nb, 128] e4m3 codes of g / vbar, box (128, 64, 1), no swizzle
+  CUtensorMap graw, vraw;     // [tc, nb, 128] e4m3 codes of g / vbar, box (128, 64, 1), 128B swizzle
   CUtensorMap lz, sg, sv;     // [tc, nb] f32 (row pitch P), box (64, 1)
   CUtensorMap excl;           // [tc, nb] u8 (row pitch P), box (64, 1)
   CUtensorMap k, v;           // [M, 128] bf16 as [2][M][64], box (64, 64, 2), 128B swizzle

@@ -128,7 +128,8 @@ def _synthetic(n, m, seed):
 @pytest.mark.parametrize("n,m,E,sink,n_tail", [(4096, 8192, 16, 1, 0),     # 2 far steps + 17 near: 19 steps
                                                (3000, 32768, 61, 2, 5),    # 8 far blocks, ragged tiles, tail
                                                (1024, 64 * 130, 0, 0, 0),  # far field only (3 far steps)
-                                               (640, 4096, 64, 0, 0)])     # everything routed: near only
+                                               (640, 4096, 64, 0, 0),      # everything routed: near only
+                                               (2048, 8192, 8, 0, 20)])    # a float32 tail (> 16 keys)
 def test_fp8_tile_kernel_on_device_state(dev, n, m, E, sink, n_tail):
     """Fed the device's own state and routing, the fp8 tile kernel reproduces the oracle's fp8 tile
     attention (weights rounded against the row's final maximum) within the fp16-weight rounding, and
