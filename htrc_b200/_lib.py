@@ -36,7 +36,7 @@ class HtrcFlatArgs(ctypes.Structure):
         ("workspace", _p), ("workspace_bytes", ctypes.c_size_t),
         ("out", _p), ("lse", _p),
         ("stage_events", ctypes.POINTER(_p)), ("n_stage_events", _i32),
-        ("group", _i32), ("order", _i32), ("curvature", _i32), ("store", _i32),
+        ("group", _i32), ("order", _i32), ("curvature", _i32), ("store", _i32), ("qk_scale_block", _i32),
     ]
 
 
@@ -57,6 +57,9 @@ SIGNATURES = {
     "htrc_tile_attention": (ctypes.c_int, [_p, _p, _p, _p, _i64, _i32, _i64, _i64, _i32, _p, _p, _p, _p, _p, _p, _i32,
                                            _i64, _p, _p, _p, _i64, _i32, _i32, _f32, _p, _p, _p, _p, _p, _p, _p, _p]),
     "htrc_tail_partial": (ctypes.c_int, [_p, _i32, _i64, _i32, _p, _p, _i32, _f32, _p, _p]),
+    "htrc_pack_int8_blocks": (ctypes.c_int, [_p, _i32, _i64, _i32, _i32, _i32, _p, _p, _p, _p]),
+    "htrc_tile_prep_ex": (ctypes.c_int, [_p, _i32, _i64, _i32, _i32, _p, _i32, _p, _p, _p, _p, _p, _p, _p, _p, _i32,
+                                         _p]),
     "htrc_tile_prep_fp8": (ctypes.c_int, [_p, _i32, _i64, _i32, _i32, _p, _i32, _p, _p, _p, _p, _p, _p]),
     "htrc_leaf_stats_fp8": (ctypes.c_int, [_p, _p, _i64, _i64, _i64, _p, _p, _i64, _i32, _i32, _f32, _p, _p, _p, _p, _p,
                                            _p, _p]),

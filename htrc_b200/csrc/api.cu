@@ -158,6 +158,8 @@ int validate(const HtrcFlatArgs* a, bool need_ptrs) {
   if (a->curvature != HTRC_CURV_LIN && a->curvature != HTRC_CURV_ISO) return HTRC_ERR_ARG;
   if (a->store != HTRC_STORE_INT8 && a->store != HTRC_STORE_FP8) return HTRC_ERR_ARG;
   if (a->store == HTRC_STORE_FP8 && a->curvature != HTRC_CURV_LIN) return HTRC_ERR_UNSUPPORTED;
+  if (a->qk_scale_block != 0 && a->qk_scale_block != 64) return HTRC_ERR_ARG;
+  if (a->qk_scale_block != 0 && a->store != HTRC_STORE_INT8) return HTRC_ERR_UNSUPPORTED;
   if (a->n_queries > (int64_t(1) << 31) - 1) return HTRC_ERR_UNSUPPORTED;
   const int64_t nb = a->n_keys / a->leaf;
   if (nb > kMaxLeaves) return HTRC_ERR_UNSUPPORTED;
@@ -369,11 +371,14 @@ int htrc_flat_forward(const HtrcFlatArgs* a, htrc_stream_t stream) {
   float* dd = L.iso ? at<float>(ws, L.dd) : nullptr;
   float* cv = L.iso ? at<float>(ws, L.cv) : nullptr;
   float* sv = L.fp8 ? at<float>(ws, L.sv) : nullptr;
-  if (!L.fp8) launch_pack_rows(a->k, HTRC_DTYPE_BF16, L.m, HTRC_ROUND_HALF_EVEN, k8, ks, kn2, st);
+  if (!L.fp8 && a->qk_scale_block)
+    launch_pack_blocks(a->k, HTRC_DTYPE_BF16, L.m, HTRC_ROUND_HALF_EVEN, k8, ks, kn2, st);
+  else if (!L.fp8)
+    launch_pack_rows(a->k, HTRC_DTYPE_BF16, L.m, HTRC_ROUND_HALF_EVEN, k8, ks, kn2, st);
   if (perm && (rc = launch_kmeans_order(a->q, a->q_dtype, L.n, perm, at<void>(ws, L.km), st)) != HTRC_OK) return rc;
   const int trows = static_cast<int>(L.trows);
   launch_tile_prep(a->q, a->q_dtype, L.n, trows, perm, group, at<float>(ws, L.mu), mu_hi, mu_lo, q8, sq, dq8, sdq, dd,
-                   L.fp8, st);
+                   L.fp8, a->qk_scale_block != 0, st);
   if (tail) launch_tail_partial(a->q, a->q_dtype, L.n, a->tail_k, a->tail_v, a->n_tail, scale, tail, st);
   if (cudaGetLastError() != cudaSuccess) return HTRC_ERR_CUDA;
   mark(1);
@@ -465,8 +470,35 @@ int htrc_tile_prep(const void* q, int32_t q_dtype, int64_t n_queries, int32_t di
   if (group > kMaxGroup) return HTRC_ERR_ARG;
   int rc = check_device();
   if (rc != HTRC_OK) return rc;
-  launch_tile_prep(q, q_dtype, n_queries, tile, perm, group, mu, mu_hi, mu_lo, q8, sq, dq8, sdq, dd, false,
+  launch_tile_prep(q, q_dtype, n_queries, tile, perm, group, mu, mu_hi, mu_lo, q8, sq, dq8, sdq, dd, false, false,
                    reinterpret_cast<cudaStream_t>(stream));
+  return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
+}
+
+int htrc_tile_prep_ex(const void* q, int32_t q_dtype, int64_t n_queries, int32_t dim, int32_t tile,
+                      const int32_t* perm, int32_t group, float* mu, uint16_t* mu_hi, uint16_t* mu_lo, int8_t* q8,
+                      float* sq, int8_t* dq8, float* sdq, float* dd, int32_t q_scale_block, htrc_stream_t stream) {
+  if (q_scale_block != 0 && q_scale_block != 64) return HTRC_ERR_ARG;
+  if (!q || !mu || !mu_hi || !mu_lo || !q8 || !sq || !dq8 || !sdq || n_queries < 1) return HTRC_ERR_ARG;
+  if (dim != kDim || (tile != kTile && tile != kTile / 2)) return HTRC_ERR_UNSUPPORTED;
+  if (q_dtype != HTRC_DTYPE_F32 && q_dtype != HTRC_DTYPE_BF16) return HTRC_ERR_ARG;
+  if (group > kMaxGroup) return HTRC_ERR_ARG;
+  int rc = check_device();
+  if (rc != HTRC_OK) return rc;
+  launch_tile_prep(q, q_dtype, n_queries, tile, perm, group, mu, mu_hi, mu_lo, q8, sq, dq8, sdq, dd, false,
+                   q_scale_block != 0, reinterpret_cast<cudaStream_t>(stream));
+  return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
+}
+
+int htrc_pack_int8_blocks(const void* x, int32_t dtype, int64_t rows, int32_t dim, int32_t rounding,
+                          int32_t block_rows, int8_t* x8, float* scale, float* sqnorm, htrc_stream_t stream) {
+  if (!x || !x8 || !scale || rows < 1) return HTRC_ERR_ARG;
+  if (dim != kDim || block_rows != 64) return HTRC_ERR_UNSUPPORTED;
+  if (dtype != HTRC_DTYPE_F32 && dtype != HTRC_DTYPE_BF16) return HTRC_ERR_ARG;
+  if (rounding != HTRC_ROUND_HALF_EVEN && rounding != HTRC_ROUND_HALF_AWAY) return HTRC_ERR_ARG;
+  int rc = check_device();
+  if (rc != HTRC_OK) return rc;
+  launch_pack_blocks(x, dtype, rows, rounding, x8, scale, sqnorm, reinterpret_cast<cudaStream_t>(stream));
   return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
 }
 
@@ -517,7 +549,7 @@ int htrc_tile_prep_fp8(const void* q, int32_t q_dtype, int64_t n_queries, int32_
   int rc = check_device();
   if (rc != HTRC_OK) return rc;
   launch_tile_prep(q, q_dtype, n_queries, tile, perm, group, mu, mu_hi, mu_lo, reinterpret_cast<int8_t*>(qb), nullptr,
-                   reinterpret_cast<int8_t*>(dqh), nullptr, nullptr, true, reinterpret_cast<cudaStream_t>(stream));
+                   reinterpret_cast<int8_t*>(dqh), nullptr, nullptr, true, false, reinterpret_cast<cudaStream_t>(stream));
   return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
 }
 

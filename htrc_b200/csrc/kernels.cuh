@@ -53,7 +53,9 @@ void launch_pack_rows(const void* x, int dtype, int64_t rows, int rounding, int8
                       cudaStream_t st);
 void launch_tile_prep(const void* q, int dtype, int64_t n, int tile_rows, const int32_t* perm, int group, float* mu,
                       uint16_t* mu_hi, uint16_t* mu_lo, int8_t* q8, float* sq, int8_t* dq8, float* sdq, float* dd,
-                      bool fp8, cudaStream_t st);
+                      bool fp8, bool qblock, cudaStream_t st);
+void launch_pack_blocks(const void* x, int dtype, int64_t rows, int rounding, int8_t* x8, float* scale,
+                        float* sqnorm, cudaStream_t st);
 size_t kmeans_scratch_bytes(int64_t n);
 int launch_kmeans_order(const void* q, int dtype, int64_t n, int32_t* perm, void* scratch, cudaStream_t st);
 void launch_fake_quant(const void* x, int x_dtype, int64_t rows, int fmt, int gsz, void* out, int out_dtype,

@@ -107,6 +107,65 @@ __global__ void __launch_bounds__(256) pack_rows_kernel(const T* __restrict__ x,
   }
 }
 
+// The same codes with one scale per block of 64 consecutive rows (an extension: BASELINE's
+// "per-64-token-block absmax" scales; the reference's are per row): s = max(amax_block|x| * (1/127), 1e-20),
+// written once per row.  One CTA per block; warp w holds rows 8w .. 8w + 7 in registers, the block maximum
+// goes through shared memory.
+template <typename T, int ROUND>
+__global__ void __launch_bounds__(256) pack_blocks_kernel(const T* __restrict__ x, int64_t rows,
+                                                          int8_t* __restrict__ x8, float* __restrict__ scale,
+                                                          float* __restrict__ sqnorm) {
+  __shared__ float bam[8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * 64 + warp * 8;
+  float v[8][4];
+  float am = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    if (r0 + i < rows) {
+      load4<T>(x + (r0 + i) * 128 + lane * 4, v[i]);
+    } else {
+      v[i][0] = v[i][1] = v[i][2] = v[i][3] = 0.f;
+    }
+    am = fmaxf(am, fmaxf(fmaxf(fabsf(v[i][0]), fabsf(v[i][1])), fmaxf(fabsf(v[i][2]), fabsf(v[i][3]))));
+  }
+  am = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(am)));
+  if (lane == 0) bam[warp] = am;
+  __syncthreads();
+  float b = bam[0];
+#pragma unroll
+  for (int w = 1; w < 8; ++w) b = fmaxf(b, bam[w]);
+  const float s = fmaxf(__fmul_rn(b, kInv127), 1e-20f);
+  const float r = __frcp_rn(s);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int64_t row = r0 + i;
+    if (row >= rows) break;                  // warp-uniform
+    reinterpret_cast<uint32_t*>(x8 + row * 128)[lane] = quant4<ROUND>(v[i], s, r);
+    if (lane == 0) scale[row] = s;
+    if (sqnorm != nullptr) {
+      const float n2 = row_sqnorm(v[i]);
+      if (lane == 0) sqnorm[row] = n2;
+    }
+  }
+}
+
+void launch_pack_blocks(const void* x, int dtype, int64_t rows, int rounding, int8_t* x8, float* scale,
+                        float* sqnorm, cudaStream_t st) {
+  const unsigned grid = static_cast<unsigned>((rows + 63) / 64);
+  if (dtype == HTRC_DTYPE_BF16) {
+    if (rounding == HTRC_ROUND_HALF_EVEN)
+      pack_blocks_kernel<uint16_t, 0><<<grid, 256, 0, st>>>(static_cast<const uint16_t*>(x), rows, x8, scale, sqnorm);
+    else
+      pack_blocks_kernel<uint16_t, 1><<<grid, 256, 0, st>>>(static_cast<const uint16_t*>(x), rows, x8, scale, sqnorm);
+  } else {
+    if (rounding == HTRC_ROUND_HALF_EVEN)
+      pack_blocks_kernel<float, 0><<<grid, 256, 0, st>>>(static_cast<const float*>(x), rows, x8, scale, sqnorm);
+    else
+      pack_blocks_kernel<float, 1><<<grid, 256, 0, st>>>(static_cast<const float*>(x), rows, x8, scale, sqnorm);
+  }
+}
+
 void launch_pack_rows(const void* x, int dtype, int64_t rows, int rounding, int8_t* x8, float* scale,
                       float* sqnorm, cudaStream_t st) {
   const unsigned grid = static_cast<unsigned>((rows + 7) / 8);
@@ -170,7 +229,9 @@ __global__ void __launch_bounds__(128) group_centre_kernel(const T* __restrict__
 
 // One CTA (4 warps) per tile of T query rows (held as 64 rows): the tile's centre (group 1; else the
 // group centre written by group_centre_kernel) and the codes of its rows and of their offsets from
-// the centre.  FP8 (the fp8 state path, h3/htrc_flat_triton.py:103-109) writes instead the rows as bf16
+// the centre.  qblock (an extension): one scale for the codes of all 64 held rows, from the tile's
+// abs-max (the held rows repeat real rows, so it is the maximum over the tile's queries); the offsets'
+// codes keep per-row scales.  FP8 (the fp8 state path, h3/htrc_flat_triton.py:103-109) writes instead the rows as bf16
 // (q8 holds uint16 bf16 rows) and the float32 offsets rounded once to fp16 (dq8 holds uint16 fp16 rows);
 // sq / sdq are not written.
 template <typename T, bool FP8>
@@ -179,9 +240,10 @@ __global__ void __launch_bounds__(128) tile_prep_kernel(const T* __restrict__ q,
                                                         uint16_t* __restrict__ mu_hi, uint16_t* __restrict__ mu_lo,
                                                         int8_t* __restrict__ q8, float* __restrict__ sq,
                                                         int8_t* __restrict__ dq8, float* __restrict__ sdq,
-                                                        float* __restrict__ dd) {
+                                                        float* __restrict__ dd, int qblock) {
   __shared__ float qs[64][129];
   __shared__ float mus[128];
+  __shared__ float tmx[4];
   const int t = blockIdx.x;
   const int tid = threadIdx.x;
   const int64_t r0 = static_cast<int64_t>(t) * 64;              // first of the tile's 64 held rows
@@ -216,6 +278,15 @@ __global__ void __launch_bounds__(128) tile_prep_kernel(const T* __restrict__ q,
   float m4[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) m4[i] = mus[lane * 4 + i];
+  float tq = 0.f;                            // qblock: the tile's abs-max (thread = column, then CTA)
+  if (qblock) {
+    float cm = 0.f;
+    for (int r = 0; r < 64; ++r) cm = fmaxf(cm, fabsf(qs[r][tid]));
+    cm = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(cm)));
+    if (lane == 0) tmx[warp] = cm;
+    __syncthreads();
+    tq = fmaxf(fmaxf(tmx[0], tmx[1]), fmaxf(tmx[2], tmx[3]));
+  }
 #pragma unroll 4
   for (int r = warp; r < 64; r += 4) {
     float v[4], d[4];
@@ -234,7 +305,7 @@ __global__ void __launch_bounds__(128) tile_prep_kernel(const T* __restrict__ q,
     float ad = fmaxf(fmaxf(fabsf(d[0]), fabsf(d[1])), fmaxf(fabsf(d[2]), fabsf(d[3])));
     aq = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(aq)));
     ad = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(ad)));
-    const float s_q = fmaxf(__fmul_rn(aq, kInv127), 1e-20f);
+    const float s_q = fmaxf(__fmul_rn(qblock ? tq : aq, kInv127), 1e-20f);
     const float s_d = fmaxf(__fmul_rn(ad, kInv127), 1e-20f);
     reinterpret_cast<uint32_t*>(q8 + gr * 128)[lane] = quant4<1>(v, s_q, __frcp_rn(s_q));
     reinterpret_cast<uint32_t*>(dq8 + gr * 128)[lane] = quant4<1>(d, s_d, __frcp_rn(s_d));
@@ -251,7 +322,7 @@ __global__ void __launch_bounds__(128) tile_prep_kernel(const T* __restrict__ q,
 
 void launch_tile_prep(const void* q, int dtype, int64_t n, int tile_rows, const int32_t* perm, int group, float* mu,
                       uint16_t* mu_hi, uint16_t* mu_lo, int8_t* q8, float* sq, int8_t* dq8, float* sdq, float* dd,
-                      bool fp8, cudaStream_t st) {
+                      bool fp8, bool qblock, cudaStream_t st) {
   const int tr = tile_rows == 32 ? 32 : 64;
   const int64_t nt = (n + tr - 1) / tr;
   const int g = group > 1 ? group : 1;
@@ -260,12 +331,14 @@ void launch_tile_prep(const void* q, int dtype, int64_t n, int tile_rows, const 
     const uint16_t* qb = static_cast<const uint16_t*>(q);
     if (g > 1) group_centre_kernel<uint16_t><<<ng, 128, 0, st>>>(qb, perm, n, tr, nt, g, mu, mu_hi, mu_lo);
     auto k = fp8 ? tile_prep_kernel<uint16_t, true> : tile_prep_kernel<uint16_t, false>;
-    k<<<static_cast<unsigned>(nt), 128, 0, st>>>(qb, perm, n, tr, g, mu, mu_hi, mu_lo, q8, sq, dq8, sdq, dd);
+    k<<<static_cast<unsigned>(nt), 128, 0, st>>>(qb, perm, n, tr, g, mu, mu_hi, mu_lo, q8, sq, dq8, sdq, dd,
+                                                 qblock ? 1 : 0);
   } else {
     const float* qf = static_cast<const float*>(q);
     if (g > 1) group_centre_kernel<float><<<ng, 128, 0, st>>>(qf, perm, n, tr, nt, g, mu, mu_hi, mu_lo);
     auto k = fp8 ? tile_prep_kernel<float, true> : tile_prep_kernel<float, false>;
-    k<<<static_cast<unsigned>(nt), 128, 0, st>>>(qf, perm, n, tr, g, mu, mu_hi, mu_lo, q8, sq, dq8, sdq, dd);
+    k<<<static_cast<unsigned>(nt), 128, 0, st>>>(qf, perm, n, tr, g, mu, mu_hi, mu_lo, q8, sq, dq8, sdq, dd,
+                                                 qblock ? 1 : 0);
   }
 }
 

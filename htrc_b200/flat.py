@@ -21,7 +21,9 @@ by the reference's k-means permutation before tiling and writes the output back 
 expansion centre, far-field state and routing (:223-231).
 
 Additions over the reference: ``return_lse=True`` also returns the log-partition per query
-(logit units, scale * q.k), and ``backend`` accepts "cuda"/"b200" as names of the same path.
+(logit units, scale * q.k), ``backend`` accepts "cuda"/"b200" as names of the same path, and
+``qk_scale_block=64`` gives the INT8 keys one scale per 64-key leaf and the query rows one per tile
+(BASELINE's "per-64-token-block absmax" scales; the reference's are per key and per row, the default).
 """
 from __future__ import annotations
 
@@ -114,6 +116,16 @@ def _check_args(q, k, v, tile, exact_leaves, order, curvature, leaf, select, bac
         raise ValueError("q, k, v must be CUDA tensors (there is no CPU path)")
 
 
+def _check_scale_block(qk_scale_block, store):
+    """qk_scale_block: None/0 (the reference's per-key and per-row INT8 scales) or 64 (one per leaf / tile)."""
+    b = int(qk_scale_block or 0)
+    if b not in (0, 64):
+        raise ValueError("qk_scale_block must be None, 0 or 64")
+    if b and store != "int8":
+        raise NotImplementedError("qk_scale_block applies to the INT8 query and key codes (store='int8')")
+    return b
+
+
 def fake_quant(x, fmt, group=0, out_dtype=torch.float32):
     """Round-trip x [..., 128] (CUDA, f32 or bf16) through a low-bit format with symmetric per-group
     scales (group 0: one scale per row; fp4: 16) -- h3/htrc_flat.py:68-97, on the device.  fmt: int8,
@@ -188,7 +200,7 @@ def curvature_code(curvature) -> int:
 
 def _args(qd, kb, vb, tk, tv, exact_leaves, sink_leaves, tile_chunk, scale, out=None, lse=None, ws=None,
           stage_events=None, group=1, order=_lib.ORDER_SEQ, tile=TILE, curvature=_lib.CURV_LIN,
-          store=_lib.STORE_INT8):
+          store=_lib.STORE_INT8, qk_scale_block=0):
     a = _lib.HtrcFlatArgs()
     a.q = ptr(qd)
     a.q_dtype = _lib.DTYPE_BF16 if qd.dtype == torch.bfloat16 else _lib.DTYPE_F32
@@ -202,6 +214,7 @@ def _args(qd, kb, vb, tk, tv, exact_leaves, sink_leaves, tile_chunk, scale, out=
     a.n_tail = int(tk.shape[0]) if tk is not None else 0
     a.out, a.lse = ptr(out), ptr(lse)
     a.group, a.order, a.curvature, a.store = int(group), int(order), int(curvature), int(store)
+    a.qk_scale_block = int(qk_scale_block or 0)
     if ws is not None:
         a.workspace, a.workspace_bytes = ptr(ws), int(ws.numel())
     if stage_events:
@@ -253,14 +266,14 @@ def _workspace(ws, nbytes, device):
 
 def forward_into(qd, kb, vb, tk, tv, *, exact_leaves, sink_leaves=0, tile_chunk=0, scale=None, out, lse=None,
                  workspace, stream=None, stage_events=None, group=1, order=_lib.ORDER_SEQ, tile=TILE,
-                 curvature=_lib.CURV_LIN, store=_lib.STORE_INT8):
+                 curvature=_lib.CURV_LIN, store=_lib.STORE_INT8, qk_scale_block=0):
     """One head through ``htrc_flat_forward`` into caller-provided buffers (no allocation; CUDA-graph
     capturable).  qd [N, 128] f32/bf16, kb/vb [M, 128] bf16, out [N, 128] f32, lse [N] f32 or None;
     stage_events: optional list of torch.cuda.Event recorded between the stages (see
     include/htrc_flat.h); group / order: ``group_of(kern)`` / ``order_code(order)``; tile: 64 or 32;
-    store: ``_lib.STORES[store]``."""
+    store: ``_lib.STORES[store]``; qk_scale_block: 0 or 64."""
     a = _args(qd, kb, vb, tk, tv, exact_leaves, sink_leaves, tile_chunk, scale, out, lse, workspace, stage_events,
-              group, order, tile, curvature, store)
+              group, order, tile, curvature, store, qk_scale_block)
     check(lib().htrc_flat_forward(a, stream_ptr(stream)), "htrc_flat_forward")
 
 
@@ -282,17 +295,18 @@ def flat_attention(q, k, v, *, tile=64, exact_leaves=64, order="seq", curvature=
                    tile_chunk=32, precision="fp32", leaf=16, scale=None, prof=None,
                    select="max", backend="torch", store="fp32", splits=8, dot="tf32",
                    sel_stride=1, kern=None, quant=None, sink_leaves=0, tail=None, ws=None,
-                   return_lse=False):
+                   return_lse=False, qk_scale_block=None):
     """q [N, 128], k/v [M, 128] on a CUDA device -> out [N, 128] float32 (and lse [N] with
     return_lse).  Signature and defaults of the reference (h3/htrc_flat.py:99-103); see PROD."""
     _check_args(q, k, v, tile, exact_leaves, order, curvature, leaf, select, backend, store, dot,
                 sel_stride, quant, sink_leaves, tail)
+    qsb = _check_scale_block(qk_scale_block, store)
     qd, kb, vb, tk, tv = _prep_inputs(q, k, v, tail, quant)
     grp, oc, cc, sc = group_of(kern), order_code(order), curvature_code(curvature), _lib.STORES[store]
     if prof is not None:
         st = run_stages(qd, kb, vb, tk, tv, exact_leaves=exact_leaves, sink_leaves=sink_leaves,
                         tile_chunk=tile_chunk, scale=scale, prof=prof, group=grp, order=oc, tile=tile, curvature=cc,
-                        store=sc)
+                        store=sc, qk_scale_block=qsb)
         return (st["out"], st["lse"]) if return_lse else st["out"]
     n = int(qd.shape[0])
     out = torch.empty((n, DIM), dtype=torch.float32, device=q.device)
@@ -302,7 +316,7 @@ def flat_attention(q, k, v, *, tile=64, exact_leaves=64, order="seq", curvature=
     w = _workspace(ws, nbytes, q.device)
     forward_into(qd, kb, vb, tk, tv, exact_leaves=exact_leaves, sink_leaves=sink_leaves,
                  tile_chunk=tile_chunk, scale=scale, out=out, lse=lse, workspace=w, group=grp, order=oc, tile=tile,
-                 curvature=cc, store=sc)
+                 curvature=cc, store=sc, qk_scale_block=qsb)
     return (out, lse) if return_lse else out
 
 
@@ -314,7 +328,7 @@ def flat_attention_prod(q, k, v, **over):
 @torch.inference_mode()
 def run_stages(qd, kb, vb, tk=None, tv=None, *, exact_leaves, sink_leaves=0, tile_chunk=0, scale=None,
                prof=None, stream=None, group=1, order=_lib.ORDER_SEQ, tile=TILE, curvature=_lib.CURV_LIN,
-               store=_lib.STORE_INT8):
+               store=_lib.STORE_INT8, qk_scale_block=0):
     """The same operator launched stage by stage through the C ABI's stage entry points, returning
     every intermediate (perm, k8, ks, mu, q8, sq, dq8, sdq, g8, sg, lz, vb, sel, idx, excl, out, lse; with
     store=STORE_FP8: perm, mu, qb, dqh, g8 / vb8 e4m3 codes, sg, sv, lz, sel, idx, excl, out, lse).
@@ -352,8 +366,12 @@ def run_stages(qd, kb, vb, tk=None, tv=None, *, exact_leaves, sink_leaves=0, til
     iso = curvature == _lib.CURV_ISO
     r.update(kn2=e(m) if iso else None, dd=e(nt * TILE) if iso else None, cv=e(ng, pitch) if iso else None)
     stp = ptr(r["status"])
-    check(L.htrc_pack_int8(ptr(kb), _lib.DTYPE_BF16, m, DIM, _lib.ROUND_HALF_EVEN, ptr(r["k8"]), ptr(r["ks"]),
-                           ptr(r["kn2"]), s), "htrc_pack_int8")
+    if qk_scale_block:
+        check(L.htrc_pack_int8_blocks(ptr(kb), _lib.DTYPE_BF16, m, DIM, _lib.ROUND_HALF_EVEN, int(qk_scale_block),
+                                      ptr(r["k8"]), ptr(r["ks"]), ptr(r["kn2"]), s), "htrc_pack_int8_blocks")
+    else:
+        check(L.htrc_pack_int8(ptr(kb), _lib.DTYPE_BF16, m, DIM, _lib.ROUND_HALF_EVEN, ptr(r["k8"]), ptr(r["ks"]),
+                               ptr(r["kn2"]), s), "htrc_pack_int8")
     if order == _lib.ORDER_KMEANS:
         r["perm"] = e(n, dt=torch.int32)
         nbytes = ctypes.c_size_t()
@@ -362,8 +380,9 @@ def run_stages(qd, kb, vb, tk=None, tv=None, *, exact_leaves, sink_leaves=0, til
         check(L.htrc_kmeans_order(ptr(qd), qdt, n, DIM, ptr(r["perm"]), ptr(scratch), int(nbytes.value), s),
               "htrc_kmeans_order")
     perm = ptr(r["perm"])
-    check(L.htrc_tile_prep(ptr(qd), qdt, n, DIM, tile, perm, grp, ptr(r["mu"]), ptr(r["mu_hi"]), ptr(r["mu_lo"]),
-                           ptr(r["q8"]), ptr(r["sq"]), ptr(r["dq8"]), ptr(r["sdq"]), ptr(r["dd"]), s), "htrc_tile_prep")
+    check(L.htrc_tile_prep_ex(ptr(qd), qdt, n, DIM, tile, perm, grp, ptr(r["mu"]), ptr(r["mu_hi"]), ptr(r["mu_lo"]),
+                              ptr(r["q8"]), ptr(r["sq"]), ptr(r["dq8"]), ptr(r["sdq"]), ptr(r["dd"]),
+                              int(qk_scale_block or 0), s), "htrc_tile_prep_ex")
     tail_part = None
     if tk is not None:
         tail_part = e(n, DIM + 2)

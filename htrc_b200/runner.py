@@ -94,6 +94,7 @@ class FlatRunner:
         self.order = _flat.order_code(base["order"])
         self.curvature = _flat.curvature_code(base.get("curvature", "lin"))
         self.store = _lib.STORES.get(base.get("store", "int8"), _lib.STORE_INT8)
+        self.qk_scale_block = int(base.get("qk_scale_block") or 0)
         if tile_chunk is None:
             if free_bytes is None and self.device.type == "cuda" and torch.cuda.is_available():
                 # plan from the device's free memory (the reference falls back to PROD's 128-tile chunk,
@@ -126,6 +127,7 @@ class FlatRunner:
         except ValueError as exc:
             if "CUDA tensors" not in str(exc):
                 raise
+        _flat._check_scale_block(base.get("qk_scale_block"), base["store"])
         if use_graph:
             self._capture()
 
@@ -158,7 +160,8 @@ class FlatRunner:
             self._w = _flat.new_workspace(nbytes, dev)
             kw = dict(exact_leaves=c["exact_leaves"], sink_leaves=c["sink_leaves"], tile_chunk=c["tile_chunk"],
                       scale=c.get("scale"), out=self._so, lse=self._sl, workspace=self._w, group=self.group,
-                      order=self.order, tile=c["tile"], curvature=self.curvature, store=self.store)
+                      order=self.order, tile=c["tile"], curvature=self.curvature, store=self.store,
+                      qk_scale_block=self.qk_scale_block)
             self._capturing = True
             try:
                 side = torch.cuda.Stream()

@@ -93,6 +93,9 @@ typedef struct HtrcFlatArgs {
   int32_t store;           /* HTRC_STORE_INT8 (store="int8": INT8 state and INT8 query/key codes), or
                               HTRC_STORE_FP8 (store="fp8", h3/htrc_flat_triton.py FP8=1: e4m3 state codes with
                               row scales, fp16 far-field dots, bf16 near field; needs HTRC_CURV_LIN) */
+  int32_t qk_scale_block;  /* 0: the reference's INT8 scales (per key, per query row); 64: an extension with no
+                              reference counterpart, one scale per 64 keys (a leaf) and per query tile
+                              (BASELINE's "per-64-token-block absmax"); HTRC_STORE_INT8 only */
 } HtrcFlatArgs;
 
 /* nb rounded up to a multiple of 16: the row pitch of the per-(tile, leaf) scalar arrays. */
@@ -190,6 +193,17 @@ int htrc_tile_attention(const int8_t* q8, const float* sq, const int8_t* dq8, co
  * n_tail <= 16 with bf16 operands; :381-388 float32 for longer tails): tail_part [N, dim + 2]. */
 int htrc_tail_partial(const void* q, int32_t q_dtype, int64_t n_queries, int32_t dim, const float* tail_k,
                       const float* tail_v, int32_t n_tail, float scale, float* tail_part, htrc_stream_t stream);
+
+/* Per-block INT8 pack (extension, no reference counterpart): as htrc_pack_int8, with one scale per block of
+ * block_rows (= 64) consecutive rows, s = max(amax_block|x| * (1/127), 1e-20), written for every row. */
+int htrc_pack_int8_blocks(const void* x, int32_t dtype, int64_t rows, int32_t dim, int32_t rounding,
+                          int32_t block_rows, int8_t* x8, float* scale, float* sqnorm, htrc_stream_t stream);
+
+/* htrc_tile_prep with q_scale_block = 0 (the same codes) or 64 (extension): the codes q8 of a tile's rows
+ * share one scale from the tile's abs-max (sq holds it for every row); dq8 / sdq stay per row. */
+int htrc_tile_prep_ex(const void* q, int32_t q_dtype, int64_t n_queries, int32_t dim, int32_t tile,
+                      const int32_t* perm, int32_t group, float* mu, uint16_t* mu_hi, uint16_t* mu_lo, int8_t* q8,
+                      float* sq, int8_t* dq8, float* sdq, float* dd, int32_t q_scale_block, htrc_stream_t stream);
 
 /* ---- stage entry points of the fp8 state path (HTRC_STORE_FP8) ---- */
 

@@ -85,6 +85,25 @@ def pack_rows_half_away(x):
     return _round_half_away_i8(x / s[..., None]), s
 
 
+def pack_blocks(x, block, rounding):
+    """Extension, not in the reference (its scales are per row): the INT8 pack with one scale per block
+    of `block` consecutive rows, BASELINE's "per-64-token-block absmax" Q/K scales.
+    s_b = max(amax_block|x| * (1/127), 1e-20); every row of the block is coded with s_b, half-even
+    (rounding "even": the keys' rule, h3/htrc_flat.py:216-218) or half-away ("away": the query rows' rule,
+    h3/htrc_flat_triton.py:110-117).  Returns (x8 int8 [R, D], s float32 [R]: the block's scale per row)."""
+    x = np.asarray(x, dtype=F32)
+    r = x.shape[0]
+    nbk = -(-r // block)
+    am = np.zeros(nbk * block, F32)
+    am[:r] = np.abs(x).max(-1)
+    s = np.maximum((am.reshape(nbk, block).max(1) * INV127).astype(F32), EPS_ROW).astype(F32)
+    sr = np.repeat(s, block)[:r]
+    y = (x / sr[:, None]).astype(F32)
+    if rounding == "even":
+        return np.clip(np.rint(y), -127, 127).astype(np.int8), sr
+    return _round_half_away_i8(y), sr
+
+
 def pack_slope(g):
     """INT8 far-field slope per (tile, leaf) row (h3/htrc_flat_triton.py:73-79):
     am = max(amax|g|, 1e-30); sg = am * (1/127); g8 = trunc(g * (127 / am) +- 0.5).
@@ -276,12 +295,18 @@ def state_int8(g, vb):
     return g8, sg, bf16_round(vb)
 
 
-def query_codes(qt, mu):
+def query_codes(qt, mu, q_block=False):
     """Per-row INT8 codes of the tile rows and of their offsets from the tile centre, as the tile
-    and row-max kernels form them in-register (h3/htrc_flat_triton.py:103-117)."""
+    and row-max kernels form them in-register (h3/htrc_flat_triton.py:103-117).  q_block (extension):
+    one scale per tile for the rows' codes (`pack_blocks`); the offsets keep per-row scales."""
     qt = np.asarray(qt, dtype=F32)
     dq = (qt - np.asarray(mu, dtype=F32)[:, None, :]).astype(F32)
-    q8, sq = pack_rows_half_away(qt)
+    if q_block:
+        nt, t, d = qt.shape
+        q8, sq = pack_blocks(qt.reshape(nt * t, d), t, "away")
+        q8, sq = q8.reshape(nt, t, d), sq.reshape(nt, t)
+    else:
+        q8, sq = pack_rows_half_away(qt)
     dq8, sdq = pack_rows_half_away(dq)
     return q8, sq, dq8, sdq
 
@@ -671,7 +696,7 @@ def pack_k(k):
 
 def flat_attention(q, k, v, *, tile=64, exact_leaves=256, leaf=64, scale=None, sink_leaves=0,
                    tail=None, return_stages=False, group=1, order="seq", perm=None, quant=None,
-                   stats_bf16=False, curvature="lin", store="int8"):
+                   stats_bf16=False, curvature="lin", store="int8", qk_scale_block=0):
     """The whole production path for one head: q [N, D], k/v [M, D] (float32 arrays holding the
     caller's values; k and v are rounded to bfloat16 as the reference's bf16 path stores them).
     group: G tiles per centre (kern["group"]); order "kmeans" permutes the queries first (``perm``
@@ -706,7 +731,8 @@ def flat_attention(q, k, v, *, tile=64, exact_leaves=256, leaf=64, scale=None, s
     if m % leaf:
         raise ValueError("key count must be a multiple of the leaf size")
     scale = 1.0 / math.sqrt(d) if scale is None else float(scale)
-    k8, ks = pack_rows_half_even(k)
+    # qk_scale_block=64 (extension): one scale per 64 keys (a leaf) and per query tile
+    k8, ks = pack_blocks(k, int(qk_scale_block), "even") if qk_scale_block else pack_rows_half_even(k)
     qt, mu, _ = tile_centres(q, tile)
     if group > 1:
         mu = group_centres(qt, group)
@@ -716,7 +742,7 @@ def flat_attention(q, k, v, *, tile=64, exact_leaves=256, leaf=64, scale=None, s
                          return_stages)
     g8, sg, vb = state_int8(g, vbf)
     mu_t = mu[np.arange(qt.shape[0]) // group]
-    q8, sq, dq8, sdq = query_codes(qt, mu_t)
+    q8, sq, dq8, sdq = query_codes(qt, mu_t, q_block=bool(qk_scale_block))
     cv = dd = None
     if curvature == "iso":
         cv = iso_coeff(mu, k if k_stats is None else k_stats, leaf, scale)

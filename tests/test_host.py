@@ -240,3 +240,26 @@ def test_plan_chunk_takes_the_largest_chunk_that_fits():
     # with room for it, the whole sequence is one chunk (2016 tiles: every SM busy in one launch)
     assert runner.plan_chunk(1 << 40, keys, 64, queries=q) == -(-q // 64)
     assert runner.plan_chunk(1 << 40, 4096, 64, queries=4096) == 1024       # <= 1024 tiles: as the reference
+
+
+def test_qk_scale_block_option_is_checked():
+    """qk_scale_block (extension): None/0 or 64; INT8 store only; the C ABI says the same."""
+    q, k, v = _qkv()
+    cfg = dict(htrc_b200.PROD, leaf=64)
+    with pytest.raises(ValueError, match="CUDA tensors"):
+        htrc_b200.flat_attention(q, k, v, **{**cfg, "qk_scale_block": 64})
+    with pytest.raises(ValueError, match="qk_scale_block"):
+        htrc_b200.flat._check_scale_block(32, "int8")
+    with pytest.raises(NotImplementedError, match="store='int8'"):
+        htrc_b200.flat._check_scale_block(64, "fp8")
+    assert htrc_b200.flat._check_scale_block(None, "int8") == 0
+    a = _lib.HtrcFlatArgs()
+    a.n_queries, a.n_keys, a.dim, a.tile, a.leaf, a.exact_leaves = 4096, 4096, 128, 64, 64, 16
+    nbytes = ctypes.c_size_t()
+    L = _lib.lib()
+    a.qk_scale_block = 64
+    assert L.htrc_flat_workspace_size(ctypes.byref(a), ctypes.byref(nbytes)) == _lib.HTRC_OK
+    a.qk_scale_block = 32
+    assert L.htrc_flat_workspace_size(ctypes.byref(a), ctypes.byref(nbytes)) == _lib.HTRC_ERR_ARG
+    a.qk_scale_block, a.store = 64, _lib.STORE_FP8
+    assert L.htrc_flat_workspace_size(ctypes.byref(a), ctypes.byref(nbytes)) == _lib.HTRC_ERR_UNSUPPORTED

@@ -310,3 +310,22 @@ def test_e4m3_codes_round_trip():
     c = np.arange(256, dtype=np.uint8)
     c = c[(c & 0x7F) != 0x7F]                       # 0x7F / 0xFF are NaN in e4m3fn
     assert np.array_equal(O.e4m3_codes(O.e4m3_values(c)), c)
+
+
+def test_pack_blocks_restates_the_block_rule():
+    """qk_scale_block extension: one scale per 64-row block from the block's abs-max, every row coded with
+    it; a single-row block equals the per-row pack."""
+    rng = np.random.default_rng(5)
+    x = (rng.standard_normal((130, 128)) * rng.random((130, 1)) * 3).astype(np.float32)
+    x[64:128] = 0.0
+    for rounding, per_row in (("even", O.pack_rows_half_even), ("away", O.pack_rows_half_away)):
+        x8, s = O.pack_blocks(x, 64, rounding)
+        assert x8.dtype == np.int8 and np.abs(x8.astype(int)).max() <= 127
+        for b0 in (0, 64, 128):
+            blk = slice(b0, min(b0 + 64, 130))
+            assert np.all(s[blk] == s[b0])
+            assert s[b0] == np.maximum(np.float32(np.abs(x[blk]).max()) * O.INV127, np.float32(1e-20))
+        assert np.abs(x8[64:128]).max() == 0
+        one8, one_s = O.pack_blocks(x, 1, rounding)
+        r8, rs = per_row(x)
+        assert np.array_equal(one8, r8) and np.array_equal(one_s, rs)
