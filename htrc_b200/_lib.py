@@ -37,6 +37,7 @@ class HtrcFlatArgs(ctypes.Structure):
         ("out", _p), ("lse", _p),
         ("stage_events", ctypes.POINTER(_p)), ("n_stage_events", _i32),
         ("group", _i32), ("order", _i32), ("curvature", _i32), ("store", _i32), ("qk_scale_block", _i32),
+        ("route_mask", _p),
     ]
 
 

@@ -413,6 +413,10 @@ int htrc_flat_forward(const HtrcFlatArgs* a, htrc_stream_t stream) {
     }
     mark(3 + 4 * chunk);
     if ((rc = launch_route(sel, L.pitch, tc, group, nb, kx, sink, idx, excl, st)) != HTRC_OK) return rc;
+    if (a->route_mask != nullptr &&
+        cudaMemcpyAsync(a->route_mask + g0 * L.pitch, excl, static_cast<size_t>(gc) * L.pitch,
+                        cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+      return HTRC_ERR_CUDA;
     mark(4 + 4 * chunk);
     if (L.fp8) {
       TileFp8Maps tmp;

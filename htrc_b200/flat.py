@@ -200,7 +200,7 @@ def curvature_code(curvature) -> int:
 
 def _args(qd, kb, vb, tk, tv, exact_leaves, sink_leaves, tile_chunk, scale, out=None, lse=None, ws=None,
           stage_events=None, group=1, order=_lib.ORDER_SEQ, tile=TILE, curvature=_lib.CURV_LIN,
-          store=_lib.STORE_INT8, qk_scale_block=0):
+          store=_lib.STORE_INT8, qk_scale_block=0, route_mask=None):
     a = _lib.HtrcFlatArgs()
     a.q = ptr(qd)
     a.q_dtype = _lib.DTYPE_BF16 if qd.dtype == torch.bfloat16 else _lib.DTYPE_F32
@@ -215,6 +215,7 @@ def _args(qd, kb, vb, tk, tv, exact_leaves, sink_leaves, tile_chunk, scale, out=
     a.out, a.lse = ptr(out), ptr(lse)
     a.group, a.order, a.curvature, a.store = int(group), int(order), int(curvature), int(store)
     a.qk_scale_block = int(qk_scale_block or 0)
+    a.route_mask = ptr(route_mask)
     if ws is not None:
         a.workspace, a.workspace_bytes = ptr(ws), int(ws.numel())
     if stage_events:
@@ -266,14 +267,17 @@ def _workspace(ws, nbytes, device):
 
 def forward_into(qd, kb, vb, tk, tv, *, exact_leaves, sink_leaves=0, tile_chunk=0, scale=None, out, lse=None,
                  workspace, stream=None, stage_events=None, group=1, order=_lib.ORDER_SEQ, tile=TILE,
-                 curvature=_lib.CURV_LIN, store=_lib.STORE_INT8, qk_scale_block=0):
+                 curvature=_lib.CURV_LIN, store=_lib.STORE_INT8, qk_scale_block=0, route_mask=None):
     """One head through ``htrc_flat_forward`` into caller-provided buffers (no allocation; CUDA-graph
     capturable).  qd [N, 128] f32/bf16, kb/vb [M, 128] bf16, out [N, 128] f32, lse [N] f32 or None;
     stage_events: optional list of torch.cuda.Event recorded between the stages (see
     include/htrc_flat.h); group / order: ``group_of(kern)`` / ``order_code(order)``; tile: 64 or 32;
-    store: ``_lib.STORES[store]``; qk_scale_block: 0 or 64."""
+    store: ``_lib.STORES[store]``; qk_scale_block: 0 or 64; route_mask: optional uint8
+    [ceil(nt / group), leaf_pitch(nb)] device tensor that receives the routing masks (1 = leaf exact)."""
+    if route_mask is not None and (route_mask.dtype != torch.uint8 or not route_mask.is_contiguous()):
+        raise ValueError("route_mask: a contiguous uint8 tensor [groups, leaf_pitch(nb)]")
     a = _args(qd, kb, vb, tk, tv, exact_leaves, sink_leaves, tile_chunk, scale, out, lse, workspace, stage_events,
-              group, order, tile, curvature, store, qk_scale_block)
+              group, order, tile, curvature, store, qk_scale_block, route_mask)
     check(lib().htrc_flat_forward(a, stream_ptr(stream)), "htrc_flat_forward")
 
 
@@ -323,6 +327,37 @@ def flat_attention(q, k, v, *, tile=64, exact_leaves=64, order="seq", curvature=
 def flat_attention_prod(q, k, v, **over):
     """Production configuration of the flat operator (h3/htrc_flat.py:397-399)."""
     return flat_attention(q, k, v, **{**PROD, **over})
+
+
+@torch.inference_mode()
+def flat_attention_heads(q, k, v, *, return_lse=False, ws=None, **cfg):
+    """Head-batched entry (an addition): q [H, N, 128], k/v [H, M, 128] -> out [H, N, 128] float32 (and lse
+    [H, N] with return_lse), every head with ``flat_attention(**cfg)`` semantics (the same defaults), on one
+    device workspace, launched back to back on the current stream."""
+    if q.dim() != 3 or k.dim() != 3 or v.dim() != 3 or q.shape[0] != k.shape[0] or k.shape != v.shape:
+        raise ValueError("q [H, N, D], k/v [H, M, D] expected")
+    h, n = int(q.shape[0]), int(q.shape[1])
+    c = {**dict(tile=64, exact_leaves=64, order="seq", curvature="lin", tile_chunk=32, leaf=16, select="max",
+                backend="torch", store="fp32", dot="tf32", sel_stride=1, kern=None, quant=None, sink_leaves=0,
+                tail=None, scale=None, qk_scale_block=None), **cfg}
+    _check_args(q[0], k[0], v[0], c["tile"], c["exact_leaves"], c["order"], c["curvature"], c["leaf"], c["select"],
+                c["backend"], c["store"], c["dot"], c["sel_stride"], c["quant"], c["sink_leaves"], c["tail"])
+    qsb = _check_scale_block(c["qk_scale_block"], c["store"])
+    out = torch.empty((h, n, DIM), dtype=torch.float32, device=q.device)
+    lse = torch.empty((h, n), dtype=torch.float32, device=q.device) if return_lse else None
+    grp, oc, cc = group_of(c["kern"]), order_code(c["order"]), curvature_code(c["curvature"])
+    sc = _lib.STORES[c["store"]]
+    w = None
+    for i in range(h):
+        qd, kb, vb, tk, tv = _prep_inputs(q[i], k[i], v[i], c["tail"], c["quant"])
+        if w is None:
+            nbytes = workspace_bytes(n, int(kb.shape[0]), c["exact_leaves"], c["sink_leaves"], c["tile_chunk"],
+                                     int(tk.shape[0]) if tk is not None else 0, grp, oc, c["tile"], cc, sc)
+            w = _workspace(ws, nbytes, q.device)
+        forward_into(qd, kb, vb, tk, tv, exact_leaves=c["exact_leaves"], sink_leaves=c["sink_leaves"],
+                     tile_chunk=c["tile_chunk"], scale=c["scale"], out=out[i], lse=lse[i] if return_lse else None,
+                     workspace=w, group=grp, order=oc, tile=c["tile"], curvature=cc, store=sc, qk_scale_block=qsb)
+    return (out, lse) if return_lse else out
 
 
 @torch.inference_mode()

@@ -96,6 +96,8 @@ typedef struct HtrcFlatArgs {
   int32_t qk_scale_block;  /* 0: the reference's INT8 scales (per key, per query row); 64: an extension with no
                               reference counterpart, one scale per 64 keys (a leaf) and per query tile
                               (BASELINE's "per-64-token-block absmax"); HTRC_STORE_INT8 only */
+  uint8_t* route_mask;     /* optional debug export (NULL = none): [ceil(nt / group), P] uint8 routing masks, the
+                              rows htrc_route writes (1 = the leaf is evaluated exactly for that centre row) */
 } HtrcFlatArgs;
 
 /* nb rounded up to a multiple of 16: the row pitch of the per-(tile, leaf) scalar arrays. */
