@@ -4,9 +4,10 @@
 //   S  = mu . K_leaf^T            (M=128 centres, N=64 tokens, K=128; mu = mu_hi + mu_lo, two bf16 MMAs
 //                                  with mu in TMEM as the A operand, which leaves shared memory to four
 //                                  K/V stages)
-//   softmax over the 64 tokens of each centre row (one thread per row, in registers): lz, w
-//   G  = W . K_leaf               (M=128, N=128, K=64; W = w_hi + w_lo, two bf16 MMAs, K_leaf MN-major)
-//   VB = W_hi . V_leaf            (M=128, N=128, K=64)
+//   softmax over the 64 tokens of each centre row (one thread per row, in registers): lz, w; W = w_hi + w_lo
+//   (bf16) goes back into TMEM over the S buffer it came from, as the A operand of the next MMAs
+//   [G | VB] = W . [K_leaf | V_leaf]  (M=128, N=256, K=64; two bf16 MMA chains (w_hi, w_lo) with A in TMEM,
+//                                  K and V of a stage adjacent in shared memory as one MN-major operand)
 //   epilogue: g = scale * G -> (g8, sg) half-away INT8 with the row abs-max scale; vbar -> bf16;
 //   g8/vbar rows staged in shared memory and written by TMA stores, lz/sg by plain stores.
 // This is the arithmetic of h3/htrc_flat_triton.py:41-85 (_stats_kernel, I8=1); the hi/lo splits keep
@@ -17,7 +18,7 @@
 // its G columns (the two halves exchange partial sums with their abs-maxima).
 // FP8 stores the state as e4m3 codes with per-(centre, leaf) row scales instead (h3/htrc_flat_triton.py:65-72,
 // store="fp8"): sg = max(amax|g| * (1/448), 1e-30), g codes = e4m3(g / sg) rounded to nearest even and
-// saturated at 448, and the same for vbar with sv (vbar from the full W . V, both W halves).
+// saturated at 448, and the same for vbar with sv.
 //
 // Warp roles (512 threads, one role per warpgroup so that setmaxnreg can move registers from the
 // issuing warps to the arithmetic): warpgroup 0 = warp 0 TMA producer, warp 1 S issuer (+ TMEM owner),
@@ -33,24 +34,21 @@ namespace htrc {
 
 namespace {
 constexpr int kThreads = 512;
-constexpr int kStages = 4;
+constexpr int kStages = 5;
 constexpr uint32_t kLeafBytes = 64 * 128 * 2;       // K (or V) of one 64-token leaf
 constexpr uint32_t kStageBytes = 2 * kLeafBytes;    // K + V
-constexpr uint32_t kWBytes = 128 * 128;             // W_hi or W_lo: 128 rows x 64 bf16
 constexpr uint32_t kOffStage = 0;
-constexpr uint32_t kOffWHi = kOffStage + kStages * kStageBytes;
-constexpr uint32_t kOffWLo = kOffWHi + kWBytes;
-constexpr uint32_t kOffStG = kOffWLo + kWBytes;     // g8 staging: 128 rows x 128 B
+constexpr uint32_t kOffStG = kOffStage + kStages * kStageBytes;   // g8 staging: 128 rows x 128 B
 constexpr uint32_t kOffStV = kOffStG + 128 * 128;   // vbar staging: 2 x (128 rows x 128 B)
 constexpr uint32_t kOffAm = kOffStV + 2 * 128 * 128;  // row abs-max halves [2 (leaf parity)][2 (half)][128]
 constexpr uint32_t kOffB2 = kOffAm + 2 * 2 * 128 * 4;   // ISO: |G|^2 halves [2][2][128]
-constexpr uint32_t kOffAw = kOffB2 + 2 * 2 * 128 * 4;   // ISO: sum_s w_s |k_s|^2 [2 (leaf parity)][128]
-constexpr uint32_t kOffKn = kOffAw + 2 * 128 * 4;       // ISO: key norms of each K/V stage [kStages][64]
+constexpr uint32_t kOffAw = kOffB2 + 2 * 2 * 128 * 4;   // ISO: sum_s w_s |k_s|^2 [4 (leaf % 4)][128]
+constexpr uint32_t kOffKn = kOffAw + 4 * 128 * 4;       // ISO: key norms of each K/V stage [kStages][64]
 constexpr uint32_t kOffBar = kOffKn + kStages * 64 * 4;
 constexpr uint32_t kSmemBytes = kOffBar + 256 + 1024;  // + barriers, + alignment slack
 
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS = 0;      // two 64-column S buffers
+constexpr uint32_t kColS = 0;      // two 64-column S buffers; W_hi / W_lo of the leaf then in 32 columns each
 constexpr uint32_t kColG = 128;    // 128 columns
 constexpr uint32_t kColV = 256;    // 128 columns
 constexpr uint32_t kColMu = 384;   // mu_hi (64 columns of bf16 pairs), then mu_lo
@@ -60,9 +58,8 @@ struct Bars {
   uint64_t kv_full[kStages];
   uint64_t kv_empty[kStages];
   uint64_t s_full[2];
-  uint64_t s_empty[2];
-  uint64_t w_full;
-  uint64_t w_empty;
+  uint64_t s_empty[2];  // G/VB of the leaf done: its W (over S in TMEM) is consumed
+  uint64_t w_full[2];   // the 128 softmax threads wrote W into the S buffer
   uint64_t gv_full;
   uint64_t gv_empty;   // the 256 epilogue threads drained G and VB into registers
   uint64_t stg_free;   // thread 0 of the epilogue: the previous TMA stores have read the staging buffers
@@ -118,10 +115,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&bars->s_full[b], 1);
-      mbar_init(&bars->s_empty[b], 128);
+      mbar_init(&bars->s_empty[b], 1);
+      mbar_init(&bars->w_full[b], 128);
     }
-    mbar_init(&bars->w_full, 128);
-    mbar_init(&bars->w_empty, 1);
     mbar_init(&bars->gv_full, 1);
     mbar_init(&bars->gv_empty, 256);
     mbar_init(&bars->stg_free, 1);
@@ -193,39 +189,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     } else if (warp == 2) {
       // ------------------------------------------------------------------ G/VB issuer
-      // G(j) = W . K_j and VB(j) = W_hi . V_j once the softmax wrote W and the epilogue drained the
-      // previous G/VB; their completion also releases the K/V stage (S(j) completed before W(j) existed)
+      // G(j) = W . K_j and VB(j) = W . V_j once the softmax wrote W (into S buffer j % 2) and the epilogue
+      // drained the previous G/VB; their completion releases the S buffer for S(j + 2) and the K/V stage
       const uint32_t leader = elect_one();
       if (nl > 0) {
-        const uint32_t id_gv = idesc_bf16(128, 128, false, true);
-        const uint32_t w_hi = smem_u32(smem + kOffWHi), w_lo = smem_u32(smem + kOffWLo);
+        const uint32_t id_gv = idesc_bf16(128, 256, false, true);
+        static_assert(kColV == kColG + 128 && kStageBytes == 2 * kLeafBytes, "[G | VB] and [K | V] side by side");
         for (int j = 0; j < nl; ++j) {
-          const int s = j % kStages;
-          if (!mbar_wait_warp(&bars->w_full, j & 1, status, abort_flag)) break;
+          const int s = j % kStages, b = j & 1;
+          if (!mbar_wait_warp(&bars->w_full[b], (j >> 1) & 1, status, abort_flag)) break;
           if (j >= 1 && !mbar_wait_warp(&bars->gv_empty, (j - 1) & 1, status, abort_flag)) break;
           tc_fence_after();
           const uint32_t kst = smem_u32(smem + kOffStage + s * kStageBytes);
-          const uint32_t vst = kst + kLeafBytes;
+          const uint32_t wt = tmem + kColS + 64 * b;      // W_hi at wt, W_lo at wt + 32 (keys in pairs)
+          // [G | VB] = (W_hi + W_lo) . [K | V]: the stage's K and V are four 64-column chunks 8 KB apart, one
+          // N = 256 operand, and TMEM holds G and VB side by side (kColV = kColG + 128)
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
-              const uint64_t a = sw128_desc((h ? w_lo : w_hi) + kk * 32, 16, 1024);
               const uint64_t bdesc = sw128_desc(kst + kk * 2048, kLeafBytes / 2, 1024);
-              mma_bf16_by(leader, tmem + kColG, a, bdesc, id_gv, (h | kk) != 0);
-            }
-          }
-#pragma unroll
-          for (int h = 0; h < (FP8 ? 2 : 1); ++h) {
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-              const uint64_t a = sw128_desc((h ? w_lo : w_hi) + kk * 32, 16, 1024);
-              const uint64_t bdesc = sw128_desc(vst + kk * 2048, kLeafBytes / 2, 1024);
-              mma_bf16_by(leader, tmem + kColV, a, bdesc, id_gv, (h | kk) != 0);
+              mma_bf16_ts_by(leader, tmem + kColG, wt + 32 * h + 8 * kk, bdesc, id_gv, (h | kk) != 0);
             }
           }
           mma_commit_by(leader, &bars->gv_full);
-          mma_commit_by(leader, &bars->w_empty);
+          mma_commit_by(leader, &bars->s_empty[b]);
           mma_commit_by(leader, &bars->kv_empty[s]);
         }
       }
@@ -240,7 +228,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int64_t tloc = static_cast<int64_t>(blk) * 128 + row;   // tile index within the chunk
     const bool valid = tloc < tc;
     const float kLog2e = 1.4426950408889634f;
-    const uint32_t wh = smem_u32(smem + kOffWHi), wl = smem_u32(smem + kOffWLo);
     if (nl > 0) {
       // this row's centre (hi and lo parts, 128 bf16 each) -> TMEM lane `row`; rows past the end are zero
       const int64_t grow = t0 + static_cast<int64_t>(blk) * 128 + row;
@@ -282,8 +269,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 32; ++i) a[32 + i] = __uint_as_float(r[i]);
       }
-      tc_fence_before();
-      mbar_arrive(&bars->s_empty[b]);
       float mxa[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
       const float2 sc2 = make_float2(scale, scale);
 #pragma unroll
@@ -324,24 +309,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!isfinite(lz)) flag_status(status, ST_NONFINITE);
       }
       const float rz = 1.0f / z;
-      if (j >= 1 && !mbar_wait(&bars->w_empty, (j - 1) & 1, status, abort_flag)) break;
-      // after w_empty(j - 1): the epilogue read this parity's value (for leaf j - 2) before G/VB(j - 1) began
-      if (ISO) reinterpret_cast<float*>(smem + kOffAw)[(j & 1) * 128 + row] = kw * rz;
+      // slot j % 4: the epilogue read slot j - 4 before G/VB(j - 3) began, and S(j) (so this softmax) came
+      // after G/VB(j - 2) completed
+      if (ISO) reinterpret_cast<float*>(smem + kOffAw)[(j & 3) * 128 + row] = kw * rz;
+      // W = w_hi + w_lo as bf16 pairs over this row's S columns (already read): hi in 32 columns, lo in 32
+      {
+        uint32_t hi[32], lo[32];
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        uint32_t hi[4], lo[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 w = mul2(make_float2(a[c * 8 + 2 * e], a[c * 8 + 2 * e + 1]), make_float2(rz, rz));
-          hi[e] = pack_bf16x2(w.x, w.y);
-          const float2 lw = sub2(w, make_float2(__uint_as_float(hi[e] << 16), __uint_as_float(hi[e] & 0xFFFF0000u)));
-          lo[e] = pack_bf16x2(lw.x, lw.y);
+        for (int i = 0; i < 32; ++i) {
+          const float2 w = mul2(make_float2(a[2 * i], a[2 * i + 1]), make_float2(rz, rz));
+          hi[i] = pack_bf16x2(w.x, w.y);
+          const float2 lw = sub2(w, make_float2(__uint_as_float(hi[i] << 16), __uint_as_float(hi[i] & 0xFFFF0000u)));
+          lo[i] = pack_bf16x2(lw.x, lw.y);
         }
-        st_shared_v4(wh + sw128_off(row, c), hi[0], hi[1], hi[2], hi[3]);
-        st_shared_v4(wl + sw128_off(row, c), lo[0], lo[1], lo[2], lo[3]);
+        tmem_st32(tmem + lane_base + kColS + 64 * b, hi);
+        tmem_st32(tmem + lane_base + kColS + 64 * b + 32, lo);
       }
-      fence_proxy_async_smem();
-      mbar_arrive(&bars->w_full);
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&bars->w_full[b]);
     }
   } else {
     // ------------------------------------------------------------------ epilogue: G, VB -> g8/sg, vbar
@@ -464,7 +450,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       float aw = 0.f, b2 = 0.f;                 // ISO: sum w |k|^2 of this row, this half's |G|^2
       if (ISO) {
-        aw = reinterpret_cast<const float*>(smem + kOffAw)[(j & 1) * 128 + row];
+        aw = reinterpret_cast<const float*>(smem + kOffAw)[(j & 3) * 128 + row];
         float2 s2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
         for (int i = 0; i < 64; i += 2) {
