@@ -574,13 +574,15 @@ __global__ void __launch_bounds__(tfx::Cfg<FAR>::kThreads, 1)
           v = fma2(make_float2(__uint_as_float(di0), __uint_as_float(di1)), make_float2(cv.x, cv.z),
                    make_float2(cv.y, cv.w));
         } else {
-          v = mul2(make_float2(__uint_as_float(di0), __uint_as_float(di1)), make_float2(c_near, c_near));
+          v = make_float2(__uint_as_float(di0), __uint_as_float(di1));   // raw S; scaled in the exponent's FMA
         }
         lg[i] = v.x;
         lg[i + 1] = v.y;
-        mxa[(i >> 1) & 3] = fmaxf(mxa[(i >> 1) & 3], fmaxf(v.x, v.y));
+        mxa[(i >> 1) & 3] = max3(mxa[(i >> 1) & 3], v.x, v.y);
       }
-      const float mx = fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3]));
+      // NEAR: logit = c_near * S with c_near = scale * log2 e > 0, so its maximum is c_near * max S
+      const float esc = FAR ? 1.0f : c_near;
+      const float mx = __fmul_rn(esc, fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])));
       // the half of an absent step (odd step count) holds stale TMEM: keep it inert
       const float m_new = has ? fmaxf(m_used, mx) : m_used;
       const bool need = m_new > m_used + kRescale;
@@ -590,12 +592,12 @@ __global__ void __launch_bounds__(tfx::Cfg<FAR>::kThreads, 1)
         m_used = m_new;
       }
       const bool live = has && m_used != -INFINITY;
-      const float2 mref2 = make_float2(live ? m_used : 0.f, live ? m_used : 0.f);
+      const float2 negm2 = make_float2(live ? -m_used : 0.f, live ? -m_used : 0.f), esc2 = make_float2(esc, esc);
       uint32_t pw[32];
       float2 rs2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
       for (int i = 0; i < 64; i += 2) {
-        const float2 e = sub2(make_float2(lg[i], lg[i + 1]), mref2);
+        const float2 e = fma2(make_float2(lg[i], lg[i + 1]), esc2, negm2);
         const float2 pp = live ? make_float2(ex2(e.x), ex2(e.y)) : make_float2(0.f, 0.f);
         rs2[(i >> 1) & 3] = add2(rs2[(i >> 1) & 3], pp);
         if constexpr (FAR) {

@@ -296,7 +296,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 10) {
     // ------------------------------------------------------------------ per-column constants
-    // far: (sg * log2 e, lz * log2 e or -inf if routed / past nb); near: (ks * scale * log2 e, 0)
+    // far: (sg * log2 e, lz * log2 e or -inf if routed / past nb) per column; near: ks * scale * log2 e per
+    // column, packed
     const float near_scale = scale * kLog2e;
     for (int j = 0; j < total; ++j) {
       const int s = j % kXSlots;
@@ -309,19 +310,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int colq = q * 32 + lane;      // tile x = colq / 64, column colq % 64
         const int x = colq >> 6, i = colq & 63;
         const uint8_t* par = st + x * kXTile + kXBytes;
-        float2 v;
         if (j < nf) {
           const float lzv = reinterpret_cast<const float*>(par)[i];
           const float sgv = reinterpret_cast<const float*>(par + 256)[i];
           const bool masked = par[512 + i] != 0 || j * 64 + i >= nb;
-          v = make_float2(sgv * kLog2e, masked ? -INFINITY : lzv * kLog2e);
+          const float2 v = make_float2(sgv * kLog2e, masked ? -INFINITY : lzv * kLog2e);
           if (ISO) reinterpret_cast<float*>(smem + kOffCC3)[s * 128 + colq] =
               reinterpret_cast<const float*>(par + 768)[i] * kLog2e;
+          c[colq] = v;
         } else {
-          v = make_float2(reinterpret_cast<const float*>(par)[i] * near_scale, 0.f);
+          // near: one constant per column, packed (tile x's 64 at x * 64 of the slot's float view)
+          reinterpret_cast<float*>(c)[colq] = reinterpret_cast<const float*>(par)[i] * near_scale;
           if (ISO) reinterpret_cast<float*>(smem + kOffCC3)[s * 128 + colq] = 0.f;
         }
-        c[colq] = v;
       }
       mbar_arrive(&bars->x_empty[s]);      // the raw parameters of this slot have been read
       mbar_arrive(&bars->cc_full[s]);
@@ -368,29 +369,54 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld_wait();
       if (!mbar_wait_warp(&bars->cc_full[s], (j / kXSlots) & 1, status, abort_flag)) { aborted = true; break; }
       const float2* c = cc + s * 128 + x * 64;
-      const float* c3 = reinterpret_cast<const float*>(smem + kOffCC3) + s * 128 + x * 64;
-      const float2 dd2 = make_float2(dd_r, dd_r);
-      const float srow = j < nf ? sdq_r : sq_r;
-      const float2 srow2 = make_float2(srow, srow);
       const float2 magic2 = make_float2(kMagic, kMagic);
       float lg[64];
       float mxa[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};   // independent chains
+      float esc;        // the exponent's argument is esc * lg - m (one FMA)
+      if (j >= nf) {
+        // near step (warp-uniform): lg = S * (ks * scale * log2 e); the row's scale sq_r > 0 multiplies after
+        // the maximum and inside the exponent's FMA.  The constants are packed one per column.
+        const float* c1 = reinterpret_cast<const float*>(cc + s * 128) + x * 64;
 #pragma unroll
-      for (int i = 0; i < 64; i += 2) {
-        const float4 cv = *reinterpret_cast<const float4*>(c + i);     // (c1_i, c2_i, c1_i+1, c2_i+1)
-        const uint32_t di0 = i < 32 ? d0[i] : d1[i - 32];
-        const uint32_t di1 = i < 32 ? d0[i + 1] : d1[i - 31];
-        const float2 xm = make_float2(__int_as_float(static_cast<int>(di0) + kMagicBits),
-                                      __int_as_float(static_cast<int>(di1) + kMagicBits));
-        const float2 fd = sub2(xm, magic2);
-        const float2 t = mul2(srow2, make_float2(cv.x, cv.z));
-        float2 v = fma2(fd, t, make_float2(cv.y, cv.w));
-        if (ISO) v = fma2(*reinterpret_cast<const float2*>(c3 + i), dd2, v);
-        lg[i] = v.x;
-        lg[i + 1] = v.y;
-        mxa[(i >> 1) & 3] = fmaxf(mxa[(i >> 1) & 3], fmaxf(v.x, v.y));
+        for (int i = 0; i < 64; i += 4) {
+          const float4 cv = *reinterpret_cast<const float4*>(c1 + i);    // c1 of columns i .. i + 3
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int ii = i + 2 * h;
+            const uint32_t di0 = ii < 32 ? d0[ii] : d1[ii - 32];
+            const uint32_t di1 = ii < 32 ? d0[ii + 1] : d1[ii - 31];
+            const float2 xm = make_float2(__int_as_float(static_cast<int>(di0) + kMagicBits),
+                                          __int_as_float(static_cast<int>(di1) + kMagicBits));
+            const float2 u = mul2(sub2(xm, magic2), h ? make_float2(cv.z, cv.w) : make_float2(cv.x, cv.y));
+            lg[ii] = u.x;
+            lg[ii + 1] = u.y;
+            mxa[(ii >> 1) & 3] = max3(mxa[(ii >> 1) & 3], u.x, u.y);
+          }
+        }
+        esc = sq_r;
+      } else {
+        // far step: lg = S * (sdq_r * sg * log2 e) + lz * log2 e (+ the iso term), masked columns -inf
+        const float* c3 = reinterpret_cast<const float*>(smem + kOffCC3) + s * 128 + x * 64;
+        const float2 dd2 = make_float2(dd_r, dd_r);
+        const float2 srow2 = make_float2(sdq_r, sdq_r);
+#pragma unroll
+        for (int i = 0; i < 64; i += 2) {
+          const float4 cv = *reinterpret_cast<const float4*>(c + i);     // (c1_i, c2_i, c1_i+1, c2_i+1)
+          const uint32_t di0 = i < 32 ? d0[i] : d1[i - 32];
+          const uint32_t di1 = i < 32 ? d0[i + 1] : d1[i - 31];
+          const float2 xm = make_float2(__int_as_float(static_cast<int>(di0) + kMagicBits),
+                                        __int_as_float(static_cast<int>(di1) + kMagicBits));
+          const float2 fd = sub2(xm, magic2);
+          const float2 t = mul2(srow2, make_float2(cv.x, cv.z));
+          float2 v = fma2(fd, t, make_float2(cv.y, cv.w));
+          if (ISO) v = fma2(*reinterpret_cast<const float2*>(c3 + i), dd2, v);
+          lg[i] = v.x;
+          lg[i + 1] = v.y;
+          mxa[(i >> 1) & 3] = max3(mxa[(i >> 1) & 3], v.x, v.y);
+        }
+        esc = 1.0f;
       }
-      const float mx = fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3]));
+      const float mx = __fmul_rn(esc, fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])));
       mbar_arrive(&bars->cc_empty[s]);
       // rows of an absent tile B (odd tile count) hold stale TMEM: keep them inert
       const float m_new = has_tile ? fmaxf(m_used, mx) : m_used;
@@ -402,12 +428,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const bool live = has_tile && m_used != -INFINITY;
       const float mref = live ? m_used : 0.f;
-      const float2 mref2 = make_float2(mref, mref);
+      const float2 negm2 = make_float2(-mref, -mref), esc2 = make_float2(esc, esc);
       uint32_t pw[32];
       float2 rs2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
       for (int i = 0; i < 64; i += 2) {
-        const float2 e = sub2(make_float2(lg[i], lg[i + 1]), mref2);
+        const float2 e = fma2(make_float2(lg[i], lg[i + 1]), esc2, negm2);
         const float2 p = live ? make_float2(ex2(e.x), ex2(e.y)) : make_float2(0.f, 0.f);
         rs2[(i >> 1) & 3] = add2(rs2[(i >> 1) & 3], p);
         pw[i >> 1] = pack_bf16x2(p.x, p.y);
