@@ -426,15 +426,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         l *= alpha;
         m_used = m_new;
       }
-      const bool live = has_tile && m_used != -INFINITY;
-      const float mref = live ? m_used : 0.f;
+      // a row whose maximum is still -inf has only -inf logits so far (P = 0 from ex2); rows of an absent
+      // tile B get garbage P, which no MMA reads (PV runs for present tiles only)
+      const float mref = m_used != -INFINITY ? m_used : 0.f;
       const float2 negm2 = make_float2(-mref, -mref), esc2 = make_float2(esc, esc);
       uint32_t pw[32];
       float2 rs2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
       for (int i = 0; i < 64; i += 2) {
         const float2 e = fma2(make_float2(lg[i], lg[i + 1]), esc2, negm2);
-        const float2 p = live ? make_float2(ex2(e.x), ex2(e.y)) : make_float2(0.f, 0.f);
+        const float2 p = make_float2(ex2(e.x), ex2(e.y));
         rs2[(i >> 1) & 3] = add2(rs2[(i >> 1) & 3], p);
         pw[i >> 1] = pack_bf16x2(p.x, p.y);
       }
