@@ -291,8 +291,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int j = 0; ok && j < total && j < kSBufs; ++j) ok = issue_qk(j);
     for (int j = 0; ok && j + kYSlots < total; ++j) {
       if (!mbar_wait_warp(&bars->pv_done[j & 3], (j >> 2) & 1, status, abort_flag)) break;
+      if (j + kSBufs < total) ok = issue_qk(j + kSBufs);    // first: QK(j + 4) is on the step's critical chain
       produce_y(j + kYSlots);
-      if (j + kSBufs < total) ok = issue_qk(j + kSBufs);
     }
   } else if (warp == 10) {
     // ------------------------------------------------------------------ per-column constants
