@@ -17,9 +17,10 @@
 // lazily: a thread rescales its O row only when its maximum grew by more than 2^8 (P <= 256 otherwise).
 //
 // Data movement: the QK operand of a step (g8 block or k8 leaf, plus its per-column parameters) goes
-// through a 4-slot ring freed as soon as the QK MMA completes; the PV operand (vbar block or v leaf)
-// through a 3-slot ring freed by the PV MMA.  The completion of PV(j) (one commit, pv_done[j % 4]) frees
-// S/P buffer j % 4 for QK(j + 4), Y slot j % 3 for step j + 3, and lets the warpgroup of step j + 2
+// through a 3-slot ring freed as soon as the QK MMA completes; the PV operand (vbar block or v leaf)
+// through a 4-slot ring freed by the PV MMA (the value loads are the longer-lead ones: a step's V is
+// requested four steps ahead).  The completion of PV(j) (one commit, pv_done[j % 4]) frees
+// S/P buffer j % 4 for QK(j + 4), Y slot j % 4 for step j + 4, and lets the warpgroup of step j + 2
 // rescale its O rows.  All waits block (a suspended thread takes no issue slots from the softmax warps).
 // The producer and issuer warps run converged and let one elected lane issue: a warp whose lanes take
 // different roles serialises them, since a lane suspended in an mbarrier wait holds up the others.
@@ -45,9 +46,10 @@ namespace htrc {
 
 namespace {
 constexpr int kThreads = 384;
-constexpr int kXSlots = 4;
-constexpr int kYSlots = 3;
+constexpr int kXSlots = 3;
+constexpr int kYSlots = 4;
 constexpr int kSBufs = 4;
+static_assert(kYSlots <= kSBufs, "the QK issuer's loop produces Y(j + kYSlots) for every QK(j + kSBufs)");
 constexpr uint32_t kXBytes = 64 * 128;                          // g8 block / k8 leaf: 64 rows x 128 B
 constexpr uint32_t kYBytes = 64 * 256;                          // vbar block / v leaf: 2 chunks of 64x64 bf16
 constexpr uint32_t kParBytes = 1024;                            // far: lz[64], sg[64], excl[64], cv[64]; near: ks[64]
@@ -239,7 +241,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 11) {
     // ------------------------------------------------------------------ QK issuer + Y-ring producer
-    // Both wait for PV(j): it frees S/P buffer j % 4 for QK(j + 4) and Y slot j % 3 for step j + 3.
+    // Both wait for PV(j): it frees S/P buffer j % 4 for QK(j + 4) and Y slot j % 4 for step j + 4.
     const uint64_t pol_stream = policy_evict_first();
     const uint64_t pol_keep = policy_evict_last();
     const uint32_t leader = elect_one();
