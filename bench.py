@@ -62,9 +62,10 @@ def parse():
     ap.add_argument("--store", default="int8", choices=["int8", "fp8"],
                     help="far-field state: int8 (the production path, the headline) or fp8 (e4m3 state, store='fp8'; "
                          "no oracle sample)")
-    ap.add_argument("--streams", type=int, default=1, choices=[1, 2],
-                    help="heads of a layer alternate over this many streams, each with its own workspace (2: "
-                         "-1.7%% device-resident, +2%% end to end, and the per-stage events then overlap)")
+    ap.add_argument("--streams", type=int, default=2, choices=[1, 2],
+                    help="heads of a layer alternate over this many streams, each with its own workspace (2, the "
+                         "default: one head's small kernels and the tile kernel's last partial wave overlap the "
+                         "next head; the per-stage events then include that overlap)")
     return ap.parse_args()
 
 
@@ -245,12 +246,13 @@ def run_ours(a, wl, rank, world, local_rank):
     ev_done = [torch.cuda.Event() for _ in my_heads]
     nev = 6
 
-    def layer(stage_events=None, gather=True):
-        for s_ in head_streams[1:]:
+    def layer(stage_events=None, gather=True, nstreams=None):
+        streams = head_streams[:nstreams] if nstreams else head_streams
+        for s_ in streams[1:]:
             s_.wait_stream(comp)
         for i, h in enumerate(my_heads):
             evs = stage_events[i] if stage_events is not None else None
-            hs = head_streams[i % len(head_streams)]
+            hs = streams[i % len(streams)]
             with torch.cuda.stream(hs):
                 F.forward_into(*dq[h], None, None, exact_leaves=E, out=out[h], lse=lse[h],
                                workspace=head_ws[i % len(head_ws)], stage_events=evs, stream=hs, store=store)
@@ -261,7 +263,7 @@ def run_ours(a, wl, rank, world, local_rank):
                 side.wait_event(ev_done[i])
                 with torch.cuda.stream(side):
                     shard.gather_slot(obf[h], out=gathered[i])
-        for s_ in head_streams[1:]:
+        for s_ in streams[1:]:
             comp.wait_stream(s_)
         if world > 1 and gather:
             comp.wait_stream(side)
@@ -294,7 +296,9 @@ def run_ours(a, wl, rank, world, local_rank):
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record(comp)
     for s in range(a.steps):
-        layer(stage_evs[s])
+        # with one head stream the stage events are taken here; with two they would include the overlap
+        # of the two streams' kernels, so they come from a separate pass below
+        layer(stage_evs[s] if a.streams == 1 else None)
     t1.record(comp)
     barrier()
     clk = clocks.stop()
@@ -315,6 +319,14 @@ def run_ours(a, wl, rank, world, local_rank):
                        "bytes_per_rank_per_step": len(my_heads) * world * n * 128 * 2,
                        "how": "bf16 outputs all-gathered (NCCL) per local head on a side stream, overlapped with the "
                               "next head; exposed = layer time - the same layer without the gathers"}
+    stage_timing = "CUDA events around each stage of every head in the timed region (heads on one stream)"
+    if a.streams > 1:
+        barrier()
+        for s in range(a.steps):
+            layer(stage_evs[s], gather=False, nstreams=1)
+        barrier()
+        stage_timing = ("CUDA events around each stage of every head in a separate pass of the same layers with the "
+                        "heads on one stream (the timed region's two streams overlap consecutive heads)")
     for w in head_ws:
         F.device_status(w)
     stage_names = ["prep", "stats", "rowmax", "route", "tile"]
@@ -529,7 +541,8 @@ def run_ours(a, wl, rank, world, local_rank):
                            "l2": "inputs larger than L2: 2.4 GB of distinct q/k/v per layer, "
                                  + ("1.0" if fp8 else "1.6") + " GB leaf state per head",
                            "parallelism": f"heads/{world}" + (" + bf16 output all_gather (NCCL)" if world > 1 else "")},
-                "stage_ms_per_head": stage_ms, "stage_roofline": stage_roof, "gather": gather_info, "modes": modes,
+                "stage_ms_per_head": stage_ms, "stage_timing": stage_timing, "stage_roofline": stage_roof,
+                "gather": gather_info, "modes": modes,
                 **parity,
                 "roofline": roof, "cpu_baseline": cpu,
                 "e2e": e2e,
