@@ -3,7 +3,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload cfg3|cfg2]
 
-Workload (default cfg3): one layer = 24 heads of a 32x48x84 video latent
+Workload (default cfg3: the benchmark's full-resolution configuration): one layer = 24 heads of a 32x48x84 video latent
 (129,024 tokens), d=128, bf16 Q/K/V from the seeded smooth-field generator (htrc_b200.synth), leaf 64,
 tile 64, fast mode (256 exact leaves), INT8 store.  A step is one whole layer: every head runs the full
 operator (key pack, tile prep, leaf stats, row-max selection, routing, far+near attention).  Under

@@ -68,6 +68,7 @@ SIGNATURES = {
     "htrc_tile_attention_fp8": (ctypes.c_int, [_p, _p, _i64, _i32, _i64, _i64, _i32, _p, _p, _p, _p, _p, _p, _p, _i32,
                                                _i64, _p, _p, _i64, _i32, _i32, _f32, _p, _p, _p, _p, _p, _p, _p]),
     "htrc_flat_forward_static_ws": (ctypes.c_int, [ctypes.POINTER(HtrcFlatArgs), _p]),
+    "htrc_flat_static_ws_status": (ctypes.c_int, [ctypes.POINTER(_i32), _p]),
     "htrc_fake_quant": (ctypes.c_int, [_p, _i32, _i64, _i32, _i32, _i32, _p, _i32, _p]),
     "htrc_dequant_rows": (ctypes.c_int, [_p, _i64, _p, _i64, _i64, _i32, _p, _p]),
     "htrc_selftest_wait_timeout": (ctypes.c_int, [_p, _i64, _p]),

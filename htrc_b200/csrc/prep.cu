@@ -107,8 +107,8 @@ __global__ void __launch_bounds__(256) pack_rows_kernel(const T* __restrict__ x,
   }
 }
 
-// The same codes with one scale per block of 64 consecutive rows (an extension: BASELINE's
-// "per-64-token-block absmax" scales; the reference's are per row): s = max(amax_block|x| * (1/127), 1e-20),
+// The same codes with one scale per block of 64 consecutive rows (an extension: one absmax scale per
+// 64-token block; the reference's are per row): s = max(amax_block|x| * (1/127), 1e-20),
 // written once per row.  One CTA per block; warp w holds rows 8w .. 8w + 7 in registers, the block maximum
 // goes through shared memory.
 template <typename T, int ROUND>

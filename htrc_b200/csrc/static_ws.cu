@@ -10,10 +10,12 @@
 //
 // The array is shared by every call on a device and keeps the last call's contents; calls that
 // overlap on the GPU (different streams, or different host threads) race on it, so issue them in
-// order on one stream.  The device status word at the start of the array is cleared by each call.
+// order on one stream.  The device status word at the start of the array is cleared by each call;
+// htrc_flat_static_ws_status reads it (and clears it) after a call.
 // The first call on each device looks up the array's device address (cudaGetSymbolAddress, with that
-// device current); make that first call before any stream capture.  No cudaMalloc, cudaFree or
-// allocating library routine is called.
+// device current); make that first call before any stream capture.  The address is cached for the life
+// of the process, so this entry point must not be used across cudaDeviceReset (which reloads the module
+// elsewhere).  No cudaMalloc, cudaFree or allocating library routine is called.
 #include <mutex>
 
 #include "common.cuh"
@@ -61,6 +63,15 @@ int htrc_flat_forward_static_ws(const HtrcFlatArgs* args, htrc_stream_t stream) 
   a.workspace = ws;
   a.workspace_bytes = kStaticWorkspaceBytes;
   return htrc_flat_forward(&a, stream);
+}
+
+int htrc_flat_static_ws_status(int32_t* status_out, htrc_stream_t stream) {
+  if (status_out == nullptr) return HTRC_ERR_ARG;
+  void* ws = nullptr;
+  int rc = static_workspace(&ws);
+  if (rc != HTRC_OK) return rc;
+  // same read-and-clear as htrc_flat_status, on the status word at the start of the static array
+  return htrc_flat_status(ws, status_out, stream);
 }
 
 }  // extern "C"

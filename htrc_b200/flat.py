@@ -23,7 +23,7 @@ expansion centre, far-field state and routing (:223-231).
 Additions over the reference: ``return_lse=True`` also returns the log-partition per query
 (logit units, scale * q.k), ``backend`` accepts "cuda"/"b200" as names of the same path, and
 ``qk_scale_block=64`` gives the INT8 keys one scale per 64-key leaf and the query rows one per tile
-(BASELINE's "per-64-token-block absmax" scales; the reference's are per key and per row, the default).
+(one absmax scale per 64-token block; the reference's are per key and per row, the default).
 """
 from __future__ import annotations
 
@@ -265,6 +265,45 @@ def _workspace(ws, nbytes, device):
     return b
 
 
+def _check_buffers(qd, kb, vb, tk, tv, out, lse, workspace, route_mask, tile, group):
+    """Shapes, dtypes, contiguity and device of every buffer the C ABI will read or write, checked on the
+    host before any launch (the library trusts its pointers and sizes)."""
+    def need(t, name, shape, dtypes):
+        if not isinstance(t, torch.Tensor) or tuple(t.shape) != tuple(shape) or t.dtype not in dtypes \
+                or not t.is_contiguous():
+            got = "None" if not isinstance(t, torch.Tensor) else \
+                f"{tuple(t.shape)} {t.dtype}" + ("" if t.is_contiguous() else " non-contiguous")
+            raise ValueError(f"{name}: a contiguous {'/'.join(str(d).split('.')[-1] for d in dtypes)} tensor "
+                             f"{list(shape)} expected, got {got}")
+
+    if qd is None or qd.dim() != 2:
+        raise ValueError("qd: [N, 128] expected")
+    n, m = int(qd.shape[0]), int(kb.shape[0]) if kb is not None and kb.dim() == 2 else -1
+    need(qd, "qd", (n, DIM), (torch.float32, torch.bfloat16))
+    need(kb, "kb", (m, DIM), (torch.bfloat16,))
+    need(vb, "vb", (m, DIM), (torch.bfloat16,))
+    need(out, "out", (n, DIM), (torch.float32,))
+    if lse is not None:
+        need(lse, "lse", (n,), (torch.float32,))
+    if tk is not None or tv is not None:
+        nt_ = int(tk.shape[0]) if tk is not None and tk.dim() == 2 else -1
+        need(tk, "tk", (nt_, DIM), (torch.float32,))
+        need(tv, "tv", (nt_, DIM), (torch.float32,))
+    if workspace is None or workspace.dtype != torch.uint8 or not workspace.is_contiguous():
+        raise ValueError("workspace: a contiguous uint8 tensor expected")
+    if route_mask is not None:
+        if route_mask.dtype != torch.uint8 or not route_mask.is_contiguous():
+            raise ValueError("route_mask: a contiguous uint8 tensor [groups, leaf_pitch(nb)]")
+        rows = -(-(-(-n // int(tile))) // max(1, int(group)))
+        pitch = -(-(m // LEAF) // 16) * 16        # htrc_leaf_pitch: leaves rounded up to 16 (host-side)
+        if route_mask.numel() < rows * pitch:
+            raise ValueError(f"route_mask: at least {rows} x {pitch} bytes expected ([ceil(tiles / group), "
+                             f"leaf_pitch(nb)]), got {route_mask.numel()}")
+    devs = {t.device for t in (qd, kb, vb, out, lse, tk, tv, workspace, route_mask) if t is not None}
+    if len(devs) != 1 or next(iter(devs)).type != "cuda":
+        raise ValueError(f"every buffer must be on one CUDA device, got {sorted(str(d) for d in devs)}")
+
+
 def forward_into(qd, kb, vb, tk, tv, *, exact_leaves, sink_leaves=0, tile_chunk=0, scale=None, out, lse=None,
                  workspace, stream=None, stage_events=None, group=1, order=_lib.ORDER_SEQ, tile=TILE,
                  curvature=_lib.CURV_LIN, store=_lib.STORE_INT8, qk_scale_block=0, route_mask=None):
@@ -274,8 +313,7 @@ def forward_into(qd, kb, vb, tk, tv, *, exact_leaves, sink_leaves=0, tile_chunk=
     include/htrc_flat.h); group / order: ``group_of(kern)`` / ``order_code(order)``; tile: 64 or 32;
     store: ``_lib.STORES[store]``; qk_scale_block: 0 or 64; route_mask: optional uint8
     [ceil(nt / group), leaf_pitch(nb)] device tensor that receives the routing masks (1 = leaf exact)."""
-    if route_mask is not None and (route_mask.dtype != torch.uint8 or not route_mask.is_contiguous()):
-        raise ValueError("route_mask: a contiguous uint8 tensor [groups, leaf_pitch(nb)]")
+    _check_buffers(qd, kb, vb, tk, tv, out, lse, workspace, route_mask, tile, group)
     a = _args(qd, kb, vb, tk, tv, exact_leaves, sink_leaves, tile_chunk, scale, out, lse, workspace, stage_events,
               group, order, tile, curvature, store, qk_scale_block, route_mask)
     check(lib().htrc_flat_forward(a, stream_ptr(stream)), "htrc_flat_forward")

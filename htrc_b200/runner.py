@@ -83,7 +83,7 @@ class FlatRunner:
         base.update(MODES[mode])
         base["leaf"] = _flat.LEAF
         overrides = dict(overrides)
-        if "kern" in overrides:                          # merge, do not replace, the kernel knobs
+        if "kern" in overrides:                          # a caller's kern dict updates PROD's launch knobs key by key
             base["kern"] = {**base.get("kern", {}), **overrides.pop("kern")}
         base.update(overrides)
         base["sink_leaves"] = int(sink_leaves)

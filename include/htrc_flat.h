@@ -95,7 +95,7 @@ typedef struct HtrcFlatArgs {
                               row scales, fp16 far-field dots, bf16 near field; needs HTRC_CURV_LIN) */
   int32_t qk_scale_block;  /* 0: the reference's INT8 scales (per key, per query row); 64: an extension with no
                               reference counterpart, one scale per 64 keys (a leaf) and per query tile
-                              (BASELINE's "per-64-token-block absmax"); HTRC_STORE_INT8 only */
+                              (one absmax scale per 64-token block); HTRC_STORE_INT8 only */
   uint8_t* route_mask;     /* optional debug export (NULL = none): [ceil(nt / group), P] uint8 routing masks, the
                               rows htrc_route writes (1 = the leaf is evaluated exactly for that centre row) */
 } HtrcFlatArgs;
@@ -252,10 +252,16 @@ int htrc_tile_attention_fp8(const uint16_t* qb, const uint16_t* dqh, int64_t n_q
  * htrc_flat_workspace_size() exceeds 64 MiB are rejected with HTRC_ERR_TOO_LARGE (about 16k queries
  * and keys at the default routing; a smaller tile_chunk admits more).  All calls share the array: calls
  * that overlap on the GPU race, so issue them in order on one stream.  The status word is cleared at
- * the start of every call and is not readable through htrc_flat_status.  The first call on a device
- * looks up the array's address; make it before any stream capture.  Allocates nothing.
+ * the start of every call; read it after a call with htrc_flat_static_ws_status.  The first call on a
+ * device looks up the array's address and caches it; make it before any stream capture, and do not use
+ * this entry point across cudaDeviceReset.  Allocates nothing.
  * This entry point has no counterpart in the reference. */
 int htrc_flat_forward_static_ws(const HtrcFlatArgs* args, htrc_stream_t stream);
+
+/* The device status word of htrc_flat_forward_static_ws's array, read and cleared like htrc_flat_status
+ * (synchronises `stream`; *status_out receives the HTRC_STATUS_* bits of the calls since the last read).
+ * Like its forward entry point it has no counterpart in the reference and allocates nothing. */
+int htrc_flat_static_ws_status(int32_t* status_out, htrc_stream_t stream);
 
 /* Low-bit round trip of x [rows, dim] (h3/htrc_flat.py:68-97 `fake_quant`, a simulation of quantised
  * inputs): every group of `group` consecutive values of a row (0: the whole row; HTRC_FQ_FP4 with 0:

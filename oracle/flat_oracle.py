@@ -22,7 +22,7 @@ Precision of the restatement: the leaf statistics are computed in float64 and ro
 float32 (the reference computes them with tf32 tensor-core dots on the GPU); every quantisation
 formula is evaluated in float32 exactly as written in the reference; the softmax sums are float64.
 Division is IEEE float32 (the reference's torch code uses IEEE division; its Triton kernels use
-``/`` whose GPU lowering may be approximate).
+``/`` whose GPU lowering may be approximate; the CUDA kernels divide with IEEE rounding too).
 
 Parity status: pinned against outputs of the reference itself run in the build container
 (``tests/golden/make_golden.py`` runs h3/htrc_flat.py on CPU; the fixtures it wrote live in
@@ -87,7 +87,7 @@ def pack_rows_half_away(x):
 
 def pack_blocks(x, block, rounding):
     """Extension, not in the reference (its scales are per row): the INT8 pack with one scale per block
-    of `block` consecutive rows, BASELINE's "per-64-token-block absmax" Q/K scales.
+    of `block` consecutive rows (one absmax scale per 64-token block of keys or queries).
     s_b = max(amax_block|x| * (1/127), 1e-20); every row of the block is coded with s_b, half-even
     (rounding "even": the keys' rule, h3/htrc_flat.py:216-218) or half-away ("away": the query rows' rule,
     h3/htrc_flat_triton.py:110-117).  Returns (x8 int8 [R, D], s float32 [R]: the block's scale per row)."""

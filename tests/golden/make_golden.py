@@ -1,9 +1,9 @@
 """Generate the golden fixtures of the flat HTRC production path by running the REFERENCE itself.
 
-Run once, in a container that has the reference checkout (default ``/root/reference``; override
-with ``HTRC_REFERENCE``):
+Run once, in a container that has the reference checkout, naming its directory with ``HTRC_REFERENCE``
+or ``--reference``:
 
-    TRITON_INTERPRET=1 python tests/golden/make_golden.py [case ...]
+    TRITON_INTERPRET=1 python tests/golden/make_golden.py --reference <checkout> [case ...]
 
 It imports the reference's ``h3/htrc_flat.py`` unmodified and calls
 ``flat_attention(q, k, v, **PROD, leaf=L, exact_leaves=E, ...)`` on CPU tensors with Triton's
@@ -35,7 +35,6 @@ import torch
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parents[1]
-REF = Path(os.environ.get("HTRC_REFERENCE", "/root/reference"))
 sys.path.insert(0, str(REPO))
 
 from htrc_b200 import synth  # noqa: E402
@@ -103,8 +102,19 @@ def _shim():
     B.create_fp_to_fp = create_fp_to_fp
 
 
-def _load_reference():
-    spec = importlib.util.spec_from_file_location("_ref_htrc_flat", REF / "h3" / "htrc_flat.py")
+def _reference_dir(argv):
+    """The reference checkout: ``--reference DIR`` on the command line, else $HTRC_REFERENCE (required)."""
+    if "--reference" in argv:
+        i = argv.index("--reference")
+        return Path(argv[i + 1]), argv[:i] + argv[i + 2:]
+    env = os.environ.get("HTRC_REFERENCE")
+    if not env:
+        raise SystemExit("name the reference checkout: --reference DIR or HTRC_REFERENCE=DIR")
+    return Path(env), argv
+
+
+def _load_reference(ref):
+    spec = importlib.util.spec_from_file_location("_ref_htrc_flat", ref / "h3" / "htrc_flat.py")
     mod = importlib.util.module_from_spec(spec)
     sys.modules["_ref_htrc_flat"] = mod
     spec.loader.exec_module(mod)
@@ -297,10 +307,11 @@ def torch_spec_fixture(flat):
 
 
 def main():
+    ref, argv = _reference_dir(sys.argv[1:])
     _shim()
-    flat = _load_reference()
+    flat = _load_reference(ref)
     torch.manual_seed(0)
-    only = set(sys.argv[1:])
+    only = set(argv)
     if not only or "torch_spec" in only:
         np.savez_compressed(HERE / "torch_spec.npz", **torch_spec_fixture(flat))
         print("torch_spec -> torch_spec.npz")

@@ -1,5 +1,5 @@
 """GPU parity of the per-block INT8 scale extension (`qk_scale_block=64`: one scale per 64-key leaf and
-per query tile, BASELINE's "per-64-token-block absmax"; the reference's scales are per key and per row,
+per query tile: one absmax scale per 64-token block; the reference's scales are per key and per row,
 so this mode has no reference fixture and is pinned to the oracle's restatement, `pack_blocks`)."""
 import numpy as np
 import pytest

@@ -263,3 +263,31 @@ def test_qk_scale_block_option_is_checked():
     assert L.htrc_flat_workspace_size(ctypes.byref(a), ctypes.byref(nbytes)) == _lib.HTRC_ERR_ARG
     a.qk_scale_block, a.store = 64, _lib.STORE_FP8
     assert L.htrc_flat_workspace_size(ctypes.byref(a), ctypes.byref(nbytes)) == _lib.HTRC_ERR_UNSUPPORTED
+
+
+def test_forward_into_checks_every_buffer_before_any_launch():
+    """forward_into rejects wrong shapes, dtypes, contiguity, an undersized route mask and buffers off the GPU
+    with ValueError on the host (no kernel is launched: these tensors live on the CPU)."""
+    n, m = 200, 256
+    q = torch.zeros((n, 128), dtype=torch.float32)
+    k = torch.zeros((m, 128), dtype=torch.bfloat16)
+    v = torch.zeros((m, 128), dtype=torch.bfloat16)
+    out = torch.zeros((n, 128), dtype=torch.float32)
+    lse = torch.zeros((n,), dtype=torch.float32)
+    ws = torch.zeros((1024,), dtype=torch.uint8)
+    good = dict(exact_leaves=2, out=out, lse=lse, workspace=ws)
+
+    def call(qd=q, kb=k, vb=v, tk=None, tv=None, **kw):
+        F.forward_into(qd, kb, vb, tk, tv, **{**good, **kw})
+
+    for kw, what in [(dict(kb=k.float()), "kb"), (dict(vb=v[:128]), "vb"), (dict(out=out[:, :64]), "out"),
+                     (dict(out=out.double()), "out"), (dict(lse=lse[:10]), "lse"), (dict(qd=q.half()), "qd"),
+                     (dict(out=torch.zeros((128, n)).T), "out"), (dict(workspace=ws.float()), "workspace"),
+                     (dict(tk=torch.zeros((3, 128)), tv=None), "tv"),
+                     (dict(route_mask=torch.zeros((3, 16), dtype=torch.uint8)), "route_mask"),
+                     (dict(route_mask=torch.zeros((4, 16), dtype=torch.int32)), "route_mask")]:
+        with pytest.raises(ValueError, match=what):
+            call(**kw)
+    # right shapes: ceil(200 / 64) = 4 tiles, leaf_pitch(256 / 64 = 4) = 16 -> 4 x 16 mask; still on the CPU
+    with pytest.raises(ValueError, match="CUDA device"):
+        call(route_mask=torch.zeros((4, 16), dtype=torch.uint8))

@@ -6,9 +6,11 @@ not grow once it has started.  Such callers pass q, k, v, out and lse as usual; 
 lives in a fixed 64 MiB array inside the library instead of a caller-provided workspace.
 
 These tests call it through the C ABI twice in a row (different inputs and routing budgets each time,
-so stale contents of the shared array would show) and compare with the ordinary entry point,
-htrc_flat_forward, on a caller-allocated workspace, within the tolerance of the parity tests.  This file
-is named so that pytest collects it last; it also passes alone in a fresh process.
+so stale contents of the shared array would show) and require bitwise the results of the ordinary entry
+point, htrc_flat_forward, on a caller-allocated workspace (the kernels fix every reduction order, so the
+workspace's address cannot change a bit), a clean device status word after each call (read through
+htrc_flat_static_ws_status), and an unchanged amount of free device memory across the calls.  This file is
+named so that pytest collects it last; it also passes alone in a fresh process.
 """
 import ctypes
 
@@ -17,10 +19,6 @@ import pytest
 import torch
 
 pytestmark = pytest.mark.gpu
-
-OUT_TOL = 2e-2
-LSE_TOL = 1e-3
-
 
 @pytest.fixture(scope="module")
 def dev():
@@ -51,11 +49,20 @@ def _inputs(grid, seed, dev):
     return q.to(dev), k.to(dev), v.to(dev)
 
 
+def _static_status(L, _lib, stream):
+    st = ctypes.c_int32(-1)
+    _lib.check(L.htrc_flat_static_ws_status(st, stream), "htrc_flat_static_ws_status")
+    return st.value
+
+
+CASES = [((4, 32, 32), 901, 16), ((8, 16, 32), 902, 5)]
+
+
 def test_static_workspace_matches_allocated_workspace_twice_in_a_row(dev):
     from htrc_b200 import _lib
     L = _lib.lib()
     stream = _lib.stream_ptr()
-    for grid, seed, E in [((4, 32, 32), 901, 16), ((8, 16, 32), 902, 5)]:
+    for grid, seed, E in CASES:
         q, k, v = _inputs(grid, seed, dev)
         n = q.shape[0]
         ref_out = torch.empty((n, 128), dtype=torch.float32, device=dev)
@@ -70,10 +77,35 @@ def test_static_workspace_matches_allocated_workspace_twice_in_a_row(dev):
         lse = torch.full((n,), float("nan"), dtype=torch.float32, device=dev)
         b = _args(q, k, v, out, lse, E)
         _lib.check(L.htrc_flat_forward_static_ws(b, stream), "htrc_flat_forward_static_ws")
+        assert _static_status(L, _lib, stream) == 0
         torch.cuda.synchronize()
         assert torch.isfinite(out).all() and torch.isfinite(lse).all()
-        assert float((out - ref_out).abs().max()) <= OUT_TOL
-        assert float((lse - ref_lse).abs().mean()) <= LSE_TOL
+        assert torch.equal(out, ref_out)
+        assert torch.equal(lse, ref_lse)
+
+
+def test_static_workspace_allocates_nothing(dev):
+    """Free device memory is the same before and after repeated calls (after one warm-up call per case, which
+    loads the kernels' code)."""
+    from htrc_b200 import _lib
+    L = _lib.lib()
+    stream = _lib.stream_ptr()
+    calls = []
+    for grid, seed, E in CASES:
+        q, k, v = _inputs(grid, seed, dev)
+        out = torch.empty((q.shape[0], 128), dtype=torch.float32, device=dev)
+        lse = torch.empty((q.shape[0],), dtype=torch.float32, device=dev)
+        calls.append((q, k, v, out, lse, _args(q, k, v, out, lse, E)))
+    for c in calls:
+        _lib.check(L.htrc_flat_forward_static_ws(c[-1], stream), "htrc_flat_forward_static_ws")
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info(dev)[0]
+    for _ in range(3):
+        for c in calls:
+            _lib.check(L.htrc_flat_forward_static_ws(c[-1], stream), "htrc_flat_forward_static_ws")
+            assert _static_status(L, _lib, stream) == 0
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info(dev)[0] == free0
 
 
 def test_static_workspace_rejects_problems_beyond_its_size(dev):
