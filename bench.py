@@ -59,9 +59,17 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-modes", action="store_true", help="skip the per-mode head timings")
+    ap.add_argument("--no-ref-gpu", action="store_true",
+                    help="skip timing the reference's own Triton operator on this GPU (installed under baseline/_ref)")
+    ap.add_argument("--ref-steps", type=int, default=3, help="layers timed for the reference's GPU operator")
+    ap.add_argument("--no-ref-cpu", action="store_true",
+                    help="skip timing the reference's own CPU implementations (torch backend, NumPy model)")
     ap.add_argument("--store", default="int8", choices=["int8", "fp8"],
                     help="far-field state: int8 (the production path, the headline) or fp8 (e4m3 state, store='fp8'; "
                          "no oracle sample)")
+    ap.add_argument("--precision", default="tf32", choices=["tf32", "fp32"],
+                    help="leaf-statistics dots: tf32 operands (PROD's setting, the reference's production path; the "
+                         "default) or float32-accurate")
     ap.add_argument("--streams", type=int, default=2, choices=[1, 2],
                     help="heads of a layer alternate over this many streams, each with its own workspace (2, the "
                          "default: one head's small kernels and the tile kernel's last partial wave overlap the "
@@ -145,8 +153,9 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def oracle_sample(q, k, v, exact_leaves, tiles, threads):
-    """CPU oracle on a tile sample of one head: (per-head seconds, per-sample seconds, out rows, lse rows)."""
+def oracle_sample(q, k, v, exact_leaves, tiles, threads, precision="fp32"):
+    """CPU oracle on a tile sample of one head: (per-head seconds, per-sample seconds, out rows, lse rows,
+    the prepared head)."""
     from threadpoolctl import threadpool_limits
 
     from oracle import flat_oracle as O
@@ -154,9 +163,264 @@ def oracle_sample(q, k, v, exact_leaves, tiles, threads):
         t0 = time.perf_counter()
         prep = O.prepare_head(q, k, v)
         t1 = time.perf_counter()
-        out, lse = O.attention_tiles(prep, tiles, exact_leaves=exact_leaves)
+        out, lse = O.attention_tiles(prep, tiles, exact_leaves=exact_leaves, precision=precision)
         t2 = time.perf_counter()
-    return t1 - t0, t2 - t1, out, lse
+    return t1 - t0, t2 - t1, out, lse, prep
+
+
+def oracle_routing(prep, tiles, exact_leaves, threads, precision="fp32"):
+    """The oracle's routing masks (bool [len(tiles), nb]) of sampled tiles: its own float64 leaf statistics,
+    INT8 state, row-max selection and top-E (parity check; not timed)."""
+    from threadpoolctl import threadpool_limits
+
+    from oracle import flat_oracle as O
+    with threadpool_limits(limits=threads):
+        mu, qt = prep["mu"][tiles], prep["qt"][tiles]
+        g, lz, vbf = O.leaf_stats(mu, prep["k"], prep["v"], prep["leaf"], 1.0 / math.sqrt(prep["k"].shape[1]),
+                                  precision)
+        g8, sg, _ = O.state_int8(g, vbf)
+        _, _, dq8, sdq = O.query_codes(qt, mu)
+        _, excl = O.route(O.rowmax_select(dq8, sdq, g8, sg, lz), exact_leaves)
+    return excl != 0
+
+
+def full_size_codes(F, head, prep, exact_leaves, threads):
+    """Bit-exactness of the INT8 codes at the full size of one head (parity check; not timed): key codes and
+    scales (k8, ks), tile centres, query and offset codes and scales (q8, sq, dq8, sdq) of every row, from
+    the device's stage-by-stage run against the oracle."""
+    import numpy as np
+    from threadpoolctl import threadpool_limits
+
+    from oracle import flat_oracle as O
+    st = F.run_stages(*head, exact_leaves=exact_leaves)
+    with threadpool_limits(limits=threads):
+        q8, sq, dq8, sdq = O.query_codes(prep["qt"], prep["mu"])
+    nt = prep["qt"].shape[0]
+    dev = {k_: st[k_].cpu().numpy() for k_ in ("k8", "ks", "mu", "q8", "sq", "dq8", "sdq")}
+    res = {"k8": bool(np.array_equal(dev["k8"], prep["k8"])), "ks": bool(np.array_equal(dev["ks"], prep["ks"])),
+           "mu": bool(np.array_equal(dev["mu"], prep["mu"])),
+           "q8": bool(np.array_equal(dev["q8"].reshape(nt, 64, -1), q8)),
+           "sq": bool(np.array_equal(dev["sq"].reshape(nt, 64), sq)),
+           "dq8": bool(np.array_equal(dev["dq8"].reshape(nt, 64, -1), dq8)),
+           "sdq": bool(np.array_equal(dev["sdq"].reshape(nt, 64), sdq)),
+           "rows": prep["n"], "keys": int(prep["k8"].shape[0])}
+    del st
+    return res
+
+
+# ------------------------------------------------------------------------------------------ installed reference
+def load_installed_reference():
+    """The unmodified reference, installed under baseline/_ref by baseline/install_ref.sh (or the directory
+    $HTRC_REFERENCE names): h3/htrc_flat.py with its Triton kernels (h3/htrc_flat_triton.py),
+    h3/htrc_flat_runner.py and the NumPy package htrc_reference.  Returns {"flat", "runner", "model", "root"};
+    raises when it is absent."""
+    import importlib.util
+    roots = [os.environ.get("HTRC_REFERENCE"), str(ROOT / "baseline" / "_ref")]
+    root = next((Path(r) for r in roots if r and (Path(r) / "h3" / "htrc_flat.py").exists()), None)
+    if root is None:
+        raise FileNotFoundError("reference not installed: no h3/htrc_flat.py under baseline/_ref or $HTRC_REFERENCE")
+
+    def load(name, path):
+        if name not in sys.modules:
+            spec = importlib.util.spec_from_file_location(name, path)
+            mod = importlib.util.module_from_spec(spec)
+            sys.modules[name] = mod
+            spec.loader.exec_module(mod)
+        return sys.modules[name]
+
+    # the runner loads htrc_flat.py under this module name (h3/htrc_flat_runner.py:38-45, :90): one copy
+    flat = load("_apl_htrc_flat", root / "h3" / "htrc_flat.py")
+    runner = load("_ref_htrc_flat_runner", root / "h3" / "htrc_flat_runner.py")
+    model = None
+    for cand in (root, root / "src"):
+        if (cand / "htrc_reference" / "model.py").exists():
+            model = load("_ref_htrc_reference_model", cand / "htrc_reference" / "model.py")
+            break
+    return {"flat": flat, "runner": runner, "model": model, "root": str(root)}
+
+
+def reference_gpu_leg(wl, dev, heads, dq, ours, steps, oracle_rows=None):
+    """The reference's own flat operator on this GPU, on the same inputs: ``flat_attention(**PROD, leaf=64)``
+    (h3/htrc_flat.py:391-399 -> _flat_triton :181-276, Triton kernels h3/htrc_flat_triton.py) eager with a
+    reused workspace dict, and through its CUDA-graph ``FlatRunner(mode="fast", leaf=64)``
+    (h3/htrc_flat_runner.py:85-177) with the chunk planned from free memory.  Head 0 once more in one chunk
+    (``tile_chunk >= tiles``) to read its routing mask ``ws["excl"]`` and split partials ``ws["pm"]``/``ws["pl"]``
+    (log-Z = logsumexp over the splits of pm + log pl), compared with this library's outputs ``ours``
+    ({"out", "lse", "mask"} of head 0) and, on ``oracle_rows`` = (rows, oracle out, oracle lse), with the CPU
+    oracle: how far each GPU operator sits from the float64 restatement on the same rows."""
+    import torch
+    try:
+        ref = load_installed_reference()
+        import triton  # noqa: F401
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"{type(e).__name__}: {e}"[:300]}
+    flat, runner = ref["flat"], ref["runner"]
+    comp = torch.cuda.current_stream(dev)
+    cfg = {**flat.PROD, **runner.MODES["fast"], "leaf": 64, "exact_leaves": wl["exact_leaves"]}
+    res = {"impl": "h3/htrc_flat.py flat_attention(**PROD, **MODES['fast'], leaf=64), Triton backend, unmodified, "
+                   "from " + ("baseline/_ref" if "baseline" in ref["root"] else "$HTRC_REFERENCE"),
+           "config": {k: (v if not isinstance(v, dict) else dict(v)) for k, v in cfg.items()}}
+    n, m = int(dq[heads[0]][0].shape[0]), int(dq[heads[0]][1].shape[0])
+    nt, nb = -(-n // 64), m // 64
+    t_c = time.time()
+    try:
+        ws = {}
+        for h in heads:                                     # warm-up layer: compiles the Triton kernels
+            flat.flat_attention(*dq[h], ws=ws, **cfg)
+        torch.cuda.synchronize(dev)
+        res["compile_and_first_layer_s"] = time.time() - t_c
+
+        def timed(fn, k):
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(comp)
+            for _ in range(k):
+                fn()
+            e1.record(comp)
+            torch.cuda.synchronize(dev)
+            return e0.elapsed_time(e1) / k
+
+        clocks = ClockSampler(dev.index)
+        clocks.start()
+        res["eager_ms_per_layer"] = timed(lambda: [flat.flat_attention(*dq[h], ws=ws, **cfg) for h in heads], steps)
+        res["eager_clocks"] = clocks.stop()
+        del ws
+        torch.cuda.empty_cache()
+        free = torch.cuda.mem_get_info(dev)[0]
+        r = runner.FlatRunner(n, m, free_bytes=free, mode="fast", leaf=64, device=dev)
+        res["runner"] = {"tile_chunk": r.cfg["tile_chunk"], "graph": r.graph is not None, "graph_error": r.graph_error}
+        for h in heads[:2]:
+            r.head(*dq[h])
+        clocks = ClockSampler(dev.index)
+        clocks.start()
+        res["runner_ms_per_layer"] = timed(lambda: [r.head(*dq[h]) for h in heads], steps)
+        res["runner_clocks"] = clocks.stop()
+        r.close()
+        del r
+        torch.cuda.empty_cache()
+        res["ms_per_layer"] = min(res["eager_ms_per_layer"], res["runner_ms_per_layer"])
+        res["heads_timed"] = len(heads)
+        res["steps"] = steps
+        # head 0 in one chunk: routing mask and log-Z of the reference against ours
+        ws0 = {}
+        out_r = flat.flat_attention(*dq[heads[0]], ws=ws0, **{**cfg, "tile_chunk": nt}).float()
+        excl_r = ws0["excl"][:nt].ne(0)
+        pm, pl = ws0["pm"][:nt].float(), ws0["pl"][:nt].float()
+        mm = pm.amax(1, keepdim=True)
+        mm = torch.where(torch.isinf(mm), torch.zeros_like(mm), mm)
+        lse_r = (mm[:, 0] + torch.log((pl * torch.exp(pm - mm)).sum(1))).reshape(-1)[:n]
+        mask = ours["mask"][:nt, :nb].ne(0)
+        tiles_agree = (mask == excl_r).all(1)
+        rows_agree = tiles_agree.repeat_interleave(64)[:n]
+        d_out = (ours["out"] - out_r).abs().amax(1)
+        d_lse = (ours["lse"] - lse_r).abs()
+        p = {"routing_agreement": (mask == excl_r).float().mean().item(),
+             "tiles_all_agree": tiles_agree.float().mean().item(),
+             "out_maxabs_all_rows": d_out.max().item(),
+             "out_maxabs_agreeing_tiles": d_out[rows_agree].max().item() if bool(rows_agree.any()) else None,
+             "rows_over_2e-2": int((d_out > 2e-2).sum().item()),
+             "lse_mae": d_lse.mean().item(), "lse_maxabs": d_lse.max().item(),
+             "precision": cfg["precision"],
+             "how": "this library's route_mask / out / lse of head 0 (the same precision setting) against the "
+                    "reference's ws['excl'], output and logsumexp of its split partials ws['pm'], ws['pl'] (one "
+                    "chunk), same inputs, same B200"}
+        if oracle_rows is not None:
+            rows, o_out, o_lse = oracle_rows
+            ri = torch.as_tensor(rows, device=dev)
+            oo, ol = torch.as_tensor(o_out, device=dev), torch.as_tensor(o_lse, device=dev)
+            p["vs_oracle_sample"] = {
+                "rows": int(len(rows)),
+                "ref_out_maxabs": (out_r[ri] - oo).abs().max().item(), "ref_lse_mae": (lse_r[ri] - ol).abs().mean().item(),
+                "ours_out_maxabs": (ours["out"][ri] - oo).abs().max().item(),
+                "ours_lse_mae": (ours["lse"][ri] - ol).abs().mean().item(),
+                "how": "both GPU operators against the CPU oracle (the float64 restatement at the same precision "
+                       "setting) on its sampled tiles"}
+        g = torch.Generator().manual_seed(5)
+        rows = torch.randperm(n, generator=g)[:256].to(dev)
+        qs = dq[heads[0]][0][rows].float()
+        s_ = (qs @ dq[heads[0]][1].float().T) / math.sqrt(128)
+        ex = torch.softmax(s_, -1) @ dq[heads[0]][2].float()
+        p["rel_l2_vs_exact_ref"] = float((out_r[rows] - ex).norm() / ex.norm())
+        p["rel_l2_vs_exact_ours"] = float((ours["out"][rows] - ex).norm() / ex.norm())
+        res["parity_head0"] = p
+        del ws0, out_r, s_
+        torch.cuda.empty_cache()
+    except Exception as e:  # noqa: BLE001
+        res["error"] = f"{type(e).__name__}: {e}"[:400]
+    return res
+
+
+def reference_cpu_legs(threads, budget_tiles=64, budget_s=20.0):
+    """The reference's own CPU implementations, timed on this host with ``threads`` threads: its float32 torch
+    backend ``flat_attention(backend="torch")`` (h3/htrc_flat.py:279-388) on configuration 1 (one head,
+    N = M = 4096, d 64), on the 24 configuration-2 heads (as many as fit in ``budget_s``, the rest
+    extrapolated) and on a ``budget_tiles``-tile sample of one configuration-3 head (x tiles x 24:
+    extrapolated); and the NumPy hierarchical model ``build_forest`` + ``evaluate``
+    (src/htrc_reference/model.py:68-137) on all 4096 configuration-1 queries (leaf 64, opening threshold
+    0.02, one expansion centre: the mean query)."""
+    import numpy as np
+    import torch
+
+    from htrc_b200 import synth
+    try:
+        ref = load_installed_reference()
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"{type(e).__name__}: {e}"[:300]}
+    flat, model = ref["flat"], ref["model"]
+    old = torch.get_num_threads()
+    torch.set_num_threads(threads)
+    res = {"kind": "reference-torch", "cores": threads}
+    try:
+        q1, k1, v1 = synth.cluster_inputs(4096, 64, seed=0)
+        tq, tk, tv = (torch.from_numpy(x) for x in (q1, k1, v1))
+        kw = dict(backend="torch", tile=64, leaf=64, exact_leaves=16, tile_chunk=32, precision="fp32")
+        flat.flat_attention(tq, tk, tv, **kw)
+        t0 = time.perf_counter()
+        for _ in range(3):
+            flat.flat_attention(tq, tk, tv, **kw)
+        res["cfg1_torch_flat_ms_per_head"] = (time.perf_counter() - t0) / 3 * 1e3
+        res["cfg1_torch_flat_config"] = "N = M = 4096, d 64, leaf 64, tile 64, exact_leaves 16, fp32"
+        if model is not None:
+            scale = 1.0 / math.sqrt(64)
+            qd, kd, vd = q1.astype(np.float64), k1.astype(np.float64), v1.astype(np.float64)
+            centre = qd.mean(0) * scale
+            t0 = time.perf_counter()
+            forest = model.build_forest(kd, vd, centre, leaf_size=64)
+            t1 = time.perf_counter()
+            for i in range(qd.shape[0]):
+                model.evaluate(kd, vd, qd[i] * scale, centre, forest, opening_threshold=0.02)
+            t2 = time.perf_counter()
+            res["cfg1_numpy_hierarchical"] = {"build_forest_ms": (t1 - t0) * 1e3, "evaluate_s_all_queries": t2 - t1,
+                                              "queries": int(qd.shape[0]), "threads": 1,
+                                              "note": "single-threaded Python/NumPy; one expansion centre (the mean "
+                                                      "query; the model takes one centre)"}
+        kw = dict(backend="torch", tile=64, leaf=64, exact_leaves=256, tile_chunk=32, precision="fp32")
+        t_all, done = 0.0, 0
+        for h in range(24):
+            q, k, v = synth.head_inputs(synth.GRID_SMALL, 128, head=h)
+            t0 = time.perf_counter()
+            flat.flat_attention(q.float(), k.float(), v.float(), **kw)
+            t_all += time.perf_counter() - t0
+            done += 1
+            if t_all > budget_s:
+                break
+        res["cfg2_torch_flat"] = {"ms_per_layer": t_all / done * 24 * 1e3, "heads_timed": done,
+                                  "extrapolated": done < 24, "timed_s": t_all,
+                                  "sample": f"{done} whole heads of 16,384 tokens" + (f", x24/{done}" if done < 24 else "")}
+        q, k, v = synth.head_inputs(synth.GRID_FULL, 128, head=0)
+        n = q.shape[0]
+        nt = -(-n // 64)
+        t0 = time.perf_counter()
+        flat.flat_attention(q[:budget_tiles * 64].float(), k.float(), v.float(), **kw)
+        dt = time.perf_counter() - t0
+        res["cfg3_torch_flat"] = {"ms_per_layer": dt / budget_tiles * nt * 24 * 1e3, "extrapolated": True,
+                                  "timed_s": dt, "sample": f"{budget_tiles} of {nt} query tiles of head 0, "
+                                                          f"x{nt}/{budget_tiles} x24"}
+    except Exception as e:  # noqa: BLE001
+        res["error"] = f"{type(e).__name__}: {e}"[:300]
+    finally:
+        torch.set_num_threads(old)
+    return res
 
 
 # ------------------------------------------------------------------------------------------ reference arm
@@ -175,7 +439,7 @@ def run_reference(a, wl, rank):
     preps, times = [], []
     for step in range(a.warmup + a.steps):
         tiles = np.sort(rng.choice(nt, size=a.cpu_tiles, replace=False))
-        dp, dt, _, _ = oracle_sample(qn, kn, vn, wl["exact_leaves"], tiles, threads)
+        dp, dt, _, _, _ = oracle_sample(qn, kn, vn, wl["exact_leaves"], tiles, threads)
         if step >= a.warmup:
             preps.append(dp)
             times.append(dt)
@@ -230,6 +494,7 @@ def run_ours(a, wl, rank, world, local_rank):
     from htrc_b200 import _lib as _L
     store = _L.STORES[a.store]
     fp8 = store == _L.STORE_FP8
+    prec = F.precision_code(a.precision)
     wsb = F.workspace_bytes(n, m, E, 0, 0, 0, store=store)
     ws = F.new_workspace(wsb, dev)
     comp = torch.cuda.current_stream(dev)
@@ -255,7 +520,8 @@ def run_ours(a, wl, rank, world, local_rank):
             hs = streams[i % len(streams)]
             with torch.cuda.stream(hs):
                 F.forward_into(*dq[h], None, None, exact_leaves=E, out=out[h], lse=lse[h],
-                               workspace=head_ws[i % len(head_ws)], stage_events=evs, stream=hs, store=store)
+                               workspace=head_ws[i % len(head_ws)], stage_events=evs, stream=hs, store=store,
+                               precision=prec)
                 if world > 1 and gather:
                     obf[h].copy_(out[h])
                     ev_done[i].record(hs)
@@ -337,20 +603,37 @@ def run_ours(a, wl, rank, world, local_rank):
     # ---- parity at full size on a tile sample of head 0 (rank 0): mean |dlogZ| vs the oracle
     parity = {}
     cpu = None
+    ref_gpu = None
+    oracle_rows = None
+    h0 = my_heads[0]
+    mask0 = None
+    if rank == 0:
+        # head 0 once more with its routing mask exported (the kernels are deterministic: same out / lse)
+        mask0 = torch.zeros((nt, F.leaf_pitch(nb)), dtype=torch.uint8, device=dev)
+        F.forward_into(*dq[h0], None, None, exact_leaves=E, out=out[h0], lse=lse[h0], workspace=ws, store=store,
+                       route_mask=mask0, precision=prec)
+        torch.cuda.synchronize(dev)
+        F.device_status(ws)
     if rank == 0 and not a.no_cpu and not fp8:
-        h0 = my_heads[0]
         qn, kn, vn = (t.float().numpy() for t in host[h0])
         rng = np.random.default_rng(1)
         tiles = np.sort(rng.choice(nt, size=a.cpu_tiles, replace=False))
         threads = host_threads()
-        dp, dt, ro, rl = oracle_sample(qn, kn, vn, E, tiles, threads)
+        dp, dt, ro, rl, prep = oracle_sample(qn, kn, vn, E, tiles, threads, a.precision)
         rows = (tiles[:, None] * 64 + np.arange(64)[None, :]).reshape(-1)
         valid = rows < n
+        oracle_rows = (rows[valid], ro[valid], rl[valid])
         lse_d = lse[h0].cpu().numpy()[rows[valid]]
         out_d = out[h0].cpu().numpy()[rows[valid]]
+        excl_o = oracle_routing(prep, tiles, E, threads, a.precision)
+        excl_d = mask0[torch.as_tensor(tiles, device=dev)][:, :nb].cpu().numpy()
         parity = {"logz_mae": float(np.abs(lse_d - rl[valid]).mean()),
                   "out_maxabs": float(np.abs(out_d - ro[valid]).max()),
-                  "sample": f"{len(tiles)} random tiles of head {h0} vs oracle/flat_oracle.py"}
+                  "routing_agreement_sample": float((excl_o == (excl_d != 0)).mean()),
+                  "sample": f"{len(tiles)} random tiles of head {h0} vs oracle/flat_oracle.py at precision "
+                            f"{a.precision} (the oracle computes its own float64 leaf statistics, selection and "
+                            f"routing for them)"}
+        parity["codes_full_size"] = full_size_codes(F, dq[h0], prep, E, threads)
         # error of the operator against exact softmax attention on the same rows
         qs = dq[h0][0][torch.as_tensor(rows[valid], device=dev)].float()
         kk, vv = dq[h0][1].float(), dq[h0][2].float()
@@ -365,6 +648,13 @@ def run_ours(a, wl, rank, world, local_rank):
             cpu = {"value": cpu_ms, "unit": "ms/layer", "cores": threads, "kind": "port",
                    "sample": f"head {h0}: per-head preparation + {len(tiles)} query tiles ({len(tiles) * 64} rows of "
                              f"{n}) through oracle/flat_oracle.py; layer = {H} x (prep + {nt} x per-tile)"}
+            if not a.no_ref_cpu:
+                cpu["reference_torch"] = reference_cpu_legs(threads)
+    if rank == 0 and world == 1 and not a.no_ref_gpu and not fp8:
+        ref_gpu = reference_gpu_leg(wl, dev, my_heads, dq, {"out": out[h0], "lse": lse[h0], "mask": mask0},
+                                    max(1, min(a.steps, a.ref_steps)), oracle_rows)
+        if "ms_per_layer" in ref_gpu:
+            ref_gpu["ours_over_ref"] = ms / ref_gpu["ms_per_layer"]
 
     # ---- end to end through the public API with pinned host buffers
     e2e = None
@@ -399,7 +689,8 @@ def run_ours(a, wl, rank, world, local_rank):
                 hs.wait_event(out_done[b])
                 with torch.cuda.stream(hs):
                     htrc_b200.forward_into(*stage_in[b], None, None, exact_leaves=E, store=store, out=stage_out[b][0],
-                                           lse=stage_out[b][1], workspace=head_ws[i % len(head_ws)], stream=hs)
+                                           lse=stage_out[b][1], workspace=head_ws[i % len(head_ws)], stream=hs,
+                                           precision=prec)
                 comp_done[b].record(hs)
                 s_out.wait_event(comp_done[b])
                 with torch.cuda.stream(s_out):
@@ -537,14 +828,15 @@ def run_ours(a, wl, rank, world, local_rank):
                 "config": {"workload": wl["name"].replace("INT8", "fp8 (e4m3) state") if fp8 else wl["name"],
                            "tokens": n, "heads": H,
                            "dim": 128, "leaf": 64, "tile": 64, "store": a.store,
-                           "exact_leaves": E, "heads_per_gpu": len(my_heads), "head_streams": a.streams,
+                           "exact_leaves": E, "precision": a.precision, "heads_per_gpu": len(my_heads),
+                           "head_streams": a.streams,
                            "l2": "inputs larger than L2: 2.4 GB of distinct q/k/v per layer, "
                                  + ("1.0" if fp8 else "1.6") + " GB leaf state per head",
                            "parallelism": f"heads/{world}" + (" + bf16 output all_gather (NCCL)" if world > 1 else "")},
                 "stage_ms_per_head": stage_ms, "stage_timing": stage_timing, "stage_roofline": stage_roof,
                 "gather": gather_info, "modes": modes,
                 **parity,
-                "roofline": roof, "cpu_baseline": cpu,
+                "roofline": roof, "cpu_baseline": cpu, "reference_gpu": ref_gpu,
                 "e2e": e2e,
                 "gpu_launches": a.steps * len(my_heads) * LAUNCHES_PER_HEAD, "clocks": clk}
         print(json.dumps(line), flush=True)

@@ -16,6 +16,8 @@ ORDER_SEQ, ORDER_KMEANS = 0, 1
 CURV_LIN, CURV_ISO = 0, 1
 STORE_INT8, STORE_FP8 = 0, 1
 STORES = {"int8": STORE_INT8, "fp8": STORE_FP8}
+PREC_FP32, PREC_TF32 = 0, 1
+PRECISIONS = {"fp32": PREC_FP32, "tf32": PREC_TF32}
 FQ_FORMATS = {"int8": 1, "int4": 2, "fp8": 3, "fp4": 4}
 ROUND_HALF_EVEN, ROUND_HALF_AWAY = 0, 1
 STATUS_BITS = {1: "bounded wait gave up", 2: "routed leaf index out of range", 4: "non-finite log-partition"}
@@ -37,7 +39,7 @@ class HtrcFlatArgs(ctypes.Structure):
         ("out", _p), ("lse", _p),
         ("stage_events", ctypes.POINTER(_p)), ("n_stage_events", _i32),
         ("group", _i32), ("order", _i32), ("curvature", _i32), ("store", _i32), ("qk_scale_block", _i32),
-        ("route_mask", _p),
+        ("route_mask", _p), ("precision", _i32),
     ]
 
 
@@ -52,7 +54,7 @@ SIGNATURES = {
     "htrc_kmeans_scratch_size": (ctypes.c_int, [_i64, ctypes.POINTER(ctypes.c_size_t)]),
     "htrc_kmeans_order": (ctypes.c_int, [_p, _i32, _i64, _i32, _p, _p, ctypes.c_size_t, _p]),
     "htrc_leaf_stats": (ctypes.c_int, [_p, _p, _i64, _i64, _i64, _p, _p, _i64, _i32, _i32, _f32, _p, _p, _p, _p, _p, _p,
-                                       _p, _p]),
+                                       _i32, _p, _p]),
     "htrc_rowmax_select": (ctypes.c_int, [_p, _p, _p, _i64, _i64, _i32, _p, _p, _p, _p, _i64, _i32, _p, _p, _p]),
     "htrc_route": (ctypes.c_int, [_p, _i64, _i64, _i32, _i32, _i32, _p, _p, _p]),
     "htrc_tile_attention": (ctypes.c_int, [_p, _p, _p, _p, _i64, _i32, _i64, _i64, _i32, _p, _p, _p, _p, _p, _p, _i32,
@@ -60,10 +62,10 @@ SIGNATURES = {
     "htrc_tail_partial": (ctypes.c_int, [_p, _i32, _i64, _i32, _p, _p, _i32, _f32, _p, _p]),
     "htrc_pack_int8_blocks": (ctypes.c_int, [_p, _i32, _i64, _i32, _i32, _i32, _p, _p, _p, _p]),
     "htrc_tile_prep_ex": (ctypes.c_int, [_p, _i32, _i64, _i32, _i32, _p, _i32, _p, _p, _p, _p, _p, _p, _p, _p, _i32,
-                                         _p]),
-    "htrc_tile_prep_fp8": (ctypes.c_int, [_p, _i32, _i64, _i32, _i32, _p, _i32, _p, _p, _p, _p, _p, _p]),
+                                         _i32, _p]),
+    "htrc_tile_prep_fp8": (ctypes.c_int, [_p, _i32, _i64, _i32, _i32, _p, _i32, _p, _p, _p, _p, _p, _i32, _p]),
     "htrc_leaf_stats_fp8": (ctypes.c_int, [_p, _p, _i64, _i64, _i64, _p, _p, _i64, _i32, _i32, _f32, _p, _p, _p, _p, _p,
-                                           _p, _p]),
+                                           _i32, _p, _p]),
     "htrc_rowmax_select_fp8": (ctypes.c_int, [_p, _i64, _i64, _i32, _p, _p, _p, _i64, _i32, _p, _p, _p]),
     "htrc_tile_attention_fp8": (ctypes.c_int, [_p, _p, _i64, _i32, _i64, _i64, _i32, _p, _p, _p, _p, _p, _p, _p, _i32,
                                                _i64, _p, _p, _i64, _i32, _i32, _f32, _p, _p, _p, _p, _p, _p, _p]),

@@ -193,11 +193,16 @@ __device__ __forceinline__ int64_t source_row(const int32_t* perm, int64_t n, in
   return perm ? static_cast<int64_t>(__ldg(perm + c)) : c;
 }
 
+// The centre in float32, and as the two bf16 parts the leaf statistics multiply with: hi + lo is the centre to
+// ~2^-16 relative (precision "fp32"), or exactly its tf32 operand value, the low 13 mantissa bits cleared, when
+// tmask = kTf32Mask (precision "tf32": the reference's tensor-core dots read float32 operands that way; an
+// 11-bit significand splits exactly into bf16 hi + lo)
 __device__ __forceinline__ void store_centre(int64_t c, int col, float m, float* mu, uint16_t* mu_hi,
-                                             uint16_t* mu_lo) {
+                                             uint16_t* mu_lo, uint32_t tmask) {
   mu[c * 128 + col] = m;
-  const __nv_bfloat16 hi = __float2bfloat16_rn(m);
-  const __nv_bfloat16 lo = __float2bfloat16_rn(__fsub_rn(m, __bfloat162float(hi)));
+  const float mt = __uint_as_float(__float_as_uint(m) & tmask);
+  const __nv_bfloat16 hi = __float2bfloat16_rn(mt);
+  const __nv_bfloat16 lo = __float2bfloat16_rn(__fsub_rn(mt, __bfloat162float(hi)));
   mu_hi[c * 128 + col] = __bfloat16_as_ushort(hi);
   mu_lo[c * 128 + col] = __bfloat16_as_ushort(lo);
 }
@@ -209,7 +214,7 @@ template <typename T>
 __global__ void __launch_bounds__(128) group_centre_kernel(const T* __restrict__ q, const int32_t* __restrict__ perm,
                                                            int64_t n, int trows, int64_t nt, int group,
                                                            float* __restrict__ mu, uint16_t* __restrict__ mu_hi,
-                                                           uint16_t* __restrict__ mu_lo) {
+                                                           uint16_t* __restrict__ mu_lo, uint32_t tmask) {
   const int64_t g = blockIdx.x;
   const int col = threadIdx.x;
   double s = 0.0;
@@ -224,7 +229,7 @@ __global__ void __launch_bounds__(128) group_centre_kernel(const T* __restrict__
         s += static_cast<double>(__uint_as_float(static_cast<uint32_t>(__ldg(q + src * 128 + col)) << 16));
     }
   }
-  store_centre(g, col, static_cast<float>(s / static_cast<double>(group * trows)), mu, mu_hi, mu_lo);
+  store_centre(g, col, static_cast<float>(s / static_cast<double>(group * trows)), mu, mu_hi, mu_lo, tmask);
 }
 
 // One CTA (4 warps) per tile of T query rows (held as 64 rows): the tile's centre (group 1; else the
@@ -240,7 +245,7 @@ __global__ void __launch_bounds__(128) tile_prep_kernel(const T* __restrict__ q,
                                                         uint16_t* __restrict__ mu_hi, uint16_t* __restrict__ mu_lo,
                                                         int8_t* __restrict__ q8, float* __restrict__ sq,
                                                         int8_t* __restrict__ dq8, float* __restrict__ sdq,
-                                                        float* __restrict__ dd, int qblock) {
+                                                        float* __restrict__ dd, int qblock, uint32_t tmask) {
   __shared__ float qs[64][129];
   __shared__ float mus[128];
   __shared__ float tmx[4];
@@ -270,7 +275,7 @@ __global__ void __launch_bounds__(128) tile_prep_kernel(const T* __restrict__ q,
     for (int r = 0; r < nreal; ++r) s += static_cast<double>(qs[r][tid]);
     const float m = static_cast<float>(s / static_cast<double>(nreal));
     mus[tid] = m;
-    store_centre(t, tid, m, mu, mu_hi, mu_lo);
+    store_centre(t, tid, m, mu, mu_hi, mu_lo, tmask);
   } else {
     mus[tid] = mu[static_cast<int64_t>(t / group) * 128 + tid];
   }
@@ -322,23 +327,24 @@ __global__ void __launch_bounds__(128) tile_prep_kernel(const T* __restrict__ q,
 
 void launch_tile_prep(const void* q, int dtype, int64_t n, int tile_rows, const int32_t* perm, int group, float* mu,
                       uint16_t* mu_hi, uint16_t* mu_lo, int8_t* q8, float* sq, int8_t* dq8, float* sdq, float* dd,
-                      bool fp8, bool qblock, cudaStream_t st) {
+                      bool fp8, bool qblock, bool tf32, cudaStream_t st) {
   const int tr = tile_rows == 32 ? 32 : 64;
+  const uint32_t tmask = tf32 ? kTf32Mask : 0xFFFFFFFFu;
   const int64_t nt = (n + tr - 1) / tr;
   const int g = group > 1 ? group : 1;
   const unsigned ng = static_cast<unsigned>((nt + g - 1) / g);
   if (dtype == HTRC_DTYPE_BF16) {
     const uint16_t* qb = static_cast<const uint16_t*>(q);
-    if (g > 1) group_centre_kernel<uint16_t><<<ng, 128, 0, st>>>(qb, perm, n, tr, nt, g, mu, mu_hi, mu_lo);
+    if (g > 1) group_centre_kernel<uint16_t><<<ng, 128, 0, st>>>(qb, perm, n, tr, nt, g, mu, mu_hi, mu_lo, tmask);
     auto k = fp8 ? tile_prep_kernel<uint16_t, true> : tile_prep_kernel<uint16_t, false>;
     k<<<static_cast<unsigned>(nt), 128, 0, st>>>(qb, perm, n, tr, g, mu, mu_hi, mu_lo, q8, sq, dq8, sdq, dd,
-                                                 qblock ? 1 : 0);
+                                                 qblock ? 1 : 0, tmask);
   } else {
     const float* qf = static_cast<const float*>(q);
-    if (g > 1) group_centre_kernel<float><<<ng, 128, 0, st>>>(qf, perm, n, tr, nt, g, mu, mu_hi, mu_lo);
+    if (g > 1) group_centre_kernel<float><<<ng, 128, 0, st>>>(qf, perm, n, tr, nt, g, mu, mu_hi, mu_lo, tmask);
     auto k = fp8 ? tile_prep_kernel<float, true> : tile_prep_kernel<float, false>;
     k<<<static_cast<unsigned>(nt), 128, 0, st>>>(qf, perm, n, tr, g, mu, mu_hi, mu_lo, q8, sq, dq8, sdq, dd,
-                                                 qblock ? 1 : 0);
+                                                 qblock ? 1 : 0, tmask);
   }
 }
 

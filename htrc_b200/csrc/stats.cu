@@ -10,8 +10,11 @@
 //                                  K and V of a stage adjacent in shared memory as one MN-major operand)
 //   epilogue: g = scale * G -> (g8, sg) half-away INT8 with the row abs-max scale; vbar -> bf16;
 //   g8/vbar rows staged in shared memory and written by TMA stores, lz/sg by plain stores.
-// This is the arithmetic of h3/htrc_flat_triton.py:41-85 (_stats_kernel, I8=1); the hi/lo splits keep
-// the products at ~2^-16 relative precision (the reference uses tf32 dots).
+// This is the arithmetic of h3/htrc_flat_triton.py:41-85 (_stats_kernel, I8=1).  Precision "fp32" (the
+// reference's PREC="ieee"): the hi/lo splits keep the products at ~2^-16 relative precision.  Precision "tf32"
+// (PREC="tf32", the reference's production setting): the float32 operands of both dots, the centre and the
+// softmax weights, enter with their low 13 mantissa bits cleared, as the reference's tensor-core dots read them
+// on sm_100 (its log-partitions match that model to ~1e-5); hi + lo then represents each operand exactly.
 // ISO adds the isotropic curvature of each (centre, leaf) (h3/htrc_flat.py:331-333, the torch
 // backend's curvature="iso"): c = 0.5 / D * max(tr, 0), tr = scale^2 (sum_s w_s |k_s|^2 - |sum_s w_s k_s|^2);
 // the softmax warps form sum_s w_s |k_s|^2 from the key norms staged with K/V, the epilogue |G|^2 from
@@ -95,7 +98,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                       const __grid_constant__ CUtensorMap tm_g8, const __grid_constant__ CUtensorMap tm_vb,
                       float* __restrict__ sg_out, float* __restrict__ lz_out, int64_t pitch, int64_t t0, int64_t tc,
                       int nb, int leaves_per_cta, float scale, const float* __restrict__ kn2,
-                      float* __restrict__ cv_out, float* __restrict__ sv_out, int* status) {
+                      float* __restrict__ cv_out, float* __restrict__ sv_out, int* status, uint32_t wmask) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Bars* bars = reinterpret_cast<Bars*>(smem + kOffBar);
@@ -317,7 +320,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t hi[32], lo[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const float2 w = mul2(make_float2(a[2 * i], a[2 * i + 1]), make_float2(rz, rz));
+          float2 w = mul2(make_float2(a[2 * i], a[2 * i + 1]), make_float2(rz, rz));
+          w.x = __uint_as_float(__float_as_uint(w.x) & wmask);     // precision "tf32": the operand value
+          w.y = __uint_as_float(__float_as_uint(w.y) & wmask);
           hi[i] = pack_bf16x2(w.x, w.y);
           const float2 lw = sub2(w, make_float2(__uint_as_float(hi[i] << 16), __uint_as_float(hi[i] & 0xFFFF0000u)));
           lo[i] = pack_bf16x2(lw.x, lw.y);
@@ -527,7 +532,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 int launch_leaf_stats(const LeafStatsMaps& maps, float* sg, float* lz, int64_t pitch, int64_t t0, int64_t tc, int nb,
-                      float scale, const float* kn2, float* cv, float* sv, int* status, int num_sms, cudaStream_t st) {
+                      float scale, const float* kn2, float* cv, float* sv, int* status, int num_sms, bool tf32,
+                      cudaStream_t st) {
   static bool attr_done[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -547,7 +553,8 @@ int launch_leaf_stats(const LeafStatsMaps& maps, float* sg, float* lz, int64_t p
   auto kernel = sv != nullptr ? leaf_stats_kernel<false, true>
                                : (cv != nullptr ? leaf_stats_kernel<true, false> : leaf_stats_kernel<false, false>);
   kernel<<<dim3(bx, by), kThreads, kSmemBytes, st>>>(maps.mu_hi, maps.mu_lo, maps.nt, maps.k, maps.v, maps.g8, maps.vb,
-                                                     sg, lz, pitch, t0, tc, nb, lpc, scale, kn2, cv, sv, status);
+                                                     sg, lz, pitch, t0, tc, nb, lpc, scale, kn2, cv, sv, status,
+                                                     tf32 ? kTf32Mask : 0xFFFFFFFFu);
   return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
 }
 

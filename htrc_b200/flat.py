@@ -20,6 +20,11 @@ by the reference's k-means permutation before tiling and writes the output back 
 (h3/htrc_flat.py:47-65, :146-147, :159-165); ``kern={"group": G}`` lets G consecutive tiles share one
 expansion centre, far-field state and routing (:223-231).
 
+Precision: ``precision="tf32"`` (PROD's setting) runs the leaf-statistics dots on tf32 operand values, the
+float32 centre and softmax weights with their low 13 mantissa bits cleared, which is how the reference's
+tensor-core dots read them on sm_100 (h3/htrc_flat_triton.py:57, :62-63); any other value runs them
+float32-accurate (the reference's "ieee").  The codes, routing and attention arithmetic are the same for both.
+
 Additions over the reference: ``return_lse=True`` also returns the log-partition per query
 (logit units, scale * q.k), ``backend`` accepts "cuda"/"b200" as names of the same path, and
 ``qk_scale_block=64`` gives the INT8 keys one scale per 64-key leaf and the query rows one per tile
@@ -194,13 +199,19 @@ def order_code(order) -> int:
     return _lib.ORDER_KMEANS if order == "kmeans" else _lib.ORDER_SEQ
 
 
+def precision_code(precision) -> int:
+    """The reference maps precision == "tf32" to tf32 dots and anything else to IEEE float32
+    (h3/htrc_flat.py:126-130)."""
+    return _lib.PREC_TF32 if precision == "tf32" else _lib.PREC_FP32
+
+
 def curvature_code(curvature) -> int:
     return _lib.CURV_ISO if curvature == "iso" else _lib.CURV_LIN
 
 
 def _args(qd, kb, vb, tk, tv, exact_leaves, sink_leaves, tile_chunk, scale, out=None, lse=None, ws=None,
           stage_events=None, group=1, order=_lib.ORDER_SEQ, tile=TILE, curvature=_lib.CURV_LIN,
-          store=_lib.STORE_INT8, qk_scale_block=0, route_mask=None):
+          store=_lib.STORE_INT8, qk_scale_block=0, route_mask=None, precision=_lib.PREC_TF32):
     a = _lib.HtrcFlatArgs()
     a.q = ptr(qd)
     a.q_dtype = _lib.DTYPE_BF16 if qd.dtype == torch.bfloat16 else _lib.DTYPE_F32
@@ -216,6 +227,7 @@ def _args(qd, kb, vb, tk, tv, exact_leaves, sink_leaves, tile_chunk, scale, out=
     a.group, a.order, a.curvature, a.store = int(group), int(order), int(curvature), int(store)
     a.qk_scale_block = int(qk_scale_block or 0)
     a.route_mask = ptr(route_mask)
+    a.precision = int(precision)
     if ws is not None:
         a.workspace, a.workspace_bytes = ptr(ws), int(ws.numel())
     if stage_events:
@@ -306,16 +318,18 @@ def _check_buffers(qd, kb, vb, tk, tv, out, lse, workspace, route_mask, tile, gr
 
 def forward_into(qd, kb, vb, tk, tv, *, exact_leaves, sink_leaves=0, tile_chunk=0, scale=None, out, lse=None,
                  workspace, stream=None, stage_events=None, group=1, order=_lib.ORDER_SEQ, tile=TILE,
-                 curvature=_lib.CURV_LIN, store=_lib.STORE_INT8, qk_scale_block=0, route_mask=None):
+                 curvature=_lib.CURV_LIN, store=_lib.STORE_INT8, qk_scale_block=0, route_mask=None,
+                 precision=_lib.PREC_TF32):
     """One head through ``htrc_flat_forward`` into caller-provided buffers (no allocation; CUDA-graph
     capturable).  qd [N, 128] f32/bf16, kb/vb [M, 128] bf16, out [N, 128] f32, lse [N] f32 or None;
     stage_events: optional list of torch.cuda.Event recorded between the stages (see
     include/htrc_flat.h); group / order: ``group_of(kern)`` / ``order_code(order)``; tile: 64 or 32;
     store: ``_lib.STORES[store]``; qk_scale_block: 0 or 64; route_mask: optional uint8
-    [ceil(nt / group), leaf_pitch(nb)] device tensor that receives the routing masks (1 = leaf exact)."""
+    [ceil(nt / group), leaf_pitch(nb)] device tensor that receives the routing masks (1 = leaf exact);
+    precision: ``_lib.PREC_TF32`` (the production setting of PROD, the default) or ``_lib.PREC_FP32``."""
     _check_buffers(qd, kb, vb, tk, tv, out, lse, workspace, route_mask, tile, group)
     a = _args(qd, kb, vb, tk, tv, exact_leaves, sink_leaves, tile_chunk, scale, out, lse, workspace, stage_events,
-              group, order, tile, curvature, store, qk_scale_block, route_mask)
+              group, order, tile, curvature, store, qk_scale_block, route_mask, precision)
     check(lib().htrc_flat_forward(a, stream_ptr(stream)), "htrc_flat_forward")
 
 
@@ -345,10 +359,11 @@ def flat_attention(q, k, v, *, tile=64, exact_leaves=64, order="seq", curvature=
     qsb = _check_scale_block(qk_scale_block, store)
     qd, kb, vb, tk, tv = _prep_inputs(q, k, v, tail, quant)
     grp, oc, cc, sc = group_of(kern), order_code(order), curvature_code(curvature), _lib.STORES[store]
+    pc = precision_code(precision)
     if prof is not None:
         st = run_stages(qd, kb, vb, tk, tv, exact_leaves=exact_leaves, sink_leaves=sink_leaves,
                         tile_chunk=tile_chunk, scale=scale, prof=prof, group=grp, order=oc, tile=tile, curvature=cc,
-                        store=sc, qk_scale_block=qsb)
+                        store=sc, qk_scale_block=qsb, precision=pc)
         return (st["out"], st["lse"]) if return_lse else st["out"]
     n = int(qd.shape[0])
     out = torch.empty((n, DIM), dtype=torch.float32, device=q.device)
@@ -358,7 +373,7 @@ def flat_attention(q, k, v, *, tile=64, exact_leaves=64, order="seq", curvature=
     w = _workspace(ws, nbytes, q.device)
     forward_into(qd, kb, vb, tk, tv, exact_leaves=exact_leaves, sink_leaves=sink_leaves,
                  tile_chunk=tile_chunk, scale=scale, out=out, lse=lse, workspace=w, group=grp, order=oc, tile=tile,
-                 curvature=cc, store=sc, qk_scale_block=qsb)
+                 curvature=cc, store=sc, qk_scale_block=qsb, precision=pc)
     return (out, lse) if return_lse else out
 
 
@@ -377,7 +392,7 @@ def flat_attention_heads(q, k, v, *, return_lse=False, ws=None, **cfg):
     h, n = int(q.shape[0]), int(q.shape[1])
     c = {**dict(tile=64, exact_leaves=64, order="seq", curvature="lin", tile_chunk=32, leaf=16, select="max",
                 backend="torch", store="fp32", dot="tf32", sel_stride=1, kern=None, quant=None, sink_leaves=0,
-                tail=None, scale=None, qk_scale_block=None), **cfg}
+                tail=None, scale=None, qk_scale_block=None, precision="fp32"), **cfg}
     _check_args(q[0], k[0], v[0], c["tile"], c["exact_leaves"], c["order"], c["curvature"], c["leaf"], c["select"],
                 c["backend"], c["store"], c["dot"], c["sel_stride"], c["quant"], c["sink_leaves"], c["tail"])
     qsb = _check_scale_block(c["qk_scale_block"], c["store"])
@@ -394,14 +409,15 @@ def flat_attention_heads(q, k, v, *, return_lse=False, ws=None, **cfg):
             w = _workspace(ws, nbytes, q.device)
         forward_into(qd, kb, vb, tk, tv, exact_leaves=c["exact_leaves"], sink_leaves=c["sink_leaves"],
                      tile_chunk=c["tile_chunk"], scale=c["scale"], out=out[i], lse=lse[i] if return_lse else None,
-                     workspace=w, group=grp, order=oc, tile=c["tile"], curvature=cc, store=sc, qk_scale_block=qsb)
+                     workspace=w, group=grp, order=oc, tile=c["tile"], curvature=cc, store=sc, qk_scale_block=qsb,
+                     precision=precision_code(c["precision"]))
     return (out, lse) if return_lse else out
 
 
 @torch.inference_mode()
 def run_stages(qd, kb, vb, tk=None, tv=None, *, exact_leaves, sink_leaves=0, tile_chunk=0, scale=None,
                prof=None, stream=None, group=1, order=_lib.ORDER_SEQ, tile=TILE, curvature=_lib.CURV_LIN,
-               store=_lib.STORE_INT8, qk_scale_block=0):
+               store=_lib.STORE_INT8, qk_scale_block=0, precision=_lib.PREC_TF32):
     """The same operator launched stage by stage through the C ABI's stage entry points, returning
     every intermediate (perm, k8, ks, mu, q8, sq, dq8, sdq, g8, sg, lz, vb, sel, idx, excl, out, lse; with
     store=STORE_FP8: perm, mu, qb, dqh, g8 / vb8 e4m3 codes, sg, sv, lz, sel, idx, excl, out, lse).
@@ -428,7 +444,7 @@ def run_stages(qd, kb, vb, tk=None, tv=None, *, exact_leaves, sink_leaves=0, til
             raise NotImplementedError("curvature='iso' is implemented on the INT8 path only")
         return _run_stages_fp8(qd, kb, vb, tk, tv, n=n, m=m, nt=nt, nb=nb, ng=ng, grp=grp, pitch=pitch, sink=sink,
                                kx=kx, sc=sc, qdt=qdt, tile=tile, tile_chunk=tile_chunk, exact_leaves=exact_leaves,
-                               order=order, s=s, tick=tick, e=e)
+                               order=order, s=s, tick=tick, e=e, precision=int(precision))
     r = dict(k8=e(m, DIM, dt=torch.int8), ks=e(m), mu=e(ng, DIM), mu_hi=e(ng, DIM, dt=torch.bfloat16),
              mu_lo=e(ng, DIM, dt=torch.bfloat16), q8=e(nt * TILE, DIM, dt=torch.int8), sq=e(nt * TILE),
              dq8=e(nt * TILE, DIM, dt=torch.int8), sdq=e(nt * TILE), g8=e(ng, nb, DIM, dt=torch.int8),
@@ -455,7 +471,7 @@ def run_stages(qd, kb, vb, tk=None, tv=None, *, exact_leaves, sink_leaves=0, til
     perm = ptr(r["perm"])
     check(L.htrc_tile_prep_ex(ptr(qd), qdt, n, DIM, tile, perm, grp, ptr(r["mu"]), ptr(r["mu_hi"]), ptr(r["mu_lo"]),
                               ptr(r["q8"]), ptr(r["sq"]), ptr(r["dq8"]), ptr(r["sdq"]), ptr(r["dd"]),
-                              int(qk_scale_block or 0), s), "htrc_tile_prep_ex")
+                              int(qk_scale_block or 0), int(precision), s), "htrc_tile_prep_ex")
     tail_part = None
     if tk is not None:
         tail_part = e(n, DIM + 2)
@@ -469,7 +485,8 @@ def run_stages(qd, kb, vb, tk=None, tv=None, *, exact_leaves, sink_leaves=0, til
             gc = min(gstep, ng - g0)
             check(L.htrc_leaf_stats(ptr(r["mu_hi"]), ptr(r["mu_lo"]), ng, g0, gc, ptr(kb), ptr(vb), m, DIM, LEAF, sc,
                                     ptr(r["g8"][g0]), ptr(r["sg"][g0]), ptr(r["lz"][g0]), ptr(r["vb"][g0]),
-                                    ptr(r["kn2"]), ptr(r["cv"][g0]) if iso else None, stp, s), "htrc_leaf_stats")
+                                    ptr(r["kn2"]), ptr(r["cv"][g0]) if iso else None, int(precision), stp, s),
+                  "htrc_leaf_stats")
     tick("stats")
     if far and kx > 0:
         check(L.htrc_rowmax_select(ptr(r["dq8"]), ptr(r["sdq"]), ptr(r["dd"]), 0, nt, grp, ptr(r["g8"]), ptr(r["sg"]),
@@ -489,7 +506,7 @@ def run_stages(qd, kb, vb, tk=None, tv=None, *, exact_leaves, sink_leaves=0, til
 
 
 def _run_stages_fp8(qd, kb, vb, tk, tv, *, n, m, nt, nb, ng, grp, pitch, sink, kx, sc, qdt, tile, tile_chunk,
-                    exact_leaves, order, s, tick, e):
+                    exact_leaves, order, s, tick, e, precision):
     """run_stages for the fp8 state (store="fp8"): tile prep with bf16 rows and fp16 offsets, e4m3 leaf
     statistics, fp8 row-max selection, routing and the fp8 tile kernel."""
     L = lib()
@@ -510,7 +527,7 @@ def _run_stages_fp8(qd, kb, vb, tk, tv, *, n, m, nt, nb, ng, grp, pitch, sink, k
               "htrc_kmeans_order")
     perm = ptr(r["perm"])
     check(L.htrc_tile_prep_fp8(ptr(qd), qdt, n, DIM, tile, perm, grp, ptr(r["mu"]), ptr(r["mu_hi"]), ptr(r["mu_lo"]),
-                               ptr(r["qb"]), ptr(r["dqh"]), s), "htrc_tile_prep_fp8")
+                               ptr(r["qb"]), ptr(r["dqh"]), precision, s), "htrc_tile_prep_fp8")
     tail_part = None
     if tk is not None:
         tail_part = e(n, DIM + 2)
@@ -524,7 +541,7 @@ def _run_stages_fp8(qd, kb, vb, tk, tv, *, n, m, nt, nb, ng, grp, pitch, sink, k
             gc = min(gstep, ng - g0)
             check(L.htrc_leaf_stats_fp8(ptr(r["mu_hi"]), ptr(r["mu_lo"]), ng, g0, gc, ptr(kb), ptr(vb), m, DIM, LEAF,
                                         sc, ptr(r["g8"][g0]), ptr(r["sg"][g0]), ptr(r["lz"][g0]), ptr(r["vb8"][g0]),
-                                        ptr(r["sv"][g0]), stp, s), "htrc_leaf_stats_fp8")
+                                        ptr(r["sv"][g0]), precision, stp, s), "htrc_leaf_stats_fp8")
     tick("stats")
     if far and kx > 0:
         check(L.htrc_rowmax_select_fp8(ptr(r["dqh"]), 0, nt, grp, ptr(r["g8"]), ptr(r["sg"]), ptr(r["lz"]), nb, DIM,

@@ -41,6 +41,28 @@ def head_inputs(grid=GRID_FULL, d=128, *, head=0, batch=0, block=0, base_seed=0,
     return q.to(dtype), k.to(dtype), v.to(dtype)
 
 
+def cluster_inputs(n=4096, d=64, *, clusters=64, swap=0.1, sigma=0.3, centre_std=2.0, seed=0):
+    """Configuration 1 of the benchmark (the CPU NumPy case), float32 NumPy arrays (q, k, v), each [n, d]:
+    ``clusters`` centres ~ N(0, centre_std^2 I); token i belongs to cluster i // (n / clusters) except a
+    ``swap`` fraction of tokens whose cluster is redrawn uniformly; q and k = centre + sigma * N(0, 1)
+    (independent memberships and noise), v ~ N(0, 1).  Seeded ``numpy.random.default_rng(seed)``."""
+    import numpy as np
+    rng = np.random.default_rng(int(seed))
+    cen = rng.standard_normal((clusters, d)) * centre_std
+    per = max(1, n // clusters)
+
+    def members():
+        ids = np.minimum(np.arange(n) // per, clusters - 1)
+        sw = rng.random(n) < swap
+        ids[sw] = rng.integers(0, clusters, int(sw.sum()))
+        return ids
+
+    q = cen[members()] + sigma * rng.standard_normal((n, d))
+    k = cen[members()] + sigma * rng.standard_normal((n, d))
+    v = rng.standard_normal((n, d))
+    return q.astype(np.float32), k.astype(np.float32), v.astype(np.float32)
+
+
 def lowrank_inputs(n, m, d=128, *, seed=1234, rank=24, noise=0.6, dtype=torch.bfloat16):
     """Low-rank mix + noise keys/queries, N(0, 1) values (CPU)."""
     gen = torch.Generator().manual_seed(int(seed))

@@ -48,6 +48,12 @@ enum { HTRC_CURV_LIN = 0, HTRC_CURV_ISO = 1 };
 enum { HTRC_ROUND_HALF_EVEN = 0, HTRC_ROUND_HALF_AWAY = 1 };
 enum { HTRC_FQ_INT8 = 1, HTRC_FQ_INT4 = 2, HTRC_FQ_FP8 = 3, HTRC_FQ_FP4 = 4 }; /* htrc_fake_quant formats */
 enum { HTRC_STORE_INT8 = 0, HTRC_STORE_FP8 = 1 };                             /* far-field state format */
+/* Precision of the leaf-statistics dots (the reference's precision= argument, h3/htrc_flat.py:101, :126-130):
+ * HTRC_PREC_FP32 ("fp32", the reference's PREC "ieee"): float32-accurate products (bf16 hi + lo splits of the
+ * float32 centre and softmax weights); HTRC_PREC_TF32 ("tf32", PROD's setting, h3/htrc_flat.py:391): the
+ * float32 operands enter as tf32, their low 13 mantissa bits cleared, the way the reference's tensor-core dots
+ * (h3/htrc_flat_triton.py:57, :62-63) read them on sm_100. */
+enum { HTRC_PREC_FP32 = 0, HTRC_PREC_TF32 = 1 };
 
 /* Device status bits (htrc_flat_status). */
 enum { HTRC_STATUS_WAIT_TIMEOUT = 1, HTRC_STATUS_BAD_INDEX = 2, HTRC_STATUS_NONFINITE = 4 };
@@ -98,6 +104,7 @@ typedef struct HtrcFlatArgs {
                               (one absmax scale per 64-token block); HTRC_STORE_INT8 only */
   uint8_t* route_mask;     /* optional debug export (NULL = none): [ceil(nt / group), P] uint8 routing masks, the
                               rows htrc_route writes (1 = the leaf is evaluated exactly for that centre row) */
+  int32_t precision;       /* HTRC_PREC_FP32 (0) or HTRC_PREC_TF32: precision of the leaf-statistics dots */
 } HtrcFlatArgs;
 
 /* nb rounded up to a multiple of 16: the row pitch of the per-(tile, leaf) scalar arrays. */
@@ -150,11 +157,13 @@ int htrc_kmeans_order(const void* q, int32_t q_dtype, int64_t n_queries, int32_t
 
 /* Leaf statistics of centre rows [t0, t0 + tc) (h3/htrc_flat_triton.py:41-85 `_stats_kernel`, I8 store):
  * g8 [tc, nb, dim] int8 and sg/lz [tc, P] f32, vb [tc, nb, dim] bf16.  mu_hi/mu_lo as written by
- * htrc_tile_prep (all nt centre rows: tiles, or groups of tiles); status: device int32 word or NULL. */
+ * htrc_tile_prep / htrc_tile_prep_ex (all nt centre rows: tiles, or groups of tiles); precision: HTRC_PREC_*
+ * for the softmax weights of the second dot (the centres' precision is set where mu_hi/mu_lo are written);
+ * status: device int32 word or NULL. */
 int htrc_leaf_stats(const uint16_t* mu_hi, const uint16_t* mu_lo, int64_t nt, int64_t t0, int64_t tc,
                     const uint16_t* k, const uint16_t* v, int64_t n_keys, int32_t dim, int32_t leaf, float scale,
-                    int8_t* g8, float* sg, float* lz, uint16_t* vb, const float* kn2, float* cv, int32_t* status,
-                    htrc_stream_t stream);
+                    int8_t* g8, float* sg, float* lz, uint16_t* vb, const float* kn2, float* cv, int32_t precision,
+                    int32_t* status, htrc_stream_t stream);
 /* kn2 / cv: both NULL, or the key norms |k|^2 [n_keys] (htrc_pack_int8's sqnorm) and the iso curvature
  * coefficients cv [tc, P] f32 = 0.5/D max(tr, 0) to write. */
 
@@ -202,10 +211,13 @@ int htrc_pack_int8_blocks(const void* x, int32_t dtype, int64_t rows, int32_t di
                           int32_t block_rows, int8_t* x8, float* scale, float* sqnorm, htrc_stream_t stream);
 
 /* htrc_tile_prep with q_scale_block = 0 (the same codes) or 64 (extension): the codes q8 of a tile's rows
- * share one scale from the tile's abs-max (sq holds it for every row); dq8 / sdq stay per row. */
+ * share one scale from the tile's abs-max (sq holds it for every row); dq8 / sdq stay per row.  precision
+ * HTRC_PREC_TF32: mu_hi + mu_lo = mu with its low 13 mantissa bits cleared, exactly (HTRC_PREC_FP32: as
+ * htrc_tile_prep); mu itself and the codes are the same for both. */
 int htrc_tile_prep_ex(const void* q, int32_t q_dtype, int64_t n_queries, int32_t dim, int32_t tile,
                       const int32_t* perm, int32_t group, float* mu, uint16_t* mu_hi, uint16_t* mu_lo, int8_t* q8,
-                      float* sq, int8_t* dq8, float* sdq, float* dd, int32_t q_scale_block, htrc_stream_t stream);
+                      float* sq, int8_t* dq8, float* sdq, float* dd, int32_t q_scale_block, int32_t precision,
+                      htrc_stream_t stream);
 
 /* ---- stage entry points of the fp8 state path (HTRC_STORE_FP8) ---- */
 
@@ -214,15 +226,15 @@ int htrc_tile_prep_ex(const void* q, int32_t q_dtype, int64_t n_queries, int32_t
  * rounded once). */
 int htrc_tile_prep_fp8(const void* q, int32_t q_dtype, int64_t n_queries, int32_t dim, int32_t tile,
                        const int32_t* perm, int32_t group, float* mu, uint16_t* mu_hi, uint16_t* mu_lo, uint16_t* qb,
-                       uint16_t* dqh, htrc_stream_t stream);
+                       uint16_t* dqh, int32_t precision, htrc_stream_t stream);   /* precision: as htrc_tile_prep_ex */
 
 /* Leaf statistics of centre rows [t0, t0 + tc) with the fp8 state (h3/htrc_flat_triton.py:41-85, FP8=1):
  * g8 [tc, nb, dim] e4m3 codes of g / sg, sg = max(amax|g| * (1/448), 1e-30); vb8 [tc, nb, dim] e4m3 codes
  * of vbar / sv with sv likewise; lz, sg, sv [tc, P] f32.  Codes are nearest even, saturated at 448. */
 int htrc_leaf_stats_fp8(const uint16_t* mu_hi, const uint16_t* mu_lo, int64_t nt, int64_t t0, int64_t tc,
                         const uint16_t* k, const uint16_t* v, int64_t n_keys, int32_t dim, int32_t leaf, float scale,
-                        uint8_t* g8, float* sg, float* lz, uint8_t* vb8, float* sv, int32_t* status,
-                        htrc_stream_t stream);
+                        uint8_t* g8, float* sg, float* lz, uint8_t* vb8, float* sv, int32_t precision,
+                        int32_t* status, htrc_stream_t stream);   /* precision: as htrc_leaf_stats */
 
 /* Row-max selection with the fp8 state (h3/htrc_flat_triton.py:214-254, FP8=1):
  * sel[t, l] = max_r (dqh_r . g_l) * sg_l + lz_l over the tile's 64 rows (fp16 operands, float32 sums);

@@ -19,7 +19,9 @@ dot="bf16", select="max", curvature="lin"``:
   split merge ............ h3/htrc_flat_triton.py:257-273 (normalised output) + log-Z (addition)
 
 Precision of the restatement: the leaf statistics are computed in float64 and rounded once to
-float32 (the reference computes them with tf32 tensor-core dots on the GPU); every quantisation
+float32, from float32 operands (precision "fp32") or from their tf32 operand values (precision "tf32",
+the reference's production setting on the GPU: the low 13 mantissa bits of the centre and of the softmax
+weights cleared, ``tf32_operand``); every quantisation
 formula is evaluated in float32 exactly as written in the reference; the softmax sums are float64.
 Division is IEEE float32 (the reference's torch code uses IEEE division; its Triton kernels use
 ``/`` whose GPU lowering may be approximate; the CUDA kernels divide with IEEE rounding too).
@@ -242,11 +244,22 @@ def tile_centres(q, tile):
     return qt, mu.astype(F32), n
 
 
-def leaf_stats(mu, k, v, leaf, scale):
+def tf32_operand(x):
+    """float32 values as a tf32 tensor-core dot reads them on sm_100: the low 13 mantissa bits cleared.  The
+    reference's Triton dots with input_precision="tf32" (h3/htrc_flat_triton.py:57, :62-63) behave this way on
+    B200: its log-partitions match a = scale (tf32(mu) . k) to ~1e-5, against ~1e-2 for rounding to nearest."""
+    b = np.ascontiguousarray(x, dtype=F32).view(np.uint32) & np.uint32(0xFFFFE000)
+    return b.view(F32)
+
+
+def leaf_stats(mu, k, v, leaf, scale, precision="fp32"):
     """Exact leaf cumulants at the tile centres (h3/htrc_flat_triton.py:41-85):
     a = scale mu.k_s, lz = logsumexp_s a, w = softmax a, g = scale sum w k, vbar = sum w v.
+    precision "tf32" (the reference's PREC="tf32", PROD's setting): mu and w enter the two dots as tf32
+    operand values (``tf32_operand``; k and v are bf16, exact in tf32).
     Returns float32 (g [nt, nb, D], lz [nt, nb], vbar [nt, nb, D])."""
-    mu = np.asarray(mu, dtype=np.float64)
+    tf32 = precision == "tf32"
+    mu = np.asarray(tf32_operand(mu) if tf32 else mu, dtype=np.float64)
     k = np.asarray(k, dtype=np.float64)
     v = np.asarray(v, dtype=np.float64)
     nb = k.shape[0] // leaf
@@ -259,6 +272,8 @@ def leaf_stats(mu, k, v, leaf, scale):
     z = w.sum(-1, keepdims=True)
     w /= z
     lz = (m + np.log(z))[..., 0]
+    if tf32:
+        w = tf32_operand(w.astype(F32)).astype(np.float64)
     g = np.einsum("tls,lsd->tld", w, k3) * float(scale)
     vb = np.einsum("tls,lsd->tld", w, v3)
     return g.astype(F32), lz.astype(F32), vb.astype(F32)
@@ -696,11 +711,13 @@ def pack_k(k):
 
 def flat_attention(q, k, v, *, tile=64, exact_leaves=256, leaf=64, scale=None, sink_leaves=0,
                    tail=None, return_stages=False, group=1, order="seq", perm=None, quant=None,
-                   stats_bf16=False, curvature="lin", store="int8", qk_scale_block=0):
+                   stats_bf16=False, curvature="lin", store="int8", qk_scale_block=0, precision="fp32"):
     """The whole production path for one head: q [N, D], k/v [M, D] (float32 arrays holding the
     caller's values; k and v are rounded to bfloat16 as the reference's bf16 path stores them).
     group: G tiles per centre (kern["group"]); order "kmeans" permutes the queries first (``perm``
-    overrides the permutation, e.g. with the device's, to check the stages after it).
+    overrides the permutation, e.g. with the device's, to check the stages after it); precision: the leaf
+    statistics' dots, "fp32" (the reference's "ieee"; its recorded fixtures, whose interpreter evaluates every
+    dot in float32) or "tf32" (PROD's setting on the GPU, see ``tf32_operand``).
     Returns (out float32 [N, D], lse float32 [N]) and, with return_stages, a dict of every stage."""
     q = np.asarray(q, dtype=F32)
     group = max(1, int(group))
@@ -736,7 +753,8 @@ def flat_attention(q, k, v, *, tile=64, exact_leaves=256, leaf=64, scale=None, s
     qt, mu, _ = tile_centres(q, tile)
     if group > 1:
         mu = group_centres(qt, group)
-    g, lz, vbf = leaf_stats(mu, k if k_stats is None else k_stats, v if v_stats is None else v_stats, leaf, scale)
+    g, lz, vbf = leaf_stats(mu, k if k_stats is None else k_stats, v if v_stats is None else v_stats, leaf, scale,
+                            precision)
     if store == "fp8":
         return _flat_fp8(qt, mu, g, lz, vbf, k, v, n, leaf, scale, exact_leaves, sink_leaves, tail, group, perm,
                          return_stages)
@@ -804,7 +822,7 @@ def prepare_head(q, k, v, *, tile=64, leaf=64):
     return dict(k=kb, v=vb, k8=k8, ks=ks, qt=qt, mu=mu, n=n, leaf=leaf)
 
 
-def attention_tiles(prep, tiles, *, exact_leaves=256, scale=None, sink_leaves=0, tail=None):
+def attention_tiles(prep, tiles, *, exact_leaves=256, scale=None, sink_leaves=0, tail=None, precision="fp32"):
     """The production path for a subset of query tiles of a prepared head (every tile is independent
     given the keys): returns (out float32 [len(tiles)*T, D], lse float32 [len(tiles)*T]) for the
     rows of those tiles, padding rows included."""
@@ -814,7 +832,7 @@ def attention_tiles(prep, tiles, *, exact_leaves=256, scale=None, sink_leaves=0,
     tiles = np.asarray(tiles, dtype=np.int64)
     qt, mu = prep["qt"][tiles], prep["mu"][tiles]
     nb = k.shape[0] // leaf
-    g, lz, vbf = leaf_stats(mu, k, v, leaf, scale)
+    g, lz, vbf = leaf_stats(mu, k, v, leaf, scale, precision)
     g8, sg, vb = state_int8(g, vbf)
     q8, sq, dq8, sdq = query_codes(qt, mu)
     sink = max(0, min(int(sink_leaves), nb))
