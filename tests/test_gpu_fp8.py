@@ -42,7 +42,7 @@ def _stages(dev, q, k, v, E, sink=0, tail=None, **kw):
         tv = torch.from_numpy(np.asarray(tail[1], np.float32)).to(dev)
     st = htrc_b200.run_stages(torch.from_numpy(q).to(dev), torch.from_numpy(k).to(torch.bfloat16).to(dev),
                               torch.from_numpy(v).to(torch.bfloat16).to(dev), tk, tv, exact_leaves=E, sink_leaves=sink,
-                              store=_lib.STORE_FP8, **kw)
+                              store=_lib.STORE_FP8, **{"precision": _lib.PREC_FP32, **kw})
     torch.cuda.synchronize()
     assert int(st["status"].item()) == 0
     return st
@@ -105,8 +105,9 @@ def test_fp8_operator_end_to_end(dev, golden_cases, case):
     q = torch.from_numpy(z["q"]).to(dev)
     k = torch.from_numpy(z["k"]).to(torch.bfloat16).to(dev)
     v = torch.from_numpy(z["v"]).to(torch.bfloat16).to(dev)
+    # the fixtures were recorded by Triton's interpreter, which evaluates the tf32 dots in float32
     cfg = {**htrc_b200.PROD, "leaf": 64, "store": "fp8", "exact_leaves": int(z["exact_leaves"]),
-           "sink_leaves": int(z["sink_leaves"])}
+           "sink_leaves": int(z["sink_leaves"]), "precision": "fp32"}
     out, lse = htrc_b200.flat_attention(q, k, v, tail=tail, return_lse=True, **cfg)
     torch.cuda.synchronize()
     assert np.abs(out.cpu().numpy() - z["out"]).max() < OUT_TOL
@@ -177,7 +178,7 @@ def test_fp8_modes_against_oracle(dev, over):
     perm = _np(st["perm"]) if st["perm"] is not None else None
     ro, rl, rst = O.flat_attention(q, k, v, exact_leaves=24, sink_leaves=1, tile=cfg["tile"],
                                    group=htrc_b200.flat.group_of(cfg.get("kern")), order=cfg.get("order", "seq"), perm=perm,
-                                   store="fp8", return_stages=True)
+                                   store="fp8", return_stages=True, precision="tf32")
     nb = st["nb"]
     assert (_np(st["excl"])[:, :nb] == rst["excl"]).mean() >= ROUTE_AGREE
     out, lse = htrc_b200.flat_attention(torch.from_numpy(q).cuda(), torch.from_numpy(k).to(torch.bfloat16).cuda(),
@@ -223,7 +224,7 @@ def test_fp8_with_input_fake_quant(dev):
                                         torch.from_numpy(v).to(torch.bfloat16).cuda(), return_lse=True, **cfg)
     torch.cuda.synchronize()
     ro, rl, rst = O.flat_attention(q, k, v, exact_leaves=16, quant=quant, stats_bf16=True, store="fp8",
-                                   return_stages=True)
+                                   return_stages=True, precision="tf32")
     o = out.cpu().numpy()
     assert np.abs(lse.cpu().numpy() - rl).mean() < LSE_TOL
     # rows of tiles whose routing the oracle reproduces are within the output tolerance

@@ -117,12 +117,13 @@ def test_end_to_end_against_reference_fixtures(dev, golden_cases, case):
         tail = (torch.from_numpy(z["tail_k"]).to(dev), torch.from_numpy(z["tail_v"]).to(dev))
     g = int(z["group"])
     order = "kmeans" if "perm" in z else "seq"
+    # the fixtures were recorded by Triton's interpreter, which evaluates the tf32 dots in float32
     cfg = {**htrc_b200.PROD, "leaf": 64, "exact_leaves": int(z["exact_leaves"]), "sink_leaves": int(z["sink_leaves"]),
-           "order": order, "kern": {**htrc_b200.PROD["kern"], "group": g}, "tile": _tile(z)}
+           "order": order, "kern": {**htrc_b200.PROD["kern"], "group": g}, "tile": _tile(z), "precision": "fp32"}
     out, lse = htrc_b200.flat_attention(q, k, v, tail=tail, return_lse=True, **cfg)
     st = htrc_b200.run_stages(q, k, v, tail[0] if tail else None, tail[1] if tail else None,
                               exact_leaves=cfg["exact_leaves"], sink_leaves=cfg["sink_leaves"], group=g,
-                              order=htrc_b200.flat.order_code(order), tile=_tile(z))
+                              order=htrc_b200.flat.order_code(order), tile=_tile(z), precision=0)
     torch.cuda.synchronize()
     assert torch.equal(out, st["out"]) and torch.equal(lse, st["lse"])
     assert int(st["status"].item()) == 0
@@ -264,7 +265,8 @@ def test_iso_curvature_on_device_state(dev, grid, seed, E, group, order, tile):
     from htrc_b200 import _lib
     q, k, v = _inputs(grid, seed)
     st = htrc_b200.run_stages(q.to(dev), k.to(dev), v.to(dev), exact_leaves=E, group=group,
-                              order=htrc_b200.flat.order_code(order), tile=tile, curvature=_lib.CURV_ISO)
+                              order=htrc_b200.flat.order_code(order), tile=tile, curvature=_lib.CURV_ISO,
+                              precision=_lib.PREC_FP32)
     torch.cuda.synchronize()
     assert int(st["status"].item()) == 0
     perm = _np(st["perm"]).astype(np.int64) if order == "kmeans" else None
@@ -310,19 +312,21 @@ def test_iso_curvature_end_to_end(dev):
     from htrc_b200 import runner
     q, k, v = _inputs((8, 32, 32), 131)
     qd, kd, vd = q.to(dev), k.to(dev), v.to(dev)
-    cfg = {**htrc_b200.PROD, "leaf": 64, "exact_leaves": 24, "backend": "cuda", "curvature": "iso"}
+    # the isotropic term is the reference's float32 torch-backend semantics: float32-accurate statistics
+    cfg = {**htrc_b200.PROD, "leaf": 64, "exact_leaves": 24, "backend": "cuda", "curvature": "iso", "precision": "fp32"}
     out, lse = htrc_b200.flat_attention(qd, kd, vd, return_lse=True, **cfg)
     with pytest.raises(ValueError, match="curvature='lin'"):
         htrc_b200.flat_attention(qd, kd, vd, **{**cfg, "backend": "triton"})
     r = runner.FlatRunner(q.shape[0], k.shape[0], mode="fast", backend="cuda", curvature="iso", lse=True,
-                          exact_leaves=24)
+                          exact_leaves=24, precision="fp32")
     assert r.graph is not None, r.graph_error
     o2, l2 = r.head(qd, kd, vd)
     torch.cuda.synchronize()
     assert torch.equal(o2, out) and torch.equal(l2, lse)
     ro, rl, rst = O.flat_attention(q.float().numpy(), k.float().numpy(), v.float().numpy(), exact_leaves=24,
                                    curvature="iso", return_stages=True)
-    st = htrc_b200.run_stages(qd, kd, vd, exact_leaves=24, curvature=htrc_b200.flat.curvature_code("iso"))
+    st = htrc_b200.run_stages(qd, kd, vd, exact_leaves=24, curvature=htrc_b200.flat.curvature_code("iso"),
+                              precision=0)
     torch.cuda.synchronize()
     nb = st["nb"]
     ex = _np(st["excl"])[:, :nb]

@@ -74,11 +74,13 @@ def test_half_away_pack_bit_exact(dev):
 
 
 @pytest.mark.parametrize("n", [1024, 1000, 64, 37])
-def test_tile_prep_bit_exact(dev, n):
+@pytest.mark.parametrize("precision", ["fp32", "tf32"])
+def test_tile_prep_bit_exact(dev, n, precision):
     import htrc_b200
+    from htrc_b200 import _lib
     q, k, v = _inputs((2, 16, 32), 21)
     q = q[:n]
-    st = htrc_b200.run_stages(q.to(dev), k.to(dev), v.to(dev), exact_leaves=2)
+    st = htrc_b200.run_stages(q.to(dev), k.to(dev), v.to(dev), exact_leaves=2, precision=_lib.PRECISIONS[precision])
     torch.cuda.synchronize()
     qt, mu, _ = O.tile_centres(q.float().numpy(), 64)
     assert np.array_equal(_np(st["mu"]).view(np.uint32), mu.view(np.uint32))
@@ -90,20 +92,27 @@ def test_tile_prep_bit_exact(dev, n):
     assert np.array_equal(_np(st["sdq"]).reshape(nt, 64).view(np.uint32), sdq.view(np.uint32))
     hi = _np(st["mu_hi"])
     lo = _np(st["mu_lo"])
+    if precision == "tf32":                  # hi + lo is the centre's tf32 operand value, exactly
+        assert np.array_equal((hi.astype(np.float64) + lo).astype(np.float32), O.tf32_operand(mu))
+        return
     assert np.array_equal(hi, O.bf16_round(mu))
     assert np.abs(hi.astype(np.float64) + lo - mu).max() <= 2.0 ** -16 * np.abs(mu).max()
 
 
 @pytest.mark.parametrize("grid,seed", [((2, 16, 32), 31), ((4, 16, 32), 32)])
-def test_leaf_stats(dev, grid, seed):
+@pytest.mark.parametrize("precision", ["fp32", "tf32"])
+def test_leaf_stats(dev, grid, seed, precision):
+    """lz, sg, g8 and vbar against the oracle at the same precision setting (tf32: the centre and the softmax
+    weights enter the dots as tf32 operand values)."""
     import htrc_b200
+    from htrc_b200 import _lib
     q, k, v = _inputs(grid, seed)
-    st = htrc_b200.run_stages(q.to(dev), k.to(dev), v.to(dev), exact_leaves=2)
+    st = htrc_b200.run_stages(q.to(dev), k.to(dev), v.to(dev), exact_leaves=2, precision=_lib.PRECISIONS[precision])
     torch.cuda.synchronize()
     nb = st["nb"]
     mu = _np(st["mu"])
     g, lz, vb = O.leaf_stats(mu, O.bf16_round(k.float().numpy()), O.bf16_round(v.float().numpy()), 64,
-                             1 / math.sqrt(128))
+                             1 / math.sqrt(128), precision)
     g8, sg = O.pack_slope(g)
     lz_d = _np(st["lz"])[:, :nb]
     sg_d = _np(st["sg"])[:, :nb]
@@ -234,10 +243,12 @@ def test_end_to_end_against_reference_fixtures(dev, golden_cases, case):
     tail = None
     if "tail_k" in z:
         tail = (torch.from_numpy(z["tail_k"]).to(dev), torch.from_numpy(z["tail_v"]).to(dev))
-    cfg = {**htrc_b200.PROD, "leaf": 64, "exact_leaves": int(z["exact_leaves"]), "sink_leaves": int(z["sink_leaves"])}
+    # the fixtures were recorded by Triton's interpreter, which evaluates the tf32 dots in float32
+    cfg = {**htrc_b200.PROD, "leaf": 64, "exact_leaves": int(z["exact_leaves"]), "sink_leaves": int(z["sink_leaves"]),
+           "precision": "fp32"}
     out, lse = htrc_b200.flat_attention(q, k, v, tail=tail, return_lse=True, **cfg)
     st = htrc_b200.run_stages(q, k, v, tail[0] if tail else None, tail[1] if tail else None,
-                              exact_leaves=cfg["exact_leaves"], sink_leaves=cfg["sink_leaves"])
+                              exact_leaves=cfg["exact_leaves"], sink_leaves=cfg["sink_leaves"], precision=0)
     torch.cuda.synchronize()
     assert np.array_equal(_np(st["k8"]), z["k8"])
     assert np.array_equal(_np(st["ks"]).view(np.uint32), z["ks"].view(np.uint32))
@@ -263,7 +274,7 @@ def test_end_to_end_against_oracle(dev, grid, seed, E, sink, ntail, drop):
     assert torch.equal(out, st["out"])
     tnp = (tail[0].numpy(), tail[1].numpy()) if tail else None
     ro, rl, rst = O.flat_attention(q.float().numpy(), k.float().numpy(), v.float().numpy(), leaf=64,
-                                   exact_leaves=E, sink_leaves=sink, tail=tnp, return_stages=True)
+                                   exact_leaves=E, sink_leaves=sink, tail=tnp, return_stages=True, precision="tf32")
     same_state = _oracle_on_device_state(q, v, st, tnp)
     _check_against(out, lse, st, ro, rl, rst["excl"], rst["sel"], q.shape[0], st["kx"], same_state, strict=False)
 
