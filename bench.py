@@ -41,6 +41,12 @@ WORKLOADS = {
                  name="cfg3: 129,024-token 32x48x84 latent layer, 24 heads, d128, leaf 64, tile 64, fast (E=256), INT8"),
     "cfg2": dict(grid=(16, 32, 32), heads=24, exact_leaves=256,
                  name="cfg2: 16,384-token 16x32x32 latent layer, 24 heads, d128, leaf 64, tile 64, fast (E=256), INT8"),
+    # the denoise-step workload: a step is one transformer block = CFG batch 2 x 24 heads (48 (batch, head)
+    # pairs), fresh seeded inputs per block (two distinct blocks resident, alternated); value = block time / 2
+    "cfg4": dict(grid=(32, 48, 84), heads=24, batch=2, blocks=2, exact_leaves=256,
+                 name="cfg4: per step one denoise-step block: CFG batch 2 x 24 heads of 129,024 tokens (48 (batch, "
+                      "head) pairs, fresh seeded Q/K/V per block, 2 distinct blocks resident and alternated), d128, "
+                      "leaf 64, tile 64, fast (E=256), INT8; value = ms per 24-head layer = block time / 2"),
     # profiling-sized case: one head, half of cfg3's frames (leaf state ~400 MB > L2, < 1 GB on the device)
     "prof": dict(grid=(16, 48, 84), heads=1, exact_leaves=256,
                  name="prof: one 64,512-token 16x48x84 head, d128, leaf 64, tile 64, fast (E=256), INT8"),
@@ -54,7 +60,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="cfg3", choices=list(WORKLOADS))
+    ap.add_argument("--workload", default="auto", choices=["auto"] + list(WORKLOADS),
+                    help="auto (default): cfg3 (one full-resolution layer) on one GPU, cfg4 (one CFG-batch block "
+                         "of the denoise step, pairs sharded over the ranks) under torchrun")
     ap.add_argument("--cpu-tiles", type=int, default=4, help="tiles of the CPU-baseline sample")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
@@ -474,23 +482,29 @@ def run_ours(a, wl, rank, world, local_rank):
     if world > 1:
         import torch.distributed as dist
     H = wl["heads"]
+    batch, nblocks = wl.get("batch", 1), wl.get("blocks", 1)
+    layers_per_step = batch                     # a step is `batch` layers of H heads
     try:
-        my_heads = list(shard.heads_of_rank(H, rank, world))
+        my_pairs = list(shard.heads_of_rank(H * batch, rank, world))   # (batch, head) pair p = batch * H + head
     except ValueError as e:
         raise SystemExit(str(e))
     E = wl["exact_leaves"]
+    # the jobs of step s: block s % nblocks, this rank's pairs, keyed (block, batch, head); slot i = i-th pair
+    step_jobs = [[(b, p // H, p % H) for p in my_pairs] for b in range(nblocks)]
+    all_jobs = [j for js in step_jobs for j in js]
+    nslots = len(my_pairs)
 
     # ---- inputs: pinned host copies (for e2e) and device-resident copies (for the device timing)
     host = {}
-    for h in my_heads:
-        q, k, v = synth.head_inputs(wl["grid"], 128, head=h)
-        host[h] = tuple(t.pin_memory() for t in (q, k, v))
-    n, m = host[my_heads[0]][0].shape[0], host[my_heads[0]][1].shape[0]
+    for j in all_jobs:
+        q, k, v = synth.head_inputs(wl["grid"], 128, block=j[0], batch=j[1], head=j[2])
+        host[j] = tuple(t.pin_memory() for t in (q, k, v))
+    n, m = host[all_jobs[0]][0].shape[0], host[all_jobs[0]][1].shape[0]
     nt, nb = -(-n // 64), m // 64
     kx = min(E, nb)
-    dq = {h: tuple(t.to(dev, non_blocking=True) for t in host[h]) for h in my_heads}
-    out = {h: torch.empty((n, 128), dtype=torch.float32, device=dev) for h in my_heads}
-    lse = {h: torch.empty((n,), dtype=torch.float32, device=dev) for h in my_heads}
+    dq = {j: tuple(t.to(dev, non_blocking=True) for t in host[j]) for j in all_jobs}
+    out = [torch.empty((n, 128), dtype=torch.float32, device=dev) for _ in range(nslots)]
+    lse = [torch.empty((n,), dtype=torch.float32, device=dev) for _ in range(nslots)]
     from htrc_b200 import _lib as _L
     store = _L.STORES[a.store]
     fp8 = store == _L.STORE_FP8
@@ -506,29 +520,29 @@ def run_ours(a, wl, rank, world, local_rank):
     gathered = None
     obf = None
     if world > 1:
-        obf = {h: torch.empty((n, 128), dtype=torch.bfloat16, device=dev) for h in my_heads}
-        gathered = [torch.empty((world, n, 128), dtype=torch.bfloat16, device=dev) for _ in my_heads]
-    ev_done = [torch.cuda.Event() for _ in my_heads]
+        obf = [torch.empty((n, 128), dtype=torch.bfloat16, device=dev) for _ in range(nslots)]
+        gathered = [torch.empty((world, n, 128), dtype=torch.bfloat16, device=dev) for _ in range(nslots)]
+    ev_done = [torch.cuda.Event() for _ in range(nslots)]
     nev = 6
 
-    def layer(stage_events=None, gather=True, nstreams=None):
+    def layer(step, stage_events=None, gather=True, nstreams=None):
         streams = head_streams[:nstreams] if nstreams else head_streams
         for s_ in streams[1:]:
             s_.wait_stream(comp)
-        for i, h in enumerate(my_heads):
+        for i, h in enumerate(step_jobs[step % nblocks]):
             evs = stage_events[i] if stage_events is not None else None
             hs = streams[i % len(streams)]
             with torch.cuda.stream(hs):
-                F.forward_into(*dq[h], None, None, exact_leaves=E, out=out[h], lse=lse[h],
+                F.forward_into(*dq[h], None, None, exact_leaves=E, out=out[i], lse=lse[i],
                                workspace=head_ws[i % len(head_ws)], stage_events=evs, stream=hs, store=store,
                                precision=prec)
                 if world > 1 and gather:
-                    obf[h].copy_(out[h])
+                    obf[i].copy_(out[i])
                     ev_done[i].record(hs)
             if world > 1 and gather:
                 side.wait_event(ev_done[i])
                 with torch.cuda.stream(side):
-                    shard.gather_slot(obf[h], out=gathered[i])
+                    shard.gather_slot(obf[i], out=gathered[i])
         for s_ in streams[1:]:
             comp.wait_stream(s_)
         if world > 1 and gather:
@@ -547,14 +561,15 @@ def run_ours(a, wl, rank, world, local_rank):
         return float(t.item())
 
     torch.cuda.synchronize(dev)
-    for _ in range(a.warmup):
-        layer()
+    for s in range(a.warmup):
+        layer(s)
     barrier()
     for w in head_ws:
         F.device_status(w)
 
     # ---- device-resident timed region, with per-stage events of every head
-    stage_evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(nev)] for _ in my_heads] for _ in range(a.steps)]
+    stage_evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(nev)] for _ in range(nslots)]
+                 for _ in range(a.steps)]
     clocks = ClockSampler(dev.index if world == 1 else int(os.environ.get("LOCAL_RANK", 0)))
     clocks.start()
     barrier()
@@ -564,11 +579,12 @@ def run_ours(a, wl, rank, world, local_rank):
     for s in range(a.steps):
         # with one head stream the stage events are taken here; with two they would include the overlap
         # of the two streams' kernels, so they come from a separate pass below
-        layer(stage_evs[s] if a.streams == 1 else None)
+        layer(s, stage_evs[s] if a.streams == 1 else None)
     t1.record(comp)
     barrier()
     clk = clocks.stop()
-    ms = max_over_ranks(t0.elapsed_time(t1) / a.steps)
+    ms_step = max_over_ranks(t0.elapsed_time(t1) / a.steps)
+    ms = ms_step / layers_per_step
     gather_info = None
     if world > 1:
         # the same layer without the output gathers: the gathers' exposed (not overlapped) time
@@ -576,20 +592,21 @@ def run_ours(a, wl, rank, world, local_rank):
         g0 = torch.cuda.Event(enable_timing=True)
         g1 = torch.cuda.Event(enable_timing=True)
         g0.record(comp)
-        for _ in range(a.steps):
-            layer(gather=False)
+        for s in range(a.steps):
+            layer(s, gather=False)
         g1.record(comp)
         barrier()
         ms_nog = max_over_ranks(g0.elapsed_time(g1) / a.steps)
-        gather_info = {"compute_only_ms": ms_nog, "exposed_ms": ms - ms_nog,
-                       "bytes_per_rank_per_step": len(my_heads) * world * n * 128 * 2,
+        gather_info = {"compute_only_ms_per_step": ms_nog, "exposed_ms_per_step": ms_step - ms_nog,
+                       "exposed_ms_per_layer": (ms_step - ms_nog) / layers_per_step,
+                       "bytes_per_rank_per_step": nslots * world * n * 128 * 2,
                        "how": "bf16 outputs all-gathered (NCCL) per local head on a side stream, overlapped with the "
                               "next head; exposed = layer time - the same layer without the gathers"}
     stage_timing = "CUDA events around each stage of every head in the timed region (heads on one stream)"
     if a.streams > 1:
         barrier()
         for s in range(a.steps):
-            layer(stage_evs[s], gather=False, nstreams=1)
+            layer(s, stage_evs[s], gather=False, nstreams=1)
         barrier()
         stage_timing = ("CUDA events around each stage of every head in a separate pass of the same layers with the "
                         "heads on one stream (the timed region's two streams overlap consecutive heads)")
@@ -597,7 +614,7 @@ def run_ours(a, wl, rank, world, local_rank):
         F.device_status(w)
     stage_names = ["prep", "stats", "rowmax", "route", "tile"]
     stage_ms = {nm: statistics.mean(stage_evs[s][i][j].elapsed_time(stage_evs[s][i][j + 1])
-                                    for s in range(a.steps) for i in range(len(my_heads)))
+                                    for s in range(a.steps) for i in range(nslots))
                 for j, nm in enumerate(stage_names)}
 
     # ---- parity at full size on a tile sample of head 0 (rank 0): mean |dlogZ| vs the oracle
@@ -605,12 +622,14 @@ def run_ours(a, wl, rank, world, local_rank):
     cpu = None
     ref_gpu = None
     oracle_rows = None
-    h0 = my_heads[0]
-    mask0 = None
+    h0 = all_jobs[0]
+    mask0 = out0 = lse0 = None
     if rank == 0:
-        # head 0 once more with its routing mask exported (the kernels are deterministic: same out / lse)
+        # the first job once more with its routing mask exported
         mask0 = torch.zeros((nt, F.leaf_pitch(nb)), dtype=torch.uint8, device=dev)
-        F.forward_into(*dq[h0], None, None, exact_leaves=E, out=out[h0], lse=lse[h0], workspace=ws, store=store,
+        out0 = torch.empty((n, 128), dtype=torch.float32, device=dev)
+        lse0 = torch.empty((n,), dtype=torch.float32, device=dev)
+        F.forward_into(*dq[h0], None, None, exact_leaves=E, out=out0, lse=lse0, workspace=ws, store=store,
                        route_mask=mask0, precision=prec)
         torch.cuda.synchronize(dev)
         F.device_status(ws)
@@ -623,8 +642,8 @@ def run_ours(a, wl, rank, world, local_rank):
         rows = (tiles[:, None] * 64 + np.arange(64)[None, :]).reshape(-1)
         valid = rows < n
         oracle_rows = (rows[valid], ro[valid], rl[valid])
-        lse_d = lse[h0].cpu().numpy()[rows[valid]]
-        out_d = out[h0].cpu().numpy()[rows[valid]]
+        lse_d = lse0.cpu().numpy()[rows[valid]]
+        out_d = out0.cpu().numpy()[rows[valid]]
         excl_o = oracle_routing(prep, tiles, E, threads, a.precision)
         excl_d = mask0[torch.as_tensor(tiles, device=dev)][:, :nb].cpu().numpy()
         parity = {"logz_mae": float(np.abs(lse_d - rl[valid]).mean()),
@@ -639,7 +658,7 @@ def run_ours(a, wl, rank, world, local_rank):
         kk, vv = dq[h0][1].float(), dq[h0][2].float()
         s_ = (qs @ kk.T) / math.sqrt(128)
         ex = torch.softmax(s_, -1) @ vv
-        od = out[h0][torch.as_tensor(rows[valid], device=dev)]
+        od = out0[torch.as_tensor(rows[valid], device=dev)]
         parity["rel_l2_vs_exact"] = float((od - ex).norm() / ex.norm())
         del s_
         if world == 1:
@@ -651,7 +670,7 @@ def run_ours(a, wl, rank, world, local_rank):
             if not a.no_ref_cpu:
                 cpu["reference_torch"] = reference_cpu_legs(threads)
     if rank == 0 and world == 1 and not a.no_ref_gpu and not fp8:
-        ref_gpu = reference_gpu_leg(wl, dev, my_heads, dq, {"out": out[h0], "lse": lse[h0], "mask": mask0},
+        ref_gpu = reference_gpu_leg(wl, dev, step_jobs[0][:H], dq, {"out": out0, "lse": lse0, "mask": mask0},
                                     max(1, min(a.steps, a.ref_steps)), oracle_rows)
         if "ms_per_layer" in ref_gpu:
             ref_gpu["ours_over_ref"] = ms / ref_gpu["ms_per_layer"]
@@ -659,21 +678,21 @@ def run_ours(a, wl, rank, world, local_rank):
     # ---- end to end through the public API with pinned host buffers
     e2e = None
     if not a.no_e2e:
-        qb = [torch.empty_like(dq[my_heads[0]][j]) for j in range(3) for _ in range(2)]
+        qb = [torch.empty_like(dq[h0][j]) for j in range(3) for _ in range(2)]
         stage_in = [(qb[0], qb[2], qb[4]), (qb[1], qb[3], qb[5])]
         stage_out = [(torch.empty((n, 128), dtype=torch.float32, device=dev),
                       torch.empty((n,), dtype=torch.float32, device=dev)) for _ in range(2)]
-        host_out = {h: (torch.empty((n, 128), dtype=torch.float32).pin_memory(),
-                        torch.empty((n,), dtype=torch.float32).pin_memory()) for h in my_heads}
+        host_out = [(torch.empty((n, 128), dtype=torch.float32).pin_memory(),
+                        torch.empty((n,), dtype=torch.float32).pin_memory()) for _ in range(nslots)]
         s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
         in_done = [torch.cuda.Event() for _ in range(2)]
         comp_done = [torch.cuda.Event() for _ in range(2)]
         out_done = [torch.cuda.Event() for _ in range(2)]
 
-        def e2e_layer():
+        def e2e_layer(step):
             for s_ in head_streams[1:]:
                 s_.wait_stream(comp)
-            for i, h in enumerate(my_heads):
+            for i, h in enumerate(step_jobs[step % nblocks]):
                 b = i % 2
                 hs = head_streams[i % len(head_streams)]
                 # staging buffer b is free once the head that last used it (two heads back, in this layer or
@@ -694,8 +713,8 @@ def run_ours(a, wl, rank, world, local_rank):
                 comp_done[b].record(hs)
                 s_out.wait_event(comp_done[b])
                 with torch.cuda.stream(s_out):
-                    host_out[h][0].copy_(stage_out[b][0], non_blocking=True)
-                    host_out[h][1].copy_(stage_out[b][1], non_blocking=True)
+                    host_out[i][0].copy_(stage_out[b][0], non_blocking=True)
+                    host_out[i][1].copy_(stage_out[b][1], non_blocking=True)
                     out_done[b].record(s_out)
             for s_ in head_streams[1:]:
                 comp.wait_stream(s_)
@@ -706,22 +725,24 @@ def run_ours(a, wl, rank, world, local_rank):
             comp.wait_stream(s_in)
             comp.wait_stream(s_out)
 
-        for _ in range(a.warmup):
-            e2e_layer()
+        for s in range(a.warmup):
+            e2e_layer(s)
         join_copies()
         barrier()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(comp)
-        for _ in range(a.steps):
-            e2e_layer()
+        for s in range(a.steps):
+            e2e_layer(s)
         join_copies()
         e1.record(comp)
         barrier()
-        e2e_ms = max_over_ranks(e0.elapsed_time(e1) / a.steps)
-        h2d = sum(sum(t.numel() * t.element_size() for t in host[h]) for h in my_heads) * world
-        d2h = sum(sum(t.numel() * t.element_size() for t in host_out[h]) for h in my_heads) * world
-        same = all(bool(torch.equal(host_out[h][0].to(dev), out[h])) for h in (my_heads[0], my_heads[-1]))
+        e2e_ms = max_over_ranks(e0.elapsed_time(e1) / a.steps) / layers_per_step
+        h2d = sum(sum(t.numel() * t.element_size() for t in host[h]) for h in step_jobs[0]) * world
+        d2h = sum(sum(t.numel() * t.element_size() for t in o) for o in host_out) * world
+        # the last timed e2e step and the last device pass computed the same block: identical outputs
+        torch.cuda.synchronize(dev)
+        same = all(bool(torch.equal(host_out[i][0].to(dev), out[i])) for i in (0, nslots - 1))
         e2e = {"value": e2e_ms, "unit": "ms/layer", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "api": "htrc_b200.forward_into, pinned host q/k/v in and out/lse back, copies overlapped on "
                       f"2 copy streams (also across layers), heads on {a.streams} compute stream(s)",
@@ -732,7 +753,6 @@ def run_ours(a, wl, rank, world, local_rank):
     modes = None
     if rank == 0 and world == 1 and not a.no_modes:
         from htrc_b200 import runner as R
-        h0 = my_heads[0]
         modes = {}
         for mode in list(R.MODES) + ["fast+iso", "fast+fp8"]:
             extra = {"fast+iso": dict(backend="cuda", curvature="iso"), "fast+fp8": dict(store="fp8")}.get(mode, {})
@@ -820,32 +840,36 @@ def run_ours(a, wl, rank, world, local_rank):
 
     if rank == 0:
         line = {"metric": METRIC, "value": ms, "unit": "ms/layer", "n_gpus": world, "steps": a.steps,
-                "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": False, "scaling": "strong",
+                "warmup": a.warmup, "ms_per_step": ms_step, "higher_is_better": False, "scaling": "strong",
                 "vs_baseline": None,
                 "dtype": ("fp8 (e4m3) state; fp16 far / bf16 near QK and PV, f32 softmax" if fp8 else
                           "int8 QK + bf16 PV, f32 softmax"),
                 "data": "synthetic: seeded smooth-field Q/K (4x8x8 grid trilinear + 0.5 noise, RMS 3), N(0,1) V, bf16",
                 "config": {"workload": wl["name"].replace("INT8", "fp8 (e4m3) state") if fp8 else wl["name"],
-                           "tokens": n, "heads": H,
+                           "tokens": n, "heads": H, "cfg_batch": batch, "blocks_resident": nblocks,
                            "dim": 128, "leaf": 64, "tile": 64, "store": a.store,
-                           "exact_leaves": E, "precision": a.precision, "heads_per_gpu": len(my_heads),
+                           "exact_leaves": E, "precision": a.precision, "pairs_per_gpu": nslots,
+                           "layers_per_step": layers_per_step,
                            "head_streams": a.streams,
                            "l2": "inputs larger than L2: 2.4 GB of distinct q/k/v per layer, "
                                  + ("1.0" if fp8 else "1.6") + " GB leaf state per head",
-                           "parallelism": f"heads/{world}" + (" + bf16 output all_gather (NCCL)" if world > 1 else "")},
+                           "parallelism": f"(batch, head) pairs/{world}" +
+                                          (" + bf16 output all_gather (NCCL)" if world > 1 else "")},
                 "stage_ms_per_head": stage_ms, "stage_timing": stage_timing, "stage_roofline": stage_roof,
                 "gather": gather_info, "modes": modes,
                 **parity,
                 "roofline": roof, "cpu_baseline": cpu, "reference_gpu": ref_gpu,
                 "e2e": e2e,
-                "gpu_launches": a.steps * len(my_heads) * LAUNCHES_PER_HEAD, "clocks": clk}
+                "gpu_launches": a.steps * nslots * LAUNCHES_PER_HEAD, "clocks": clk}
         print(json.dumps(line), flush=True)
 
 
 def main():
     a = parse()
-    wl = WORKLOADS[a.workload]
     world = int(os.environ.get("WORLD_SIZE", "1"))
+    if a.workload == "auto":
+        a.workload = "cfg3" if world == 1 else "cfg4"
+    wl = WORKLOADS[a.workload]
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if a.impl == "reference":
