@@ -78,6 +78,10 @@ def parse():
     ap.add_argument("--precision", default="tf32", choices=["tf32", "fp32"],
                     help="leaf-statistics dots: tf32 operands (PROD's setting, the reference's production path; the "
                          "default) or float32-accurate")
+    ap.add_argument("--division", default="triton", choices=["triton", "ieee"],
+                    help="division forming the query/offset/slope codes: the reference's GPU division (div.full.f32, "
+                         "the default: PROD as the reference computes it on the GPU) or IEEE (its formula as "
+                         "written); the oracle comparison always uses an IEEE run of head 0")
     ap.add_argument("--streams", type=int, default=2, choices=[1, 2],
                     help="heads of a layer alternate over this many streams, each with its own workspace (2, the "
                          "default: one head's small kernels and the tile kernel's last partial wave overlap the "
@@ -328,7 +332,7 @@ def reference_gpu_leg(wl, dev, heads, dq, ours, steps, oracle_rows=None):
              "out_maxabs_agreeing_tiles": d_out[rows_agree].max().item() if bool(rows_agree.any()) else None,
              "rows_over_2e-2": int((d_out > 2e-2).sum().item()),
              "lse_mae": d_lse.mean().item(), "lse_maxabs": d_lse.max().item(),
-             "precision": cfg["precision"],
+             "precision": cfg["precision"], "division": ours["division"],
              "how": "this library's route_mask / out / lse of head 0 (the same precision setting) against the "
                     "reference's ws['excl'], output and logsumexp of its split partials ws['pm'], ws['pl'] (one "
                     "chunk), same inputs, same B200"}
@@ -339,10 +343,11 @@ def reference_gpu_leg(wl, dev, heads, dq, ours, steps, oracle_rows=None):
             p["vs_oracle_sample"] = {
                 "rows": int(len(rows)),
                 "ref_out_maxabs": (out_r[ri] - oo).abs().max().item(), "ref_lse_mae": (lse_r[ri] - ol).abs().mean().item(),
-                "ours_out_maxabs": (ours["out"][ri] - oo).abs().max().item(),
-                "ours_lse_mae": (ours["lse"][ri] - ol).abs().mean().item(),
+                "ours_out_maxabs": (ours["out_ieee"][ri] - oo).abs().max().item(),
+                "ours_lse_mae": (ours["lse_ieee"][ri] - ol).abs().mean().item(),
                 "how": "both GPU operators against the CPU oracle (the float64 restatement at the same precision "
-                       "setting) on its sampled tiles"}
+                       "setting, IEEE division) on its sampled tiles; this library's row from its IEEE-division "
+                       "run"}
         g = torch.Generator().manual_seed(5)
         rows = torch.randperm(n, generator=g)[:256].to(dev)
         qs = dq[heads[0]][0][rows].float()
@@ -508,7 +513,8 @@ def run_ours(a, wl, rank, world, local_rank):
     from htrc_b200 import _lib as _L
     store = _L.STORES[a.store]
     fp8 = store == _L.STORE_FP8
-    prec = F.precision_code(a.precision)
+    prec = F.precision_code(a.precision, a.division)
+    prec_ieee = F.precision_code(a.precision, "ieee")
     wsb = F.workspace_bytes(n, m, E, 0, 0, 0, store=store)
     ws = F.new_workspace(wsb, dev)
     comp = torch.cuda.current_stream(dev)
@@ -631,6 +637,10 @@ def run_ours(a, wl, rank, world, local_rank):
         lse0 = torch.empty((n,), dtype=torch.float32, device=dev)
         F.forward_into(*dq[h0], None, None, exact_leaves=E, out=out0, lse=lse0, workspace=ws, store=store,
                        route_mask=mask0, precision=prec)
+        # and with IEEE code division, the oracle's arithmetic (the same run when --division ieee)
+        mask0i, out0i, lse0i = torch.zeros_like(mask0), torch.empty_like(out0), torch.empty_like(lse0)
+        F.forward_into(*dq[h0], None, None, exact_leaves=E, out=out0i, lse=lse0i, workspace=ws, store=store,
+                       route_mask=mask0i, precision=prec_ieee)
         torch.cuda.synchronize(dev)
         F.device_status(ws)
     if rank == 0 and not a.no_cpu and not fp8:
@@ -642,23 +652,23 @@ def run_ours(a, wl, rank, world, local_rank):
         rows = (tiles[:, None] * 64 + np.arange(64)[None, :]).reshape(-1)
         valid = rows < n
         oracle_rows = (rows[valid], ro[valid], rl[valid])
-        lse_d = lse0.cpu().numpy()[rows[valid]]
-        out_d = out0.cpu().numpy()[rows[valid]]
+        lse_d = lse0i.cpu().numpy()[rows[valid]]
+        out_d = out0i.cpu().numpy()[rows[valid]]
         excl_o = oracle_routing(prep, tiles, E, threads, a.precision)
-        excl_d = mask0[torch.as_tensor(tiles, device=dev)][:, :nb].cpu().numpy()
+        excl_d = mask0i[torch.as_tensor(tiles, device=dev)][:, :nb].cpu().numpy()
         parity = {"logz_mae": float(np.abs(lse_d - rl[valid]).mean()),
                   "out_maxabs": float(np.abs(out_d - ro[valid]).max()),
                   "routing_agreement_sample": float((excl_o == (excl_d != 0)).mean()),
                   "sample": f"{len(tiles)} random tiles of head {h0} vs oracle/flat_oracle.py at precision "
-                            f"{a.precision} (the oracle computes its own float64 leaf statistics, selection and "
-                            f"routing for them)"}
+                            f"{a.precision}, IEEE code division (the oracle computes its own float64 leaf "
+                            f"statistics, selection and routing for them)"}
         parity["codes_full_size"] = full_size_codes(F, dq[h0], prep, E, threads)
         # error of the operator against exact softmax attention on the same rows
         qs = dq[h0][0][torch.as_tensor(rows[valid], device=dev)].float()
         kk, vv = dq[h0][1].float(), dq[h0][2].float()
         s_ = (qs @ kk.T) / math.sqrt(128)
         ex = torch.softmax(s_, -1) @ vv
-        od = out0[torch.as_tensor(rows[valid], device=dev)]
+        od = out0i[torch.as_tensor(rows[valid], device=dev)]
         parity["rel_l2_vs_exact"] = float((od - ex).norm() / ex.norm())
         del s_
         if world == 1:
@@ -670,7 +680,9 @@ def run_ours(a, wl, rank, world, local_rank):
             if not a.no_ref_cpu:
                 cpu["reference_torch"] = reference_cpu_legs(threads)
     if rank == 0 and world == 1 and not a.no_ref_gpu and not fp8:
-        ref_gpu = reference_gpu_leg(wl, dev, step_jobs[0][:H], dq, {"out": out0, "lse": lse0, "mask": mask0},
+        ref_gpu = reference_gpu_leg(wl, dev, step_jobs[0][:H], dq, {"out": out0, "lse": lse0, "mask": mask0,
+                                                                    "out_ieee": out0i, "lse_ieee": lse0i,
+                                                                    "division": a.division},
                                     max(1, min(a.steps, a.ref_steps)), oracle_rows)
         if "ms_per_layer" in ref_gpu:
             ref_gpu["ours_over_ref"] = ms / ref_gpu["ms_per_layer"]
@@ -848,7 +860,7 @@ def run_ours(a, wl, rank, world, local_rank):
                 "config": {"workload": wl["name"].replace("INT8", "fp8 (e4m3) state") if fp8 else wl["name"],
                            "tokens": n, "heads": H, "cfg_batch": batch, "blocks_resident": nblocks,
                            "dim": 128, "leaf": 64, "tile": 64, "store": a.store,
-                           "exact_leaves": E, "precision": a.precision, "pairs_per_gpu": nslots,
+                           "exact_leaves": E, "precision": a.precision, "division": a.division, "pairs_per_gpu": nslots,
                            "layers_per_step": layers_per_step,
                            "head_streams": a.streams,
                            "l2": "inputs larger than L2: 2.4 GB of distinct q/k/v per layer, "

@@ -16,8 +16,9 @@ ORDER_SEQ, ORDER_KMEANS = 0, 1
 CURV_LIN, CURV_ISO = 0, 1
 STORE_INT8, STORE_FP8 = 0, 1
 STORES = {"int8": STORE_INT8, "fp8": STORE_FP8}
-PREC_FP32, PREC_TF32 = 0, 1
+PREC_FP32, PREC_TF32, PREC_TRITON_DIV = 0, 1, 2      # flags, OR-ed
 PRECISIONS = {"fp32": PREC_FP32, "tf32": PREC_TF32}
+DIVISIONS = {"ieee": 0, "triton": PREC_TRITON_DIV}
 FQ_FORMATS = {"int8": 1, "int4": 2, "fp8": 3, "fp4": 4}
 ROUND_HALF_EVEN, ROUND_HALF_AWAY = 0, 1
 STATUS_BITS = {1: "bounded wait gave up", 2: "routed leaf index out of range", 4: "non-finite log-partition"}

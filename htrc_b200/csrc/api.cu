@@ -160,7 +160,7 @@ int validate(const HtrcFlatArgs* a, bool need_ptrs) {
   if (a->store == HTRC_STORE_FP8 && a->curvature != HTRC_CURV_LIN) return HTRC_ERR_UNSUPPORTED;
   if (a->qk_scale_block != 0 && a->qk_scale_block != 64) return HTRC_ERR_ARG;
   if (a->qk_scale_block != 0 && a->store != HTRC_STORE_INT8) return HTRC_ERR_UNSUPPORTED;
-  if (a->precision != HTRC_PREC_FP32 && a->precision != HTRC_PREC_TF32) return HTRC_ERR_ARG;
+  if ((a->precision & ~(HTRC_PREC_TF32 | HTRC_PREC_TRITON_DIV)) != 0) return HTRC_ERR_ARG;
   if (a->n_queries > (int64_t(1) << 31) - 1) return HTRC_ERR_UNSUPPORTED;
   const int64_t nb = a->n_keys / a->leaf;
   if (nb > kMaxLeaves) return HTRC_ERR_UNSUPPORTED;
@@ -379,7 +379,8 @@ int htrc_flat_forward(const HtrcFlatArgs* a, htrc_stream_t stream) {
   if (perm && (rc = launch_kmeans_order(a->q, a->q_dtype, L.n, perm, at<void>(ws, L.km), st)) != HTRC_OK) return rc;
   const int trows = static_cast<int>(L.trows);
   launch_tile_prep(a->q, a->q_dtype, L.n, trows, perm, group, at<float>(ws, L.mu), mu_hi, mu_lo, q8, sq, dq8, sdq, dd,
-                   L.fp8, a->qk_scale_block != 0, a->precision == HTRC_PREC_TF32, st);
+                   L.fp8, a->qk_scale_block != 0, (a->precision & HTRC_PREC_TF32) != 0,
+                   (a->precision & HTRC_PREC_TRITON_DIV) != 0, st);
   if (tail) launch_tail_partial(a->q, a->q_dtype, L.n, a->tail_k, a->tail_v, a->n_tail, scale, tail, st);
   if (cudaGetLastError() != cudaSuccess) return HTRC_ERR_CUDA;
   mark(1);
@@ -393,7 +394,8 @@ int htrc_flat_forward(const HtrcFlatArgs* a, htrc_stream_t stream) {
       LeafStatsMaps smp;
       if ((rc = stats_maps(&smp, mu_hi, mu_lo, L.ng, a->k, a->v, L.m, g8, vb, gc, L.nb, L.fp8)) != HTRC_OK) return rc;
       if ((rc = launch_leaf_stats(smp, sg, lz, L.pitch, g0, gc, nb, scale, kn2, cv, sv, status, device_info().sms,
-                                  a->precision == HTRC_PREC_TF32, st)) != HTRC_OK)
+                                  (a->precision & HTRC_PREC_TF32) != 0, (a->precision & HTRC_PREC_TRITON_DIV) != 0,
+                                  st)) != HTRC_OK)
         return rc;
     }
     mark(2 + 4 * chunk);
@@ -476,7 +478,7 @@ int htrc_tile_prep(const void* q, int32_t q_dtype, int64_t n_queries, int32_t di
   int rc = check_device();
   if (rc != HTRC_OK) return rc;
   launch_tile_prep(q, q_dtype, n_queries, tile, perm, group, mu, mu_hi, mu_lo, q8, sq, dq8, sdq, dd, false, false,
-                   false, reinterpret_cast<cudaStream_t>(stream));
+                   false, false, reinterpret_cast<cudaStream_t>(stream));
   return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
 }
 
@@ -485,7 +487,7 @@ int htrc_tile_prep_ex(const void* q, int32_t q_dtype, int64_t n_queries, int32_t
                       float* sq, int8_t* dq8, float* sdq, float* dd, int32_t q_scale_block, int32_t precision,
                       htrc_stream_t stream) {
   if (q_scale_block != 0 && q_scale_block != 64) return HTRC_ERR_ARG;
-  if (precision != HTRC_PREC_FP32 && precision != HTRC_PREC_TF32) return HTRC_ERR_ARG;
+  if ((precision & ~(HTRC_PREC_TF32 | HTRC_PREC_TRITON_DIV)) != 0) return HTRC_ERR_ARG;
   if (!q || !mu || !mu_hi || !mu_lo || !q8 || !sq || !dq8 || !sdq || n_queries < 1) return HTRC_ERR_ARG;
   if (dim != kDim || (tile != kTile && tile != kTile / 2)) return HTRC_ERR_UNSUPPORTED;
   if (q_dtype != HTRC_DTYPE_F32 && q_dtype != HTRC_DTYPE_BF16) return HTRC_ERR_ARG;
@@ -493,7 +495,8 @@ int htrc_tile_prep_ex(const void* q, int32_t q_dtype, int64_t n_queries, int32_t
   int rc = check_device();
   if (rc != HTRC_OK) return rc;
   launch_tile_prep(q, q_dtype, n_queries, tile, perm, group, mu, mu_hi, mu_lo, q8, sq, dq8, sdq, dd, false,
-                   q_scale_block != 0, precision == HTRC_PREC_TF32, reinterpret_cast<cudaStream_t>(stream));
+                   q_scale_block != 0, (precision & HTRC_PREC_TF32) != 0, (precision & HTRC_PREC_TRITON_DIV) != 0,
+                   reinterpret_cast<cudaStream_t>(stream));
   return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
 }
 
@@ -534,7 +537,7 @@ int htrc_leaf_stats(const uint16_t* mu_hi, const uint16_t* mu_lo, int64_t nt, in
                     float* lz, uint16_t* vb, const float* kn2, float* cv, int32_t precision, int32_t* status,
                     htrc_stream_t stream) {
   if (!mu_hi || !mu_lo || !k || !v || !g8 || !sg || !lz || !vb) return HTRC_ERR_ARG;
-  if (precision != HTRC_PREC_FP32 && precision != HTRC_PREC_TF32) return HTRC_ERR_ARG;
+  if ((precision & ~(HTRC_PREC_TF32 | HTRC_PREC_TRITON_DIV)) != 0) return HTRC_ERR_ARG;
   if ((kn2 == nullptr) != (cv == nullptr)) return HTRC_ERR_ARG;
   if (dim != kDim || leaf != kLeaf) return HTRC_ERR_UNSUPPORTED;
   if (nt < 1 || t0 < 0 || tc < 1 || t0 + tc > nt || n_keys < leaf || n_keys % leaf) return HTRC_ERR_ARG;
@@ -545,23 +548,23 @@ int htrc_leaf_stats(const uint16_t* mu_hi, const uint16_t* mu_lo, int64_t nt, in
   LeafStatsMaps mp;
   if ((rc = stats_maps(&mp, mu_hi, mu_lo, nt, k, v, n_keys, g8, vb, tc, nb, false)) != HTRC_OK) return rc;
   return launch_leaf_stats(mp, sg, lz, pitch_of(nb), t0, tc, static_cast<int>(nb), scale_of(scale), kn2, cv, nullptr,
-                           status, device_info().sms, precision == HTRC_PREC_TF32,
-                           reinterpret_cast<cudaStream_t>(stream));
+                           status, device_info().sms, (precision & HTRC_PREC_TF32) != 0,
+                           (precision & HTRC_PREC_TRITON_DIV) != 0, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int htrc_tile_prep_fp8(const void* q, int32_t q_dtype, int64_t n_queries, int32_t dim, int32_t tile,
                        const int32_t* perm, int32_t group, float* mu, uint16_t* mu_hi, uint16_t* mu_lo, uint16_t* qb,
                        uint16_t* dqh, int32_t precision, htrc_stream_t stream) {
   if (!q || !mu || !mu_hi || !mu_lo || !qb || !dqh || n_queries < 1) return HTRC_ERR_ARG;
-  if (precision != HTRC_PREC_FP32 && precision != HTRC_PREC_TF32) return HTRC_ERR_ARG;
+  if ((precision & ~(HTRC_PREC_TF32 | HTRC_PREC_TRITON_DIV)) != 0) return HTRC_ERR_ARG;
   if (dim != kDim || (tile != kTile && tile != kTile / 2)) return HTRC_ERR_UNSUPPORTED;
   if (q_dtype != HTRC_DTYPE_F32 && q_dtype != HTRC_DTYPE_BF16) return HTRC_ERR_ARG;
   if (group > kMaxGroup) return HTRC_ERR_ARG;
   int rc = check_device();
   if (rc != HTRC_OK) return rc;
   launch_tile_prep(q, q_dtype, n_queries, tile, perm, group, mu, mu_hi, mu_lo, reinterpret_cast<int8_t*>(qb), nullptr,
-                   reinterpret_cast<int8_t*>(dqh), nullptr, nullptr, true, false, precision == HTRC_PREC_TF32,
-                   reinterpret_cast<cudaStream_t>(stream));
+                   reinterpret_cast<int8_t*>(dqh), nullptr, nullptr, true, false, (precision & HTRC_PREC_TF32) != 0,
+                   (precision & HTRC_PREC_TRITON_DIV) != 0, reinterpret_cast<cudaStream_t>(stream));
   return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
 }
 
@@ -570,7 +573,7 @@ int htrc_leaf_stats_fp8(const uint16_t* mu_hi, const uint16_t* mu_lo, int64_t nt
                         uint8_t* g8, float* sg, float* lz, uint8_t* vb8, float* sv, int32_t precision,
                         int32_t* status, htrc_stream_t stream) {
   if (!mu_hi || !mu_lo || !k || !v || !g8 || !sg || !lz || !vb8 || !sv) return HTRC_ERR_ARG;
-  if (precision != HTRC_PREC_FP32 && precision != HTRC_PREC_TF32) return HTRC_ERR_ARG;
+  if ((precision & ~(HTRC_PREC_TF32 | HTRC_PREC_TRITON_DIV)) != 0) return HTRC_ERR_ARG;
   if (dim != kDim || leaf != kLeaf) return HTRC_ERR_UNSUPPORTED;
   if (nt < 1 || t0 < 0 || tc < 1 || t0 + tc > nt || n_keys < leaf || n_keys % leaf) return HTRC_ERR_ARG;
   const int64_t nb = n_keys / leaf;
@@ -580,8 +583,8 @@ int htrc_leaf_stats_fp8(const uint16_t* mu_hi, const uint16_t* mu_lo, int64_t nt
   LeafStatsMaps mp;
   if ((rc = stats_maps(&mp, mu_hi, mu_lo, nt, k, v, n_keys, g8, vb8, tc, nb, true)) != HTRC_OK) return rc;
   return launch_leaf_stats(mp, sg, lz, pitch_of(nb), t0, tc, static_cast<int>(nb), scale_of(scale), nullptr, nullptr,
-                           sv, status, device_info().sms, precision == HTRC_PREC_TF32,
-                           reinterpret_cast<cudaStream_t>(stream));
+                           sv, status, device_info().sms, (precision & HTRC_PREC_TF32) != 0,
+                           (precision & HTRC_PREC_TRITON_DIV) != 0, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int htrc_rowmax_select_fp8(const uint16_t* dqh, int64_t t0, int64_t tc, int32_t group, const uint8_t* g8,

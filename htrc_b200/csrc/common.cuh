@@ -353,6 +353,14 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
 
+// a / b with PTX div.full.f32: the instruction the reference's Triton kernels use for their float32 `/`
+// (approximate, full range); the opt-in HTRC_PREC_TRITON_DIV mode forms its codes with it
+__device__ __forceinline__ float div_full(float a, float b) {
+  float y;
+  asm("div.full.f32 %0, %1, %2;" : "=f"(y) : "f"(a), "f"(b));
+  return y;
+}
+
 // round half away from zero of an fp32 value already scaled into [-127.5, 127.5] (the reference's
 // trunc(x +- 0.5) in float32)
 __device__ __forceinline__ int round_half_away_i8(float y) {

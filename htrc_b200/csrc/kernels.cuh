@@ -56,7 +56,7 @@ void launch_pack_rows(const void* x, int dtype, int64_t rows, int rounding, int8
                       cudaStream_t st);
 void launch_tile_prep(const void* q, int dtype, int64_t n, int tile_rows, const int32_t* perm, int group, float* mu,
                       uint16_t* mu_hi, uint16_t* mu_lo, int8_t* q8, float* sq, int8_t* dq8, float* sdq, float* dd,
-                      bool fp8, bool qblock, bool tf32, cudaStream_t st);
+                      bool fp8, bool qblock, bool tf32, bool tdiv, cudaStream_t st);
 void launch_pack_blocks(const void* x, int dtype, int64_t rows, int rounding, int8_t* x8, float* scale,
                         float* sqnorm, cudaStream_t st);
 size_t kmeans_scratch_bytes(int64_t n);
@@ -69,7 +69,7 @@ void launch_tail_partial(const void* q, int dtype, int64_t n, const float* tk, c
                          float* part, cudaStream_t st);
 int launch_leaf_stats(const LeafStatsMaps& maps, float* sg, float* lz, int64_t pitch, int64_t t0, int64_t tc, int nb,
                       float scale, const float* kn2, float* cv, float* sv, int* status, int num_sms, bool tf32,
-                      cudaStream_t st);
+                      bool tdiv, cudaStream_t st);
 int launch_rowmax(const RowmaxMaps& maps, const float* sdq, const float* dd, float* sel, int64_t pitch, int64_t t0,
                   int64_t tc, int nb, int group, int* status, cudaStream_t st);
 int launch_route(const float* sel, int64_t pitch, int64_t tc, int group, int nb, int kx, int sink, int32_t* idx,

@@ -42,13 +42,13 @@ __device__ __forceinline__ uint32_t pack_i8x4(int a, int b, int c, int d) {
 // k + 1/2, where the correctly rounded quotient and the reference's formula decide.  Away from the
 // boundaries both rounding modes give the nearest integer.  No transcendental-unit instruction on the
 // fast path: floor and nearest integer come from adding 2^23 (toward zero / to nearest).
-template <int ROUND>
+template <int ROUND, bool DIVF = false>
 __device__ __forceinline__ int quant_code(float v, float s, float r) {
   const float ya = __fmul_rn(v, r);
   const float h = __fadd_rn(fabsf(ya), 0.5f);                          // boundaries -> integers
   const float n = __fsub_rn(__fadd_rn(h, 12582912.0f), 12582912.0f);   // nearest integer to h
   if (fabsf(__fsub_rn(h, n)) < 2.44140625e-4f) {
-    const float y = __fdiv_rn(v, s);
+    const float y = DIVF ? div_full(v, s) : __fdiv_rn(v, s);
     if (ROUND == 0) return max(-127, min(127, static_cast<int>(rintf(y))));
     return round_half_away_i8(y);
   }
@@ -59,7 +59,7 @@ __device__ __forceinline__ int quant_code(float v, float s, float r) {
 // x8 codes of 4 values given the row scale s and its reciprocal r: the fast path of quant_code on pairs
 // (paired fp32 arithmetic), the exact quotient only for the values near a rounding boundary (rare: the
 // whole warp takes that branch only when one of its lanes needs it)
-template <int ROUND>
+template <int ROUND, bool DIVF = false>
 __device__ __forceinline__ uint32_t quant4(const float (&v)[4], float s, float r) {
   const float2 r2 = make_float2(r, r);
   const float2 m2 = make_float2(12582912.0f, 12582912.0f);
@@ -80,7 +80,7 @@ __device__ __forceinline__ uint32_t quant4(const float (&v)[4], float s, float r
   }
   if (__any_sync(0xffffffffu, near)) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) c[i] = quant_code<ROUND>(v[i], s, r);
+    for (int i = 0; i < 4; ++i) c[i] = quant_code<ROUND, DIVF>(v[i], s, r);
   }
   return pack_i8x4(c[0], c[1], c[2], c[3]);
 }
@@ -245,7 +245,8 @@ __global__ void __launch_bounds__(128) tile_prep_kernel(const T* __restrict__ q,
                                                         uint16_t* __restrict__ mu_hi, uint16_t* __restrict__ mu_lo,
                                                         int8_t* __restrict__ q8, float* __restrict__ sq,
                                                         int8_t* __restrict__ dq8, float* __restrict__ sdq,
-                                                        float* __restrict__ dd, int qblock, uint32_t tmask) {
+                                                        float* __restrict__ dd, int qblock, uint32_t tmask,
+                                                        int tdiv) {
   __shared__ float qs[64][129];
   __shared__ float mus[128];
   __shared__ float tmx[4];
@@ -312,8 +313,15 @@ __global__ void __launch_bounds__(128) tile_prep_kernel(const T* __restrict__ q,
     ad = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(ad)));
     const float s_q = fmaxf(__fmul_rn(qblock ? tq : aq, kInv127), 1e-20f);
     const float s_d = fmaxf(__fmul_rn(ad, kInv127), 1e-20f);
-    reinterpret_cast<uint32_t*>(q8 + gr * 128)[lane] = quant4<1>(v, s_q, __frcp_rn(s_q));
-    reinterpret_cast<uint32_t*>(dq8 + gr * 128)[lane] = quant4<1>(d, s_d, __frcp_rn(s_d));
+    // the quotient x / s decides a code only near a rounding boundary: there it is the IEEE quotient (the
+    // reference's formula as written), or div.full.f32 (tdiv: what its Triton kernels compute on the GPU)
+    if (tdiv) {
+      reinterpret_cast<uint32_t*>(q8 + gr * 128)[lane] = quant4<1, true>(v, s_q, __frcp_rn(s_q));
+      reinterpret_cast<uint32_t*>(dq8 + gr * 128)[lane] = quant4<1, true>(d, s_d, __frcp_rn(s_d));
+    } else {
+      reinterpret_cast<uint32_t*>(q8 + gr * 128)[lane] = quant4<1>(v, s_q, __frcp_rn(s_q));
+      reinterpret_cast<uint32_t*>(dq8 + gr * 128)[lane] = quant4<1>(d, s_d, __frcp_rn(s_d));
+    }
     if (lane == 0) {
       sq[gr] = s_q;
       sdq[gr] = s_d;
@@ -327,7 +335,7 @@ __global__ void __launch_bounds__(128) tile_prep_kernel(const T* __restrict__ q,
 
 void launch_tile_prep(const void* q, int dtype, int64_t n, int tile_rows, const int32_t* perm, int group, float* mu,
                       uint16_t* mu_hi, uint16_t* mu_lo, int8_t* q8, float* sq, int8_t* dq8, float* sdq, float* dd,
-                      bool fp8, bool qblock, bool tf32, cudaStream_t st) {
+                      bool fp8, bool qblock, bool tf32, bool tdiv, cudaStream_t st) {
   const int tr = tile_rows == 32 ? 32 : 64;
   const uint32_t tmask = tf32 ? kTf32Mask : 0xFFFFFFFFu;
   const int64_t nt = (n + tr - 1) / tr;
@@ -338,13 +346,13 @@ void launch_tile_prep(const void* q, int dtype, int64_t n, int tile_rows, const 
     if (g > 1) group_centre_kernel<uint16_t><<<ng, 128, 0, st>>>(qb, perm, n, tr, nt, g, mu, mu_hi, mu_lo, tmask);
     auto k = fp8 ? tile_prep_kernel<uint16_t, true> : tile_prep_kernel<uint16_t, false>;
     k<<<static_cast<unsigned>(nt), 128, 0, st>>>(qb, perm, n, tr, g, mu, mu_hi, mu_lo, q8, sq, dq8, sdq, dd,
-                                                 qblock ? 1 : 0, tmask);
+                                                 qblock ? 1 : 0, tmask, tdiv ? 1 : 0);
   } else {
     const float* qf = static_cast<const float*>(q);
     if (g > 1) group_centre_kernel<float><<<ng, 128, 0, st>>>(qf, perm, n, tr, nt, g, mu, mu_hi, mu_lo, tmask);
     auto k = fp8 ? tile_prep_kernel<float, true> : tile_prep_kernel<float, false>;
     k<<<static_cast<unsigned>(nt), 128, 0, st>>>(qf, perm, n, tr, g, mu, mu_hi, mu_lo, q8, sq, dq8, sdq, dd,
-                                                 qblock ? 1 : 0, tmask);
+                                                 qblock ? 1 : 0, tmask, tdiv ? 1 : 0);
   }
 }
 

@@ -98,7 +98,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                       const __grid_constant__ CUtensorMap tm_g8, const __grid_constant__ CUtensorMap tm_vb,
                       float* __restrict__ sg_out, float* __restrict__ lz_out, int64_t pitch, int64_t t0, int64_t tc,
                       int nb, int leaves_per_cta, float scale, const float* __restrict__ kn2,
-                      float* __restrict__ cv_out, float* __restrict__ sv_out, int* status, uint32_t wmask) {
+                      float* __restrict__ cv_out, float* __restrict__ sv_out, int* status, uint32_t wmask,
+                      int tdiv) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Bars* bars = reinterpret_cast<Bars*>(smem + kOffBar);
@@ -396,8 +397,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t gw[16], vw[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const float2 a = mul2(mul2(make_float2(__uint_as_float(gr[4 * i]), __uint_as_float(gr[4 * i + 1])), sc2), rg2);
-          const float2 b = mul2(mul2(make_float2(__uint_as_float(gr[4 * i + 2]), __uint_as_float(gr[4 * i + 3])), sc2), rg2);
+          const float2 ga = mul2(make_float2(__uint_as_float(gr[4 * i]), __uint_as_float(gr[4 * i + 1])), sc2);
+          const float2 gb = mul2(make_float2(__uint_as_float(gr[4 * i + 2]), __uint_as_float(gr[4 * i + 3])), sc2);
+          // g / sg: g * (1 / sg), or per value with div.full.f32 like the reference's Triton kernel (tdiv)
+          const float2 a = tdiv ? make_float2(div_full(ga.x, sgv), div_full(ga.y, sgv)) : mul2(ga, rg2);
+          const float2 b = tdiv ? make_float2(div_full(gb.x, sgv), div_full(gb.y, sgv)) : mul2(gb, rg2);
           gw[i] = f32x2_to_e4m3x2(a.x, a.y) | (f32x2_to_e4m3x2(b.x, b.y) << 16);
         }
 #pragma unroll
@@ -407,8 +411,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld_wait();
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
-            const float2 a = mul2(make_float2(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1])), rv2);
-            const float2 b = mul2(make_float2(__uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3])), rv2);
+            const float2 va = make_float2(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]));
+            const float2 vb2 = make_float2(__uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
+            const float2 a = tdiv ? make_float2(div_full(va.x, svv), div_full(va.y, svv)) : mul2(va, rv2);
+            const float2 b = tdiv ? make_float2(div_full(vb2.x, svv), div_full(vb2.y, svv)) : mul2(vb2, rv2);
             vw[8 * c + i] = f32x2_to_e4m3x2(a.x, a.y) | (f32x2_to_e4m3x2(b.x, b.y) << 16);
           }
         }
@@ -486,7 +492,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       am = fmaxf(am, 1e-30f);
       const float sgv = __fmul_rn(am, 1.0f / 127.0f);
-      const float rr = __fdiv_rn(127.0f, am);
+      // the factor 127 / am: IEEE, or div.full.f32 like the reference's Triton kernel (tdiv)
+      const float rr = tdiv ? div_full(127.0f, am) : __fdiv_rn(127.0f, am);
       if (valid && half == 0) sg_out[tloc * pitch + leaf] = sgv;
       // INT8 codes
       uint32_t gw[16];
@@ -533,7 +540,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 int launch_leaf_stats(const LeafStatsMaps& maps, float* sg, float* lz, int64_t pitch, int64_t t0, int64_t tc, int nb,
                       float scale, const float* kn2, float* cv, float* sv, int* status, int num_sms, bool tf32,
-                      cudaStream_t st) {
+                      bool tdiv, cudaStream_t st) {
   static bool attr_done[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -554,7 +561,7 @@ int launch_leaf_stats(const LeafStatsMaps& maps, float* sg, float* lz, int64_t p
                                : (cv != nullptr ? leaf_stats_kernel<true, false> : leaf_stats_kernel<false, false>);
   kernel<<<dim3(bx, by), kThreads, kSmemBytes, st>>>(maps.mu_hi, maps.mu_lo, maps.nt, maps.k, maps.v, maps.g8, maps.vb,
                                                      sg, lz, pitch, t0, tc, nb, lpc, scale, kn2, cv, sv, status,
-                                                     tf32 ? kTf32Mask : 0xFFFFFFFFu);
+                                                     tf32 ? kTf32Mask : 0xFFFFFFFFu, tdiv ? 1 : 0);
   return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
 }
 

@@ -8,24 +8,20 @@
 //   near (one routed 64-token leaf per step):           S = q8 . k8^T,
 //        logit = S * (sq_r * ks_j * scale), value v_j (bf16).
 // Every MMA is M=64 per tile: tile A's rows live in TMEM lanes {0..15} + 32k, tile B's at lane offset
-// 16, so a softmax thread's TMEM lane is one query row of S, P and O.  P (bf16) is written back into the
+// 16, so each softmax thread owns one query row of S, P and O.  P (bf16) is written back into the
 // TMEM columns of its S buffer and feeds O += P . V as the TMEM A operand; V comes from shared memory
 // as an MN-major B operand.
 //
-// Steps alternate between two parities, each with its own running (max, sum) and O accumulator; the two
-// partials (and the tail partial) are merged in the epilogue.  A step's 64 columns are split between two
-// softmax warpgroups (columns 0-31 and 32-63 of every row), which exchange their partial row maxima through
-// shared memory and an mbarrier, keep partial row sums under the same running maximum, and each write P and
-// rescale O for their half: the serial softmax of a step is half as long as with one warpgroup per step.
-// The running maximum is updated lazily: a row's O is rescaled only when its maximum grew by more than 2^8
-// (P <= 256 otherwise).
+// Two softmax warpgroups take alternate steps, each with its own running (max, sum) and O accumulator;
+// the two partials (and the tail partial) are merged in the epilogue.  The running maximum is updated
+// lazily: a thread rescales its O row only when its maximum grew by more than 2^8 (P <= 256 otherwise).
 //
 // Data movement: the QK operand of a step (g8 block or k8 leaf, plus its per-column parameters) goes
-// through a 2-slot ring freed as soon as the QK MMA completes; the PV operand (vbar block or v leaf)
+// through a 3-slot ring freed as soon as the QK MMA completes; the PV operand (vbar block or v leaf)
 // through a 4-slot ring freed by the PV MMA (the value loads are the longer-lead ones: a step's V is
 // requested four steps ahead).  The completion of PV(j) (one commit, pv_done[j % 4]) frees
-// S/P buffer j % 4 for QK(j + 4), Y slot j % 4 for step j + 4, and lets the warpgroups of step j + 2
-// rescale their O columns.  All waits block (a suspended thread takes no issue slots from the softmax warps).
+// S/P buffer j % 4 for QK(j + 4), Y slot j % 4 for step j + 4, and lets the warpgroup of step j + 2
+// rescale its O rows.  All waits block (a suspended thread takes no issue slots from the softmax warps).
 // The producer and issuer warps run converged and let one elected lane issue: a warp whose lanes take
 // different roles serialises them, since a lane suspended in an mbarrier wait holds up the others.
 //
@@ -40,18 +36,17 @@
 // tile t of the chunk reads state row t / G.  k-means order (:146-147, :159-165): tile row i is query
 // perm[i], so the epilogue writes out/lse row perm[i] (and reads the tail partial of that row).
 //
-// Warp roles (640 threads, five warpgroups): warp 0 X-ring producer; warp 1 PV issuer (+ TMEM owner);
-// warp 2 per-column constants (scale * log2 e, lz * log2 e or -inf); warp 3 QK issuer and Y-ring producer
-// (both wait for the same PV completions); warpgroups 1-4 (warps 4-19) the softmax: warpgroup 1 + sw takes
-// the steps of parity sw & 1, columns 32 (sw >> 1) .. + 31.
+// Warp roles (384 threads): warp 0 X-ring producer; warp 1 PV issuer (+ TMEM owner); warp 11 QK issuer
+// and Y-ring producer (both wait for the same PV completions); warps 2-5 and 6-9 the two softmax
+// warpgroups; warp 10 per-column constants (scale * log2 e, lz * log2 e or -inf).
 #include "common.cuh"
 #include "kernels.cuh"
 
 namespace htrc {
 
 namespace {
-constexpr int kThreads = 640;
-constexpr int kXSlots = 2;
+constexpr int kThreads = 384;
+constexpr int kXSlots = 3;
 constexpr int kYSlots = 4;
 constexpr int kSBufs = 4;
 static_assert(kYSlots <= kSBufs, "the QK issuer's loop produces Y(j + kYSlots) for every QK(j + kSBufs)");
@@ -66,9 +61,8 @@ constexpr uint32_t kOffDq8 = 16384;                             // 2 tiles x 8 K
 constexpr uint32_t kOffX = 32768;
 constexpr uint32_t kOffY = kOffX + kXSlots * kXSlot;
 constexpr uint32_t kOffCC = kOffY + kYSlots * kYSlot;           // [X slot][tile][64] float2 constants
-constexpr uint32_t kOffXm = kOffCC + kXSlots * 2 * 64 * 8;      // [parity][slot][half][128] partial row maxima
-constexpr uint32_t kOffEpi = kOffXm + 2 * 2 * 2 * 128 * 4;      // m1 [128], l1 [2][128], l0 [2][128]
-constexpr uint32_t kOffIdx = kOffEpi + 5 * 128 * 4;             // [tile][kMaxKx] uint16
+constexpr uint32_t kOffEpi = kOffCC + kXSlots * 2 * 64 * 8;     // m1, l1 [128] each
+constexpr uint32_t kOffIdx = kOffEpi + 2 * 128 * 4;             // [tile][kMaxKx] uint16
 constexpr int kMaxKx = 1024;
 constexpr uint32_t kOffCC3 = kOffIdx + 2 * kMaxKx * 2;          // ISO: [X slot][tile][64] c * log2 e (0 for near)
 constexpr uint32_t kOffBar = kOffCC3 + kXSlots * 2 * 64 * 4;
@@ -88,12 +82,11 @@ struct Bars {
   uint64_t x_empty[kXSlots];    // QK MMA done (commit) + constants read (32 helper lanes)
   uint64_t y_full[kYSlots];
   uint64_t cc_full[kXSlots];    // 32 helper lanes
-  uint64_t cc_empty[kXSlots];   // 256 softmax threads of the step's two warpgroups
+  uint64_t cc_empty[kXSlots];   // 128 softmax threads of the step's warpgroup
   uint64_t s_full[kSBufs];      // QK done
-  uint64_t p_full[kSBufs];      // 256 softmax threads wrote P into the buffer (and rescaled O if needed)
+  uint64_t p_full[kSBufs];      // 128 softmax threads wrote P into the buffer (and rescaled O if needed)
   uint64_t pv_done[kSBufs];     // PV of the step in this buffer done
-  uint64_t xch[2][2];           // [parity][slot]: 256 softmax threads wrote their half-row maxima
-  uint64_t epi0, epi1;          // 256 threads of the even / odd parity wrote their partial sums
+  uint64_t epi1;
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -138,18 +131,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars->x_full[s], 1);
       mbar_init(&bars->x_empty[s], 1 + 32);
       mbar_init(&bars->cc_full[s], 32);
-      mbar_init(&bars->cc_empty[s], 256);
+      mbar_init(&bars->cc_empty[s], 128);
     }
     for (int s = 0; s < kYSlots; ++s) mbar_init(&bars->y_full[s], 1);
     for (int b = 0; b < kSBufs; ++b) {
       mbar_init(&bars->s_full[b], 1);
-      mbar_init(&bars->p_full[b], 256);
+      mbar_init(&bars->p_full[b], 128);
       mbar_init(&bars->pv_done[b], 1);
     }
-    for (int p2 = 0; p2 < 2; ++p2)
-      for (int sl = 0; sl < 2; ++sl) mbar_init(&bars->xch[p2][sl], 256);
-    mbar_init(&bars->epi0, 256);
-    mbar_init(&bars->epi1, 256);
+    mbar_init(&bars->epi1, 128);
     bars->abort_flag = 0;
     fence_barrier_init();
   }
@@ -249,7 +239,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mma_commit_by(leader, &bars->pv_done[b]);
       if (++ys == kYSlots) { ys = 0; yph ^= 1; }
     }
-  } else if (warp == 3) {
+  } else if (warp == 11) {
     // ------------------------------------------------------------------ QK issuer + Y-ring producer
     // Both wait for PV(j): it frees S/P buffer j % 4 for QK(j + 4) and Y slot j % 4 for step j + 4.
     const uint64_t pol_stream = policy_evict_first();
@@ -306,7 +296,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (j + kSBufs < total) ok = issue_qk(j + kSBufs);    // first: QK(j + 4) is on the step's critical chain
       produce_y(j + kYSlots);
     }
-  } else if (warp == 2) {
+  } else if (warp == 10) {
     // ------------------------------------------------------------------ per-column constants
     // far: (sg * log2 e, lz * log2 e or -inf if routed / past nb) per column; near: ks * scale * log2 e per
     // column, packed
@@ -341,17 +331,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------------ softmax warpgroups
-    // warpgroup sw = 0..3: step parity g = sw & 1, columns [32 h, 32 h + 32) of each step with h = sw >> 1; the
-    // two halves of a step exchange their partial row maxima through shared memory (one mbarrier per
-    // (parity, slot)), keep partial row sums, and each rescales and writes half of the O columns
-    const int sw = (warp >> 2) - 1;
-    const int g = sw & 1;
-    const int half = sw >> 1;
+    const int g = (warp - 2) >> 2;            // warpgroup: 0 takes even steps, 1 odd steps
     const int quarter = warp & 3;
     const int x = lane >> 4;                  // tile of this thread's query row
     const int r = quarter * 16 + (lane & 15);
     const int col = x * 64 + r;
-    const int tix = quarter * 32 + lane;      // the same row in the other half of the step
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const bool has_tile = x < ntiles;
     const bool warp_rows = quarter * 16 < TROWS;   // warp-uniform: false for the held copies of row 31
@@ -360,57 +344,52 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float sq_r = has_tile ? __ldg(sq + gr) : 0.f;
     const float sdq_r = has_tile ? __ldg(sdq + gr) : 0.f;
     const float dd_r = (ISO && has_tile) ? __ldg(dd + gr) : 0.f;
-    float* xm = reinterpret_cast<float*>(smem + kOffXm);       // [parity][slot][half][128] partial maxima
     float m_used = -INFINITY, l = 0.f;
     bool aborted = false;
     int kcount = 0;
     for (int j = g; j < total; j += 2, ++kcount) {
-      const int s = j % kXSlots, b = j & 3, sl = (j >> 1) & 1;
-      float* xs = xm + ((g * 2 + sl) * 2) * 128;
+      const int s = j % kXSlots, b = j & 3;
       if (!mbar_wait_warp(&bars->s_full[b], (j >> 2) & 1, status, abort_flag)) { aborted = true; break; }
       __syncwarp();
       tc_fence_after();
       if (TROWS < 64 && !warp_rows) {
-        // held copies only: consume the step's constants in order, take part in the maximum exchange and write
-        // P = 0 after QK(j)
+        // held copies only: consume the step's constants in order and write P = 0 after QK(j)
         if (!mbar_wait_warp(&bars->cc_full[s], (j / kXSlots) & 1, status, abort_flag)) { aborted = true; break; }
         mbar_arrive(&bars->cc_empty[s]);
-        xs[half * 128 + tix] = -INFINITY;
-        tc_fence_before();
-        mbar_arrive(&bars->xch[g][sl]);
-        if (!mbar_wait_warp(&bars->xch[g][sl], (j >> 2) & 1, status, abort_flag)) { aborted = true; break; }
-        tc_fence_after();
-        uint32_t z[16];
+        uint32_t z[32];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) z[i] = 0u;
-        tmem_st16(tmem + lane_base + kColS + 64 * b + 16 * half, z);
+        for (int i = 0; i < 32; ++i) z[i] = 0u;
+        tmem_st32(tmem + lane_base + kColS + 64 * b, z);
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive(&bars->p_full[b]);
         continue;
       }
-      uint32_t d0[32];
-      tmem_ld32(tmem + lane_base + kColS + 64 * b + 32 * half, d0);
+      uint32_t d0[32], d1[32];
+      tmem_ld32(tmem + lane_base + kColS + 64 * b, d0);
+      tmem_ld32(tmem + lane_base + kColS + 64 * b + 32, d1);
       tmem_ld_wait();
       if (!mbar_wait_warp(&bars->cc_full[s], (j / kXSlots) & 1, status, abort_flag)) { aborted = true; break; }
-      const float2* c = cc + s * 128 + x * 64 + 32 * half;
+      const float2* c = cc + s * 128 + x * 64;
       const float2 magic2 = make_float2(kMagic, kMagic);
-      float lg[32];
+      float lg[64];
       float mxa[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};   // independent chains
       float esc;        // the exponent's argument is esc * lg - m (one FMA)
       if (j >= nf) {
         // near step (warp-uniform): lg = S * (ks * scale * log2 e); the row's scale sq_r > 0 multiplies after
         // the maximum and inside the exponent's FMA.  The constants are packed one per column.
-        const float* c1 = reinterpret_cast<const float*>(cc + s * 128) + x * 64 + 32 * half;
+        const float* c1 = reinterpret_cast<const float*>(cc + s * 128) + x * 64;
 #pragma unroll
-        for (int i = 0; i < 32; i += 4) {
+        for (int i = 0; i < 64; i += 4) {
           const float4 cv = *reinterpret_cast<const float4*>(c1 + i);    // c1 of columns i .. i + 3
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             const int ii = i + 2 * h;
-            const float2 xm2 = make_float2(__int_as_float(static_cast<int>(d0[ii]) + kMagicBits),
-                                           __int_as_float(static_cast<int>(d0[ii + 1]) + kMagicBits));
-            const float2 u = mul2(sub2(xm2, magic2), h ? make_float2(cv.z, cv.w) : make_float2(cv.x, cv.y));
+            const uint32_t di0 = ii < 32 ? d0[ii] : d1[ii - 32];
+            const uint32_t di1 = ii < 32 ? d0[ii + 1] : d1[ii - 31];
+            const float2 xm = make_float2(__int_as_float(static_cast<int>(di0) + kMagicBits),
+                                          __int_as_float(static_cast<int>(di1) + kMagicBits));
+            const float2 u = mul2(sub2(xm, magic2), h ? make_float2(cv.z, cv.w) : make_float2(cv.x, cv.y));
             lg[ii] = u.x;
             lg[ii + 1] = u.y;
             mxa[(ii >> 1) & 3] = max3(mxa[(ii >> 1) & 3], u.x, u.y);
@@ -419,15 +398,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         esc = sq_r;
       } else {
         // far step: lg = S * (sdq_r * sg * log2 e) + lz * log2 e (+ the iso term), masked columns -inf
-        const float* c3 = reinterpret_cast<const float*>(smem + kOffCC3) + s * 128 + x * 64 + 32 * half;
+        const float* c3 = reinterpret_cast<const float*>(smem + kOffCC3) + s * 128 + x * 64;
         const float2 dd2 = make_float2(dd_r, dd_r);
         const float2 srow2 = make_float2(sdq_r, sdq_r);
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) {
+        for (int i = 0; i < 64; i += 2) {
           const float4 cv = *reinterpret_cast<const float4*>(c + i);     // (c1_i, c2_i, c1_i+1, c2_i+1)
-          const float2 xm2 = make_float2(__int_as_float(static_cast<int>(d0[i]) + kMagicBits),
-                                         __int_as_float(static_cast<int>(d0[i + 1]) + kMagicBits));
-          const float2 fd = sub2(xm2, magic2);
+          const uint32_t di0 = i < 32 ? d0[i] : d1[i - 32];
+          const uint32_t di1 = i < 32 ? d0[i + 1] : d1[i - 31];
+          const float2 xm = make_float2(__int_as_float(static_cast<int>(di0) + kMagicBits),
+                                        __int_as_float(static_cast<int>(di1) + kMagicBits));
+          const float2 fd = sub2(xm, magic2);
           const float2 t = mul2(srow2, make_float2(cv.x, cv.z));
           float2 v = fma2(fd, t, make_float2(cv.y, cv.w));
           if (ISO) v = fma2(*reinterpret_cast<const float2*>(c3 + i), dd2, v);
@@ -437,17 +418,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         esc = 1.0f;
       }
+      const float mx = __fmul_rn(esc, fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])));
       mbar_arrive(&bars->cc_empty[s]);
-      // the row maximum over both halves of the step's columns
-      const float mh = fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3]));
-      xs[half * 128 + tix] = mh;
-      // the exchange also orders this half's S loads (complete: tcgen05.wait::ld above) before the other
-      // half's P stores into S columns 16..31
-      tc_fence_before();
-      mbar_arrive(&bars->xch[g][sl]);
-      if (!mbar_wait_warp(&bars->xch[g][sl], (j >> 2) & 1, status, abort_flag)) { aborted = true; break; }
-      tc_fence_after();
-      const float mx = __fmul_rn(esc, fmaxf(mh, xs[(1 - half) * 128 + tix]));
       // rows of an absent tile B (odd tile count) hold stale TMEM: keep them inert
       const float m_new = has_tile ? fmaxf(m_used, mx) : m_used;
       const bool need = m_new > m_used + kRescale;
@@ -460,10 +432,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       // tile B get garbage P, which no MMA reads (PV runs for present tiles only)
       const float mref = m_used != -INFINITY ? m_used : 0.f;
       const float2 negm2 = make_float2(-mref, -mref), esc2 = make_float2(esc, esc);
-      uint32_t pw[16];
+      uint32_t pw[32];
       float2 rs2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
-      for (int i = 0; i < 32; i += 2) {
+      for (int i = 0; i < 64; i += 2) {
         const float2 e = fma2(make_float2(lg[i], lg[i + 1]), esc2, negm2);
         const float2 p = make_float2(ex2(e.x), ex2(e.y));
         rs2[(i >> 1) & 3] = add2(rs2[(i >> 1) & 3], p);
@@ -471,9 +443,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const float2 rsa = add2(add2(rs2[0], rs2[1]), add2(rs2[2], rs2[3]));
       l += rsa.x + rsa.y;
-      // this half's 64 columns of the O row are rescaled only after this parity's previous PV (step j - 2) is
-      // done; the whole warp takes part because TMEM loads and stores are warp-collective.  pv_done[(j - 2) % 4]
-      // is then at most one phase behind: QK(j) was issued after PV(j - 4) completed.
+      // the O row is rescaled only after this warpgroup's previous PV (step j - 2) is done; the whole
+      // warp takes part because TMEM loads and stores are warp-collective.  pv_done[(j - 2) % 4] is then
+      // at most one phase behind: QK(j - 2) was issued after PV(j - 6) completed.
       __syncwarp();
       const bool any_need = __any_sync(0xffffffffu, need);
       if (kcount >= 1 && any_need) {
@@ -484,42 +456,32 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         tc_fence_after();
 #pragma unroll
-        for (int q2 = 0; q2 < 4; ++q2) {
-          uint32_t o[16];
-          const uint32_t oa = tmem + lane_base + kColO + 128 * g + 64 * half + 16 * q2;
-          tmem_ld16(oa, o);
+        for (int q4 = 0; q4 < 4; ++q4) {
+          uint32_t o[32];
+          tmem_ld32(tmem + lane_base + kColO + 128 * g + 32 * q4, o);
           tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          tmem_st16(oa, o);
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(tmem + lane_base + kColO + 128 * g + 32 * q4, o);
         }
       }
-      // P of this half's keys (16 bf16 pairs) over the S columns both halves have read (the exchange above)
-      tmem_st16(tmem + lane_base + kColS + 64 * b + 16 * half, pw);
+      tmem_st32(tmem + lane_base + kColS + 64 * b, pw);
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&bars->p_full[b]);
     }
     // ---------------------------------------------------------------- epilogue
-    // partial sums: l1s[half] of the odd parity, l0s[half] of the even one; m1s the odd parity's maximum
-    const int jl = g + 2 * (kcount - 1);     // this parity's last step
+    const int jl = g + 2 * (kcount - 1);     // this warpgroup's last step
     const bool last_ok =
         !aborted && (kcount == 0 || mbar_wait_warp(&bars->pv_done[jl & 3], (jl >> 2) & 1, status, abort_flag));
-    float* m1s = reinterpret_cast<float*>(smem + kOffEpi);
-    float* l1s = m1s + 128;                   // [half][128]
-    float* l0s = m1s + 3 * 128;               // [half][128]
+    float* m1s = epi;
+    float* l1s = epi + 128;
     if (g == 1) {
-      if (half == 0) m1s[col] = kcount ? m_used : -INFINITY;
-      l1s[half * 128 + col] = l;
+      m1s[col] = kcount ? m_used : -INFINITY;
+      l1s[col] = l;
       mbar_arrive(&bars->epi1);
-    } else {
-      l0s[half * 128 + col] = l;
-      mbar_arrive(&bars->epi0);
-    }
-    if (g == 0 && last_ok && mbar_wait_warp(&bars->epi1, 0, status, abort_flag) &&
-        mbar_wait_warp(&bars->epi0, 0, status, abort_flag)) {
-      const float m1 = m1s[col], l1 = l1s[col] + l1s[128 + col];
-      const float l0 = l0s[col] + l0s[128 + col];
+    } else if (last_ok && mbar_wait_warp(&bars->epi1, 0, status, abort_flag)) {
+      const float m1 = m1s[col], l1 = l1s[col];
       const float m0 = kcount ? m_used : -INFINITY;
       const float n0 = m0 * kLn2, n1 = m1 * kLn2;           // natural-log units
       const int64_t li = (t0 + tl) * TROWS + r;                  // query index in tile order
@@ -531,29 +493,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float a0 = n0 == -INFINITY ? 0.f : expf(n0 - mm);
       const float a1 = n1 == -INFINITY ? 0.f : expf(n1 - mm);
       const float at = mt == -INFINITY ? 0.f : expf(mt - mm);
-      const float den = l0 * a0 + l1 * a1 + lt * at;
+      const float den = l * a0 + l1 * a1 + lt * at;
       const float inv = 1.0f / fmaxf(den, 1e-30f);
       const float c0 = a0 * inv, c1 = a1 * inv, ct = at * inv;
-      if (valid && lse != nullptr && half == 0) lse[orow] = mm + logf(fmaxf(den, 1e-30f));
+      if (valid && lse != nullptr) lse[orow] = mm + logf(fmaxf(den, 1e-30f));
       __syncwarp();
       tc_fence_after();
 #pragma unroll 1
-      for (int q4 = 4 * half; q4 < 4 * half + 4; ++q4) {       // this half's 64 columns, 16 at a time
-        uint32_t o0[16], o1[16];
-        tmem_ld16(tmem + lane_base + kColO + 16 * q4, o0);
-        tmem_ld16(tmem + lane_base + kColO + 128 + 16 * q4, o1);
+      for (int q4 = 0; q4 < 4; ++q4) {
+        uint32_t o0[32], o1[32];
+        tmem_ld32(tmem + lane_base + kColO + 32 * q4, o0);
+        tmem_ld32(tmem + lane_base + kColO + 128 + 32 * q4, o1);
         tmem_ld_wait();
         if (valid) {
-          float4* dst = reinterpret_cast<float4*>(out + orow * 128 + 16 * q4);
+          float4* dst = reinterpret_cast<float4*>(out + orow * 128 + 32 * q4);
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
+          for (int i = 0; i < 8; ++i) {
             float v[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               float a = 0.f;
               if (c0 != 0.f) a = __uint_as_float(o0[4 * i + e]) * c0;
               if (c1 != 0.f) a = fmaf(__uint_as_float(o1[4 * i + e]), c1, a);
-              if (ct != 0.f) a = fmaf(tp[16 * q4 + 4 * i + e], ct, a);
+              if (ct != 0.f) a = fmaf(tp[32 * q4 + 4 * i + e], ct, a);
               v[e] = a;
             }
             dst[i] = make_float4(v[0], v[1], v[2], v[3]);

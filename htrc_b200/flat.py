@@ -23,7 +23,10 @@ expansion centre, far-field state and routing (:223-231).
 Precision: ``precision="tf32"`` (PROD's setting) runs the leaf-statistics dots on tf32 operand values, the
 float32 centre and softmax weights with their low 13 mantissa bits cleared, which is how the reference's
 tensor-core dots read them on sm_100 (h3/htrc_flat_triton.py:57, :62-63); any other value runs them
-float32-accurate (the reference's "ieee").  The codes, routing and attention arithmetic are the same for both.
+float32-accurate (the reference's "ieee").  ``division="triton"`` (an addition; default "ieee") forms the query
+and offset codes and the slope scaling with PTX div.full.f32, the instruction the reference's Triton kernels
+use for their float32 ``/`` on the GPU: with PROD's precision the codes then match the reference's GPU
+operator, while "ieee" matches its formula as written (and its CPU-recorded fixtures).
 
 Additions over the reference: ``return_lse=True`` also returns the log-partition per query
 (logit units, scale * q.k), ``backend`` accepts "cuda"/"b200" as names of the same path, and
@@ -199,10 +202,13 @@ def order_code(order) -> int:
     return _lib.ORDER_KMEANS if order == "kmeans" else _lib.ORDER_SEQ
 
 
-def precision_code(precision) -> int:
-    """The reference maps precision == "tf32" to tf32 dots and anything else to IEEE float32
-    (h3/htrc_flat.py:126-130)."""
-    return _lib.PREC_TF32 if precision == "tf32" else _lib.PREC_FP32
+def precision_code(precision, division="ieee") -> int:
+    """The arithmetic flags of the C ABI: the reference maps precision == "tf32" to tf32 dots and anything else
+    to IEEE float32 (h3/htrc_flat.py:126-130); division "triton" adds the reference's GPU division of the
+    codes."""
+    if division not in _lib.DIVISIONS:
+        raise ValueError("division must be 'ieee' or 'triton'")
+    return (_lib.PREC_TF32 if precision == "tf32" else _lib.PREC_FP32) | _lib.DIVISIONS[division]
 
 
 def curvature_code(curvature) -> int:
@@ -351,7 +357,7 @@ def flat_attention(q, k, v, *, tile=64, exact_leaves=64, order="seq", curvature=
                    tile_chunk=32, precision="fp32", leaf=16, scale=None, prof=None,
                    select="max", backend="torch", store="fp32", splits=8, dot="tf32",
                    sel_stride=1, kern=None, quant=None, sink_leaves=0, tail=None, ws=None,
-                   return_lse=False, qk_scale_block=None):
+                   return_lse=False, qk_scale_block=None, division="ieee"):
     """q [N, 128], k/v [M, 128] on a CUDA device -> out [N, 128] float32 (and lse [N] with
     return_lse).  Signature and defaults of the reference (h3/htrc_flat.py:99-103); see PROD."""
     _check_args(q, k, v, tile, exact_leaves, order, curvature, leaf, select, backend, store, dot,
@@ -359,7 +365,7 @@ def flat_attention(q, k, v, *, tile=64, exact_leaves=64, order="seq", curvature=
     qsb = _check_scale_block(qk_scale_block, store)
     qd, kb, vb, tk, tv = _prep_inputs(q, k, v, tail, quant)
     grp, oc, cc, sc = group_of(kern), order_code(order), curvature_code(curvature), _lib.STORES[store]
-    pc = precision_code(precision)
+    pc = precision_code(precision, division)
     if prof is not None:
         st = run_stages(qd, kb, vb, tk, tv, exact_leaves=exact_leaves, sink_leaves=sink_leaves,
                         tile_chunk=tile_chunk, scale=scale, prof=prof, group=grp, order=oc, tile=tile, curvature=cc,
@@ -392,7 +398,7 @@ def flat_attention_heads(q, k, v, *, return_lse=False, ws=None, **cfg):
     h, n = int(q.shape[0]), int(q.shape[1])
     c = {**dict(tile=64, exact_leaves=64, order="seq", curvature="lin", tile_chunk=32, leaf=16, select="max",
                 backend="torch", store="fp32", dot="tf32", sel_stride=1, kern=None, quant=None, sink_leaves=0,
-                tail=None, scale=None, qk_scale_block=None, precision="fp32"), **cfg}
+                tail=None, scale=None, qk_scale_block=None, precision="fp32", division="ieee"), **cfg}
     _check_args(q[0], k[0], v[0], c["tile"], c["exact_leaves"], c["order"], c["curvature"], c["leaf"], c["select"],
                 c["backend"], c["store"], c["dot"], c["sel_stride"], c["quant"], c["sink_leaves"], c["tail"])
     qsb = _check_scale_block(c["qk_scale_block"], c["store"])
@@ -410,7 +416,7 @@ def flat_attention_heads(q, k, v, *, return_lse=False, ws=None, **cfg):
         forward_into(qd, kb, vb, tk, tv, exact_leaves=c["exact_leaves"], sink_leaves=c["sink_leaves"],
                      tile_chunk=c["tile_chunk"], scale=c["scale"], out=out[i], lse=lse[i] if return_lse else None,
                      workspace=w, group=grp, order=oc, tile=c["tile"], curvature=cc, store=sc, qk_scale_block=qsb,
-                     precision=precision_code(c["precision"]))
+                     precision=precision_code(c["precision"], c["division"]))
     return (out, lse) if return_lse else out
 
 

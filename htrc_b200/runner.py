@@ -161,7 +161,8 @@ class FlatRunner:
             kw = dict(exact_leaves=c["exact_leaves"], sink_leaves=c["sink_leaves"], tile_chunk=c["tile_chunk"],
                       scale=c.get("scale"), out=self._so, lse=self._sl, workspace=self._w, group=self.group,
                       order=self.order, tile=c["tile"], curvature=self.curvature, store=self.store,
-                      qk_scale_block=self.qk_scale_block, precision=_flat.precision_code(c.get("precision", "fp32")))
+                      qk_scale_block=self.qk_scale_block, precision=_flat.precision_code(c.get("precision", "fp32"),
+                                                                               c.get("division", "ieee")))
             self._capturing = True
             try:
                 side = torch.cuda.Stream()

@@ -48,12 +48,19 @@ enum { HTRC_CURV_LIN = 0, HTRC_CURV_ISO = 1 };
 enum { HTRC_ROUND_HALF_EVEN = 0, HTRC_ROUND_HALF_AWAY = 1 };
 enum { HTRC_FQ_INT8 = 1, HTRC_FQ_INT4 = 2, HTRC_FQ_FP8 = 3, HTRC_FQ_FP4 = 4 }; /* htrc_fake_quant formats */
 enum { HTRC_STORE_INT8 = 0, HTRC_STORE_FP8 = 1 };                             /* far-field state format */
-/* Precision of the leaf-statistics dots (the reference's precision= argument, h3/htrc_flat.py:101, :126-130):
- * HTRC_PREC_FP32 ("fp32", the reference's PREC "ieee"): float32-accurate products (bf16 hi + lo splits of the
- * float32 centre and softmax weights); HTRC_PREC_TF32 ("tf32", PROD's setting, h3/htrc_flat.py:391): the
- * float32 operands enter as tf32, their low 13 mantissa bits cleared, the way the reference's tensor-core dots
- * (h3/htrc_flat_triton.py:57, :62-63) read them on sm_100. */
-enum { HTRC_PREC_FP32 = 0, HTRC_PREC_TF32 = 1 };
+/* Arithmetic flags (HtrcFlatArgs.precision and the stage entry points' `precision`), OR-ed:
+ * the leaf-statistics dots (the reference's precision= argument, h3/htrc_flat.py:101, :126-130):
+ *   HTRC_PREC_FP32 ("fp32", the reference's PREC "ieee"): float32-accurate products (bf16 hi + lo splits of
+ *   the float32 centre and softmax weights); HTRC_PREC_TF32 ("tf32", PROD's setting, h3/htrc_flat.py:391): the
+ *   float32 operands enter as tf32, their low 13 mantissa bits cleared, the way the reference's tensor-core
+ *   dots (h3/htrc_flat_triton.py:57, :62-63) read them on sm_100;
+ * the division that forms the query and offset codes (x / s, h3/htrc_flat_triton.py:110-117) and the INT8
+ * slope factor 127 / am (:75-77) or the fp8 state values g / sg, vbar / sv (:65-72):
+ *   IEEE division without HTRC_PREC_TRITON_DIV (the reference's formula as written; its CPU-recorded
+ *   fixtures); with HTRC_PREC_TRITON_DIV, PTX div.full.f32, what the reference's Triton kernels compute for
+ *   `/` on the GPU (so the codes match its GPU operator's).  The key codes (a torch division,
+ *   h3/htrc_flat.py:213-219) are IEEE in both. */
+enum { HTRC_PREC_FP32 = 0, HTRC_PREC_TF32 = 1, HTRC_PREC_TRITON_DIV = 2 };
 
 /* Device status bits (htrc_flat_status). */
 enum { HTRC_STATUS_WAIT_TIMEOUT = 1, HTRC_STATUS_BAD_INDEX = 2, HTRC_STATUS_NONFINITE = 4 };
@@ -104,7 +111,7 @@ typedef struct HtrcFlatArgs {
                               (one absmax scale per 64-token block); HTRC_STORE_INT8 only */
   uint8_t* route_mask;     /* optional debug export (NULL = none): [ceil(nt / group), P] uint8 routing masks, the
                               rows htrc_route writes (1 = the leaf is evaluated exactly for that centre row) */
-  int32_t precision;       /* HTRC_PREC_FP32 (0) or HTRC_PREC_TF32: precision of the leaf-statistics dots */
+  int32_t precision;       /* HTRC_PREC_* flags: tf32 statistics operands, Triton (div.full.f32) code division */
 } HtrcFlatArgs;
 
 /* nb rounded up to a multiple of 16: the row pitch of the per-(tile, leaf) scalar arrays. */
