@@ -88,6 +88,25 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, i
   return __all_sync(0xffffffffu, ok);
 }
 
+// Before a CTA leaves: wait until the last phase of every slot of a ring of mbarriers completed, where step
+// i of `steps` arrived on slot i % slots (tcgen05.commit arrivals included).  An MMA-completion arrival that no
+// consumer waits for (the "slot free" signals of a ring's last steps) could otherwise land after the CTA has
+// exited, in shared memory that already belongs to the next CTA on the SM.  Call with every lane of a warp
+// (WARP) or from one thread.
+template <bool WARP>
+__device__ __forceinline__ void drain_ring(uint64_t* ring, int slots, int steps, int* status,
+                                           volatile int* abort_flag) {
+  for (int s = 0; s < slots && s < steps; ++s) {
+    const int phases = (steps - s + slots - 1) / slots;
+    const uint32_t parity = static_cast<uint32_t>(phases - 1) & 1u;
+    if (WARP) {
+      if (!mbar_wait_warp(ring + s, parity, status, abort_flag)) return;
+    } else if (!mbar_wait(ring + s, parity, status, abort_flag)) {
+      return;
+    }
+  }
+}
+
 // named barrier over a subset of warps
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");

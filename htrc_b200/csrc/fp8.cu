@@ -164,6 +164,7 @@ __global__ void __launch_bounds__(rmx::kThreads, 2)
       const uint32_t idesc = idesc_f16(128, 64, false, false);
       const uint32_t dq = smem_u32(smem + kOffDq);
       bool ok = mbar_wait(&bars->dq_full, 0, status, abort_flag);
+      int nmma = 0;                   // blocks whose MMAs were issued (and committed)
       for (int j = 0; ok && j < nblk; ++j) {
         const int s = j % kOpStages, b = j & 1;
         if (!mbar_wait(&bars->op_full[s], (j / kOpStages) & 1, status, abort_flag)) break;
@@ -178,7 +179,10 @@ __global__ void __launch_bounds__(rmx::kThreads, 2)
                      sw128_desc(dq + h * (64 * 128) + kk * 32, 16, 1024), idesc, (h | kk) != 0);
         mma_commit(&bars->acc_full[b]);
         mma_commit(&bars->op_empty[s]);
+        nmma = j + 1;
       }
+      // the operand-stage release signals of the last blocks have no waiter: let them land before the CTA leaves
+      drain_ring<false>(bars->op_empty, kOpStages, nmma, status, abort_flag);
     }
   } else if (warp < 6) {
     // reduce block j: sel over the tile's 64 rows for the leaf of this thread's TMEM lane
@@ -435,6 +439,7 @@ __global__ void __launch_bounds__(tfx::Cfg<FAR>::kThreads, 1)
     } else if (warp == 1) {
       // ---------------------------------------------------------------- PV issuer
       const uint32_t idesc = FAR ? idesc_f16(64, 128, false, true) : idesc_bf16(64, 128, false, true);
+      int npv = 0;                    // steps whose PV MMAs were issued (and committed)
       for (int p = 0; p < np; ++p) {
         const int b = p & 3, g = p & 1, ys = p % C::kYP;
         if (!mbar_wait_warp(&bars->p_full[b], (p >> 2) & 1, status, abort_flag)) break;
@@ -454,13 +459,17 @@ __global__ void __launch_bounds__(tfx::Cfg<FAR>::kThreads, 1)
           }
         }
         mma_commit_by(leader, &bars->pv_done[b]);
+        npv = p + 1;
       }
+      // every PV completion signal has landed before the CTA leaves (the last ones have no other waiter)
+      drain_ring<true>(bars->pv_done, 4, npv, status, abort_flag);
     } else if (warp == 2) {
       // ---------------------------------------------------------------- QK issuer
       // QK(p) into S/P buffer p % 4 once PV(p - 4) freed it and the pair's X slot landed
       const uint32_t idesc = FAR ? idesc_f16(64, 64, false, false) : idesc_bf16(64, 64, false, false);
       const uint32_t a0 = smem_u32(smem + C::kOffQ);
       bool ok = mbar_wait_warp(&bars->qd_full, 0, status, abort_flag);
+      int nqk = 0;                    // steps whose QK MMAs were issued (and committed)
       for (int p = 0; ok && p < np; ++p) {
         const int xs = p % C::kXP;
         if (p >= 4 && !mbar_wait_warp(&bars->pv_done[p & 3], ((p - 4) >> 2) & 1, status, abort_flag)) break;
@@ -482,7 +491,11 @@ __global__ void __launch_bounds__(tfx::Cfg<FAR>::kThreads, 1)
         }
         mma_commit_by(leader, &bars->s_full[b]);
         mma_commit_by(leader, &bars->x_empty[xs]);
+        nqk = p + 1;
       }
+      // every X-slot release (the QK commit and, in the far pass, the constants warp's reads) has landed before
+      // the CTA leaves
+      drain_ring<true>(bars->x_empty, C::kXP, nqk, status, abort_flag);
     } else if constexpr (FAR) {
       // ---------------------------------------------------------------- per-column constants (FAR)
       // (sg * log2 e, lz * log2 e or -inf if routed / past nb) and sv

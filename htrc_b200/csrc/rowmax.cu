@@ -97,6 +97,7 @@ __global__ void __launch_bounds__(192)
       const uint32_t idesc = idesc_i8(128, 64);
       const uint32_t dq = smem_u32(smem + kOffDq);
       bool ok = mbar_wait(&bars->dq_full, 0, status, abort_flag);
+      int nmma = 0;                   // blocks whose MMAs were issued (and committed)
       for (int j = 0; ok && j < nblk; ++j) {
         const int s = j % kStages, b = j & 1;
         if (!mbar_wait(&bars->full[s], (j / kStages) & 1, status, abort_flag)) break;
@@ -109,7 +110,10 @@ __global__ void __launch_bounds__(192)
         }
         mma_commit(&bars->acc_full[b]);
         mma_commit(&bars->empty[s]);
+        nmma = j + 1;
       }
+      // the stage release signals of the last blocks have no waiter: let them land before the CTA leaves
+      drain_ring<false>(bars->empty, kStages, nmma, status, abort_flag);
     }
   } else {
     const int quarter = warp & 3;

@@ -198,6 +198,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t leader = elect_one();
       if (nl > 0) {
         const uint32_t id_gv = idesc_bf16(128, 256, false, true);
+        int ngv = 0;                    // leaves whose G/VB MMAs were issued (and committed)
         static_assert(kColV == kColG + 128 && kStageBytes == 2 * kLeafBytes, "[G | VB] and [K | V] side by side");
         for (int j = 0; j < nl; ++j) {
           const int s = j % kStages, b = j & 1;
@@ -219,7 +220,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma_commit_by(leader, &bars->gv_full);
           mma_commit_by(leader, &bars->s_empty[b]);
           mma_commit_by(leader, &bars->kv_empty[s]);
+          ngv = j + 1;
         }
+        // the S-buffer and K/V-stage release signals of the last leaves have no waiter: let them land before
+        // the CTA leaves
+        drain_ring<true>(bars->s_empty, 2, ngv, status, abort_flag);
+        drain_ring<true>(bars->kv_empty, kStages, ngv, status, abort_flag);
       }
     }
     // warp 3: nothing (it completes warpgroup 0 for setmaxnreg)

@@ -217,6 +217,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lo0 = (smem_u32(smem + kOffY) >> 4) | ((kYBytes / 2) >> 4 << 16);   // + LBO (chunk stride)
     int ys = 0;
     uint32_t yph = 0;
+    int npv = 0;
     for (int np = 0; np < total; ++np) {
       if (!mbar_wait_warp(&bars->p_full[np & 3], (np >> 2) & 1, status, abort_flag)) break;
       if (!mbar_wait_warp(&bars->y_full[ys], yph, status, abort_flag)) break;
@@ -238,7 +239,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       mma_commit_by(leader, &bars->pv_done[b]);
       if (++ys == kYSlots) { ys = 0; yph ^= 1; }
+      npv = np + 1;
     }
+    // every PV completion signal has landed before the CTA leaves (the last ones have no other waiter)
+    drain_ring<true>(bars->pv_done, kSBufs, npv, status, abort_flag);
   } else if (warp == 11) {
     // ------------------------------------------------------------------ QK issuer + Y-ring producer
     // Both wait for PV(j): it frees S/P buffer j % 4 for QK(j + 4) and Y slot j % 4 for step j + 4.
@@ -267,6 +271,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
     };
     // QK of step nq into S/P buffer nq % 4, once its X slot landed
+    int nqk = 0;                    // QK steps issued (and committed)
     auto issue_qk = [&](int nq) -> bool {
       const int s = nq % kXSlots;
       if (!mbar_wait_warp(&bars->x_full[s], (nq / kXSlots) & 1, status, abort_flag)) return false;
@@ -286,6 +291,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       mma_commit_by(leader, &bars->s_full[b]);
       mma_commit_by(leader, &bars->x_empty[s]);
+      nqk = nq + 1;
       return true;
     };
     bool ok = mbar_wait_warp(&bars->qd_full, 0, status, abort_flag);
@@ -296,6 +302,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (j + kSBufs < total) ok = issue_qk(j + kSBufs);    // first: QK(j + 4) is on the step's critical chain
       produce_y(j + kYSlots);
     }
+    // every QK-operand slot's release (the QK commit and the constants warp's reads) has landed before the
+    // CTA leaves
+    drain_ring<true>(bars->x_empty, kXSlots, nqk, status, abort_flag);
   } else if (warp == 10) {
     // ------------------------------------------------------------------ per-column constants
     // far: (sg * log2 e, lz * log2 e or -inf if routed / past nb) per column; near: ks * scale * log2 e per
