@@ -78,10 +78,11 @@ def parse():
     ap.add_argument("--precision", default="tf32", choices=["tf32", "fp32"],
                     help="leaf-statistics dots: tf32 operands (PROD's setting, the reference's production path; the "
                          "default) or float32-accurate")
-    ap.add_argument("--division", default="triton", choices=["triton", "ieee"],
-                    help="division forming the query/offset/slope codes: the reference's GPU division (div.full.f32, "
-                         "the default: PROD as the reference computes it on the GPU) or IEEE (its formula as "
-                         "written); the oracle comparison always uses an IEEE run of head 0")
+    ap.add_argument("--division", default="ieee", choices=["ieee", "triton"],
+                    help="division forming the query/offset/slope codes in the timed layers: IEEE (the reference's "
+                         "formula as written, the library's default) or the reference's GPU division (div.full.f32); "
+                         "the comparison with the reference's own operator uses a Triton-division run of head 0, the "
+                         "comparison with the oracle an IEEE one")
     ap.add_argument("--streams", type=int, default=2, choices=[1, 2],
                     help="heads of a layer alternate over this many streams, each with its own workspace (2, the "
                          "default: one head's small kernels and the tile kernel's last partial wave overlap the "
@@ -515,6 +516,7 @@ def run_ours(a, wl, rank, world, local_rank):
     fp8 = store == _L.STORE_FP8
     prec = F.precision_code(a.precision, a.division)
     prec_ieee = F.precision_code(a.precision, "ieee")
+    prec_ref = F.precision_code(a.precision, "triton")
     wsb = F.workspace_bytes(n, m, E, 0, 0, 0, store=store)
     ws = F.new_workspace(wsb, dev)
     comp = torch.cuda.current_stream(dev)
@@ -635,9 +637,10 @@ def run_ours(a, wl, rank, world, local_rank):
         mask0 = torch.zeros((nt, F.leaf_pitch(nb)), dtype=torch.uint8, device=dev)
         out0 = torch.empty((n, 128), dtype=torch.float32, device=dev)
         lse0 = torch.empty((n,), dtype=torch.float32, device=dev)
+        # with the reference's GPU arithmetic (its Triton division), for the comparison with its operator
         F.forward_into(*dq[h0], None, None, exact_leaves=E, out=out0, lse=lse0, workspace=ws, store=store,
-                       route_mask=mask0, precision=prec)
-        # and with IEEE code division, the oracle's arithmetic (the same run when --division ieee)
+                       route_mask=mask0, precision=prec_ref)
+        # and with IEEE code division, the oracle's arithmetic
         mask0i, out0i, lse0i = torch.zeros_like(mask0), torch.empty_like(out0), torch.empty_like(lse0)
         F.forward_into(*dq[h0], None, None, exact_leaves=E, out=out0i, lse=lse0i, workspace=ws, store=store,
                        route_mask=mask0i, precision=prec_ieee)
@@ -682,7 +685,7 @@ def run_ours(a, wl, rank, world, local_rank):
     if rank == 0 and world == 1 and not a.no_ref_gpu and not fp8:
         ref_gpu = reference_gpu_leg(wl, dev, step_jobs[0][:H], dq, {"out": out0, "lse": lse0, "mask": mask0,
                                                                     "out_ieee": out0i, "lse_ieee": lse0i,
-                                                                    "division": a.division},
+                                                                    "division": "triton"},
                                     max(1, min(a.steps, a.ref_steps)), oracle_rows)
         if "ms_per_layer" in ref_gpu:
             ref_gpu["ours_over_ref"] = ms / ref_gpu["ms_per_layer"]

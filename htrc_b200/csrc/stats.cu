@@ -91,15 +91,14 @@ __device__ __forceinline__ uint2 half_away_codes2(float2 y) {
 }
 }  // namespace
 
-template <bool ISO, bool FP8>
+template <bool ISO, bool FP8, bool TDIV>
 __global__ void __launch_bounds__(kThreads, 1)
     leaf_stats_kernel(const uint16_t* __restrict__ mu_hi_g, const uint16_t* __restrict__ mu_lo_g, int64_t nt,
                       const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                       const __grid_constant__ CUtensorMap tm_g8, const __grid_constant__ CUtensorMap tm_vb,
                       float* __restrict__ sg_out, float* __restrict__ lz_out, int64_t pitch, int64_t t0, int64_t tc,
                       int nb, int leaves_per_cta, float scale, const float* __restrict__ kn2,
-                      float* __restrict__ cv_out, float* __restrict__ sv_out, int* status, uint32_t wmask,
-                      int tdiv) {
+                      float* __restrict__ cv_out, float* __restrict__ sv_out, int* status, uint32_t wmask) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Bars* bars = reinterpret_cast<Bars*>(smem + kOffBar);
@@ -198,7 +197,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t leader = elect_one();
       if (nl > 0) {
         const uint32_t id_gv = idesc_bf16(128, 256, false, true);
-        int ngv = 0;                    // leaves whose G/VB MMAs were issued (and committed)
         static_assert(kColV == kColG + 128 && kStageBytes == 2 * kLeafBytes, "[G | VB] and [K | V] side by side");
         for (int j = 0; j < nl; ++j) {
           const int s = j % kStages, b = j & 1;
@@ -218,14 +216,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
           mma_commit_by(leader, &bars->gv_full);
-          mma_commit_by(leader, &bars->s_empty[b]);
-          mma_commit_by(leader, &bars->kv_empty[s]);
-          ngv = j + 1;
+          // the S buffer and the K/V stage are released only for a later leaf that waits for them: every
+          // commit issued is observed before the CTA leaves (an arrival nobody waits for could land after it
+          // exited, in shared memory that already belongs to the next CTA on the SM)
+          if (j + 2 < nl) mma_commit_by(leader, &bars->s_empty[b]);
+          if (j + kStages < nl) mma_commit_by(leader, &bars->kv_empty[s]);
         }
-        // the S-buffer and K/V-stage release signals of the last leaves have no waiter: let them land before
-        // the CTA leaves
-        drain_ring<true>(bars->s_empty, 2, ngv, status, abort_flag);
-        drain_ring<true>(bars->kv_empty, kStages, ngv, status, abort_flag);
       }
     }
     // warp 3: nothing (it completes warpgroup 0 for setmaxnreg)
@@ -406,8 +402,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float2 ga = mul2(make_float2(__uint_as_float(gr[4 * i]), __uint_as_float(gr[4 * i + 1])), sc2);
           const float2 gb = mul2(make_float2(__uint_as_float(gr[4 * i + 2]), __uint_as_float(gr[4 * i + 3])), sc2);
           // g / sg: g * (1 / sg), or per value with div.full.f32 like the reference's Triton kernel (tdiv)
-          const float2 a = tdiv ? make_float2(div_full(ga.x, sgv), div_full(ga.y, sgv)) : mul2(ga, rg2);
-          const float2 b = tdiv ? make_float2(div_full(gb.x, sgv), div_full(gb.y, sgv)) : mul2(gb, rg2);
+          const float2 a = TDIV ? make_float2(div_full(ga.x, sgv), div_full(ga.y, sgv)) : mul2(ga, rg2);
+          const float2 b = TDIV ? make_float2(div_full(gb.x, sgv), div_full(gb.y, sgv)) : mul2(gb, rg2);
           gw[i] = f32x2_to_e4m3x2(a.x, a.y) | (f32x2_to_e4m3x2(b.x, b.y) << 16);
         }
 #pragma unroll
@@ -419,8 +415,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 8; ++i) {
             const float2 va = make_float2(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]));
             const float2 vb2 = make_float2(__uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
-            const float2 a = tdiv ? make_float2(div_full(va.x, svv), div_full(va.y, svv)) : mul2(va, rv2);
-            const float2 b = tdiv ? make_float2(div_full(vb2.x, svv), div_full(vb2.y, svv)) : mul2(vb2, rv2);
+            const float2 a = TDIV ? make_float2(div_full(va.x, svv), div_full(va.y, svv)) : mul2(va, rv2);
+            const float2 b = TDIV ? make_float2(div_full(vb2.x, svv), div_full(vb2.y, svv)) : mul2(vb2, rv2);
             vw[8 * c + i] = f32x2_to_e4m3x2(a.x, a.y) | (f32x2_to_e4m3x2(b.x, b.y) << 16);
           }
         }
@@ -499,7 +495,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       am = fmaxf(am, 1e-30f);
       const float sgv = __fmul_rn(am, 1.0f / 127.0f);
       // the factor 127 / am: IEEE, or div.full.f32 like the reference's Triton kernel (tdiv)
-      const float rr = tdiv ? div_full(127.0f, am) : __fdiv_rn(127.0f, am);
+      const float rr = TDIV ? div_full(127.0f, am) : __fdiv_rn(127.0f, am);
       if (valid && half == 0) sg_out[tloc * pitch + leaf] = sgv;
       // INT8 codes
       uint32_t gw[16];
@@ -552,7 +548,9 @@ int launch_leaf_stats(const LeafStatsMaps& maps, float* sg, float* lz, int64_t p
   cudaGetDevice(&dev);
   if (dev < 64 && !attr_done[dev]) {
     bool ok = true;
-    for (auto k : {leaf_stats_kernel<false, false>, leaf_stats_kernel<true, false>, leaf_stats_kernel<false, true>})
+    for (auto k : {leaf_stats_kernel<false, false, false>, leaf_stats_kernel<true, false, false>,
+                   leaf_stats_kernel<false, true, false>, leaf_stats_kernel<false, false, true>,
+                   leaf_stats_kernel<true, false, true>, leaf_stats_kernel<false, true, true>})
       ok = ok && cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) == cudaSuccess;
     if (!ok) return HTRC_ERR_CUDA;
     attr_done[dev] = true;
@@ -563,11 +561,15 @@ int launch_leaf_stats(const LeafStatsMaps& maps, float* sg, float* lz, int64_t p
   by = min(by, nb);
   const int lpc = (nb + by - 1) / by;
   by = (nb + lpc - 1) / lpc;
-  auto kernel = sv != nullptr ? leaf_stats_kernel<false, true>
-                               : (cv != nullptr ? leaf_stats_kernel<true, false> : leaf_stats_kernel<false, false>);
+  auto kernel = tdiv ? (sv != nullptr ? leaf_stats_kernel<false, true, true>
+                                      : (cv != nullptr ? leaf_stats_kernel<true, false, true>
+                                                       : leaf_stats_kernel<false, false, true>))
+                     : (sv != nullptr ? leaf_stats_kernel<false, true, false>
+                                      : (cv != nullptr ? leaf_stats_kernel<true, false, false>
+                                                       : leaf_stats_kernel<false, false, false>));
   kernel<<<dim3(bx, by), kThreads, kSmemBytes, st>>>(maps.mu_hi, maps.mu_lo, maps.nt, maps.k, maps.v, maps.g8, maps.vb,
                                                      sg, lz, pitch, t0, tc, nb, lpc, scale, kn2, cv, sv, status,
-                                                     tf32 ? kTf32Mask : 0xFFFFFFFFu, tdiv ? 1 : 0);
+                                                     tf32 ? kTf32Mask : 0xFFFFFFFFu);
   return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
 }
 
