@@ -195,6 +195,7 @@ __global__ void __launch_bounds__(rmx::kThreads, 2)
       const uint8_t* st = smem + kOffRaw + s * kRawStage;
       const float sgl = reinterpret_cast<const float*>(st + kRawBytes)[r];
       const float lzl = reinterpret_cast<const float*>(st + kRawBytes + 512)[r];
+      fence_proxy_async_smem();          // the TMA refill (async proxy) must not overtake these generic reads
       mbar_arrive(&bars->raw_empty[s]);
       if (!mbar_wait_warp(&bars->acc_full[b], (j >> 1) & 1, status, abort_flag)) break;
       __syncwarp();
@@ -514,6 +515,7 @@ __global__ void __launch_bounds__(tfx::Cfg<FAR>::kThreads, 1)
           cc[(cs_slot * 2 + x) * 64 + i] = make_float2(pf[64 + i] * kLog2e, masked ? -INFINITY : pf[i] * kLog2e);
           cs[(cs_slot * 2 + x) * 64 + i] = masked ? 0.f : pf[128 + i];
         }
+        fence_proxy_async_smem();             // generic reads of a slot that TMA refills
         mbar_arrive(&bars->x_empty[xs]);      // the raw parameters of this slot have been read
         mbar_arrive(&bars->cc_full[cs_slot]);
       }

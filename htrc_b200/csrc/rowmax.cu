@@ -138,6 +138,10 @@ __global__ void __launch_bounds__(192)
         const float sgl = reinterpret_cast<const float*>(st + kBlkBytes)[r];
         const float lzl = reinterpret_cast<const float*>(st + kBlkBytes + 512)[r];
         const float cvl = ISO ? reinterpret_cast<const float*>(st + kBlkBytes + 1024)[r] : 0.f;
+        // the stage is refilled by TMA (async proxy) once this arrival lands: without the proxy fence the
+        // refill can overtake these generic reads (seen as the next block's sg or lz in about one warp-block
+        // in 10^7)
+        fence_proxy_async_smem();
         mbar_arrive(&bars->empty[s]);
         float best = -INFINITY;
 #pragma unroll

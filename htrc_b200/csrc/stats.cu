@@ -335,6 +335,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tmem_st_wait();
       tc_fence_before();
+      if (ISO) fence_proxy_async_smem();   // the key norms read above sit in a K/V stage that TMA refills
       mbar_arrive(&bars->w_full[b]);
     }
   } else {

@@ -335,6 +335,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (ISO) reinterpret_cast<float*>(smem + kOffCC3)[s * 128 + colq] = 0.f;
         }
       }
+      fence_proxy_async_smem();            // generic reads of a slot that TMA refills
       mbar_arrive(&bars->x_empty[s]);      // the raw parameters of this slot have been read
       mbar_arrive(&bars->cc_full[s]);
     }

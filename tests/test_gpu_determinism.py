@@ -93,3 +93,38 @@ def test_heads_on_two_streams_equal_one_stream(dev, store):
             F.device_status(w)
         for (o, l), (ro, rl) in zip(got, ref):
             assert torch.equal(o, ro) and torch.equal(l, rl)
+
+
+@pytest.mark.parametrize("store,runs", [("int8", 10000), ("fp8", 5000)])
+def test_row_max_stage_repeats_bitwise(dev, store, runs):
+    """The row-max selection of one full-size head (129,024 tokens: 2,016 tiles x 16 blocks of 128 leaves),
+    launched thousands of times on the same state, writes bitwise the same sel every time.  The reducing
+    warps read each stage's sg / lz with ordinary shared-memory loads before releasing the stage to the TMA
+    refill; without a generic-to-async proxy fence between those reads and the release, the refill could land
+    first (about one warp-block in 10^7 read the next block's sg or lz), which this many blocks exposes."""
+    from htrc_b200 import _lib, synth
+    from htrc_b200 import flat as F
+    from htrc_b200._lib import check, ptr
+    q, k, v = (t.to(dev) for t in synth.head_inputs((32, 48, 84), 128, head=5, base_seed=31))
+    sc = _lib.STORES[store]
+    r = F.run_stages(q, k, v, exact_leaves=256, precision=F.precision_code("tf32", "triton"), store=sc)
+    del r["vb"]
+    torch.cuda.synchronize()
+    L = _lib.lib()
+    nt, nb = r["sel"].shape[0], r["nb"]
+    s = torch.cuda.current_stream().cuda_stream
+    stp = ptr(r["status"])
+    sel0 = r["sel"][:, :nb].clone()
+    buf = torch.zeros_like(r["sel"])
+    bad = torch.zeros((), dtype=torch.int64, device=dev)
+    for _ in range(runs):
+        if sc == _lib.STORE_FP8:
+            check(L.htrc_rowmax_select_fp8(ptr(r["dqh"]), 0, nt, 1, ptr(r["g8"]), ptr(r["sg"]), ptr(r["lz"]), nb,
+                                           128, ptr(buf), stp, s), "htrc_rowmax_select_fp8")
+        else:
+            check(L.htrc_rowmax_select(ptr(r["dq8"]), ptr(r["sdq"]), None, 0, nt, 1, ptr(r["g8"]), ptr(r["sg"]),
+                                       ptr(r["lz"]), None, nb, 128, ptr(buf), stp, s), "htrc_rowmax_select")
+        bad += (buf[:, :nb] != sel0).sum()
+    torch.cuda.synchronize()
+    assert int(r["status"].item()) == 0
+    assert int(bad) == 0, f"{int(bad)} sel entries differed over {runs} runs"
