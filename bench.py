@@ -769,9 +769,10 @@ def run_ours(a, wl, rank, world, local_rank):
     if rank == 0 and world == 1 and not a.no_modes:
         from htrc_b200 import runner as R
         modes = {}
-        for mode in list(R.MODES) + ["fast+iso", "fast+fp8"]:
-            extra = {"fast+iso": dict(backend="cuda", curvature="iso"), "fast+fp8": dict(store="fp8")}.get(mode, {})
-            r = R.FlatRunner(n, m, mode=mode.split("+")[0], device=dev, **extra)
+        for mode in list(R.MODES) + ["fast+iso", "fast+fp8", "fast+leaf32", "fast+leaf16"]:
+            extra = {"fast+iso": dict(backend="cuda", curvature="iso"), "fast+fp8": dict(store="fp8"),
+                     "fast+leaf32": dict(leaf=32), "fast+leaf16": dict(leaf=16)}.get(mode, {})
+            r = R.FlatRunner(n, m, mode=mode.split("+")[0], device=dev, **{"leaf": 64, **extra})
             if r.graph is None:
                 modes[mode] = f"graph capture failed: {r.graph_error}"
                 continue
@@ -811,7 +812,9 @@ def run_ours(a, wl, rank, world, local_rank):
                  "note": "head 0 of the workload through FlatRunner (CUDA graph) per mode of "
                          "h3/htrc_flat_runner.py:48-53: fast E=256, balanced E=512, accurate E=1024 + k-means, "
                          "max E=1024 + k-means + 32-row tiles; fast+iso: fast with the isotropic curvature term; "
-                         "fast+fp8: fast with the e4m3 far-field state (store='fp8')"}
+                         "fast+fp8: fast with the e4m3 far-field state (store='fp8'); fast+leaf32 / fast+leaf16: "
+                         "fast with leaves of 32 / 16 keys (E=256 leaves, so 8,192 / 4,096 exact keys per tile; leaf "
+                         "16 is the default of the reference's runner); the others leaf 64"}
 
     # ---- roofline of the dominant kernel (tile attention) from the live events
     peaks, peak_src = measured_peaks()

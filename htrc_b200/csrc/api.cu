@@ -15,7 +15,9 @@ namespace {
 
 constexpr int kDim = 128;
 constexpr int kTile = 64;        // rows of a tile as the kernels hold it (a 32-row tile is padded to 64)
-constexpr int kLeaf = 64;
+constexpr int kLeaf = 64;          // the leaf every configuration supports
+// other leaves (32, 16 keys) run with the INT8 state and the linear far field
+bool leaf_ok(int64_t leaf) { return leaf == 64 || leaf == 32 || leaf == 16; }
 constexpr int64_t kMaxLeaves = 8192;
 constexpr int64_t kMaxRouted = 1024;
 
@@ -136,6 +138,7 @@ size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 // rows) are per group of `group` tiles; a chunk holds gcm groups = gcm * group tiles.
 struct Layout {
   int64_t n = 0, m = 0, nt = 0, nb = 0, pitch = 0, kx = 0, group = 1, ng = 0, gcm = 0, tcm = 0, trows = 64;
+  int64_t leaf = 64;
   bool kmeans = false;
   size_t status = 0, k8 = 0, ks = 0, mu = 0, mu_hi = 0, mu_lo = 0, q8 = 0, sq = 0, dq8 = 0, sdq = 0, tail = 0;
   size_t g8 = 0, vb = 0, sg = 0, lz = 0, sel = 0, excl = 0, idx = 0, perm = 0, km = 0, total = 0;
@@ -149,7 +152,7 @@ constexpr int kMaxGroup = 65536;
 
 int validate(const HtrcFlatArgs* a, bool need_ptrs) {
   if (a == nullptr) return HTRC_ERR_ARG;
-  if (a->dim != kDim || (a->tile != kTile && a->tile != kTile / 2) || a->leaf != kLeaf) return HTRC_ERR_UNSUPPORTED;
+  if (a->dim != kDim || (a->tile != kTile && a->tile != kTile / 2) || !leaf_ok(a->leaf)) return HTRC_ERR_UNSUPPORTED;
   if (a->n_queries < 1 || a->n_keys < a->leaf || a->n_keys % a->leaf) return HTRC_ERR_ARG;
   if (a->q_dtype != HTRC_DTYPE_F32 && a->q_dtype != HTRC_DTYPE_BF16) return HTRC_ERR_ARG;
   if (a->exact_leaves < 0 || a->sink_leaves < 0 || a->n_tail < 0) return HTRC_ERR_ARG;
@@ -160,6 +163,9 @@ int validate(const HtrcFlatArgs* a, bool need_ptrs) {
   if (a->store == HTRC_STORE_FP8 && a->curvature != HTRC_CURV_LIN) return HTRC_ERR_UNSUPPORTED;
   if (a->qk_scale_block != 0 && a->qk_scale_block != 64) return HTRC_ERR_ARG;
   if (a->qk_scale_block != 0 && a->store != HTRC_STORE_INT8) return HTRC_ERR_UNSUPPORTED;
+  if (a->leaf != kLeaf &&
+      (a->store != HTRC_STORE_INT8 || a->curvature != HTRC_CURV_LIN || a->qk_scale_block != 0))
+    return HTRC_ERR_UNSUPPORTED;
   if ((a->precision & ~(HTRC_PREC_TF32 | HTRC_PREC_TRITON_DIV)) != 0) return HTRC_ERR_ARG;
   if (a->n_queries > (int64_t(1) << 31) - 1) return HTRC_ERR_UNSUPPORTED;
   const int64_t nb = a->n_keys / a->leaf;
@@ -180,7 +186,8 @@ Layout layout_of(const HtrcFlatArgs* a) {
   L.m = a->n_keys;
   L.trows = a->tile;
   L.nt = (L.n + L.trows - 1) / L.trows;
-  L.nb = L.m / kLeaf;
+  L.leaf = a->leaf;
+  L.nb = L.m / L.leaf;
   L.pitch = pitch_of(L.nb);
   const int64_t sink = std::min<int64_t>(a->sink_leaves, L.nb);
   L.kx = std::min<int64_t>(static_cast<int64_t>(a->exact_leaves) + sink, L.nb);
@@ -289,12 +296,12 @@ int rowmax_maps(RowmaxMaps* mp, const int8_t* dq8, int64_t rows, const int8_t* g
 
 int tile_maps(TileMaps* mp, const int8_t* q8, const int8_t* dq8, int64_t rows, const int8_t* g8, const uint16_t* vb,
               const float* lz, const float* sg, const float* cv, const uint8_t* excl, int64_t tc, int64_t nb,
-              int64_t pitch, const int8_t* k8, const uint16_t* v, int64_t m) {
+              int64_t pitch, const int8_t* k8, const uint16_t* v, int64_t m, int leaf) {
   bool ok = map_rows(&mp->q8, q8, rows, false, 64) && map_rows(&mp->dq8, dq8, rows, false, 64) &&
             map_state(&mp->g8, g8, tc, nb, false, 64, 1) && map_state_halves(&mp->vb, vb, tc, nb, 64) &&
             map_scalars(&mp->lz, lz, tc, nb, pitch, true, 64) && map_scalars(&mp->sg, sg, tc, nb, pitch, true, 64) &&
-            map_scalars(&mp->excl, excl, tc, nb, pitch, false, 64) && map_rows(&mp->k8, k8, m, false, 64) &&
-            map_rows_halves(&mp->v, v, m, 64) && map_scalars(&mp->cv, cv ? cv : sg, tc, nb, pitch, true, 64);
+            map_scalars(&mp->excl, excl, tc, nb, pitch, false, 64) && map_rows(&mp->k8, k8, m, false, leaf) &&
+            map_rows_halves(&mp->v, v, m, leaf) && map_scalars(&mp->cv, cv ? cv : sg, tc, nb, pitch, true, 64);
   return ok ? HTRC_OK : HTRC_ERR_CUDA;
 }
 
@@ -393,7 +400,8 @@ int htrc_flat_forward(const HtrcFlatArgs* a, htrc_stream_t stream) {
     if (far) {
       LeafStatsMaps smp;
       if ((rc = stats_maps(&smp, mu_hi, mu_lo, L.ng, a->k, a->v, L.m, g8, vb, gc, L.nb, L.fp8)) != HTRC_OK) return rc;
-      if ((rc = launch_leaf_stats(smp, sg, lz, L.pitch, g0, gc, nb, scale, kn2, cv, sv, status, device_info().sms,
+      if ((rc = launch_leaf_stats(smp, sg, lz, L.pitch, g0, gc, nb, static_cast<int>(L.leaf), scale, kn2, cv, sv,
+                                  status, device_info().sms,
                                   (a->precision & HTRC_PREC_TF32) != 0, (a->precision & HTRC_PREC_TRITON_DIV) != 0,
                                   st)) != HTRC_OK)
         return rc;
@@ -435,10 +443,11 @@ int htrc_flat_forward(const HtrcFlatArgs* a, htrc_stream_t stream) {
       continue;
     }
     TileMaps tmp;
-    if ((rc = tile_maps(&tmp, q8, dq8, L.nt * 64, g8, vb, lz, sg, cv, excl, gc, L.nb, L.pitch, k8, a->v, L.m)) !=
-        HTRC_OK)
+    if ((rc = tile_maps(&tmp, q8, dq8, L.nt * 64, g8, vb, lz, sg, cv, excl, gc, L.nb, L.pitch, k8, a->v, L.m,
+                        static_cast<int>(L.leaf))) != HTRC_OK)
       return rc;
-    if ((rc = launch_tile_attention(tmp, sq, sdq, ks, idx, kx, nb, L.n, trows, t0, tc, group, scale, tail, perm,
+    if ((rc = launch_tile_attention(tmp, sq, sdq, ks, idx, kx, nb, static_cast<int>(L.leaf), L.n, trows, t0, tc,
+                                    group, scale, tail, perm,
                                     dd, a->out, a->lse, status, st)) != HTRC_OK)
       return rc;
     mark(5 + 4 * chunk);
@@ -539,7 +548,7 @@ int htrc_leaf_stats(const uint16_t* mu_hi, const uint16_t* mu_lo, int64_t nt, in
   if (!mu_hi || !mu_lo || !k || !v || !g8 || !sg || !lz || !vb) return HTRC_ERR_ARG;
   if ((precision & ~(HTRC_PREC_TF32 | HTRC_PREC_TRITON_DIV)) != 0) return HTRC_ERR_ARG;
   if ((kn2 == nullptr) != (cv == nullptr)) return HTRC_ERR_ARG;
-  if (dim != kDim || leaf != kLeaf) return HTRC_ERR_UNSUPPORTED;
+  if (dim != kDim || !leaf_ok(leaf) || (leaf != kLeaf && cv != nullptr)) return HTRC_ERR_UNSUPPORTED;
   if (nt < 1 || t0 < 0 || tc < 1 || t0 + tc > nt || n_keys < leaf || n_keys % leaf) return HTRC_ERR_ARG;
   const int64_t nb = n_keys / leaf;
   if (nb > kMaxLeaves) return HTRC_ERR_UNSUPPORTED;
@@ -547,7 +556,8 @@ int htrc_leaf_stats(const uint16_t* mu_hi, const uint16_t* mu_lo, int64_t nt, in
   if (rc != HTRC_OK) return rc;
   LeafStatsMaps mp;
   if ((rc = stats_maps(&mp, mu_hi, mu_lo, nt, k, v, n_keys, g8, vb, tc, nb, false)) != HTRC_OK) return rc;
-  return launch_leaf_stats(mp, sg, lz, pitch_of(nb), t0, tc, static_cast<int>(nb), scale_of(scale), kn2, cv, nullptr,
+  return launch_leaf_stats(mp, sg, lz, pitch_of(nb), t0, tc, static_cast<int>(nb), leaf, scale_of(scale), kn2, cv,
+                           nullptr,
                            status, device_info().sms, (precision & HTRC_PREC_TF32) != 0,
                            (precision & HTRC_PREC_TRITON_DIV) != 0, reinterpret_cast<cudaStream_t>(stream));
 }
@@ -582,7 +592,8 @@ int htrc_leaf_stats_fp8(const uint16_t* mu_hi, const uint16_t* mu_lo, int64_t nt
   if (rc != HTRC_OK) return rc;
   LeafStatsMaps mp;
   if ((rc = stats_maps(&mp, mu_hi, mu_lo, nt, k, v, n_keys, g8, vb8, tc, nb, true)) != HTRC_OK) return rc;
-  return launch_leaf_stats(mp, sg, lz, pitch_of(nb), t0, tc, static_cast<int>(nb), scale_of(scale), nullptr, nullptr,
+  return launch_leaf_stats(mp, sg, lz, pitch_of(nb), t0, tc, static_cast<int>(nb), kLeaf, scale_of(scale), nullptr,
+                           nullptr,
                            sv, status, device_info().sms, (precision & HTRC_PREC_TF32) != 0,
                            (precision & HTRC_PREC_TRITON_DIV) != 0, reinterpret_cast<cudaStream_t>(stream));
 }
@@ -678,7 +689,8 @@ int htrc_tile_attention(const int8_t* q8, const float* sq, const int8_t* dq8, co
   if ((dd == nullptr) != (cv == nullptr)) return HTRC_ERR_ARG;
   const int64_t g = group > 1 ? group : 1;
   if (g > kMaxGroup || t0 % g) return HTRC_ERR_ARG;
-  if (dim != kDim || leaf != kLeaf || (tile != kTile && tile != kTile / 2)) return HTRC_ERR_UNSUPPORTED;
+  if (dim != kDim || !leaf_ok(leaf) || (leaf != kLeaf && cv != nullptr) || (tile != kTile && tile != kTile / 2))
+    return HTRC_ERR_UNSUPPORTED;
   if (nb < 1 || n_keys != nb * leaf || kx < 0 || kx > nb) return HTRC_ERR_ARG;
   if (kx > kMaxRouted || nb > kMaxLeaves) return HTRC_ERR_UNSUPPORTED;
   if (kx < nb && (!g8 || !sg || !lz || !vb || !excl)) return HTRC_ERR_ARG;
@@ -696,10 +708,11 @@ int htrc_tile_attention(const int8_t* q8, const float* sq, const int8_t* dq8, co
   TileMaps mp;
   if ((rc = tile_maps(&mp, q8, dq8, nt * 64, static_cast<const int8_t*>(g8p), static_cast<const uint16_t*>(vbp),
                       static_cast<const float*>(lzp), static_cast<const float*>(sgp), cv,
-                      static_cast<const uint8_t*>(exp_), (tc + g - 1) / g, nb, pitch_of(nb), k8, v, n_keys)) != HTRC_OK)
+                      static_cast<const uint8_t*>(exp_), (tc + g - 1) / g, nb, pitch_of(nb), k8, v, n_keys, leaf)) !=
+      HTRC_OK)
     return rc;
-  return launch_tile_attention(mp, sq, sdq, ks, idx, kx, static_cast<int>(nb), n_queries, tile, t0, tc, static_cast<int>(g),
-                               scale_of(scale), tail_part, perm, cv ? dd : nullptr, out, lse, status,
+  return launch_tile_attention(mp, sq, sdq, ks, idx, kx, static_cast<int>(nb), leaf, n_queries, tile, t0, tc,
+                               static_cast<int>(g), scale_of(scale), tail_part, perm, cv ? dd : nullptr, out, lse, status,
                                reinterpret_cast<cudaStream_t>(stream));
 }
 

@@ -67,15 +67,17 @@ void launch_dequant_rows(const uint8_t* x8, int64_t stride_x, const float* scale
                          uint16_t* out, cudaStream_t st);
 void launch_tail_partial(const void* q, int dtype, int64_t n, const float* tk, const float* tv, int n_tail, float scale,
                          float* part, cudaStream_t st);
+// leaf: 64, or 32 / 16 for the INT8 state with the linear far field
 int launch_leaf_stats(const LeafStatsMaps& maps, float* sg, float* lz, int64_t pitch, int64_t t0, int64_t tc, int nb,
-                      float scale, const float* kn2, float* cv, float* sv, int* status, int num_sms, bool tf32,
-                      bool tdiv, cudaStream_t st);
+                      int leaf, float scale, const float* kn2, float* cv, float* sv, int* status, int num_sms,
+                      bool tf32, bool tdiv, cudaStream_t st);
 int launch_rowmax(const RowmaxMaps& maps, const float* sdq, const float* dd, float* sel, int64_t pitch, int64_t t0,
                   int64_t tc, int nb, int group, int* status, cudaStream_t st);
 int launch_route(const float* sel, int64_t pitch, int64_t tc, int group, int nb, int kx, int sink, int32_t* idx,
                  uint8_t* excl, cudaStream_t st);
+// the maps' key-leaf boxes (k8, v) are `leaf` rows high
 int launch_tile_attention(const TileMaps& maps, const float* sq, const float* sdq, const float* ks, const int32_t* idx,
-                          int kx, int nb, int64_t n, int tile_rows, int64_t t0, int64_t tc, int group, float scale,
+                          int kx, int nb, int leaf, int64_t n, int tile_rows, int64_t t0, int64_t tc, int group, float scale,
                           const float* tail_part, const int32_t* perm, const float* dd, float* out, float* lse,
                           int* status, cudaStream_t st);
 int launch_rowmax_fp8(const RowmaxFp8Maps& maps, float* sel, int64_t pitch, int64_t t0, int64_t tc, int nb, int group,

@@ -19,6 +19,9 @@
 // backend's curvature="iso"): c = 0.5 / D * max(tr, 0), tr = scale^2 (sum_s w_s |k_s|^2 - |sum_s w_s k_s|^2);
 // the softmax warps form sum_s w_s |k_s|^2 from the key norms staged with K/V, the epilogue |G|^2 from
 // its G columns (the two halves exchange partial sums with their abs-maxima).
+// LEAF (64, 32 or 16 keys; INT8 state, linear far field) sets the leaf: a K/V stage still holds 64 keys, i.e.
+// 64 / LEAF leaves, and each leaf takes its own S (N = LEAF), softmax, [G | VB] (K = LEAF) and epilogue
+// (h3/htrc_flat.py:99-103: the reference takes any leaf that divides the key count, default 16).
 // FP8 stores the state as e4m3 codes with per-(centre, leaf) row scales instead (h3/htrc_flat_triton.py:65-72,
 // store="fp8"): sg = max(amax|g| * (1/448), 1e-30), g codes = e4m3(g / sg) rounded to nearest even and
 // saturated at 448, and the same for vbar with sv.
@@ -91,7 +94,7 @@ __device__ __forceinline__ uint2 half_away_codes2(float2 y) {
 }
 }  // namespace
 
-template <bool ISO, bool FP8, bool TDIV>
+template <bool ISO, bool FP8, bool TDIV, int LEAF>
 __global__ void __launch_bounds__(kThreads, 1)
     leaf_stats_kernel(const uint16_t* __restrict__ mu_hi_g, const uint16_t* __restrict__ mu_lo_g, int64_t nt,
                       const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
@@ -108,6 +111,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int l_begin = blockIdx.y * leaves_per_cta;
   const int l_end = min(nb, l_begin + leaves_per_cta);
   const int nl = max(0, l_end - l_begin);
+  static_assert(LEAF == 64 || LEAF == 32 || LEAF == 16, "leaf of 16, 32 or 64 keys");
+  static_assert(LEAF == 64 || (!ISO && !FP8), "the iso and fp8 variants take leaf 64");
+  constexpr int kPerStage = 64 / LEAF;            // leaves per K/V stage
+  const int nst = (nl + kPerStage - 1) / kPerStage;   // K/V stages of this CTA
   volatile int* abort_flag = &bars->abort_flag;
 
   if (threadIdx.x == 0) {
@@ -146,12 +153,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_prefetch_desc(&tm_k);
           tma_prefetch_desc(&tm_v);
         }
-        for (int j = 0; j < nl; ++j) {
-          const int s = j % kStages;
-          if (j >= kStages && !mbar_wait_warp(&bars->kv_empty[s], ((j / kStages) - 1) & 1, status, abort_flag)) break;
+        // one stage = the next 64 keys = kPerStage leaves
+        for (int gi = 0; gi < nst; ++gi) {
+          const int s = gi % kStages;
+          if (gi >= kStages && !mbar_wait_warp(&bars->kv_empty[s], ((gi / kStages) - 1) & 1, status, abort_flag))
+            break;
           if (leader) {
             uint8_t* st = smem + kOffStage + s * kStageBytes;
-            const int row = (l_begin + j) * 64;
+            const int row = l_begin * LEAF + gi * 64;
             mbar_arrive_expect_tx(&bars->kv_full[s], kStageBytes + (ISO ? 256 : 0));
             tma_load_3d(st, &tm_k, &bars->kv_full[s], 0, row, 0, pol_keep);        // both 64-column halves
             tma_load_3d(st + kLeafBytes, &tm_v, &bars->kv_full[s], 0, row, 0, pol_keep);
@@ -165,14 +174,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       // S(j) = mu . K_j^T into S buffer j % 2 once the K/V stage landed and the softmax released it
       const uint32_t leader = elect_one();
       if (nl > 0) {
-        const uint32_t id_s = idesc_bf16(128, 64, false, false);
+        const uint32_t id_s = idesc_bf16(128, LEAF, false, false);
         bool ok = mbar_wait_warp(&bars->mu_full, 0, status, abort_flag);
         for (int j = 0; ok && j < nl; ++j) {
-          const int s = j % kStages, b = j & 1;
-          if (!mbar_wait_warp(&bars->kv_full[s], (j / kStages) & 1, status, abort_flag)) break;
+          const int gi = j / kPerStage, s = gi % kStages, b = j & 1;
+          if (!mbar_wait_warp(&bars->kv_full[s], (gi / kStages) & 1, status, abort_flag)) break;
           if (j >= 2 && !mbar_wait_warp(&bars->s_empty[b], ((j >> 1) - 1) & 1, status, abort_flag)) break;
           tc_fence_after();
-          const uint32_t kst = smem_u32(smem + kOffStage + s * kStageBytes);
+          // this leaf's keys are rows LEAF * (j % kPerStage) .. of the stage's 64 (whole 8-row swizzle atoms)
+          const uint32_t kst = smem_u32(smem + kOffStage + s * kStageBytes) + (j % kPerStage) * LEAF * 128;
           const uint32_t d = tmem + kColS + 64 * b;
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
@@ -199,18 +209,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t id_gv = idesc_bf16(128, 256, false, true);
         static_assert(kColV == kColG + 128 && kStageBytes == 2 * kLeafBytes, "[G | VB] and [K | V] side by side");
         for (int j = 0; j < nl; ++j) {
-          const int s = j % kStages, b = j & 1;
+          const int gi = j / kPerStage, s = gi % kStages, b = j & 1;
           if (!mbar_wait_warp(&bars->w_full[b], (j >> 1) & 1, status, abort_flag)) break;
           if (j >= 1 && !mbar_wait_warp(&bars->gv_empty, (j - 1) & 1, status, abort_flag)) break;
           tc_fence_after();
-          const uint32_t kst = smem_u32(smem + kOffStage + s * kStageBytes);
+          // this leaf's keys: the 16-key K steps (j % kPerStage) * LEAF / 16 .. of the stage
+          const uint32_t kst = smem_u32(smem + kOffStage + s * kStageBytes) + (j % kPerStage) * LEAF * 128;
           const uint32_t wt = tmem + kColS + 64 * b;      // W_hi at wt, W_lo at wt + 32 (keys in pairs)
           // [G | VB] = (W_hi + W_lo) . [K | V]: the stage's K and V are four 64-column chunks 8 KB apart, one
           // N = 256 operand, and TMEM holds G and VB side by side (kColV = kColG + 128)
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
+            for (int kk = 0; kk < LEAF / 16; ++kk) {
               const uint64_t bdesc = sw128_desc(kst + kk * 2048, kLeafBytes / 2, 1024);
               mma_bf16_ts_by(leader, tmem + kColG, wt + 32 * h + 8 * kk, bdesc, id_gv, (h | kk) != 0);
             }
@@ -220,7 +231,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           // commit issued is observed before the CTA leaves (an arrival nobody waits for could land after it
           // exited, in shared memory that already belongs to the next CTA on the SM)
           if (j + 2 < nl) mma_commit_by(leader, &bars->s_empty[b]);
-          if (j + kStages < nl) mma_commit_by(leader, &bars->kv_empty[s]);
+          if ((j % kPerStage == kPerStage - 1 || j == nl - 1) && gi + kStages < nst)
+            mma_commit_by(leader, &bars->kv_empty[s]);
         }
       }
     }
@@ -263,22 +275,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(&bars->s_full[b], (j >> 1) & 1, status, abort_flag)) break;
       __syncwarp();
       tc_fence_after();
-      float a[64];
-      {
-        uint32_t r[32];
-        tmem_ld32(tmem + lane_base + kColS + 64 * b, r);
+      float a[LEAF];
+      if constexpr (LEAF == 16) {
+        uint32_t r[16];
+        tmem_ld16(tmem + lane_base + kColS + 64 * b, r);
         tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) a[i] = __uint_as_float(r[i]);
-        tmem_ld32(tmem + lane_base + kColS + 64 * b + 32, r);
-        tmem_ld_wait();
+        for (int i = 0; i < 16; ++i) a[i] = __uint_as_float(r[i]);
+      } else {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) a[32 + i] = __uint_as_float(r[i]);
+        for (int c = 0; c < LEAF / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tmem + lane_base + kColS + 64 * b + 32 * c, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) a[32 * c + i] = __uint_as_float(r[i]);
+        }
       }
       float mxa[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
       const float2 sc2 = make_float2(scale, scale);
 #pragma unroll
-      for (int i = 0; i < 64; i += 2) {
+      for (int i = 0; i < LEAF; i += 2) {
         const float2 v = mul2(make_float2(a[i], a[i + 1]), sc2);
         a[i] = v.x;
         a[i + 1] = v.y;
@@ -288,7 +305,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       float2 zs[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
       const float2 m2 = make_float2(m, m), l2e2 = make_float2(kLog2e, kLog2e);
 #pragma unroll
-      for (int i = 0; i < 64; i += 2) {
+      for (int i = 0; i < LEAF; i += 2) {
         const float2 e = mul2(sub2(make_float2(a[i], a[i + 1]), m2), l2e2);
         a[i] = ex2(e.x);
         a[i + 1] = ex2(e.y);
@@ -298,7 +315,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float z = zz.x + zz.y;
       const float lz = m + logf(z);
       float kw = 0.f;                           // ISO: sum_s e_s |k_s|^2 (divided by z below)
-      if (ISO) {
+      if constexpr (ISO && LEAF == 64) {
         const float4* kn = reinterpret_cast<const float4*>(smem + kOffKn + (j % kStages) * 256);
         float2 acc2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
@@ -320,9 +337,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ISO) reinterpret_cast<float*>(smem + kOffAw)[(j & 3) * 128 + row] = kw * rz;
       // W = w_hi + w_lo as bf16 pairs over this row's S columns (already read): hi in 32 columns, lo in 32
       {
-        uint32_t hi[32], lo[32];
+        uint32_t hi[LEAF / 2], lo[LEAF / 2];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
+        for (int i = 0; i < LEAF / 2; ++i) {
           float2 w = mul2(make_float2(a[2 * i], a[2 * i + 1]), make_float2(rz, rz));
           w.x = __uint_as_float(__float_as_uint(w.x) & wmask);     // precision "tf32": the operand value
           w.y = __uint_as_float(__float_as_uint(w.y) & wmask);
@@ -330,8 +347,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float2 lw = sub2(w, make_float2(__uint_as_float(hi[i] << 16), __uint_as_float(hi[i] & 0xFFFF0000u)));
           lo[i] = pack_bf16x2(lw.x, lw.y);
         }
-        tmem_st32(tmem + lane_base + kColS + 64 * b, hi);
-        tmem_st32(tmem + lane_base + kColS + 64 * b + 32, lo);
+        tmem_st_cols<LEAF / 2>(tmem + lane_base + kColS + 64 * b, hi);
+        tmem_st_cols<LEAF / 2>(tmem + lane_base + kColS + 64 * b + 32, lo);
       }
       tmem_st_wait();
       tc_fence_before();
@@ -542,32 +559,44 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 int launch_leaf_stats(const LeafStatsMaps& maps, float* sg, float* lz, int64_t pitch, int64_t t0, int64_t tc, int nb,
-                      float scale, const float* kn2, float* cv, float* sv, int* status, int num_sms, bool tf32,
-                      bool tdiv, cudaStream_t st) {
+                      int leaf, float scale, const float* kn2, float* cv, float* sv, int* status, int num_sms,
+                      bool tf32, bool tdiv, cudaStream_t st) {
   static bool attr_done[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr_done[dev]) {
     bool ok = true;
-    for (auto k : {leaf_stats_kernel<false, false, false>, leaf_stats_kernel<true, false, false>,
-                   leaf_stats_kernel<false, true, false>, leaf_stats_kernel<false, false, true>,
-                   leaf_stats_kernel<true, false, true>, leaf_stats_kernel<false, true, true>})
+    for (auto k : {leaf_stats_kernel<false, false, false, 64>, leaf_stats_kernel<true, false, false, 64>,
+                   leaf_stats_kernel<false, true, false, 64>, leaf_stats_kernel<false, false, true, 64>,
+                   leaf_stats_kernel<true, false, true, 64>, leaf_stats_kernel<false, true, true, 64>,
+                   leaf_stats_kernel<false, false, false, 32>, leaf_stats_kernel<false, false, true, 32>,
+                   leaf_stats_kernel<false, false, false, 16>, leaf_stats_kernel<false, false, true, 16>})
       ok = ok && cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) == cudaSuccess;
     if (!ok) return HTRC_ERR_CUDA;
     attr_done[dev] = true;
   }
   if (sv != nullptr && cv != nullptr) return HTRC_ERR_UNSUPPORTED;
+  if (leaf != 64 && leaf != 32 && leaf != 16) return HTRC_ERR_UNSUPPORTED;
+  if (leaf != 64 && (sv != nullptr || cv != nullptr)) return HTRC_ERR_UNSUPPORTED;
   const int bx = static_cast<int>((tc + 127) / 128);
   int by = max(1, num_sms / bx);                    // one wave: bx * by <= SMs
   by = min(by, nb);
-  const int lpc = (nb + by - 1) / by;
+  const int per_stage = 64 / leaf;                  // a CTA's leaf range covers whole K/V stages
+  int lpc = (nb + by - 1) / by;
+  lpc = (lpc + per_stage - 1) / per_stage * per_stage;
   by = (nb + lpc - 1) / lpc;
-  auto kernel = tdiv ? (sv != nullptr ? leaf_stats_kernel<false, true, true>
-                                      : (cv != nullptr ? leaf_stats_kernel<true, false, true>
-                                                       : leaf_stats_kernel<false, false, true>))
-                     : (sv != nullptr ? leaf_stats_kernel<false, true, false>
-                                      : (cv != nullptr ? leaf_stats_kernel<true, false, false>
-                                                       : leaf_stats_kernel<false, false, false>));
+  decltype(&leaf_stats_kernel<false, false, false, 64>) kernel;
+  if (leaf == 32)
+    kernel = tdiv ? leaf_stats_kernel<false, false, true, 32> : leaf_stats_kernel<false, false, false, 32>;
+  else if (leaf == 16)
+    kernel = tdiv ? leaf_stats_kernel<false, false, true, 16> : leaf_stats_kernel<false, false, false, 16>;
+  else
+    kernel = tdiv ? (sv != nullptr ? leaf_stats_kernel<false, true, true, 64>
+                                   : (cv != nullptr ? leaf_stats_kernel<true, false, true, 64>
+                                                    : leaf_stats_kernel<false, false, true, 64>))
+                  : (sv != nullptr ? leaf_stats_kernel<false, true, false, 64>
+                                   : (cv != nullptr ? leaf_stats_kernel<true, false, false, 64>
+                                                    : leaf_stats_kernel<false, false, false, 64>));
   kernel<<<dim3(bx, by), kThreads, kSmemBytes, st>>>(maps.mu_hi, maps.mu_lo, maps.nt, maps.k, maps.v, maps.g8, maps.vb,
                                                      sg, lz, pitch, t0, tc, nb, lpc, scale, kn2, cv, sv, status,
                                                      tf32 ? kTf32Mask : 0xFFFFFFFFu);

@@ -5,8 +5,9 @@
 // One CTA per pair of 64-row tiles (A = 2p, B = 2p+1).  Steps of 64 columns:
 //   far  (blocks of 64 leaves of the tile's own state): S = dq8 . g8^T (int8 -> int32),
 //        logit = S * (sdq_r * sg_l) + lz_l, excluded / padding leaves masked, value vbar_l (bf16);
-//   near (one routed 64-token leaf per step):           S = q8 . k8^T,
-//        logit = S * (sq_r * ks_j * scale), value v_j (bf16).
+//   near (64 keys of routed leaves per step: one leaf of 64, two of 32 or four of 16 keys):
+//        S = q8 . k8^T, logit = S * (sq_r * ks_j * scale), value v_j (bf16).  A last step with fewer
+//        routed leaves than fit masks its empty columns and issues no PV MMA for them.
 // Every MMA is M=64 per tile: tile A's rows live in TMEM lanes {0..15} + 32k, tile B's at lane offset
 // 16, so each softmax thread owns one query row of S, P and O.  P (bf16) is written back into the
 // TMEM columns of its S buffer and feeds O += P . V as the TMEM A operand; V comes from shared memory
@@ -108,7 +109,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                           const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_cv,
                           const float* __restrict__ dd, const float* __restrict__ sq,
                           const float* __restrict__ sdq, const float* __restrict__ ks, const int32_t* __restrict__ idx,
-                          int kx, int nb, int nf, int64_t n, int64_t t0, int64_t tc, int group,
+                          int kx, int nb, int nf, int leaf, int64_t n, int64_t t0, int64_t tc, int group,
                           float scale,
                           const float* __restrict__ tail_part, const int32_t* __restrict__ perm,
                           float* __restrict__ out, float* __restrict__ lse, int* status) {
@@ -122,7 +123,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tlocA = 2 * blockIdx.x;
   const int ntiles = (tlocA + 1 < tc) ? 2 : 1;
   const int srow[2] = {tlocA / group, (tlocA + 1) / group};     // state rows of tiles A and B
-  const int total = nf + kx;        // far steps + near steps (one routed leaf per step)
+  const int rl = 64 / leaf;          // routed leaves per near step
+  const int total = nf + (kx + rl - 1) / rl;     // far steps + near steps
+  const int tail_cols = (kx % rl) ? (kx % rl) * leaf : 64;   // key columns of the last near step
   volatile int* abort_flag = &bars->abort_flag;
 
   if (threadIdx.x == 0) {
@@ -196,12 +199,17 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (ISO) tma_load_2d(tx + kXBytes + 768, &tm_cv, &bars->x_full[s], nx * 64, tl, pol_stream);
             }
           } else {
-            mbar_arrive_expect_tx(&bars->x_full[s], (kXBytes + 256) * ntiles);
+            // the step's routed leaves: rows leaf * i .. of the k8 block, key scales at 4 leaf * i
+            const int e0 = (nx - nf) * rl, cnt = min(rl, kx - e0);
+            mbar_arrive_expect_tx(&bars->x_full[s], (128 + 4) * leaf * cnt * ntiles);
             for (int x = 0; x < ntiles; ++x) {
               uint8_t* tx = st + x * kXTile;
-              const int leaf = idx_s[x * kMaxKx + (nx - nf)];
-              tma_load_2d(tx, &tm_k8, &bars->x_full[s], 0, leaf * 64, pol_keep);
-              bulk_load(tx + kXBytes, ks + static_cast<int64_t>(leaf) * 64, 256, &bars->x_full[s], pol_keep);
+              for (int i = 0; i < cnt; ++i) {
+                const int lf = idx_s[x * kMaxKx + e0 + i];
+                tma_load_2d(tx + i * leaf * 128, &tm_k8, &bars->x_full[s], 0, lf * leaf, pol_keep);
+                bulk_load(tx + kXBytes + i * leaf * 4, ks + static_cast<int64_t>(lf) * leaf, leaf * 4,
+                          &bars->x_full[s], pol_keep);
+              }
             }
           }
         }
@@ -215,6 +223,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t id_pv = idesc_bf16(64, 128, /*a_mn_major=*/false, /*b_mn_major=*/true);
     const uint32_t hi = (1024u >> 4) | (1u << 14) | (2u << 29);          // SBO 1024, version, SWIZZLE_128B
     const uint32_t lo0 = (smem_u32(smem + kOffY) >> 4) | ((kYBytes / 2) >> 4 << 16);   // + LBO (chunk stride)
+    // near steps: the Y slot holds [leaf][half][leaf rows][64] (one load per routed leaf), so the 64-column
+    // halves are leaf * 128 bytes apart and K step kk (keys 16 kk ..) starts in leaf 16 kk / leaf
+    const uint32_t lo0n = (smem_u32(smem + kOffY) >> 4) | (static_cast<uint32_t>(leaf * 128) >> 4 << 16);
+    uint32_t koff_near[4];
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk)
+      koff_near[kk] = static_cast<uint32_t>((16 * kk / leaf) * leaf * 256 + (16 * kk % leaf) * 128) >> 4;
     int ys = 0;
     uint32_t yph = 0;
     int npv = 0;
@@ -223,7 +238,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait_warp(&bars->y_full[ys], yph, status, abort_flag)) break;
       tc_fence_after();
       const uint32_t b = np & 3, g = np & 1, k = np >> 1;
-      const uint32_t lo = lo0 + ys * (kYSlot >> 4);
+      const bool near = np >= nf;
+      const uint32_t lo = (near ? lo0n : lo0) + ys * (kYSlot >> 4);
+      const int kks = (near && np == total - 1) ? tail_cols / 16 : 4;     // K steps with keys
 #pragma unroll
       for (int x = 0; x < 2; ++x) {
         if (x < ntiles) {
@@ -232,9 +249,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t a = tmem + lane_off + kColS + 64 * b;
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            mma_bf16_ts_by(leader, d, a + 8 * kk,
-                           (static_cast<uint64_t>(hi) << 32) | (lo + ((x * kYBytes + kk * 2048) >> 4)), id_pv,
-                           (k | kk) != 0);
+            if (kk < kks)
+              mma_bf16_ts_by(leader, d, a + 8 * kk,
+                             (static_cast<uint64_t>(hi) << 32) |
+                                 (lo + ((x * kYBytes) >> 4) + (near ? koff_near[kk] : (kk * 2048) >> 4)),
+                             id_pv, (k | kk) != 0);
         }
       }
       mma_commit_by(leader, &bars->pv_done[b]);
@@ -258,14 +277,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (leader) {
         const int s = ny % kYSlots;
         uint8_t* st = smem + kOffY + s * kYSlot;
-        mbar_arrive_expect_tx(&bars->y_full[s], kYBytes * ntiles);
+        const int e0 = (ny - nf) * rl, cnt = ny < nf ? 0 : min(rl, kx - e0);
+        mbar_arrive_expect_tx(&bars->y_full[s], (ny < nf ? kYBytes : 256u * leaf * cnt) * ntiles);
         for (int x = 0; x < ntiles; ++x) {
           uint8_t* ty = st + x * kYBytes;
-          // both 64-column halves in one load: [half][64 rows][64] at ty, ty + kYBytes / 2
+          // both 64-column halves in one load: [half][rows][64]; a near step's leaves one after another
           if (ny < nf)
             tma_load_4d(ty, &tm_vb, &bars->y_full[s], 0, ny * 64, 0, srow[x], pol_stream);
           else
-            tma_load_3d(ty, &tm_v, &bars->y_full[s], 0, idx_s[x * kMaxKx + (ny - nf)] * 64, 0, pol_keep);
+            for (int i = 0; i < cnt; ++i)
+              tma_load_3d(ty + i * leaf * 256, &tm_v, &bars->y_full[s], 0, idx_s[x * kMaxKx + e0 + i] * leaf, 0,
+                          pol_keep);
         }
       }
       __syncwarp();
@@ -405,6 +427,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             mxa[(ii >> 1) & 3] = max3(mxa[(ii >> 1) & 3], u.x, u.y);
           }
         }
+        if (j == total - 1 && tail_cols < 64) {
+          // the last near step holds fewer routed leaves than fit: its other columns are no keys
+#pragma unroll
+          for (int i = 0; i < 64; ++i)
+            if (i >= tail_cols) lg[i] = -INFINITY;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) mxa[i] = -INFINITY;
+#pragma unroll
+          for (int i = 0; i < 64; i += 2) mxa[(i >> 1) & 3] = max3(mxa[(i >> 1) & 3], lg[i], lg[i + 1]);
+        }
         esc = sq_r;
       } else {
         // far step: lg = S * (sdq_r * sg * log2 e) + lz * log2 e (+ the iso term), masked columns -inf
@@ -541,10 +573,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 int launch_tile_attention(const TileMaps& maps, const float* sq, const float* sdq, const float* ks, const int32_t* idx,
-                          int kx, int nb, int64_t n, int tile_rows, int64_t t0, int64_t tc, int group, float scale,
-                          const float* tail_part, const int32_t* perm, const float* dd, float* out, float* lse,
-                          int* status, cudaStream_t st) {
+                          int kx, int nb, int leaf, int64_t n, int tile_rows, int64_t t0, int64_t tc, int group,
+                          float scale, const float* tail_part, const int32_t* perm, const float* dd, float* out,
+                          float* lse, int* status, cudaStream_t st) {
   if (kx > kMaxKx || nb > 65535) return HTRC_ERR_UNSUPPORTED;
+  if (leaf != 64 && leaf != 32 && leaf != 16) return HTRC_ERR_UNSUPPORTED;
   static bool attr_done[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -562,7 +595,7 @@ int launch_tile_attention(const TileMaps& maps, const float* sq, const float* sd
   auto kernel = tile_rows == 32 ? (iso ? tile_attention_kernel<32, true> : tile_attention_kernel<32, false>)
                                 : (iso ? tile_attention_kernel<64, true> : tile_attention_kernel<64, false>);
   kernel<<<grid, kThreads, kSmemBytes, st>>>(maps.q8, maps.dq8, maps.g8, maps.vb, maps.lz, maps.sg, maps.excl, maps.k8,
-                                             maps.v, maps.cv, dd, sq, sdq, ks, idx, kx, nb, nf, n, t0, tc,
+                                             maps.v, maps.cv, dd, sq, sdq, ks, idx, kx, nb, nf, leaf, n, t0, tc,
                                              group > 1 ? group : 1, scale, tail_part, perm, out, lse, status);
   return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
 }

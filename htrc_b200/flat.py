@@ -45,6 +45,7 @@ from . import _lib
 from ._lib import check, lib, ptr, stream_ptr
 
 DIM, TILE, LEAF = 128, 64, 64
+LEAVES = (64, 32, 16)       # leaf sizes with kernels (32 and 16: INT8 state, linear far field)
 TILES = (64, 32)          # query tile rows the kernels take (32: the "max" mode, held as 64 rows)
 
 PROD = dict(tile=64, exact_leaves=256, tile_chunk=128, backend="triton", precision="tf32",
@@ -110,8 +111,12 @@ def _check_args(q, k, v, tile, exact_leaves, order, curvature, leaf, select, bac
                                   "implemented")
     if store == "fp8" and curvature != "lin":
         raise NotImplementedError("curvature='iso' is implemented on the INT8 path only")
-    if int(tile) not in TILES or int(leaf) != LEAF:
-        raise NotImplementedError(f"the kernels implement tile=64 or 32, leaf={LEAF} (got tile={tile}, leaf={leaf})")
+    if int(tile) not in TILES or int(leaf) not in LEAVES:
+        raise NotImplementedError(f"the kernels implement tile=64 or 32 and leaf=64, 32 or 16 (got tile={tile}, "
+                                  f"leaf={leaf})")
+    if int(leaf) != LEAF and (store != "int8" or curvature != "lin"):
+        raise NotImplementedError(f"leaf={leaf} is implemented for store='int8' with curvature='lin' (the fp8 "
+                                  f"state and the iso term take leaf={LEAF})")
     if int(sel_stride) != 1:
         raise NotImplementedError("sel_stride != 1 is not implemented")
     for key in ("kv", "q"):
@@ -124,13 +129,15 @@ def _check_args(q, k, v, tile, exact_leaves, order, curvature, leaf, select, bac
         raise ValueError("q, k, v must be CUDA tensors (there is no CPU path)")
 
 
-def _check_scale_block(qk_scale_block, store):
+def _check_scale_block(qk_scale_block, store, leaf=LEAF):
     """qk_scale_block: None/0 (the reference's per-key and per-row INT8 scales) or 64 (one per leaf / tile)."""
     b = int(qk_scale_block or 0)
     if b not in (0, 64):
         raise ValueError("qk_scale_block must be None, 0 or 64")
     if b and store != "int8":
         raise NotImplementedError("qk_scale_block applies to the INT8 query and key codes (store='int8')")
+    if b and int(leaf) != LEAF:
+        raise NotImplementedError(f"qk_scale_block=64 gives one key scale per 64-key leaf (leaf={LEAF})")
     return b
 
 
@@ -217,13 +224,13 @@ def curvature_code(curvature) -> int:
 
 def _args(qd, kb, vb, tk, tv, exact_leaves, sink_leaves, tile_chunk, scale, out=None, lse=None, ws=None,
           stage_events=None, group=1, order=_lib.ORDER_SEQ, tile=TILE, curvature=_lib.CURV_LIN,
-          store=_lib.STORE_INT8, qk_scale_block=0, route_mask=None, precision=_lib.PREC_TF32):
+          store=_lib.STORE_INT8, qk_scale_block=0, route_mask=None, precision=_lib.PREC_TF32, leaf=LEAF):
     a = _lib.HtrcFlatArgs()
     a.q = ptr(qd)
     a.q_dtype = _lib.DTYPE_BF16 if qd.dtype == torch.bfloat16 else _lib.DTYPE_F32
     a.k, a.v = ptr(kb), ptr(vb)
     a.n_queries, a.n_keys = int(qd.shape[0]), int(kb.shape[0])
-    a.dim, a.tile, a.leaf = DIM, int(tile), LEAF
+    a.dim, a.tile, a.leaf = DIM, int(tile), int(leaf)
     a.exact_leaves, a.sink_leaves = int(exact_leaves), int(sink_leaves)
     a.tile_chunk = int(tile_chunk) if tile_chunk else 0
     a.scale = float(scale) if scale is not None else 0.0
@@ -250,10 +257,10 @@ def _args(qd, kb, vb, tk, tv, exact_leaves, sink_leaves, tile_chunk, scale, out=
 
 
 def workspace_bytes(n_queries, n_keys, exact_leaves, sink_leaves=0, tile_chunk=0, n_tail=0, group=1,
-                    order=_lib.ORDER_SEQ, tile=TILE, curvature=_lib.CURV_LIN, store=_lib.STORE_INT8) -> int:
+                    order=_lib.ORDER_SEQ, tile=TILE, curvature=_lib.CURV_LIN, store=_lib.STORE_INT8, leaf=LEAF) -> int:
     """Device workspace one forward call needs."""
     a = _lib.HtrcFlatArgs()
-    a.n_queries, a.n_keys, a.dim, a.tile, a.leaf = int(n_queries), int(n_keys), DIM, int(tile), LEAF
+    a.n_queries, a.n_keys, a.dim, a.tile, a.leaf = int(n_queries), int(n_keys), DIM, int(tile), int(leaf)
     a.q_dtype = _lib.DTYPE_F32
     a.exact_leaves, a.sink_leaves = int(exact_leaves), int(sink_leaves)
     a.tile_chunk, a.n_tail = int(tile_chunk or 0), int(n_tail)
@@ -283,7 +290,7 @@ def _workspace(ws, nbytes, device):
     return b
 
 
-def _check_buffers(qd, kb, vb, tk, tv, out, lse, workspace, route_mask, tile, group):
+def _check_buffers(qd, kb, vb, tk, tv, out, lse, workspace, route_mask, tile, group, leaf=LEAF):
     """Shapes, dtypes, contiguity and device of every buffer the C ABI will read or write, checked on the
     host before any launch (the library trusts its pointers and sizes)."""
     def need(t, name, shape, dtypes):
@@ -313,7 +320,7 @@ def _check_buffers(qd, kb, vb, tk, tv, out, lse, workspace, route_mask, tile, gr
         if route_mask.dtype != torch.uint8 or not route_mask.is_contiguous():
             raise ValueError("route_mask: a contiguous uint8 tensor [groups, leaf_pitch(nb)]")
         rows = -(-(-(-n // int(tile))) // max(1, int(group)))
-        pitch = -(-(m // LEAF) // 16) * 16        # htrc_leaf_pitch: leaves rounded up to 16 (host-side)
+        pitch = -(-(m // int(leaf)) // 16) * 16   # htrc_leaf_pitch: leaves rounded up to 16 (host-side)
         if route_mask.numel() < rows * pitch:
             raise ValueError(f"route_mask: at least {rows} x {pitch} bytes expected ([ceil(tiles / group), "
                              f"leaf_pitch(nb)]), got {route_mask.numel()}")
@@ -325,17 +332,18 @@ def _check_buffers(qd, kb, vb, tk, tv, out, lse, workspace, route_mask, tile, gr
 def forward_into(qd, kb, vb, tk, tv, *, exact_leaves, sink_leaves=0, tile_chunk=0, scale=None, out, lse=None,
                  workspace, stream=None, stage_events=None, group=1, order=_lib.ORDER_SEQ, tile=TILE,
                  curvature=_lib.CURV_LIN, store=_lib.STORE_INT8, qk_scale_block=0, route_mask=None,
-                 precision=_lib.PREC_TF32):
+                 precision=_lib.PREC_TF32, leaf=LEAF):
     """One head through ``htrc_flat_forward`` into caller-provided buffers (no allocation; CUDA-graph
     capturable).  qd [N, 128] f32/bf16, kb/vb [M, 128] bf16, out [N, 128] f32, lse [N] f32 or None;
     stage_events: optional list of torch.cuda.Event recorded between the stages (see
     include/htrc_flat.h); group / order: ``group_of(kern)`` / ``order_code(order)``; tile: 64 or 32;
     store: ``_lib.STORES[store]``; qk_scale_block: 0 or 64; route_mask: optional uint8
     [ceil(nt / group), leaf_pitch(nb)] device tensor that receives the routing masks (1 = leaf exact);
-    precision: ``_lib.PREC_TF32`` (the production setting of PROD, the default) or ``_lib.PREC_FP32``."""
-    _check_buffers(qd, kb, vb, tk, tv, out, lse, workspace, route_mask, tile, group)
+    precision: ``_lib.PREC_TF32`` (the production setting of PROD, the default) or ``_lib.PREC_FP32``;
+    leaf: 64, 32 or 16 keys (32 and 16 with the INT8 state and the linear far field)."""
+    _check_buffers(qd, kb, vb, tk, tv, out, lse, workspace, route_mask, tile, group, leaf)
     a = _args(qd, kb, vb, tk, tv, exact_leaves, sink_leaves, tile_chunk, scale, out, lse, workspace, stage_events,
-              group, order, tile, curvature, store, qk_scale_block, route_mask, precision)
+              group, order, tile, curvature, store, qk_scale_block, route_mask, precision, leaf)
     check(lib().htrc_flat_forward(a, stream_ptr(stream)), "htrc_flat_forward")
 
 
@@ -362,24 +370,24 @@ def flat_attention(q, k, v, *, tile=64, exact_leaves=64, order="seq", curvature=
     return_lse).  Signature and defaults of the reference (h3/htrc_flat.py:99-103); see PROD."""
     _check_args(q, k, v, tile, exact_leaves, order, curvature, leaf, select, backend, store, dot,
                 sel_stride, quant, sink_leaves, tail)
-    qsb = _check_scale_block(qk_scale_block, store)
+    qsb = _check_scale_block(qk_scale_block, store, leaf)
     qd, kb, vb, tk, tv = _prep_inputs(q, k, v, tail, quant)
     grp, oc, cc, sc = group_of(kern), order_code(order), curvature_code(curvature), _lib.STORES[store]
     pc = precision_code(precision, division)
     if prof is not None:
         st = run_stages(qd, kb, vb, tk, tv, exact_leaves=exact_leaves, sink_leaves=sink_leaves,
                         tile_chunk=tile_chunk, scale=scale, prof=prof, group=grp, order=oc, tile=tile, curvature=cc,
-                        store=sc, qk_scale_block=qsb, precision=pc)
+                        store=sc, qk_scale_block=qsb, precision=pc, leaf=leaf)
         return (st["out"], st["lse"]) if return_lse else st["out"]
     n = int(qd.shape[0])
     out = torch.empty((n, DIM), dtype=torch.float32, device=q.device)
     lse = torch.empty((n,), dtype=torch.float32, device=q.device) if return_lse else None
     nbytes = workspace_bytes(n, int(kb.shape[0]), exact_leaves, sink_leaves, tile_chunk,
-                             int(tk.shape[0]) if tk is not None else 0, grp, oc, tile, cc, sc)
+                             int(tk.shape[0]) if tk is not None else 0, grp, oc, tile, cc, sc, leaf)
     w = _workspace(ws, nbytes, q.device)
     forward_into(qd, kb, vb, tk, tv, exact_leaves=exact_leaves, sink_leaves=sink_leaves,
                  tile_chunk=tile_chunk, scale=scale, out=out, lse=lse, workspace=w, group=grp, order=oc, tile=tile,
-                 curvature=cc, store=sc, qk_scale_block=qsb, precision=pc)
+                 curvature=cc, store=sc, qk_scale_block=qsb, precision=pc, leaf=leaf)
     return (out, lse) if return_lse else out
 
 
@@ -401,7 +409,7 @@ def flat_attention_heads(q, k, v, *, return_lse=False, ws=None, **cfg):
                 tail=None, scale=None, qk_scale_block=None, precision="fp32", division="ieee"), **cfg}
     _check_args(q[0], k[0], v[0], c["tile"], c["exact_leaves"], c["order"], c["curvature"], c["leaf"], c["select"],
                 c["backend"], c["store"], c["dot"], c["sel_stride"], c["quant"], c["sink_leaves"], c["tail"])
-    qsb = _check_scale_block(c["qk_scale_block"], c["store"])
+    qsb = _check_scale_block(c["qk_scale_block"], c["store"], c["leaf"])
     out = torch.empty((h, n, DIM), dtype=torch.float32, device=q.device)
     lse = torch.empty((h, n), dtype=torch.float32, device=q.device) if return_lse else None
     grp, oc, cc = group_of(c["kern"]), order_code(c["order"]), curvature_code(c["curvature"])
@@ -411,19 +419,20 @@ def flat_attention_heads(q, k, v, *, return_lse=False, ws=None, **cfg):
         qd, kb, vb, tk, tv = _prep_inputs(q[i], k[i], v[i], c["tail"], c["quant"])
         if w is None:
             nbytes = workspace_bytes(n, int(kb.shape[0]), c["exact_leaves"], c["sink_leaves"], c["tile_chunk"],
-                                     int(tk.shape[0]) if tk is not None else 0, grp, oc, c["tile"], cc, sc)
+                                     int(tk.shape[0]) if tk is not None else 0, grp, oc, c["tile"], cc, sc,
+                                     c["leaf"])
             w = _workspace(ws, nbytes, q.device)
         forward_into(qd, kb, vb, tk, tv, exact_leaves=c["exact_leaves"], sink_leaves=c["sink_leaves"],
                      tile_chunk=c["tile_chunk"], scale=c["scale"], out=out[i], lse=lse[i] if return_lse else None,
                      workspace=w, group=grp, order=oc, tile=c["tile"], curvature=cc, store=sc, qk_scale_block=qsb,
-                     precision=precision_code(c["precision"], c["division"]))
+                     precision=precision_code(c["precision"], c["division"]), leaf=c["leaf"])
     return (out, lse) if return_lse else out
 
 
 @torch.inference_mode()
 def run_stages(qd, kb, vb, tk=None, tv=None, *, exact_leaves, sink_leaves=0, tile_chunk=0, scale=None,
                prof=None, stream=None, group=1, order=_lib.ORDER_SEQ, tile=TILE, curvature=_lib.CURV_LIN,
-               store=_lib.STORE_INT8, qk_scale_block=0, precision=_lib.PREC_TF32):
+               store=_lib.STORE_INT8, qk_scale_block=0, precision=_lib.PREC_TF32, leaf=LEAF):
     """The same operator launched stage by stage through the C ABI's stage entry points, returning
     every intermediate (perm, k8, ks, mu, q8, sq, dq8, sdq, g8, sg, lz, vb, sel, idx, excl, out, lse; with
     store=STORE_FP8: perm, mu, qb, dqh, g8 / vb8 e4m3 codes, sg, sv, lz, sel, idx, excl, out, lse).
@@ -436,7 +445,7 @@ def run_stages(qd, kb, vb, tk=None, tv=None, *, exact_leaves, sink_leaves=0, til
     tick = _Tick(prof)
     n, m = int(qd.shape[0]), int(kb.shape[0])
     tile = int(tile)
-    nt, nb = -(-n // tile), m // LEAF
+    nt, nb = -(-n // tile), m // int(leaf)
     grp = max(1, int(group))
     ng = -(-nt // grp)
     pitch = leaf_pitch(nb)
@@ -445,6 +454,9 @@ def run_stages(qd, kb, vb, tk=None, tv=None, *, exact_leaves, sink_leaves=0, til
     sc = 1.0 / math.sqrt(DIM) if scale is None else float(scale)
     qdt = _lib.DTYPE_BF16 if qd.dtype == torch.bfloat16 else _lib.DTYPE_F32
     e = lambda *shape, dt=torch.float32: torch.empty(shape, dtype=dt, device=dev)  # noqa: E731
+    if int(leaf) not in LEAVES or (int(leaf) != LEAF and (store != _lib.STORE_INT8 or curvature != _lib.CURV_LIN
+                                                            or qk_scale_block)):
+        raise NotImplementedError(f"leaf={leaf}: leaves of 64, or 32 / 16 with the INT8 state and the linear far field")
     if store == _lib.STORE_FP8:
         if curvature != _lib.CURV_LIN:
             raise NotImplementedError("curvature='iso' is implemented on the INT8 path only")
@@ -489,7 +501,7 @@ def run_stages(qd, kb, vb, tk=None, tv=None, *, exact_leaves, sink_leaves=0, til
     if far:
         for g0 in range(0, ng, gstep):
             gc = min(gstep, ng - g0)
-            check(L.htrc_leaf_stats(ptr(r["mu_hi"]), ptr(r["mu_lo"]), ng, g0, gc, ptr(kb), ptr(vb), m, DIM, LEAF, sc,
+            check(L.htrc_leaf_stats(ptr(r["mu_hi"]), ptr(r["mu_lo"]), ng, g0, gc, ptr(kb), ptr(vb), m, DIM, int(leaf), sc,
                                     ptr(r["g8"][g0]), ptr(r["sg"][g0]), ptr(r["lz"][g0]), ptr(r["vb"][g0]),
                                     ptr(r["kn2"]), ptr(r["cv"][g0]) if iso else None, int(precision), stp, s),
                   "htrc_leaf_stats")
@@ -503,11 +515,11 @@ def run_stages(qd, kb, vb, tk=None, tv=None, *, exact_leaves, sink_leaves=0, til
     check(L.htrc_tile_attention(ptr(r["q8"]), ptr(r["sq"]), ptr(r["dq8"]), ptr(r["sdq"]), n, tile, 0, nt, grp,
                                 ptr(r["g8"]),
                                 ptr(r["sg"]), ptr(r["lz"]), ptr(r["vb"]), ptr(r["excl"]), ptr(r["idx"]), kx, nb,
-                                ptr(r["k8"]), ptr(r["ks"]), ptr(vb), m, DIM, LEAF, sc, ptr(tail_part), perm,
+                                ptr(r["k8"]), ptr(r["ks"]), ptr(vb), m, DIM, int(leaf), sc, ptr(tail_part), perm,
                                 ptr(r["cv"]), ptr(r["dd"]), ptr(r["out"]), ptr(r["lse"]), stp, s), "htrc_tile_attention")
     tick("tile")
     tick("finish")
-    r["kx"], r["nb"], r["pitch"], r["group"], r["tile"] = kx, nb, pitch, grp, tile
+    r["kx"], r["nb"], r["pitch"], r["group"], r["tile"], r["leaf"] = kx, nb, pitch, grp, tile, int(leaf)
     return r
 
 
@@ -562,5 +574,5 @@ def _run_stages_fp8(qd, kb, vb, tk, tv, *, n, m, nt, nb, ng, grp, pitch, sink, k
                                     ptr(r["out"]), ptr(r["lse"]), stp, s), "htrc_tile_attention_fp8")
     tick("tile")
     tick("finish")
-    r["kx"], r["nb"], r["pitch"], r["group"], r["tile"] = kx, nb, pitch, grp, tile
+    r["kx"], r["nb"], r["pitch"], r["group"], r["tile"], r["leaf"] = kx, nb, pitch, grp, tile, LEAF
     return r

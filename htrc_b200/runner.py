@@ -3,13 +3,16 @@
 Same call shape as the reference's h3/htrc_flat_runner.py (``FlatRunner``, ``MODES``, ``CHUNKS``,
 ``predicted_peak_mib``, ``plan_chunk``):
 
-    runner = FlatRunner(queries, keys, free_bytes=free_vram, mode="fast", leaf=64)
+    runner = FlatRunner(queries, keys, free_bytes=free_vram, mode="fast", leaf=64)   # leaf default: 16
     outputs = runner.run([(head, q, k, v), ...])          # q [Q,128], k/v [K,128] on CUDA
     runner.run(jobs, sink=lambda i, out: block_out[i].copy_(out))
 
 One head is a single ``htrc_flat_forward`` launch sequence with no host synchronisation and no
 allocation, so it is captured once into a CUDA graph (static q/k/v/out/lse buffers) and replayed per
 head; if capture fails the runner falls back to eager launches and records ``graph_error``.
+As in the reference, the configuration is PROD updated by the mode and the caller's overrides, so without a
+``leaf=`` override the leaf is ``flat_attention``'s default of 16 keys (pass ``leaf=64`` for the production
+benchmark's leaf).
 Differences from the reference: ``head()`` and ``run()`` without a sink always return fresh tensors
 (the reference's eager path returns views of one reused workspace buffer, h3/htrc_flat.py:234 with
 h3/htrc_flat_triton.py:302-312); ``lse=True`` also returns the per-query log-partition.
@@ -34,7 +37,7 @@ STATIC_MIB = 0.0      # graph runner's static q (fp32) / k / v (bf16) copies, ad
 KMEANS_MIB = 0.0      # the k-means ordering's scratch is part of the library workspace (order="kmeans")
 
 
-def predicted_peak_mib(keys: int, tile: int, tile_chunk: int, splits: int = 8, leaf: int = 64,
+def predicted_peak_mib(keys: int, tile: int, tile_chunk: int, splits: int = 8, leaf: int = 16,
                        dim: int = 128, order: str = "seq", graph: bool = True, queries: int = 0,
                        exact_leaves: int = 256, group: int = 1) -> float:
     """Device memory of one head above the caller's q/k/v, in MiB: this library's workspace
@@ -43,14 +46,14 @@ def predicted_peak_mib(keys: int, tile: int, tile_chunk: int, splits: int = 8, l
     ``splits`` is accepted and unused."""
     q = int(queries) if queries else int(tile) * max(1, int(tile_chunk))
     ws = _flat.workspace_bytes(q, int(keys), int(exact_leaves), 0, int(tile_chunk), 0, int(group),
-                               _flat.order_code(order), int(tile))
+                               _flat.order_code(order), int(tile), leaf=int(leaf))
     static = (q * dim * 4 + 2 * keys * dim * 2 + q * (dim + 1) * 4) if graph else 0
     kmeans = KMEANS_MIB if order == "kmeans" else 0.0
     return (ws + static) / 2 ** 20 + kmeans
 
 
 def plan_chunk(free_bytes: int, keys: int, tile: int, splits: int = 8, order: str = "seq",
-               graph: bool = True, queries: int = 0, leaf: int = 64, exact_leaves: int = 256,
+               graph: bool = True, queries: int = 0, leaf: int = 16, exact_leaves: int = 256,
                group: int = 1) -> int:
     """Largest tile chunk whose predicted peak fits in ``free_bytes`` (h3/htrc_flat_runner.py:71-84);
     raises MemoryError when even the smallest chunk does not fit."""
@@ -81,12 +84,13 @@ class FlatRunner:
         self.device = torch.device(device)
         base = dict(_flat.PROD)
         base.update(MODES[mode])
-        base["leaf"] = _flat.LEAF
         overrides = dict(overrides)
         if "kern" in overrides:                          # a caller's kern dict updates PROD's launch knobs key by key
             base["kern"] = {**base.get("kern", {}), **overrides.pop("kern")}
         base.update(overrides)
         base["sink_leaves"] = int(sink_leaves)
+        base["leaf"] = int(base.get("leaf", 16))        # flat_attention's default leaf (h3/htrc_flat.py:100)
+        self.leaf = base["leaf"]
         self.tail_rows = int(tail_rows)
         self.want_lse = bool(lse)
         self.queries, self.keys, self.dim = int(queries), int(keys), int(dim)
@@ -102,14 +106,14 @@ class FlatRunner:
                 free_bytes = int(torch.cuda.mem_get_info(self.device)[0] * 0.8)
             if free_bytes is not None:
                 tile_chunk = plan_chunk(free_bytes, keys, base["tile"], base.get("splits", 8), base["order"],
-                                        use_graph, queries=int(queries), exact_leaves=base["exact_leaves"],
-                                        group=self.group)
+                                        use_graph, queries=int(queries), leaf=self.leaf,
+                                        exact_leaves=base["exact_leaves"], group=self.group)
             else:
                 tile_chunk = base["tile_chunk"]
         base["tile_chunk"] = int(tile_chunk)
         self.cfg = base
         self.predicted_mib = predicted_peak_mib(keys, base["tile"], base["tile_chunk"], base.get("splits", 8),
-                                                order=base["order"], graph=use_graph, queries=int(queries),
+                                                self.leaf, order=base["order"], graph=use_graph, queries=int(queries),
                                                 exact_leaves=base["exact_leaves"], group=self.group)
         self.ws = {}
         self.graph = None
@@ -127,7 +131,7 @@ class FlatRunner:
         except ValueError as exc:
             if "CUDA tensors" not in str(exc):
                 raise
-        _flat._check_scale_block(base.get("qk_scale_block"), base["store"])
+        _flat._check_scale_block(base.get("qk_scale_block"), base["store"], self.leaf)
         if use_graph:
             self._capture()
 
@@ -156,13 +160,14 @@ class FlatRunner:
             self._sl = torch.empty((self.queries,), device=dev, dtype=torch.float32)
             nbytes = _flat.workspace_bytes(self.queries, self.keys, c["exact_leaves"], c["sink_leaves"],
                                            c["tile_chunk"], self.tail_rows, self.group, self.order, c["tile"],
-                                           self.curvature, self.store)
+                                           self.curvature, self.store, self.leaf)
             self._w = _flat.new_workspace(nbytes, dev)
             kw = dict(exact_leaves=c["exact_leaves"], sink_leaves=c["sink_leaves"], tile_chunk=c["tile_chunk"],
                       scale=c.get("scale"), out=self._so, lse=self._sl, workspace=self._w, group=self.group,
                       order=self.order, tile=c["tile"], curvature=self.curvature, store=self.store,
                       qk_scale_block=self.qk_scale_block, precision=_flat.precision_code(c.get("precision", "fp32"),
-                                                                               c.get("division", "ieee")))
+                                                                               c.get("division", "ieee")),
+                      leaf=self.leaf)
             self._capturing = True
             try:
                 side = torch.cuda.Stream()

@@ -76,7 +76,7 @@ typedef struct HtrcFlatArgs {
   int32_t dim;             /* D, must be 128 */
   int32_t tile;            /* query tile rows: 64, or 32 (the "max" mode; held as 64 rows, rows 32..63
                               repeating row 31) */
-  int32_t leaf;            /* key leaf tokens, must be 64 */
+  int32_t leaf;            /* key leaf tokens: 64, or 32 / 16 with store INT8 and curvature LIN */
   int32_t exact_leaves;    /* E >= 0: leaves evaluated exactly per tile (clamped to nb) */
   int32_t sink_leaves;     /* leading leaves always exact (clamped to nb) */
   int32_t tile_chunk;      /* tiles per chunk of the far-field state (<= 0: all tiles at once) */
@@ -124,7 +124,7 @@ int htrc_flat_workspace_size(const HtrcFlatArgs* args, size_t* bytes);
  * row-max selection, top-E routing, far field + near field + tail, normalised output and log-Z
  * (store HTRC_STORE_FP8: the fp8 stage entry points below instead of the INT8 ones, no key pack).
  * Replaces flat_attention(q, k, v, backend="triton", store="int8"|"fp8", dot="bf16", select="max",
- * tile=64|32, leaf=64, exact_leaves=E, sink_leaves=S, tail=(tk, tv), order="seq"|"kmeans",
+ * tile=64|32, leaf=64|32|16, exact_leaves=E, sink_leaves=S, tail=(tk, tv), order="seq"|"kmeans",
  * kern={"group": G}) of the reference (h3/htrc_flat.py:99-124 -> _flat_triton :181-276), plus the
  * log-Z output the reference lacks. */
 int htrc_flat_forward(const HtrcFlatArgs* args, htrc_stream_t stream);
@@ -166,7 +166,7 @@ int htrc_kmeans_order(const void* q, int32_t q_dtype, int64_t n_queries, int32_t
  * g8 [tc, nb, dim] int8 and sg/lz [tc, P] f32, vb [tc, nb, dim] bf16.  mu_hi/mu_lo as written by
  * htrc_tile_prep / htrc_tile_prep_ex (all nt centre rows: tiles, or groups of tiles); precision: HTRC_PREC_*
  * for the softmax weights of the second dot (the centres' precision is set where mu_hi/mu_lo are written);
- * status: device int32 word or NULL. */
+ * leaf: 64, 32 or 16 (kn2 / cv only with 64); status: device int32 word or NULL. */
 int htrc_leaf_stats(const uint16_t* mu_hi, const uint16_t* mu_lo, int64_t nt, int64_t t0, int64_t tc,
                     const uint16_t* k, const uint16_t* v, int64_t n_keys, int32_t dim, int32_t leaf, float scale,
                     int8_t* g8, float* sg, float* lz, uint16_t* vb, const float* kn2, float* cv, int32_t precision,
@@ -197,7 +197,7 @@ int htrc_route(const float* sel, int64_t tc, int64_t nb, int32_t exact_leaves, i
  * multiple of group); k8/ks from htrc_pack_int8 (half-even) of k; tail_part: NULL or
  * [n_queries, dim + 2] f32 rows (acc, m, l) from the tail, in the caller's row order; perm: NULL, or the
  * permutation given to htrc_tile_prep (query i in tile order is written to out/lse row perm[i]); tile: the
- * tile rows given to htrc_tile_prep. */
+ * tile rows given to htrc_tile_prep; leaf: 64, 32 or 16 (cv / dd only with 64). */
 int htrc_tile_attention(const int8_t* q8, const float* sq, const int8_t* dq8, const float* sdq, int64_t n_queries,
                         int32_t tile, int64_t t0, int64_t tc, int32_t group, const int8_t* g8, const float* sg,
                         const float* lz,

@@ -43,8 +43,21 @@ int main(void) {
   a.n_keys = 129024 + 1;
   if (htrc_flat_workspace_size(&a, &need) != HTRC_ERR_ARG) return fail("keys not a multiple of the leaf");
   a.n_keys = 129024;
-  a.leaf = 16;
-  if (htrc_flat_workspace_size(&a, &need) != HTRC_ERR_UNSUPPORTED) return fail("leaf 16");
+  {
+    size_t need16 = 0, need32 = 0;
+    a.leaf = 32;
+    if (htrc_flat_workspace_size(&a, &need32) != HTRC_OK || need32 <= need) return fail("leaf 32 size");
+    a.leaf = 16;
+    if (htrc_flat_workspace_size(&a, &need16) != HTRC_OK || need16 <= need32) return fail("leaf 16 size");
+    a.curvature = HTRC_CURV_ISO;
+    if (htrc_flat_workspace_size(&a, &need16) != HTRC_ERR_UNSUPPORTED) return fail("leaf 16 with iso curvature");
+    a.curvature = HTRC_CURV_LIN;
+    a.store = HTRC_STORE_FP8;
+    if (htrc_flat_workspace_size(&a, &need16) != HTRC_ERR_UNSUPPORTED) return fail("leaf 16 with the fp8 state");
+    a.store = HTRC_STORE_INT8;
+    a.leaf = 8;
+    if (htrc_flat_workspace_size(&a, &need16) != HTRC_ERR_UNSUPPORTED) return fail("leaf 8");
+  }
   a.leaf = 64;
   if (htrc_flat_forward(&a, NULL) != HTRC_ERR_ARG) return fail("forward without pointers");
   if (htrc_leaf_pitch(2016) != 2016 || htrc_leaf_pitch(2017) != 2032) return fail("leaf pitch");

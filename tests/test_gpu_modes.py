@@ -239,7 +239,7 @@ def test_runner_kmeans_modes(dev, mode):
     from htrc_b200 import runner
     q, k, v = _inputs((8, 32, 48), 111)
     n = q.shape[0]
-    r = runner.FlatRunner(n, n, mode=mode, lse=True)
+    r = runner.FlatRunner(n, n, mode=mode, lse=True, leaf=64)
     assert r.graph is not None, r.graph_error
     out, lse = r.head(q.to(dev), k.to(dev), v.to(dev))
     ref, rl = htrc_b200.flat_attention(q.to(dev), k.to(dev), v.to(dev), return_lse=True,
@@ -318,7 +318,7 @@ def test_iso_curvature_end_to_end(dev):
     with pytest.raises(ValueError, match="curvature='lin'"):
         htrc_b200.flat_attention(qd, kd, vd, **{**cfg, "backend": "triton"})
     r = runner.FlatRunner(q.shape[0], k.shape[0], mode="fast", backend="cuda", curvature="iso", lse=True,
-                          exact_leaves=24, precision="fp32")
+                          exact_leaves=24, precision="fp32", leaf=64)
     assert r.graph is not None, r.graph_error
     o2, l2 = r.head(qd, kd, vd)
     torch.cuda.synchronize()

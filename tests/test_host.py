@@ -65,7 +65,10 @@ def test_workspace_size_validation():
     assert size(_args(m=4096 + 32)) == _lib.HTRC_ERR_ARG            # keys not a multiple of the leaf
     assert size(_args(n=0)) == _lib.HTRC_ERR_ARG
     assert size(_args(dim=64)) == _lib.HTRC_ERR_UNSUPPORTED
-    assert size(_args(leaf=32)) == _lib.HTRC_ERR_UNSUPPORTED
+    assert size(_args(leaf=32)) == _lib.HTRC_OK                        # INT8 state, linear far field
+    assert size(_args(leaf=16)) == _lib.HTRC_OK
+    assert size(_args(leaf=8)) == _lib.HTRC_ERR_UNSUPPORTED
+    assert size(_args(leaf=128)) == _lib.HTRC_ERR_UNSUPPORTED
     assert size(_args(tile=128)) == _lib.HTRC_ERR_UNSUPPORTED
     assert size(_args(tile=16)) == _lib.HTRC_ERR_UNSUPPORTED
     assert size(_args(tile=32)) == _lib.HTRC_OK                        # the "max" mode
@@ -137,7 +140,13 @@ def test_flat_attention_unimplemented_configurations_say_so():
     with pytest.raises(NotImplementedError, match="tile=64 or 32"):
         htrc_b200.flat_attention(q, k, v, **{**cfg, "tile": 16})
     with pytest.raises(NotImplementedError, match="leaf"):
-        htrc_b200.flat_attention(q, k, v, **{**cfg, "leaf": 32})
+        htrc_b200.flat_attention(q, k, v, **{**cfg, "leaf": 8})
+    with pytest.raises(NotImplementedError, match="leaf=32 is implemented for store='int8'"):
+        htrc_b200.flat_attention(q, k, v, **{**cfg, "leaf": 32, "store": "fp8"})
+    with pytest.raises(NotImplementedError, match="leaf=16 is implemented for store='int8'"):
+        htrc_b200.flat_attention(q, k, v, **{**cfg, "leaf": 16, "backend": "cuda", "curvature": "iso"})
+    with pytest.raises(NotImplementedError, match="one key scale per 64-key leaf"):
+        htrc_b200.flat._check_scale_block(64, "int8", 16)
     with pytest.raises(NotImplementedError):
         htrc_b200.flat_attention(q, k, v, **{**cfg, "store": "bf16"})
     with pytest.raises(NotImplementedError):
