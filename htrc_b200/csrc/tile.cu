@@ -100,7 +100,9 @@ __device__ __forceinline__ float ex2(float x) {
 
 }  // namespace
 
-template <int TROWS, bool ISO>
+// ML: near steps of several routed leaves (leaf 32 or 16); the leaf-64 instantiation keeps the one-leaf step's
+// straight-line producer code (the producers' per-leaf loops, even unexecuted, slowed the QK issuer's loop)
+template <int TROWS, bool ISO, bool ML>
 __global__ void __launch_bounds__(kThreads, 1)
     tile_attention_kernel(const __grid_constant__ CUtensorMap tm_q8, const __grid_constant__ CUtensorMap tm_dq8,
                           const __grid_constant__ CUtensorMap tm_g8, const __grid_constant__ CUtensorMap tm_vb,
@@ -123,9 +125,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tlocA = 2 * blockIdx.x;
   const int ntiles = (tlocA + 1 < tc) ? 2 : 1;
   const int srow[2] = {tlocA / group, (tlocA + 1) / group};     // state rows of tiles A and B
-  const int rl = 64 / leaf;          // routed leaves per near step
-  const int total = nf + (kx + rl - 1) / rl;     // far steps + near steps
-  const int tail_cols = (kx % rl) ? (kx % rl) * leaf : 64;   // key columns of the last near step
+  const int rl = ML ? 64 / leaf : 1;                 // routed leaves per near step
+  const int total = nf + (kx + rl - 1) / rl;          // far steps + near steps
+  const int tail_cols = (ML && kx % rl) ? (kx % rl) * leaf : 64;   // key columns of the last near step
   volatile int* abort_flag = &bars->abort_flag;
 
   if (threadIdx.x == 0) {
@@ -200,15 +202,26 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           } else {
             // the step's routed leaves: rows leaf * i .. of the k8 block, key scales at 4 leaf * i
-            const int e0 = (nx - nf) * rl, cnt = min(rl, kx - e0);
-            mbar_arrive_expect_tx(&bars->x_full[s], (128 + 4) * leaf * cnt * ntiles);
-            for (int x = 0; x < ntiles; ++x) {
-              uint8_t* tx = st + x * kXTile;
-              for (int i = 0; i < cnt; ++i) {
-                const int lf = idx_s[x * kMaxKx + e0 + i];
-                tma_load_2d(tx + i * leaf * 128, &tm_k8, &bars->x_full[s], 0, lf * leaf, pol_keep);
-                bulk_load(tx + kXBytes + i * leaf * 4, ks + static_cast<int64_t>(lf) * leaf, leaf * 4,
-                          &bars->x_full[s], pol_keep);
+            if constexpr (!ML) {
+              mbar_arrive_expect_tx(&bars->x_full[s], (kXBytes + 256) * ntiles);
+              for (int x = 0; x < ntiles; ++x) {
+                uint8_t* tx = st + x * kXTile;
+                const int lf = idx_s[x * kMaxKx + (nx - nf)];
+                tma_load_2d(tx, &tm_k8, &bars->x_full[s], 0, lf * 64, pol_keep);
+                bulk_load(tx + kXBytes, ks + static_cast<int64_t>(lf) * 64, 256, &bars->x_full[s], pol_keep);
+              }
+            } else {
+              const int e0 = (nx - nf) * rl, cnt = min(rl, kx - e0);
+              mbar_arrive_expect_tx(&bars->x_full[s], (128 + 4) * leaf * cnt * ntiles);
+              for (int x = 0; x < ntiles; ++x) {
+                uint8_t* tx = st + x * kXTile;
+#pragma unroll 1
+                for (int i = 0; i < cnt; ++i) {
+                  const int lf = idx_s[x * kMaxKx + e0 + i];
+                  tma_load_2d(tx + i * leaf * 128, &tm_k8, &bars->x_full[s], 0, lf * leaf, pol_keep);
+                  bulk_load(tx + kXBytes + i * leaf * 4, ks + static_cast<int64_t>(lf) * leaf, leaf * 4,
+                            &bars->x_full[s], pol_keep);
+                }
               }
             }
           }
@@ -238,9 +251,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait_warp(&bars->y_full[ys], yph, status, abort_flag)) break;
       tc_fence_after();
       const uint32_t b = np & 3, g = np & 1, k = np >> 1;
-      const bool near = np >= nf;
+      const bool near = ML && np >= nf;
       const uint32_t lo = (near ? lo0n : lo0) + ys * (kYSlot >> 4);
-      const int kks = (near && np == total - 1) ? tail_cols / 16 : 4;     // K steps with keys
+      const int kks = (ML && near && np == total - 1) ? tail_cols / 16 : 4;     // K steps with keys
 #pragma unroll
       for (int x = 0; x < 2; ++x) {
         if (x < ntiles) {
@@ -277,17 +290,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (leader) {
         const int s = ny % kYSlots;
         uint8_t* st = smem + kOffY + s * kYSlot;
-        const int e0 = (ny - nf) * rl, cnt = ny < nf ? 0 : min(rl, kx - e0);
-        mbar_arrive_expect_tx(&bars->y_full[s], (ny < nf ? kYBytes : 256u * leaf * cnt) * ntiles);
-        for (int x = 0; x < ntiles; ++x) {
-          uint8_t* ty = st + x * kYBytes;
-          // both 64-column halves in one load: [half][rows][64]; a near step's leaves one after another
-          if (ny < nf)
-            tma_load_4d(ty, &tm_vb, &bars->y_full[s], 0, ny * 64, 0, srow[x], pol_stream);
-          else
-            for (int i = 0; i < cnt; ++i)
-              tma_load_3d(ty + i * leaf * 256, &tm_v, &bars->y_full[s], 0, idx_s[x * kMaxKx + e0 + i] * leaf, 0,
-                          pol_keep);
+        // both 64-column halves in one load: [half][rows][64]; a near step's leaves one after another
+        if constexpr (!ML) {
+          mbar_arrive_expect_tx(&bars->y_full[s], kYBytes * ntiles);
+          for (int x = 0; x < ntiles; ++x) {
+            uint8_t* ty = st + x * kYBytes;
+            if (ny < nf)
+              tma_load_4d(ty, &tm_vb, &bars->y_full[s], 0, ny * 64, 0, srow[x], pol_stream);
+            else
+              tma_load_3d(ty, &tm_v, &bars->y_full[s], 0, idx_s[x * kMaxKx + (ny - nf)] * 64, 0, pol_keep);
+          }
+        } else {
+          const int e0 = (ny - nf) * rl, cnt = ny < nf ? 1 : min(rl, kx - e0);
+          mbar_arrive_expect_tx(&bars->y_full[s], (ny < nf ? kYBytes : 256u * leaf * cnt) * ntiles);
+          for (int x = 0; x < ntiles; ++x) {
+            uint8_t* ty = st + x * kYBytes;
+            if (ny < nf) {
+              tma_load_4d(ty, &tm_vb, &bars->y_full[s], 0, ny * 64, 0, srow[x], pol_stream);
+            } else {
+#pragma unroll 1
+              for (int i = 0; i < cnt; ++i)
+                tma_load_3d(ty + i * leaf * 256, &tm_v, &bars->y_full[s], 0, idx_s[x * kMaxKx + e0 + i] * leaf, 0,
+                            pol_keep);
+            }
+          }
         }
       }
       __syncwarp();
@@ -351,9 +377,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (ISO) reinterpret_cast<float*>(smem + kOffCC3)[s * 128 + colq] =
               reinterpret_cast<const float*>(par + 768)[i] * kLog2e;
           c[colq] = v;
-        } else {
+        } else if (j != total - 1 || tail_cols == 64) {
           // near: one constant per column, packed (tile x's 64 at x * 64 of the slot's float view)
           reinterpret_cast<float*>(c)[colq] = reinterpret_cast<const float*>(par)[i] * near_scale;
+          if (ISO) reinterpret_cast<float*>(smem + kOffCC3)[s * 128 + colq] = 0.f;
+        } else {
+          // partial last near step: (key constant, 0) per column as the far steps lay them out, columns past
+          // the routed leaves (stale key scales) (0, -inf)
+          const bool key = i < tail_cols;
+          c[colq] = make_float2(key ? reinterpret_cast<const float*>(par)[i] * near_scale : 0.f,
+                                key ? 0.f : -INFINITY);
           if (ISO) reinterpret_cast<float*>(smem + kOffCC3)[s * 128 + colq] = 0.f;
         }
       }
@@ -407,7 +440,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       float lg[64];
       float mxa[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};   // independent chains
       float esc;        // the exponent's argument is esc * lg - m (one FMA)
-      if (j >= nf) {
+      if (j >= nf && (j != total - 1 || tail_cols == 64)) {
         // near step (warp-uniform): lg = S * (ks * scale * log2 e); the row's scale sq_r > 0 multiplies after
         // the maximum and inside the exponent's FMA.  The constants are packed one per column.
         const float* c1 = reinterpret_cast<const float*>(cc + s * 128) + x * 64;
@@ -427,22 +460,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             mxa[(ii >> 1) & 3] = max3(mxa[(ii >> 1) & 3], u.x, u.y);
           }
         }
-        if (j == total - 1 && tail_cols < 64) {
-          // the last near step holds fewer routed leaves than fit: its other columns are no keys
-#pragma unroll
-          for (int i = 0; i < 64; ++i)
-            if (i >= tail_cols) lg[i] = -INFINITY;
-#pragma unroll
-          for (int i = 0; i < 4; ++i) mxa[i] = -INFINITY;
-#pragma unroll
-          for (int i = 0; i < 64; i += 2) mxa[(i >> 1) & 3] = max3(mxa[(i >> 1) & 3], lg[i], lg[i + 1]);
-        }
         esc = sq_r;
       } else {
-        // far step: lg = S * (sdq_r * sg * log2 e) + lz * log2 e (+ the iso term), masked columns -inf
+        // far step: lg = S * (sdq_r * sg * log2 e) + lz * log2 e (+ the iso term), masked columns -inf; a
+        // partial last near step (fewer routed leaves than fit) the same way with sq_r and the key constants,
+        // its columns past the routed leaves masked
         const float* c3 = reinterpret_cast<const float*>(smem + kOffCC3) + s * 128 + x * 64;
         const float2 dd2 = make_float2(dd_r, dd_r);
-        const float2 srow2 = make_float2(sdq_r, sdq_r);
+        const float sr = (!ML || j < nf) ? sdq_r : sq_r;
+        const float2 srow2 = make_float2(sr, sr);
 #pragma unroll
         for (int i = 0; i < 64; i += 2) {
           const float4 cv = *reinterpret_cast<const float4*>(c + i);     // (c1_i, c2_i, c1_i+1, c2_i+1)
@@ -583,8 +609,9 @@ int launch_tile_attention(const TileMaps& maps, const float* sq, const float* sd
   cudaGetDevice(&dev);
   if (dev < 64 && !attr_done[dev]) {
     bool ok = true;
-    for (auto k : {tile_attention_kernel<64, false>, tile_attention_kernel<32, false>, tile_attention_kernel<64, true>,
-                   tile_attention_kernel<32, true>})
+    for (auto k : {tile_attention_kernel<64, false, false>, tile_attention_kernel<32, false, false>,
+                   tile_attention_kernel<64, true, false>, tile_attention_kernel<32, true, false>,
+                   tile_attention_kernel<64, false, true>, tile_attention_kernel<32, false, true>})
       ok = ok && cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) == cudaSuccess;
     if (!ok) return HTRC_ERR_CUDA;
     attr_done[dev] = true;
@@ -592,8 +619,13 @@ int launch_tile_attention(const TileMaps& maps, const float* sq, const float* sd
   const int nf = kx >= nb ? 0 : (nb + 63) / 64;
   const unsigned grid = static_cast<unsigned>((tc + 1) / 2);
   const bool iso = dd != nullptr;
-  auto kernel = tile_rows == 32 ? (iso ? tile_attention_kernel<32, true> : tile_attention_kernel<32, false>)
-                                : (iso ? tile_attention_kernel<64, true> : tile_attention_kernel<64, false>);
+  if (iso && leaf != 64) return HTRC_ERR_UNSUPPORTED;
+  auto kernel = leaf != 64 ? (tile_rows == 32 ? tile_attention_kernel<32, false, true>
+                                              : tile_attention_kernel<64, false, true>)
+                           : tile_rows == 32 ? (iso ? tile_attention_kernel<32, true, false>
+                                                    : tile_attention_kernel<32, false, false>)
+                                             : (iso ? tile_attention_kernel<64, true, false>
+                                                    : tile_attention_kernel<64, false, false>);
   kernel<<<grid, kThreads, kSmemBytes, st>>>(maps.q8, maps.dq8, maps.g8, maps.vb, maps.lz, maps.sg, maps.excl, maps.k8,
                                              maps.v, maps.cv, dd, sq, sdq, ks, idx, kx, nb, nf, leaf, n, t0, tc,
                                              group > 1 ? group : 1, scale, tail_part, perm, out, lse, status);
