@@ -554,6 +554,26 @@ def state_fp8(g, vb):
     return gq, sg, vq, sv
 
 
+def state_bf16(g, vb):
+    """The bf16 far-field state (h3/htrc_flat_triton.py:82-84, store="bf16"): g and vbar rounded to bf16
+    (nearest even), no row scales.  Returns (g values, vbar values) as float32."""
+    return bf16_round(np.asarray(g, F32)), bf16_round(np.asarray(vb, F32))
+
+
+def query_codes_bf16(qt, mu):
+    """The bf16 state's query operands (h3/htrc_flat_triton.py:106-107, DOT=1): bf16(q) for the near field and
+    bf16(q - mu) for the far field (float32 offsets rounded once)."""
+    qt = np.asarray(qt, F32)
+    dq = (qt - np.asarray(mu, F32)[:, None, :]).astype(F32)
+    return bf16_round(qt), bf16_round(dq)
+
+
+def rowmax_select_bf16(dqb, gb, lz, group=1):
+    """SEL[t, l] = max_r (bf16(dq_r) . g_l) + lz_l (h3/htrc_flat_triton.py:247-248, DOT=1 with the bf16
+    state): float32 sums of exact bf16 products; groups as rowmax_select."""
+    return rowmax_select_fp8(dqb, gb, np.ones(np.asarray(lz).shape, F32), lz, group)
+
+
 def query_codes_fp8(qt, mu):
     """The fp8 path's query operands (h3/htrc_flat_triton.py:103-109): bf16(q) for the near field and
     fp16(q - mu) for the far field (float32 offsets rounded once)."""
@@ -575,11 +595,13 @@ def rowmax_select_fp8(dqh, gq, sg, lz, group=1):
     return out
 
 
-def tile_attention_fp8(qt, qb, dqh, gq, sg, lz, vq, sv, excl, idx, kb, vbf, leaf, scale, tail=None, group=1):
+def tile_attention_fp8(qt, qb, dqh, gq, sg, lz, vq, sv, excl, idx, kb, vbf, leaf, scale, tail=None, group=1,
+                       far_weight="f16"):
     """Far + near (+ tail) of every tile with the fp8 state (h3/htrc_flat_triton.py:118-211, FP8=1, DOT=1),
     order-free: far logit = (fp16 dq . g) * sg + lz, value weight fp16(p * sv) on the e4m3 values of vbar;
     near logit = (bf16 q . bf16 k) * scale, weight bf16(p); the normaliser sums float32 p.
-    Returns (out [nt*T, D], lse [nt*T])."""
+    far_weight="bf16" with sg = sv = 1, bf16 dq and the bf16 state is the bf16-state path (:139-140, :154):
+    far logit = (bf16 dq . g) + lz, weight bf16(p).  Returns (out [nt*T, D], lse [nt*T])."""
     nt, T, d = qt.shape
     out = np.zeros((nt, T, d), F32)
     lse = np.zeros((nt, T), F32)
@@ -594,7 +616,7 @@ def tile_attention_fp8(qt, qb, dqh, gq, sg, lz, vq, sv, excl, idx, kb, vbf, leaf
             sc = (dqh[t].astype(np.float64) @ gq[gt][keep].astype(np.float64).T).astype(F32)
             ss.append((sc * sg[gt][keep][None, :]).astype(F32) + lz[gt][keep][None, :])
             vs.append(vq[gt][keep])
-            ws.append(("f16", sv[gt][keep]))
+            ws.append((far_weight, sv[gt][keep]) if far_weight == "f16" else ("bf16", None))
         if idx.shape[1]:
             tok = (idx[gt][:, None].astype(np.int64) * leaf + ar[None, :]).reshape(-1)
             sc = (qb[t].astype(np.float64) @ kb[tok].astype(np.float64).T).astype(F32)
@@ -633,7 +655,7 @@ def tile_attention_fp8(qt, qb, dqh, gq, sg, lz, vq, sv, excl, idx, kb, vbf, leaf
 
 
 def tile_attention_fp8_ordered(qt, qb, dqh, gq, sg, lz, vq, sv, excl, idx, kb, vbf, leaf, scale, tail=None,
-                               splits=4, bn=64, group=1):
+                               splits=4, bn=64, group=1, far_weight="f16"):
     """The fp8 tile attention in the reference kernel's own order (splits, blocks of bn, float32 online
     softmax, weights rounded against the running maximum, split merge); idx in the reference's order.
     Pins the restatement against fixtures recorded from the reference."""
@@ -672,7 +694,8 @@ def tile_attention_fp8_ordered(qt, qb, dqh, gq, sg, lz, vq, sv, excl, idx, kb, v
                 sc = ((sc * sg[gt][c][None, :]).astype(F32) + lz[gt][c][None, :]).astype(F32)
                 sc = np.where((excl[gt][c] == 0)[None, :], sc, F32(-np.inf))
                 svc = sv[gt][c]
-                m, l, acc = step(m, l, acc, sc, vq[gt][c], lambda p, svc=svc: f16_round((p * svc[None, :]).astype(F32)))
+                wf = (lambda p, svc=svc: f16_round((p * svc[None, :]).astype(F32))) if far_weight == "f16" else bf16_round
+                m, l, acc = step(m, l, acc, sc, vq[gt][c], wf)
             e_lo, e_hi = sp * eps, min(e_n, sp * eps + eps)
             for e0 in range(e_lo, e_hi, bn):
                 j = np.arange(e0, min(e0 + bn, e_hi))
@@ -755,9 +778,9 @@ def flat_attention(q, k, v, *, tile=64, exact_leaves=256, leaf=64, scale=None, s
         mu = group_centres(qt, group)
     g, lz, vbf = leaf_stats(mu, k if k_stats is None else k_stats, v if v_stats is None else v_stats, leaf, scale,
                             precision)
-    if store == "fp8":
+    if store in ("fp8", "bf16"):
         return _flat_fp8(qt, mu, g, lz, vbf, k, v, n, leaf, scale, exact_leaves, sink_leaves, tail, group, perm,
-                         return_stages)
+                         return_stages, store=store)
     g8, sg, vb = state_int8(g, vbf)
     mu_t = mu[np.arange(qt.shape[0]) // group]
     q8, sq, dq8, sdq = query_codes(qt, mu_t, q_block=bool(qk_scale_block))
@@ -786,18 +809,28 @@ def flat_attention(q, k, v, *, tile=64, exact_leaves=256, leaf=64, scale=None, s
                           sq=sq, dq8=dq8, sdq=sdq, sel=sel, idx=idx, excl=excl, perm=perm, q=q_caller, cv=cv, dd=dd)
 
 
-def _flat_fp8(qt, mu, g, lz, vbf, kb, vb, n, leaf, scale, exact_leaves, sink_leaves, tail, group, perm, return_stages):
-    """store="fp8" after the leaf statistics: e4m3 state, fp16 far field, bf16 near field."""
-    gq, sg, vq, sv = state_fp8(g, vbf)
+def _flat_fp8(qt, mu, g, lz, vbf, kb, vb, n, leaf, scale, exact_leaves, sink_leaves, tail, group, perm, return_stages,
+              store="fp8"):
+    """store="fp8" after the leaf statistics: e4m3 state, fp16 far field, bf16 near field; store="bf16": the
+    bf16 state without scales, bf16 far and near fields."""
     mu_t = mu[np.arange(qt.shape[0]) // group]
-    qb, dqh = query_codes_fp8(qt, mu_t)
+    if store == "bf16":
+        gq, vq = state_bf16(g, vbf)
+        sg = np.ones(np.asarray(lz).shape, F32)
+        sv = sg
+        qb, dqh = query_codes_bf16(qt, mu_t)
+        far_weight = "bf16"
+    else:
+        gq, sg, vq, sv = state_fp8(g, vbf)
+        qb, dqh = query_codes_fp8(qt, mu_t)
+        far_weight = "f16"
     nb = kb.shape[0] // leaf
     sink = max(0, min(int(sink_leaves), nb))
     kx = min(int(exact_leaves) + sink, nb)
     sel = rowmax_select_fp8(dqh, gq, sg, lz, group) if kx > 0 else np.zeros((mu.shape[0], nb), F32)
     idx, excl = route(sel, exact_leaves, sink)
     out, lse = tile_attention_fp8(qt, qb, dqh, gq, sg, lz, vq, sv, excl, idx, kb, vb, leaf, scale, tail=tail,
-                                  group=group)
+                                  group=group, far_weight=far_weight)
     out, lse = out[:n], lse[:n]
     if perm is not None:
         full, full_l = np.empty_like(out), np.empty_like(lse)

@@ -137,7 +137,9 @@ def _recorder(flat):
 
     def leaf_stats(mu, kf, vf, nb, scale, **kw):
         g, lz, vb, sg, sv = o_stats(mu, kf, vf, nb, scale, **kw)
-        ent = dict(mu=mu.clone(), g8=g.clone(), lz=lz.clone(), vb=vb.clone(), sg=sg.clone())
+        ent = dict(mu=mu.clone(), g8=g.clone(), lz=lz.clone(), vb=vb.clone())
+        if sg is not None:                         # int8 / fp8 store: slope row scales (bf16: none)
+            ent["sg"] = sg.clone()
         if sv is not None:                         # fp8 store: value row scales too
             ent["sv"] = sv.clone()
         rec["stats"].append(ent)
@@ -197,6 +199,9 @@ CASES = [
     # the fp8 (e4m3) leaf state with row scales (store="fp8"): fp16 far-field dots, bf16 near field
     dict(name="fp8_state", grid=(2, 16, 16), leaf=64, E=2, sink=0, tail=0, trim=23, seed=28, store="fp8"),
     dict(name="fp8_sink_tail", grid=(2, 16, 16), leaf=64, E=3, sink=1, tail=5, trim=0, seed=29, store="fp8"),
+    # the bf16 leaf state (store="bf16"): bf16 g and vbar without scales, bf16 far- and near-field dots
+    dict(name="bf16_state", grid=(2, 16, 16), leaf=64, E=2, sink=0, tail=0, trim=23, seed=30, store="bf16"),
+    dict(name="bf16_sink_tail", grid=(2, 16, 16), leaf=64, E=3, sink=1, tail=5, trim=0, seed=31, store="bf16"),
 ]
 
 
@@ -226,12 +231,19 @@ def run_case(flat, c):
     st = rec["stats"]
     ti = rec["tile"]
     fp8 = c.get("store") == "fp8"
+    bf16 = c.get("store") == "bf16"
     res = dict(q=q.float().numpy(), k=k.float().numpy(), v=v.float().numpy(),
                leaf=np.int64(c["leaf"]), exact_leaves=np.int64(c["E"]), sink_leaves=np.int64(c["sink"]),
                group=np.int64(c.get("group", 1)), tile=np.int64(c.get("tile", 64)),
-               mu=_cat(st, "mu").numpy(), sg=_cat(st, "sg").numpy(), lz=_cat(st, "lz").numpy(),
+               mu=_cat(st, "mu").numpy(), lz=_cat(st, "lz").numpy(),
                excl=_cat(ti, "excl").numpy().astype(np.uint8), out=out.float().numpy())
-    if fp8:
+    if "sg" in st[0]:
+        res["sg"] = _cat(st, "sg").numpy()
+    if bf16:
+        # bf16 state as its bit patterns; no INT8 keys, no scales
+        res.update(store=np.array("bf16"), g_bf16=_cat(st, "g8").view(torch.int16).numpy().view(np.uint16),
+                   vb_bf16=_cat(st, "vb").view(torch.int16).numpy().view(np.uint16))
+    elif fp8:
         # e4m3 state as its codes (bytes), with the row scales of g and vbar; no INT8 keys
         res.update(store=np.array("fp8"), g_e4m3=_cat(st, "g8").view(torch.uint8).numpy(),
                    vb_e4m3=_cat(st, "vb").view(torch.uint8).numpy(), sv=_cat(st, "sv").numpy())

@@ -306,6 +306,68 @@ def test_fp8_order_free_oracle_within_tolerance(golden_cases, case):
     assert np.abs(lse - z["lse"]).max() < 1e-4
 
 
+BF16_CASES = ["bf16_state", "bf16_sink_tail"]
+
+
+def _bf16_values(bits):
+    return (np.asarray(bits, np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def _bf16(z):
+    tail = (z["tail_k"], z["tail_v"]) if "tail_k" in z else None
+    out, lse, st = O.flat_attention(z["q"], z["k"], z["v"], leaf=int(z["leaf"]),
+                                    exact_leaves=int(z["exact_leaves"]), sink_leaves=int(z["sink_leaves"]),
+                                    tail=tail, return_stages=True, store="bf16")
+    return out, lse, st, tail
+
+
+@pytest.mark.parametrize("case", BF16_CASES)
+def test_bf16_state_matches_reference(golden_cases, case):
+    """store="bf16": g and vbar are the reference's bf16 values (its float32 statistics rounded once: at most
+    one bf16 step apart where the float64 restatement lands on the other side of a rounding boundary), the
+    selection to float32 rounding, the routing equal."""
+    z = golden_cases[case]
+    out, lse, st, _ = _bf16(z)
+    for mine, ref in ((st["gq"], z["g_bf16"]), (st["vq"], z["vb_bf16"])):
+        bits = mine.view(np.uint32) >> 16
+        diff = np.abs(bits.astype(np.int64) - ref.astype(np.int64))
+        assert diff.max() <= 1 and (diff == 0).mean() >= 0.999, (diff.max(), (diff != 0).sum())
+    assert "sg" not in z
+    assert np.allclose(st["sel"], z["sel"], rtol=0, atol=1e-3)
+    assert np.array_equal(st["excl"], z["excl"])
+    assert np.array_equal(np.sort(st["idx"], 1), np.sort(z["idx"], 1))
+
+
+@pytest.mark.parametrize("case", BF16_CASES)
+def test_bf16_ordered_restatement_matches_reference(golden_cases, case):
+    """The bf16-state tile attention in the reference kernel's order, fed the reference's own bf16 state,
+    reproduces its output to float32 accumulation-order error."""
+    z = golden_cases[case]
+    out, lse, st, tail = _bf16(z)
+    gq, vq = _bf16_values(z["g_bf16"]), _bf16_values(z["vb_bf16"])
+    qb, dqb = O.query_codes_bf16(st["qt"], z["mu"])
+    one = np.ones(z["lz"].shape, np.float32)
+    assert np.allclose(O.rowmax_select_bf16(dqb, gq, z["lz"]), z["sel"], rtol=0, atol=2e-5)
+    o, l = O.tile_attention_fp8_ordered(st["qt"], qb, dqb, gq, one, z["lz"], vq, one, z["excl"], z["idx"],
+                                        O.bf16_round(z["k"]), O.bf16_round(z["v"]), int(z["leaf"]),
+                                        1.0 / np.sqrt(z["q"].shape[1]), tail=tail, far_weight="bf16")
+    n = z["q"].shape[0]
+    # the float32 exponentials may differ in the last bit, which moves a bf16-rounded weight by one bf16 step
+    # (2^-8 relative) where it sits on a rounding boundary: a few elements, bounded by that step
+    err = np.abs(o[:n] - z["out"])
+    assert (err < 5e-5).mean() >= 0.999 and err.max() < 2e-3, (err.max(), (err >= 5e-5).sum())
+    assert np.abs(l[:n] - z["lse"]).max() < 5e-5
+
+
+@pytest.mark.parametrize("case", BF16_CASES)
+def test_bf16_order_free_oracle_within_tolerance(golden_cases, case):
+    """The order-free bf16-state oracle stays within the bf16-weight rounding of the reference."""
+    z = golden_cases[case]
+    out, lse, _, _ = _bf16(z)
+    assert np.abs(out - z["out"]).max() < 1e-2
+    assert np.abs(lse - z["lse"]).max() < 1e-4
+
+
 def test_e4m3_codes_round_trip():
     c = np.arange(256, dtype=np.uint8)
     c = c[(c & 0x7F) != 0x7F]                       # 0x7F / 0xFF are NaN in e4m3fn
