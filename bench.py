@@ -72,9 +72,9 @@ def parse():
     ap.add_argument("--ref-steps", type=int, default=3, help="layers timed for the reference's GPU operator")
     ap.add_argument("--no-ref-cpu", action="store_true",
                     help="skip timing the reference's own CPU implementations (torch backend, NumPy model)")
-    ap.add_argument("--store", default="int8", choices=["int8", "fp8"],
-                    help="far-field state: int8 (the production path, the headline) or fp8 (e4m3 state, store='fp8'; "
-                         "no oracle sample)")
+    ap.add_argument("--store", default="int8", choices=["int8", "fp8", "bf16"],
+                    help="far-field state: int8 (the production path, the headline), fp8 (e4m3 state, store='fp8') "
+                         "or bf16 (store='bf16'); the last two without the oracle sample")
     ap.add_argument("--precision", default="tf32", choices=["tf32", "fp32"],
                     help="leaf-statistics dots: tf32 operands (PROD's setting, the reference's production path; the "
                          "default) or float32-accurate")
@@ -513,7 +513,8 @@ def run_ours(a, wl, rank, world, local_rank):
     lse = [torch.empty((n,), dtype=torch.float32, device=dev) for _ in range(nslots)]
     from htrc_b200 import _lib as _L
     store = _L.STORES[a.store]
-    fp8 = store == _L.STORE_FP8
+    fp8 = store != _L.STORE_INT8           # the operand-form state paths (fp8 or bf16)
+    bf16_state = store == _L.STORE_BF16
     prec = F.precision_code(a.precision, a.division)
     prec_ieee = F.precision_code(a.precision, "ieee")
     prec_ref = F.precision_code(a.precision, "triton")
@@ -769,9 +770,10 @@ def run_ours(a, wl, rank, world, local_rank):
     if rank == 0 and world == 1 and not a.no_modes:
         from htrc_b200 import runner as R
         modes = {}
-        for mode in list(R.MODES) + ["fast+iso", "fast+fp8", "fast+leaf32", "fast+leaf16"]:
+        for mode in list(R.MODES) + ["fast+iso", "fast+fp8", "fast+bf16", "fast+leaf32", "fast+leaf16"]:
             extra = {"fast+iso": dict(backend="cuda", curvature="iso"), "fast+fp8": dict(store="fp8"),
-                     "fast+leaf32": dict(leaf=32), "fast+leaf16": dict(leaf=16)}.get(mode, {})
+                     "fast+bf16": dict(store="bf16"), "fast+leaf32": dict(leaf=32),
+                     "fast+leaf16": dict(leaf=16)}.get(mode, {})
             r = R.FlatRunner(n, m, mode=mode.split("+")[0], device=dev, **{"leaf": 64, **extra})
             if r.graph is None:
                 modes[mode] = f"graph capture failed: {r.graph_error}"
@@ -812,7 +814,8 @@ def run_ours(a, wl, rank, world, local_rank):
                  "note": "head 0 of the workload through FlatRunner (CUDA graph) per mode of "
                          "h3/htrc_flat_runner.py:48-53: fast E=256, balanced E=512, accurate E=1024 + k-means, "
                          "max E=1024 + k-means + 32-row tiles; fast+iso: fast with the isotropic curvature term; "
-                         "fast+fp8: fast with the e4m3 far-field state (store='fp8'); fast+leaf32 / fast+leaf16: "
+                         "fast+fp8: fast with the e4m3 far-field state (store='fp8'); fast+bf16: with the bf16 "
+                         "far-field state (store='bf16'); fast+leaf32 / fast+leaf16: "
                          "fast with leaves of 32 / 16 keys (E=256 leaves, so 8,192 / 4,096 exact keys per tile; leaf "
                          "16 is the default of the reference's runner); the others leaf 64"}
 
@@ -850,6 +853,10 @@ def run_ours(a, wl, rank, world, local_rank):
     if fp8:
         stage_bytes["prep"] = n * 2 * 128 + npad * 2 * 2 * 128                  # bf16 q read; bf16 + fp16 rows
         stage_bytes["stats"] = nt * nb * (128 + 128) + 3 * nt * pitch * 4       # g + vbar codes, sg/sv/lz
+        stage_bytes["rowmax"] = nt * nb * 128 + 2 * nt * pitch * 4 + nt * pitch * 4
+    if bf16_state:
+        stage_bytes["stats"] = nt * nb * (256 + 256) + nt * pitch * 4           # bf16 g + vbar, lz
+        stage_bytes["rowmax"] = nt * nb * 256 + nt * pitch * 4 + nt * pitch * 4  # bf16 g + lz read, sel written
     stage_roof = {nm: {"bound": "hbm", "bytes": b_, "achieved_gbs": b_ / (stage_ms[nm] * 1e-3) / 1e9,
                        "frac": b_ / (stage_ms[nm] * 1e-3) / 1e9 / hbm}
                   for nm, b_ in stage_bytes.items()}
@@ -860,17 +867,19 @@ def run_ours(a, wl, rank, world, local_rank):
         line = {"metric": METRIC, "value": ms, "unit": "ms/layer", "n_gpus": world, "steps": a.steps,
                 "warmup": a.warmup, "ms_per_step": ms_step, "higher_is_better": False, "scaling": "strong",
                 "vs_baseline": None,
-                "dtype": ("fp8 (e4m3) state; fp16 far / bf16 near QK and PV, f32 softmax" if fp8 else
+                "dtype": ("bf16 state; bf16 QK and PV, f32 softmax" if bf16_state else
+                          "fp8 (e4m3) state; fp16 far / bf16 near QK and PV, f32 softmax" if fp8 else
                           "int8 QK + bf16 PV, f32 softmax"),
                 "data": "synthetic: seeded smooth-field Q/K (4x8x8 grid trilinear + 0.5 noise, RMS 3), N(0,1) V, bf16",
-                "config": {"workload": wl["name"].replace("INT8", "fp8 (e4m3) state") if fp8 else wl["name"],
+                "config": {"workload": (wl["name"].replace("INT8", "bf16 state") if bf16_state else
+                                        wl["name"].replace("INT8", "fp8 (e4m3) state") if fp8 else wl["name"]),
                            "tokens": n, "heads": H, "cfg_batch": batch, "blocks_resident": nblocks,
                            "dim": 128, "leaf": 64, "tile": 64, "store": a.store,
                            "exact_leaves": E, "precision": a.precision, "division": a.division, "pairs_per_gpu": nslots,
                            "layers_per_step": layers_per_step,
                            "head_streams": a.streams,
                            "l2": "inputs larger than L2: 2.4 GB of distinct q/k/v per layer, "
-                                 + ("1.0" if fp8 else "1.6") + " GB leaf state per head",
+                                 + ("2.1" if bf16_state else "1.0" if fp8 else "1.6") + " GB leaf state per head",
                            "parallelism": f"(batch, head) pairs/{world}" +
                                           (" + bf16 output all_gather (NCCL)" if world > 1 else "")},
                 "stage_ms_per_head": stage_ms, "stage_timing": stage_timing, "stage_roofline": stage_roof,

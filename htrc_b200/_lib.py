@@ -14,8 +14,8 @@ HTRC_OK, HTRC_ERR_ARG, HTRC_ERR_UNSUPPORTED, HTRC_ERR_WORKSPACE, HTRC_ERR_CUDA, 
 DTYPE_F32, DTYPE_BF16 = 0, 1
 ORDER_SEQ, ORDER_KMEANS = 0, 1
 CURV_LIN, CURV_ISO = 0, 1
-STORE_INT8, STORE_FP8 = 0, 1
-STORES = {"int8": STORE_INT8, "fp8": STORE_FP8}
+STORE_INT8, STORE_FP8, STORE_BF16 = 0, 1, 2
+STORES = {"int8": STORE_INT8, "fp8": STORE_FP8, "bf16": STORE_BF16}
 PREC_FP32, PREC_TF32, PREC_TRITON_DIV = 0, 1, 2      # flags, OR-ed
 PRECISIONS = {"fp32": PREC_FP32, "tf32": PREC_TF32}
 DIVISIONS = {"ieee": 0, "triton": PREC_TRITON_DIV}
@@ -70,6 +70,13 @@ SIGNATURES = {
     "htrc_rowmax_select_fp8": (ctypes.c_int, [_p, _i64, _i64, _i32, _p, _p, _p, _i64, _i32, _p, _p, _p]),
     "htrc_tile_attention_fp8": (ctypes.c_int, [_p, _p, _i64, _i32, _i64, _i64, _i32, _p, _p, _p, _p, _p, _p, _p, _i32,
                                                _i64, _p, _p, _i64, _i32, _i32, _f32, _p, _p, _p, _p, _p, _p, _p]),
+    # bf16 state (htrc_flat.h: qb, dqb / gb, vbb bf16; no scales)
+    "htrc_tile_prep_bf16": (ctypes.c_int, [_p, _i32, _i64, _i32, _i32, _p, _i32, _p, _p, _p, _p, _p, _i32, _p]),
+    "htrc_leaf_stats_bf16": (ctypes.c_int, [_p, _p, _i64, _i64, _i64, _p, _p, _i64, _i32, _i32, _f32, _p, _p, _p,
+                                            _i32, _p, _p]),
+    "htrc_rowmax_select_bf16": (ctypes.c_int, [_p, _i64, _i64, _i32, _p, _p, _i64, _i32, _p, _p, _p]),
+    "htrc_tile_attention_bf16": (ctypes.c_int, [_p, _p, _i64, _i32, _i64, _i64, _i32, _p, _p, _p, _p, _p, _i32, _i64,
+                                                _p, _p, _i64, _i32, _i32, _f32, _p, _p, _p, _p, _p, _p, _p]),
     "htrc_flat_forward_static_ws": (ctypes.c_int, [ctypes.POINTER(HtrcFlatArgs), _p]),
     "htrc_flat_static_ws_status": (ctypes.c_int, [ctypes.POINTER(_i32), _p]),
     "htrc_fake_quant": (ctypes.c_int, [_p, _i32, _i64, _i32, _i32, _i32, _p, _i32, _p]),

@@ -145,6 +145,8 @@ struct Layout {
   bool iso = false;
   size_t kn2 = 0, dd = 0, cv = 0;           // iso curvature: key norms, row offsets, coefficients
   bool fp8 = false;                         // fp8 state: q8 / dq8 hold bf16 / fp16 rows, vb the vbar codes
+  bool bf = false;                          // bf16 state: q8 / dq8 hold bf16 rows, g8 / vb bf16 values
+  bool opf = false;                         // fp8 or bf16 state: the operand-form kernels of fp8.cu
   size_t sv = 0, fpart = 0;
 };
 
@@ -159,8 +161,8 @@ int validate(const HtrcFlatArgs* a, bool need_ptrs) {
   if (a->group > kMaxGroup) return HTRC_ERR_ARG;
   if (a->order != HTRC_ORDER_SEQ && a->order != HTRC_ORDER_KMEANS) return HTRC_ERR_ARG;
   if (a->curvature != HTRC_CURV_LIN && a->curvature != HTRC_CURV_ISO) return HTRC_ERR_ARG;
-  if (a->store != HTRC_STORE_INT8 && a->store != HTRC_STORE_FP8) return HTRC_ERR_ARG;
-  if (a->store == HTRC_STORE_FP8 && a->curvature != HTRC_CURV_LIN) return HTRC_ERR_UNSUPPORTED;
+  if (a->store != HTRC_STORE_INT8 && a->store != HTRC_STORE_FP8 && a->store != HTRC_STORE_BF16) return HTRC_ERR_ARG;
+  if (a->store != HTRC_STORE_INT8 && a->curvature != HTRC_CURV_LIN) return HTRC_ERR_UNSUPPORTED;
   if (a->qk_scale_block != 0 && a->qk_scale_block != 64) return HTRC_ERR_ARG;
   if (a->qk_scale_block != 0 && a->store != HTRC_STORE_INT8) return HTRC_ERR_UNSUPPORTED;
   if (a->leaf != kLeaf &&
@@ -209,9 +211,11 @@ Layout layout_of(const HtrcFlatArgs* a) {
     return at;
   };
   L.fp8 = a->store == HTRC_STORE_FP8;
-  const size_t qes = L.fp8 ? 2 : 1;         // bytes per value of the query operands
+  L.bf = a->store == HTRC_STORE_BF16;
+  L.opf = L.fp8 || L.bf;
+  const size_t qes = L.opf ? 2 : 1;         // bytes per value of the query operands
   L.status = take(256);
-  if (!L.fp8) {
+  if (!L.opf) {
     L.k8 = take(static_cast<size_t>(L.m) * 128);
     L.ks = take(static_cast<size_t>(L.m) * 4);
   }
@@ -220,17 +224,15 @@ Layout layout_of(const HtrcFlatArgs* a) {
   L.mu_lo = take(static_cast<size_t>(L.ng) * 128 * 2);
   L.q8 = take(static_cast<size_t>(L.nt) * 64 * 128 * qes);
   L.dq8 = take(static_cast<size_t>(L.nt) * 64 * 128 * qes);
-  if (!L.fp8) {
+  if (!L.opf) {
     L.sq = take(static_cast<size_t>(L.nt) * 64 * 4);
     L.sdq = take(static_cast<size_t>(L.nt) * 64 * 4);
   }
   L.tail = a->n_tail > 0 ? take(static_cast<size_t>(L.n) * 130 * 4) : 0;
-  L.g8 = take(static_cast<size_t>(gcm_rows) * L.nb * 128);
+  L.g8 = take(static_cast<size_t>(gcm_rows) * L.nb * (L.bf ? 256 : 128));
   L.vb = take(static_cast<size_t>(gcm_rows) * L.nb * (L.fp8 ? 128 : 256));
-  if (L.fp8) {
-    L.sv = take(static_cast<size_t>(gcm_rows) * L.pitch * 4);
-    if (L.kx < L.nb) L.fpart = take(static_cast<size_t>(L.n) * 130 * 4);   // far-field partial rows
-  }
+  if (L.fp8) L.sv = take(static_cast<size_t>(gcm_rows) * L.pitch * 4);
+  if (L.opf && L.kx < L.nb) L.fpart = take(static_cast<size_t>(L.n) * 130 * 4);   // far-field partial rows
   L.sg = take(static_cast<size_t>(gcm_rows) * L.pitch * 4);
   L.lz = take(static_cast<size_t>(gcm_rows) * L.pitch * 4);
   L.sel = take(static_cast<size_t>(L.tcm) * L.pitch * 4);
@@ -257,13 +259,38 @@ T* at(void* base, size_t off) {
 
 int check_device() { return device_info().ok ? HTRC_OK : HTRC_ERR_DEVICE; }
 
+// store: HTRC_STORE_INT8 / FP8 / BF16 (the g rows' element type: byte codes, or bf16 values)
 int stats_maps(LeafStatsMaps* mp, const uint16_t* mu_hi, const uint16_t* mu_lo, int64_t nt, const uint16_t* k,
-               const uint16_t* v, int64_t m, const void* g8, const void* vb, int64_t tc, int64_t nb, bool fp8) {
+               const uint16_t* v, int64_t m, const void* g8, const void* vb, int64_t tc, int64_t nb, int store) {
   mp->mu_hi = mu_hi;
   mp->mu_lo = mu_lo;
   mp->nt = nt;
   bool ok = map_rows_halves(&mp->k, k, m, 64) && map_rows_halves(&mp->v, v, m, 64) &&
-            map_state(&mp->g8, g8, tc, nb, false, 1, 128) && map_state(&mp->vb, vb, tc, nb, !fp8, 1, 128);
+            map_state(&mp->g8, g8, tc, nb, store == HTRC_STORE_BF16, 1, 128) &&
+            map_state(&mp->vb, vb, tc, nb, store != HTRC_STORE_FP8, 1, 128);
+  return ok ? HTRC_OK : HTRC_ERR_CUDA;
+}
+
+// the bf16 state's row-max operands: bf16 offsets and g as [2][rows][64] halves (box of 128 leaves)
+int rowmax_bf16_maps(RowmaxMaps* mp, const uint16_t* dqb, int64_t rows, const uint16_t* gb, const float* lz, int64_t tc,
+                     int64_t nb, int64_t pitch) {
+  bool ok = map_rows_halves(&mp->dq8, dqb, rows, 64) && map_state_halves(&mp->g8, gb, tc, nb, 128) &&
+            map_scalars(&mp->lz, lz, tc, nb, pitch, true, 128) && map_scalars(&mp->sg, lz, tc, nb, pitch, true, 128) &&
+            map_scalars(&mp->cv, lz, tc, nb, pitch, true, 128);
+  return ok ? HTRC_OK : HTRC_ERR_CUDA;
+}
+
+// the bf16 state's tile maps: g and vbar as [2][nb][64] halves per state row (box of 64 leaves); the scale maps
+// the kernel does not read point at lz
+int tile_bf16_maps(TileFp8Maps* mp, const uint16_t* qb, const uint16_t* dqb, int64_t rows, const uint16_t* gb,
+                   const uint16_t* vbb, const float* lz, const uint8_t* excl, int64_t tc, int64_t nb, int64_t pitch,
+                   const uint16_t* k, const uint16_t* v, int64_t m) {
+  bool ok = map_rows_halves(&mp->qb, qb, rows, 64) && map_rows_halves(&mp->dqh, dqb, rows, 64) &&
+            map_state_halves(&mp->graw, gb, tc, nb, 64) && map_state_halves(&mp->vraw, vbb, tc, nb, 64) &&
+            map_scalars(&mp->lz, lz, tc, nb, pitch, true, 64) && map_scalars(&mp->sg, lz, tc, nb, pitch, true, 64) &&
+            map_scalars(&mp->sv, lz, tc, nb, pitch, true, 64) &&
+            map_scalars(&mp->excl, excl, tc, nb, pitch, false, 64) && map_rows_halves(&mp->k, k, m, 64) &&
+            map_rows_halves(&mp->v, v, m, 64);
   return ok ? HTRC_OK : HTRC_ERR_CUDA;
 }
 
@@ -379,15 +406,15 @@ int htrc_flat_forward(const HtrcFlatArgs* a, htrc_stream_t stream) {
   float* dd = L.iso ? at<float>(ws, L.dd) : nullptr;
   float* cv = L.iso ? at<float>(ws, L.cv) : nullptr;
   float* sv = L.fp8 ? at<float>(ws, L.sv) : nullptr;
-  if (!L.fp8 && a->qk_scale_block)
+  if (!L.opf && a->qk_scale_block)
     launch_pack_blocks(a->k, HTRC_DTYPE_BF16, L.m, HTRC_ROUND_HALF_EVEN, k8, ks, kn2, st);
-  else if (!L.fp8)
+  else if (!L.opf)
     launch_pack_rows(a->k, HTRC_DTYPE_BF16, L.m, HTRC_ROUND_HALF_EVEN, k8, ks, kn2, st);
   if (perm && (rc = launch_kmeans_order(a->q, a->q_dtype, L.n, perm, at<void>(ws, L.km), st)) != HTRC_OK) return rc;
   const int trows = static_cast<int>(L.trows);
   launch_tile_prep(a->q, a->q_dtype, L.n, trows, perm, group, at<float>(ws, L.mu), mu_hi, mu_lo, q8, sq, dq8, sdq, dd,
-                   L.fp8, a->qk_scale_block != 0, (a->precision & HTRC_PREC_TF32) != 0,
-                   (a->precision & HTRC_PREC_TRITON_DIV) != 0, st);
+                   L.opf, a->qk_scale_block != 0, (a->precision & HTRC_PREC_TF32) != 0,
+                   (a->precision & HTRC_PREC_TRITON_DIV) != 0, st, L.bf);
   if (tail) launch_tail_partial(a->q, a->q_dtype, L.n, a->tail_k, a->tail_v, a->n_tail, scale, tail, st);
   if (cudaGetLastError() != cudaSuccess) return HTRC_ERR_CUDA;
   mark(1);
@@ -399,11 +426,12 @@ int htrc_flat_forward(const HtrcFlatArgs* a, htrc_stream_t stream) {
     const int64_t tc = std::min<int64_t>(gc * L.group, L.nt - t0);
     if (far) {
       LeafStatsMaps smp;
-      if ((rc = stats_maps(&smp, mu_hi, mu_lo, L.ng, a->k, a->v, L.m, g8, vb, gc, L.nb, L.fp8)) != HTRC_OK) return rc;
+      if ((rc = stats_maps(&smp, mu_hi, mu_lo, L.ng, a->k, a->v, L.m, g8, vb, gc, L.nb, a->store)) != HTRC_OK)
+        return rc;
       if ((rc = launch_leaf_stats(smp, sg, lz, L.pitch, g0, gc, nb, static_cast<int>(L.leaf), scale, kn2, cv, sv,
                                   status, device_info().sms,
                                   (a->precision & HTRC_PREC_TF32) != 0, (a->precision & HTRC_PREC_TRITON_DIV) != 0,
-                                  st)) != HTRC_OK)
+                                  st, L.bf)) != HTRC_OK)
         return rc;
     }
     mark(2 + 4 * chunk);
@@ -414,6 +442,15 @@ int htrc_flat_forward(const HtrcFlatArgs* a, htrc_stream_t stream) {
                                   reinterpret_cast<const uint8_t*>(g8), sg, lz, gc, L.nb, L.pitch)) != HTRC_OK)
           return rc;
         if ((rc = launch_rowmax_fp8(rmp, sel, L.pitch, t0, tc, nb, group, status, st)) != HTRC_OK) return rc;
+      }
+    } else if (far && L.bf) {
+      if (kx > 0) {
+        RowmaxMaps rmp;
+        if ((rc = rowmax_bf16_maps(&rmp, reinterpret_cast<const uint16_t*>(dq8), L.nt * 64,
+                                   reinterpret_cast<const uint16_t*>(g8), lz, gc, L.nb, L.pitch)) != HTRC_OK)
+          return rc;
+        if ((rc = launch_rowmax(rmp, nullptr, nullptr, sel, L.pitch, t0, tc, nb, group, status, st, true)) != HTRC_OK)
+          return rc;
       }
     } else if (far) {
       if (kx > 0) {
@@ -429,15 +466,18 @@ int htrc_flat_forward(const HtrcFlatArgs* a, htrc_stream_t stream) {
                         cudaMemcpyDeviceToDevice, st) != cudaSuccess)
       return HTRC_ERR_CUDA;
     mark(4 + 4 * chunk);
-    if (L.fp8) {
+    if (L.opf) {
       TileFp8Maps tmp;
-      if ((rc = tile_fp8_maps(&tmp, reinterpret_cast<const uint16_t*>(q8), reinterpret_cast<const uint16_t*>(dq8),
-                              L.nt * 64, reinterpret_cast<const uint8_t*>(g8), reinterpret_cast<const uint8_t*>(vb), lz,
-                              sg, sv, excl, gc, L.nb, L.pitch, a->k, a->v, L.m)) != HTRC_OK)
-        return rc;
+      rc = L.bf ? tile_bf16_maps(&tmp, reinterpret_cast<const uint16_t*>(q8), reinterpret_cast<const uint16_t*>(dq8),
+                                 L.nt * 64, reinterpret_cast<const uint16_t*>(g8), reinterpret_cast<const uint16_t*>(vb),
+                                 lz, excl, gc, L.nb, L.pitch, a->k, a->v, L.m)
+                : tile_fp8_maps(&tmp, reinterpret_cast<const uint16_t*>(q8), reinterpret_cast<const uint16_t*>(dq8),
+                                L.nt * 64, reinterpret_cast<const uint8_t*>(g8), reinterpret_cast<const uint8_t*>(vb), lz,
+                                sg, sv, excl, gc, L.nb, L.pitch, a->k, a->v, L.m);
+      if (rc != HTRC_OK) return rc;
       float* fpart = L.fpart ? at<float>(ws, L.fpart) : nullptr;
       if ((rc = launch_tile_fp8(tmp, idx, kx, nb, L.n, trows, t0, tc, group, scale, tail, perm, fpart, a->out, a->lse,
-                                status, st)) != HTRC_OK)
+                                status, st, L.bf)) != HTRC_OK)
         return rc;
       mark(5 + 4 * chunk);
       continue;
@@ -555,7 +595,7 @@ int htrc_leaf_stats(const uint16_t* mu_hi, const uint16_t* mu_lo, int64_t nt, in
   int rc = check_device();
   if (rc != HTRC_OK) return rc;
   LeafStatsMaps mp;
-  if ((rc = stats_maps(&mp, mu_hi, mu_lo, nt, k, v, n_keys, g8, vb, tc, nb, false)) != HTRC_OK) return rc;
+  if ((rc = stats_maps(&mp, mu_hi, mu_lo, nt, k, v, n_keys, g8, vb, tc, nb, HTRC_STORE_INT8)) != HTRC_OK) return rc;
   return launch_leaf_stats(mp, sg, lz, pitch_of(nb), t0, tc, static_cast<int>(nb), leaf, scale_of(scale), kn2, cv,
                            nullptr,
                            status, device_info().sms, (precision & HTRC_PREC_TF32) != 0,
@@ -591,7 +631,7 @@ int htrc_leaf_stats_fp8(const uint16_t* mu_hi, const uint16_t* mu_lo, int64_t nt
   int rc = check_device();
   if (rc != HTRC_OK) return rc;
   LeafStatsMaps mp;
-  if ((rc = stats_maps(&mp, mu_hi, mu_lo, nt, k, v, n_keys, g8, vb8, tc, nb, true)) != HTRC_OK) return rc;
+  if ((rc = stats_maps(&mp, mu_hi, mu_lo, nt, k, v, n_keys, g8, vb8, tc, nb, HTRC_STORE_FP8)) != HTRC_OK) return rc;
   return launch_leaf_stats(mp, sg, lz, pitch_of(nb), t0, tc, static_cast<int>(nb), kLeaf, scale_of(scale), nullptr,
                            nullptr,
                            sv, status, device_info().sms, (precision & HTRC_PREC_TF32) != 0,
@@ -645,6 +685,87 @@ int htrc_tile_attention_fp8(const uint16_t* qb, const uint16_t* dqh, int64_t n_q
   return launch_tile_fp8(mp, idx, kx, static_cast<int>(nb), n_queries, tile, t0, tc, static_cast<int>(g),
                          scale_of(scale), tail_part, perm, far_part, out, lse, status,
                          reinterpret_cast<cudaStream_t>(stream));
+}
+
+int htrc_tile_prep_bf16(const void* q, int32_t q_dtype, int64_t n_queries, int32_t dim, int32_t tile,
+                        const int32_t* perm, int32_t group, float* mu, uint16_t* mu_hi, uint16_t* mu_lo, uint16_t* qb,
+                        uint16_t* dqb, int32_t precision, htrc_stream_t stream) {
+  if (!q || !mu || !mu_hi || !mu_lo || !qb || !dqb || n_queries < 1) return HTRC_ERR_ARG;
+  if ((precision & ~(HTRC_PREC_TF32 | HTRC_PREC_TRITON_DIV)) != 0) return HTRC_ERR_ARG;
+  if (dim != kDim || (tile != kTile && tile != kTile / 2)) return HTRC_ERR_UNSUPPORTED;
+  if (q_dtype != HTRC_DTYPE_F32 && q_dtype != HTRC_DTYPE_BF16) return HTRC_ERR_ARG;
+  if (group > kMaxGroup) return HTRC_ERR_ARG;
+  int rc = check_device();
+  if (rc != HTRC_OK) return rc;
+  launch_tile_prep(q, q_dtype, n_queries, tile, perm, group, mu, mu_hi, mu_lo, reinterpret_cast<int8_t*>(qb), nullptr,
+                   reinterpret_cast<int8_t*>(dqb), nullptr, nullptr, true, false, (precision & HTRC_PREC_TF32) != 0,
+                   (precision & HTRC_PREC_TRITON_DIV) != 0, reinterpret_cast<cudaStream_t>(stream), true);
+  return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
+}
+
+int htrc_leaf_stats_bf16(const uint16_t* mu_hi, const uint16_t* mu_lo, int64_t nt, int64_t t0, int64_t tc,
+                         const uint16_t* k, const uint16_t* v, int64_t n_keys, int32_t dim, int32_t leaf, float scale,
+                         uint16_t* gb, float* lz, uint16_t* vbb, int32_t precision, int32_t* status,
+                         htrc_stream_t stream) {
+  if (!mu_hi || !mu_lo || !k || !v || !gb || !lz || !vbb) return HTRC_ERR_ARG;
+  if ((precision & ~(HTRC_PREC_TF32 | HTRC_PREC_TRITON_DIV)) != 0) return HTRC_ERR_ARG;
+  if (dim != kDim || leaf != kLeaf) return HTRC_ERR_UNSUPPORTED;
+  if (nt < 1 || t0 < 0 || tc < 1 || t0 + tc > nt || n_keys < leaf || n_keys % leaf) return HTRC_ERR_ARG;
+  const int64_t nb = n_keys / leaf;
+  if (nb > kMaxLeaves) return HTRC_ERR_UNSUPPORTED;
+  int rc = check_device();
+  if (rc != HTRC_OK) return rc;
+  LeafStatsMaps mp;
+  if ((rc = stats_maps(&mp, mu_hi, mu_lo, nt, k, v, n_keys, gb, vbb, tc, nb, HTRC_STORE_BF16)) != HTRC_OK) return rc;
+  return launch_leaf_stats(mp, nullptr, lz, pitch_of(nb), t0, tc, static_cast<int>(nb), kLeaf, scale_of(scale),
+                           nullptr, nullptr, nullptr, status, device_info().sms, (precision & HTRC_PREC_TF32) != 0,
+                           false, reinterpret_cast<cudaStream_t>(stream), true);
+}
+
+int htrc_rowmax_select_bf16(const uint16_t* dqb, int64_t t0, int64_t tc, int32_t group, const uint16_t* gb,
+                            const float* lz, int64_t nb, int32_t dim, float* sel, int32_t* status,
+                            htrc_stream_t stream) {
+  if (!dqb || !gb || !lz || !sel || t0 < 0 || tc < 1 || nb < 1) return HTRC_ERR_ARG;
+  const int64_t g = group > 1 ? group : 1;
+  if (g > kMaxGroup || t0 % g) return HTRC_ERR_ARG;
+  if (dim != kDim) return HTRC_ERR_UNSUPPORTED;
+  if (nb > kMaxLeaves) return HTRC_ERR_UNSUPPORTED;
+  int rc = check_device();
+  if (rc != HTRC_OK) return rc;
+  RowmaxMaps mp;
+  if ((rc = rowmax_bf16_maps(&mp, dqb, (t0 + tc) * 64, gb, lz, (tc + g - 1) / g, nb, pitch_of(nb))) != HTRC_OK)
+    return rc;
+  return launch_rowmax(mp, nullptr, nullptr, sel, pitch_of(nb), t0, tc, static_cast<int>(nb), static_cast<int>(g),
+                       status, reinterpret_cast<cudaStream_t>(stream), true);
+}
+
+int htrc_tile_attention_bf16(const uint16_t* qb, const uint16_t* dqb, int64_t n_queries, int32_t tile, int64_t t0,
+                             int64_t tc, int32_t group, const uint16_t* gb, const float* lz, const uint16_t* vbb,
+                             const uint8_t* excl, const int32_t* idx, int32_t kx, int64_t nb, const uint16_t* k,
+                             const uint16_t* v, int64_t n_keys, int32_t dim, int32_t leaf, float scale,
+                             const float* tail_part, const int32_t* perm, float* far_part, float* out, float* lse,
+                             int32_t* status, htrc_stream_t stream) {
+  if (!qb || !dqb || !k || !v || !out || n_queries < 1 || t0 < 0 || tc < 1) return HTRC_ERR_ARG;
+  const int64_t g = group > 1 ? group : 1;
+  if (g > kMaxGroup || t0 % g) return HTRC_ERR_ARG;
+  if (dim != kDim || leaf != kLeaf || (tile != kTile && tile != kTile / 2)) return HTRC_ERR_UNSUPPORTED;
+  if (nb < 1 || n_keys != nb * leaf || kx < 0 || kx > nb) return HTRC_ERR_ARG;
+  if (kx > kMaxRouted || nb > kMaxLeaves) return HTRC_ERR_UNSUPPORTED;
+  if (kx < nb && (!gb || !lz || !vbb || !excl || !far_part)) return HTRC_ERR_ARG;
+  if (kx > 0 && !idx) return HTRC_ERR_ARG;
+  const int64_t nt = (n_queries + tile - 1) / tile;
+  if (t0 + tc > nt) return HTRC_ERR_ARG;
+  int rc = check_device();
+  if (rc != HTRC_OK) return rc;
+  // unused state maps (everything routed) still need a valid address: point them at the keys
+  TileFp8Maps mp;
+  if ((rc = tile_bf16_maps(&mp, qb, dqb, nt * 64, gb ? gb : k, vbb ? vbb : v, lz ? lz : reinterpret_cast<const float*>(k),
+                           excl ? excl : reinterpret_cast<const uint8_t*>(k), (tc + g - 1) / g, nb, pitch_of(nb), k, v,
+                           n_keys)) != HTRC_OK)
+    return rc;
+  return launch_tile_fp8(mp, idx, kx, static_cast<int>(nb), n_queries, tile, t0, tc, static_cast<int>(g),
+                         scale_of(scale), tail_part, perm, far_part, out, lse, status,
+                         reinterpret_cast<cudaStream_t>(stream), true);
 }
 
 int htrc_rowmax_select(const int8_t* dq8, const float* sdq, const float* dd, int64_t t0, int64_t tc, int32_t group,

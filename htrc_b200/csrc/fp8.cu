@@ -258,6 +258,9 @@ int launch_rowmax_fp8(const RowmaxFp8Maps& maps, float* sel, int64_t pitch, int6
 
 // ================================================================================================
 // Tile attention, in two passes over the tiles of a chunk that share one kernel body:
+// (BF: the bf16 state, store="bf16", h3/htrc_flat_triton.py:139-140 and :154 with DOT=1 -- the far pass lands g and
+// vbar as bf16 operands directly, logit = (bf16 dq . g) + lz and weights bf16(p); the converting warps only hand
+// the landed blocks on.  The near pass is the same for both states.)
 //   FAR:  the far field alone (blocks of 64 leaves of the tile's state, fp16 from the codes), written as one
 //         partial (acc[128], m, l) per query row, like the tail partial;
 //   NEAR: the routed leaves (bf16 keys and values, by TMA), merged in the epilogue with the far partial and
@@ -328,7 +331,7 @@ static_assert(sizeof(Bars) <= 512, "barrier block");
 }  // namespace tfx
 }  // namespace
 
-template <int TROWS, bool FAR>
+template <int TROWS, bool FAR, bool BF = false>
 __global__ void __launch_bounds__(tfx::Cfg<FAR>::kThreads, 1)
     tile_fp8_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_graw,
                     const __grid_constant__ CUtensorMap tm_vraw, const __grid_constant__ CUtensorMap tm_lz,
@@ -416,14 +419,19 @@ __global__ void __launch_bounds__(tfx::Cfg<FAR>::kThreads, 1)
         if (leader) {
           uint32_t tx = 0;
           for (int x = 0; x < 2; ++x)
-            if (2 * p + x < total) tx += FAR ? kRawBytes + 3 * 256 + 64 : kOpBytes;
+            if (2 * p + x < total) tx += FAR ? (BF ? kOpBytes + 256 + 64 : kRawBytes + 3 * 256 + 64) : kOpBytes;
           uint64_t* bar = FAR ? &bars->xr_full[xs] : &bars->x_full[xs];
           mbar_arrive_expect_tx(bar, tx);
           for (int x = 0; x < 2; ++x) {
             const int j = 2 * p + x;
             if (j >= total) continue;
             uint8_t* xp = xsub(p, x);
-            if constexpr (FAR) {
+            if constexpr (FAR && BF) {
+              // the block's bf16 g as its operand (both halves), lz and the exclusion bytes
+              tma_load_4d(xp, &tm_graw, bar, 0, j * 64, 0, srow, pol_stream);
+              tma_load_2d(xp + kOpBytes, &tm_lz, bar, j * 64, srow, pol_stream);
+              tma_load_2d(xp + kOpBytes + 768, &tm_excl, bar, j * 64, srow, pol_stream);
+            } else if constexpr (FAR) {
               // the block's g codes into the upper half of its operand slot (converted there in place)
               tma_load_3d(xp + kOpBytes / 2, &tm_graw, bar, 0, j * 64, srow, pol_stream);
               tma_load_2d(xp + kOpBytes, &tm_lz, bar, j * 64, srow, pol_stream);
@@ -439,7 +447,7 @@ __global__ void __launch_bounds__(tfx::Cfg<FAR>::kThreads, 1)
       }
     } else if (warp == 1) {
       // ---------------------------------------------------------------- PV issuer
-      const uint32_t idesc = FAR ? idesc_f16(64, 128, false, true) : idesc_bf16(64, 128, false, true);
+      const uint32_t idesc = (FAR && !BF) ? idesc_f16(64, 128, false, true) : idesc_bf16(64, 128, false, true);
       int npv = 0;                    // steps whose PV MMAs were issued (and committed)
       for (int p = 0; p < np; ++p) {
         const int b = p & 3, g = p & 1, ys = p % C::kYP;
@@ -467,7 +475,7 @@ __global__ void __launch_bounds__(tfx::Cfg<FAR>::kThreads, 1)
     } else if (warp == 2) {
       // ---------------------------------------------------------------- QK issuer
       // QK(p) into S/P buffer p % 4 once PV(p - 4) freed it and the pair's X slot landed
-      const uint32_t idesc = FAR ? idesc_f16(64, 64, false, false) : idesc_bf16(64, 64, false, false);
+      const uint32_t idesc = (FAR && !BF) ? idesc_f16(64, 64, false, false) : idesc_bf16(64, 64, false, false);
       const uint32_t a0 = smem_u32(smem + C::kOffQ);
       bool ok = mbar_wait_warp(&bars->qd_full, 0, status, abort_flag);
       int nqk = 0;                    // steps whose QK MMAs were issued (and committed)
@@ -512,8 +520,10 @@ __global__ void __launch_bounds__(tfx::Cfg<FAR>::kThreads, 1)
           const uint8_t* par = xsub(p, x) + kOpBytes;
           const float* pf = reinterpret_cast<const float*>(par);
           const bool masked = j >= total || par[768 + i] != 0 || j * 64 + i >= nb;
-          cc[(cs_slot * 2 + x) * 64 + i] = make_float2(pf[64 + i] * kLog2e, masked ? -INFINITY : pf[i] * kLog2e);
-          cs[(cs_slot * 2 + x) * 64 + i] = masked ? 0.f : pf[128 + i];
+          // the bf16 state has no row scales: sg = sv = 1
+          cc[(cs_slot * 2 + x) * 64 + i] = make_float2(BF ? kLog2e : pf[64 + i] * kLog2e,
+                                                       masked ? -INFINITY : pf[i] * kLog2e);
+          cs[(cs_slot * 2 + x) * 64 + i] = masked ? 0.f : (BF ? 1.0f : pf[128 + i]);
         }
         fence_proxy_async_smem();             // generic reads of a slot that TMA refills
         mbar_arrive(&bars->x_empty[xs]);      // the raw parameters of this slot have been read
@@ -615,7 +625,7 @@ __global__ void __launch_bounds__(tfx::Cfg<FAR>::kThreads, 1)
         const float2 e = fma2(make_float2(lg[i], lg[i + 1]), esc2, negm2);
         const float2 pp = live ? make_float2(ex2(e.x), ex2(e.y)) : make_float2(0.f, 0.f);
         rs2[(i >> 1) & 3] = add2(rs2[(i >> 1) & 3], pp);
-        if constexpr (FAR) {
+        if constexpr (FAR && !BF) {
           // far weights fp16(p * sv), as the reference's (p * sv).to(fp16) on the vbar codes
           const float2 w = mul2(pp, *reinterpret_cast<const float2*>(sv + i));
           pw[i >> 1] = pack_f16x2(w.x, w.y);
@@ -741,9 +751,11 @@ __global__ void __launch_bounds__(tfx::Cfg<FAR>::kThreads, 1)
       for (int p = 0; p < np; ++p) {
         const int xs = p % C::kXP;
         if (!mbar_wait_warp(&bars->xr_full[xs], (p / C::kXP) & 1, status, abort_flag)) break;
-        codes_to_f16_in_place(smem_u32(xsub(p, 0)), row);
-        codes_to_f16_in_place(smem_u32(xsub(p, 1)), row);
-        fence_proxy_async_smem();        // the fp16 operand is read by the tensor cores (async proxy)
+        if constexpr (!BF) {
+          codes_to_f16_in_place(smem_u32(xsub(p, 0)), row);
+          codes_to_f16_in_place(smem_u32(xsub(p, 1)), row);
+          fence_proxy_async_smem();      // the fp16 operand is read by the tensor cores (async proxy)
+        }
         mbar_arrive(&bars->x_full[xs]);
       }
     } else {
@@ -759,10 +771,14 @@ __global__ void __launch_bounds__(tfx::Cfg<FAR>::kThreads, 1)
             !mbar_wait_warp(&bars->pv_done[(p - C::kYP) & 3], ((p - C::kYP) >> 2) & 1, status, abort_flag))
           return false;
         if (leader) {
-          mbar_arrive_expect_tx(&bars->yr_full[ys], 2 * kRawBytes);
-          for (int x = 0; x < 2; ++x)
-            tma_load_3d(ysub(p, x) + kOpBytes / 2, &tm_vraw, &bars->yr_full[ys], 0, (2 * p + x) * 64, srow,
-                        pol_stream);
+          mbar_arrive_expect_tx(&bars->yr_full[ys], 2 * (BF ? kOpBytes : kRawBytes));
+          for (int x = 0; x < 2; ++x) {
+            if constexpr (BF)     // the bf16 vbar block as its operand (both halves)
+              tma_load_4d(ysub(p, x), &tm_vraw, &bars->yr_full[ys], 0, (2 * p + x) * 64, 0, srow, pol_stream);
+            else
+              tma_load_3d(ysub(p, x) + kOpBytes / 2, &tm_vraw, &bars->yr_full[ys], 0, (2 * p + x) * 64, srow,
+                          pol_stream);
+          }
         }
         __syncwarp();
         return true;
@@ -772,9 +788,11 @@ __global__ void __launch_bounds__(tfx::Cfg<FAR>::kThreads, 1)
         if (!load(p + 2)) break;
         const int ys = p % C::kYP;
         if (!mbar_wait_warp(&bars->yr_full[ys], (p / C::kYP) & 1, status, abort_flag)) break;
-        codes_to_f16_in_place(smem_u32(ysub(p, 0)), row);
-        codes_to_f16_in_place(smem_u32(ysub(p, 1)), row);
-        fence_proxy_async_smem();
+        if constexpr (!BF) {
+          codes_to_f16_in_place(smem_u32(ysub(p, 0)), row);
+          codes_to_f16_in_place(smem_u32(ysub(p, 1)), row);
+          fence_proxy_async_smem();
+        }
         mbar_arrive(&bars->y_full[ys]);
       }
     }
@@ -786,12 +804,12 @@ __global__ void __launch_bounds__(tfx::Cfg<FAR>::kThreads, 1)
 }
 
 namespace {
-template <bool FAR>
+template <bool FAR, bool BF>
 int set_tile_attr() {
   using C = tfx::Cfg<FAR>;
-  bool ok = cudaFuncSetAttribute(tile_fp8_kernel<64, FAR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  bool ok = cudaFuncSetAttribute(tile_fp8_kernel<64, FAR, BF>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  C::kSmemBytes) == cudaSuccess &&
-            cudaFuncSetAttribute(tile_fp8_kernel<32, FAR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            cudaFuncSetAttribute(tile_fp8_kernel<32, FAR, BF>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  C::kSmemBytes) == cudaSuccess;
   return ok ? HTRC_OK : HTRC_ERR_CUDA;
 }
@@ -799,21 +817,24 @@ int set_tile_attr() {
 
 int launch_tile_fp8(const TileFp8Maps& maps, const int32_t* idx, int kx, int nb, int64_t n, int tile_rows, int64_t t0,
                     int64_t tc, int group, float scale, const float* tail_part, const int32_t* perm, float* far_part,
-                    float* out, float* lse, int* status, cudaStream_t st) {
+                    float* out, float* lse, int* status, cudaStream_t st, bool bf16_state) {
   if (kx > tfx::kMaxKx || nb > 65535) return HTRC_ERR_UNSUPPORTED;
   if (kx < nb && far_part == nullptr) return HTRC_ERR_ARG;
   static bool attr_done[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr_done[dev]) {
-    if (set_tile_attr<true>() != HTRC_OK || set_tile_attr<false>() != HTRC_OK) return HTRC_ERR_CUDA;
+    if (set_tile_attr<true, false>() != HTRC_OK || set_tile_attr<false, false>() != HTRC_OK ||
+        set_tile_attr<true, true>() != HTRC_OK)
+      return HTRC_ERR_CUDA;
     attr_done[dev] = true;
   }
   const int g = group > 1 ? group : 1;
   const unsigned grid = static_cast<unsigned>(tc);
   if (kx < nb) {
     // the far field (all leaves not routed) first, as per-row partials
-    auto kf = tile_rows == 32 ? tile_fp8_kernel<32, true> : tile_fp8_kernel<64, true>;
+    auto kf = bf16_state ? (tile_rows == 32 ? tile_fp8_kernel<32, true, true> : tile_fp8_kernel<64, true, true>)
+                         : (tile_rows == 32 ? tile_fp8_kernel<32, true> : tile_fp8_kernel<64, true>);
     kf<<<grid, tfx::Cfg<true>::kThreads, tfx::Cfg<true>::kSmemBytes, st>>>(
         maps.dqh, maps.graw, maps.vraw, maps.lz, maps.sg, maps.sv, maps.excl, maps.k, maps.v, idx, kx, nb, n, t0, g,
         scale, nullptr, perm, far_part, nullptr, nullptr, status);

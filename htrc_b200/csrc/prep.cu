@@ -237,8 +237,8 @@ __global__ void __launch_bounds__(128) group_centre_kernel(const T* __restrict__
 // the centre.  qblock (an extension): one scale for the codes of all 64 held rows, from the tile's
 // abs-max (the held rows repeat real rows, so it is the maximum over the tile's queries); the offsets'
 // codes keep per-row scales.  FP8 (the fp8 state path, h3/htrc_flat_triton.py:103-109) writes instead the rows as bf16
-// (q8 holds uint16 bf16 rows) and the float32 offsets rounded once to fp16 (dq8 holds uint16 fp16 rows);
-// sq / sdq are not written.
+// (q8 holds uint16 bf16 rows) and the float32 offsets rounded once to fp16 (dq8 holds uint16 fp16 rows), or, with
+// dqbf (the bf16 state, :106-107), to bf16; sq / sdq are not written.
 template <typename T, bool FP8>
 __global__ void __launch_bounds__(128) tile_prep_kernel(const T* __restrict__ q, const int32_t* __restrict__ perm,
                                                         int64_t n, int trows, int group, float* __restrict__ mu,
@@ -246,7 +246,7 @@ __global__ void __launch_bounds__(128) tile_prep_kernel(const T* __restrict__ q,
                                                         int8_t* __restrict__ q8, float* __restrict__ sq,
                                                         int8_t* __restrict__ dq8, float* __restrict__ sdq,
                                                         float* __restrict__ dd, int qblock, uint32_t tmask,
-                                                        int tdiv) {
+                                                        int tdiv, int dqbf) {
   __shared__ float qs[64][129];
   __shared__ float mus[128];
   __shared__ float tmx[4];
@@ -304,7 +304,9 @@ __global__ void __launch_bounds__(128) tile_prep_kernel(const T* __restrict__ q,
     const int64_t gr = r0 + r;
     if constexpr (FP8) {
       reinterpret_cast<uint2*>(q8 + gr * 256)[lane] = make_uint2(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]));
-      reinterpret_cast<uint2*>(dq8 + gr * 256)[lane] = make_uint2(pack_f16x2(d[0], d[1]), pack_f16x2(d[2], d[3]));
+      reinterpret_cast<uint2*>(dq8 + gr * 256)[lane] =
+          dqbf ? make_uint2(pack_bf16x2(d[0], d[1]), pack_bf16x2(d[2], d[3]))
+               : make_uint2(pack_f16x2(d[0], d[1]), pack_f16x2(d[2], d[3]));
       continue;
     }
     float aq = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
@@ -335,7 +337,7 @@ __global__ void __launch_bounds__(128) tile_prep_kernel(const T* __restrict__ q,
 
 void launch_tile_prep(const void* q, int dtype, int64_t n, int tile_rows, const int32_t* perm, int group, float* mu,
                       uint16_t* mu_hi, uint16_t* mu_lo, int8_t* q8, float* sq, int8_t* dq8, float* sdq, float* dd,
-                      bool fp8, bool qblock, bool tf32, bool tdiv, cudaStream_t st) {
+                      bool fp8, bool qblock, bool tf32, bool tdiv, cudaStream_t st, bool dq_bf16) {
   const int tr = tile_rows == 32 ? 32 : 64;
   const uint32_t tmask = tf32 ? kTf32Mask : 0xFFFFFFFFu;
   const int64_t nt = (n + tr - 1) / tr;
@@ -346,13 +348,13 @@ void launch_tile_prep(const void* q, int dtype, int64_t n, int tile_rows, const 
     if (g > 1) group_centre_kernel<uint16_t><<<ng, 128, 0, st>>>(qb, perm, n, tr, nt, g, mu, mu_hi, mu_lo, tmask);
     auto k = fp8 ? tile_prep_kernel<uint16_t, true> : tile_prep_kernel<uint16_t, false>;
     k<<<static_cast<unsigned>(nt), 128, 0, st>>>(qb, perm, n, tr, g, mu, mu_hi, mu_lo, q8, sq, dq8, sdq, dd,
-                                                 qblock ? 1 : 0, tmask, tdiv ? 1 : 0);
+                                                 qblock ? 1 : 0, tmask, tdiv ? 1 : 0, dq_bf16 ? 1 : 0);
   } else {
     const float* qf = static_cast<const float*>(q);
     if (g > 1) group_centre_kernel<float><<<ng, 128, 0, st>>>(qf, perm, n, tr, nt, g, mu, mu_hi, mu_lo, tmask);
     auto k = fp8 ? tile_prep_kernel<float, true> : tile_prep_kernel<float, false>;
     k<<<static_cast<unsigned>(nt), 128, 0, st>>>(qf, perm, n, tr, g, mu, mu_hi, mu_lo, q8, sq, dq8, sdq, dd,
-                                                 qblock ? 1 : 0, tmask, tdiv ? 1 : 0);
+                                                 qblock ? 1 : 0, tmask, tdiv ? 1 : 0, dq_bf16 ? 1 : 0);
   }
 }
 

@@ -9,28 +9,35 @@
 // state row (h3/htrc_flat.py:223-231) the CTA of tile t reads state row t / G and writes its own sel row;
 // the maximum over the group's tiles is taken by the routing kernel.  ISO adds the isotropic curvature
 // term c_l * |q_r - mu|^2 to every logit before the maximum (h3/htrc_flat.py:331-333).
+// BF: the bf16 state (store="bf16", h3/htrc_flat_triton.py:247-248 with DOT=1): SEL[t, l] = max_r (bf16(dq_r) . g_l)
+// + lz_l with bf16 g and dq as the operands of kind::f16 MMAs (no scales); a stage is the block's two 64-column
+// halves of g (32 KB), two stages, two CTAs per SM.
 #include "common.cuh"
 #include "kernels.cuh"
 
 namespace htrc {
 
 namespace {
-constexpr int kStages = 3;
-constexpr uint32_t kBlkBytes = 128 * 128;          // 128 leaves x 128 B of g8
-constexpr uint32_t kParBytes = 3 * 128 * 4;         // sg[128], lz[128], cv[128] (ISO)
-constexpr uint32_t kStageBytes = kBlkBytes + kParBytes;
-constexpr uint32_t kOffDq = 0;                      // 64 rows x 128 B
-constexpr uint32_t kOffSdq = kOffDq + 64 * 128;     // 64 floats, then dd[64] (ISO)
-constexpr uint32_t kOffStage = kOffSdq + 1024;      // 1024-aligned
-constexpr uint32_t kOffBar = kOffStage + kStages * ((kStageBytes + 1023) / 1024 * 1024);
-constexpr uint32_t kStageStride = (kStageBytes + 1023) / 1024 * 1024;
-constexpr uint32_t kSmemBytes = kOffBar + 256 + 1024;
+constexpr int kMaxStages = 3;
 constexpr uint32_t kTmemCols = 128;
+template <bool BF>
+struct RLay {
+  static constexpr int kStages = BF ? 2 : 3;
+  static constexpr uint32_t kBlkBytes = (BF ? 2 : 1) * 128 * 128;     // 128 leaves x 128 B of g8 (BF: 2 halves)
+  static constexpr uint32_t kParBytes = 3 * 128 * 4;                 // sg[128], lz[128], cv[128] (ISO)
+  static constexpr uint32_t kStageBytes = kBlkBytes + kParBytes;
+  static constexpr uint32_t kOffDq = 0;                              // 64 rows x 128 B (BF: 2 halves)
+  static constexpr uint32_t kOffSdq = kOffDq + (BF ? 2 : 1) * 64 * 128;   // 64 floats, then dd[64] (ISO)
+  static constexpr uint32_t kOffStage = kOffSdq + 1024;              // 1024-aligned
+  static constexpr uint32_t kStageStride = (kStageBytes + 1023) / 1024 * 1024;
+  static constexpr uint32_t kOffBar = kOffStage + kStages * kStageStride;
+  static constexpr uint32_t kSmemBytes = kOffBar + 256 + 1024;
+};
 
 struct Bars {
   uint64_t dq_full;
-  uint64_t full[kStages];
-  uint64_t empty[kStages];
+  uint64_t full[kMaxStages];
+  uint64_t empty[kMaxStages];
   uint64_t acc_full[2];
   uint64_t acc_empty[2];
   uint32_t tmem_base;
@@ -38,16 +45,21 @@ struct Bars {
 };
 }  // namespace
 
-template <bool ISO>
+template <bool ISO, bool BF>
 __global__ void __launch_bounds__(192)
     rowmax_kernel(const __grid_constant__ CUtensorMap tm_dq8, const __grid_constant__ CUtensorMap tm_g8,
                   const __grid_constant__ CUtensorMap tm_sg, const __grid_constant__ CUtensorMap tm_lz,
                   const __grid_constant__ CUtensorMap tm_cv, const float* __restrict__ sdq,
                   const float* __restrict__ dd, float* __restrict__ sel, int64_t pitch, int64_t t0, int nb,
                   int group, int* status) {
+  using Y = RLay<BF>;
+  constexpr int kStages = Y::kStages;
+  constexpr uint32_t kBlkBytes = Y::kBlkBytes, kOffDq = Y::kOffDq, kOffSdq = Y::kOffSdq, kOffStage = Y::kOffStage;
+  constexpr uint32_t kStageStride = Y::kStageStride;
+  static_assert(!(ISO && BF), "the bf16 state has the linear far field");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  Bars* bars = reinterpret_cast<Bars*>(smem + kOffBar);
+  Bars* bars = reinterpret_cast<Bars*>(smem + Y::kOffBar);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tloc = blockIdx.x;
   const int srow = tloc / group;             // state row of this tile
@@ -77,14 +89,26 @@ __global__ void __launch_bounds__(192)
   if (warp == 0) {
     if (lane == 0) {
       const uint64_t pol_stream = policy_evict_first();
-      mbar_arrive_expect_tx(&bars->dq_full, 64 * 128 + 256 + (ISO ? 256 : 0));
-      tma_load_2d(smem + kOffDq, &tm_dq8, &bars->dq_full, 0, static_cast<int>(tg * 64), pol_stream);
-      bulk_load(smem + kOffSdq, sdq + tg * 64, 256, &bars->dq_full, pol_stream);
-      if (ISO) bulk_load(smem + kOffSdq + 256, dd + tg * 64, 256, &bars->dq_full, pol_stream);
+      if constexpr (BF) {
+        // bf16 offsets of the tile as two 64-column halves; no row scales
+        mbar_arrive_expect_tx(&bars->dq_full, 2 * 64 * 128);
+        tma_load_3d(smem + kOffDq, &tm_dq8, &bars->dq_full, 0, static_cast<int>(tg * 64), 0, pol_stream);
+      } else {
+        mbar_arrive_expect_tx(&bars->dq_full, 64 * 128 + 256 + (ISO ? 256 : 0));
+        tma_load_2d(smem + kOffDq, &tm_dq8, &bars->dq_full, 0, static_cast<int>(tg * 64), pol_stream);
+        bulk_load(smem + kOffSdq, sdq + tg * 64, 256, &bars->dq_full, pol_stream);
+        if (ISO) bulk_load(smem + kOffSdq + 256, dd + tg * 64, 256, &bars->dq_full, pol_stream);
+      }
       for (int j = 0; j < nblk; ++j) {
         const int s = j % kStages;
         if (j >= kStages && !mbar_wait(&bars->empty[s], ((j / kStages) - 1) & 1, status, abort_flag)) break;
         uint8_t* st = smem + kOffStage + s * kStageStride;
+        if constexpr (BF) {
+          mbar_arrive_expect_tx(&bars->full[s], kBlkBytes + 512);
+          tma_load_4d(st, &tm_g8, &bars->full[s], 0, j * 128, 0, srow, pol_stream);     // both halves
+          tma_load_2d(st + kBlkBytes + 512, &tm_lz, &bars->full[s], j * 128, srow, pol_stream);
+          continue;
+        }
         mbar_arrive_expect_tx(&bars->full[s], kBlkBytes + 1024 + (ISO ? 512 : 0));
         tma_load_3d(st, &tm_g8, &bars->full[s], 0, j * 128, srow, pol_stream);
         tma_load_2d(st + kBlkBytes, &tm_sg, &bars->full[s], j * 128, srow, pol_stream);
@@ -94,7 +118,7 @@ __global__ void __launch_bounds__(192)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc = idesc_i8(128, 64);
+      const uint32_t idesc = BF ? idesc_bf16(128, 64, false, false) : idesc_i8(128, 64);
       const uint32_t dq = smem_u32(smem + kOffDq);
       bool ok = mbar_wait(&bars->dq_full, 0, status, abort_flag);
       int nmma = 0;                   // blocks whose MMAs were issued (and committed)
@@ -104,9 +128,19 @@ __global__ void __launch_bounds__(192)
         if (j >= 2 && !mbar_wait(&bars->acc_empty[b], ((j >> 1) - 1) & 1, status, abort_flag)) break;
         tc_fence_after();
         const uint32_t gst = smem_u32(smem + kOffStage + s * kStageStride);
+        if constexpr (BF) {
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          mma_i8(tmem + 64 * b, sw128_desc(gst + kk * 32, 16, 1024), sw128_desc(dq + kk * 32, 16, 1024), idesc, kk != 0);
+          for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              mma_bf16(tmem + 64 * b, sw128_desc(gst + h * 16384 + kk * 32, 16, 1024),
+                       sw128_desc(dq + h * 8192 + kk * 32, 16, 1024), idesc, (h | kk) != 0);
+        } else {
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            mma_i8(tmem + 64 * b, sw128_desc(gst + kk * 32, 16, 1024), sw128_desc(dq + kk * 32, 16, 1024), idesc,
+                   kk != 0);
+          }
         }
         mma_commit(&bars->acc_full[b]);
         mma_commit(&bars->empty[s]);
@@ -135,7 +169,7 @@ __global__ void __launch_bounds__(192)
         tc_fence_before();
         mbar_arrive(&bars->acc_empty[b]);
         const uint8_t* st = smem + kOffStage + s * kStageStride;
-        const float sgl = reinterpret_cast<const float*>(st + kBlkBytes)[r];
+        const float sgl = BF ? 1.0f : reinterpret_cast<const float*>(st + kBlkBytes)[r];
         const float lzl = reinterpret_cast<const float*>(st + kBlkBytes + 512)[r];
         const float cvl = ISO ? reinterpret_cast<const float*>(st + kBlkBytes + 1024)[r] : 0.f;
         // the stage is refilled by TMA (async proxy) once this arrival lands: without the proxy fence the
@@ -146,6 +180,10 @@ __global__ void __launch_bounds__(192)
         float best = -INFINITY;
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
+          if constexpr (BF) {           // float32 accumulators: the logit is the dot itself
+            best = fmaxf(best, fmaxf(__uint_as_float(d0[i]), __uint_as_float(d1[i])));
+            continue;
+          }
           float a = __fmul_rn(static_cast<float>(static_cast<int>(d0[i])), __fmul_rn(sdq_s[i], sgl));
           float b = __fmul_rn(static_cast<float>(static_cast<int>(d1[i])), __fmul_rn(sdq_s[32 + i], sgl));
           if (ISO) {
@@ -166,20 +204,25 @@ __global__ void __launch_bounds__(192)
 }
 
 int launch_rowmax(const RowmaxMaps& maps, const float* sdq, const float* dd, float* sel, int64_t pitch, int64_t t0,
-                  int64_t tc, int nb, int group, int* status, cudaStream_t st) {
+                  int64_t tc, int nb, int group, int* status, cudaStream_t st, bool bf16_state) {
   static bool attr_done[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr_done[dev]) {
-    if (cudaFuncSetAttribute(rowmax_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
-            cudaSuccess ||
-        cudaFuncSetAttribute(rowmax_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess)
+    if (cudaFuncSetAttribute(rowmax_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             RLay<false>::kSmemBytes) != cudaSuccess ||
+        cudaFuncSetAttribute(rowmax_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             RLay<false>::kSmemBytes) != cudaSuccess ||
+        cudaFuncSetAttribute(rowmax_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             RLay<true>::kSmemBytes) != cudaSuccess)
       return HTRC_ERR_CUDA;
     attr_done[dev] = true;
   }
-  auto kernel = dd != nullptr ? rowmax_kernel<true> : rowmax_kernel<false>;
-  kernel<<<static_cast<unsigned>(tc), 192, kSmemBytes, st>>>(maps.dq8, maps.g8, maps.sg, maps.lz, maps.cv, sdq, dd, sel,
-                                                             pitch, t0, nb, group > 1 ? group : 1, status);
+  if (bf16_state && dd != nullptr) return HTRC_ERR_UNSUPPORTED;
+  auto kernel = bf16_state ? rowmax_kernel<false, true> : dd != nullptr ? rowmax_kernel<true, false> : rowmax_kernel<false, false>;
+  const uint32_t smem = bf16_state ? RLay<true>::kSmemBytes : RLay<false>::kSmemBytes;
+  kernel<<<static_cast<unsigned>(tc), 192, smem, st>>>(maps.dq8, maps.g8, maps.sg, maps.lz, maps.cv, sdq, dd, sel,
+                                                       pitch, t0, nb, group > 1 ? group : 1, status);
   return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;
 }
 

@@ -22,6 +22,8 @@
 // LEAF (64, 32 or 16 keys; INT8 state, linear far field) sets the leaf: a K/V stage still holds 64 keys, i.e.
 // 64 / LEAF leaves, and each leaf takes its own S (N = LEAF), softmax, [G | VB] (K = LEAF) and epilogue
 // (h3/htrc_flat.py:99-103: the reference takes any leaf that divides the key count, default 16).
+// BF stores the state as bf16 values without scales (store="bf16", h3/htrc_flat_triton.py:82-84): g = bf16(scale
+// G), vbar = bf16(VB), each staged as two 64-column boxes; its staging needs 32 KB more, so it runs four K/V stages.
 // FP8 stores the state as e4m3 codes with per-(centre, leaf) row scales instead (h3/htrc_flat_triton.py:65-72,
 // store="fp8"): sg = max(amax|g| * (1/448), 1e-30), g codes = e4m3(g / sg) rounded to nearest even and
 // saturated at 448, and the same for vbar with sv.
@@ -40,18 +42,24 @@ namespace htrc {
 
 namespace {
 constexpr int kThreads = 512;
-constexpr int kStages = 5;
+constexpr int kMaxStages = 5;
 constexpr uint32_t kLeafBytes = 64 * 128 * 2;       // K (or V) of one 64-token leaf
 constexpr uint32_t kStageBytes = 2 * kLeafBytes;    // K + V
 constexpr uint32_t kOffStage = 0;
-constexpr uint32_t kOffStG = kOffStage + kStages * kStageBytes;   // g8 staging: 128 rows x 128 B
-constexpr uint32_t kOffStV = kOffStG + 128 * 128;   // vbar staging: 2 x (128 rows x 128 B)
-constexpr uint32_t kOffAm = kOffStV + 2 * 128 * 128;  // row abs-max halves [2 (leaf parity)][2 (half)][128]
-constexpr uint32_t kOffB2 = kOffAm + 2 * 2 * 128 * 4;   // ISO: |G|^2 halves [2][2][128]
-constexpr uint32_t kOffAw = kOffB2 + 2 * 2 * 128 * 4;   // ISO: sum_s w_s |k_s|^2 [4 (leaf % 4)][128]
-constexpr uint32_t kOffKn = kOffAw + 4 * 128 * 4;       // ISO: key norms of each K/V stage [kStages][64]
-constexpr uint32_t kOffBar = kOffKn + kStages * 64 * 4;
-constexpr uint32_t kSmemBytes = kOffBar + 256 + 1024;  // + barriers, + alignment slack
+// shared-memory layout; BF (bf16 state) stages g as two boxes and runs one K/V stage fewer
+template <bool BF>
+struct SLay {
+  static constexpr int kStages = BF ? 4 : 5;
+  static constexpr uint32_t kOffStG = kOffStage + kStages * kStageBytes;   // g staging: 128 rows x 128 B (BF: x2)
+  static constexpr uint32_t kOffStV = kOffStG + (BF ? 2 : 1) * 128 * 128;  // vbar staging: 2 x (128 rows x 128 B)
+  static constexpr uint32_t kOffAm = kOffStV + 2 * 128 * 128;   // row abs-max halves [2 (leaf parity)][2 (half)][128]
+  static constexpr uint32_t kOffB2 = kOffAm + 2 * 2 * 128 * 4;  // ISO: |G|^2 halves [2][2][128]
+  static constexpr uint32_t kOffAw = kOffB2 + 2 * 2 * 128 * 4;  // ISO: sum_s w_s |k_s|^2 [4 (leaf % 4)][128]
+  static constexpr uint32_t kOffKn = kOffAw + 4 * 128 * 4;      // ISO: key norms of each K/V stage [kStages][64]
+  static constexpr uint32_t kOffBar = kOffKn + kStages * 64 * 4;
+  static constexpr uint32_t kSmemBytes = kOffBar + 256 + 1024;  // + barriers, + alignment slack
+  static_assert(kSmemBytes <= 232448, "shared memory per CTA");
+};
 
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0;      // two 64-column S buffers; W_hi / W_lo of the leaf then in 32 columns each
@@ -61,8 +69,8 @@ constexpr uint32_t kColMu = 384;   // mu_hi (64 columns of bf16 pairs), then mu_
 
 struct Bars {
   uint64_t mu_full;    // the 128 softmax threads stored their mu rows in TMEM
-  uint64_t kv_full[kStages];
-  uint64_t kv_empty[kStages];
+  uint64_t kv_full[kMaxStages];
+  uint64_t kv_empty[kMaxStages];
   uint64_t s_full[2];
   uint64_t s_empty[2];  // G/VB of the leaf done: its W (over S in TMEM) is consumed
   uint64_t w_full[2];   // the 128 softmax threads wrote W into the S buffer
@@ -94,7 +102,7 @@ __device__ __forceinline__ uint2 half_away_codes2(float2 y) {
 }
 }  // namespace
 
-template <bool ISO, bool FP8, bool TDIV, int LEAF>
+template <bool ISO, bool FP8, bool TDIV, int LEAF, bool BF = false>
 __global__ void __launch_bounds__(kThreads, 1)
     leaf_stats_kernel(const uint16_t* __restrict__ mu_hi_g, const uint16_t* __restrict__ mu_lo_g, int64_t nt,
                       const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
@@ -102,9 +110,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                       float* __restrict__ sg_out, float* __restrict__ lz_out, int64_t pitch, int64_t t0, int64_t tc,
                       int nb, int leaves_per_cta, float scale, const float* __restrict__ kn2,
                       float* __restrict__ cv_out, float* __restrict__ sv_out, int* status, uint32_t wmask) {
+  constexpr int kStages = SLay<BF>::kStages;
+  constexpr uint32_t kOffStG = SLay<BF>::kOffStG, kOffStV = SLay<BF>::kOffStV, kOffAm = SLay<BF>::kOffAm;
+  constexpr uint32_t kOffB2 = SLay<BF>::kOffB2, kOffAw = SLay<BF>::kOffAw, kOffKn = SLay<BF>::kOffKn;
+  static_assert(!BF || (!ISO && !FP8 && LEAF == 64), "the bf16 state: linear far field, leaf 64");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  Bars* bars = reinterpret_cast<Bars*>(smem + kOffBar);
+  Bars* bars = reinterpret_cast<Bars*>(smem + SLay<BF>::kOffBar);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int blk = blockIdx.x;                       // block of 128 centres (local to the chunk)
@@ -375,6 +387,51 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(&bars->gv_full, j & 1, status, abort_flag)) break;
       __syncwarp();
       tc_fence_after();
+      if constexpr (BF) {
+        // this half of G and VB (64 columns each) as bf16 pairs; TMEM is released at once
+        uint32_t gw[32], vw[32];
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tmem + lane_base + colg + 32 * c, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            gw[16 * c + i] = pack_bf16x2(__fmul_rn(__uint_as_float(r[2 * i]), scale),
+                                         __fmul_rn(__uint_as_float(r[2 * i + 1]), scale));
+          tmem_ld32(tmem + lane_base + colv + 32 * c, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) vw[16 * c + i] = pack_bf16x2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+        }
+        tc_fence_before();
+        mbar_arrive(&bars->gv_empty);
+        if (lead) {
+          bulk_wait_group_read0();
+          mbar_arrive(&bars->stg_free);
+        }
+        if (!mbar_wait(&bars->stg_free, j & 1, status, abort_flag)) break;
+        __syncwarp();
+        // this half is the 128-byte row of staging box `half` of g and of vbar
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          st_shared_v4(stg + half * (128 * 128) + sw128_off(row, c), gw[4 * c], gw[4 * c + 1], gw[4 * c + 2],
+                       gw[4 * c + 3]);
+          st_shared_v4(stv + half * (128 * 128) + sw128_off(row, c), vw[4 * c], vw[4 * c + 1], vw[4 * c + 2],
+                       vw[4 * c + 3]);
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&bars->stg_full);
+        if (lead) {
+          if (!mbar_wait(&bars->stg_full, j & 1, status, abort_flag)) break;
+          tma_store_3d(&tm_g8, smem + kOffStG, 0, leaf, blk * 128);
+          tma_store_3d(&tm_g8, smem + kOffStG + 128 * 128, 64, leaf, blk * 128);
+          tma_store_3d(&tm_vb, smem + kOffStV, 0, leaf, blk * 128);
+          tma_store_3d(&tm_vb, smem + kOffStV + 128 * 128, 64, leaf, blk * 128);
+          bulk_commit_group();
+        }
+        continue;
+      }
       if constexpr (FP8) {
         // this half of G and its abs-max, then the abs-max of this half of VB (read twice from TMEM, so that
         // only G stays in registers); the halves of a row exchange both through shared memory
@@ -560,7 +617,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 int launch_leaf_stats(const LeafStatsMaps& maps, float* sg, float* lz, int64_t pitch, int64_t t0, int64_t tc, int nb,
                       int leaf, float scale, const float* kn2, float* cv, float* sv, int* status, int num_sms,
-                      bool tf32, bool tdiv, cudaStream_t st) {
+                      bool tf32, bool tdiv, cudaStream_t st, bool bf16_state) {
   static bool attr_done[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -571,13 +628,17 @@ int launch_leaf_stats(const LeafStatsMaps& maps, float* sg, float* lz, int64_t p
                    leaf_stats_kernel<true, false, true, 64>, leaf_stats_kernel<false, true, true, 64>,
                    leaf_stats_kernel<false, false, false, 32>, leaf_stats_kernel<false, false, true, 32>,
                    leaf_stats_kernel<false, false, false, 16>, leaf_stats_kernel<false, false, true, 16>})
-      ok = ok && cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) == cudaSuccess;
+      ok = ok && cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SLay<false>::kSmemBytes) ==
+                     cudaSuccess;
+    ok = ok && cudaFuncSetAttribute(leaf_stats_kernel<false, false, false, 64, true>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, SLay<true>::kSmemBytes) == cudaSuccess;
     if (!ok) return HTRC_ERR_CUDA;
     attr_done[dev] = true;
   }
   if (sv != nullptr && cv != nullptr) return HTRC_ERR_UNSUPPORTED;
   if (leaf != 64 && leaf != 32 && leaf != 16) return HTRC_ERR_UNSUPPORTED;
   if (leaf != 64 && (sv != nullptr || cv != nullptr)) return HTRC_ERR_UNSUPPORTED;
+  if (bf16_state && (leaf != 64 || sv != nullptr || cv != nullptr)) return HTRC_ERR_UNSUPPORTED;
   const int bx = static_cast<int>((tc + 127) / 128);
   int by = max(1, num_sms / bx);                    // one wave: bx * by <= SMs
   by = min(by, nb);
@@ -586,7 +647,9 @@ int launch_leaf_stats(const LeafStatsMaps& maps, float* sg, float* lz, int64_t p
   lpc = (lpc + per_stage - 1) / per_stage * per_stage;
   by = (nb + lpc - 1) / lpc;
   decltype(&leaf_stats_kernel<false, false, false, 64>) kernel;
-  if (leaf == 32)
+  if (bf16_state)
+    kernel = leaf_stats_kernel<false, false, false, 64, true>;     // no division in its epilogue
+  else if (leaf == 32)
     kernel = tdiv ? leaf_stats_kernel<false, false, true, 32> : leaf_stats_kernel<false, false, false, 32>;
   else if (leaf == 16)
     kernel = tdiv ? leaf_stats_kernel<false, false, true, 16> : leaf_stats_kernel<false, false, false, 16>;
@@ -597,7 +660,8 @@ int launch_leaf_stats(const LeafStatsMaps& maps, float* sg, float* lz, int64_t p
                   : (sv != nullptr ? leaf_stats_kernel<false, true, false, 64>
                                    : (cv != nullptr ? leaf_stats_kernel<true, false, false, 64>
                                                     : leaf_stats_kernel<false, false, false, 64>));
-  kernel<<<dim3(bx, by), kThreads, kSmemBytes, st>>>(maps.mu_hi, maps.mu_lo, maps.nt, maps.k, maps.v, maps.g8, maps.vb,
+  const uint32_t smem = bf16_state ? SLay<true>::kSmemBytes : SLay<false>::kSmemBytes;
+  kernel<<<dim3(bx, by), kThreads, smem, st>>>(maps.mu_hi, maps.mu_lo, maps.nt, maps.k, maps.v, maps.g8, maps.vb,
                                                      sg, lz, pitch, t0, tc, nb, lpc, scale, kn2, cv, sv, status,
                                                      tf32 ? kTf32Mask : 0xFFFFFFFFu);
   return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA;

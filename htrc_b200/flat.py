@@ -107,9 +107,9 @@ def _check_args(q, k, v, tile, exact_leaves, order, curvature, leaf, select, bac
     if store in ("fp8", "int8") and (dot != "bf16" or select == "bound" or (quant or {}).get("state")):
         raise ValueError("store='fp8' needs dot='bf16', select='max' and no state fake-quant")
     if store not in _lib.STORES or dot != "bf16":
-        raise NotImplementedError("only the dot='bf16' paths with store='int8' (production) or store='fp8' are "
+        raise NotImplementedError("only the dot='bf16' paths with store='int8' (production), 'fp8' or 'bf16' are "
                                   "implemented")
-    if store == "fp8" and curvature != "lin":
+    if store in ("fp8", "bf16") and curvature != "lin":
         raise NotImplementedError("curvature='iso' is implemented on the INT8 path only")
     if int(tile) not in TILES or int(leaf) not in LEAVES:
         raise NotImplementedError(f"the kernels implement tile=64 or 32 and leaf=64, 32 or 16 (got tile={tile}, "
@@ -457,12 +457,13 @@ def run_stages(qd, kb, vb, tk=None, tv=None, *, exact_leaves, sink_leaves=0, til
     if int(leaf) not in LEAVES or (int(leaf) != LEAF and (store != _lib.STORE_INT8 or curvature != _lib.CURV_LIN
                                                             or qk_scale_block)):
         raise NotImplementedError(f"leaf={leaf}: leaves of 64, or 32 / 16 with the INT8 state and the linear far field")
-    if store == _lib.STORE_FP8:
+    if store in (_lib.STORE_FP8, _lib.STORE_BF16):
         if curvature != _lib.CURV_LIN:
             raise NotImplementedError("curvature='iso' is implemented on the INT8 path only")
         return _run_stages_fp8(qd, kb, vb, tk, tv, n=n, m=m, nt=nt, nb=nb, ng=ng, grp=grp, pitch=pitch, sink=sink,
                                kx=kx, sc=sc, qdt=qdt, tile=tile, tile_chunk=tile_chunk, exact_leaves=exact_leaves,
-                               order=order, s=s, tick=tick, e=e, precision=int(precision))
+                               order=order, s=s, tick=tick, e=e, precision=int(precision),
+                               bf16=store == _lib.STORE_BF16)
     r = dict(k8=e(m, DIM, dt=torch.int8), ks=e(m), mu=e(ng, DIM), mu_hi=e(ng, DIM, dt=torch.bfloat16),
              mu_lo=e(ng, DIM, dt=torch.bfloat16), q8=e(nt * TILE, DIM, dt=torch.int8), sq=e(nt * TILE),
              dq8=e(nt * TILE, DIM, dt=torch.int8), sdq=e(nt * TILE), g8=e(ng, nb, DIM, dt=torch.int8),
@@ -524,9 +525,15 @@ def run_stages(qd, kb, vb, tk=None, tv=None, *, exact_leaves, sink_leaves=0, til
 
 
 def _run_stages_fp8(qd, kb, vb, tk, tv, *, n, m, nt, nb, ng, grp, pitch, sink, kx, sc, qdt, tile, tile_chunk,
-                    exact_leaves, order, s, tick, e, precision):
+                    exact_leaves, order, s, tick, e, precision, bf16=False):
     """run_stages for the fp8 state (store="fp8"): tile prep with bf16 rows and fp16 offsets, e4m3 leaf
-    statistics, fp8 row-max selection, routing and the fp8 tile kernel."""
+    statistics, fp8 row-max selection, routing and the fp8 tile kernel.  bf16=True: the bf16 state
+    (store="bf16"): bf16 offsets (key "dqh" holds bf16 then), bf16 g / vbar values in "g8" / "vb8" (uint16
+    bit patterns viewed as bfloat16), no scales."""
+    if bf16:
+        return _run_stages_bf16(qd, kb, vb, tk, tv, n=n, m=m, nt=nt, nb=nb, ng=ng, grp=grp, pitch=pitch, sink=sink,
+                                kx=kx, sc=sc, qdt=qdt, tile=tile, tile_chunk=tile_chunk, exact_leaves=exact_leaves,
+                                order=order, s=s, tick=tick, e=e, precision=precision)
     L = lib()
     dev = qd.device
     r = dict(mu=e(ng, DIM), mu_hi=e(ng, DIM, dt=torch.bfloat16), mu_lo=e(ng, DIM, dt=torch.bfloat16),
@@ -572,6 +579,62 @@ def _run_stages_fp8(qd, kb, vb, tk, tv, *, n, m, nt, nb, ng, grp, pitch, sink, k
                                     ptr(r["lz"]), ptr(r["vb8"]), ptr(r["sv"]), ptr(r["excl"]), ptr(r["idx"]), kx, nb,
                                     ptr(kb), ptr(vb), m, DIM, LEAF, sc, ptr(tail_part), perm, ptr(r["far_part"]),
                                     ptr(r["out"]), ptr(r["lse"]), stp, s), "htrc_tile_attention_fp8")
+    tick("tile")
+    tick("finish")
+    r["kx"], r["nb"], r["pitch"], r["group"], r["tile"], r["leaf"] = kx, nb, pitch, grp, tile, LEAF
+    return r
+
+
+def _run_stages_bf16(qd, kb, vb, tk, tv, *, n, m, nt, nb, ng, grp, pitch, sink, kx, sc, qdt, tile, tile_chunk,
+                     exact_leaves, order, s, tick, e, precision):
+    """run_stages for the bf16 state (store="bf16"): tile prep with bf16 rows and bf16 offsets, bf16 leaf
+    statistics (no scales), bf16 row-max selection, routing and the bf16-state tile kernel.  Keys: qb, dqb, gb,
+    vbb (bfloat16), lz, sel, idx, excl, out, lse."""
+    L = lib()
+    dev = qd.device
+    r = dict(mu=e(ng, DIM), mu_hi=e(ng, DIM, dt=torch.bfloat16), mu_lo=e(ng, DIM, dt=torch.bfloat16),
+             qb=e(nt * TILE, DIM, dt=torch.bfloat16), dqb=e(nt * TILE, DIM, dt=torch.bfloat16),
+             gb=e(ng, nb, DIM, dt=torch.bfloat16), vbb=e(ng, nb, DIM, dt=torch.bfloat16),
+             lz=e(ng, pitch), sel=torch.zeros((nt, pitch), dtype=torch.float32, device=dev),
+             idx=e(ng, max(kx, 1), dt=torch.int32), excl=e(ng, pitch, dt=torch.uint8), out=e(n, DIM), lse=e(n),
+             status=torch.zeros((1,), dtype=torch.int32, device=dev), perm=None)
+    stp = ptr(r["status"])
+    if order == _lib.ORDER_KMEANS:
+        r["perm"] = e(n, dt=torch.int32)
+        nbytes = ctypes.c_size_t()
+        check(L.htrc_kmeans_scratch_size(n, nbytes), "htrc_kmeans_scratch_size")
+        scratch = torch.empty(int(nbytes.value), dtype=torch.uint8, device=dev)
+        check(L.htrc_kmeans_order(ptr(qd), qdt, n, DIM, ptr(r["perm"]), ptr(scratch), int(nbytes.value), s),
+              "htrc_kmeans_order")
+    perm = ptr(r["perm"])
+    check(L.htrc_tile_prep_bf16(ptr(qd), qdt, n, DIM, tile, perm, grp, ptr(r["mu"]), ptr(r["mu_hi"]), ptr(r["mu_lo"]),
+                                ptr(r["qb"]), ptr(r["dqb"]), precision, s), "htrc_tile_prep_bf16")
+    tail_part = None
+    if tk is not None:
+        tail_part = e(n, DIM + 2)
+        check(L.htrc_tail_partial(ptr(qd), qdt, n, DIM, ptr(tk), ptr(tv), int(tk.shape[0]), sc, ptr(tail_part), s),
+              "htrc_tail_partial")
+    tick("prep")
+    gstep = ng if not tile_chunk or tile_chunk <= 0 else min(max(1, int(tile_chunk) // grp), ng)
+    far = kx < nb
+    if far:
+        for g0 in range(0, ng, gstep):
+            gc = min(gstep, ng - g0)
+            check(L.htrc_leaf_stats_bf16(ptr(r["mu_hi"]), ptr(r["mu_lo"]), ng, g0, gc, ptr(kb), ptr(vb), m, DIM, LEAF,
+                                         sc, ptr(r["gb"][g0]), ptr(r["lz"][g0]), ptr(r["vbb"][g0]), precision, stp, s),
+                  "htrc_leaf_stats_bf16")
+    tick("stats")
+    if far and kx > 0:
+        check(L.htrc_rowmax_select_bf16(ptr(r["dqb"]), 0, nt, grp, ptr(r["gb"]), ptr(r["lz"]), nb, DIM,
+                                        ptr(r["sel"]), stp, s), "htrc_rowmax_select_bf16")
+    check(L.htrc_route(ptr(r["sel"]), nt, nb, int(exact_leaves), sink, grp, ptr(r["idx"]), ptr(r["excl"]), s),
+          "htrc_route")
+    tick("select")
+    r["far_part"] = e(n, DIM + 2) if far else None
+    check(L.htrc_tile_attention_bf16(ptr(r["qb"]), ptr(r["dqb"]), n, tile, 0, nt, grp, ptr(r["gb"]), ptr(r["lz"]),
+                                     ptr(r["vbb"]), ptr(r["excl"]), ptr(r["idx"]), kx, nb, ptr(kb), ptr(vb), m, DIM,
+                                     LEAF, sc, ptr(tail_part), perm, ptr(r["far_part"]), ptr(r["out"]), ptr(r["lse"]),
+                                     stp, s), "htrc_tile_attention_bf16")
     tick("tile")
     tick("finish")
     r["kx"], r["nb"], r["pitch"], r["group"], r["tile"], r["leaf"] = kx, nb, pitch, grp, tile, LEAF

@@ -47,7 +47,7 @@ enum { HTRC_ORDER_SEQ = 0, HTRC_ORDER_KMEANS = 1 };
 enum { HTRC_CURV_LIN = 0, HTRC_CURV_ISO = 1 };
 enum { HTRC_ROUND_HALF_EVEN = 0, HTRC_ROUND_HALF_AWAY = 1 };
 enum { HTRC_FQ_INT8 = 1, HTRC_FQ_INT4 = 2, HTRC_FQ_FP8 = 3, HTRC_FQ_FP4 = 4 }; /* htrc_fake_quant formats */
-enum { HTRC_STORE_INT8 = 0, HTRC_STORE_FP8 = 1 };                             /* far-field state format */
+enum { HTRC_STORE_INT8 = 0, HTRC_STORE_FP8 = 1, HTRC_STORE_BF16 = 2 };       /* far-field state format */
 /* Arithmetic flags (HtrcFlatArgs.precision and the stage entry points' `precision`), OR-ed:
  * the leaf-statistics dots (the reference's precision= argument, h3/htrc_flat.py:101, :126-130):
  *   HTRC_PREC_FP32 ("fp32", the reference's PREC "ieee"): float32-accurate products (bf16 hi + lo splits of
@@ -105,7 +105,9 @@ typedef struct HtrcFlatArgs {
                               backend's curvature="iso" (h3/htrc_flat.py:331-333) on the INT8 path */
   int32_t store;           /* HTRC_STORE_INT8 (store="int8": INT8 state and INT8 query/key codes), or
                               HTRC_STORE_FP8 (store="fp8", h3/htrc_flat_triton.py FP8=1: e4m3 state codes with
-                              row scales, fp16 far-field dots, bf16 near field; needs HTRC_CURV_LIN) */
+                              row scales, fp16 far-field dots, bf16 near field; needs HTRC_CURV_LIN), or
+                              HTRC_STORE_BF16 (store="bf16", :82-84: bf16 state without scales, bf16 far- and
+                              near-field dots; needs HTRC_CURV_LIN and leaf 64) */
   int32_t qk_scale_block;  /* 0: the reference's INT8 scales (per key, per query row); 64: an extension with no
                               reference counterpart, one scale per 64 keys (a leaf) and per query tile
                               (one absmax scale per 64-token block); HTRC_STORE_INT8 only */
@@ -262,6 +264,40 @@ int htrc_tile_attention_fp8(const uint16_t* qb, const uint16_t* dqh, int64_t n_q
                             int64_t nb, const uint16_t* k, const uint16_t* v, int64_t n_keys, int32_t dim,
                             int32_t leaf, float scale, const float* tail_part, const int32_t* perm,
                             float* far_part, float* out, float* lse, int32_t* status, htrc_stream_t stream);
+
+/* ---- stage entry points of the bf16 state path (HTRC_STORE_BF16) ---- */
+
+/* Tile centres as htrc_tile_prep, with the bf16 state's query operands (h3/htrc_flat_triton.py:106-107):
+ * qb [nt*64, dim] bf16 rows of q and dqb [nt*64, dim] bf16 = bf16(q - mu[tile / G]) (float32 offsets rounded
+ * once). */
+int htrc_tile_prep_bf16(const void* q, int32_t q_dtype, int64_t n_queries, int32_t dim, int32_t tile,
+                        const int32_t* perm, int32_t group, float* mu, uint16_t* mu_hi, uint16_t* mu_lo, uint16_t* qb,
+                        uint16_t* dqb, int32_t precision, htrc_stream_t stream);   /* precision: as htrc_tile_prep_ex */
+
+/* Leaf statistics of centre rows [t0, t0 + tc) with the bf16 state (h3/htrc_flat_triton.py:41-85, :82-84):
+ * gb [tc, nb, dim] bf16 = bf16(scale * sum w k), vbb [tc, nb, dim] bf16 = bf16(sum w v), lz [tc, P] f32; leaf
+ * 64. */
+int htrc_leaf_stats_bf16(const uint16_t* mu_hi, const uint16_t* mu_lo, int64_t nt, int64_t t0, int64_t tc,
+                         const uint16_t* k, const uint16_t* v, int64_t n_keys, int32_t dim, int32_t leaf, float scale,
+                         uint16_t* gb, float* lz, uint16_t* vbb, int32_t precision, int32_t* status,
+                         htrc_stream_t stream);   /* precision: as htrc_leaf_stats */
+
+/* Row-max selection with the bf16 state (h3/htrc_flat_triton.py:214-254, DOT=1):
+ * sel[t, l] = max_r (dqb_r . g_l) + lz_l over the tile's 64 rows (bf16 operands, float32 sums); state row
+ * (t - t0) / group as htrc_rowmax_select. */
+int htrc_rowmax_select_bf16(const uint16_t* dqb, int64_t t0, int64_t tc, int32_t group, const uint16_t* gb,
+                            const float* lz, int64_t nb, int32_t dim, float* sel, int32_t* status,
+                            htrc_stream_t stream);
+
+/* Far field + near field (+ tail partial) with the bf16 state (h3/htrc_flat_triton.py:88-211, DOT=1, merged
+ * as :257-273): far logit (dqb . g) + lz with weight bf16(p) on vbar, near logit (qb . bf16 k) * scale with
+ * weight bf16(p) on v; two launches with far_part as htrc_tile_attention_fp8. */
+int htrc_tile_attention_bf16(const uint16_t* qb, const uint16_t* dqb, int64_t n_queries, int32_t tile, int64_t t0,
+                             int64_t tc, int32_t group, const uint16_t* gb, const float* lz, const uint16_t* vbb,
+                             const uint8_t* excl, const int32_t* idx, int32_t kx, int64_t nb, const uint16_t* k,
+                             const uint16_t* v, int64_t n_keys, int32_t dim, int32_t leaf, float scale,
+                             const float* tail_part, const int32_t* perm, float* far_part, float* out, float* lse,
+                             int32_t* status, htrc_stream_t stream);
 
 /* The forward pass for callers that cannot allocate device memory (a plugin host that owns all device
  * allocations and lends only input and output buffers, or an embedding whose device footprint must not

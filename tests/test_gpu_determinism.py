@@ -25,7 +25,7 @@ def _fill(w, pattern, gen):
     w[:256].zero_()          # the status word starts at zero
 
 
-@pytest.mark.parametrize("store,group,chunk", [("int8", 1, 0), ("int8", 2, 8), ("fp8", 1, 0)])
+@pytest.mark.parametrize("store,group,chunk", [("int8", 1, 0), ("int8", 2, 8), ("fp8", 1, 0), ("bf16", 1, 0)])
 def test_results_do_not_depend_on_workspace_contents(dev, store, group, chunk):
     from htrc_b200 import _lib, synth
     from htrc_b200 import flat as F
@@ -51,7 +51,7 @@ def test_results_do_not_depend_on_workspace_contents(dev, store, group, chunk):
         assert torch.equal(o, o0) and torch.equal(l, l0)
 
 
-@pytest.mark.parametrize("store", ["int8", "fp8"])
+@pytest.mark.parametrize("store", ["int8", "fp8", "bf16"])
 def test_heads_on_two_streams_equal_one_stream(dev, store):
     """Heads alternating over two streams with a workspace each (as the benchmark runs a layer: one head's
     small kernels and the tail of its tile kernel overlap the next head) give bitwise the results of the
@@ -95,7 +95,7 @@ def test_heads_on_two_streams_equal_one_stream(dev, store):
             assert torch.equal(o, ro) and torch.equal(l, rl)
 
 
-@pytest.mark.parametrize("store,runs", [("int8", 10000), ("fp8", 5000)])
+@pytest.mark.parametrize("store,runs", [("int8", 10000), ("fp8", 5000), ("bf16", 5000)])
 def test_row_max_stage_repeats_bitwise(dev, store, runs):
     """The row-max selection of one full-size head (129,024 tokens: 2,016 tiles x 16 blocks of 128 leaves),
     launched thousands of times on the same state, writes bitwise the same sel every time.  The reducing
@@ -108,7 +108,8 @@ def test_row_max_stage_repeats_bitwise(dev, store, runs):
     q, k, v = (t.to(dev) for t in synth.head_inputs((32, 48, 84), 128, head=5, base_seed=31))
     sc = _lib.STORES[store]
     r = F.run_stages(q, k, v, exact_leaves=256, precision=F.precision_code("tf32", "triton"), store=sc)
-    r.pop("vb", None)
+    for key in ("vb", "vbb"):
+        r.pop(key, None)
     torch.cuda.synchronize()
     L = _lib.lib()
     nt, nb = r["sel"].shape[0], r["nb"]
@@ -121,6 +122,9 @@ def test_row_max_stage_repeats_bitwise(dev, store, runs):
         if sc == _lib.STORE_FP8:
             check(L.htrc_rowmax_select_fp8(ptr(r["dqh"]), 0, nt, 1, ptr(r["g8"]), ptr(r["sg"]), ptr(r["lz"]), nb,
                                            128, ptr(buf), stp, s), "htrc_rowmax_select_fp8")
+        elif sc == _lib.STORE_BF16:
+            check(L.htrc_rowmax_select_bf16(ptr(r["dqb"]), 0, nt, 1, ptr(r["gb"]), ptr(r["lz"]), nb, 128, ptr(buf),
+                                            stp, s), "htrc_rowmax_select_bf16")
         else:
             check(L.htrc_rowmax_select(ptr(r["dq8"]), ptr(r["sdq"]), None, 0, nt, 1, ptr(r["g8"]), ptr(r["sg"]),
                                        ptr(r["lz"]), None, nb, 128, ptr(buf), stp, s), "htrc_rowmax_select")

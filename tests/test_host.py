@@ -148,7 +148,9 @@ def test_flat_attention_unimplemented_configurations_say_so():
     with pytest.raises(NotImplementedError, match="one key scale per 64-key leaf"):
         htrc_b200.flat._check_scale_block(64, "int8", 16)
     with pytest.raises(NotImplementedError):
-        htrc_b200.flat_attention(q, k, v, **{**cfg, "store": "bf16"})
+        htrc_b200.flat_attention(q, k, v, **{**cfg, "store": "fp32", "dot": "tf32"})
+    with pytest.raises(NotImplementedError, match="leaf=32 is implemented for store='int8'"):
+        htrc_b200.flat_attention(q, k, v, **{**cfg, "leaf": 32, "store": "bf16"})
     with pytest.raises(NotImplementedError):
         htrc_b200.flat_attention(q, k, v, **{**cfg, "backend": "torch"})
 
