@@ -86,24 +86,32 @@ __device__ __forceinline__ uint32_t quant4(const float (&v)[4], float s, float r
 }
 }  // namespace
 
-// One warp per row of 128 values; each lane owns 4 consecutive values.
+// One warp per kPackRows rows of 128 values (all of its loads issued first, for memory-level parallelism);
+// each lane owns 4 consecutive values of a row.
+constexpr int kPackRows = 4;
 template <typename T, int ROUND>
 __global__ void __launch_bounds__(256) pack_rows_kernel(const T* __restrict__ x, int64_t rows,
                                                         int8_t* __restrict__ x8, float* __restrict__ scale,
                                                         float* __restrict__ sqnorm) {
   const int lane = threadIdx.x & 31;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
-  if (row >= rows) return;
-  float v[4];
-  load4<T>(x + row * 128 + lane * 4, v);
-  float am = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
-  am = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(am)));   // non-negative: uint order
-  const float s = fmaxf(__fmul_rn(am, kInv127), 1e-20f);
-  reinterpret_cast<uint32_t*>(x8 + row * 128)[lane] = quant4<ROUND>(v, s, __frcp_rn(s));
-  if (lane == 0) scale[row] = s;
-  if (sqnorm != nullptr) {                 // |x_row|^2 (the iso curvature's key norms)
-    const float n2 = row_sqnorm(v);
-    if (lane == 0) sqnorm[row] = n2;
+  const int64_t r0 = (static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5)) * kPackRows;
+  float v[kPackRows][4];
+#pragma unroll
+  for (int i = 0; i < kPackRows; ++i)
+    if (r0 + i < rows) load4<T>(x + (r0 + i) * 128 + lane * 4, v[i]);
+#pragma unroll
+  for (int i = 0; i < kPackRows; ++i) {
+    const int64_t row = r0 + i;
+    if (row >= rows) break;                  // warp-uniform
+    float am = fmaxf(fmaxf(fabsf(v[i][0]), fabsf(v[i][1])), fmaxf(fabsf(v[i][2]), fabsf(v[i][3])));
+    am = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(am)));   // non-negative: uint order
+    const float s = fmaxf(__fmul_rn(am, kInv127), 1e-20f);
+    reinterpret_cast<uint32_t*>(x8 + row * 128)[lane] = quant4<ROUND>(v[i], s, __frcp_rn(s));
+    if (lane == 0) scale[row] = s;
+    if (sqnorm != nullptr) {               // |x_row|^2 (the iso curvature's key norms)
+      const float n2 = row_sqnorm(v[i]);
+      if (lane == 0) sqnorm[row] = n2;
+    }
   }
 }
 
@@ -168,7 +176,7 @@ void launch_pack_blocks(const void* x, int dtype, int64_t rows, int rounding, in
 
 void launch_pack_rows(const void* x, int dtype, int64_t rows, int rounding, int8_t* x8, float* scale,
                       float* sqnorm, cudaStream_t st) {
-  const unsigned grid = static_cast<unsigned>((rows + 7) / 8);
+  const unsigned grid = static_cast<unsigned>((rows + 8 * kPackRows - 1) / (8 * kPackRows));
   if (dtype == HTRC_DTYPE_BF16) {
     if (rounding == HTRC_ROUND_HALF_EVEN)
       pack_rows_kernel<uint16_t, 0><<<grid, 256, 0, st>>>(static_cast<const uint16_t*>(x), rows, x8, scale, sqnorm);
