@@ -212,7 +212,8 @@ def _check_against(out, lse, st, ref_out, ref_lse, ref_excl, ref_sel, n, kx, ora
         assert err.max() < OUT_TOL
     else:
         # independent leaf statistics: a one-LSB slope-code flip moves a far logit by up to
-        # |dq|max * |g|max / 127, so a few far-dominated rows may pass 2e-2
+        # |dq|max * |g|max / 127, so a few far-dominated rows may pass 2e-2 (the reference's own GPU operator
+        # is 0.031 max-abs from the same float64 restatement on sampled full-size tiles)
         assert (err < OUT_TOL).mean() >= 0.999 and err.max() < 2.5 * OUT_TOL, (err.max(), (err >= OUT_TOL).sum())
     if ref_lse is not None:
         assert np.abs(lse.cpu().numpy() - ref_lse).mean() < LSE_TOL
