@@ -255,7 +255,9 @@ __global__ void __launch_bounds__(128) tile_prep_kernel(const T* __restrict__ q,
                                                         int8_t* __restrict__ dq8, float* __restrict__ sdq,
                                                         float* __restrict__ dd, int qblock, uint32_t tmask,
                                                         int tdiv, int dqbf) {
-  __shared__ float qs[64][129];
+  // row pitch 132 floats: a lane's 4 values are one aligned 16-byte access (a warp's row read or write is
+  // conflict-free), and the column walk of the centre (thread = column, one row at a time) hits 32 banks
+  __shared__ __align__(16) float qs[64][132];
   __shared__ float mus[128];
   __shared__ float tmx[4];
   const int t = blockIdx.x;
@@ -275,7 +277,7 @@ __global__ void __launch_bounds__(128) tile_prep_kernel(const T* __restrict__ q,
 #pragma unroll
     for (int i = 0; i < 16; ++i)
 #pragma unroll
-      for (int c = 0; c < 4; ++c) qs[warp + 4 * i][lane * 4 + c] = v[i][c];
+      *reinterpret_cast<float4*>(&qs[warp + 4 * i][lane * 4]) = make_float4(v[i][0], v[i][1], v[i][2], v[i][3]);
   }
   __syncthreads();
   if (group <= 1) {
@@ -304,11 +306,12 @@ __global__ void __launch_bounds__(128) tile_prep_kernel(const T* __restrict__ q,
 #pragma unroll 4
   for (int r = warp; r < 64; r += 4) {
     float v[4], d[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      v[i] = qs[r][lane * 4 + i];
-      d[i] = __fsub_rn(v[i], m4[i]);
+    {
+      const float4 x = *reinterpret_cast<const float4*>(&qs[r][lane * 4]);
+      v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
     }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) d[i] = __fsub_rn(v[i], m4[i]);
     const int64_t gr = r0 + r;
     if constexpr (FP8) {
       reinterpret_cast<uint2*>(q8 + gr * 256)[lane] = make_uint2(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]));
