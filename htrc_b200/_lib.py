@@ -1,4 +1,4 @@
-"""ctypes binding of libhtrc_flat.so (the C ABI declared in include/htrc_flat.h).
+"""ctypes binding of libhtrc_flat.so (the C ABI declared in include/htrc_flat.h and include/htrc_tree.h).
 
 The library is built in-tree (``python -m htrc_b200.build``) and loaded from this package directory.
 There is no fallback: if the library is missing, every operator call raises.
@@ -44,7 +44,15 @@ class HtrcFlatArgs(ctypes.Structure):
     ]
 
 
-# name -> (restype, argtypes); every symbol include/htrc_flat.h declares
+class HtrcTreeDims(ctypes.Structure):
+    """Mirror of include/htrc_tree.h HtrcTreeDims."""
+    _fields_ = [("n_keys", _i64), ("n_queries", _i64), ("n_centres", _i32), ("leaf_size", _i32), ("fanout", _i32),
+                ("kv_dtype", _i32), ("q_dtype", _i32), ("scale", _f32), ("threshold", _f32)]
+
+
+TREE_MAX_LEVELS, TREE_MAX_CENTRES, TREE_KMEANS_CENTRES = 16, 256, 32
+
+# name -> (restype, argtypes); every symbol include/htrc_flat.h and include/htrc_tree.h declare
 SIGNATURES = {
     "htrc_leaf_pitch": (_i64, [_i64]),
     "htrc_flat_workspace_size": (ctypes.c_int, [ctypes.POINTER(HtrcFlatArgs), ctypes.POINTER(ctypes.c_size_t)]),
@@ -83,6 +91,19 @@ SIGNATURES = {
     "htrc_dequant_rows": (ctypes.c_int, [_p, _i64, _p, _i64, _i64, _i32, _p, _p]),
     "htrc_selftest_wait_timeout": (ctypes.c_int, [_p, _i64, _p]),
     "htrc_strerror": (ctypes.c_char_p, [ctypes.c_int]),
+    # hierarchical operator (include/htrc_tree.h)
+    "htrc_tree_levels": (ctypes.c_int, [ctypes.POINTER(HtrcTreeDims), ctypes.POINTER(_i32), ctypes.POINTER(_i32)]),
+    "htrc_tree_forest_size": (ctypes.c_int, [ctypes.POINTER(HtrcTreeDims), ctypes.POINTER(ctypes.c_size_t)]),
+    "htrc_tree_build": (ctypes.c_int, [ctypes.POINTER(HtrcTreeDims), _p, _p, _p, _p, ctypes.c_size_t, _p]),
+    "htrc_tree_forest_view": (ctypes.c_int, [ctypes.POINTER(HtrcTreeDims), _p, _i32] + [ctypes.POINTER(_p)] * 6),
+    "htrc_tree_walk_size": (ctypes.c_int, [ctypes.POINTER(HtrcTreeDims), ctypes.POINTER(ctypes.c_size_t)]),
+    "htrc_tree_walk": (ctypes.c_int, [ctypes.POINTER(HtrcTreeDims), _p, _p, _p, _p, _p, ctypes.c_size_t, _p, _p,
+                                      ctypes.POINTER(_i64), _p]),
+    "htrc_tree_records_size": (ctypes.c_int, [_i64, ctypes.POINTER(ctypes.c_size_t)]),
+    "htrc_tree_values": (ctypes.c_int, [ctypes.POINTER(HtrcTreeDims), _p, _p, _p, _p, _p, _p, _p, _i64,
+                                        ctypes.c_size_t, _p, _p, _p, _p]),
+    "htrc_tree_centres_scratch_size": (ctypes.c_int, [_i64, ctypes.POINTER(ctypes.c_size_t)]),
+    "htrc_tree_centres": (ctypes.c_int, [_p, _i32, _i64, _f32, _p, _p, _p, ctypes.c_size_t, _p]),
 }
 
 _lib = None

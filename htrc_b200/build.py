@@ -17,7 +17,7 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libhtrc_flat.so"
-SOURCES = ["api.cu", "prep.cu", "stats.cu", "rowmax.cu", "route.cu", "tile.cu", "kmeans.cu", "quant.cu", "static_ws.cu", "fp8.cu"]
+SOURCES = ["api.cu", "prep.cu", "stats.cu", "rowmax.cu", "route.cu", "tile.cu", "kmeans.cu", "quant.cu", "static_ws.cu", "fp8.cu", "tree.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -30,7 +30,7 @@ def nvcc_path() -> str:
 
 def build(verbose: bool = False, ptxas_verbose: bool = False, force: bool = False) -> Path:
     srcs = [CSRC / s for s in SOURCES]
-    deps = srcs + list(CSRC.glob("*.cuh")) + [ROOT / "include" / "htrc_flat.h"]
+    deps = srcs + list(CSRC.glob("*.cuh")) + list((ROOT / "include").glob("*.h"))
     if LIB.exists() and not force and all(LIB.stat().st_mtime >= d.stat().st_mtime for d in deps):
         return LIB
     out_dir = ROOT / "_build"

@@ -63,6 +63,7 @@ void launch_pack_blocks(const void* x, int dtype, int64_t rows, int rounding, in
                         float* sqnorm, cudaStream_t st);
 size_t kmeans_scratch_bytes(int64_t n);
 int launch_kmeans_order(const void* q, int dtype, int64_t n, int32_t* perm, void* scratch, cudaStream_t st);
+void kmeans_views(void* scratch, int64_t n, float** centres, uint8_t** assign);
 void launch_fake_quant(const void* x, int x_dtype, int64_t rows, int fmt, int gsz, void* out, int out_dtype,
                        cudaStream_t st);
 void launch_dequant_rows(const uint8_t* x8, int64_t stride_x, const float* scale, int64_t stride_s, int64_t rows,

@@ -262,6 +262,16 @@ size_t kmeans_scratch_bytes(int64_t n) {
          a256(size_t(kMaxBlocks) * kClusters * 4) + a256(size_t(n)) + 2 * a256(size_t(nchunk) * kClusters * 4);
 }
 
+// the scratch's centre rows [32][128] (unscaled query space) and per-row nearest centre [n] (uint8)
+void kmeans_views(void* scratch, int64_t n, float** centres, uint8_t** assign) {
+  auto a256 = [](size_t x) { return (x + 255) & ~size_t(255); };
+  uint8_t* p = static_cast<uint8_t*>(scratch);
+  *centres = reinterpret_cast<float*>(p);
+  *assign = p + a256(kClusters * 128 * 4) + a256(size_t(kMaxBlocks) * kClusters * 128 * 4) +
+            a256(size_t(kMaxBlocks) * kClusters * 4);
+  (void)n;
+}
+
 int launch_kmeans_order(const void* q, int dtype, int64_t n, int32_t* perm, void* scratch, cudaStream_t st) {
   const int64_t nchunk = (n + kChunk - 1) / kChunk;
   auto a256 = [](size_t x) { return (x + 255) & ~size_t(255); };
