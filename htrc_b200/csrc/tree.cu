@@ -32,6 +32,9 @@
 #include "kernels.cuh"
 #include "../../include/htrc_tree.h"
 
+#include <cstdlib>
+#include <type_traits>
+
 namespace htrc {
 
 namespace {
@@ -1026,6 +1029,285 @@ __global__ void __launch_bounds__(256) tree_final_kernel(int64_t nq, const int64
 }
 
 // ---------------------------------------------------------------------------------------------------
+// Leaf blocks on the tensor cores (bfloat16 keys, values and queries; forests of two or more levels): the
+// arithmetic of tree_leafblock_kernel with chunks of 128 queries and, per leaf,
+//   S' = q . k_s    tcgen05.mma kind::f16, M 128 x N 64 x K 128 (bf16 products are exact; f32 sums) -> TMEM
+//   row math        one thread per query row = TMEM lane: S = scale S', prediction, decision, coefficients P
+//   O += P . v_s    tcgen05.mma kind::f16, M 128 x N 128 x K 64, P from TMEM as bf16 hi + lo parts
+// Operands are staged by the CTA's threads into 128-byte-swizzled shared tiles (the queries are gathered
+// rows); one thread issues the MMAs; every wait on an MMA completion is bounded.
+constexpr int kTcQ = 128;
+constexpr int kTcCols = 256;         // TMEM columns: S 0..63, P hi 64..95, P lo 96..127, O 128..255
+struct __align__(1024) TcSmem {
+  uint8_t qs[2 * kTcQ * 128];        // queries: two K-blocks of [128 rows][128 B]  (K-major A)
+  uint8_t ks[2 * 64 * 128];          // keys: two K-blocks of [64 rows][128 B]       (K-major B)
+  uint8_t vs[2 * 64 * 128];          // values: two N-chunks of [64 key rows][128 B] (MN-major B)
+  float as[64], ws[64];
+  int64_t rec[kTcQ];
+  int list[kWindow];
+  int wsum[4];
+  uint64_t bar_s, bar_pv;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+constexpr size_t kTcSmemBytes = 110 * 1024;   // > 228 KB / 3: at most two CTAs (512 TMEM columns) per SM
+static_assert(sizeof(TcSmem) + 1024 <= kTcSmemBytes, "tree tensor-core shared layout");
+
+// gather_window for 128 threads
+__device__ int gather_window128(const int32_t* __restrict__ perm, int64_t lo, int64_t hi,
+                                const uint32_t* __restrict__ mask, int words, int bit, int* list, int* wsum) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  int total = 0;
+  for (int64_t base = lo; base < hi; base += 128) {
+    const int64_t i = base + tid;
+    bool take = false;
+    int q = 0;
+    if (i < hi) {
+      q = perm[i];
+      take = (mask[static_cast<int64_t>(q) * words + (bit >> 5)] >> (bit & 31)) & 1u;
+    }
+    const uint32_t b = __ballot_sync(0xffffffffu, take);
+    if (lane == 0) wsum[warp] = __popc(b);
+    __syncthreads();
+    int before = total, add = 0;
+    for (int w = 0; w < 4; ++w) {
+      if (w < warp) before += wsum[w];
+      add += wsum[w];
+    }
+    if (take) list[before + __popc(b & ((1u << lane) - 1u))] = q;
+    total += add;
+    __syncthreads();
+  }
+  return total;
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+__global__ void __launch_bounds__(128, 1) tree_leafblock_tc_kernel(
+    const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, const uint16_t* __restrict__ v, int64_t m,
+    float scale, const float* __restrict__ a, const int32_t* __restrict__ perm, const int64_t* __restrict__ coff,
+    int64_t slice, TreeLevels lv, float thr, const float* __restrict__ norm, const int64_t* __restrict__ base,
+    int64_t nrec, float* __restrict__ rec_val, float* __restrict__ rec_lm, int32_t* __restrict__ rec_ex,
+    int* __restrict__ status) {
+  extern __shared__ unsigned char smem_raw[];
+  TcSmem& sh = *reinterpret_cast<TcSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int c = blockIdx.y, p = blockIdx.x, tid = threadIdx.x, warp = tid >> 5;
+  const int64_t lo = coff[c] + static_cast<int64_t>(blockIdx.z) * slice;
+  const int64_t hi = min(coff[c + 1], lo + slice);
+  if (lo >= hi) return;
+  const int nl = lv.n[0], leaf = lv.leaf;
+  const int l0 = p * lv.fanout, l1 = min(nl, l0 + lv.fanout);
+  const float* ac = a + static_cast<int64_t>(c) * m;
+  const float* lL = lv.L[0] + static_cast<int64_t>(c) * nl;
+  if (tid == 0) {
+    mbar_init(&sh.bar_s, 1);
+    mbar_init(&sh.bar_pv, 1);
+    sh.abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) tmem_alloc(&sh.tmem_base, kTcCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh.tmem_base;
+  const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+  const uint32_t id_s = idesc_bf16(128, 64, false, false);
+  const uint32_t id_pv = idesc_bf16(128, 128, false, true);
+  const uint32_t qa = smem_u32(sh.qs), ka = smem_u32(sh.ks), va = smem_u32(sh.vs);
+  uint32_t ph_s = 0, ph_pv = 0;
+  bool ok = true;
+  for (int64_t win = lo; win < hi && ok; win += kWindow) {
+    const int cnt = gather_window128(perm, win, min(hi, win + kWindow), lv.open[1], lv.words[1], p, sh.list, sh.wsum);
+    for (int b0 = 0; b0 < cnt && ok; b0 += kTcQ) {
+      const int nq = min(kTcQ, cnt - b0);
+      const int* lst = sh.list + b0;
+      for (int x = tid; x < kTcQ * 16; x += 128) {
+        const int r = x >> 4, cc = x & 15;
+        uint4 val = make_uint4(0u, 0u, 0u, 0u);
+        if (r < nq) val = __ldg(reinterpret_cast<const uint4*>(q + static_cast<int64_t>(lst[r]) * kD) + cc);
+        st_shared_v4(qa + (cc >> 3) * (kTcQ * 128) + sw128_off(r, cc & 7), val);
+      }
+      const bool live = tid < nq;
+      const float nrm = live ? norm[lst[tid]] : 0.f;
+      float m_run = -INFINITY, s_run = 0.f;
+      int nex = 0;
+      for (int l = l0; l < l1; ++l) {
+        const int64_t s0 = static_cast<int64_t>(l) * leaf;
+        const int kc = static_cast<int>(m - s0 < leaf ? m - s0 : leaf);
+        const float ll = lL[l];
+        for (int x = tid; x < 64 * 16; x += 128) {
+          const int r = x >> 4, cc = x & 15;
+          uint4 kv = make_uint4(0u, 0u, 0u, 0u), vv = kv;
+          if (r < kc) {
+            kv = __ldg(reinterpret_cast<const uint4*>(k + (s0 + r) * kD) + cc);
+            vv = __ldg(reinterpret_cast<const uint4*>(v + (s0 + r) * kD) + cc);
+          }
+          st_shared_v4(ka + (cc >> 3) * (64 * 128) + sw128_off(r, cc & 7), kv);
+          st_shared_v4(va + (cc >> 3) * (64 * 128) + sw128_off(r, cc & 7), vv);
+        }
+        if (tid < 64) {
+          const float av = tid < kc ? ac[s0 + tid] : 0.f;
+          sh.as[tid] = av;
+          sh.ws[tid] = tid < kc ? expf(av - ll) : 0.f;
+        }
+        fence_proxy_async_smem();
+        __syncthreads();
+        if (tid == 0) {
+          tc_fence_after();
+#pragma unroll
+          for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks)
+              mma_bf16(tmem, sw128_desc(qa + kb * (kTcQ * 128) + ks * 32, 16, 1024),
+                       sw128_desc(ka + kb * (64 * 128) + ks * 32, 16, 1024), id_s, (kb | ks) != 0);
+          mma_commit(&sh.bar_s);
+        }
+        ok = mbar_wait(&sh.bar_s, ph_s, status, &sh.abort_flag);
+        ph_s ^= 1u;
+        if (!__syncthreads_and(ok)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        float S[64];
+        {
+          uint32_t r0[32], r1[32];
+          tmem_ld32(tmem + lane_off, r0);
+          tmem_ld32(tmem + lane_off + 32, r1);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            S[j] = scale * __uint_as_float(r0[j]);
+            S[32 + j] = scale * __uint_as_float(r1[j]);
+          }
+        }
+        float xb = 0.f;
+#pragma unroll
+        for (int j = 0; j < 64; ++j) xb = fmaf(sh.ws[j], S[j] - sh.as[j], xb);
+        float qd = 0.f;
+#pragma unroll
+        for (int j = 0; j < 64; ++j) {
+          const float e = S[j] - sh.as[j] - xb;
+          qd = fmaf(sh.ws[j] * e, e, qd);
+        }
+        const float lmv = ll + xb + 0.5f * qd;
+        const bool open = live && score_of(lmv, qd, nrm) > thr;
+        float mass = lmv;
+        if (open) {
+          float mx = -INFINITY;
+#pragma unroll
+          for (int j = 0; j < 64; ++j)
+            if (j < kc) mx = fmaxf(mx, S[j]);
+          float se = 0.f;
+#pragma unroll
+          for (int j = 0; j < 64; ++j)
+            if (j < kc) se += expf(S[j] - mx);
+          mass = mx + logf(se);
+        }
+        const float mn = live ? fmaxf(m_run, mass) : 0.f;
+        const float al = live ? expf(m_run - mn) : 1.f;
+        if (live) {
+          s_run = s_run * al + expf(mass - mn);
+          m_run = mn;
+        }
+        nex += open;
+        const float fw = expf(lmv - mn);
+        // rescale O (its previous PV has completed).  tcgen05.ld / st are warp-collective (.sync.aligned):
+        // the warp takes the branch as a whole, rows whose maximum did not move scale by 1
+        if (__any_sync(0xffffffffu, l > l0 && al != 1.f)) {
+#pragma unroll 1
+          for (int cb = 0; cb < 4; ++cb) {
+            uint32_t o[32];
+            tmem_ld32(tmem + lane_off + 128 + 32 * cb, o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * al);
+            tmem_st32(tmem + lane_off + 128 + 32 * cb, o);
+          }
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {            // P as bf16 hi and lo parts, 32 keys at a time
+          uint32_t ph[16], pl[16];
+#pragma unroll
+          for (int j = 0; j < 32; j += 2) {
+            float pc[2];
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+              const int jj = 32 * h + j + t;
+              pc[t] = 0.f;
+              if (live && jj < kc)
+                pc[t] = open ? expf(S[jj] - mn) : fw * sh.ws[jj] * (1.f + (S[jj] - sh.as[jj] - xb));
+            }
+            const __nv_bfloat162 hb = __floats2bfloat162_rn(pc[0], pc[1]);
+            const float2 hf = __bfloat1622float2(hb);
+            ph[j >> 1] = *reinterpret_cast<const uint32_t*>(&hb);
+            pl[j >> 1] = pack_bf16x2(pc[0] - hf.x, pc[1] - hf.y);
+          }
+          tmem_st16(tmem + lane_off + 64 + 16 * h, ph);
+          tmem_st16(tmem + lane_off + 96 + 16 * h, pl);
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        __syncthreads();
+        if (tid == 0) {
+          tc_fence_after();
+#pragma unroll
+          for (int part = 0; part < 2; ++part)
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              mma_bf16_ts_by(1u, tmem + 128, tmem + 64 + 32 * part + 8 * kk,
+                             sw128_desc(va + kk * 2048, 64 * 128, 1024), id_pv, (l > l0 || part || kk) ? 1u : 0u);
+          mma_commit(&sh.bar_pv);
+        }
+        ok = mbar_wait(&sh.bar_pv, ph_pv, status, &sh.abort_flag);
+        ph_pv ^= 1u;
+        if (!__syncthreads_and(ok)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+      }
+      if (!ok) break;
+      int64_t r = -1;
+      if (live) {
+        const int64_t qq = lst[tid];
+        r = record_of_block(lv, base, qq, p);
+        if (r < 0 || r >= nrec) {
+          flag_status(status, ST_BAD_INDEX);
+          r = -1;
+        } else {
+          rec_lm[r] = m_run + logf(s_run);
+          rec_ex[r] = nex;
+        }
+      }
+      const float inv = 1.f / s_run;
+#pragma unroll
+      for (int cb = 0; cb < 4; ++cb) {
+        uint32_t o[32];
+        tmem_ld32(tmem + lane_off + 128 + 32 * cb, o);
+        tmem_ld_wait();
+        if (r >= 0) {
+          float4* dst = reinterpret_cast<float4*>(rec_val + r * kD + 32 * cb);
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            dst[j] = make_float4(__uint_as_float(o[4 * j]) * inv, __uint_as_float(o[4 * j + 1]) * inv,
+                                 __uint_as_float(o[4 * j + 2]) * inv, __uint_as_float(o[4 * j + 3]) * inv);
+        }
+      }
+      tc_fence_before();
+      __syncthreads();
+      tc_fence_after();
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, kTcCols);
+}
+
+// ---------------------------------------------------------------------------------------------------
 // centres for the operator from the k-means of the accurate mode: scaled centres and int32 assignment
 __global__ void tree_centres_kernel(const float* __restrict__ km_centres, const uint8_t* __restrict__ km_assign,
                                     int64_t n, float scale, float* __restrict__ centres, int32_t* __restrict__ assign) {
@@ -1189,6 +1471,13 @@ int set_smem(K kernel, size_t bytes) {
 
 int launched() { return cudaGetLastError() == cudaSuccess ? HTRC_OK : HTRC_ERR_CUDA; }
 
+// the bfloat16 leaf blocks run on the tensor cores unless HTRC_TREE_SIMT_LEAVES=1 selects the CUDA-core
+// kernel (same arithmetic in float32 throughout; used by the tests to compare the two)
+bool tc_leaves_enabled() {
+  const char* e = getenv("HTRC_TREE_SIMT_LEAVES");
+  return !(e && e[0] == '1');
+}
+
 // largest per-centre query count (reads the grouped offsets back: one stream synchronisation)
 int max_count(const int64_t* coff_dev, int ncen, cudaStream_t st, int64_t* mx) {
   int64_t host[HTRC_TREE_MAX_CENTRES + 1];
@@ -1295,7 +1584,7 @@ int walk_impl(const HtrcTreeDims* d, const Shape& s, const T* q, const int32_t* 
 template <typename T>
 int values_impl(const HtrcTreeDims* d, const Shape& s, const T* k, const T* v, const T* q, const float* centres,
                 const void* forest, void* walk, void* records, int64_t n_records, float* out, float* lse,
-                int32_t* exact, cudaStream_t st) {
+                int32_t* exact, cudaStream_t st, bool tc_leaves) {
   const WalkLayout w = walk_layout(d, s);
   const ForestLayout f = forest_layout(d, s);
   const RecordLayout r = record_layout(n_records);
@@ -1325,10 +1614,18 @@ int values_impl(const HtrcTreeDims* d, const Shape& s, const T* k, const T* v, c
       if ((rc = launched()) != HTRC_OK) return rc;
     }
   }
-  if ((rc = set_smem(tree_leafblock_kernel<T>, sizeof(BlockSmem))) != HTRC_OK) return rc;
-  tree_leafblock_kernel<T><<<dim3(top >= 1 ? s.n[1] : 1, C, slices(mx, kSlice)), 256, sizeof(BlockSmem), st>>>(
-      q, k, v, d->n_keys, d->scale, centres, a, perm, coff, kSlice, lv, d->threshold, norm, base, n_records, rec_val,
-      rec_lm, rec_ex, status);
+  if (std::is_same<T, uint16_t>::value && top >= 1 && tc_leaves) {
+    if ((rc = set_smem(tree_leafblock_tc_kernel, kTcSmemBytes)) != HTRC_OK) return rc;
+    tree_leafblock_tc_kernel<<<dim3(s.n[1], C, slices(mx, kSlice)), 128, kTcSmemBytes, st>>>(
+        reinterpret_cast<const uint16_t*>(q), reinterpret_cast<const uint16_t*>(k),
+        reinterpret_cast<const uint16_t*>(v), d->n_keys, d->scale, a, perm, coff, kSlice, lv, d->threshold, norm,
+        base, n_records, rec_val, rec_lm, rec_ex, status);
+  } else {
+    if ((rc = set_smem(tree_leafblock_kernel<T>, sizeof(BlockSmem))) != HTRC_OK) return rc;
+    tree_leafblock_kernel<T><<<dim3(top >= 1 ? s.n[1] : 1, C, slices(mx, kSlice)), 256, sizeof(BlockSmem), st>>>(
+        q, k, v, d->n_keys, d->scale, centres, a, perm, coff, kSlice, lv, d->threshold, norm, base, n_records,
+        rec_val, rec_lm, rec_ex, status);
+  }
   if ((rc = launched()) != HTRC_OK) return rc;
   tree_final_kernel<<<static_cast<unsigned>((N + 7) / 8), 256, 0, st>>>(N, base, rec_val, rec_lm, rec_ex, out, lse,
                                                                         exact);
@@ -1453,10 +1750,10 @@ int htrc_tree_values(const HtrcTreeDims* dims, const void* keys, const void* val
   if (dims->kv_dtype == HTRC_DTYPE_BF16)
     return values_impl<uint16_t>(dims, s, static_cast<const uint16_t*>(keys), static_cast<const uint16_t*>(values),
                                  static_cast<const uint16_t*>(queries), centres, forest, walk, records, n_records,
-                                 out, lse, exact_leaves, st);
+                                 out, lse, exact_leaves, st, tc_leaves_enabled());
   return values_impl<float>(dims, s, static_cast<const float*>(keys), static_cast<const float*>(values),
                             static_cast<const float*>(queries), centres, forest, walk, records, n_records, out, lse,
-                            exact_leaves, st);
+                            exact_leaves, st, false);
 }
 
 int htrc_tree_centres_scratch_size(int64_t n_queries, size_t* bytes) {
