@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark of the flat HTRC operator on B200: milliseconds per attention layer.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload cfg3|cfg2]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload cfg3|cfg2|cfg4|cfg5]
 
 Workload (default cfg3: the benchmark's full-resolution configuration): one layer = 24 heads of a 32x48x84 video latent
 (129,024 tokens), d=128, bf16 Q/K/V from the seeded smooth-field generator (htrc_b200.synth), leaf 64,
@@ -14,6 +14,10 @@ Printed JSON line (rank 0): value = ms per layer, device-resident inputs, max ov
 through the public API (htrc_b200.forward_into) with pinned host inputs and outputs, host<->device copies
 inside the timed region; roofline of the dominant kernel from live CUDA events; cpu_baseline = the
 oracle port timed on a bounded tile sample on this host (rank 0, N=1).
+
+--workload cfg5 times the hierarchical operator (htrc_b200.tree, the NumPy law of src/htrc_reference/model.py on the
+GPU) on the 243-frame configuration instead; its cpu_baseline times the float64 tree oracle on a sample, and its
+reference arm the reference's own NumPy model (build_forest + evaluate) on a sample, both extrapolated.
 
 --impl reference times the reference's algorithm on the host CPU (the NumPy oracle port of
 h3/htrc_flat.py's production path, all host threads) on a bounded sample of the same workload.
@@ -47,6 +51,10 @@ WORKLOADS = {
                  name="cfg4: per step one denoise-step block: CFG batch 2 x 24 heads of 129,024 tokens (48 (batch, "
                       "head) pairs, fresh seeded Q/K/V per block, 2 distinct blocks resident and alternated), d128, "
                       "leaf 64, tile 64, fast (E=256), INT8; value = ms per 24-head layer = block time / 2"),
+    # the hierarchical operator (htrc_b200.tree): a step is one 24-head layer at 243 frames; heads split over ranks
+    "cfg5": dict(grid=(61, 48, 84), heads=24, tree=True, leaf=64, fanout=16, threshold=0.02,
+                 name="cfg5: hierarchical HTRC, 245,952-token 61x48x84 latent layer, 24 heads, d128, leaf 64, fanout "
+                      "16, threshold 0.02, 32 k-means query centres, second-order log-mass + value dipole"),
     # profiling-sized case: one head, half of cfg3's frames (leaf state ~400 MB > L2, < 1 GB on the device)
     "prof": dict(grid=(16, 48, 84), heads=1, exact_leaves=256,
                  name="prof: one 64,512-token 16x48x84 head, d128, leaf 64, tile 64, fast (E=256), INT8"),
@@ -891,6 +899,223 @@ def run_ours(a, wl, rank, world, local_rank):
         print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------------------------------------------
+# the hierarchical operator (workload cfg5)
+
+def tree_launches(levels):
+    """Kernels one head launches through htrc_b200.tree.tree_attention with a forest of `levels` levels: the
+    k-means (8 x 2 + 3) and the centre conversion, the build (leaves, level 1 from the keys, one merge per higher
+    level), the walk (2 grouping, one per internal level, count, scan) and the values (one per internal level,
+    the leaf blocks, the final merge)."""
+    internal = max(0, levels - 1)
+    return 20 + (1 + (1 if levels >= 2 else 0) + max(0, levels - 2)) + (2 + internal + 2) + (internal + 2)
+
+
+def tree_oracle_sample(k, v, q, centres, assign, rows_per_centre=6, ncentres=2, wl=None, out=None, lse=None,
+                       cnt=None):
+    """The float64 tree oracle on a bounded sample of one head: the forests of `ncentres` centres and
+    `rows_per_centre` of their queries.  Returns (timing dict, parity dict or None)."""
+    import numpy as np
+    from oracle import tree_oracle as T
+    kn, vn = k.float().cpu().numpy(), v.float().cpu().numpy()
+    qn = q.float().cpu().numpy()
+    cen = centres.float().cpu().numpy().astype(np.float64)
+    asg = assign.cpu().numpy().astype(np.int64)
+    sc = 1.0 / math.sqrt(128)
+    t_forest, t_eval, nq = 0.0, 0.0, 0
+    errs, lerr, agree, total = [], [], 0, 0
+    for c in np.unique(asg)[:ncentres]:
+        rows = np.nonzero(asg == c)[0]
+        rows = rows[np.linspace(0, rows.size - 1, min(rows_per_centre, rows.size)).round().astype(int)]
+        t0 = time.perf_counter()
+        lv = T.forest(kn, vn, cen[c], leaf_size=wl["leaf"], fanout=wl["fanout"])
+        t1 = time.perf_counter()
+        ref, ref_lse, info = T.evaluate(kn, vn, qn[rows].astype(np.float64) * sc, cen[c], lv,
+                                        opening_threshold=wl["threshold"])
+        t2 = time.perf_counter()
+        t_forest += t1 - t0
+        t_eval += t2 - t1
+        nq += rows.size
+        if out is not None:
+            errs.append(np.abs(out[rows] - ref).max())
+            lerr.append(np.abs(lse[rows] - ref_lse))
+            rc = np.stack([info[x] for x in ("visited_nodes", "accepted_nodes", "exact_leaves")], 1)
+            agree += int((cnt[rows] == rc).all(1).sum())
+            total += rows.size
+    timing = {"forest_s_per_centre": t_forest / ncentres, "evaluate_s_per_query": t_eval / nq, "queries": nq,
+              "centres": ncentres}
+    parity = None
+    if out is not None:
+        parity = {"rows": total, "centres": ncentres, "out_maxabs": float(max(errs)),
+                  "logz_mae": float(np.concatenate(lerr).mean()), "counters_agree": agree / total,
+                  "oracle": "oracle/tree_oracle.py (float64 restatement of src/htrc_reference/model.py)"}
+    return timing, parity
+
+
+def run_tree(a, wl, rank, world, local_rank):
+    import numpy as np
+    import torch
+
+    from htrc_b200 import shard, synth, tree
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+    H = wl["heads"]
+    try:
+        mine = list(shard.heads_of_rank(H, rank, world))
+    except ValueError as e:
+        raise SystemExit(str(e))
+    kw = dict(leaf_size=wl["leaf"], fanout=wl["fanout"], opening_threshold=wl["threshold"])
+    host = {h: tuple(t.pin_memory() for t in synth.head_inputs(wl["grid"], 128, head=h)) for h in mine}
+    dq = {h: tuple(t.to(dev, non_blocking=True) for t in host[h]) for h in mine}
+    n = host[mine[0]][0].shape[0]
+    out_host = {h: torch.empty((n, 128), dtype=torch.float32).pin_memory() for h in mine}
+    lse_host = {h: torch.empty((n,), dtype=torch.float32).pin_memory() for h in mine}
+
+    def layer():
+        for h in mine:
+            tree.tree_attention(*dq[h], **kw)
+
+    def layer_e2e():
+        for h in mine:
+            q, k, v = (t.to(dev, non_blocking=True) for t in host[h])
+            o, l_ = tree.tree_attention(q, k, v, return_lse=True, **kw)
+            out_host[h].copy_(o, non_blocking=True)
+            lse_host[h].copy_(l_, non_blocking=True)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(a.warmup):
+        layer()
+    barrier()
+    clk_s = ClockSampler(local_rank)
+    clk_s.start()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.steps):
+        layer()
+    e1.record()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1) / a.steps)
+    clk = clk_s.stop()
+    e2e = None
+    if not a.no_e2e:
+        layer_e2e()
+        barrier()
+        e0.record()
+        for _ in range(a.steps):
+            layer_e2e()
+        e1.record()
+        barrier()
+        e2e_ms = max_over_ranks(e0.elapsed_time(e1) / a.steps)
+        per_head_in = sum(t.numel() * t.element_size() for t in host[mine[0]])
+        e2e = {"value": e2e_ms, "unit": "ms/layer", "h2d_bytes_per_step": per_head_in * len(mine) * world,
+               "d2h_bytes_per_step": (n * 128 * 4 + n * 4) * len(mine) * world,
+               "api": "htrc_b200.tree.tree_attention with pinned host q/k/v copied in and out / lse copied back"}
+    # stage times of one head (its own pass, events between the stages)
+    marks = []
+    h0 = mine[0]
+    out, lse, info = tree.tree_attention(*dq[h0], return_lse=True, return_info=True, marks=marks, **kw)
+    torch.cuda.synchronize()
+    stage_ms = {marks[i][0]: marks[i - 1][1].elapsed_time(marks[i][1]) for i in range(1, len(marks))}
+    stage_ms["start"] = stage_ms.pop("start", 0.0)          # build -> walk gap (host allocation): reported as is
+    leaves = int(info["leaves"].sum().item())
+    levels = info["forest"].levels
+    peaks, src = measured_peaks()
+    peak = peaks["bf16_tflops"]
+    flop = leaves * 2 * (2 * 64 * 128)                       # S = q.k and P.v per (query, visited leaf) of 64 keys
+    achieved = flop / (stage_ms["leaves"] * 1e-3) / 1e12
+    roof = {"kernel": "tree_leafblock_tc_kernel", "bound": "tensor", "achieved": achieved, "peak": peak,
+            "unit": "TFLOP/s", "frac": achieved / peak, "traffic": None,
+            "peak_source": f"{src} bf16_tflops (burst: the stage is timed alone)",
+            "flop_per_launch": flop, "note": "bf16-equivalent flop of the law's leaf work: 2 x 2*64*128 per (query, "
+            "visited leaf); the kernel issues the PV product twice (bf16 hi + lo parts of P)"}
+    counters = {x: float(info[x].float().mean().item()) for x in ("visited_nodes", "accepted_nodes", "exact_leaves",
+                                                                   "leaves")}
+    cpu, parity = None, None
+    if rank == 0 and world == 1 and not a.no_cpu:
+        q0, k0, v0 = dq[h0]
+        cnt = torch.stack([info["visited_nodes"], info["accepted_nodes"], info["exact_leaves"]], 1).cpu().numpy()
+        timing, parity = tree_oracle_sample(k0, v0, q0, info["centres"], info["assign"], wl=wl,
+                                            out=out.float().cpu().numpy(), lse=lse.float().cpu().numpy(), cnt=cnt)
+        ncen = int(info["centres"].shape[0])
+        layer_s = (timing["forest_s_per_centre"] * ncen + timing["evaluate_s_per_query"] * n) * H
+        cpu = {"value": layer_s * 1e3, "unit": "ms/layer", "cores": 1, "kind": "port",
+               "sample": f"oracle/tree_oracle.py (float64 NumPy) on head 0: the forests of {timing['centres']} "
+                         f"centres and {timing['queries']} of their queries, extrapolated to {ncen} centres x {n} "
+                         f"queries x {H} heads", **timing}
+    if rank == 0:
+        line = {"metric": "hierarchical-HTRC ms per 245,952-token 24-head d128 layer", "value": ms, "unit": "ms/layer",
+                "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": False,
+                "scaling": "strong", "vs_baseline": None,
+                "dtype": "bf16 q.k and P.v on tcgen05 (P as bf16 hi + lo), f32 node predictions and decisions",
+                "data": "synthetic: seeded smooth-field Q/K (4x8x8 grid trilinear + 0.5 noise, RMS 3), N(0,1) V, bf16",
+                "config": {"workload": wl["name"], "tokens": n, "heads": H, "dim": 128, "leaf": wl["leaf"],
+                           "fanout": wl["fanout"], "threshold": wl["threshold"], "levels": levels,
+                           "nodes_per_level": info["forest"].nodes, "heads_per_gpu": len(mine),
+                           "l2": "inputs larger than L2: 189 MB of q/k/v and 1.1 GB of forest per head",
+                           "parallelism": f"heads/{world}, no collective (outputs stay on their rank)"},
+                "stage_ms_head0": stage_ms, "counters_mean_head0": counters,
+                "roofline": roof, "cpu_baseline": cpu, "parity_head0": parity, "e2e": e2e,
+                "gpu_launches": a.steps * len(mine) * tree_launches(levels), "clocks": clk}
+        print(json.dumps(line), flush=True)
+
+
+def run_tree_reference(a, wl, rank):
+    """The reference's own NumPy hierarchical model (src/htrc_reference: build_forest + evaluate, one query at a
+    time) on a bounded sample of the cfg5 workload, extrapolated to the layer; rank 0 only."""
+    if rank != 0:
+        return
+    import numpy as np
+    from htrc_b200 import synth
+    model = None
+    ref_dir = ROOT / "baseline" / "_ref"
+    if (ref_dir / "htrc_reference" / "model.py").exists():
+        sys.path.insert(0, str(ref_dir))
+        from htrc_reference import model                        # noqa: F401
+    if model is None:
+        print(json.dumps({"impl": "reference", "unavailable": "the reference package is not installed under "
+                          "baseline/_ref (baseline/install_ref.sh)"}), flush=True)
+        return
+    q, k, v = (t.float().numpy().astype(np.float64) for t in synth.head_inputs(wl["grid"], 128, head=0))
+    sc = 1.0 / math.sqrt(128)
+    centre = (q[::64] * sc).mean(0)
+    times = []
+    for step in range(a.warmup + a.steps):
+        t0 = time.perf_counter()
+        forest = model.build_forest(k, v, centre, leaf_size=wl["leaf"], fanout=wl["fanout"])
+        t1 = time.perf_counter()
+        for i in range(2):
+            model.evaluate(k, v, q[(1000 * step + 977 * i) % q.shape[0]] * sc, centre, forest,
+                           opening_threshold=wl["threshold"])
+        t2 = time.perf_counter()
+        times.append(((t1 - t0) * 32 + (t2 - t1) / 2 * q.shape[0]) * wl["heads"] * 1e3)
+    val = statistics.median(times[a.warmup:])
+    print(json.dumps({"impl": "reference", "metric": "hierarchical-HTRC ms per 245,952-token 24-head d128 layer",
+                      "value": val, "unit": "ms/layer", "n_gpus": 1, "steps": a.steps, "warmup": a.warmup,
+                      "higher_is_better": False, "config": {"workload": wl["name"]},
+                      "cpu_baseline": {"value": val, "unit": "ms/layer", "cores": 1, "kind": "reference",
+                                       "sample": "src/htrc_reference build_forest at one centre + evaluate of 2 "
+                                                 "queries per step on head 0, extrapolated to 32 centres x 245,952 "
+                                                 "queries x 24 heads"},
+                      "e2e": {"value": val, "unit": "ms/layer", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+          flush=True)
+
+
 def main():
     a = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -900,7 +1125,10 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if a.impl == "reference":
-        run_reference(a, wl, rank)
+        if wl.get("tree"):
+            run_tree_reference(a, wl, rank)
+        else:
+            run_reference(a, wl, rank)
         return
     if world > 1:
         import torch
@@ -909,7 +1137,10 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        run_ours(a, wl, rank, world, local_rank)
+        if wl.get("tree"):
+            run_tree(a, wl, rank, world, local_rank)
+        else:
+            run_ours(a, wl, rank, world, local_rank)
     finally:
         if world > 1:
             import torch.distributed as dist

@@ -51,6 +51,7 @@ class HtrcTreeDims(ctypes.Structure):
 
 
 TREE_MAX_LEVELS, TREE_MAX_CENTRES, TREE_KMEANS_CENTRES = 16, 256, 32
+TREE_STAGE_ACCEPT, TREE_STAGE_LEAVES, TREE_STAGE_FINAL, TREE_STAGE_ALL = 1, 2, 4, 7
 
 # name -> (restype, argtypes); every symbol include/htrc_flat.h and include/htrc_tree.h declare
 SIGNATURES = {
@@ -98,10 +99,10 @@ SIGNATURES = {
     "htrc_tree_forest_view": (ctypes.c_int, [ctypes.POINTER(HtrcTreeDims), _p, _i32] + [ctypes.POINTER(_p)] * 6),
     "htrc_tree_walk_size": (ctypes.c_int, [ctypes.POINTER(HtrcTreeDims), ctypes.POINTER(ctypes.c_size_t)]),
     "htrc_tree_walk": (ctypes.c_int, [ctypes.POINTER(HtrcTreeDims), _p, _p, _p, _p, _p, ctypes.c_size_t, _p, _p,
-                                      ctypes.POINTER(_i64), _p]),
+                                      _p, ctypes.POINTER(_i64), _p]),
     "htrc_tree_records_size": (ctypes.c_int, [_i64, ctypes.POINTER(ctypes.c_size_t)]),
     "htrc_tree_values": (ctypes.c_int, [ctypes.POINTER(HtrcTreeDims), _p, _p, _p, _p, _p, _p, _p, _i64,
-                                        ctypes.c_size_t, _p, _p, _p, _p]),
+                                        ctypes.c_size_t, _p, _p, _p, _i32, _p]),
     "htrc_tree_centres_scratch_size": (ctypes.c_int, [_i64, ctypes.POINTER(ctypes.c_size_t)]),
     "htrc_tree_centres": (ctypes.c_int, [_p, _i32, _i64, _f32, _p, _p, _p, ctypes.c_size_t, _p]),
 }

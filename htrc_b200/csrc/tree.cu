@@ -567,7 +567,8 @@ __global__ void __launch_bounds__(256) tree_walk_kernel(const T* __restrict__ q,
 // node and every visited leaf add one accepted entry).
 __global__ void __launch_bounds__(256) tree_count_kernel(TreeLevels lv, int64_t nq, int64_t* __restrict__ count,
                                                          int32_t* __restrict__ visited,
-                                                         int32_t* __restrict__ accepted) {
+                                                         int32_t* __restrict__ accepted,
+                                                         int32_t* __restrict__ leaves_out) {
   const int64_t qq = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
   if (qq >= nq) return;
   const int top = lv.top, F = lv.fanout;
@@ -575,6 +576,7 @@ __global__ void __launch_bounds__(256) tree_count_kernel(TreeLevels lv, int64_t 
     count[qq] = 1;
     visited[qq] = lv.n[0];
     accepted[qq] = lv.n[0];
+    if (leaves_out) leaves_out[qq] = lv.n[0];
     return;
   }
   int vis = lv.n[top], acc_int = 0;
@@ -594,6 +596,7 @@ __global__ void __launch_bounds__(256) tree_count_kernel(TreeLevels lv, int64_t 
   count[qq] = cnt;
   visited[qq] = vis + leaves;
   accepted[qq] = acc_int + leaves;
+  if (leaves_out) leaves_out[qq] = leaves;
 }
 
 // Exclusive prefix sum of count[0 .. n) into base[0 .. n] (base[n] = total).  One CTA of 1024 threads,
@@ -1528,8 +1531,8 @@ int build_impl(const HtrcTreeDims* d, const Shape& s, const T* k, const T* v, co
 
 template <typename T>
 int walk_impl(const HtrcTreeDims* d, const Shape& s, const T* q, const int32_t* assign, const float* centres,
-              const void* forest, void* walk, int32_t* visited, int32_t* accepted, int64_t* n_records,
-              cudaStream_t st) {
+              const void* forest, void* walk, int32_t* visited, int32_t* accepted, int32_t* leaves,
+              int64_t* n_records, cudaStream_t st) {
   const WalkLayout w = walk_layout(d, s);
   uint8_t* wb = static_cast<uint8_t*>(walk);
   const int C = d->n_centres;
@@ -1567,7 +1570,8 @@ int walk_impl(const HtrcTreeDims* d, const Shape& s, const T* q, const int32_t* 
     }
   }
   if (N > 0) {
-    tree_count_kernel<<<static_cast<unsigned>((N + 255) / 256), 256, 0, st>>>(lv, N, count, visited, accepted);
+    tree_count_kernel<<<static_cast<unsigned>((N + 255) / 256), 256, 0, st>>>(lv, N, count, visited, accepted,
+                                                                              leaves);
     tree_scan_kernel<<<1, 1024, 0, st>>>(count, N, base);
     if ((rc = launched()) != HTRC_OK) return rc;
   }
@@ -1584,7 +1588,7 @@ int walk_impl(const HtrcTreeDims* d, const Shape& s, const T* q, const int32_t* 
 template <typename T>
 int values_impl(const HtrcTreeDims* d, const Shape& s, const T* k, const T* v, const T* q, const float* centres,
                 const void* forest, void* walk, void* records, int64_t n_records, float* out, float* lse,
-                int32_t* exact, cudaStream_t st, bool tc_leaves) {
+                int32_t* exact, cudaStream_t st, bool tc_leaves, int stages) {
   const WalkLayout w = walk_layout(d, s);
   const ForestLayout f = forest_layout(d, s);
   const RecordLayout r = record_layout(n_records);
@@ -1606,7 +1610,7 @@ int values_impl(const HtrcTreeDims* d, const Shape& s, const T* k, const T* v, c
   if (rc != HTRC_OK) return rc;
   const TreeLevels lv = levels_of(d, s, forest, walk);
   const int top = s.levels - 1;
-  if (top >= 1) {
+  if (top >= 1 && (stages & HTRC_TREE_STAGE_ACCEPT)) {
     if ((rc = set_smem(tree_accept_kernel<T>, sizeof(AcceptSmem))) != HTRC_OK) return rc;
     for (int l = top; l >= 1; --l) {
       tree_accept_kernel<T><<<dim3(s.n[l], C, slices(mx, kSlice)), 256, sizeof(AcceptSmem), st>>>(
@@ -1614,7 +1618,8 @@ int values_impl(const HtrcTreeDims* d, const Shape& s, const T* k, const T* v, c
       if ((rc = launched()) != HTRC_OK) return rc;
     }
   }
-  if (std::is_same<T, uint16_t>::value && top >= 1 && tc_leaves) {
+  if (!(stages & HTRC_TREE_STAGE_LEAVES)) {
+  } else if (std::is_same<T, uint16_t>::value && top >= 1 && tc_leaves) {
     if ((rc = set_smem(tree_leafblock_tc_kernel, kTcSmemBytes)) != HTRC_OK) return rc;
     tree_leafblock_tc_kernel<<<dim3(s.n[1], C, slices(mx, kSlice)), 128, kTcSmemBytes, st>>>(
         reinterpret_cast<const uint16_t*>(q), reinterpret_cast<const uint16_t*>(k),
@@ -1627,9 +1632,11 @@ int values_impl(const HtrcTreeDims* d, const Shape& s, const T* k, const T* v, c
         rec_val, rec_lm, rec_ex, status);
   }
   if ((rc = launched()) != HTRC_OK) return rc;
-  tree_final_kernel<<<static_cast<unsigned>((N + 7) / 8), 256, 0, st>>>(N, base, rec_val, rec_lm, rec_ex, out, lse,
-                                                                        exact);
-  if ((rc = launched()) != HTRC_OK) return rc;
+  if (stages & HTRC_TREE_STAGE_FINAL) {
+    tree_final_kernel<<<static_cast<unsigned>((N + 7) / 8), 256, 0, st>>>(N, base, rec_val, rec_lm, rec_ex, out, lse,
+                                                                          exact);
+    if ((rc = launched()) != HTRC_OK) return rc;
+  }
   int stat = 0;
   if (cudaMemcpyAsync(&stat, status, 4, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
       cudaStreamSynchronize(st) != cudaSuccess)
@@ -1708,7 +1715,7 @@ int htrc_tree_walk_size(const HtrcTreeDims* dims, size_t* bytes) {
 
 int htrc_tree_walk(const HtrcTreeDims* dims, const void* queries, const int32_t* assign, const float* centres,
                    const void* forest, void* walk, size_t walk_bytes, int32_t* visited, int32_t* accepted,
-                   int64_t* n_records, htrc_stream_t stream) {
+                   int32_t* leaves, int64_t* n_records, htrc_stream_t stream) {
   Shape s;
   int rc = shape_of(dims, &s);
   if (rc != HTRC_OK) return rc;
@@ -1722,9 +1729,9 @@ int htrc_tree_walk(const HtrcTreeDims* dims, const void* queries, const int32_t*
   const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (dims->q_dtype == HTRC_DTYPE_BF16)
     return walk_impl<uint16_t>(dims, s, static_cast<const uint16_t*>(queries), assign, centres, forest, walk, visited,
-                               accepted, n_records, st);
+                               accepted, leaves, n_records, st);
   return walk_impl<float>(dims, s, static_cast<const float*>(queries), assign, centres, forest, walk, visited,
-                          accepted, n_records, st);
+                          accepted, leaves, n_records, st);
 }
 
 int htrc_tree_records_size(int64_t n_records, size_t* bytes) {
@@ -1735,12 +1742,14 @@ int htrc_tree_records_size(int64_t n_records, size_t* bytes) {
 
 int htrc_tree_values(const HtrcTreeDims* dims, const void* keys, const void* values, const void* queries,
                      const float* centres, const void* forest, void* walk, void* records, int64_t n_records,
-                     size_t records_bytes, float* out, float* lse, int32_t* exact_leaves, htrc_stream_t stream) {
+                     size_t records_bytes, float* out, float* lse, int32_t* exact_leaves, int32_t stages,
+                     htrc_stream_t stream) {
   Shape s;
   int rc = shape_of(dims, &s);
   if (rc != HTRC_OK) return rc;
   if (dims->n_queries == 0) return HTRC_OK;
-  if (!keys || !values || !queries || !centres || !forest || !out || !lse || !exact_leaves || n_records < 0)
+  if (!keys || !values || !queries || !centres || !forest || !out || !lse || !exact_leaves || n_records < 0 ||
+      stages < 1 || stages > HTRC_TREE_STAGE_ALL)
     return HTRC_ERR_ARG;
   if (dims->q_dtype != dims->kv_dtype) return HTRC_ERR_UNSUPPORTED;
   if (!walk || !aligned(walk)) return HTRC_ERR_WORKSPACE;
@@ -1750,10 +1759,10 @@ int htrc_tree_values(const HtrcTreeDims* dims, const void* keys, const void* val
   if (dims->kv_dtype == HTRC_DTYPE_BF16)
     return values_impl<uint16_t>(dims, s, static_cast<const uint16_t*>(keys), static_cast<const uint16_t*>(values),
                                  static_cast<const uint16_t*>(queries), centres, forest, walk, records, n_records,
-                                 out, lse, exact_leaves, st, tc_leaves_enabled());
+                                 out, lse, exact_leaves, st, tc_leaves_enabled(), stages);
   return values_impl<float>(dims, s, static_cast<const float*>(keys), static_cast<const float*>(values),
                             static_cast<const float*>(queries), centres, forest, walk, records, n_records, out, lse,
-                            exact_leaves, st, false);
+                            exact_leaves, st, false, stages);
 }
 
 int htrc_tree_centres_scratch_size(int64_t n_queries, size_t* bytes) {

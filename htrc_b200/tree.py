@@ -155,15 +155,17 @@ def build_forest(keys, values, center, *, leaf_size=16, fanout=4, device=None):
     return Forest(kd, vd, cd, int(leaf_size), int(fanout), int(kt.shape[1]), int(vt.shape[1]), dev)
 
 
-def _run(forest, qd, assign, scale, thr, stream=None):
-    """Walk + values for device queries qd [N, 128] (forest's dtype) -> out [N, 128], lse [N], counters."""
+def _run(forest, qd, assign, scale, thr, stream=None, marks=None):
+    """Walk + values for device queries qd [N, 128] (forest's dtype) -> out [N, 128], lse [N] and counters
+    [4, N] int32 (visited_nodes, accepted_nodes, exact_leaves, leaves visited).  marks: None, or a list that
+    receives (name, CUDA event) after each stage (walk, accept, leaves, final) for stage timing."""
     n = qd.shape[0]
     dev = forest.device
     L = _lib.lib()
     dims = forest.dims(n, scale, thr, _code(qd))
     out = torch.empty((n, D_MAX), dtype=torch.float32, device=dev)
     lse = torch.empty((n,), dtype=torch.float32, device=dev)
-    cnt = torch.zeros((3, n), dtype=torch.int32, device=dev)
+    cnt = torch.zeros((4, n), dtype=torch.int32, device=dev)
     if n == 0:
         return out, lse, cnt
     need = ctypes.c_size_t()
@@ -171,16 +173,30 @@ def _run(forest, qd, assign, scale, thr, stream=None):
     wbuf = _buffer(need.value, dev)
     wptr, wbytes = _aligned(wbuf)
     s = _lib.stream_ptr(stream)
+
+    def mark(name):
+        if marks is not None:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record(torch.cuda.current_stream() if stream is None else stream)
+            marks.append((name, e))
+
+    mark("start")
     nrec = _lib._i64()
     _lib.check(L.htrc_tree_walk(ctypes.byref(dims), _lib.ptr(qd), _lib.ptr(assign), _lib.ptr(forest.centres),
-                                forest._ptr, wptr, wbytes, _lib.ptr(cnt[0]), _lib.ptr(cnt[1]), ctypes.byref(nrec), s),
-               "tree walk")
+                                forest._ptr, wptr, wbytes, _lib.ptr(cnt[0]), _lib.ptr(cnt[1]), _lib.ptr(cnt[3]),
+                                ctypes.byref(nrec), s), "tree walk")
+    mark("walk")
     _lib.check(L.htrc_tree_records_size(nrec.value, ctypes.byref(need)), "tree records size")
     rbuf = _buffer(need.value, dev)
     rptr, rbytes = _aligned(rbuf)
-    _lib.check(L.htrc_tree_values(ctypes.byref(dims), _lib.ptr(forest.keys), _lib.ptr(forest.values), _lib.ptr(qd),
-                                  _lib.ptr(forest.centres), forest._ptr, wptr, rptr, nrec.value, rbytes, _lib.ptr(out),
-                                  _lib.ptr(lse), _lib.ptr(cnt[2]), s), "tree values")
+    stages = [(_lib.TREE_STAGE_ALL, None)] if marks is None else \
+        [(_lib.TREE_STAGE_ACCEPT, "accept"), (_lib.TREE_STAGE_LEAVES, "leaves"), (_lib.TREE_STAGE_FINAL, "final")]
+    for bits, name in stages:
+        _lib.check(L.htrc_tree_values(ctypes.byref(dims), _lib.ptr(forest.keys), _lib.ptr(forest.values),
+                                      _lib.ptr(qd), _lib.ptr(forest.centres), forest._ptr, wptr, rptr, nrec.value,
+                                      rbytes, _lib.ptr(out), _lib.ptr(lse), _lib.ptr(cnt[2]), bits, s), "tree values")
+        if name:
+            mark(name)
     return out, lse, cnt
 
 
@@ -243,7 +259,7 @@ def queries_centres(q, scale, device=None):
 
 
 def tree_attention(q, k, v, *, leaf_size=64, fanout=16, opening_threshold=0.02, scale=None, return_lse=False,
-                   return_info=False, centres=None, assign=None):
+                   return_info=False, centres=None, assign=None, marks=None):
     """The hierarchical operator on one head: q [N, 128], k / v [M, 128] (bfloat16 or float32, on the
     GPU).  Query centres: the k-means of `queries_centres` unless `centres` [C, 128] (scaled space) and
     `assign` [N] are given.  Returns out [N, 128] float32 (+ lse [N], + counters dict)."""
@@ -256,17 +272,30 @@ def tree_attention(q, k, v, *, leaf_size=64, fanout=16, opening_threshold=0.02, 
     dev = q.device
     kv_dtype = torch.bfloat16 if k.dtype == torch.bfloat16 else torch.float32
     qd, kd, vd = (x.to(dtype=kv_dtype).contiguous() for x in (q, k, v))
+    if marks is not None:
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        marks.append(("begin", e))
     if centres is None:
         centres, assign = queries_centres(qd, sc)
     elif assign is None:
         raise ValueError("assign= is required with explicit centres")
+    if marks is not None:
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        marks.append(("centres", e))
     forest = Forest(kd, vd, centres.to(device=dev, dtype=torch.float32).contiguous(), int(leaf_size), int(fanout),
                     D_MAX, D_MAX, dev)
-    out, lse, cnt = _run(forest, qd, assign.to(device=dev, dtype=torch.int32).contiguous(), sc, opening_threshold)
+    if marks is not None:
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        marks.append(("build", e))
+    out, lse, cnt = _run(forest, qd, assign.to(device=dev, dtype=torch.int32).contiguous(), sc, opening_threshold,
+                         marks=marks)
     res = [out]
     if return_lse:
         res.append(lse)
     if return_info:
-        res.append({"visited_nodes": cnt[0], "accepted_nodes": cnt[1], "exact_leaves": cnt[2], "centres": centres,
-                    "assign": assign, "forest": forest})
+        res.append({"visited_nodes": cnt[0], "accepted_nodes": cnt[1], "exact_leaves": cnt[2], "leaves": cnt[3],
+                    "centres": centres, "assign": assign, "forest": forest})
     return res[0] if len(res) == 1 else tuple(res)

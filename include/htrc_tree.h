@@ -27,6 +27,9 @@ extern "C" {
 #endif
 
 enum { HTRC_TREE_MAX_LEVELS = 16, HTRC_TREE_MAX_CENTRES = 256, HTRC_TREE_KMEANS_CENTRES = 32 };
+/* htrc_tree_values stages (OR-ed; run in this order): records of accepted internal nodes, records of the
+ * opened level-1 nodes' leaf blocks, and the per-query merge into out / lse / exact_leaves */
+enum { HTRC_TREE_STAGE_ACCEPT = 1, HTRC_TREE_STAGE_LEAVES = 2, HTRC_TREE_STAGE_FINAL = 4, HTRC_TREE_STAGE_ALL = 7 };
 
 typedef struct {
   int64_t n_keys;      /* >= 1 */
@@ -54,21 +57,24 @@ int htrc_tree_forest_view(const HtrcTreeDims* dims, const void* forest, int32_t 
                           const float** L, const float** g, const float** u, const float** H, const float** JT);
 
 /* Walk (model.py:104-127): per query the opened / accepted nodes of every level, and the reference's
- * counters visited_nodes and accepted_nodes [n_queries] int32.  Synchronises the stream and returns the
- * number of partial records in *n_records.  HTRC_ERR_ARG if an assign entry is out of range. */
+ * counters visited_nodes and accepted_nodes [n_queries] int32 (leaves: NULL or [n_queries] int32, the leaves
+ * each query visits).  Synchronises the stream and returns the number of partial records in *n_records.
+ * HTRC_ERR_ARG if an assign entry is out of range. */
 int htrc_tree_walk_size(const HtrcTreeDims* dims, size_t* bytes);
 int htrc_tree_walk(const HtrcTreeDims* dims, const void* queries, const int32_t* assign, const float* centres,
                    const void* forest, void* walk, size_t walk_bytes, int32_t* visited, int32_t* accepted,
-                   int64_t* n_records, htrc_stream_t stream);
+                   int32_t* leaves, int64_t* n_records, htrc_stream_t stream);
 
 /* Values (model.py:91-96, :122-137): out [n_queries, 128] float32, lse [n_queries] float32 (log-sum-exp
  * of the accepted log-masses, the operator's log-Z; the reference does not return it) and exact_leaves
  * [n_queries] int32.  records: htrc_tree_records_size(n_records) bytes, n_records as htrc_tree_walk
- * returned it.  keys, values and queries share one dtype. */
+ * returned it; stages: HTRC_TREE_STAGE_* bits (HTRC_TREE_STAGE_ALL for the whole evaluation; a subset lets a
+ * caller time the stages).  keys, values and queries share one dtype. */
 int htrc_tree_records_size(int64_t n_records, size_t* bytes);
 int htrc_tree_values(const HtrcTreeDims* dims, const void* keys, const void* values, const void* queries,
                      const float* centres, const void* forest, void* walk, void* records, int64_t n_records,
-                     size_t records_bytes, float* out, float* lse, int32_t* exact_leaves, htrc_stream_t stream);
+                     size_t records_bytes, float* out, float* lse, int32_t* exact_leaves, int32_t stages,
+                     htrc_stream_t stream);
 
 /* Query centres for the operator: the k-means of htrc_kmeans_order (32 clusters, Lloyd x 8 on an even
  * sample of at most 4096 rows), scaled by `scale` -> centres [32, 128] float32, and the nearest centre

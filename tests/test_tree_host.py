@@ -62,15 +62,16 @@ def test_entry_points_validate_before_the_device():
     nrec = _lib._i64(-5)
     # null inputs are argument errors; a missing walk buffer is a workspace error
     assert L.htrc_tree_build(ctypes.byref(d), None, None, None, None, 0, None) == _lib.HTRC_ERR_ARG
-    assert L.htrc_tree_walk(ctypes.byref(d), None, None, None, None, None, 0, None, None, None, None) == _lib.HTRC_ERR_ARG
-    assert L.htrc_tree_walk(ctypes.byref(d), 1, 1, 1, 1, None, 0, 1, 1, ctypes.byref(nrec), None) == \
+    assert L.htrc_tree_walk(ctypes.byref(d), None, None, None, None, None, 0, None, None, None, None, None) == \
+        _lib.HTRC_ERR_ARG
+    assert L.htrc_tree_walk(ctypes.byref(d), 1, 1, 1, 1, None, 0, 1, 1, None, ctypes.byref(nrec), None) == \
         _lib.HTRC_ERR_WORKSPACE
     assert nrec.value == 0
     d.q_dtype = _lib.DTYPE_BF16                            # queries and keys must share a dtype
-    assert L.htrc_tree_walk(ctypes.byref(d), 1, 1, 1, 1, None, 0, 1, 1, ctypes.byref(nrec), None) == \
+    assert L.htrc_tree_walk(ctypes.byref(d), 1, 1, 1, 1, None, 0, 1, 1, None, ctypes.byref(nrec), None) == \
         _lib.HTRC_ERR_UNSUPPORTED
     d0 = tree._dims(1000, 0, 1, 16, 4, _lib.DTYPE_F32, _lib.DTYPE_F32, 1.0, 0.01)
-    assert L.htrc_tree_walk(ctypes.byref(d0), None, None, None, None, None, 0, None, None, ctypes.byref(nrec),
+    assert L.htrc_tree_walk(ctypes.byref(d0), None, None, None, None, None, 0, None, None, None, ctypes.byref(nrec),
                             None) == _lib.HTRC_OK
     assert nrec.value == 0
 
