@@ -1043,9 +1043,9 @@ constexpr int kTcQ = 128;
 constexpr int kTcCols = 256;         // TMEM columns: S 0..63, P hi 64..95, P lo 96..127, O 128..255
 struct __align__(1024) TcSmem {
   uint8_t qs[2 * kTcQ * 128];        // queries: two K-blocks of [128 rows][128 B]  (K-major A)
-  uint8_t ks[2 * 64 * 128];          // keys: two K-blocks of [64 rows][128 B]       (K-major B)
-  uint8_t vs[2 * 64 * 128];          // values: two N-chunks of [64 key rows][128 B] (MN-major B)
-  float as[64], ws[64];
+  uint8_t ks[2][2 * 64 * 128];       // keys, two leaves in flight: two K-blocks of [64 rows][128 B] (K-major B)
+  uint8_t vs[2][2 * 64 * 128];       // values, two leaves: two N-chunks of [64 key rows][128 B]   (MN-major B)
+  float as[2][64], ws[2][64];
   int64_t rec[kTcQ];
   int list[kWindow];
   int wsum[4];
@@ -1084,6 +1084,14 @@ __device__ int gather_window128(const int32_t* __restrict__ perm, int64_t lo, in
   return total;
 }
 
+// 16-byte asynchronous global -> shared copy; src_bytes 0 writes zeros (the source is not read)
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
                : "memory");
@@ -1119,7 +1127,22 @@ __global__ void __launch_bounds__(128, 1) tree_leafblock_tc_kernel(
   const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
   const uint32_t id_s = idesc_bf16(128, 64, false, false);
   const uint32_t id_pv = idesc_bf16(128, 128, false, true);
-  const uint32_t qa = smem_u32(sh.qs), ka = smem_u32(sh.ks), va = smem_u32(sh.vs);
+  const uint32_t qa = smem_u32(sh.qs);
+  // the keys and values of leaf l into buffer b (one cp.async group; rows past the leaf's keys are zeros)
+  auto stage_kv = [&](int l, int b) {
+    const int64_t s0 = static_cast<int64_t>(l) * leaf;
+    const int kc = static_cast<int>(m - s0 < leaf ? m - s0 : leaf);
+    const uint32_t kb = smem_u32(sh.ks[b]), vb = smem_u32(sh.vs[b]);
+    for (int x = tid; x < 64 * 16; x += 128) {
+      const int r = x >> 4, cc = x & 15;
+      const uint32_t nb = r < kc ? 16u : 0u;
+      const int64_t row = s0 + (r < kc ? r : 0);
+      const uint32_t off = (cc >> 3) * (64 * 128) + sw128_off(r, cc & 7);
+      cp_async16(kb + off, k + row * kD + cc * 8, nb);
+      cp_async16(vb + off, v + row * kD + cc * 8, nb);
+    }
+    cp_async_commit();
+  };
   uint32_t ph_s = 0, ph_pv = 0;
   bool ok = true;
   for (int64_t win = lo; win < hi && ok; win += kWindow) {
@@ -1137,25 +1160,27 @@ __global__ void __launch_bounds__(128, 1) tree_leafblock_tc_kernel(
       const float nrm = live ? norm[lst[tid]] : 0.f;
       float m_run = -INFINITY, s_run = 0.f;
       int nex = 0;
+      stage_kv(l0, 0);
       for (int l = l0; l < l1; ++l) {
+        const int b = (l - l0) & 1;
         const int64_t s0 = static_cast<int64_t>(l) * leaf;
         const int kc = static_cast<int>(m - s0 < leaf ? m - s0 : leaf);
         const float ll = lL[l];
-        for (int x = tid; x < 64 * 16; x += 128) {
-          const int r = x >> 4, cc = x & 15;
-          uint4 kv = make_uint4(0u, 0u, 0u, 0u), vv = kv;
-          if (r < kc) {
-            kv = __ldg(reinterpret_cast<const uint4*>(k + (s0 + r) * kD) + cc);
-            vv = __ldg(reinterpret_cast<const uint4*>(v + (s0 + r) * kD) + cc);
-          }
-          st_shared_v4(ka + (cc >> 3) * (64 * 128) + sw128_off(r, cc & 7), kv);
-          st_shared_v4(va + (cc >> 3) * (64 * 128) + sw128_off(r, cc & 7), vv);
+        // the next leaf's copies go out now (its buffer's last readers, the MMAs of leaf l - 1, completed)
+        if (l + 1 < l1) {
+          stage_kv(l + 1, b ^ 1);
+          cp_async_wait<1>();
+        } else {
+          cp_async_wait<0>();
         }
         if (tid < 64) {
           const float av = tid < kc ? ac[s0 + tid] : 0.f;
-          sh.as[tid] = av;
-          sh.ws[tid] = tid < kc ? expf(av - ll) : 0.f;
+          sh.as[b][tid] = av;
+          sh.ws[b][tid] = tid < kc ? expf(av - ll) : 0.f;
         }
+        const uint32_t ka = smem_u32(sh.ks[b]), va = smem_u32(sh.vs[b]);
+        const float* as_ = sh.as[b];
+        const float* ws_ = sh.ws[b];
         fence_proxy_async_smem();
         __syncthreads();
         if (tid == 0) {
@@ -1187,28 +1212,59 @@ __global__ void __launch_bounds__(128, 1) tree_leafblock_tc_kernel(
             S[32 + j] = scale * __uint_as_float(r1[j]);
           }
         }
-        float xb = 0.f;
+        // four independent partial sums per reduction (the chains are the row math's latency)
+        const float4* w4p = reinterpret_cast<const float4*>(ws_);
+        const float4* a4p = reinterpret_cast<const float4*>(as_);
+        float xb;
+        {
+          float p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
 #pragma unroll
-        for (int j = 0; j < 64; ++j) xb = fmaf(sh.ws[j], S[j] - sh.as[j], xb);
-        float qd = 0.f;
+          for (int j = 0; j < 64; j += 4) {
+            const float4 w4 = w4p[j >> 2], a4 = a4p[j >> 2];
+            p0 = fmaf(w4.x, S[j] - a4.x, p0);
+            p1 = fmaf(w4.y, S[j + 1] - a4.y, p1);
+            p2 = fmaf(w4.z, S[j + 2] - a4.z, p2);
+            p3 = fmaf(w4.w, S[j + 3] - a4.w, p3);
+          }
+          xb = (p0 + p1) + (p2 + p3);
+        }
+        float qd;
+        {
+          float p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
 #pragma unroll
-        for (int j = 0; j < 64; ++j) {
-          const float e = S[j] - sh.as[j] - xb;
-          qd = fmaf(sh.ws[j] * e, e, qd);
+          for (int j = 0; j < 64; j += 4) {
+            const float4 w4 = w4p[j >> 2], a4 = a4p[j >> 2];
+            const float e0 = S[j] - a4.x - xb, e1 = S[j + 1] - a4.y - xb;
+            const float e2 = S[j + 2] - a4.z - xb, e3 = S[j + 3] - a4.w - xb;
+            p0 = fmaf(w4.x * e0, e0, p0);
+            p1 = fmaf(w4.y * e1, e1, p1);
+            p2 = fmaf(w4.z * e2, e2, p2);
+            p3 = fmaf(w4.w * e3, e3, p3);
+          }
+          qd = (p0 + p1) + (p2 + p3);
         }
         const float lmv = ll + xb + 0.5f * qd;
         const bool open = live && score_of(lmv, qd, nrm) > thr;
         float mass = lmv;
         if (open) {
-          float mx = -INFINITY;
+          float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
 #pragma unroll
-          for (int j = 0; j < 64; ++j)
-            if (j < kc) mx = fmaxf(mx, S[j]);
-          float se = 0.f;
+          for (int j = 0; j < 64; j += 4) {
+            if (j < kc) m0 = fmaxf(m0, S[j]);
+            if (j + 1 < kc) m1 = fmaxf(m1, S[j + 1]);
+            if (j + 2 < kc) m2 = fmaxf(m2, S[j + 2]);
+            if (j + 3 < kc) m3 = fmaxf(m3, S[j + 3]);
+          }
+          const float mx = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
+          float e0 = 0.f, e1 = 0.f, e2 = 0.f, e3 = 0.f;
 #pragma unroll
-          for (int j = 0; j < 64; ++j)
-            if (j < kc) se += expf(S[j] - mx);
-          mass = mx + logf(se);
+          for (int j = 0; j < 64; j += 4) {
+            if (j < kc) e0 += __expf(S[j] - mx);
+            if (j + 1 < kc) e1 += __expf(S[j + 1] - mx);
+            if (j + 2 < kc) e2 += __expf(S[j + 2] - mx);
+            if (j + 3 < kc) e3 += __expf(S[j + 3] - mx);
+          }
+          mass = mx + logf((e0 + e1) + (e2 + e3));
         }
         const float mn = live ? fmaxf(m_run, mass) : 0.f;
         const float al = live ? expf(m_run - mn) : 1.f;
@@ -1218,6 +1274,7 @@ __global__ void __launch_bounds__(128, 1) tree_leafblock_tc_kernel(
         }
         nex += open;
         const float fw = expf(lmv - mn);
+        const float c0 = fw * (1.f - xb);          // far coefficient: w (fw (1 + x - xbar)) = w (fw x + c0)
         // rescale O (its previous PV has completed).  tcgen05.ld / st are warp-collective (.sync.aligned):
         // the warp takes the branch as a whole, rows whose maximum did not move scale by 1
         if (__any_sync(0xffffffffu, l > l0 && al != 1.f)) {
@@ -1242,7 +1299,7 @@ __global__ void __launch_bounds__(128, 1) tree_leafblock_tc_kernel(
               const int jj = 32 * h + j + t;
               pc[t] = 0.f;
               if (live && jj < kc)
-                pc[t] = open ? expf(S[jj] - mn) : fw * sh.ws[jj] * (1.f + (S[jj] - sh.as[jj] - xb));
+                pc[t] = open ? __expf(S[jj] - mn) : ws_[jj] * fmaf(fw, S[jj] - as_[jj], c0);
             }
             const __nv_bfloat162 hb = __floats2bfloat162_rn(pc[0], pc[1]);
             const float2 hf = __bfloat1622float2(hb);
@@ -1305,6 +1362,7 @@ __global__ void __launch_bounds__(128, 1) tree_leafblock_tc_kernel(
       tc_fence_after();
     }
   }
+  cp_async_wait<0>();                       // no copy may land after the CTA leaves (an aborted chunk)
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, kTcCols);
