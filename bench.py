@@ -55,6 +55,10 @@ WORKLOADS = {
     "cfg5": dict(grid=(61, 48, 84), heads=24, tree=True, leaf=64, fanout=16, threshold=0.02,
                  name="cfg5: hierarchical HTRC, 245,952-token 61x48x84 latent layer, 24 heads, d128, leaf 64, fanout "
                       "16, threshold 0.02, 32 k-means query centres, second-order log-mass + value dipole"),
+    # profiling-sized hierarchical case: one 64,512-token head (forest 0.3 GB, records ~1.7 GB)
+    "tree_prof": dict(grid=(16, 48, 84), heads=1, tree=True, leaf=64, fanout=16, threshold=0.02,
+                      name="tree_prof: hierarchical HTRC, one 64,512-token 16x48x84 head, d128, leaf 64, fanout 16, "
+                           "threshold 0.02, 32 k-means query centres"),
     # profiling-sized case: one head, half of cfg3's frames (leaf state ~400 MB > L2, < 1 GB on the device)
     "prof": dict(grid=(16, 48, 84), heads=1, exact_leaves=256,
                  name="prof: one 64,512-token 16x48x84 head, d128, leaf 64, tile 64, fast (E=256), INT8"),
@@ -1059,7 +1063,7 @@ def run_tree(a, wl, rank, world, local_rank):
                          f"centres and {timing['queries']} of their queries, extrapolated to {ncen} centres x {n} "
                          f"queries x {H} heads", **timing}
     if rank == 0:
-        line = {"metric": "hierarchical-HTRC ms per 245,952-token 24-head d128 layer", "value": ms, "unit": "ms/layer",
+        line = {"metric": f"hierarchical-HTRC ms per {n:,}-token {H}-head d128 layer", "value": ms, "unit": "ms/layer",
                 "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": False,
                 "scaling": "strong", "vs_baseline": None,
                 "dtype": "bf16 q.k and P.v on tcgen05 (P as bf16 hi + lo), f32 node predictions and decisions",
