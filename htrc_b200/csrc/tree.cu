@@ -211,6 +211,21 @@ __global__ void __launch_bounds__(64) tree_leaf_kernel(const T* __restrict__ k, 
   if (tid == 0) leaf_l[static_cast<int64_t>(c) * nl + l] = mx + logf(red[0]);
 }
 
+// 8 floats -> their bf16 parts: hi = bf16(x), lo = bf16(x - hi) (16 bytes each)
+__device__ __forceinline__ void split_bf16x8(const float* x, uint4* hi, uint4* lo) {
+  uint32_t h[4], l[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __nv_bfloat162 hb = __floats2bfloat162_rn(x[2 * i], x[2 * i + 1]);
+    const float2 hf = __bfloat1622float2(hb);
+    h[i] = *reinterpret_cast<const uint32_t*>(&hb);
+    const __nv_bfloat162 lb = __floats2bfloat162_rn(x[2 * i] - hf.x, x[2 * i + 1] - hf.y);
+    l[i] = *reinterpret_cast<const uint32_t*>(&lb);
+  }
+  *hi = make_uint4(h[0], h[1], h[2], h[3]);
+  *lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
 // ---------------------------------------------------------------------------------------------------
 // Level-1 nodes from their keys (model.py:35-49 over the node's keys, equal by the merge identity of
 // model.py:51-66 to merging its leaves).  One CTA of 256 threads per (node, centre); the node's keys
@@ -231,7 +246,8 @@ __global__ void __launch_bounds__(256, 1) tree_gram_kernel(const T* __restrict__
                                                            const float* __restrict__ leaf_l, int n1,
                                                            float* __restrict__ L1, float* __restrict__ g1,
                                                            float* __restrict__ u1, float* __restrict__ H1,
-                                                           float* __restrict__ JT1) {
+                                                           float* __restrict__ JT1, uint16_t* __restrict__ Hb1,
+                                                           uint16_t* __restrict__ Jb1) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   GramSmem& sh = *reinterpret_cast<GramSmem*>(smem_raw);
   const int i = blockIdx.x, c = blockIdx.y, tid = threadIdx.x;
@@ -326,6 +342,19 @@ __global__ void __launch_bounds__(256, 1) tree_gram_kernel(const T* __restrict__
     *reinterpret_cast<float4*>(jn + (cb * 8 + y) * kD + rb * 8) = make_float4(j[0][y], j[1][y], j[2][y], j[3][y]);
     *reinterpret_cast<float4*>(jn + (cb * 8 + y) * kD + rb * 8 + 4) = make_float4(j[4][y], j[5][y], j[6][y], j[7][y]);
   }
+  // bf16 hi / lo operand copies for the tensor-core walk: H rows and J rows (J[d][e], d = value dim)
+  uint16_t* hb = Hb1 + node * 2 * kD * kD;
+  uint16_t* jb = Jb1 + node * 2 * kD * kD;
+#pragma unroll
+  for (int x = 0; x < 8; ++x) {
+    uint4 hi, lo;
+    split_bf16x8(h[x], &hi, &lo);
+    *reinterpret_cast<uint4*>(hb + (rb * 8 + x) * kD + cb * 8) = hi;
+    *reinterpret_cast<uint4*>(hb + kD * kD + (rb * 8 + x) * kD + cb * 8) = lo;
+    split_bf16x8(j[x], &hi, &lo);
+    *reinterpret_cast<uint4*>(jb + (rb * 8 + x) * kD + cb * 8) = hi;
+    *reinterpret_cast<uint4*>(jb + kD * kD + (rb * 8 + x) * kD + cb * 8) = lo;
+  }
 }
 
 // Levels >= 2 (model.py:51-66): w = softmax of the children's log-masses, g = sum w g_c, u = sum w u_c,
@@ -344,7 +373,8 @@ __global__ void __launch_bounds__(256) tree_merge_kernel(int fanout, int nch, co
                                                          const float* __restrict__ Hc, const float* __restrict__ JTc,
                                                          int np, float* __restrict__ Lp, float* __restrict__ gp,
                                                          float* __restrict__ up, float* __restrict__ Hp,
-                                                         float* __restrict__ JTp) {
+                                                         float* __restrict__ JTp, uint16_t* __restrict__ Hbp,
+                                                         uint16_t* __restrict__ Jbp) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   MergeSmem& sh = *reinterpret_cast<MergeSmem*>(smem_raw);
   const int i = blockIdx.x, c = blockIdx.y, tid = threadIdx.x;
@@ -388,6 +418,13 @@ __global__ void __launch_bounds__(256) tree_merge_kernel(int fanout, int nch, co
     }
     Hp[node * kD * kD + e] = hs;
     JTp[node * kD * kD + e] = js;
+    const __nv_bfloat16 hh = __float2bfloat16_rn(hs), jh = __float2bfloat16_rn(js);
+    uint16_t* hb = Hbp + node * 2 * kD * kD;
+    uint16_t* jb = Jbp + node * 2 * kD * kD;
+    hb[e] = __bfloat16_as_ushort(hh);
+    hb[kD * kD + e] = __bfloat16_as_ushort(__float2bfloat16_rn(hs - __bfloat162float(hh)));
+    jb[f * kD + r] = __bfloat16_as_ushort(jh);                       // J[f][r] = J^T[r][f]
+    jb[kD * kD + f * kD + r] = __bfloat16_as_ushort(__float2bfloat16_rn(js - __bfloat162float(jh)));
   }
 }
 
@@ -405,6 +442,8 @@ struct TreeLevels {
   const float* u[kMaxLevels]; // [C][n][128]     (l >= 1)
   const float* H[kMaxLevels]; // [C][n][128][128] (l >= 1)
   const float* JT[kMaxLevels];// [C][n][128][128] (l >= 1), J transposed
+  const uint16_t* Hb[kMaxLevels];  // [C][n][2][128][128] bf16 hi and lo parts of H (rows)
+  const uint16_t* Jb[kMaxLevels];  // [C][n][2][128][128] bf16 hi and lo parts of J (rows: value dims)
 };
 
 // Stage delta rows (scale * q - c) of list[0 .. nq) into ds[64][kStr]; rows nq..63 are zero.
@@ -1369,6 +1408,238 @@ __global__ void __launch_bounds__(128, 1) tree_leafblock_tc_kernel(
 }
 
 // ---------------------------------------------------------------------------------------------------
+// Internal nodes on the tensor cores: for a chunk of 128 gathered queries, Y = D . M with D = scale q - c
+// (float32, split into bf16 hi + lo parts) and M a node's H (walk) or J (accept) as bf16 hi + lo rows:
+// Y = Dh Mh + Dh Ml + Dl Mh, three chains of kind::f16 MMAs (M 128 x N 128 x K 128) into TMEM.
+//   walk   (ACCEPT = false): one CTA per (parent, centre, slice) over the queries that opened the parent; the
+//          parent's children one after another, their operands double-buffered by cp.async and Y
+//          double-buffered in TMEM so that the next child's MMAs run during this child's epilogue; per row
+//          lm = L + g.d + d.Y / 2, the decision (model.py:112-127), the bits (the roots stay on
+//          tree_walk_kernel, whose decisions need every root's prediction first)
+//   accept (ACCEPT = true):  one CTA per (node, centre, slice) over the queries that accepted the node;
+//          val = u + Y (model.py:91-96) -> the query's record
+// One thread per query row (= TMEM lane); every MMA completion wait is bounded.
+struct __align__(1024) NodeSmem {
+  uint8_t a[2][2][kTcQ * 128];       // D: [hi, lo][K-block][128 rows x 128 B]  (K-major A)
+  uint8_t b[2][2][2][kTcQ * 128];    // M: [buffer][hi, lo][K-block][128 rows x 128 B] (K-major B)
+  int64_t rec[kTcQ];
+  int list[kWindow];
+  int wsum[4];
+  uint64_t bar[2];
+  uint32_t tmem_base;
+  int abort_flag;
+};
+constexpr size_t kNodeSmemBytes = sizeof(NodeSmem) + 1024;
+
+template <typename T>
+__device__ __forceinline__ void load_row128(const T* q, int64_t row, float scale, const float* __restrict__ c,
+                                            float (&d)[kD]) {
+#pragma unroll
+  for (int c4 = 0; c4 < 32; ++c4) {
+    const float4 x = ld_row4<T>(q, row, c4);
+    const float4 cc = __ldg(reinterpret_cast<const float4*>(c) + c4);
+    d[4 * c4] = fmaf(scale, x.x, -cc.x);
+    d[4 * c4 + 1] = fmaf(scale, x.y, -cc.y);
+    d[4 * c4 + 2] = fmaf(scale, x.z, -cc.z);
+    d[4 * c4 + 3] = fmaf(scale, x.w, -cc.w);
+  }
+}
+
+template <typename T, bool ACCEPT>
+__global__ void __launch_bounds__(128, 1) tree_node_tc_kernel(
+    const T* __restrict__ q, float scale, const float* __restrict__ centres, const int32_t* __restrict__ perm,
+    const int64_t* __restrict__ coff, int64_t slice, TreeLevels lv, int lev, float thr,
+    const float* __restrict__ norm, const int64_t* __restrict__ base, int64_t nrec, float* __restrict__ rec_val,
+    float* __restrict__ rec_lm, int32_t* __restrict__ rec_ex, int* __restrict__ status) {
+  extern __shared__ unsigned char smem_raw[];
+  NodeSmem& sh = *reinterpret_cast<NodeSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int c = blockIdx.y, tid = threadIdx.x, warp = tid >> 5;
+  const int64_t lo = coff[c] + static_cast<int64_t>(blockIdx.z) * slice;
+  const int64_t hi = min(coff[c + 1], lo + slice);
+  if (lo >= hi) return;
+  const int n_lev = lv.n[lev];
+  // walk: the children of parent blockIdx.x (level lev + 1); accept: node blockIdx.x of level lev
+  const int ch0 = ACCEPT ? static_cast<int>(blockIdx.x) : static_cast<int>(blockIdx.x) * lv.fanout;
+  const int ch1 = ACCEPT ? ch0 + 1 : min(n_lev, ch0 + lv.fanout);
+  const int nc = ch1 - ch0;
+  const uint32_t* mask = ACCEPT ? lv.acc[lev] : lv.open[lev + 1];
+  const int mwords = ACCEPT ? lv.words[lev] : lv.words[lev + 1];
+  const int mbit = static_cast<int>(blockIdx.x);
+  const float* cen = centres + static_cast<int64_t>(c) * kD;
+  const int64_t nodes0 = static_cast<int64_t>(c) * n_lev;
+  const uint16_t* Mb = ACCEPT ? lv.Jb[lev] : lv.Hb[lev];
+  if (tid == 0) {
+    mbar_init(&sh.bar[0], 1);
+    mbar_init(&sh.bar[1], 1);
+    sh.abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) tmem_alloc(&sh.tmem_base, 256);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh.tmem_base;
+  const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+  const uint32_t idesc = idesc_bf16(128, 128, false, false);
+  const uint32_t a0 = smem_u32(sh.a);
+  auto stage_b = [&](int node, int buf) {         // node's M hi + lo rows -> b[buf] (one cp.async group)
+    const uint16_t* src = Mb + (nodes0 + node) * 2 * kD * kD;
+    const uint32_t dst = smem_u32(sh.b[buf]);
+    for (int x = tid; x < 2 * kD * 16; x += 128) {
+      const int part = x >> 11, r = (x >> 4) & 127, cc = x & 15;
+      cp_async16(dst + part * (2 * kTcQ * 128) + (cc >> 3) * (kTcQ * 128) + sw128_off(r, cc & 7),
+                 src + part * kD * kD + r * kD + cc * 8, 16u);
+    }
+    cp_async_commit();
+  };
+  auto issue = [&](int buf, uint32_t ycol) {      // Y[ycol] = Dh Mh + Dh Ml + Dl Mh (thread 0)
+    tc_fence_after();
+    const uint32_t b0 = smem_u32(sh.b[buf]);
+#pragma unroll
+    for (int pr = 0; pr < 3; ++pr) {
+      const int ap = pr == 2 ? 1 : 0, bp = pr == 1 ? 1 : 0;
+#pragma unroll
+      for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          mma_bf16(tmem + ycol, sw128_desc(a0 + (ap * 2 + kb) * (kTcQ * 128) + ks * 32, 16, 1024),
+                   sw128_desc(b0 + (bp * 2 + kb) * (kTcQ * 128) + ks * 32, 16, 1024), idesc, (pr | kb | ks) != 0);
+    }
+  };
+  uint32_t uses[2] = {0u, 0u};                     // completed phases per barrier
+  bool ok = true;
+  if (ACCEPT) {                                    // the one node's J, for every chunk
+    stage_b(ch0, 0);
+    cp_async_wait<0>();
+  }
+  for (int64_t win = lo; win < hi && ok; win += kWindow) {
+    const int cnt = gather_window128(perm, win, min(hi, win + kWindow), mask, mwords, mbit, sh.list, sh.wsum);
+    for (int b0i = 0; b0i < cnt && ok; b0i += kTcQ) {
+      const int nq = min(kTcQ, cnt - b0i);
+      const int* lst = sh.list + b0i;
+      const bool live = tid < nq;
+      const int64_t qq = live ? lst[tid] : 0;
+      if (!ACCEPT) stage_b(ch0, 0);
+      // D = scale q - c of this thread's row, kept in registers (the walk's epilogue reads it), split into
+      // the A operand's bf16 hi and lo parts
+      float d[kD];
+      if (live) {
+        load_row128<T>(q, qq, scale, cen, d);
+      } else {
+#pragma unroll
+        for (int j = 0; j < kD; ++j) d[j] = 0.f;
+      }
+#pragma unroll
+      for (int cc = 0; cc < 16; ++cc) {
+        uint4 h, l;
+        split_bf16x8(d + 8 * cc, &h, &l);
+        const uint32_t off = (cc >> 3) * (kTcQ * 128) + sw128_off(tid, cc & 7);
+        st_shared_v4(a0 + off, h);
+        st_shared_v4(a0 + 2 * (kTcQ * 128) + off, l);
+      }
+      const float nrm = (!ACCEPT && live) ? norm[qq] : 0.f;
+      if (ACCEPT && live) {
+        int64_t r = record_of_internal(lv, base, qq, lev, ch0);
+        if (r < 0 || r >= nrec) {
+          flag_status(status, ST_BAD_INDEX);
+          r = -1;
+        }
+        sh.rec[tid] = r;
+      }
+      if (!ACCEPT) cp_async_wait<0>();
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncthreads();
+      if (tid == 0) {
+        issue(0, 0);
+        mma_commit(&sh.bar[0]);
+      }
+      if (!ACCEPT && nc > 1) stage_b(ch0 + 1, 1);
+      for (int i = 0; i < nc; ++i) {
+        const int yb = i & 1;
+        if (!ACCEPT && i + 1 < nc) {               // next child's MMAs, into the other Y buffer
+          cp_async_wait<0>();
+          fence_proxy_async_smem();
+          tc_fence_before();
+          __syncthreads();
+          if (tid == 0) {
+            issue(yb ^ 1, 128u * (yb ^ 1));
+            mma_commit(&sh.bar[yb ^ 1]);
+          }
+        }
+        ok = mbar_wait(&sh.bar[yb], uses[yb] & 1u, status, &sh.abort_flag);
+        ++uses[yb];
+        if (!__syncthreads_and(ok)) {
+          ok = false;
+          break;
+        }
+        if (!ACCEPT && i + 2 < nc) stage_b(ch0 + i + 2, yb);   // this buffer's MMAs have completed
+        tc_fence_after();
+        const int n = ch0 + i;
+        const int64_t node = nodes0 + n;
+        if (ACCEPT) {
+          const float* un = lv.u[lev] + node * kD;
+          const int64_t r = live ? sh.rec[tid] : -1;
+#pragma unroll 1
+          for (int cb = 0; cb < 4; ++cb) {
+            uint32_t y[32];
+            tmem_ld32(tmem + lane_off + 128u * yb + 32 * cb, y);
+            tmem_ld_wait();
+            if (r >= 0) {
+              float4* dst = reinterpret_cast<float4*>(rec_val + r * kD + 32 * cb);
+              const float4* u4 = reinterpret_cast<const float4*>(un + 32 * cb);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const float4 uu = __ldg(u4 + j);
+                dst[j] = make_float4(uu.x + __uint_as_float(y[4 * j]), uu.y + __uint_as_float(y[4 * j + 1]),
+                                     uu.z + __uint_as_float(y[4 * j + 2]), uu.w + __uint_as_float(y[4 * j + 3]));
+              }
+            }
+          }
+          if (r >= 0) {
+            rec_lm[r] = lv.lm[lev][qq * n_lev + n];
+            rec_ex[r] = 0;
+          }
+        } else {
+          const float* gn = lv.g[lev] + node * kD;
+          float qd = 0.f, rg = 0.f;
+#pragma unroll
+          for (int cb = 0; cb < 4; ++cb) {
+            uint32_t y[32];
+            tmem_ld32(tmem + lane_off + 128u * yb + 32 * cb, y);
+            tmem_ld_wait();
+            float q0 = 0.f, q1 = 0.f, g0 = 0.f, g1 = 0.f;
+#pragma unroll
+            for (int j = 0; j < 32; j += 2) {
+              const float2 gg = __ldg(reinterpret_cast<const float2*>(gn + 32 * cb + j));
+              q0 = fmaf(d[32 * cb + j], __uint_as_float(y[j]), q0);
+              q1 = fmaf(d[32 * cb + j + 1], __uint_as_float(y[j + 1]), q1);
+              g0 = fmaf(d[32 * cb + j], gg.x, g0);
+              g1 = fmaf(d[32 * cb + j + 1], gg.y, g1);
+            }
+            qd += q0 + q1;
+            rg += g0 + g1;
+          }
+          if (live) {
+            const float lm = lv.L[lev][node] + rg + 0.5f * qd;
+            lv.lm[lev][qq * n_lev + n] = lm;
+            uint32_t* dstm = score_of(lm, qd, nrm) > thr ? lv.open[lev] : lv.acc[lev];
+            atomicOr(dstm + qq * lv.words[lev] + (n >> 5), 1u << (n & 31));
+          }
+        }
+        tc_fence_before();
+      }
+      if (!ok) break;
+      __syncthreads();
+    }
+  }
+  cp_async_wait<0>();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 256);
+}
+
+// ---------------------------------------------------------------------------------------------------
 // centres for the operator from the k-means of the accurate mode: scaled centres and int32 assignment
 __global__ void tree_centres_kernel(const float* __restrict__ km_centres, const uint8_t* __restrict__ km_assign,
                                     int64_t n, float scale, float* __restrict__ centres, int32_t* __restrict__ assign) {
@@ -1411,7 +1682,7 @@ int shape_of(const HtrcTreeDims* d, Shape* s) {
 
 struct ForestLayout {
   size_t a = 0, L[kMaxLevels] = {}, g[kMaxLevels] = {}, u[kMaxLevels] = {}, H[kMaxLevels] = {},
-         JT[kMaxLevels] = {}, total = 0;
+         JT[kMaxLevels] = {}, Hb[kMaxLevels] = {}, Jb[kMaxLevels] = {}, total = 0;
 };
 ForestLayout forest_layout(const HtrcTreeDims* d, const Shape& s) {
   ForestLayout f;
@@ -1433,6 +1704,10 @@ ForestLayout forest_layout(const HtrcTreeDims* d, const Shape& s) {
     o += a256(nn * kD * kD * 4);
     f.JT[l] = o;
     o += a256(nn * kD * kD * 4);
+    f.Hb[l] = o;                              // [C][n][hi, lo][128][128] bf16: H rows
+    o += a256(nn * 2 * kD * kD * 2);
+    f.Jb[l] = o;                              // [C][n][hi, lo][128][128] bf16: J rows (value dim major)
+    o += a256(nn * 2 * kD * kD * 2);
   }
   f.total = o;
   return f;
@@ -1503,6 +1778,8 @@ TreeLevels levels_of(const HtrcTreeDims* d, const Shape& s, const void* forest, 
       lv.u[l] = reinterpret_cast<const float*>(fb + f.u[l]);
       lv.H[l] = reinterpret_cast<const float*>(fb + f.H[l]);
       lv.JT[l] = reinterpret_cast<const float*>(fb + f.JT[l]);
+      lv.Hb[l] = reinterpret_cast<const uint16_t*>(fb + f.Hb[l]);
+      lv.Jb[l] = reinterpret_cast<const uint16_t*>(fb + f.Jb[l]);
       if (wb) {
         lv.lm[l] = reinterpret_cast<float*>(wb + w.lm[l]);
         lv.open[l] = reinterpret_cast<uint32_t*>(wb + w.open[l]);
@@ -1539,6 +1816,13 @@ bool tc_leaves_enabled() {
   return !(e && e[0] == '1');
 }
 
+// the internal nodes below the roots run on the tensor cores unless HTRC_TREE_SIMT_NODES=1 selects the
+// float32 CUDA-core kernels (tree_walk_kernel / tree_accept_kernel)
+bool tc_nodes_enabled() {
+  const char* e = getenv("HTRC_TREE_SIMT_NODES");
+  return !(e && e[0] == '1');
+}
+
 // largest per-centre query count (reads the grouped offsets back: one stream synchronisation)
 int max_count(const int64_t* coff_dev, int ncen, cudaStream_t st, int64_t* mx) {
   int64_t host[HTRC_TREE_MAX_CENTRES + 1];
@@ -1571,7 +1855,8 @@ int build_impl(const HtrcTreeDims* d, const Shape& s, const T* k, const T* v, co
       k, v, d->n_keys, d->leaf_size, d->fanout, s.n[0], a, reinterpret_cast<const float*>(fb + f.L[0]), s.n[1],
       reinterpret_cast<float*>(fb + f.L[1]), reinterpret_cast<float*>(fb + f.g[1]),
       reinterpret_cast<float*>(fb + f.u[1]), reinterpret_cast<float*>(fb + f.H[1]),
-      reinterpret_cast<float*>(fb + f.JT[1]));
+      reinterpret_cast<float*>(fb + f.JT[1]), reinterpret_cast<uint16_t*>(fb + f.Hb[1]),
+      reinterpret_cast<uint16_t*>(fb + f.Jb[1]));
   if ((rc = launched()) != HTRC_OK) return rc;
   if ((rc = set_smem(tree_merge_kernel, sizeof(MergeSmem))) != HTRC_OK) return rc;
   for (int l = 2; l < s.levels; ++l) {
@@ -1581,7 +1866,8 @@ int build_impl(const HtrcTreeDims* d, const Shape& s, const T* k, const T* v, co
         reinterpret_cast<const float*>(fb + f.H[l - 1]), reinterpret_cast<const float*>(fb + f.JT[l - 1]), s.n[l],
         reinterpret_cast<float*>(fb + f.L[l]), reinterpret_cast<float*>(fb + f.g[l]),
         reinterpret_cast<float*>(fb + f.u[l]), reinterpret_cast<float*>(fb + f.H[l]),
-        reinterpret_cast<float*>(fb + f.JT[l]));
+        reinterpret_cast<float*>(fb + f.JT[l]), reinterpret_cast<uint16_t*>(fb + f.Hb[l]),
+        reinterpret_cast<uint16_t*>(fb + f.Jb[l]));
     if ((rc = launched()) != HTRC_OK) return rc;
   }
   return HTRC_OK;
@@ -1621,9 +1907,16 @@ int walk_impl(const HtrcTreeDims* d, const Shape& s, const T* q, const int32_t* 
     tree_walk_kernel<T><<<dim3(1, C, slices(mx, kRootSlice)), 256, sizeof(WalkSmem), st>>>(
         q, d->scale, centres, perm, coff, kRootSlice, lv, top, 1, d->threshold, norm);
     if ((rc = launched()) != HTRC_OK) return rc;
+    const bool tc = tc_nodes_enabled();
+    if (tc && top >= 2 && (rc = set_smem(tree_node_tc_kernel<T, false>, kNodeSmemBytes)) != HTRC_OK) return rc;
     for (int l = top - 1; l >= 1; --l) {
-      tree_walk_kernel<T><<<dim3(s.n[l + 1], C, slices(mx, kSlice)), 256, sizeof(WalkSmem), st>>>(
-          q, d->scale, centres, perm, coff, kSlice, lv, l, 0, d->threshold, norm);
+      if (tc)
+        tree_node_tc_kernel<T, false><<<dim3(s.n[l + 1], C, slices(mx, kSlice)), 128, kNodeSmemBytes, st>>>(
+            q, d->scale, centres, perm, coff, kSlice, lv, l, d->threshold, norm, nullptr, 0, nullptr, nullptr,
+            nullptr, status);
+      else
+        tree_walk_kernel<T><<<dim3(s.n[l + 1], C, slices(mx, kSlice)), 256, sizeof(WalkSmem), st>>>(
+            q, d->scale, centres, perm, coff, kSlice, lv, l, 0, d->threshold, norm);
       if ((rc = launched()) != HTRC_OK) return rc;
     }
   }
@@ -1669,10 +1962,17 @@ int values_impl(const HtrcTreeDims* d, const Shape& s, const T* k, const T* v, c
   const TreeLevels lv = levels_of(d, s, forest, walk);
   const int top = s.levels - 1;
   if (top >= 1 && (stages & HTRC_TREE_STAGE_ACCEPT)) {
+    const bool tc = tc_nodes_enabled();
     if ((rc = set_smem(tree_accept_kernel<T>, sizeof(AcceptSmem))) != HTRC_OK) return rc;
+    if (tc && (rc = set_smem(tree_node_tc_kernel<T, true>, kNodeSmemBytes)) != HTRC_OK) return rc;
     for (int l = top; l >= 1; --l) {
-      tree_accept_kernel<T><<<dim3(s.n[l], C, slices(mx, kSlice)), 256, sizeof(AcceptSmem), st>>>(
-          q, d->scale, centres, perm, coff, kSlice, lv, l, base, n_records, rec_val, rec_lm, rec_ex, status);
+      if (tc)
+        tree_node_tc_kernel<T, true><<<dim3(s.n[l], C, slices(mx, kSlice)), 128, kNodeSmemBytes, st>>>(
+            q, d->scale, centres, perm, coff, kSlice, lv, l, d->threshold, norm, base, n_records, rec_val, rec_lm,
+            rec_ex, status);
+      else
+        tree_accept_kernel<T><<<dim3(s.n[l], C, slices(mx, kSlice)), 256, sizeof(AcceptSmem), st>>>(
+            q, d->scale, centres, perm, coff, kSlice, lv, l, base, n_records, rec_val, rec_lm, rec_ex, status);
       if ((rc = launched()) != HTRC_OK) return rc;
     }
   }

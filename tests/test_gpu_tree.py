@@ -191,3 +191,27 @@ def test_operator_on_the_video_generator():
         rcnt = np.stack([ref_info[x] for x in ("visited_nodes", "accepted_nodes", "exact_leaves")], 1)
         # RMS-3 inputs: logits up to ~100, whose float32 rounding (~1e-5 relative) moves outputs by a few 1e-4
         _check(_np(out)[rows], cnt, ref, rcnt, _np(lse)[rows], ref_lse, agree=0.95, same_tol=1e-3)
+
+
+def test_tensor_core_nodes_match_cuda_core_nodes():
+    """The internal nodes below the roots on tcgen05 (D and M as bf16 hi + lo parts, three MMA chains) against the
+    float32 CUDA-core kernels (HTRC_TREE_SIMT_NODES=1) on the three-level fixtures."""
+    import os
+    from htrc_b200 import tree
+    for name in ("cluster", "ragged"):
+        fx = np.load(HERE / "golden" / f"tree_{name}.npz")
+        q, k, v = G.inputs(name)
+        qs = torch.from_numpy(q).float() * float(fx["scale"])
+        forest = tree.build_forest(k, v, fx["centres"], leaf_size=int(fx["leaf"]), fanout=int(fx["fanout"]))
+        assert forest.levels == 3
+        args = (k, v, qs, fx["centres"], forest)
+        kw = dict(opening_threshold=float(fx["thr"]), assign=fx["assign"], return_lse=True)
+        ot, it, lt = tree.evaluate(*args, **kw)
+        os.environ["HTRC_TREE_SIMT_NODES"] = "1"
+        try:
+            os_, is_, ls_ = tree.evaluate(*args, **kw)
+        finally:
+            del os.environ["HTRC_TREE_SIMT_NODES"]
+        cnt = np.stack([_np(it[x]) for x in ("visited_nodes", "accepted_nodes", "exact_leaves")], 1)
+        ref = np.stack([_np(is_[x]) for x in ("visited_nodes", "accepted_nodes", "exact_leaves")], 1)
+        _check(ot, cnt, _np(os_), ref, lt, _np(ls_), same_tol=2e-4)
