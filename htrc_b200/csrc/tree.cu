@@ -1085,9 +1085,10 @@ struct __align__(1024) TcSmem {
   uint8_t ks[2][2 * 64 * 128];       // keys, two leaves in flight: two K-blocks of [64 rows][128 B] (K-major B)
   uint8_t vs[2][2 * 64 * 128];       // values, two leaves: two N-chunks of [64 key rows][128 B]   (MN-major B)
   float as[2][64], ws[2][64];
+  float xch[4][2][kTcQ];              // per-row partial sums of the two halves (xbar, quad, max, sum)
   int64_t rec[kTcQ];
   int list[kWindow];
-  int wsum[4];
+  int wsum[8];
   uint64_t bar_s, bar_pv;
   uint32_t tmem_base;
   int abort_flag;
@@ -1136,7 +1137,7 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
                : "memory");
 }
 
-__global__ void __launch_bounds__(128, 1) tree_leafblock_tc_kernel(
+__global__ void __launch_bounds__(256, 2) tree_leafblock_tc_kernel(
     const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, const uint16_t* __restrict__ v, int64_t m,
     float scale, const float* __restrict__ a, const int32_t* __restrict__ perm, const int64_t* __restrict__ coff,
     int64_t slice, TreeLevels lv, float thr, const float* __restrict__ norm, const int64_t* __restrict__ base,
@@ -1145,6 +1146,9 @@ __global__ void __launch_bounds__(128, 1) tree_leafblock_tc_kernel(
   extern __shared__ unsigned char smem_raw[];
   TcSmem& sh = *reinterpret_cast<TcSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int c = blockIdx.y, p = blockIdx.x, tid = threadIdx.x, warp = tid >> 5;
+  // two threads per query row: row = TMEM lane (tid & 127), half hf = keys 32 hf .. + 31 and O columns
+  // 64 hf .. + 63; the warps (w, w + 4) hold the same rows and exchange partial sums through shared memory
+  const int row = tid & 127, hf = tid >> 7, pair_bar = 1 + ((tid & 127) >> 5);
   const int64_t lo = coff[c] + static_cast<int64_t>(blockIdx.z) * slice;
   const int64_t hi = min(coff[c + 1], lo + slice);
   if (lo >= hi) return;
@@ -1163,7 +1167,7 @@ __global__ void __launch_bounds__(128, 1) tree_leafblock_tc_kernel(
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sh.tmem_base;
-  const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+  const uint32_t lane_off = static_cast<uint32_t>(row & ~31) << 16;
   const uint32_t id_s = idesc_bf16(128, 64, false, false);
   const uint32_t id_pv = idesc_bf16(128, 128, false, true);
   const uint32_t qa = smem_u32(sh.qs);
@@ -1172,31 +1176,31 @@ __global__ void __launch_bounds__(128, 1) tree_leafblock_tc_kernel(
     const int64_t s0 = static_cast<int64_t>(l) * leaf;
     const int kc = static_cast<int>(m - s0 < leaf ? m - s0 : leaf);
     const uint32_t kb = smem_u32(sh.ks[b]), vb = smem_u32(sh.vs[b]);
-    for (int x = tid; x < 64 * 16; x += 128) {
+    for (int x = tid; x < 64 * 16; x += 256) {
       const int r = x >> 4, cc = x & 15;
       const uint32_t nb = r < kc ? 16u : 0u;
-      const int64_t row = s0 + (r < kc ? r : 0);
+      const int64_t kr = s0 + (r < kc ? r : 0);
       const uint32_t off = (cc >> 3) * (64 * 128) + sw128_off(r, cc & 7);
-      cp_async16(kb + off, k + row * kD + cc * 8, nb);
-      cp_async16(vb + off, v + row * kD + cc * 8, nb);
+      cp_async16(kb + off, k + kr * kD + cc * 8, nb);
+      cp_async16(vb + off, v + kr * kD + cc * 8, nb);
     }
     cp_async_commit();
   };
   uint32_t ph_s = 0, ph_pv = 0;
   bool ok = true;
   for (int64_t win = lo; win < hi && ok; win += kWindow) {
-    const int cnt = gather_window128(perm, win, min(hi, win + kWindow), lv.open[1], lv.words[1], p, sh.list, sh.wsum);
+    const int cnt = gather_window(perm, win, min(hi, win + kWindow), lv.open[1], lv.words[1], p, sh.list, sh.wsum);
     for (int b0 = 0; b0 < cnt && ok; b0 += kTcQ) {
       const int nq = min(kTcQ, cnt - b0);
       const int* lst = sh.list + b0;
-      for (int x = tid; x < kTcQ * 16; x += 128) {
+      for (int x = tid; x < kTcQ * 16; x += 256) {
         const int r = x >> 4, cc = x & 15;
         uint4 val = make_uint4(0u, 0u, 0u, 0u);
         if (r < nq) val = __ldg(reinterpret_cast<const uint4*>(q + static_cast<int64_t>(lst[r]) * kD) + cc);
         st_shared_v4(qa + (cc >> 3) * (kTcQ * 128) + sw128_off(r, cc & 7), val);
       }
-      const bool live = tid < nq;
-      const float nrm = live ? norm[lst[tid]] : 0.f;
+      const bool live = row < nq;
+      const float nrm = live ? norm[lst[row]] : 0.f;
       float m_run = -INFINITY, s_run = 0.f;
       int nex = 0;
       stage_kv(l0, 0);
@@ -1218,8 +1222,9 @@ __global__ void __launch_bounds__(128, 1) tree_leafblock_tc_kernel(
           sh.ws[b][tid] = tid < kc ? expf(av - ll) : 0.f;
         }
         const uint32_t ka = smem_u32(sh.ks[b]), va = smem_u32(sh.vs[b]);
-        const float* as_ = sh.as[b];
-        const float* ws_ = sh.ws[b];
+        const float* as_ = sh.as[b] + 32 * hf;            // this half's keys
+        const float* ws_ = sh.ws[b] + 32 * hf;
+        const int kh = min(32, max(0, kc - 32 * hf));     // this half's valid keys
         fence_proxy_async_smem();
         __syncthreads();
         if (tid == 0) {
@@ -1239,39 +1244,36 @@ __global__ void __launch_bounds__(128, 1) tree_leafblock_tc_kernel(
           break;
         }
         tc_fence_after();
-        float S[64];
+        float S[32];
         {
-          uint32_t r0[32], r1[32];
-          tmem_ld32(tmem + lane_off, r0);
-          tmem_ld32(tmem + lane_off + 32, r1);
+          uint32_t r0[32];
+          tmem_ld32(tmem + lane_off + 32 * hf, r0);
           tmem_ld_wait();
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            S[j] = scale * __uint_as_float(r0[j]);
-            S[32 + j] = scale * __uint_as_float(r1[j]);
-          }
+          for (int j = 0; j < 32; ++j) S[j] = scale * __uint_as_float(r0[j]);
         }
-        // four independent partial sums per reduction (the chains are the row math's latency)
         const float4* w4p = reinterpret_cast<const float4*>(ws_);
         const float4* a4p = reinterpret_cast<const float4*>(as_);
-        float xb;
+        // prediction (model.py:91-96 from the keys): xbar = sum w x, quad = sum w (x - xbar)^2, x = S - a;
+        // each half sums its 32 keys, the pair adds the two halves in a fixed order
         {
           float p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
 #pragma unroll
-          for (int j = 0; j < 64; j += 4) {
+          for (int j = 0; j < 32; j += 4) {
             const float4 w4 = w4p[j >> 2], a4 = a4p[j >> 2];
             p0 = fmaf(w4.x, S[j] - a4.x, p0);
             p1 = fmaf(w4.y, S[j + 1] - a4.y, p1);
             p2 = fmaf(w4.z, S[j + 2] - a4.z, p2);
             p3 = fmaf(w4.w, S[j + 3] - a4.w, p3);
           }
-          xb = (p0 + p1) + (p2 + p3);
+          sh.xch[0][hf][row] = (p0 + p1) + (p2 + p3);
         }
-        float qd;
+        named_bar_sync(pair_bar, 64);
+        const float xb = sh.xch[0][0][row] + sh.xch[0][1][row];
         {
           float p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
 #pragma unroll
-          for (int j = 0; j < 64; j += 4) {
+          for (int j = 0; j < 32; j += 4) {
             const float4 w4 = w4p[j >> 2], a4 = a4p[j >> 2];
             const float e0 = S[j] - a4.x - xb, e1 = S[j + 1] - a4.y - xb;
             const float e2 = S[j + 2] - a4.z - xb, e3 = S[j + 3] - a4.w - xb;
@@ -1280,33 +1282,46 @@ __global__ void __launch_bounds__(128, 1) tree_leafblock_tc_kernel(
             p2 = fmaf(w4.z * e2, e2, p2);
             p3 = fmaf(w4.w * e3, e3, p3);
           }
-          qd = (p0 + p1) + (p2 + p3);
+          sh.xch[1][hf][row] = (p0 + p1) + (p2 + p3);
         }
+        named_bar_sync(pair_bar, 64);
+        const float qd = sh.xch[1][0][row] + sh.xch[1][1][row];
         const float lmv = ll + xb + 0.5f * qd;
         const bool open = live && score_of(lmv, qd, nrm) > thr;
-        float mass = lmv;
-        if (open) {
-          float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
+        // an opened leaf's log-mass: logsumexp of its scores (both halves, fixed order)
+        {
+          float m0 = -INFINITY, m1 = -INFINITY;
+          if (open) {
 #pragma unroll
-          for (int j = 0; j < 64; j += 4) {
-            if (j < kc) m0 = fmaxf(m0, S[j]);
-            if (j + 1 < kc) m1 = fmaxf(m1, S[j + 1]);
-            if (j + 2 < kc) m2 = fmaxf(m2, S[j + 2]);
-            if (j + 3 < kc) m3 = fmaxf(m3, S[j + 3]);
+            for (int j = 0; j < 32; j += 2) {
+              if (j < kh) m0 = fmaxf(m0, S[j]);
+              if (j + 1 < kh) m1 = fmaxf(m1, S[j + 1]);
+            }
           }
-          const float mx = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
-          float e0 = 0.f, e1 = 0.f, e2 = 0.f, e3 = 0.f;
-#pragma unroll
-          for (int j = 0; j < 64; j += 4) {
-            if (j < kc) e0 += __expf(S[j] - mx);
-            if (j + 1 < kc) e1 += __expf(S[j + 1] - mx);
-            if (j + 2 < kc) e2 += __expf(S[j + 2] - mx);
-            if (j + 3 < kc) e3 += __expf(S[j + 3] - mx);
-          }
-          mass = mx + logf((e0 + e1) + (e2 + e3));
+          sh.xch[2][hf][row] = fmaxf(m0, m1);
         }
-        const float mn = live ? fmaxf(m_run, mass) : 0.f;
-        const float al = live ? expf(m_run - mn) : 1.f;
+        named_bar_sync(pair_bar, 64);
+        const float mx = fmaxf(sh.xch[2][0][row], sh.xch[2][1][row]);
+        {
+          float e0 = 0.f, e1 = 0.f, e2 = 0.f, e3 = 0.f;
+          if (open) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              if (j < kh) e0 += __expf(S[j] - mx);
+              if (j + 1 < kh) e1 += __expf(S[j + 1] - mx);
+              if (j + 2 < kh) e2 += __expf(S[j + 2] - mx);
+              if (j + 3 < kh) e3 += __expf(S[j + 3] - mx);
+            }
+          }
+          sh.xch[3][hf][row] = (e0 + e1) + (e2 + e3);
+        }
+        named_bar_sync(pair_bar, 64);
+        const float mass = open ? mx + logf(sh.xch[3][0][row] + sh.xch[3][1][row]) : lmv;
+        // lazy reference: the running maximum moves only when a leaf's mass exceeds it by more than 8 (so the
+        // coefficients stay below e^8 and O is rescaled rarely); out and log-Z are relative to the same reference
+        const bool bump = live && mass > m_run + 8.f;
+        const float mn = live ? (bump ? mass : m_run) : 0.f;
+        const float al = bump ? expf(m_run - mn) : 1.f;
         if (live) {
           s_run = s_run * al + expf(mass - mn);
           m_run = mn;
@@ -1314,39 +1329,38 @@ __global__ void __launch_bounds__(128, 1) tree_leafblock_tc_kernel(
         nex += open;
         const float fw = expf(lmv - mn);
         const float c0 = fw * (1.f - xb);          // far coefficient: w (fw (1 + x - xbar)) = w (fw x + c0)
-        // rescale O (its previous PV has completed).  tcgen05.ld / st are warp-collective (.sync.aligned):
-        // the warp takes the branch as a whole, rows whose maximum did not move scale by 1
+        // rescale this half of O (its previous PV has completed).  tcgen05.ld / st are warp-collective
+        // (.sync.aligned): the warp takes the branch as a whole, rows whose reference did not move scale by 1
         if (__any_sync(0xffffffffu, l > l0 && al != 1.f)) {
 #pragma unroll 1
-          for (int cb = 0; cb < 4; ++cb) {
+          for (int cb = 0; cb < 2; ++cb) {
             uint32_t o[32];
-            tmem_ld32(tmem + lane_off + 128 + 32 * cb, o);
+            const uint32_t col = 128 + 64 * hf + 32 * cb;
+            tmem_ld32(tmem + lane_off + col, o);
             tmem_ld_wait();
 #pragma unroll
             for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * al);
-            tmem_st32(tmem + lane_off + 128 + 32 * cb, o);
+            tmem_st32(tmem + lane_off + col, o);
           }
         }
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {            // P as bf16 hi and lo parts, 32 keys at a time
+        {                                          // P as bf16 hi and lo parts for this half's 32 keys
           uint32_t ph[16], pl[16];
 #pragma unroll
           for (int j = 0; j < 32; j += 2) {
             float pc[2];
 #pragma unroll
             for (int t = 0; t < 2; ++t) {
-              const int jj = 32 * h + j + t;
+              const int jj = j + t;
               pc[t] = 0.f;
-              if (live && jj < kc)
-                pc[t] = open ? __expf(S[jj] - mn) : ws_[jj] * fmaf(fw, S[jj] - as_[jj], c0);
+              if (live && jj < kh) pc[t] = open ? __expf(S[jj] - mn) : ws_[jj] * fmaf(fw, S[jj] - as_[jj], c0);
             }
             const __nv_bfloat162 hb = __floats2bfloat162_rn(pc[0], pc[1]);
-            const float2 hf = __bfloat1622float2(hb);
+            const float2 hf2 = __bfloat1622float2(hb);
             ph[j >> 1] = *reinterpret_cast<const uint32_t*>(&hb);
-            pl[j >> 1] = pack_bf16x2(pc[0] - hf.x, pc[1] - hf.y);
+            pl[j >> 1] = pack_bf16x2(pc[0] - hf2.x, pc[1] - hf2.y);
           }
-          tmem_st16(tmem + lane_off + 64 + 16 * h, ph);
-          tmem_st16(tmem + lane_off + 96 + 16 * h, pl);
+          tmem_st16(tmem + lane_off + 64 + 16 * hf, ph);
+          tmem_st16(tmem + lane_off + 96 + 16 * hf, pl);
         }
         tmem_st_wait();
         tc_fence_before();
@@ -1370,26 +1384,31 @@ __global__ void __launch_bounds__(128, 1) tree_leafblock_tc_kernel(
         tc_fence_after();
       }
       if (!ok) break;
-      int64_t r = -1;
-      if (live) {
-        const int64_t qq = lst[tid];
-        r = record_of_block(lv, base, qq, p);
-        if (r < 0 || r >= nrec) {
-          flag_status(status, ST_BAD_INDEX);
-          r = -1;
-        } else {
-          rec_lm[r] = m_run + logf(s_run);
-          rec_ex[r] = nex;
+      if (hf == 0) {
+        int64_t r = -1;
+        if (live) {
+          const int64_t qq = lst[row];
+          r = record_of_block(lv, base, qq, p);
+          if (r < 0 || r >= nrec) {
+            flag_status(status, ST_BAD_INDEX);
+            r = -1;
+          } else {
+            rec_lm[r] = m_run + logf(s_run);
+            rec_ex[r] = nex;
+          }
         }
+        sh.rec[row] = r;
       }
+      __syncthreads();
+      const int64_t r = sh.rec[row];
       const float inv = 1.f / s_run;
 #pragma unroll
-      for (int cb = 0; cb < 4; ++cb) {
+      for (int cb = 0; cb < 2; ++cb) {
         uint32_t o[32];
-        tmem_ld32(tmem + lane_off + 128 + 32 * cb, o);
+        tmem_ld32(tmem + lane_off + 128 + 64 * hf + 32 * cb, o);
         tmem_ld_wait();
-        if (r >= 0) {
-          float4* dst = reinterpret_cast<float4*>(rec_val + r * kD + 32 * cb);
+        if (live && r >= 0) {
+          float4* dst = reinterpret_cast<float4*>(rec_val + r * kD + 64 * hf + 32 * cb);
 #pragma unroll
           for (int j = 0; j < 8; ++j)
             dst[j] = make_float4(__uint_as_float(o[4 * j]) * inv, __uint_as_float(o[4 * j + 1]) * inv,
@@ -1979,7 +1998,7 @@ int values_impl(const HtrcTreeDims* d, const Shape& s, const T* k, const T* v, c
   if (!(stages & HTRC_TREE_STAGE_LEAVES)) {
   } else if (std::is_same<T, uint16_t>::value && top >= 1 && tc_leaves) {
     if ((rc = set_smem(tree_leafblock_tc_kernel, kTcSmemBytes)) != HTRC_OK) return rc;
-    tree_leafblock_tc_kernel<<<dim3(s.n[1], C, slices(mx, kSlice)), 128, kTcSmemBytes, st>>>(
+    tree_leafblock_tc_kernel<<<dim3(s.n[1], C, slices(mx, kSlice)), 256, kTcSmemBytes, st>>>(
         reinterpret_cast<const uint16_t*>(q), reinterpret_cast<const uint16_t*>(k),
         reinterpret_cast<const uint16_t*>(v), d->n_keys, d->scale, a, perm, coff, kSlice, lv, d->threshold, norm,
         base, n_records, rec_val, rec_lm, rec_ex, status);
