@@ -168,7 +168,8 @@ __global__ void __launch_bounds__(256) tree_perm_kernel(const int32_t* __restric
 template <typename T>
 __global__ void __launch_bounds__(64) tree_leaf_kernel(const T* __restrict__ k, int64_t m, int leaf,
                                                        const float* __restrict__ centres, int nl,
-                                                       float* __restrict__ a_out, float* __restrict__ leaf_l) {
+                                                       float* __restrict__ a_out, float* __restrict__ leaf_l,
+                                                       float* __restrict__ w_out) {
   __shared__ __align__(16) float ks[64][132];
   __shared__ __align__(16) float cs[kD];
   __shared__ float red[64];
@@ -208,7 +209,10 @@ __global__ void __launch_bounds__(64) tree_leaf_kernel(const T* __restrict__ k, 
     if (tid < o) red[tid] += red[tid + o];
     __syncthreads();
   }
-  if (tid == 0) leaf_l[static_cast<int64_t>(c) * nl + l] = mx + logf(red[0]);
+  __syncthreads();
+  const float ll = mx + logf(red[0]);
+  if (tid == 0) leaf_l[static_cast<int64_t>(c) * nl + l] = ll;
+  if (tid < cnt) w_out[static_cast<int64_t>(c) * m + s0 + tid] = expf(a - ll);
 }
 
 // 8 floats -> their bf16 parts: hi = bf16(x), lo = bf16(x - hi) (16 bytes each)
@@ -1124,6 +1128,10 @@ __device__ int gather_window128(const int32_t* __restrict__ perm, int64_t lo, in
   return total;
 }
 
+// 4-byte asynchronous global -> shared copy; src_bytes 0 writes zeros (the source is not read)
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
 // 16-byte asynchronous global -> shared copy; src_bytes 0 writes zeros (the source is not read)
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
@@ -1139,7 +1147,8 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
 
 __global__ void __launch_bounds__(256, 2) tree_leafblock_tc_kernel(
     const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, const uint16_t* __restrict__ v, int64_t m,
-    float scale, const float* __restrict__ a, const int32_t* __restrict__ perm, const int64_t* __restrict__ coff,
+    float scale, const float* __restrict__ a, const float* __restrict__ wk, const int32_t* __restrict__ perm,
+    const int64_t* __restrict__ coff,
     int64_t slice, TreeLevels lv, float thr, const float* __restrict__ norm, const int64_t* __restrict__ base,
     int64_t nrec, float* __restrict__ rec_val, float* __restrict__ rec_lm, int32_t* __restrict__ rec_ex,
     int* __restrict__ status) {
@@ -1155,6 +1164,7 @@ __global__ void __launch_bounds__(256, 2) tree_leafblock_tc_kernel(
   const int nl = lv.n[0], leaf = lv.leaf;
   const int l0 = p * lv.fanout, l1 = min(nl, l0 + lv.fanout);
   const float* ac = a + static_cast<int64_t>(c) * m;
+  const float* wc = wk + static_cast<int64_t>(c) * m;
   const float* lL = lv.L[0] + static_cast<int64_t>(c) * nl;
   if (tid == 0) {
     mbar_init(&sh.bar_s, 1);
@@ -1183,6 +1193,11 @@ __global__ void __launch_bounds__(256, 2) tree_leafblock_tc_kernel(
       const uint32_t off = (cc >> 3) * (64 * 128) + sw128_off(r, cc & 7);
       cp_async16(kb + off, k + kr * kD + cc * 8, nb);
       cp_async16(vb + off, v + kr * kD + cc * 8, nb);
+    }
+    if (tid < 128) {                          // the leaf's key logits a and weights w (zeros past its keys)
+      const int r = tid & 63;
+      const float* src = (tid < 64 ? ac : wc) + s0 + (r < kc ? r : 0);
+      cp_async4(smem_u32(tid < 64 ? &sh.as[b][r] : &sh.ws[b][r]), src, r < kc ? 4u : 0u);
     }
     cp_async_commit();
   };
@@ -1215,11 +1230,6 @@ __global__ void __launch_bounds__(256, 2) tree_leafblock_tc_kernel(
           cp_async_wait<1>();
         } else {
           cp_async_wait<0>();
-        }
-        if (tid < 64) {
-          const float av = tid < kc ? ac[s0 + tid] : 0.f;
-          sh.as[b][tid] = av;
-          sh.ws[b][tid] = tid < kc ? expf(av - ll) : 0.f;
         }
         const uint32_t ka = smem_u32(sh.ks[b]), va = smem_u32(sh.vs[b]);
         const float* as_ = sh.as[b] + 32 * hf;            // this half's keys
@@ -1700,7 +1710,7 @@ int shape_of(const HtrcTreeDims* d, Shape* s) {
 }
 
 struct ForestLayout {
-  size_t a = 0, L[kMaxLevels] = {}, g[kMaxLevels] = {}, u[kMaxLevels] = {}, H[kMaxLevels] = {},
+  size_t a = 0, w = 0, L[kMaxLevels] = {}, g[kMaxLevels] = {}, u[kMaxLevels] = {}, H[kMaxLevels] = {},
          JT[kMaxLevels] = {}, Hb[kMaxLevels] = {}, Jb[kMaxLevels] = {}, total = 0;
 };
 ForestLayout forest_layout(const HtrcTreeDims* d, const Shape& s) {
@@ -1708,6 +1718,8 @@ ForestLayout forest_layout(const HtrcTreeDims* d, const Shape& s) {
   const size_t C = d->n_centres;
   size_t o = 0;
   f.a = o;
+  o += a256(C * d->n_keys * 4);
+  f.w = o;                                    // w = e^(a - L) of every key within its leaf
   o += a256(C * d->n_keys * 4);
   f.L[0] = o;
   o += a256(C * s.n[0] * 4);
@@ -1866,7 +1878,8 @@ int build_impl(const HtrcTreeDims* d, const Shape& s, const T* k, const T* v, co
   float* a = reinterpret_cast<float*>(fb + f.a);
   const int C = d->n_centres;
   tree_leaf_kernel<T><<<dim3(s.n[0], C), 64, 0, st>>>(k, d->n_keys, d->leaf_size, centres, s.n[0], a,
-                                                       reinterpret_cast<float*>(fb + f.L[0]));
+                                                       reinterpret_cast<float*>(fb + f.L[0]),
+                                                       reinterpret_cast<float*>(fb + f.w));
   int rc = launched();
   if (rc != HTRC_OK || s.levels < 2) return rc;
   if ((rc = set_smem(tree_gram_kernel<T>, sizeof(GramSmem))) != HTRC_OK) return rc;
@@ -2000,8 +2013,9 @@ int values_impl(const HtrcTreeDims* d, const Shape& s, const T* k, const T* v, c
     if ((rc = set_smem(tree_leafblock_tc_kernel, kTcSmemBytes)) != HTRC_OK) return rc;
     tree_leafblock_tc_kernel<<<dim3(s.n[1], C, slices(mx, kSlice)), 256, kTcSmemBytes, st>>>(
         reinterpret_cast<const uint16_t*>(q), reinterpret_cast<const uint16_t*>(k),
-        reinterpret_cast<const uint16_t*>(v), d->n_keys, d->scale, a, perm, coff, kSlice, lv, d->threshold, norm,
-        base, n_records, rec_val, rec_lm, rec_ex, status);
+        reinterpret_cast<const uint16_t*>(v), d->n_keys, d->scale, a,
+        reinterpret_cast<const float*>(static_cast<const uint8_t*>(forest) + f.w), perm, coff, kSlice, lv,
+        d->threshold, norm, base, n_records, rec_val, rec_lm, rec_ex, status);
   } else {
     if ((rc = set_smem(tree_leafblock_kernel<T>, sizeof(BlockSmem))) != HTRC_OK) return rc;
     tree_leafblock_kernel<T><<<dim3(top >= 1 ? s.n[1] : 1, C, slices(mx, kSlice)), 256, sizeof(BlockSmem), st>>>(
