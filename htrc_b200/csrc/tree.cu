@@ -215,6 +215,11 @@ __global__ void __launch_bounds__(64) tree_leaf_kernel(const T* __restrict__ k, 
   if (tid < cnt) w_out[static_cast<int64_t>(c) * m + s0 + tid] = expf(a - ll);
 }
 
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
 // 8 floats -> their bf16 parts: hi = bf16(x), lo = bf16(x - hi) (16 bytes each)
 __device__ __forceinline__ void split_bf16x8(const float* x, uint4* hi, uint4* lo) {
   uint32_t h[4], l[4];
@@ -359,6 +364,209 @@ __global__ void __launch_bounds__(256, 1) tree_gram_kernel(const T* __restrict__
     *reinterpret_cast<uint4*>(jb + (rb * 8 + x) * kD + cb * 8) = hi;
     *reinterpret_cast<uint4*>(jb + kD * kD + (rb * 8 + x) * kD + cb * 8) = lo;
   }
+}
+
+// Level-1 nodes on the tensor cores: pass 1 as tree_gram_kernel (L, g, u on the CUDA cores), then
+//   H = (W ck)^T ck,  J = (W cv)^T ck    (ck = k - g, cv = v - u, W = e^(a - L) over the node's keys)
+// as tcgen05 kind::f16 MMAs (M 128 dims x N 128 dims x K 32 keys per stage) with every operand split into three
+// bf16 parts (x = h + m + l, 24 significant bits) and the six products of order up to 2^-16 (hh, hm, mh, hl,
+// lh, mm): float32-level sums over the node's 1024 keys.  The operands are written by the CTA's threads in the
+// 128-byte-swizzled MN-major layout (a key's 128 dims contiguous); H in TMEM columns 0..127, J in 128..255.
+// One CTA of 256 threads per (node, centre), two per SM.
+constexpr int kGtKeys = 32;                             // keys per stage
+constexpr uint32_t kGtTile = 2 * kGtKeys * 128;         // one operand part: two 64-dim chunks of [32 key rows][128 B]
+struct __align__(1024) GramTcSmem {
+  uint8_t t[9][kGtTile];      // W ck h, m, l | W cv h, m, l | ck h, m, l   (pass 1 reuses the space as float rows)
+  float g[kD], u[kD];
+  float w[64];
+  float ln;
+  uint64_t bar;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+constexpr size_t kGramTcSmemBytes = 80 * 1024;          // > 228 KB / 3: at most two CTAs (512 TMEM columns) per SM
+static_assert(sizeof(GramTcSmem) + 1024 <= kGramTcSmemBytes, "tree build shared layout");
+
+// 8 floats -> three bf16 parts each (x = h + m + l to 24 significant bits), 16 bytes per part
+__device__ __forceinline__ void split3_bf16x8(const float* x, uint4* h, uint4* mm, uint4* l) {
+  float r[8];
+  uint4 t;
+  split_bf16x8(x, h, &t);
+  const uint32_t hw[4] = {h->x, h->y, h->z, h->w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 hf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&hw[i]));
+    r[2 * i] = x[2 * i] - hf.x;
+    r[2 * i + 1] = x[2 * i + 1] - hf.y;
+  }
+  split_bf16x8(r, mm, l);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256, 1) tree_gram_tc_kernel(
+    const T* __restrict__ k, const T* __restrict__ v, int64_t m, int leaf, int fanout, int nl,
+    const float* __restrict__ a, const float* __restrict__ leaf_l, int n1, float* __restrict__ L1,
+    float* __restrict__ g1, float* __restrict__ u1, float* __restrict__ H1, float* __restrict__ JT1,
+    uint16_t* __restrict__ Hb1, uint16_t* __restrict__ Jb1, int* __restrict__ status) {
+  extern __shared__ unsigned char smem_raw[];
+  GramTcSmem& sh = *reinterpret_cast<GramTcSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int i = blockIdx.x, c = blockIdx.y, tid = threadIdx.x, warp = tid >> 5;
+  const int l0 = i * fanout, l1 = min(nl, l0 + fanout);
+  const int64_t k0 = static_cast<int64_t>(l0) * leaf;
+  const int64_t k1 = min(m, static_cast<int64_t>(l1) * leaf);
+  const float* ac = a + static_cast<int64_t>(c) * m;
+  if (tid == 0) {
+    float mx = -INFINITY;
+    for (int l = l0; l < l1; ++l) mx = fmaxf(mx, leaf_l[static_cast<int64_t>(c) * nl + l]);
+    float s = 0.f;
+    for (int l = l0; l < l1; ++l) s += expf(leaf_l[static_cast<int64_t>(c) * nl + l] - mx);
+    sh.ln = mx + logf(s);
+    mbar_init(&sh.bar, 1);
+    sh.abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) tmem_alloc(&sh.tmem_base, 256);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const float ln = sh.ln;
+  const uint32_t tmem = sh.tmem_base;
+  // pass 1: g = sum W k (threads 0..127), u = sum W v (threads 128..255), keys in order
+  {
+    float (*kr)[132] = reinterpret_cast<float (*)[132]>(sh.t[0]);
+    float (*vr)[132] = reinterpret_cast<float (*)[132]>(sh.t[0] + 32 * 132 * 4);
+    float acc1 = 0.f;
+    for (int64_t base = k0; base < k1; base += 32) {
+      const int cnt = static_cast<int>(k1 - base < 32 ? k1 - base : 32);
+      for (int x = tid; x < cnt * 32; x += 256) {
+        const int r = x >> 5, c4 = x & 31;
+        *reinterpret_cast<float4*>(&kr[r][4 * c4]) = ld_row4<T>(k, base + r, c4);
+        *reinterpret_cast<float4*>(&vr[r][4 * c4]) = ld_row4<T>(v, base + r, c4);
+      }
+      if (tid < cnt) sh.w[tid] = expf(ac[base + tid] - ln);
+      __syncthreads();
+      if (tid < kD) {
+        for (int s = 0; s < cnt; ++s) acc1 = fmaf(sh.w[s], kr[s][tid], acc1);
+      } else {
+        for (int s = 0; s < cnt; ++s) acc1 = fmaf(sh.w[s], vr[s][tid - kD], acc1);
+      }
+      __syncthreads();
+    }
+    if (tid < kD) sh.g[tid] = acc1; else sh.u[tid - kD] = acc1;
+  }
+  __syncthreads();
+  const int64_t node = static_cast<int64_t>(c) * n1 + i;
+  if (tid < kD) g1[node * kD + tid] = sh.g[tid]; else u1[node * kD + tid - kD] = sh.u[tid - kD];
+  if (tid == 0) L1[node] = ln;
+  // pass 2 on the tensor cores, 32 keys per stage; warps 0..3 own the H rows (TMEM lane d = row d), warps 4..7
+  // the J rows (value dim dv = lane)
+  const int d = tid & 127;
+  const uint32_t lane_off = static_cast<uint32_t>(d & ~31) << 16;
+  const bool isj = tid >= 128;
+  float racc[kD];
+#pragma unroll
+  for (int j = 0; j < kD; ++j) racc[j] = 0.f;
+  const uint32_t idesc = idesc_bf16(128, 128, true, true);
+  const uint32_t t0 = smem_u32(sh.t[0]);
+  uint32_t phase = 0;
+  bool ok = true;
+  for (int64_t base = k0; base < k1 && ok; base += kGtKeys) {
+    const int cnt = static_cast<int>(k1 - base < kGtKeys ? k1 - base : kGtKeys);
+    if (tid < kGtKeys) sh.w[tid] = tid < cnt ? expf(ac[base + tid] - ln) : 0.f;
+    __syncthreads();
+    for (int x = tid; x < kGtKeys * 16; x += 256) {
+      const int r = x >> 4, cc = x & 15;
+      float ck[8], aw[8], jw[8];
+      if (r < cnt) {
+        const float4 k0v = ld_row4<T>(k, base + r, 2 * cc), k1v = ld_row4<T>(k, base + r, 2 * cc + 1);
+        const float4 v0v = ld_row4<T>(v, base + r, 2 * cc), v1v = ld_row4<T>(v, base + r, 2 * cc + 1);
+        const float kk[8] = {k0v.x, k0v.y, k0v.z, k0v.w, k1v.x, k1v.y, k1v.z, k1v.w};
+        const float vv[8] = {v0v.x, v0v.y, v0v.z, v0v.w, v1v.x, v1v.y, v1v.z, v1v.w};
+        const float w = sh.w[r];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          ck[e] = kk[e] - sh.g[8 * cc + e];
+          aw[e] = w * ck[e];
+          jw[e] = w * (vv[e] - sh.u[8 * cc + e]);
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ck[e] = aw[e] = jw[e] = 0.f;
+      }
+      const uint32_t off = (cc >> 3) * (kGtKeys * 128) + sw128_off(r, cc & 7);
+      uint4 p0, p1, p2;
+      split3_bf16x8(aw, &p0, &p1, &p2);
+      st_shared_v4(t0 + 0 * kGtTile + off, p0);
+      st_shared_v4(t0 + 1 * kGtTile + off, p1);
+      st_shared_v4(t0 + 2 * kGtTile + off, p2);
+      split3_bf16x8(jw, &p0, &p1, &p2);
+      st_shared_v4(t0 + 3 * kGtTile + off, p0);
+      st_shared_v4(t0 + 4 * kGtTile + off, p1);
+      st_shared_v4(t0 + 5 * kGtTile + off, p2);
+      split3_bf16x8(ck, &p0, &p1, &p2);
+      st_shared_v4(t0 + 6 * kGtTile + off, p0);
+      st_shared_v4(t0 + 7 * kGtTile + off, p1);
+      st_shared_v4(t0 + 8 * kGtTile + off, p2);
+    }
+    fence_proxy_async_smem();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      // (A part, B part): h.h, h.m, m.h, h.l, l.h, m.m; each stage's sum starts afresh in TMEM
+      const int ap[6] = {0, 0, 1, 0, 2, 1}, bp[6] = {0, 1, 0, 2, 0, 1};
+#pragma unroll
+      for (int kk = 0; kk < kGtKeys / 16; ++kk)
+#pragma unroll
+        for (int pr = 0; pr < 6; ++pr) {
+          const uint64_t bd = sw128_desc(t0 + (6 + bp[pr]) * kGtTile + kk * 2048, kGtKeys * 128, 1024);
+          const uint32_t acc = (kk || pr) ? 1u : 0u;
+          mma_bf16(tmem, sw128_desc(t0 + (0 + ap[pr]) * kGtTile + kk * 2048, kGtKeys * 128, 1024), bd, idesc, acc);
+          mma_bf16(tmem + 128, sw128_desc(t0 + (3 + ap[pr]) * kGtTile + kk * 2048, kGtKeys * 128, 1024), bd, idesc,
+                   acc);
+        }
+      mma_commit(&sh.bar);
+    }
+    ok = mbar_wait(&sh.bar, phase, status, &sh.abort_flag);
+    phase ^= 1u;
+    ok = __syncthreads_and(ok);
+    if (!ok) break;
+    // fold this stage's 32-key sums into the row's float32 accumulators (IEEE adds across stages: the tensor
+    // core's own accumulation covers 32 keys only)
+    tc_fence_after();
+#pragma unroll
+    for (int cb = 0; cb < 4; ++cb) {
+      uint32_t y[32];
+      tmem_ld32(tmem + lane_off + (isj ? 128 : 0) + 32 * cb, y);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) racc[32 * cb + j] += __uint_as_float(y[j]);
+    }
+    tc_fence_before();
+    __syncthreads();
+  }
+  if (ok) {
+    float* hn = H1 + node * kD * kD;
+    float* jt = JT1 + node * kD * kD;
+    uint16_t* bn = (isj ? Jb1 : Hb1) + node * 2 * kD * kD;
+    if (!isj) {
+#pragma unroll
+      for (int j = 0; j < kD; j += 4)
+        *reinterpret_cast<float4*>(hn + d * kD + j) = make_float4(racc[j], racc[j + 1], racc[j + 2], racc[j + 3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < kD; ++j) jt[j * kD + d] = racc[j];          // J^T[e][dv]
+    }
+#pragma unroll
+    for (int j = 0; j < kD; j += 8) {
+      uint4 h, l;
+      split_bf16x8(racc + j, &h, &l);
+      *reinterpret_cast<uint4*>(bn + d * kD + j) = h;
+      *reinterpret_cast<uint4*>(bn + kD * kD + d * kD + j) = l;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 256);
 }
 
 // Levels >= 2 (model.py:51-66): w = softmax of the children's log-masses, g = sum w g_c, u = sum w u_c,
@@ -1140,10 +1348,6 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
-  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
-               : "memory");
-}
 
 __global__ void __launch_bounds__(256, 2) tree_leafblock_tc_kernel(
     const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, const uint16_t* __restrict__ v, int64_t m,
@@ -1710,13 +1914,15 @@ int shape_of(const HtrcTreeDims* d, Shape* s) {
 }
 
 struct ForestLayout {
-  size_t a = 0, w = 0, L[kMaxLevels] = {}, g[kMaxLevels] = {}, u[kMaxLevels] = {}, H[kMaxLevels] = {},
+  size_t status = 0, a = 0, w = 0, L[kMaxLevels] = {}, g[kMaxLevels] = {}, u[kMaxLevels] = {}, H[kMaxLevels] = {},
          JT[kMaxLevels] = {}, Hb[kMaxLevels] = {}, Jb[kMaxLevels] = {}, total = 0;
 };
 ForestLayout forest_layout(const HtrcTreeDims* d, const Shape& s) {
   ForestLayout f;
   const size_t C = d->n_centres;
   size_t o = 0;
+  f.status = o;                               // the build's device status word
+  o += 256;
   f.a = o;
   o += a256(C * d->n_keys * 4);
   f.w = o;                                    // w = e^(a - L) of every key within its leaf
@@ -1876,12 +2082,23 @@ int build_impl(const HtrcTreeDims* d, const Shape& s, const T* k, const T* v, co
   const ForestLayout f = forest_layout(d, s);
   uint8_t* fb = static_cast<uint8_t*>(forest);
   float* a = reinterpret_cast<float*>(fb + f.a);
+  int* status = reinterpret_cast<int*>(fb + f.status);
   const int C = d->n_centres;
+  if (cudaMemsetAsync(status, 0, 4, st) != cudaSuccess) return HTRC_ERR_CUDA;
   tree_leaf_kernel<T><<<dim3(s.n[0], C), 64, 0, st>>>(k, d->n_keys, d->leaf_size, centres, s.n[0], a,
                                                        reinterpret_cast<float*>(fb + f.L[0]),
                                                        reinterpret_cast<float*>(fb + f.w));
   int rc = launched();
   if (rc != HTRC_OK || s.levels < 2) return rc;
+  if (tc_nodes_enabled()) {
+    if ((rc = set_smem(tree_gram_tc_kernel<T>, kGramTcSmemBytes)) != HTRC_OK) return rc;
+    tree_gram_tc_kernel<T><<<dim3(s.n[1], C), 256, kGramTcSmemBytes, st>>>(
+        k, v, d->n_keys, d->leaf_size, d->fanout, s.n[0], a, reinterpret_cast<const float*>(fb + f.L[0]), s.n[1],
+        reinterpret_cast<float*>(fb + f.L[1]), reinterpret_cast<float*>(fb + f.g[1]),
+        reinterpret_cast<float*>(fb + f.u[1]), reinterpret_cast<float*>(fb + f.H[1]),
+        reinterpret_cast<float*>(fb + f.JT[1]), reinterpret_cast<uint16_t*>(fb + f.Hb[1]),
+        reinterpret_cast<uint16_t*>(fb + f.Jb[1]), status);
+  } else {
   if ((rc = set_smem(tree_gram_kernel<T>, sizeof(GramSmem))) != HTRC_OK) return rc;
   tree_gram_kernel<T><<<dim3(s.n[1], C), 256, sizeof(GramSmem), st>>>(
       k, v, d->n_keys, d->leaf_size, d->fanout, s.n[0], a, reinterpret_cast<const float*>(fb + f.L[0]), s.n[1],
@@ -1889,6 +2106,7 @@ int build_impl(const HtrcTreeDims* d, const Shape& s, const T* k, const T* v, co
       reinterpret_cast<float*>(fb + f.u[1]), reinterpret_cast<float*>(fb + f.H[1]),
       reinterpret_cast<float*>(fb + f.JT[1]), reinterpret_cast<uint16_t*>(fb + f.Hb[1]),
       reinterpret_cast<uint16_t*>(fb + f.Jb[1]));
+  }
   if ((rc = launched()) != HTRC_OK) return rc;
   if ((rc = set_smem(tree_merge_kernel, sizeof(MergeSmem))) != HTRC_OK) return rc;
   for (int l = 2; l < s.levels; ++l) {
@@ -1959,13 +2177,16 @@ int walk_impl(const HtrcTreeDims* d, const Shape& s, const T* q, const int32_t* 
     if ((rc = launched()) != HTRC_OK) return rc;
   }
   int64_t total = 0;
-  int stat = 0;
+  int stat = 0, fstat = 0;
+  const int* fstatus = reinterpret_cast<const int*>(static_cast<const uint8_t*>(forest) + forest_layout(d, s).status);
   if ((N > 0 && cudaMemcpyAsync(&total, base + N, 8, cudaMemcpyDeviceToHost, st) != cudaSuccess) ||
       cudaMemcpyAsync(&stat, status, 4, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaMemcpyAsync(&fstat, fstatus, 4, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
       cudaStreamSynchronize(st) != cudaSuccess)
     return HTRC_ERR_CUDA;
   *n_records = total;
-  return stat ? HTRC_ERR_ARG : HTRC_OK;
+  if (fstat) return HTRC_ERR_DEVICE;            // the build's MMA wait gave up
+  return stat & ST_BAD_INDEX ? HTRC_ERR_ARG : stat ? HTRC_ERR_DEVICE : HTRC_OK;
 }
 
 template <typename T>
