@@ -1385,25 +1385,51 @@ __global__ void __launch_bounds__(256, 2) tree_leafblock_tc_kernel(
   const uint32_t id_s = idesc_bf16(128, 64, false, false);
   const uint32_t id_pv = idesc_bf16(128, 128, false, true);
   const uint32_t qa = smem_u32(sh.qs);
-  // the keys and values of leaf l into buffer b (one cp.async group; rows past the leaf's keys are zeros)
-  auto stage_kv = [&](int l, int b) {
-    const int64_t s0 = static_cast<int64_t>(l) * leaf;
-    const int kc = static_cast<int>(m - s0 < leaf ? m - s0 : leaf);
-    const uint32_t kb = smem_u32(sh.ks[b]), vb = smem_u32(sh.vs[b]);
-    for (int x = tid; x < 64 * 16; x += 256) {
-      const int r = x >> 4, cc = x & 15;
-      const uint32_t nb = r < kc ? 16u : 0u;
-      const int64_t kr = s0 + (r < kc ? r : 0);
-      const uint32_t off = (cc >> 3) * (64 * 128) + sw128_off(r, cc & 7);
-      cp_async16(kb + off, k + kr * kD + cc * 8, nb);
-      cp_async16(vb + off, v + kr * kD + cc * 8, nb);
-    }
-    if (tid < 128) {                          // the leaf's key logits a and weights w (zeros past its keys)
-      const int r = tid & 63;
-      const float* src = (tid < 64 ? ac : wc) + s0 + (r < kc ? r : 0);
-      cp_async4(smem_u32(tid < 64 ? &sh.as[b][r] : &sh.ws[b][r]), src, r < kc ? 4u : 0u);
+  // leaf l's keys into K buffer b, and its values with its key logits a and weights w into V buffer b (one
+  // cp.async group each; rows past the leaf's keys are zeros).  l >= l1 commits an empty group, which keeps the
+  // group count of every step the same (the waits below count groups).
+  auto stage_k = [&](int l, int b) {
+    if (l < l1) {
+      const int64_t s0 = static_cast<int64_t>(l) * leaf;
+      const int kc = static_cast<int>(m - s0 < leaf ? m - s0 : leaf);
+      const uint32_t kb = smem_u32(sh.ks[b]);
+      for (int x = tid; x < 64 * 16; x += 256) {
+        const int r = x >> 4, cc = x & 15;
+        const int64_t kr = s0 + (r < kc ? r : 0);
+        cp_async16(kb + (cc >> 3) * (64 * 128) + sw128_off(r, cc & 7), k + kr * kD + cc * 8, r < kc ? 16u : 0u);
+      }
     }
     cp_async_commit();
+  };
+  auto stage_v = [&](int l, int b) {
+    if (l < l1) {
+      const int64_t s0 = static_cast<int64_t>(l) * leaf;
+      const int kc = static_cast<int>(m - s0 < leaf ? m - s0 : leaf);
+      const uint32_t vb = smem_u32(sh.vs[b]);
+      for (int x = tid; x < 64 * 16; x += 256) {
+        const int r = x >> 4, cc = x & 15;
+        const int64_t kr = s0 + (r < kc ? r : 0);
+        cp_async16(vb + (cc >> 3) * (64 * 128) + sw128_off(r, cc & 7), v + kr * kD + cc * 8, r < kc ? 16u : 0u);
+      }
+      if (tid < 128) {
+        const int r = tid & 63;
+        const float* src = (tid < 64 ? ac : wc) + s0 + (r < kc ? r : 0);
+        cp_async4(smem_u32(tid < 64 ? &sh.as[b][r] : &sh.ws[b][r]), src, r < kc ? 4u : 0u);
+      }
+    }
+    cp_async_commit();
+  };
+  // S(l) = q . k of leaf l into TMEM columns 64 b .. 64 b + 63 (thread 0)
+  auto issue_s = [&](int b) {
+    tc_fence_after();
+    const uint32_t ka = smem_u32(sh.ks[b]);
+#pragma unroll
+    for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        mma_bf16(tmem + 64 * b, sw128_desc(qa + kb * (kTcQ * 128) + ks * 32, 16, 1024),
+                 sw128_desc(ka + kb * (64 * 128) + ks * 32, 16, 1024), id_s, (kb | ks) != 0);
+    mma_commit(&sh.bar_s);
   };
   uint32_t ph_s = 0, ph_pv = 0;
   bool ok = true;
@@ -1422,50 +1448,58 @@ __global__ void __launch_bounds__(256, 2) tree_leafblock_tc_kernel(
       const float nrm = live ? norm[lst[row]] : 0.f;
       float m_run = -INFINITY, s_run = 0.f;
       int nex = 0;
-      stage_kv(l0, 0);
+      // pipeline over the block's leaves i = l - l0: S(i + 1) runs on the tensor cores during the row math of
+      // leaf i, K(i + 2) and V(i + 1) load during leaf i; leaf i's S and then its P use TMEM columns 64 (i & 1)..,
+      // O columns 128..255.  Prologue: K(0), (empty), K(1), V(0), then S(0).
+      stage_k(l0, 0);
+      cp_async_commit();
+      stage_k(l0 + 1, 1);
+      stage_v(l0, 0);
+      cp_async_wait<2>();
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncthreads();
+      if (tid == 0) issue_s(0);
       for (int l = l0; l < l1; ++l) {
         const int b = (l - l0) & 1;
         const int64_t s0 = static_cast<int64_t>(l) * leaf;
         const int kc = static_cast<int>(m - s0 < leaf ? m - s0 : leaf);
         const float ll = lL[l];
-        // the next leaf's copies go out now (its buffer's last readers, the MMAs of leaf l - 1, completed)
-        if (l + 1 < l1) {
-          stage_kv(l + 1, b ^ 1);
-          cp_async_wait<1>();
-        } else {
-          cp_async_wait<0>();
-        }
-        const uint32_t ka = smem_u32(sh.ks[b]), va = smem_u32(sh.vs[b]);
-        const float* as_ = sh.as[b] + 32 * hf;            // this half's keys
-        const float* ws_ = sh.ws[b] + 32 * hf;
-        const int kh = min(32, max(0, kc - 32 * hf));     // this half's valid keys
-        fence_proxy_async_smem();
-        __syncthreads();
-        if (tid == 0) {
-          tc_fence_after();
-#pragma unroll
-          for (int kb = 0; kb < 2; ++kb)
-#pragma unroll
-            for (int ks = 0; ks < 4; ++ks)
-              mma_bf16(tmem, sw128_desc(qa + kb * (kTcQ * 128) + ks * 32, 16, 1024),
-                       sw128_desc(ka + kb * (64 * 128) + ks * 32, 16, 1024), id_s, (kb | ks) != 0);
-          mma_commit(&sh.bar_s);
-        }
-        ok = mbar_wait(&sh.bar_s, ph_s, status, &sh.abort_flag);
+        ok = mbar_wait(&sh.bar_s, ph_s, status, &sh.abort_flag);            // S(i)
         ph_s ^= 1u;
         if (!__syncthreads_and(ok)) {
           ok = false;
           break;
         }
         tc_fence_after();
+        stage_k(l + 2, b);                         // K buffer b: its last reader S(i) has completed
         float S[32];
         {
           uint32_t r0[32];
-          tmem_ld32(tmem + lane_off + 32 * hf, r0);
+          tmem_ld32(tmem + lane_off + 64 * b + 32 * hf, r0);
           tmem_ld_wait();
 #pragma unroll
           for (int j = 0; j < 32; ++j) S[j] = scale * __uint_as_float(r0[j]);
         }
+        if (l > l0) {                              // PV(i - 1): frees V buffer b ^ 1, TMEM columns 64 (b ^ 1).., O
+          ok = mbar_wait(&sh.bar_pv, ph_pv, status, &sh.abort_flag);
+          ph_pv ^= 1u;
+          if (!__syncthreads_and(ok)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+        }
+        stage_v(l + 1, b ^ 1);
+        cp_async_wait<2>();                        // K(i + 1), V(i), a(i), w(i) have landed
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        if (tid == 0 && l + 1 < l1) issue_s(b ^ 1);
+        const uint32_t va = smem_u32(sh.vs[b]);
+        const float* as_ = sh.as[b] + 32 * hf;            // this half's keys
+        const float* ws_ = sh.ws[b] + 32 * hf;
+        const int kh = min(32, max(0, kc - 32 * hf));     // this half's valid keys
         const float4* w4p = reinterpret_cast<const float4*>(ws_);
         const float4* a4p = reinterpret_cast<const float4*>(as_);
         // prediction (model.py:91-96 from the keys): xbar = sum w x, quad = sum w (x - xbar)^2, x = S - a;
@@ -1573,28 +1607,27 @@ __global__ void __launch_bounds__(256, 2) tree_leafblock_tc_kernel(
             ph[j >> 1] = *reinterpret_cast<const uint32_t*>(&hb);
             pl[j >> 1] = pack_bf16x2(pc[0] - hf2.x, pc[1] - hf2.y);
           }
-          tmem_st16(tmem + lane_off + 64 + 16 * hf, ph);
-          tmem_st16(tmem + lane_off + 96 + 16 * hf, pl);
+          tmem_st16(tmem + lane_off + 64 * b + 16 * hf, ph);
+          tmem_st16(tmem + lane_off + 64 * b + 32 + 16 * hf, pl);
         }
         tmem_st_wait();
         tc_fence_before();
         __syncthreads();
-        if (tid == 0) {
+        if (tid == 0) {                            // PV(i): O += P(i) . V(i), P from TMEM columns 64 b..
           tc_fence_after();
 #pragma unroll
           for (int part = 0; part < 2; ++part)
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
-              mma_bf16_ts_by(1u, tmem + 128, tmem + 64 + 32 * part + 8 * kk,
+              mma_bf16_ts_by(1u, tmem + 128, tmem + 64 * b + 32 * part + 8 * kk,
                              sw128_desc(va + kk * 2048, 64 * 128, 1024), id_pv, (l > l0 || part || kk) ? 1u : 0u);
           mma_commit(&sh.bar_pv);
         }
+      }
+      if (ok) {                                    // PV of the block's last leaf
         ok = mbar_wait(&sh.bar_pv, ph_pv, status, &sh.abort_flag);
         ph_pv ^= 1u;
-        if (!__syncthreads_and(ok)) {
-          ok = false;
-          break;
-        }
+        ok = __syncthreads_and(ok);
         tc_fence_after();
       }
       if (!ok) break;
