@@ -215,3 +215,27 @@ def test_tensor_core_nodes_match_cuda_core_nodes():
         cnt = np.stack([_np(it[x]) for x in ("visited_nodes", "accepted_nodes", "exact_leaves")], 1)
         ref = np.stack([_np(is_[x]) for x in ("visited_nodes", "accepted_nodes", "exact_leaves")], 1)
         _check(ot, cnt, _np(os_), ref, lt, _np(ls_), same_tol=2e-4)
+
+
+@pytest.mark.parametrize("m,leaf,fanout", [(1000, 16, 4), (4096, 16, 4), (3000, 40, 8)])
+def test_tensor_core_path_on_other_shapes(m, leaf, fanout):
+    """bfloat16 inputs through the tensor-core kernels (build, node products, leaf blocks) with leaves of 16 and
+    40 keys, a ragged last leaf (1000 = 62 x 16 + 8, 3000 = 75 x 40) and four levels (4096 keys, leaf 16,
+    fanout 4), against the float64 oracle on the same bfloat16 values."""
+    from htrc_b200 import synth, tree
+    q, k, v = synth.cluster_inputs(m, 128, clusters=32, seed=m + leaf)
+    q, k, v = (torch.from_numpy(x).bfloat16() for x in (q, k, v))
+    qn, kn, vn = (x.float().numpy().astype(np.float64) for x in (q, k, v))
+    sc = 1.0 / np.sqrt(128)
+    cen, asg = G.centres_of(qn * sc, 4)
+    dev = torch.device("cuda")
+    out, lse, info = tree.tree_attention(q.to(dev), k.to(dev), v.to(dev), leaf_size=leaf, fanout=fanout,
+                                         centres=torch.from_numpy(cen).float().to(dev),
+                                         assign=torch.from_numpy(asg).int().to(dev), return_lse=True, return_info=True)
+    assert info["forest"].levels == (4 if m == 4096 else 3)
+    rows = np.arange(0, m, max(1, m // 96))
+    ref, ref_lse, ref_cnt, _ = T.evaluate_centres(kn, vn, qn[rows] * sc, cen, asg[rows], leaf_size=leaf, fanout=fanout,
+                                                  opening_threshold=0.02)
+    cnt = np.stack([_np(info[x])[rows] for x in ("visited_nodes", "accepted_nodes", "exact_leaves")], 1)
+    rc = np.stack([ref_cnt[x] for x in ("visited_nodes", "accepted_nodes", "exact_leaves")], 1)
+    _check(_np(out)[rows], cnt, ref, rc, _np(lse)[rows], ref_lse, agree=0.97, same_tol=1e-3)
