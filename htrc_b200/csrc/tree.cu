@@ -1503,9 +1503,10 @@ __global__ void __launch_bounds__(256, 2) tree_leafblock_tc_kernel(
         const float4* w4p = reinterpret_cast<const float4*>(ws_);
         const float4* a4p = reinterpret_cast<const float4*>(as_);
         // prediction (model.py:91-96 from the keys): xbar = sum w x, quad = sum w (x - xbar)^2, x = S - a;
-        // each half sums its 32 keys, the pair adds the two halves in a fixed order
+        // each half sums its 32 keys, the pair adds the two halves in a fixed order.  The first exchange also
+        // carries the half's maximum score, which an opened leaf's logsumexp needs.
         {
-          float p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
+          float p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f, m0 = -INFINITY, m1 = -INFINITY;
 #pragma unroll
           for (int j = 0; j < 32; j += 4) {
             const float4 w4 = w4p[j >> 2], a4 = a4p[j >> 2];
@@ -1513,11 +1514,17 @@ __global__ void __launch_bounds__(256, 2) tree_leafblock_tc_kernel(
             p1 = fmaf(w4.y, S[j + 1] - a4.y, p1);
             p2 = fmaf(w4.z, S[j + 2] - a4.z, p2);
             p3 = fmaf(w4.w, S[j + 3] - a4.w, p3);
+            if (j < kh) m0 = fmaxf(m0, S[j]);
+            if (j + 1 < kh) m1 = fmaxf(m1, S[j + 1]);
+            if (j + 2 < kh) m0 = fmaxf(m0, S[j + 2]);
+            if (j + 3 < kh) m1 = fmaxf(m1, S[j + 3]);
           }
           sh.xch[0][hf][row] = (p0 + p1) + (p2 + p3);
+          sh.xch[2][hf][row] = fmaxf(m0, m1);
         }
         named_bar_sync(pair_bar, 64);
         const float xb = sh.xch[0][0][row] + sh.xch[0][1][row];
+        const float mx = fmaxf(sh.xch[2][0][row], sh.xch[2][1][row]);
         {
           float p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
 #pragma unroll
@@ -1536,29 +1543,21 @@ __global__ void __launch_bounds__(256, 2) tree_leafblock_tc_kernel(
         const float qd = sh.xch[1][0][row] + sh.xch[1][1][row];
         const float lmv = ll + xb + 0.5f * qd;
         const bool open = live && score_of(lmv, qd, nrm) > thr;
-        // an opened leaf's log-mass: logsumexp of its scores (both halves, fixed order)
-        {
-          float m0 = -INFINITY, m1 = -INFINITY;
-          if (open) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 2) {
-              if (j < kh) m0 = fmaxf(m0, S[j]);
-              if (j + 1 < kh) m1 = fmaxf(m1, S[j + 1]);
-            }
-          }
-          sh.xch[2][hf][row] = fmaxf(m0, m1);
-        }
-        named_bar_sync(pair_bar, 64);
-        const float mx = fmaxf(sh.xch[2][0][row], sh.xch[2][1][row]);
+        // an opened leaf's log-mass: logsumexp of its scores (both halves, fixed order); its exponentials
+        // e^(S - mx) replace the scores in S, and its P below is e^(S - mx) e^(mx - mn)
         {
           float e0 = 0.f, e1 = 0.f, e2 = 0.f, e3 = 0.f;
           if (open) {
 #pragma unroll
             for (int j = 0; j < 32; j += 4) {
-              if (j < kh) e0 += __expf(S[j] - mx);
-              if (j + 1 < kh) e1 += __expf(S[j + 1] - mx);
-              if (j + 2 < kh) e2 += __expf(S[j + 2] - mx);
-              if (j + 3 < kh) e3 += __expf(S[j + 3] - mx);
+              S[j] = __expf(S[j] - mx);
+              S[j + 1] = __expf(S[j + 1] - mx);
+              S[j + 2] = __expf(S[j + 2] - mx);
+              S[j + 3] = __expf(S[j + 3] - mx);
+              if (j < kh) e0 += S[j];
+              if (j + 1 < kh) e1 += S[j + 1];
+              if (j + 2 < kh) e2 += S[j + 2];
+              if (j + 3 < kh) e3 += S[j + 3];
             }
           }
           sh.xch[3][hf][row] = (e0 + e1) + (e2 + e3);
@@ -1577,6 +1576,7 @@ __global__ void __launch_bounds__(256, 2) tree_leafblock_tc_kernel(
         nex += open;
         const float fw = expf(lmv - mn);
         const float c0 = fw * (1.f - xb);          // far coefficient: w (fw (1 + x - xbar)) = w (fw x + c0)
+        const float fo = open ? __expf(mx - mn) : 0.f;   // opened: P = e^(S - mx) e^(mx - mn)
         // rescale this half of O (its previous PV has completed).  tcgen05.ld / st are warp-collective
         // (.sync.aligned): the warp takes the branch as a whole, rows whose reference did not move scale by 1
         if (__any_sync(0xffffffffu, l > l0 && al != 1.f)) {
@@ -1600,7 +1600,7 @@ __global__ void __launch_bounds__(256, 2) tree_leafblock_tc_kernel(
             for (int t = 0; t < 2; ++t) {
               const int jj = j + t;
               pc[t] = 0.f;
-              if (live && jj < kh) pc[t] = open ? __expf(S[jj] - mn) : ws_[jj] * fmaf(fw, S[jj] - as_[jj], c0);
+              if (live && jj < kh) pc[t] = open ? S[jj] * fo : ws_[jj] * fmaf(fw, S[jj] - as_[jj], c0);
             }
             const __nv_bfloat162 hb = __floats2bfloat162_rn(pc[0], pc[1]);
             const float2 hf2 = __bfloat1622float2(hb);
