@@ -239,3 +239,28 @@ def test_tensor_core_path_on_other_shapes(m, leaf, fanout):
     cnt = np.stack([_np(info[x])[rows] for x in ("visited_nodes", "accepted_nodes", "exact_leaves")], 1)
     rc = np.stack([ref_cnt[x] for x in ("visited_nodes", "accepted_nodes", "exact_leaves")], 1)
     _check(_np(out)[rows], cnt, ref, rc, _np(lse)[rows], ref_lse, agree=0.97, same_tol=1e-3)
+
+
+def test_edge_cases():
+    """One key; one query; a centre that no query uses; queries exactly at a centre."""
+    from htrc_b200 import tree
+    rng = np.random.default_rng(21)
+    k1, v1 = rng.normal(size=(1, 8)), rng.normal(size=(1, 5))
+    c = rng.normal(size=8) * 0.2
+    qs = c + rng.normal(size=(3, 8)) * 0.1
+    f = tree.build_forest(k1, v1, c)
+    assert f.nodes == [1]
+    out, info = tree.evaluate(k1, v1, qs, c, f, opening_threshold=0.01)
+    np.testing.assert_allclose(_np(out), np.repeat(v1, 3, 0), atol=1e-6)     # one key: its value, exactly
+    k, v = rng.normal(size=(300, 8)), rng.normal(size=(300, 5))
+    cen = np.stack([c, c + 5.0])                                            # the second centre is never assigned
+    f2 = tree.build_forest(k, v, cen, leaf_size=16, fanout=4)
+    q1 = c + rng.normal(size=8) * 0.1
+    o1, i1 = tree.evaluate(k, v, q1[None], cen, f2, assign=[0])
+    lv = T.forest(k, v, c, leaf_size=16, fanout=4)
+    ref, _, rinfo = T.evaluate(k, v, q1[None], c, lv)
+    np.testing.assert_allclose(_np(o1)[0], ref[0], atol=2e-5)
+    assert int(i1["exact_leaves"][0]) == int(rinfo["exact_leaves"][0])
+    oc, ic = tree.evaluate(k, v, np.stack([c, c]), cen, f2, assign=[0, 0])  # at the centre: no leaf opens
+    np.testing.assert_allclose(_np(oc), np.repeat(T.exact_attention(k, v, c)[0], 2, 0), atol=2e-5)
+    assert int(ic["exact_leaves"].sum()) == 0
