@@ -220,6 +220,13 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
                : "memory");
 }
 
+// Element offset of (row r, column e) of one 128 x 128 bf16 operand part stored as its shared-memory image:
+// two K-blocks of 64 columns, each [128 rows][128 B] with the 128-byte swizzle (16-byte chunk c of row r at
+// chunk c ^ (r & 7)), so that one bulk copy lands a node's operand ready for the MMA descriptors.
+__host__ __device__ __forceinline__ int img_elem(int r, int e) {
+  return (e >> 6) * (128 * 64) + r * 64 + ((((e & 63) >> 3) ^ (r & 7)) << 3) + (e & 7);
+}
+
 // 8 floats -> their bf16 parts: hi = bf16(x), lo = bf16(x - hi) (16 bytes each)
 __device__ __forceinline__ void split_bf16x8(const float* x, uint4* hi, uint4* lo) {
   uint32_t h[4], l[4];
@@ -357,12 +364,13 @@ __global__ void __launch_bounds__(256, 1) tree_gram_kernel(const T* __restrict__
 #pragma unroll
   for (int x = 0; x < 8; ++x) {
     uint4 hi, lo;
+    const int e = img_elem(rb * 8 + x, cb * 8);
     split_bf16x8(h[x], &hi, &lo);
-    *reinterpret_cast<uint4*>(hb + (rb * 8 + x) * kD + cb * 8) = hi;
-    *reinterpret_cast<uint4*>(hb + kD * kD + (rb * 8 + x) * kD + cb * 8) = lo;
+    *reinterpret_cast<uint4*>(hb + e) = hi;
+    *reinterpret_cast<uint4*>(hb + kD * kD + e) = lo;
     split_bf16x8(j[x], &hi, &lo);
-    *reinterpret_cast<uint4*>(jb + (rb * 8 + x) * kD + cb * 8) = hi;
-    *reinterpret_cast<uint4*>(jb + kD * kD + (rb * 8 + x) * kD + cb * 8) = lo;
+    *reinterpret_cast<uint4*>(jb + e) = hi;
+    *reinterpret_cast<uint4*>(jb + kD * kD + e) = lo;
   }
 }
 
@@ -560,8 +568,8 @@ __global__ void __launch_bounds__(256, 1) tree_gram_tc_kernel(
     for (int j = 0; j < kD; j += 8) {
       uint4 h, l;
       split_bf16x8(racc + j, &h, &l);
-      *reinterpret_cast<uint4*>(bn + d * kD + j) = h;
-      *reinterpret_cast<uint4*>(bn + kD * kD + d * kD + j) = l;
+      *reinterpret_cast<uint4*>(bn + img_elem(d, j)) = h;
+      *reinterpret_cast<uint4*>(bn + kD * kD + img_elem(d, j)) = l;
     }
   }
   tc_fence_before();
@@ -633,10 +641,10 @@ __global__ void __launch_bounds__(256) tree_merge_kernel(int fanout, int nch, co
     const __nv_bfloat16 hh = __float2bfloat16_rn(hs), jh = __float2bfloat16_rn(js);
     uint16_t* hb = Hbp + node * 2 * kD * kD;
     uint16_t* jb = Jbp + node * 2 * kD * kD;
-    hb[e] = __bfloat16_as_ushort(hh);
-    hb[kD * kD + e] = __bfloat16_as_ushort(__float2bfloat16_rn(hs - __bfloat162float(hh)));
-    jb[f * kD + r] = __bfloat16_as_ushort(jh);                       // J[f][r] = J^T[r][f]
-    jb[kD * kD + f * kD + r] = __bfloat16_as_ushort(__float2bfloat16_rn(js - __bfloat162float(jh)));
+    hb[img_elem(r, f)] = __bfloat16_as_ushort(hh);
+    hb[kD * kD + img_elem(r, f)] = __bfloat16_as_ushort(__float2bfloat16_rn(hs - __bfloat162float(hh)));
+    jb[img_elem(f, r)] = __bfloat16_as_ushort(jh);                   // J[f][r] = J^T[r][f]
+    jb[kD * kD + img_elem(f, r)] = __bfloat16_as_ushort(__float2bfloat16_rn(js - __bfloat162float(jh)));
   }
 }
 
@@ -654,8 +662,8 @@ struct TreeLevels {
   const float* u[kMaxLevels]; // [C][n][128]     (l >= 1)
   const float* H[kMaxLevels]; // [C][n][128][128] (l >= 1)
   const float* JT[kMaxLevels];// [C][n][128][128] (l >= 1), J transposed
-  const uint16_t* Hb[kMaxLevels];  // [C][n][2][128][128] bf16 hi and lo parts of H (rows)
-  const uint16_t* Jb[kMaxLevels];  // [C][n][2][128][128] bf16 hi and lo parts of J (rows: value dims)
+  const uint16_t* Hb[kMaxLevels];  // [C][n][hi, lo] bf16 parts of H as shared-memory images (img_elem)
+  const uint16_t* Jb[kMaxLevels];  // [C][n][hi, lo] bf16 parts of J (rows: value dims) as images
 };
 
 // Stage delta rows (scale * q - c) of list[0 .. nq) into ds[64][kStr]; rows nq..63 are zero.
@@ -1692,6 +1700,7 @@ struct __align__(1024) NodeSmem {
   int list[kWindow];
   int wsum[4];
   uint64_t bar[2];
+  uint64_t bar_b[2];                 // operand buffer b[i] landed (bulk copy)
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -1737,6 +1746,8 @@ __global__ void __launch_bounds__(128, 1) tree_node_tc_kernel(
   if (tid == 0) {
     mbar_init(&sh.bar[0], 1);
     mbar_init(&sh.bar[1], 1);
+    mbar_init(&sh.bar_b[0], 1);
+    mbar_init(&sh.bar_b[1], 1);
     sh.abort_flag = 0;
     fence_barrier_init();
   }
@@ -1748,15 +1759,18 @@ __global__ void __launch_bounds__(128, 1) tree_node_tc_kernel(
   const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
   const uint32_t idesc = idesc_bf16(128, 128, false, false);
   const uint32_t a0 = smem_u32(sh.a);
-  auto stage_b = [&](int node, int buf) {         // node's M hi + lo rows -> b[buf] (one cp.async group)
-    const uint16_t* src = Mb + (nodes0 + node) * 2 * kD * kD;
-    const uint32_t dst = smem_u32(sh.b[buf]);
-    for (int x = tid; x < 2 * kD * 16; x += 128) {
-      const int part = x >> 11, r = (x >> 4) & 127, cc = x & 15;
-      cp_async16(dst + part * (2 * kTcQ * 128) + (cc >> 3) * (kTcQ * 128) + sw128_off(r, cc & 7),
-                 src + part * kD * kD + r * kD + cc * 8, 16u);
-    }
-    cp_async_commit();
+  // node's M hi + lo images (64 KB, the forest stores them in this shared-memory layout) -> b[buf] by one
+  // bulk copy (thread 0); the MMA issuer waits for bar_b[buf] before it reads them
+  uint32_t loads_b[2] = {0u, 0u}, issued_b[2] = {0u, 0u};
+  auto stage_b = [&](int node, int buf) {
+    ++issued_b[buf];
+    mbar_arrive_expect_tx(&sh.bar_b[buf], 2 * kD * kD * 2);
+    bulk_load(sh.b[buf], Mb + (nodes0 + node) * 2 * kD * kD, 2 * kD * kD * 2, &sh.bar_b[buf], policy_evict_normal());
+  };
+  auto wait_b = [&](int buf) {                    // thread 0, before the MMAs that read b[buf]
+    const bool w = mbar_wait(&sh.bar_b[buf], loads_b[buf] & 1u, status, &sh.abort_flag);
+    ++loads_b[buf];
+    return w;
   };
   auto issue = [&](int buf, uint32_t ycol) {      // Y[ycol] = Dh Mh + Dh Ml + Dl Mh (thread 0)
     tc_fence_after();
@@ -1774,10 +1788,8 @@ __global__ void __launch_bounds__(128, 1) tree_node_tc_kernel(
   };
   uint32_t uses[2] = {0u, 0u};                     // completed phases per barrier
   bool ok = true;
-  if (ACCEPT) {                                    // the one node's J, for every chunk
-    stage_b(ch0, 0);
-    cp_async_wait<0>();
-  }
+  bool b_ready = false;                            // accept: the one node's J has landed
+  if (ACCEPT && tid == 0) stage_b(ch0, 0);         // the one node's J, for every chunk
   for (int64_t win = lo; win < hi && ok; win += kWindow) {
     const int cnt = gather_window128(perm, win, min(hi, win + kWindow), mask, mwords, mbit, sh.list, sh.wsum);
     for (int b0i = 0; b0i < cnt && ok; b0i += kTcQ) {
@@ -1785,7 +1797,7 @@ __global__ void __launch_bounds__(128, 1) tree_node_tc_kernel(
       const int* lst = sh.list + b0i;
       const bool live = tid < nq;
       const int64_t qq = live ? lst[tid] : 0;
-      if (!ACCEPT) stage_b(ch0, 0);
+      if (!ACCEPT && tid == 0) stage_b(ch0, 0);
       // D = scale q - c of this thread's row, kept in registers (the walk's epilogue reads it), split into
       // the A operand's bf16 hi and lo parts
       float d[kD];
@@ -1812,24 +1824,24 @@ __global__ void __launch_bounds__(128, 1) tree_node_tc_kernel(
         }
         sh.rec[tid] = r;
       }
-      if (!ACCEPT) cp_async_wait<0>();
       fence_proxy_async_smem();
       tc_fence_before();
       __syncthreads();
       if (tid == 0) {
-        issue(0, 0);
+        bool w = true;
+        if (!ACCEPT || !b_ready) w = wait_b(0);
+        b_ready = true;
+        if (w) issue(0, 0);                       // (a failed wait leaves bar[0] incomplete: the wait below ends)
         mma_commit(&sh.bar[0]);
+        if (!ACCEPT && nc > 1) stage_b(ch0 + 1, 1);
       }
-      if (!ACCEPT && nc > 1) stage_b(ch0 + 1, 1);
       for (int i = 0; i < nc; ++i) {
         const int yb = i & 1;
         if (!ACCEPT && i + 1 < nc) {               // next child's MMAs, into the other Y buffer
-          cp_async_wait<0>();
-          fence_proxy_async_smem();
           tc_fence_before();
-          __syncthreads();
+          __syncthreads();                         // the epilogue of child i - 1 has read that Y buffer
           if (tid == 0) {
-            issue(yb ^ 1, 128u * (yb ^ 1));
+            if (wait_b(yb ^ 1)) issue(yb ^ 1, 128u * (yb ^ 1));
             mma_commit(&sh.bar[yb ^ 1]);
           }
         }
@@ -1839,7 +1851,7 @@ __global__ void __launch_bounds__(128, 1) tree_node_tc_kernel(
           ok = false;
           break;
         }
-        if (!ACCEPT && i + 2 < nc) stage_b(ch0 + i + 2, yb);   // this buffer's MMAs have completed
+        if (!ACCEPT && i + 2 < nc && tid == 0) stage_b(ch0 + i + 2, yb);   // this buffer's MMAs completed
         tc_fence_after();
         const int n = ch0 + i;
         const int64_t node = nodes0 + n;
@@ -1899,7 +1911,14 @@ __global__ void __launch_bounds__(128, 1) tree_node_tc_kernel(
       __syncthreads();
     }
   }
-  cp_async_wait<0>();
+  if (tid == 0) {                                  // no bulk copy may land after the CTA leaves
+    volatile int none = 0;
+    for (int bb = 0; bb < 2; ++bb)
+      while (loads_b[bb] < issued_b[bb]) {
+        mbar_wait_for(&sh.bar_b[bb], loads_b[bb] & 1u, status, &none, kWaitCycles);
+        ++loads_b[bb];
+      }
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, 256);
@@ -1974,9 +1993,9 @@ ForestLayout forest_layout(const HtrcTreeDims* d, const Shape& s) {
     o += a256(nn * kD * kD * 4);
     f.JT[l] = o;
     o += a256(nn * kD * kD * 4);
-    f.Hb[l] = o;                              // [C][n][hi, lo][128][128] bf16: H rows
+    f.Hb[l] = o;                              // [C][n][hi, lo] bf16 images (img_elem) of H
     o += a256(nn * 2 * kD * kD * 2);
-    f.Jb[l] = o;                              // [C][n][hi, lo][128][128] bf16: J rows (value dim major)
+    f.Jb[l] = o;                              // [C][n][hi, lo] bf16 images of J (rows: value dims)
     o += a256(nn * 2 * kD * kD * 2);
   }
   f.total = o;
