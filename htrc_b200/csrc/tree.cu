@@ -62,32 +62,55 @@ __device__ __forceinline__ float score_of(float lm, float quad, float norm) {
   return expf(fminf(0.f, lm - norm)) * expm1f(fminf(0.5f * fabsf(quad), 80.f));
 }
 
-// Gather the queries of centre c in [lo, hi) of the grouped order whose bit `bit` is set in
-// mask[q * words + bit / 32] (mask == nullptr: every query) into list[0 .. return).  256 threads.
-__device__ int gather_window(const int32_t* __restrict__ perm, int64_t lo, int64_t hi,
-                             const uint32_t* __restrict__ mask, int words, int bit, int* list, int* wsum) {
+// Gather the queries of centre c in [lo, hi) of the grouped order (hi - lo <= kWindow) whose bit `bit` is
+// set in mask[q * words + bit / 32] (mask == nullptr: every query) into list[0 .. return), in candidate order.
+// NT threads; thread t owns candidates lo + t * (kWindow / NT) + j: all of its loads go out first (the grouped
+// order, then the mask words it names), then one block-wide scan of the per-thread counts places them.
+template <int NT>
+__device__ int gather_window_n(const int32_t* __restrict__ perm, int64_t lo, int64_t hi,
+                               const uint32_t* __restrict__ mask, int words, int bit, int* list, int* wsum) {
+  constexpr int kPer = kWindow / NT;
+  constexpr int kWarps = NT / 32;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  int total = 0;
-  for (int64_t base = lo; base < hi; base += 256) {
-    const int64_t i = base + tid;
-    bool take = false;
-    int q = 0;
-    if (i < hi) {
-      q = perm[i];
-      take = mask == nullptr || ((mask[static_cast<int64_t>(q) * words + (bit >> 5)] >> (bit & 31)) & 1u);
-    }
-    const uint32_t b = __ballot_sync(0xffffffffu, take);
-    if (lane == 0) wsum[warp] = __popc(b);
-    __syncthreads();
-    int before = total;
-    for (int w = 0; w < warp; ++w) before += wsum[w];
-    if (take) list[before + __popc(b & ((1u << lane) - 1u))] = q;
-    int add = 0;
-    for (int w = 0; w < 8; ++w) add += wsum[w];
-    total += add;
-    __syncthreads();
+  const int64_t i0 = lo + static_cast<int64_t>(tid) * kPer;
+  int qv[kPer];
+  bool tk[kPer];
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) qv[j] = i0 + j < hi ? perm[i0 + j] : 0;
+  int cnt = 0;
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    bool t = i0 + j < hi;
+    if (t && mask != nullptr) t = (mask[static_cast<int64_t>(qv[j]) * words + (bit >> 5)] >> (bit & 31)) & 1u;
+    tk[j] = t;
+    cnt += t;
   }
+  int x = cnt;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) wsum[warp] = x;
+  __syncthreads();
+  int before = x - cnt, total = 0;
+#pragma unroll
+  for (int w = 0; w < kWarps; ++w) {
+    const int ws = wsum[w];
+    if (w < warp) before += ws;
+    total += ws;
+  }
+#pragma unroll
+  for (int j = 0; j < kPer; ++j)
+    if (tk[j]) list[before++] = qv[j];
+  __syncthreads();
   return total;
+}
+
+__device__ __forceinline__ int gather_window(const int32_t* __restrict__ perm, int64_t lo, int64_t hi,
+                                             const uint32_t* __restrict__ mask, int words, int bit, int* list,
+                                             int* wsum) {
+  return gather_window_n<256>(perm, lo, hi, mask, words, bit, list, wsum);
 }
 
 // number of children of node p of a level with n_parent nodes over a child level of n_child nodes
@@ -1317,31 +1340,10 @@ constexpr size_t kTcSmemBytes = 110 * 1024;   // > 228 KB / 3: at most two CTAs 
 static_assert(sizeof(TcSmem) + 1024 <= kTcSmemBytes, "tree tensor-core shared layout");
 
 // gather_window for 128 threads
-__device__ int gather_window128(const int32_t* __restrict__ perm, int64_t lo, int64_t hi,
-                                const uint32_t* __restrict__ mask, int words, int bit, int* list, int* wsum) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  int total = 0;
-  for (int64_t base = lo; base < hi; base += 128) {
-    const int64_t i = base + tid;
-    bool take = false;
-    int q = 0;
-    if (i < hi) {
-      q = perm[i];
-      take = (mask[static_cast<int64_t>(q) * words + (bit >> 5)] >> (bit & 31)) & 1u;
-    }
-    const uint32_t b = __ballot_sync(0xffffffffu, take);
-    if (lane == 0) wsum[warp] = __popc(b);
-    __syncthreads();
-    int before = total, add = 0;
-    for (int w = 0; w < 4; ++w) {
-      if (w < warp) before += wsum[w];
-      add += wsum[w];
-    }
-    if (take) list[before + __popc(b & ((1u << lane) - 1u))] = q;
-    total += add;
-    __syncthreads();
-  }
-  return total;
+__device__ __forceinline__ int gather_window128(const int32_t* __restrict__ perm, int64_t lo, int64_t hi,
+                                                const uint32_t* __restrict__ mask, int words, int bit, int* list,
+                                                int* wsum) {
+  return gather_window_n<128>(perm, lo, hi, mask, words, bit, list, wsum);
 }
 
 // 4-byte asynchronous global -> shared copy; src_bytes 0 writes zeros (the source is not read)
