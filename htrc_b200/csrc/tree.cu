@@ -1711,14 +1711,31 @@ constexpr size_t kNodeSmemBytes = sizeof(NodeSmem) + 1024;
 template <typename T>
 __device__ __forceinline__ void load_row128(const T* q, int64_t row, float scale, const float* __restrict__ c,
                                             float (&d)[kD]) {
+  if constexpr (std::is_same<T, uint16_t>::value) {     // bf16 rows: 16-byte loads of 8 values, all issued first
+    const uint4* src = reinterpret_cast<const uint4*>(q + row * kD);
+    uint4 raw[16];
 #pragma unroll
-  for (int c4 = 0; c4 < 32; ++c4) {
-    const float4 x = ld_row4<T>(q, row, c4);
-    const float4 cc = __ldg(reinterpret_cast<const float4*>(c) + c4);
-    d[4 * c4] = fmaf(scale, x.x, -cc.x);
-    d[4 * c4 + 1] = fmaf(scale, x.y, -cc.y);
-    d[4 * c4 + 2] = fmaf(scale, x.z, -cc.z);
-    d[4 * c4 + 3] = fmaf(scale, x.w, -cc.w);
+    for (int i = 0; i < 16; ++i) raw[i] = __ldg(src + i);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const uint32_t w[4] = {raw[i].x, raw[i].y, raw[i].z, raw[i].w};
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const int e = 8 * i + 2 * h;
+        d[e] = fmaf(scale, __uint_as_float(w[h] << 16), -__ldg(c + e));
+        d[e + 1] = fmaf(scale, __uint_as_float(w[h] & 0xFFFF0000u), -__ldg(c + e + 1));
+      }
+    }
+  } else {
+#pragma unroll
+    for (int c4 = 0; c4 < 32; ++c4) {
+      const float4 x = ld_row4<T>(q, row, c4);
+      const float4 cc = __ldg(reinterpret_cast<const float4*>(c) + c4);
+      d[4 * c4] = fmaf(scale, x.x, -cc.x);
+      d[4 * c4 + 1] = fmaf(scale, x.y, -cc.y);
+      d[4 * c4 + 2] = fmaf(scale, x.z, -cc.z);
+      d[4 * c4 + 3] = fmaf(scale, x.w, -cc.w);
+    }
   }
 }
 
@@ -1818,7 +1835,9 @@ __global__ void __launch_bounds__(128, 1) tree_node_tc_kernel(
         st_shared_v4(a0 + 2 * (kTcQ * 128) + off, l);
       }
       const float nrm = (!ACCEPT && live) ? norm[qq] : 0.f;
+      float lm_acc = 0.f;                          // accept: the node's predicted log-mass, read early
       if (ACCEPT && live) {
+        lm_acc = lv.lm[lev][qq * n_lev + ch0];
         int64_t r = record_of_internal(lv, base, qq, lev, ch0);
         if (r < 0 || r >= nrec) {
           flag_status(status, ST_BAD_INDEX);
@@ -1877,7 +1896,7 @@ __global__ void __launch_bounds__(128, 1) tree_node_tc_kernel(
             }
           }
           if (r >= 0) {
-            rec_lm[r] = lv.lm[lev][qq * n_lev + n];
+            rec_lm[r] = lm_acc;
             rec_ex[r] = 0;
           }
         } else {
